@@ -1,0 +1,160 @@
+// Host side of the tcgen05 GEMM: template dispatch, plans and the C ABI.
+#include "gemm_plan.cuh"
+
+namespace fm {
+
+namespace {
+
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
+
+template <int BN>
+struct BnTable {
+  static GemmKernel get(int epi) {
+    switch (epi) {
+      case EPI_STORE: return gemm_bf16_tc<BN, EPI_STORE>;
+      case EPI_GELU: return gemm_bf16_tc<BN, EPI_GELU>;
+      case EPI_SWIGLU: return gemm_bf16_tc<BN, EPI_SWIGLU>;
+      case EPI_RESID: return gemm_bf16_tc<BN, EPI_RESID>;
+      case EPI_QKNORM: return gemm_bf16_tc<BN, EPI_QKNORM>;
+      case EPI_KVCACHE: return gemm_bf16_tc<BN, EPI_KVCACHE>;
+      case EPI_LOGITS: return gemm_bf16_tc<BN, EPI_LOGITS>;
+      case EPI_F32: return gemm_bf16_tc<BN, EPI_F32>;
+      default: return nullptr;
+    }
+  }
+  static size_t smem() { return GemmShape<BN>::SMEM; }
+};
+
+GemmKernel kernel_for(int bn, int epi, size_t* smem) {
+  switch (bn) {
+    case 16: *smem = BnTable<16>::smem(); return BnTable<16>::get(epi);
+    case 32: *smem = BnTable<32>::smem(); return BnTable<32>::get(epi);
+    case 64: *smem = BnTable<64>::smem(); return BnTable<64>::get(epi);
+    case 128: *smem = BnTable<128>::smem(); return BnTable<128>::get(epi);
+    case 256: *smem = BnTable<256>::smem(); return BnTable<256>::get(epi);
+    default: return nullptr;
+  }
+}
+
+// cudaFuncSetAttribute once per (device, kernel)
+bool ensure_smem_attr(GemmKernel k, size_t smem) {
+  static thread_local int cached_dev = -1;
+  static thread_local GemmKernel done[64];
+  static thread_local int ndone = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev != cached_dev) {
+    ndone = 0;
+    cached_dev = dev;
+  }
+  for (int i = 0; i < ndone; ++i)
+    if (done[i] == k) return true;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
+  if (ndone < 64) done[ndone++] = k;
+  return true;
+}
+
+}  // namespace
+
+int gemm_bn_for(int64_t N) {
+  if (N <= 16) return 16;
+  if (N <= 32) return 32;
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  return 256;
+}
+
+static int64_t gemm_grid_for(int64_t units) {
+  const int64_t sms = num_sms();
+  return units < sms ? units : sms;
+}
+
+size_t gemm_partials_bytes(int64_t M, int64_t N, int64_t K) {
+  const int bn = gemm_bn_for(N);
+  const int64_t units = ((M + 127) / 128) * ((N + bn - 1) / bn) * ((K + 63) / 64);
+  return (size_t)gemm_grid_for(units) * 2 * bn * 128 * sizeof(float);
+}
+
+fm_status gemm_prepare(GemmPlan* p, const void* W, int64_t M, int64_t K, int64_t ldw, const void* X, int64_t N,
+                       int64_t ldx, int epi, float* ws, int* counters, int* err) {
+  if (!W || !X) return set_error(FM_ERR_INVALID, "gemm: null operand");
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(FM_ERR_SHAPE, "gemm: empty shape M=%lld N=%lld K=%lld",
+                                                   (long long)M, (long long)N, (long long)K);
+  if (K % 8 != 0 || ldw % 8 != 0 || ldx % 8 != 0)
+    return set_error(FM_ERR_ALIGN, "gemm: K and leading dimensions must be multiples of 8 (16 bytes)");
+  if (M >= (1ll << 31) || N >= (1ll << 31)) return set_error(FM_ERR_SHAPE, "gemm: dimension too large");
+  *p = GemmPlan{};
+  const int bn = gemm_bn_for(N);
+  fm_status st = make_tmap_bf16(&p->tmA, W, (uint64_t)M, (uint64_t)K, (uint64_t)ldw, 128);
+  if (st) return st;
+  st = make_tmap_bf16(&p->tmB, X, (uint64_t)N, (uint64_t)K, (uint64_t)ldx, (uint32_t)bn);
+  if (st) return st;
+  GemmArgs& a = p->args;
+  a.M = (int)M;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.kb = (int)((K + 63) / 64);
+  a.m_tiles = (int)((M + 127) / 128);
+  a.n_tiles = (int)((N + bn - 1) / bn);
+  a.units = (long long)a.m_tiles * a.n_tiles * a.kb;
+  a.ws = ws;
+  a.counters = counters;
+  a.err = err;
+  p->bn = bn;
+  p->epi = epi;
+  p->grid = (int)gemm_grid_for(a.units);
+  size_t smem = 0;
+  if (!kernel_for(bn, epi, &smem)) return set_error(FM_ERR_UNSUPPORTED, "gemm: no kernel for epilogue %d", epi);
+  p->smem = smem;
+  return FM_OK;
+}
+
+fm_status gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
+  size_t smem = 0;
+  GemmKernel k = kernel_for(p.bn, p.epi, &smem);
+  if (!k) return set_error(FM_ERR_UNSUPPORTED, "gemm: no kernel for bn %d epilogue %d", p.bn, p.epi);
+  const bool split_possible = p.grid > 1 || p.args.units > p.args.kb;
+  if (split_possible && (!p.args.ws || !p.args.counters))
+    return set_error(FM_ERR_WORKSPACE, "gemm: split-K workspace missing");
+  if (!ensure_smem_attr(k, smem)) return set_error(FM_ERR_CUDA, "gemm: cannot set shared memory size");
+  return launch_kernel(k, dim3(p.grid), dim3(192), smem, stream, pdl, p.tmA, p.tmB, p.args);
+}
+
+}  // namespace fm
+
+using namespace fm;
+
+extern "C" size_t fm_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
+  const int bn = gemm_bn_for(N);
+  const size_t tiles = (size_t)((M + 127) / 128) * (size_t)((N + bn - 1) / bn);
+  return 256 + ((tiles * sizeof(int) + 255) / 256) * 256 + gemm_partials_bytes(M, N, K);
+}
+
+extern "C" fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
+                                  int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
+                                  size_t workspace_bytes, int32_t* err, fm_stream stream) {
+  if (!out) return set_error(FM_ERR_INVALID, "gemm: null output");
+  if (epilogue != EPI_STORE && epilogue != EPI_GELU && epilogue != EPI_SWIGLU && epilogue != EPI_RESID &&
+      epilogue != EPI_F32)
+    return set_error(FM_ERR_UNSUPPORTED, "gemm: epilogue %d is not exposed here", epilogue);
+  if (epilogue == EPI_RESID && !gate) return set_error(FM_ERR_INVALID, "gemm: residual epilogue needs a gate");
+  if (epilogue == EPI_SWIGLU && M % 128 != 0)
+    return set_error(FM_ERR_SHAPE, "gemm: swiglu needs M a multiple of 128 (64 features per tile)");
+  const size_t need = fm_gemm_workspace_size(M, N, K);
+  if (!workspace || workspace_bytes < need)
+    return set_error(FM_ERR_WORKSPACE, "gemm: workspace of %zu bytes needed", need);
+  const int bn = gemm_bn_for(N);
+  const size_t tiles = (size_t)((M + 127) / 128) * (size_t)((N + bn - 1) / bn);
+  char* wsb = static_cast<char*>(workspace);
+  int* counters = reinterpret_cast<int*>(wsb + 256);
+  float* partials = reinterpret_cast<float*>(wsb + 256 + ((tiles * sizeof(int) + 255) / 256) * 256);
+  GemmPlan p;
+  fm_status st = gemm_prepare(&p, W, M, K, K, X, N, K, epilogue, partials, counters, err);
+  if (st) return st;
+  p.args.out = static_cast<__nv_bfloat16*>(out);
+  p.args.out32 = static_cast<float*>(out);
+  p.args.ldo = ldo;
+  p.args.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.args.gate = static_cast<const __nv_bfloat16*>(gate);
+  return gemm_launch(p, static_cast<cudaStream_t>(stream), false);
+}

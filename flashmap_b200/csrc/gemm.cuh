@@ -1,0 +1,488 @@
+// tcgen05 GEMM for the FlashMap drafter: Y[n, m] = sum_k X[n, k] * W[m, k].
+//
+// Orientation ("swap-AB"): the weight W (nn.Linear layout, out x in) is the
+// 128-row A operand and the tokens X are the N = BN operand, so a batch-1
+// draft (16 tokens) runs M=128 x N=16 UMMAs that stream W straight from HBM.
+//
+// Work decomposition: the (tile, k-block) units of the whole GEMM are split
+// evenly over the grid (stream-K).  A tile whose k-range spans several CTAs
+// is finished by the last contributor to arrive: every contributor writes its
+// fp32 partial to the workspace and bumps a per-tile counter; the one that
+// sees the final count sums all partials in contributor order (so the result
+// does not depend on arrival order) and runs the epilogue.  Nothing spins on
+// another CTA.
+//
+// Roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues
+// tcgen05.mma and owns the TMEM allocation, warps 2-5 read the accumulators
+// (TMEM lane quarter = warp % 4) and run the fused epilogue.
+//
+// Programmatic dependent launch: the producer loads the first pipeline
+// stages of W (constant weights) before griddepcontrol.wait, so the weight
+// stream of this GEMM overlaps the tail of the kernel before it.
+#pragma once
+
+#include "common.cuh"
+
+namespace fm {
+
+enum GemmEpilogue : int {
+  EPI_STORE = 0,    // out = bf16(acc + bias)
+  EPI_GELU = 1,     // out = bf16(gelu(bf16(acc + bias)))
+  EPI_SWIGLU = 2,   // tiles hold 64 gate rows then 64 up rows: out = bf16(bf16(silu(g)) * u)
+  EPI_RESID = 3,    // out (in place) = bf16(out + bf16(gate * bf16(acc + bias)))
+  EPI_QKNORM = 4,   // parts q | k | v: q,k get per-head RMSNorm + interleaved RoPE
+  EPI_KVCACHE = 5,  // rows (layer, k|v, head, dim): k gets norm + RoPE; written into the cache
+  EPI_LOGITS = 6,   // out = bf16(acc + bias) at column col_ids[m]; per-token argmax key
+  EPI_F32 = 7,      // out32 = acc (fp32, no rounding): one-time constants
+  EPI_COUNT = 8,
+};
+
+struct GemmArgs {
+  int M, N, K;  // output features (rows of W), tokens (rows of X), reduction
+  int kb;       // k-blocks of 64
+  int m_tiles, n_tiles;
+  long long units;  // m_tiles * n_tiles * kb
+  __nv_bfloat16* out;
+  float* out32;
+  long long ldo;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* norm_w0;  // q-norm (QKNORM) or per-layer k-norm base (KVCACHE)
+  const __nv_bfloat16* norm_w1;  // k-norm (QKNORM)
+  int part_rows;                 // rows per q/k/v part (the hidden size)
+  int head_dim;
+  float eps;
+  const float* rope_cos;  // [rope_len][head_dim/2]
+  const float* rope_sin;
+  int rope_len;
+  const int* positions;  // [N]
+  const int* token_seq;  // [N] (KVCACHE)
+  __nv_bfloat16* cache;  // (L, 2, cache_batch, heads, cache_len, head_dim)
+  int cache_batch, cache_heads, cache_len;
+  int norm_layer_stride;  // elements between layers' k-norm weights
+  unsigned long long* argmax_keys;  // [N] or null (no argmax)
+  const long long* col_ids;         // [M] target ids of the rows, or null (row = id)
+  int scatter;                      // LOGITS: store row m at column col_ids[m] (else at m)
+  float* ws;                        // split-K partials: grid * 2 slots * BN * 128 fp32
+  int* counters;                    // [m_tiles * n_tiles], zero between launches
+  int* err;
+};
+
+template <int BN>
+struct GemmShape {
+  static constexpr int A_BYTES = 128 * 64 * 2;
+  static constexpr int B_BYTES = BN * 64 * 2;
+  static constexpr int STAGES = BN <= 16 ? 5 : BN <= 32 ? 4 : BN <= 64 ? 7 : BN <= 128 ? 5 : 4;
+  static constexpr int ACC = 2;
+  static constexpr uint32_t TMEM_COLS =
+      ACC * BN <= 32 ? 32 : ACC * BN <= 64 ? 64 : ACC * BN <= 128 ? 128 : ACC * BN <= 256 ? 256 : 512;
+  static constexpr int SCRATCH = 4096 + 1024;  // epilogue exchange (union) + split flags
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 /*alignment slack*/ + STAGES * (A_BYTES + B_BYTES) + BAR_BYTES + SCRATCH;
+};
+
+__device__ __forceinline__ long long cta_of_unit(long long u, long long U, int G) {
+  return ((u + 1) * (long long)G - 1) / U;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Epilogue on 16 accumulator columns (tokens n0 .. n0+15) of tile row r (feature m).
+// Threads of the 4 epilogue warps call it together (it may use named barrier 1).
+template <int EPI>
+__device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, int r, int m, int mt, int n0,
+                                           float* xch, unsigned long long* xch64) {
+  const int lane = threadIdx.x & 31;
+  const int q = (threadIdx.x >> 5) & 3;
+  const bool mvalid = m < a.M;
+  if constexpr (EPI == EPI_F32) {
+    if (mvalid)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < a.N) a.out32[(long long)(n0 + j) * a.ldo + m] = v[j];
+  } else if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
+    if (!mvalid) return;
+    const float b = a.bias ? bf2f(a.bias[m]) : 0.0f;
+    const float g = (EPI == EPI_RESID) ? bf2f(a.gate[m]) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = n0 + j;
+      if (n >= a.N) continue;
+      float y = round_bf(__fadd_rn(v[j], b));
+      __nv_bfloat16* dst = a.out + (long long)n * a.ldo + m;
+      if constexpr (EPI == EPI_GELU) {
+        y = __fmul_rn(__fmul_rn(y, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(y, 0.70710678118654752f))));
+        *dst = f2bf(y);
+      } else if constexpr (EPI == EPI_RESID) {
+        const float gy = round_bf(__fmul_rn(g, y));
+        *dst = f2bf(__fadd_rn(bf2f(*dst), gy));
+      } else {
+        *dst = f2bf(y);
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    // rows 64..127 of the tile are the "up" halves of features mt*64 + (r - 64)
+    if (r >= 64) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xch[(r - 64) * 16 + j] = round_bf(v[j]);
+    }
+    named_bar_sync(1, 128);
+    if (r < 64) {
+      const int f = mt * 64 + r;
+      if (f < a.M / 2) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = n0 + j;
+          if (n >= a.N) continue;
+          const float gt = round_bf(v[j]);
+          const float s = round_bf(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))));
+          a.out[(long long)n * a.ldo + f] = f2bf(__fmul_rn(s, xch[r * 16 + j]));
+        }
+      }
+    }
+    named_bar_sync(1, 128);
+  } else if constexpr (EPI == EPI_QKNORM || EPI == EPI_KVCACHE) {
+    const int hd = a.head_dim;
+    int part, layer = 0;
+    if constexpr (EPI == EPI_QKNORM) {
+      part = (mt * 128) / a.part_rows;  // 0 q, 1 k, 2 v (uniform over the tile)
+    } else {
+      layer = (mt * 128) / (2 * a.part_rows);
+      part = ((mt * 128) / a.part_rows) & 1;  // 0 k, 1 v
+    }
+    const bool normed = (EPI == EPI_QKNORM) ? (part < 2) : (part == 0);
+    const int d = (m % a.part_rows) % hd;
+    float y[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = round_bf(v[j]);
+    if (normed) {  // uniform branch over the whole tile
+      // per-head sum of squares: warp butterfly, then the head's warp quarters in order
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float s = __fmul_rn(y[j], y[j]);
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+        if (lane == j) xch[q * 16 + j] = s;
+      }
+      named_bar_sync(1, 128);
+      const int hq = hd >> 5;  // warp quarters per head
+      const int q0 = (q / hq) * hq;
+      const __nv_bfloat16* w;
+      if constexpr (EPI == EPI_QKNORM)
+        w = part == 0 ? a.norm_w0 : a.norm_w1;
+      else
+        w = a.norm_w0 + (long long)layer * a.norm_layer_stride;
+      const float wd = bf2f(w[d]);
+      const int half = hd >> 1;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float tot = 0.0f;
+        for (int qq = q0; qq < q0 + hq; ++qq) tot = __fadd_rn(tot, xch[qq * 16 + j]);
+        const float mean = __fdiv_rn(tot, (float)hd);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        const float scale = round_bf(__fmul_rn(wd, inv));
+        const float xn = round_bf(__fmul_rn(y[j], scale));
+        const float other = __shfl_xor_sync(0xffffffffu, xn, 1);
+        const int n = n0 + j;
+        int pos = (n < a.N) ? a.positions[n] : 0;
+        if (pos < 0 || pos >= a.rope_len) {
+          if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
+          pos = 0;
+        }
+        const float cs = a.rope_cos[(long long)pos * half + (d >> 1)];
+        const float sn = a.rope_sin[(long long)pos * half + (d >> 1)];
+        float o;
+        if ((d & 1) == 0)
+          o = __fsub_rn(__fmul_rn(xn, cs), __fmul_rn(other, sn));
+        else
+          o = __fadd_rn(__fmul_rn(xn, cs), __fmul_rn(other, sn));
+        y[j] = round_bf(o);
+      }
+      named_bar_sync(1, 128);  // xch is reused by the next chunk
+    }
+    if (!mvalid) return;
+    if constexpr (EPI == EPI_QKNORM) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (n0 + j < a.N) a.out[(long long)(n0 + j) * a.ldo + m] = f2bf(y[j]);
+    } else {
+      const int h = (m % a.part_rows) / hd;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        if (n >= a.N) continue;
+        const int seq = a.token_seq[n];
+        const int pos = a.positions[n];
+        if (seq < 0 || seq >= a.cache_batch || pos < 0 || pos >= a.cache_len) {
+          record_error(a.err, DEV_BAD_INDEX);
+          continue;
+        }
+        const long long idx =
+            ((((long long)(layer * 2 + part) * a.cache_batch + seq) * a.cache_heads + h) * a.cache_len + pos) * hd +
+            d;
+        a.cache[idx] = f2bf(y[j]);
+      }
+    }
+  } else if constexpr (EPI == EPI_LOGITS) {
+    const float b = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
+    const long long id = mvalid ? (a.col_ids ? a.col_ids[m] : (long long)m) : 0;
+    const long long col = a.scatter ? id : (long long)m;
+    const bool want_argmax = a.argmax_keys != nullptr;  // uniform over the launch
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = n0 + j;
+      const float y = round_bf(__fadd_rn(v[j], b));
+      if (mvalid && n < a.N) a.out[(long long)n * a.ldo + col] = f2bf(y);
+      if (!want_argmax) continue;
+      unsigned long long key = mvalid ? argmax_key(y, (uint32_t)id) : 0ull;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (lane == j) xch64[q * 16 + j] = key;
+    }
+    if (!want_argmax) return;
+    named_bar_sync(1, 128);
+    if (threadIdx.x >= 64 && threadIdx.x < 80) {
+      const int j = threadIdx.x - 64;
+      unsigned long long key = xch64[j];
+      for (int qq = 1; qq < 4; ++qq) key = xch64[qq * 16 + j] > key ? xch64[qq * 16 + j] : key;
+      if (n0 + j < a.N) atomicMax(a.argmax_keys + n0 + j, key);
+    }
+    named_bar_sync(1, 128);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+template <int BN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const GemmArgs a) {
+  using S = GemmShape<BN>;
+  constexpr int STAGES = S::STAGES;
+  constexpr int ACC = S::ACC;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + ACC;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + ACC);
+  int* flags = reinterpret_cast<int*>(tmem_slot + 2);  // [0] abort, [1] last-arriver, [2..3] segment ok
+  uint8_t* scratch = smem + STAGES * (S::A_BYTES + S::B_BYTES) + S::BAR_BYTES;
+  float* xch = reinterpret_cast<float*>(scratch);
+  unsigned long long* xch64 = reinterpret_cast<unsigned long long*>(scratch);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long U = a.units;
+  const int G = gridDim.x;
+  const int c = blockIdx.x;
+  const long long u0 = (long long)c * U / G, u1 = (long long)(c + 1) * U / G;
+  const int kb = a.kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < ACC; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    flags[2] = 0;
+    flags[3] = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  // every CTA now holds its TMEM: the next kernel may be scheduled
+  pdl_launch_dependents();
+  volatile int* abort_flag = flags;
+
+  if (warp == 0) {
+    if (lane == 0 && u1 > u0) {
+      const uint64_t pol = a.n_tiles == 1 ? policy_evict_first() : policy_evict_last();
+      const long long n = u1 - u0;
+      const int pre = (int)(n < STAGES ? n : STAGES);
+      // weights of the first stages before the dependency wait
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const int tile = (int)(u / kb), k = (int)(u % kb);
+        mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
+        tma_load_2d_hint(sA + i * S::A_BYTES, &tmA, &full[i], k * 64, (tile / a.n_tiles) * 128, pol);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const int tile = (int)(u / kb), k = (int)(u % kb);
+        tma_load_2d(sB + i * S::B_BYTES, &tmB, &full[i], k * 64, (tile % a.n_tiles) * BN);
+      }
+      bool ok = true;
+      for (long long i = pre; i < n; ++i) {
+        const int s = (int)(i % STAGES);
+        const uint32_t r = (uint32_t)(i / STAGES);
+        if (!mbar_wait(&empty[s], (r - 1) & 1u, abort_flag)) {
+          record_error(a.err, DEV_TIMEOUT_EMPTY);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        const long long u = u0 + i;
+        const int tile = (int)(u / kb), k = (int)(u % kb);
+        mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+        tma_load_2d_hint(sA + s * S::A_BYTES, &tmA, &full[s], k * 64, (tile / a.n_tiles) * 128, pol);
+        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], k * 64, (tile % a.n_tiles) * BN);
+      }
+      if (!ok) {
+        // drain: every issued stage must land before the CTA's shared memory goes away
+        const long long issued_end = n;
+        for (long long i = (issued_end > STAGES ? issued_end - STAGES : 0); i < issued_end; ++i)
+          mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && u1 > u0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(128, BN);
+      long long i = 0;
+      int seg = 0;
+      for (long long u = u0; u < u1; ++seg) {
+        const int tile = (int)(u / kb);
+        const long long seg_begin = u;
+        const long long seg_end = (long long)(tile + 1) * kb < u1 ? (long long)(tile + 1) * kb : u1;
+        const int acc = seg % ACC;
+        const uint32_t ar = (uint32_t)(seg / ACC);
+        if (ar > 0 && !mbar_wait(&acc_empty[acc], (ar - 1) & 1u, abort_flag)) {
+          record_error(a.err, DEV_TIMEOUT_ACC);
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (; u < seg_end; ++u, ++i) {
+          const int s = (int)(i % STAGES);
+          if (!mbar_wait(&full[s], (uint32_t)(i / STAGES) & 1u, abort_flag)) {
+            record_error(a.err, DEV_TIMEOUT_FULL);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sdesc_k_sw128(smem_u32(sA + s * S::A_BYTES));
+          const uint64_t bd = sdesc_k_sw128(smem_u32(sB + s * S::B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(d_tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
+                      (u > seg_begin || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // epilogue warps
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    pdl_wait();
+    int seg = 0;
+    for (long long u = u0; u < u1; ++seg) {
+      const int tile = (int)(u / kb);
+      const long long seg_begin = u;
+      const long long seg_end = (long long)(tile + 1) * kb < u1 ? (long long)(tile + 1) * kb : u1;
+      u = seg_end;
+      const int acc = seg % ACC;
+      // one thread waits (bounded) and publishes the outcome, so that every
+      // epilogue thread leaves the loop together if the wait gave up
+      if (threadIdx.x == 64) {
+        const bool ok = mbar_wait(&acc_full[acc], (uint32_t)(seg / ACC) & 1u, abort_flag);
+        if (!ok) {
+          record_error(a.err, DEV_TIMEOUT_ACC);
+          *abort_flag = 1;
+        }
+        flags[2 + (seg & 1)] = ok ? 1 : 0;
+      }
+      named_bar_sync(1, 128);
+      if (!flags[2 + (seg & 1)]) break;
+      tc_fence_after();
+      const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      const int m = mt * 128 + r;
+      const int n0 = nt * BN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const bool whole = (seg_begin == (long long)tile * kb) && (seg_end == (long long)(tile + 1) * kb);
+      if (whole) {
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld_x16(taddr + c0, v);
+          tmem_wait_ld();
+          epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64);
+        }
+      } else {
+        const long long c_first = cta_of_unit((long long)tile * kb, U, G);
+        const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
+        const int slot = (seg_begin == u0) ? 0 : 1;
+        float* mine = a.ws + ((long long)(c * 2 + slot) * BN) * 128;
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld_x16(taddr + c0, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(mine + (long long)(c0 + j) * 128 + r, v[j]);
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (threadIdx.x == 64) {
+          const int old = atomicAdd(a.counters + tile, 1);
+          flags[1] = (old == (int)(c_last - c_first));
+        }
+        named_bar_sync(1, 128);
+        if (flags[1]) {
+          __threadfence();
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float own[16], v[16];
+            tmem_ld_x16(taddr + c0, own);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+            for (long long cc = c_first; cc <= c_last; ++cc) {
+              if (cc == c) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], own[j]);
+              } else {
+                const long long first_tile = ((long long)cc * U / G) / kb;
+                const int cs = (first_tile == tile) ? 0 : 1;
+                const float* p = a.ws + ((cc * 2 + cs) * BN + c0) * 128 + r;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], __ldcg(p + (long long)j * 128));
+              }
+            }
+            epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64);
+          }
+          if (threadIdx.x == 64) a.counters[tile] = 0;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace fm

@@ -1,0 +1,829 @@
+// Row-wise, noise, sampling and acceptance kernels of the FlashMap hot path,
+// and their C-ABI entry points.
+#include "attention.cuh"
+#include "ops.cuh"
+#include "philox.cuh"
+
+namespace fm {
+
+namespace {
+
+constexpr int RT = 256;  // threads of the row kernels
+
+// Sum over a 256-thread block in a fixed tree: offsets 16..1 inside each
+// warp, then 4, 2, 1 over the 8 warp sums.  `red` holds >= 9 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, o));
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float r = lane < (RT / 32) ? red[lane] : 0.0f;
+#pragma unroll
+    for (int o = RT / 64; o >= 1; o >>= 1) r = __fadd_rn(r, __shfl_down_sync(0xffffffffu, r, o));
+    if (lane == 0) red[RT / 32] = r;
+  }
+  __syncthreads();
+  const float out = red[RT / 32];
+  __syncthreads();
+  return out;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int w = 1; w < RT / 32; ++w) r = fmaxf(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int block_min_int(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_min_sync(0xffffffffu, v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int r = red[0];
+  for (int w = 1; w < RT / 32; ++w) r = min(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+__device__ __forceinline__ int block_max_int(int v, int* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = __reduce_max_sync(0xffffffffu, v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  int r = red[0];
+  for (int w = 1; w < RT / 32; ++w) r = max(r, red[w]);
+  __syncthreads();
+  return r;
+}
+
+// 8 consecutive bf16 of a row (vector `vec`), zero-padded past V
+__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* row, long long vec, long long V, bool aligned,
+                                           float* x) {
+  const long long v0 = vec * 8;
+  if (aligned && v0 + 8 <= V) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + v0);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = (v0 + j < V) ? bf2f(row[v0 + j]) : 0.0f;
+  }
+}
+
+// max of x/T, and (first) argmax of the raw values, over one row
+__device__ void row_max_argmax(const __nv_bfloat16* row, long long V, float temperature, float* red, float* m_out,
+                               long long* arg_out) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8;
+  float m = -INFINITY, bv = -INFINITY;
+  long long bi = V;  // sentinel larger than any index
+  for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
+    float x[8];
+    load8_bf16(row, vec, V, aligned, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const long long v = vec * 8 + j;
+      if (v >= V) break;
+      if (bi == V || x[j] > bv) {  // strict: the first index of a tie stays
+        bv = x[j];
+        bi = v;
+      }
+      if (temperature > 0.0f) m = fmaxf(m, __fdiv_rn(x[j], temperature));
+    }
+  }
+  // block argmax: largest value, smallest index among equals
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const long long oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float rv[RT / 32];
+  __shared__ long long ri[RT / 32];
+  if (lane == 0) {
+    rv[warp] = bv;
+    ri[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = rv[0];
+    long long i = ri[0];
+    for (int w = 1; w < RT / 32; ++w)
+      if (rv[w] > b || (rv[w] == b && ri[w] < i)) {
+        b = rv[w];
+        i = ri[w];
+      }
+    *arg_out = i;
+  }
+  __syncthreads();
+  *m_out = temperature > 0.0f ? block_max(m, red) : 0.0f;
+}
+
+// fixed-order sum of fm_exp(x/T - m): thread i walks vectors i, i+256, ...
+__device__ float row_sumexp(const __nv_bfloat16* row, long long V, float temperature, float m, float* red) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8;
+  float acc = 0.0f;
+  for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
+    float x[8];
+    load8_bf16(row, vec, V, aligned, x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (vec * 8 + j >= V) break;
+      acc = __fadd_rn(acc, fm_exp(__fsub_rn(__fdiv_rn(x[j], temperature), m)));
+    }
+  }
+  return block_sum(acc, red);
+}
+
+__device__ __forceinline__ long long range_width(long long V) {
+  const long long w = (V + RT - 1) / RT;
+  return (w + 7) / 8 * 8;
+}
+
+// Categorical draw over non-negative weights w(v), v < V, with uniform u:
+// contiguous per-thread ranges, scan, two-level search (see the C oracle).
+template <typename F>
+__device__ long long block_categorical(F weight, long long V, float u, float* sm) {
+  const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+  const long long W = range_width(V);
+  const long long lo = (long long)i * W, hi = min(lo + W, V);
+  float t = 0.0f;
+  for (long long v = lo; v < hi; ++v) t = __fadd_rn(t, weight(v));
+  float h = t;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, h, off);
+    if (lane >= off) h = __fadd_rn(y, h);
+  }
+  if (lane == 31) sm[RT + warp] = h;
+  __syncthreads();
+  if (i == 0) {
+    float base = 0.0f;
+    for (int w = 0; w < RT / 32; ++w) {
+      const float tot = sm[RT + w];
+      sm[RT + 8 + w] = base;
+      base = (w == 0) ? tot : __fadd_rn(base, tot);
+    }
+  }
+  __syncthreads();
+  if (warp > 0) h = __fadd_rn(sm[RT + 8 + warp], h);
+  sm[i] = h;
+  __syncthreads();
+  const float total = sm[RT - 1];
+  const float target = __fmul_rn(u, total);
+  int* ired = reinterpret_cast<int*>(sm + RT + 16);
+  const int first = block_min_int(h > target ? i : RT, ired);
+  const int lastpos = block_max_int(t > 0.0f ? i : -1, ired);
+  __shared__ long long result;
+  if (i == 0) {
+    const int chosen = first < RT ? first : lastpos;
+    long long pick = 0;
+    if (chosen >= 0) {
+      float run = chosen > 0 ? sm[chosen - 1] : 0.0f;
+      const long long clo = (long long)chosen * W, chi = min(clo + W, V);
+      long long last = -1;
+      pick = -1;
+      for (long long v = clo; v < chi; ++v) {
+        const float wv = weight(v);
+        run = __fadd_rn(run, wv);
+        if (wv > 0.0f) last = v;
+        if (run > target) {
+          pick = v;
+          break;
+        }
+      }
+      if (pick < 0) pick = last >= 0 ? last : clo;
+    }
+    result = pick;
+  }
+  __syncthreads();
+  return result;
+}
+
+// ------------------------------------------------------------------ kernels
+
+__global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
+                                                     __nv_bfloat16* y, int cols, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const __nv_bfloat16* xr = x + (long long)blockIdx.x * cols;
+  float ss = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += RT) {
+    const float v = bf2f(xr[c]);
+    ss = __fmaf_rn(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
+  __nv_bfloat16* yr = y + (long long)blockIdx.x * cols;
+  for (int c = threadIdx.x; c < cols; c += RT) {
+    const float scale = round_bf(__fmul_rn(bf2f(w[c]), inv));
+    yr[c] = f2bf(__fmul_rn(bf2f(xr[c]), scale));
+  }
+}
+
+__global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const __nv_bfloat16* mod,
+                                                   __nv_bfloat16* y, int cols, float eps) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const __nv_bfloat16* xr = x + (long long)blockIdx.x * cols;
+  float s = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += RT) s = __fadd_rn(s, bf2f(xr[c]));
+  const float mean = __fdiv_rn(block_sum(s, red), (float)cols);
+  float v = 0.0f;
+  for (int c = threadIdx.x; c < cols; c += RT) {
+    const float d = __fsub_rn(bf2f(xr[c]), mean);
+    v = __fmaf_rn(d, d, v);
+  }
+  const float var = __fdiv_rn(block_sum(v, red), (float)cols);
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  __nv_bfloat16* yr = y + (long long)blockIdx.x * cols;
+  for (int c = threadIdx.x; c < cols; c += RT) {
+    const float ln = round_bf(__fmul_rn(__fsub_rn(bf2f(xr[c]), mean), rstd));
+    const float one_plus = round_bf(__fadd_rn(1.0f, bf2f(mod[c])));
+    const float scaled = round_bf(__fmul_rn(ln, one_plus));
+    yr[c] = f2bf(__fadd_rn(scaled, bf2f(mod[cols + c])));
+  }
+}
+
+__global__ void rope_table_kernel(float* cs, float* sn, int max_pos, int hd, const float* inv_freq) {
+  const int half = hd / 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long long)max_pos * half) return;
+  const int pos = (int)(idx / half), i = (int)(idx % half);
+  // modeling_flashmap.py:57-58 in fp32: angle = pos * inv_freq[i]
+  const float ang = __fmul_rn((float)pos, inv_freq[i]);
+  cs[idx] = cosf(ang);
+  sn[idx] = sinf(ang);
+}
+
+__global__ void __launch_bounds__(RT) draft_prep_kernel(DraftPrepArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;
+  long long id = a.anchor_ids[b];
+  const int len = a.lengths[b];
+  if (id < 0 || id >= a.V) {
+    if (threadIdx.x == 0) record_error(a.err, DEV_BAD_INDEX);
+    id = 0;
+  }
+  if (threadIdx.x == 0 && (len < 0 || len + a.K + 1 > a.rope_len || len >= a.cache_len))
+    record_error(a.err, DEV_BAD_INDEX);
+  const __nv_bfloat16* src = a.embed + id * a.Ht;
+  __nv_bfloat16* dst = a.anchor_rows + (long long)b * a.Ht;
+  for (int c = threadIdx.x; c < a.Ht; c += RT) dst[c] = src[c];
+  if (threadIdx.x == 0) {
+    a.anchor_pos[b] = len;
+    a.anchor_seq[b] = b;
+  }
+  for (int k = threadIdx.x; k < a.K; k += RT) {
+    a.slot_pos[b * a.K + k] = len + 1 + k;
+    a.keys[b * a.K + k] = 0ull;
+  }
+}
+
+__global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* pr = a.post + (long long)t * a.post_stride;
+  const __nv_bfloat16* sr = a.state + (long long)t * a.Ht;
+  float sp = 0.0f, ss = 0.0f;
+  for (int c = threadIdx.x; c < a.Ht; c += RT) {
+    const float p = bf2f(pr[c]), s = bf2f(sr[c]);
+    sp = __fmaf_rn(p, p, sp);
+    ss = __fmaf_rn(s, s, ss);
+  }
+  sp = block_sum(sp, red);
+  ss = block_sum(ss, red);
+  const float ip = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sp, (float)a.Ht), a.eps)));
+  const float is = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.Ht), a.eps)));
+  __nv_bfloat16* o = a.out + (long long)t * a.Ht;
+  for (int c = threadIdx.x; c < a.Ht; c += RT) {
+    const float pn = round_bf(__fmul_rn(bf2f(pr[c]), round_bf(__fmul_rn(bf2f(a.state_norm_w[c]), ip))));
+    const float nn = round_bf(__fmul_rn(bf2f(sr[c]), round_bf(__fmul_rn(bf2f(a.noise_norm_w[c]), is))));
+    const float term = round_bf(__fmul_rn(a.gate, nn));
+    o[c] = f2bf(__fadd_rn(pn, term));
+  }
+}
+
+// Box-Muller on Philox words: pair p = element / 2 uses counter (p, 0, offset, 4)
+__device__ __forceinline__ void normal_pair(uint64_t seed, uint32_t offset, long long p, float& z0, float& z1) {
+  const Philox4 r = philox4x32_10((uint32_t)p, (uint32_t)(p >> 32), offset, 4u, seed);
+  const float u1 = __fmul_rn((float)(r.v[0] >> 8) + 0.5f, 5.9604644775390625e-08f);
+  const float u2 = __fmul_rn((float)(r.v[1] >> 8), 5.9604644775390625e-08f);
+  const float rad = sqrtf(-2.0f * logf(u1));
+  float sv, cv;
+  sincospif(2.0f * u2, &sv, &cv);
+  z0 = rad * cv;
+  z1 = rad * sv;
+}
+
+__global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (2 * p >= count) return;
+  float z0, z1;
+  normal_pair(seed, offset, p, z0, z1);
+  out[2 * p] = f2bf(z0);
+  if (2 * p + 1 < count) out[2 * p + 1] = f2bf(z1);
+}
+
+__global__ void philox_normal_f32_kernel(float* out, long long count, uint64_t seed, uint32_t offset) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (2 * p >= count) return;
+  float z0, z1;
+  normal_pair(seed, offset, p, z0, z1);
+  out[2 * p] = z0;
+  if (2 * p + 1 < count) out[2 * p + 1] = z1;
+}
+
+__global__ void argmax_tokens_kernel(const unsigned long long* keys, int64_t* tokens, int n) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) tokens[i] = (int64_t)argmax_key_index(keys[i]);
+}
+
+// rows of the multi-step featurisation GEMM input
+__global__ void __launch_bounds__(RT) state_rows_kernel(const float* state, __nv_bfloat16* out, int T, int S,
+                                                        float c, int with_posterior) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const int t = blockIdx.x;
+  const float* sr = state + (long long)t * S;
+  __nv_bfloat16* st_out = out + (long long)(with_posterior ? T + t : t) * S;
+  for (int v = threadIdx.x; v < S; v += RT) st_out[v] = f2bf(sr[v]);
+  if (!with_posterior) return;
+  float m = -INFINITY;
+  for (int v = threadIdx.x; v < S; v += RT) m = fmaxf(m, __fmul_rn(sr[v], c));
+  m = block_max(m, red);
+  float acc = 0.0f;
+  for (int v = threadIdx.x; v < S; v += RT) acc = __fadd_rn(acc, fm_exp(__fsub_rn(__fmul_rn(sr[v], c), m)));
+  const float sum = block_sum(acc, red);
+  __nv_bfloat16* po = out + (long long)t * S;
+  for (int v = threadIdx.x; v < S; v += RT)
+    po[v] = f2bf(__fdiv_rn(fm_exp(__fsub_rn(__fmul_rn(sr[v], c), m)), sum));
+}
+
+__global__ void __launch_bounds__(RT) state_update_kernel(float* state, const __nv_bfloat16* logits, long long ldl,
+                                                          int S, float a, float b, float d) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const int t = blockIdx.x;
+  const __nv_bfloat16* lr = logits + (long long)t * ldl;
+  float* sr = state + (long long)t * S;
+  float m = -INFINITY;
+  for (int v = threadIdx.x; v < S; v += RT) m = fmaxf(m, bf2f(lr[v]));
+  m = block_max(m, red);
+  float acc = 0.0f;
+  for (int v = threadIdx.x; v < S; v += RT) acc = __fadd_rn(acc, fm_exp(__fsub_rn(bf2f(lr[v]), m)));
+  const float sum = block_sum(acc, red);
+  for (int v = threadIdx.x; v < S; v += RT) {
+    const float p = __fdiv_rn(fm_exp(__fsub_rn(bf2f(lr[v]), m)), sum);
+    sr[v] = __fdiv_rn(__fadd_rn(__fmul_rn(a, sr[v]), __fmul_rn(b, p)), d);
+  }
+}
+
+__global__ void extend_prep_kernel(ExtendPrepArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= a.rows) return;
+  int lo = 0, hi = a.B;  // find b with cu[b] <= r < cu[b+1]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) / 2;
+    if (a.cu_rows[mid] <= r)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  const int pos = a.lengths[lo] + (r - a.cu_rows[lo]);
+  if (pos < 0 || pos >= a.cache_len || pos >= a.rope_len) record_error(a.err, DEV_BAD_INDEX);
+  a.token_seq[r] = lo;
+  a.positions[r] = pos;
+}
+
+__global__ void extend_commit_kernel(const int32_t* cu, int32_t* lengths, int B) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) lengths[b] += cu[b + 1] - cu[b];
+}
+
+// ------------------------------------------------------------------ sampling / acceptance
+
+__global__ void __launch_bounds__(RT) row_stats_kernel(const __nv_bfloat16* logits, long long V, float temperature,
+                                                       float* stats, int64_t* argmax) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const __nv_bfloat16* row = logits + (long long)blockIdx.x * V;
+  float m;
+  long long am;
+  row_max_argmax(row, V, temperature, red, &m, &am);
+  if (argmax && threadIdx.x == 0) argmax[blockIdx.x] = am;
+  if (stats) {
+    const float s = temperature > 0.0f ? row_sumexp(row, V, temperature, m, red) : 0.0f;
+    if (threadIdx.x == 0) {
+      stats[2 * blockIdx.x] = m;
+      stats[2 * blockIdx.x + 1] = s;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(RT) softmax_rows_kernel(const __nv_bfloat16* logits, long long V,
+                                                          float temperature, float* probs) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const __nv_bfloat16* row = logits + (long long)blockIdx.x * V;
+  float m;
+  long long am;
+  row_max_argmax(row, V, temperature, red, &m, &am);
+  const float s = row_sumexp(row, V, temperature, m, red);
+  float* pr = probs + (long long)blockIdx.x * V;
+  for (long long v = threadIdx.x; v < V; v += RT)
+    pr[v] = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(bf2f(row[v]), temperature), m)), s);
+}
+
+__global__ void __launch_bounds__(RT) sample_rows_kernel(const float* probs, long long V, int K, uint64_t seed,
+                                                         uint32_t offset, int64_t* tokens) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float sm[RT + 32];
+  const int row = blockIdx.x, b = row / K, k = row % K;
+  const float* pr = probs + (long long)row * V;
+  const float u = philox_uniform(seed, (uint32_t)k, (uint32_t)b, offset, 3u);
+  const long long pick = block_categorical([&](long long v) { return pr[v]; }, V, u, sm);
+  if (threadIdx.x == 0) tokens[row] = pick;
+}
+
+__global__ void accept_greedy_kernel(const int64_t* draft, const int64_t* argmax, int K, int64_t* accepted,
+                                     int64_t* bonus) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const int b = blockIdx.x;  // one thread per sequence
+  int acc = 0;
+  while (acc < K && draft[(long long)b * K + acc] == argmax[(long long)b * (K + 1) + acc]) ++acc;
+  accepted[b] = acc;
+  bonus[b] = argmax[(long long)b * (K + 1) + acc];
+}
+
+__global__ void __launch_bounds__(RT) accept_rejection_kernel(const __nv_bfloat16* target, const int64_t* draft,
+                                                              const float* q, long long V, int K, float temperature,
+                                                              uint64_t seed, uint32_t offset, const float* stats,
+                                                              int64_t* accepted, int64_t* bonus) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float sm[RT + 32];
+  __shared__ int s_acc;
+  __shared__ int s_any;
+  const int b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (; acc < K; ++acc) {
+      const long long row = (long long)b * (K + 1) + acc;
+      const long long d = draft[(long long)b * K + acc];
+      const float m = stats[2 * row], s = stats[2 * row + 1];
+      const float x = __fdiv_rn(bf2f(target[row * V + d]), temperature);
+      const float p = __fdiv_rn(fm_exp(__fsub_rn(x, m)), s);
+      const float qd = q[((long long)b * K + acc) * V + d];
+      const float u = philox_uniform(seed, (uint32_t)acc, (uint32_t)b, offset, 1u);
+      if (!(__fmul_rn(u, qd) < p)) break;
+    }
+    s_acc = acc;
+    accepted[b] = acc;
+  }
+  __syncthreads();
+  const int acc = s_acc;
+  const long long row = (long long)b * (K + 1) + acc;
+  const __nv_bfloat16* tr = target + row * V;
+  const float m = stats[2 * row], s = stats[2 * row + 1];
+  const float* qr = q + ((long long)b * K + (acc < K ? acc : 0)) * V;
+  auto target_p = [&](long long v) {
+    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(bf2f(tr[v]), temperature), m)), s);
+  };
+  auto residual = [&](long long v) {
+    const float pv = target_p(v);
+    if (acc >= K) return pv;
+    const float dlt = __fsub_rn(pv, qr[v]);
+    return dlt > 0.0f ? dlt : 0.0f;
+  };
+  int any = 0;
+  for (long long v = threadIdx.x; v < V && !any; v += RT) any = residual(v) > 0.0f;
+  if (threadIdx.x == 0) s_any = 0;
+  __syncthreads();
+  if (any) atomicOr(&s_any, 1);
+  __syncthreads();
+  const float u = philox_uniform(seed, 0u, (uint32_t)b, offset, 2u);
+  long long pick;
+  if (s_any)
+    pick = block_categorical(residual, V, u, sm);
+  else
+    pick = block_categorical(target_p, V, u, sm);
+  if (threadIdx.x == 0) bonus[b] = pick;
+}
+
+__global__ void transpose_bf16_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, long long R, long long C) {
+  __shared__ __nv_bfloat16 tile[32][33];
+  const long long r0 = (long long)blockIdx.y * 32, c0 = (long long)blockIdx.x * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long r = r0 + i, c = c0 + threadIdx.x;
+    if (r < R && c < C) tile[i][threadIdx.x] = in[r * C + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const long long c = c0 + i, r = r0 + threadIdx.x;
+    if (r < R && c < C) out[c * R + r] = tile[threadIdx.x][i];
+  }
+}
+
+__global__ void time_sinusoid_kernel(__nv_bfloat16* out, int dim, float s, float t, float scale) {
+  const int half = dim / 2;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= 2 * half) return;
+  const int row = idx / half, i = idx % half;
+  // modeling_flashmap.py:93-96 in fp32
+  const float freq = expf(__fdiv_rn(__fmul_rn(-9.21034037197618273607f, (float)i), (float)half));
+  const float arg = __fmul_rn(__fmul_rn(row == 0 ? s : t, scale), freq);
+  out[row * dim + i] = f2bf(cosf(arg));
+  out[row * dim + half + i] = f2bf(sinf(arg));
+}
+
+__global__ void silu_kernel(const __nv_bfloat16* x, __nv_bfloat16* y, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = bf2f(x[i]);
+  y[i] = f2bf(__fdiv_rn(v, __fadd_rn(1.0f, expf(-v))));
+}
+
+__global__ void add_kernel(const __nv_bfloat16* a, const __nv_bfloat16* b, __nv_bfloat16* y, long long n) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = f2bf(__fadd_rn(bf2f(a[i]), bf2f(b[i])));
+}
+
+inline unsigned blocks_for(long long n, int per) { return (unsigned)((n + per - 1) / per); }
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+fm_status launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int64_t rows,
+                         int64_t cols, float eps, cudaStream_t s, bool pdl) {
+  return launch_kernel(rmsnorm_kernel, dim3((unsigned)rows), dim3(RT), 0, s, pdl, x, w, y, (int)cols, eps);
+}
+fm_status launch_adaln(const __nv_bfloat16* x, const __nv_bfloat16* mod, __nv_bfloat16* y, int64_t rows,
+                       int64_t cols, float eps, cudaStream_t s, bool pdl) {
+  return launch_kernel(adaln_kernel, dim3((unsigned)rows), dim3(RT), 0, s, pdl, x, mod, y, (int)cols, eps);
+}
+fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl) {
+  return launch_kernel(draft_prep_kernel, dim3(a.B), dim3(RT), 0, s, pdl, a);
+}
+fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl) {
+  return launch_kernel(mix_state_kernel, dim3(a.T), dim3(RT), 0, s, pdl, a);
+}
+fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
+                                    cudaStream_t s, bool pdl) {
+  return launch_kernel(philox_normal_bf16_kernel, dim3(blocks_for((count + 1) / 2, 256)), dim3(256), 0, s, pdl,
+                       out, count, seed, offset);
+}
+fm_status launch_philox_normal_f32(float* out, long long count, uint64_t seed, uint32_t offset, cudaStream_t s,
+                                   bool pdl) {
+  return launch_kernel(philox_normal_f32_kernel, dim3(blocks_for((count + 1) / 2, 256)), dim3(256), 0, s, pdl, out,
+                       count, seed, offset);
+}
+fm_status launch_argmax_tokens(const unsigned long long* keys, int64_t* tokens, int n, cudaStream_t s, bool pdl) {
+  return launch_kernel(argmax_tokens_kernel, dim3(blocks_for(n, 128)), dim3(128), 0, s, pdl, keys, tokens, n);
+}
+fm_status launch_state_rows(const float* state, __nv_bfloat16* out, int T, int S, float c, int with_posterior,
+                            cudaStream_t s, bool pdl) {
+  return launch_kernel(state_rows_kernel, dim3(T), dim3(RT), 0, s, pdl, state, out, T, S, c, with_posterior);
+}
+fm_status launch_state_update(float* state, const __nv_bfloat16* logits, long long ldl, int T, int S, float a,
+                              float b, float d, cudaStream_t s, bool pdl) {
+  return launch_kernel(state_update_kernel, dim3(T), dim3(RT), 0, s, pdl, state, logits, ldl, S, a, b, d);
+}
+fm_status launch_extend_prep(const ExtendPrepArgs& a, cudaStream_t s, bool pdl) {
+  return launch_kernel(extend_prep_kernel, dim3(blocks_for(a.rows, 128)), dim3(128), 0, s, pdl, a);
+}
+fm_status launch_extend_commit(const int32_t* cu_rows, int32_t* lengths, int B, cudaStream_t s, bool pdl) {
+  return launch_kernel(extend_commit_kernel, dim3(blocks_for(B, 128)), dim3(128), 0, s, pdl, cu_rows, lengths, B);
+}
+
+fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl);
+fm_status launch_cross_attn(const CrossAttnArgs& a, const CUtensorMap& tm, cudaStream_t stream, bool pdl);
+size_t cross_attn_smem(int hd);
+
+}  // namespace fm
+
+// ====================================================================== C ABI
+using namespace fm;
+
+namespace {
+cudaStream_t as_stream(fm_stream s) { return static_cast<cudaStream_t>(s); }
+const __nv_bfloat16* cbf(const void* p) { return static_cast<const __nv_bfloat16*>(p); }
+__nv_bfloat16* bf(void* p) { return static_cast<__nv_bfloat16*>(p); }
+}  // namespace
+
+extern "C" fm_status fm_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
+                                fm_stream stream) {
+  if (!x || !w || !y) return set_error(FM_ERR_INVALID, "rmsnorm: null pointer");
+  if (rows <= 0 || cols <= 0) return set_error(FM_ERR_SHAPE, "rmsnorm: empty shape");
+  return launch_rmsnorm(cbf(x), cbf(w), bf(y), rows, cols, eps, as_stream(stream), false);
+}
+
+extern "C" fm_status fm_adaln(const void* x, const void* mod, void* y, int64_t rows, int64_t cols, float eps,
+                              fm_stream stream) {
+  if (!x || !mod || !y) return set_error(FM_ERR_INVALID, "adaln: null pointer");
+  if (rows <= 0 || cols <= 0) return set_error(FM_ERR_SHAPE, "adaln: empty shape");
+  return launch_adaln(cbf(x), cbf(mod), bf(y), rows, cols, eps, as_stream(stream), false);
+}
+
+extern "C" fm_status fm_rope_table(float* cos_out, float* sin_out, int64_t max_pos, int64_t head_dim,
+                                   const float* inv_freq, fm_stream stream) {
+  if (!cos_out || !sin_out || !inv_freq) return set_error(FM_ERR_INVALID, "rope_table: null pointer");
+  if (max_pos <= 0 || head_dim <= 0 || head_dim % 2) return set_error(FM_ERR_SHAPE, "rope_table: bad shape");
+  const long long n = max_pos * (head_dim / 2);
+  return launch_kernel(rope_table_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, as_stream(stream), false,
+                       cos_out, sin_out, (int)max_pos, (int)head_dim, inv_freq);
+}
+
+extern "C" fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, uint32_t offset, fm_stream stream) {
+  if (!out) return set_error(FM_ERR_INVALID, "philox_normal: null pointer");
+  if (count <= 0) return FM_OK;
+  return launch_philox_normal_bf16(bf(out), count, seed, offset, as_stream(stream), false);
+}
+
+extern "C" fm_status fm_block_self_attn(const void* qkv, void* out, int64_t batch, int64_t block, int64_t heads,
+                                        int64_t head_dim, fm_stream stream) {
+  if (!qkv || !out) return set_error(FM_ERR_INVALID, "self_attn: null pointer");
+  if (batch <= 0 || block <= 0 || block > 64 || heads <= 0 || head_dim <= 0)
+    return set_error(FM_ERR_SHAPE, "self_attn: bad shape");
+  SelfAttnArgs a{};
+  a.qkv = cbf(qkv);
+  a.out = bf(out);
+  a.block = (int)block;
+  a.heads = (int)heads;
+  a.head_dim = (int)head_dim;
+  a.hidden = (int)(heads * head_dim);
+  a.scale = (float)(1.0 / sqrt((double)head_dim));
+  return launch_self_attn(a, (int)batch, as_stream(stream), false);
+}
+
+extern "C" size_t fm_cross_attn_workspace_size(int64_t batch, int64_t heads, int64_t head_dim, int64_t nsplit) {
+  const size_t counters = ((size_t)batch * heads * sizeof(int) + 255) / 256 * 256;
+  return counters + (size_t)batch * heads * nsplit * (16 * head_dim + 32) * sizeof(float);
+}
+
+extern "C" fm_status fm_cross_attn(const void* q, const void* cache, void* out, const int32_t* lengths,
+                                   int64_t batch, int64_t heads, int64_t head_dim, int64_t layers, int64_t layer,
+                                   int64_t cache_batch, int64_t cache_len, int64_t nsplit, void* workspace,
+                                   size_t workspace_bytes, int32_t* err, fm_stream stream) {
+  if (!q || !cache || !out || !lengths) return set_error(FM_ERR_INVALID, "cross_attn: null pointer");
+  if (nsplit < 1 || layer < 0 || layer >= layers || batch > cache_batch)
+    return set_error(FM_ERR_SHAPE, "cross_attn: bad shape");
+  const size_t need = fm_cross_attn_workspace_size(batch, heads, head_dim, nsplit);
+  if (!workspace || workspace_bytes < need) return set_error(FM_ERR_WORKSPACE, "cross_attn: %zu bytes needed", need);
+  CUtensorMap tm;
+  const uint64_t rows = (uint64_t)layers * 2 * cache_batch * heads * cache_len;
+  fm_status st = make_tmap_bf16(&tm, cache, rows, (uint64_t)head_dim, (uint64_t)head_dim, 64);
+  if (st) return st;
+  CrossAttnArgs a{};
+  a.q = cbf(q);
+  a.out = bf(out);
+  a.lengths = lengths;
+  a.batch = (int)batch;
+  a.heads = (int)heads;
+  a.head_dim = (int)head_dim;
+  a.hidden = (int)(heads * head_dim);
+  a.layer = (int)layer;
+  a.cache_batch = (int)cache_batch;
+  a.cache_len = (int)cache_len;
+  a.nsplit = (int)nsplit;
+  a.scale = (float)(1.0 / sqrt((double)head_dim));
+  const size_t counters = ((size_t)batch * heads * sizeof(int) + 255) / 256 * 256;
+  a.counters = static_cast<int*>(workspace);
+  a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + counters);
+  a.err = err;
+  return launch_cross_attn(a, tm, as_stream(stream), false);
+}
+
+extern "C" fm_status fm_row_stats(const void* logits, int64_t rows, int64_t V, float temperature, float* stats,
+                                  int64_t* argmax, fm_stream stream) {
+  if (!logits) return set_error(FM_ERR_INVALID, "row_stats: null logits");
+  if (rows <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "row_stats: empty shape");
+  return launch_kernel(row_stats_kernel, dim3((unsigned)rows), dim3(RT), 0, as_stream(stream), false, cbf(logits),
+                       (long long)V, temperature, stats, argmax);
+}
+
+extern "C" fm_status fm_softmax_rows(const void* logits, int64_t rows, int64_t V, float temperature, float* probs,
+                                     fm_stream stream) {
+  if (!logits || !probs) return set_error(FM_ERR_INVALID, "softmax_rows: null pointer");
+  if (rows <= 0 || V <= 0 || !(temperature > 0.0f)) return set_error(FM_ERR_SHAPE, "softmax_rows: bad arguments");
+  return launch_kernel(softmax_rows_kernel, dim3((unsigned)rows), dim3(RT), 0, as_stream(stream), false,
+                       cbf(logits), (long long)V, temperature, probs);
+}
+
+extern "C" fm_status fm_sample_rows(const void* logits, const float* probs, int64_t B, int64_t K, int64_t V,
+                                    float temperature, uint64_t seed, uint32_t offset, int64_t* tokens,
+                                    fm_stream stream) {
+  if (!tokens) return set_error(FM_ERR_INVALID, "sample_rows: null tokens");
+  if (B <= 0 || K <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "sample_rows: empty shape");
+  if (temperature <= 0.0f) {
+    if (!logits) return set_error(FM_ERR_INVALID, "sample_rows: null logits");
+    return launch_kernel(row_stats_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false,
+                         cbf(logits), (long long)V, 0.0f, (float*)nullptr, tokens);
+  }
+  if (!probs) return set_error(FM_ERR_INVALID, "sample_rows: T > 0 needs probs");
+  return launch_kernel(sample_rows_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false, probs,
+                       (long long)V, (int)K, seed, offset, tokens);
+}
+
+extern "C" size_t fm_accept_workspace_size(int64_t B, int64_t K) {
+  return (size_t)B * (K + 1) * (2 * sizeof(float) + sizeof(int64_t)) + 256;
+}
+
+extern "C" fm_status fm_accept_greedy(const void* target_logits, const int64_t* draft, int64_t B, int64_t K,
+                                      int64_t V, int64_t* accepted, int64_t* bonus, void* workspace,
+                                      size_t workspace_bytes, fm_stream stream) {
+  if (!target_logits || !draft || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept: null pointer");
+  if (B <= 0 || K <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "accept: empty shape");
+  if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
+    return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
+  int64_t* am = static_cast<int64_t*>(workspace);
+  fm_status st = launch_kernel(row_stats_kernel, dim3((unsigned)(B * (K + 1))), dim3(RT), 0, as_stream(stream),
+                               false, cbf(target_logits), (long long)V, 0.0f, (float*)nullptr, am);
+  if (st) return st;
+  return launch_kernel(accept_greedy_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
+                       (const int64_t*)am, (int)K, accepted, bonus);
+}
+
+extern "C" fm_status fm_accept_rejection(const void* target_logits, const int64_t* draft, const float* q,
+                                         int64_t B, int64_t K, int64_t V, float temperature, uint64_t seed,
+                                         uint32_t offset, int64_t* accepted, int64_t* bonus, void* workspace,
+                                         size_t workspace_bytes, fm_stream stream) {
+  if (!target_logits || !draft || !q || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept: null pointer");
+  if (B <= 0 || K <= 0 || V <= 0 || !(temperature > 0.0f)) return set_error(FM_ERR_SHAPE, "accept: bad arguments");
+  if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
+    return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
+  float* stats = static_cast<float*>(workspace);
+  fm_status st = launch_kernel(row_stats_kernel, dim3((unsigned)(B * (K + 1))), dim3(RT), 0, as_stream(stream),
+                               false, cbf(target_logits), (long long)V, temperature, stats, (int64_t*)nullptr);
+  if (st) return st;
+  return launch_kernel(accept_rejection_kernel, dim3((unsigned)B), dim3(RT), 0, as_stream(stream), false,
+                       cbf(target_logits), draft, q, (long long)V, (int)K, temperature, seed, offset,
+                       (const float*)stats, accepted, bonus);
+}
+
+extern "C" fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, int64_t cols, fm_stream stream) {
+  if (!in || !out) return set_error(FM_ERR_INVALID, "transpose: null pointer");
+  if (rows <= 0 || cols <= 0) return set_error(FM_ERR_SHAPE, "transpose: empty shape");
+  dim3 grid((unsigned)((cols + 31) / 32), (unsigned)((rows + 31) / 32));
+  return launch_kernel(transpose_bf16_kernel, grid, dim3(32, 8), 0, as_stream(stream), false, cbf(in), bf(out),
+                       (long long)rows, (long long)cols);
+}
+
+extern "C" fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, fm_stream stream) {
+  if (!out) return set_error(FM_ERR_INVALID, "time_sinusoid: null pointer");
+  if (dim <= 0 || dim % 2) return set_error(FM_ERR_SHAPE, "time_sinusoid: bad dim");
+  return launch_kernel(time_sinusoid_kernel, dim3(blocks_for(dim, 256)), dim3(256), 0, as_stream(stream), false,
+                       bf(out), (int)dim, s, t, scale);
+}
+
+extern "C" fm_status fm_silu(const void* x, void* y, int64_t n, fm_stream stream) {
+  if (!x || !y) return set_error(FM_ERR_INVALID, "silu: null pointer");
+  if (n <= 0) return FM_OK;
+  return launch_kernel(silu_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, as_stream(stream), false, cbf(x), bf(y),
+                       (long long)n);
+}
+
+extern "C" fm_status fm_add(const void* a, const void* b, void* y, int64_t n, fm_stream stream) {
+  if (!a || !b || !y) return set_error(FM_ERR_INVALID, "add: null pointer");
+  if (n <= 0) return FM_OK;
+  return launch_kernel(add_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, as_stream(stream), false, cbf(a), cbf(b),
+                       bf(y), (long long)n);
+}

@@ -1,0 +1,71 @@
+// Philox4x32-10 counter-based generator and the fixed-order arithmetic the
+// sampling/acceptance kernels share with the CPU oracle.
+//
+// Philox4x32-10: Salmon, Moraes, Dror and Shaw, "Parallel random numbers: as
+// easy as 1, 2, 3" (SC'11); multipliers 0xD2511F53 / 0xCD9E8D57, Weyl key
+// increments 0x9E3779B9 / 0xBB67AE85, ten rounds.
+//
+// fm_exp: e^x by Cody-Waite range reduction (x = n ln2 + r, ln2 split into a
+// 16-bit head and a tail), the degree-7 Taylor polynomial of e^r in Horner
+// form with fused multiply-adds, and an exact power-of-two scale.  Every
+// operation is an explicitly rounded intrinsic, so host C with the same
+// steps reproduces it bit for bit.
+#pragma once
+
+#include "common.cuh"
+
+namespace fm {
+
+struct Philox4 {
+  uint32_t v[4];
+};
+
+__device__ __forceinline__ Philox4 philox4x32_10(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint64_t seed) {
+  uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+#pragma unroll
+  for (int round = 0; round < 10; ++round) {
+    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  Philox4 r;
+  r.v[0] = c0;
+  r.v[1] = c1;
+  r.v[2] = c2;
+  r.v[3] = c3;
+  return r;
+}
+
+// uniform in [0, 1): top 24 bits of word 0 times 2^-24
+__device__ __forceinline__ float philox_uniform(uint64_t seed, uint32_t a, uint32_t b, uint32_t c, uint32_t purpose) {
+  const Philox4 r = philox4x32_10(a, b, c, purpose, seed);
+  return __fmul_rn((float)(r.v[0] >> 8), 5.9604644775390625e-08f);
+}
+
+__device__ __forceinline__ float fm_exp(float x) {
+  if (x != x) return x;
+  if (x > 88.7228394f) return __int_as_float(0x7f800000);
+  if (x < -103.972084f) return 0.0f;
+  const float n = rintf(__fmul_rn(x, 1.44269502162933349609f));
+  float r = __fmaf_rn(-n, 0.693145751953125f, x);
+  r = __fmaf_rn(-n, 1.42860682030941723212e-6f, r);
+  float p = 1.98412698e-4f;
+  p = __fmaf_rn(p, r, 1.38888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int e = (int)n;
+  if (e >= -126) return __fmul_rn(p, __uint_as_float((uint32_t)(e + 127) << 23));
+  return __fmul_rn(__fmul_rn(p, __uint_as_float((uint32_t)(e + 126 + 127) << 23)), __uint_as_float(1u << 23));
+}
+
+}  // namespace fm

@@ -1,0 +1,606 @@
+// The whole drafter pass and extend_context as a fixed launch sequence over
+// caller-owned memory (fm_plan_* / fm_draft / fm_extend_context).
+//
+// One draft (modeling_flashmap.py:422-479, batch B, block K, T = B*K rows):
+//   draft_prep                         anchor embedding rows, positions
+//   anchor_proj GEMM -> anchor_norm    (:453)
+//   cross k|v GEMM of every layer for the anchor row, k-norm + RoPE fused,
+//     written into the cache at position lengths[b]            (:456-457)
+//   one step:  z (Philox) -> z L^T GEMM -> mix_state           (:462-466)
+//   multi-step: state rows -> E_S^T GEMM -> mix_state          (:473, :378-399)
+//   x_embed GEMM, then per layer:                               (:309-311)
+//     adaln -> qkv GEMM (q/k norm + RoPE fused) -> self-attention
+//       -> o GEMM (gated residual fused)
+//     adaln -> q GEMM (norm + RoPE fused) -> cross-attention
+//       -> o GEMM (gated residual fused)
+//     adaln -> fc1/gate_up GEMM (GELU/SwiGLU fused) -> fc2/down GEMM (gated residual)
+//   final adaln -> head GEMM -> LM-head GEMM (logits + argmax fused)  (:312-313, :475)
+//   multi-step: state update between jumps                     (:476-478)
+// Every kernel is launched with programmatic dependent launch on one stream.
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemm_plan.cuh"
+#include "ops.cuh"
+
+namespace fm {
+fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl);
+fm_status launch_cross_attn(const CrossAttnArgs& a, const CUtensorMap& tm, cudaStream_t stream, bool pdl);
+}  // namespace fm
+
+using namespace fm;
+
+struct fm_plan {
+  fm_model_desc m;
+  std::vector<fm_layer_weights> layers;
+  fm_plan_config cfg;
+  std::vector<fm_jump> jumps;
+  int B, K, T, D, H, hd, I, L, Ht, S, ctxw;
+  // workspace carve-out
+  int* err;
+  int* gemm_counters;
+  int* xattn_counters;
+  float* gemm_ws;
+  float* xattn_part;
+  int nsplit;
+  __nv_bfloat16 *anchor_rows, *anchor_h, *anchor_ctx;
+  int *anchor_pos, *anchor_seq, *slot_pos;
+  unsigned long long* keys;
+  __nv_bfloat16 *z, *zl, *inputs, *x, *h, *qkv, *attn, *qc, *mlp, *hidden, *logits_s;
+  float* state;
+  __nv_bfloat16 *srows, *semb;
+  __nv_bfloat16 *ext_fc, *ext_ctx;
+  int *ext_seq, *ext_pos;
+  // launch plans
+  GemmPlan g_anchor_proj, g_anchor_kv, g_zl, g_xembed, g_head, g_lm;
+  GemmPlan g_state_first, g_state_next;
+  std::vector<GemmPlan> g_layer;  // 6 per layer: qkv, o, q, cross_o, mlp1, mlp2
+  CUtensorMap cache_map;
+};
+
+namespace {
+
+struct Carver {
+  char* base;
+  size_t off = 0;
+  template <typename Tp>
+  Tp* take(size_t count) {
+    off = (off + 255) / 256 * 256;
+    Tp* p = base ? reinterpret_cast<Tp*>(base + off) : nullptr;
+    off += count * sizeof(Tp);
+    return p;
+  }
+};
+
+size_t max_gemm_partials(const fm_model_desc* m, const fm_plan_config* c) {
+  const int64_t T = (int64_t)c->batch * m->block, B = c->batch, D = m->hidden, Ht = m->target_hidden;
+  const int64_t I = m->inter, L = m->layers, S = m->state_vocab, R = c->max_extend_rows;
+  const int64_t mlp1 = m->swiglu ? 2 * I : I;
+  size_t mx = 0;
+  auto upd = [&](int64_t M, int64_t N, int64_t K) {
+    if (N <= 0) return;
+    const size_t b = gemm_partials_bytes(M, N, K);
+    if (b > mx) mx = b;
+  };
+  upd(D, B, Ht);
+  upd(L * 2 * D, B, D);
+  upd(Ht, T, Ht);
+  upd(D, T, Ht);
+  upd(3 * D, T, D);
+  upd(D, T, D);
+  upd(mlp1, T, D);
+  upd(D, T, I);
+  upd(Ht, T, D);
+  upd(S, T, Ht);
+  if (c->num_steps > 1) {
+    upd(Ht, T, S);
+    upd(Ht, 2 * T, S);
+  }
+  upd(D, R, (int64_t)m->n_target_layers * Ht);
+  upd(L * 2 * D, R, D);
+  return mx;
+}
+
+size_t max_gemm_tiles(const fm_model_desc* m, const fm_plan_config* c) {
+  const int64_t T = (int64_t)c->batch * m->block, D = m->hidden, Ht = m->target_hidden;
+  const int64_t S = m->state_vocab, L = m->layers, R = c->max_extend_rows, I = m->inter;
+  int64_t mx = 0;
+  auto upd = [&](int64_t M, int64_t N) {
+    if (N <= 0) return;
+    const int bn = gemm_bn_for(N);
+    const int64_t t = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    if (t > mx) mx = t;
+  };
+  upd(S, T);
+  upd(L * 2 * D, R);
+  upd(L * 2 * D, c->batch);
+  upd(2 * I, T);
+  upd(Ht, 2 * T);
+  upd(D, R);
+  return (size_t)mx;
+}
+
+int pick_nsplit(int B, int H, int cache_len) {
+  const int sms = num_sms();
+  int ns = (2 * sms + B * H - 1) / (B * H);
+  const int maxs = (cache_len + 63) / 64;
+  if (ns > maxs) ns = maxs;
+  if (ns < 1) ns = 1;
+  return ns;
+}
+
+// Lay out every buffer; with base == nullptr only the size is computed.
+size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* base) {
+  Carver cv{static_cast<char*>(base)};
+  const int64_t B = c->batch, K = m->block, T = B * K, D = m->hidden, Ht = m->target_hidden;
+  const int64_t I = m->inter, S = m->state_vocab, R = c->max_extend_rows > 0 ? c->max_extend_rows : 1;
+  const int64_t H = m->heads, hd = m->head_dim;
+  const int ns = pick_nsplit((int)B, (int)H, c->cache_len);
+  // zero-initialised region first (counters and the error word)
+  int* err = cv.take<int>(64);
+  int* gc = cv.take<int>(max_gemm_tiles(m, c) + 64);
+  int* xc = cv.take<int>((size_t)B * H + 64);
+  float* gws = cv.take<float>(max_gemm_partials(m, c) / sizeof(float) + 64);
+  float* xp = cv.take<float>((size_t)B * H * ns * (16 * hd + 32));
+  __nv_bfloat16* anchor_rows = cv.take<__nv_bfloat16>(B * Ht);
+  __nv_bfloat16* anchor_h = cv.take<__nv_bfloat16>(B * D);
+  __nv_bfloat16* anchor_ctx = cv.take<__nv_bfloat16>(B * D);
+  int* anchor_pos = cv.take<int>(B);
+  int* anchor_seq = cv.take<int>(B);
+  int* slot_pos = cv.take<int>(T);
+  unsigned long long* keys = cv.take<unsigned long long>(T);
+  __nv_bfloat16* z = cv.take<__nv_bfloat16>(T * Ht);
+  __nv_bfloat16* zl = cv.take<__nv_bfloat16>(T * Ht);
+  __nv_bfloat16* inputs = cv.take<__nv_bfloat16>(T * Ht);
+  __nv_bfloat16* x = cv.take<__nv_bfloat16>(T * D);
+  __nv_bfloat16* h = cv.take<__nv_bfloat16>(T * D);
+  __nv_bfloat16* qkv = cv.take<__nv_bfloat16>(T * 3 * D);
+  __nv_bfloat16* attn = cv.take<__nv_bfloat16>(T * D);
+  __nv_bfloat16* qc = cv.take<__nv_bfloat16>(T * D);
+  __nv_bfloat16* mlp = cv.take<__nv_bfloat16>(T * I);
+  __nv_bfloat16* hidden = cv.take<__nv_bfloat16>(T * Ht);
+  __nv_bfloat16* logits_s = cv.take<__nv_bfloat16>(T * S);
+  float* state = nullptr;
+  __nv_bfloat16 *srows = nullptr, *semb = nullptr;
+  if (c->num_steps > 1) {
+    state = cv.take<float>(T * S);
+    srows = cv.take<__nv_bfloat16>(2 * T * S);
+    semb = cv.take<__nv_bfloat16>(2 * T * Ht);
+  }
+  __nv_bfloat16* ext_fc = cv.take<__nv_bfloat16>(R * D);
+  __nv_bfloat16* ext_ctx = cv.take<__nv_bfloat16>(R * D);
+  int* ext_seq = cv.take<int>(R);
+  int* ext_pos = cv.take<int>(R);
+  if (p) {
+    p->err = err;
+    p->gemm_counters = gc;
+    p->xattn_counters = xc;
+    p->gemm_ws = gws;
+    p->xattn_part = xp;
+    p->nsplit = ns;
+    p->anchor_rows = anchor_rows;
+    p->anchor_h = anchor_h;
+    p->anchor_ctx = anchor_ctx;
+    p->anchor_pos = anchor_pos;
+    p->anchor_seq = anchor_seq;
+    p->slot_pos = slot_pos;
+    p->keys = keys;
+    p->z = z;
+    p->zl = zl;
+    p->inputs = inputs;
+    p->x = x;
+    p->h = h;
+    p->qkv = qkv;
+    p->attn = attn;
+    p->qc = qc;
+    p->mlp = mlp;
+    p->hidden = hidden;
+    p->logits_s = logits_s;
+    p->state = state;
+    p->srows = srows;
+    p->semb = semb;
+    p->ext_fc = ext_fc;
+    p->ext_ctx = ext_ctx;
+    p->ext_seq = ext_seq;
+    p->ext_pos = ext_pos;
+  }
+  return cv.off + 256;
+}
+
+fm_status validate(const fm_model_desc* m, const fm_plan_config* c) {
+  if (!m || !c) return set_error(FM_ERR_INVALID, "plan: null model or config");
+  if (m->hidden <= 0 || m->heads <= 0 || m->head_dim * m->heads != m->hidden)
+    return set_error(FM_ERR_SHAPE, "plan: hidden must equal heads * head_dim");
+  if (m->head_dim != 64 && m->head_dim != 128) return set_error(FM_ERR_UNSUPPORTED, "plan: head_dim must be 64 or 128");
+  if (m->hidden % 128 != 0) return set_error(FM_ERR_UNSUPPORTED, "plan: hidden must be a multiple of 128");
+  if (m->block != 16) return set_error(FM_ERR_UNSUPPORTED, "plan: the kernels serve block_size 16");
+  if (m->swiglu && m->inter % 64 != 0) return set_error(FM_ERR_UNSUPPORTED, "plan: swiglu width must be a multiple of 64");
+  if (m->target_hidden % 8 || m->inter % 8 || m->state_vocab % 8)
+    return set_error(FM_ERR_ALIGN, "plan: widths must be multiples of 8");
+  if (c->batch <= 0 || c->num_steps <= 0 || !c->jumps || !c->cache)
+    return set_error(FM_ERR_INVALID, "plan: bad config");
+  if (c->num_steps > 1 && !m->embed_state_t)
+    return set_error(FM_ERR_INVALID, "plan: multi-step drafts need embed_state_t");
+  if (c->cache_batch < c->batch) return set_error(FM_ERR_SHAPE, "plan: cache batch smaller than plan batch");
+  if (!m->layer || !m->embed || !m->lm_w || !m->chol || !m->rope_cos || !m->rope_sin)
+    return set_error(FM_ERR_INVALID, "plan: missing weights");
+  return FM_OK;
+}
+
+}  // namespace
+
+extern "C" fm_status fm_plan_workspace_size(const fm_model_desc* m, const fm_plan_config* c, size_t* bytes) {
+  fm_status st = validate(m, c);
+  if (st) return st;
+  if (!bytes) return set_error(FM_ERR_INVALID, "plan: null size pointer");
+  *bytes = carve(nullptr, m, c, nullptr);
+  return FM_OK;
+}
+
+extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config* c, void* workspace,
+                                    size_t workspace_bytes, fm_plan** out) {
+  fm_status st = validate(m, c);
+  if (st) return st;
+  if (!out) return set_error(FM_ERR_INVALID, "plan: null output");
+  const size_t need = carve(nullptr, m, c, nullptr);
+  if (!workspace || workspace_bytes < need) return set_error(FM_ERR_WORKSPACE, "plan: workspace of %zu bytes needed", need);
+  fm_plan* p = new (std::nothrow) fm_plan();
+  if (!p) return set_error(FM_ERR_INVALID, "plan: host allocation failed");
+  p->m = *m;
+  p->layers.assign(m->layer, m->layer + m->layers);
+  p->m.layer = p->layers.data();
+  p->cfg = *c;
+  p->jumps.assign(c->jumps, c->jumps + c->num_steps);
+  p->cfg.jumps = p->jumps.data();
+  p->B = c->batch;
+  p->K = m->block;
+  p->T = p->B * p->K;
+  p->D = m->hidden;
+  p->H = m->heads;
+  p->hd = m->head_dim;
+  p->I = m->inter;
+  p->L = m->layers;
+  p->Ht = m->target_hidden;
+  p->S = m->state_vocab;
+  p->ctxw = m->n_target_layers * m->target_hidden;
+  carve(p, m, c, workspace);
+  const int T = p->T, B = p->B, D = p->D, Ht = p->Ht, L = p->L, S = p->S;
+  int* gc = p->gemm_counters;
+  float* ws = p->gemm_ws;
+  int* err = p->err;
+  auto fail = [&](fm_status s) {
+    delete p;
+    return s;
+  };
+  // anchor path
+  if ((st = gemm_prepare(&p->g_anchor_proj, m->anchor_proj_w, D, Ht, Ht, p->anchor_rows, B, Ht, EPI_STORE, ws, gc, err)))
+    return fail(st);
+  p->g_anchor_proj.args.out = p->anchor_h;
+  p->g_anchor_proj.args.ldo = D;
+  p->g_anchor_proj.args.bias = static_cast<const __nv_bfloat16*>(m->anchor_proj_b);
+  if ((st = gemm_prepare(&p->g_anchor_kv, m->cross_kv_w, (int64_t)L * 2 * D, D, D, p->anchor_ctx, B, D, EPI_KVCACHE, ws,
+                         gc, err)))
+    return fail(st);
+  {
+    GemmArgs& a = p->g_anchor_kv.args;
+    a.norm_w0 = static_cast<const __nv_bfloat16*>(m->cross_k_norm);
+    a.norm_layer_stride = p->hd;
+    a.part_rows = D;
+    a.head_dim = p->hd;
+    a.eps = m->qk_eps;
+    a.rope_cos = m->rope_cos;
+    a.rope_sin = m->rope_sin;
+    a.rope_len = m->rope_len;
+    a.positions = p->anchor_pos;
+    a.token_seq = p->anchor_seq;
+    a.cache = static_cast<__nv_bfloat16*>(c->cache);
+    a.cache_batch = c->cache_batch;
+    a.cache_heads = p->H;
+    a.cache_len = c->cache_len;
+  }
+  // noise path
+  if ((st = gemm_prepare(&p->g_zl, m->chol, Ht, Ht, Ht, p->z, T, Ht, EPI_STORE, ws, gc, err))) return fail(st);
+  p->g_zl.args.out = p->zl;
+  p->g_zl.args.ldo = Ht;
+  if (c->num_steps > 1) {
+    if ((st = gemm_prepare(&p->g_state_first, m->embed_state_t, Ht, S, S, p->srows, T, S, EPI_STORE, ws, gc, err)))
+      return fail(st);
+    p->g_state_first.args.out = p->semb;
+    p->g_state_first.args.ldo = Ht;
+    if ((st = gemm_prepare(&p->g_state_next, m->embed_state_t, Ht, S, S, p->srows, 2 * T, S, EPI_STORE, ws, gc, err)))
+      return fail(st);
+    p->g_state_next.args.out = p->semb;
+    p->g_state_next.args.ldo = Ht;
+  }
+  if ((st = gemm_prepare(&p->g_xembed, m->x_embed_w, D, Ht, Ht, p->inputs, T, Ht, EPI_STORE, ws, gc, err)))
+    return fail(st);
+  p->g_xembed.args.out = p->x;
+  p->g_xembed.args.ldo = D;
+  p->g_xembed.args.bias = static_cast<const __nv_bfloat16*>(m->x_embed_b);
+  // layers
+  p->g_layer.resize((size_t)L * 6);
+  const int64_t mlp1_rows = m->swiglu ? 2 * (int64_t)p->I : p->I;
+  for (int l = 0; l < L; ++l) {
+    const fm_layer_weights& w = p->layers[l];
+    GemmPlan* g = &p->g_layer[(size_t)l * 6];
+    if ((st = gemm_prepare(&g[0], w.self_qkv_w, 3 * D, D, D, p->h, T, D, EPI_QKNORM, ws, gc, err))) return fail(st);
+    if ((st = gemm_prepare(&g[1], w.self_o_w, D, D, D, p->attn, T, D, EPI_RESID, ws, gc, err))) return fail(st);
+    if ((st = gemm_prepare(&g[2], w.cross_q_w, D, D, D, p->h, T, D, EPI_QKNORM, ws, gc, err))) return fail(st);
+    if ((st = gemm_prepare(&g[3], w.cross_o_w, D, D, D, p->attn, T, D, EPI_RESID, ws, gc, err))) return fail(st);
+    if ((st = gemm_prepare(&g[4], w.mlp_w1, mlp1_rows, D, D, p->h, T, D, m->swiglu ? EPI_SWIGLU : EPI_GELU, ws, gc,
+                           err)))
+      return fail(st);
+    if ((st = gemm_prepare(&g[5], w.mlp_w2, D, p->I, p->I, p->mlp, T, p->I, EPI_RESID, ws, gc, err))) return fail(st);
+    for (int q = 0; q < 3; q += 2) {
+      GemmArgs& a = g[q].args;
+      a.out = q == 0 ? p->qkv : p->qc;
+      a.ldo = q == 0 ? 3 * D : D;
+      a.norm_w0 = static_cast<const __nv_bfloat16*>(q == 0 ? w.self_q_norm : w.cross_q_norm);
+      a.norm_w1 = static_cast<const __nv_bfloat16*>(q == 0 ? w.self_k_norm : nullptr);
+      a.part_rows = D;
+      a.head_dim = p->hd;
+      a.eps = m->qk_eps;
+      a.rope_cos = m->rope_cos;
+      a.rope_sin = m->rope_sin;
+      a.rope_len = m->rope_len;
+      a.positions = p->slot_pos;
+    }
+    g[1].args.out = p->x;
+    g[1].args.ldo = D;
+    g[3].args.out = p->x;
+    g[3].args.ldo = D;
+    g[4].args.out = p->mlp;
+    g[4].args.ldo = p->I;
+    g[4].args.bias = static_cast<const __nv_bfloat16*>(w.mlp_b1);
+    g[5].args.out = p->x;
+    g[5].args.ldo = D;
+    g[5].args.bias = static_cast<const __nv_bfloat16*>(w.mlp_b2);
+  }
+  if ((st = gemm_prepare(&p->g_head, m->head_w, Ht, D, D, p->h, T, D, EPI_STORE, ws, gc, err))) return fail(st);
+  p->g_head.args.out = p->hidden;
+  p->g_head.args.ldo = Ht;
+  p->g_head.args.bias = static_cast<const __nv_bfloat16*>(m->head_b);
+  if ((st = gemm_prepare(&p->g_lm, m->lm_w, S, Ht, Ht, p->hidden, T, Ht, EPI_LOGITS, ws, gc, err))) return fail(st);
+  p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_b);
+  p->g_lm.args.argmax_keys = p->keys;
+  // the cache as one [rows, head_dim] matrix for the cross-attention TMA
+  const uint64_t rows = (uint64_t)L * 2 * c->cache_batch * p->H * c->cache_len;
+  if ((st = make_tmap_bf16(&p->cache_map, c->cache, rows, (uint64_t)p->hd, (uint64_t)p->hd, 64))) return fail(st);
+  *out = p;
+  return FM_OK;
+}
+
+extern "C" fm_status fm_plan_destroy(fm_plan* p) {
+  delete p;
+  return FM_OK;
+}
+
+extern "C" int32_t* fm_plan_error_word(fm_plan* p) { return p ? p->err : nullptr; }
+
+namespace {
+
+fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s) {
+  const fm_model_desc& m = p->m;
+  const int T = p->T, D = p->D, L = p->L;
+  const __nv_bfloat16* mods = static_cast<const __nv_bfloat16*>(j.mods);
+  fm_status st;
+  if ((st = gemm_launch(p->g_xembed, s, true))) return st;
+  for (int l = 0; l < L; ++l) {
+    GemmPlan* g = &p->g_layer[(size_t)l * 6];
+    const __nv_bfloat16* ms = mods + (size_t)(l * 3 + 0) * 3 * D;
+    const __nv_bfloat16* mc = mods + (size_t)(l * 3 + 1) * 3 * D;
+    const __nv_bfloat16* mm = mods + (size_t)(l * 3 + 2) * 3 * D;
+    if ((st = launch_adaln(p->x, ms, p->h, T, D, m.ln_eps, s, true))) return st;
+    if ((st = gemm_launch(g[0], s, true))) return st;
+    SelfAttnArgs sa{};
+    sa.qkv = p->qkv;
+    sa.out = p->attn;
+    sa.block = p->K;
+    sa.heads = p->H;
+    sa.head_dim = p->hd;
+    sa.hidden = D;
+    sa.scale = (float)(1.0 / std::sqrt((double)p->hd));
+    if ((st = launch_self_attn(sa, p->B, s, true))) return st;
+    GemmPlan go = g[1];
+    go.args.gate = ms + 2 * D;
+    if ((st = gemm_launch(go, s, true))) return st;
+    if ((st = launch_adaln(p->x, mc, p->h, T, D, m.ln_eps, s, true))) return st;
+    if ((st = gemm_launch(g[2], s, true))) return st;
+    CrossAttnArgs ca{};
+    ca.q = p->qc;
+    ca.out = p->attn;
+    ca.batch = p->B;
+    ca.heads = p->H;
+    ca.head_dim = p->hd;
+    ca.hidden = D;
+    ca.layer = l;
+    ca.cache_batch = p->cfg.cache_batch;
+    ca.cache_len = p->cfg.cache_len;
+    ca.nsplit = p->nsplit;
+    ca.scale = sa.scale;
+    ca.part = p->xattn_part;
+    ca.counters = p->xattn_counters;
+    ca.err = p->err;
+    ca.lengths = p->anchor_pos;  // lengths[b], as copied by draft_prep
+    if ((st = launch_cross_attn(ca, p->cache_map, s, true))) return st;
+    GemmPlan gc = g[3];
+    gc.args.gate = mc + 2 * D;
+    if ((st = gemm_launch(gc, s, true))) return st;
+    if ((st = launch_adaln(p->x, mm, p->h, T, D, m.ln_eps, s, true))) return st;
+    if ((st = gemm_launch(g[4], s, true))) return st;
+    GemmPlan gm = g[5];
+    gm.args.gate = mm + 2 * D;
+    if ((st = gemm_launch(gm, s, true))) return st;
+  }
+  const __nv_bfloat16* mf = mods + (size_t)(L * 3) * 3 * D;
+  if ((st = launch_adaln(p->x, mf, p->h, T, D, m.ln_eps, s, true))) return st;
+  return gemm_launch(p->g_head, s, true);
+}
+
+}  // namespace
+
+extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream stream) {
+  if (!p || !io || !io->anchor_ids || !io->lengths) return set_error(FM_ERR_INVALID, "draft: null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const fm_model_desc& m = p->m;
+  const int T = p->T, Ht = p->Ht, S = p->S;
+  fm_status st;
+  DraftPrepArgs pa{};
+  pa.anchor_ids = io->anchor_ids;
+  pa.lengths = io->lengths;
+  pa.embed = static_cast<const __nv_bfloat16*>(m.embed);
+  pa.anchor_rows = p->anchor_rows;
+  pa.anchor_pos = p->anchor_pos;
+  pa.anchor_seq = p->anchor_seq;
+  pa.slot_pos = p->slot_pos;
+  pa.keys = p->keys;
+  pa.B = p->B;
+  pa.K = p->K;
+  pa.Ht = Ht;
+  pa.V = m.vocab;
+  pa.rope_len = m.rope_len;
+  pa.cache_len = p->cfg.cache_len;
+  pa.err = p->err;
+  if ((st = launch_draft_prep(pa, s, true))) return st;
+  if ((st = gemm_launch(p->g_anchor_proj, s, true))) return st;
+  if ((st = launch_rmsnorm(p->anchor_h, static_cast<const __nv_bfloat16*>(m.anchor_norm_w), p->anchor_ctx, p->B,
+                           p->D, m.rms_eps, s, true)))
+    return st;
+  if ((st = gemm_launch(p->g_anchor_kv, s, true))) return st;
+
+  const int n = p->cfg.num_steps;
+  for (int ji = 0; ji < n; ++ji) {
+    const fm_jump& j = p->jumps[ji];
+    MixArgs mx{};
+    mx.state_norm_w = static_cast<const __nv_bfloat16*>(m.state_norm_w);
+    mx.noise_norm_w = static_cast<const __nv_bfloat16*>(m.noise_norm_w);
+    mx.out = p->inputs;
+    mx.gate = j.noise_gate;
+    mx.eps = m.rms_eps;
+    mx.T = T;
+    mx.Ht = Ht;
+    if (n == 1) {
+      if (io->z) {
+        if ((st = check_cuda(cudaMemcpyAsync(p->z, io->z, (size_t)T * Ht * 2, cudaMemcpyDeviceToDevice, s),
+                             "draft: copy z")))
+          return st;
+      } else if ((st = launch_philox_normal_bf16(p->z, (long long)T * Ht, io->seed, io->offset, s, true))) {
+        return st;
+      }
+      if ((st = gemm_launch(p->g_zl, s, true))) return st;
+      mx.post = static_cast<const __nv_bfloat16*>(m.uniform_embeds);
+      mx.post_stride = 0;
+      mx.state = p->zl;
+    } else {
+      if (ji == 0) {
+        if (io->noise) {
+          if ((st = check_cuda(cudaMemcpyAsync(p->state, io->noise, (size_t)T * S * 4, cudaMemcpyDeviceToDevice, s),
+                               "draft: copy noise")))
+            return st;
+        } else if ((st = launch_philox_normal_f32(p->state, (long long)T * S, io->seed, io->offset, s, true))) {
+          return st;
+        }
+      }
+      const int with_post = j.s != 0.0f;
+      const float c = with_post ? (float)((double)j.s / std::pow(std::fmax(1.0 - (double)j.s, 1e-3), 2.0)) : 0.0f;
+      if ((st = launch_state_rows(p->state, p->srows, T, S, c, with_post, s, true))) return st;
+      if ((st = gemm_launch(with_post ? p->g_state_next : p->g_state_first, s, true))) return st;
+      if (with_post) {
+        mx.post = p->semb;
+        mx.post_stride = Ht;
+        mx.state = p->semb + (size_t)T * Ht;
+      } else {
+        mx.post = static_cast<const __nv_bfloat16*>(m.uniform_embeds);
+        mx.post_stride = 0;
+        mx.state = p->semb;
+      }
+    }
+    if ((st = launch_mix_state(mx, s, true))) return st;
+    if ((st = run_dit(p, j, s))) return st;
+    const bool last = ji == n - 1;
+    GemmPlan lm = p->g_lm;
+    lm.args.col_ids = reinterpret_cast<const long long*>(m.draft_ids);  // token ids of the argmax
+    if (last && io->logits) {
+      lm.args.out = static_cast<__nv_bfloat16*>(io->logits);
+      lm.args.ldo = io->ldl;
+      lm.args.scatter = (io->scatter && m.draft_ids) ? 1 : 0;
+    } else {
+      lm.args.out = p->logits_s;
+      lm.args.ldo = S;
+      lm.args.scatter = 0;
+    }
+    lm.args.argmax_keys = last ? p->keys : nullptr;
+    if ((st = gemm_launch(lm, s, true))) return st;
+    if (!last) {
+      const double sd = j.s, nd = j.next;
+      if ((st = launch_state_update(p->state, p->logits_s, S, T, S, (float)(1.0 - nd), (float)(nd - sd),
+                                    (float)(1.0 - sd), s, true)))
+        return st;
+    }
+  }
+  if (io->hidden &&
+      (st = check_cuda(cudaMemcpyAsync(io->hidden, p->hidden, (size_t)T * Ht * 2, cudaMemcpyDeviceToDevice, s),
+                       "draft: copy hidden")))
+    return st;
+  if (io->tokens && (st = launch_argmax_tokens(p->keys, io->tokens, T, s, true))) return st;
+  return FM_OK;
+}
+
+extern "C" fm_status fm_extend_context(fm_plan* p, const fm_extend_io* io, fm_stream stream) {
+  if (!p || !io || !io->target_hidden || !io->cu_rows || !io->lengths)
+    return set_error(FM_ERR_INVALID, "extend_context: null argument");
+  if (io->rows <= 0) return FM_OK;
+  if (io->rows > p->cfg.max_extend_rows)
+    return set_error(FM_ERR_SHAPE, "extend_context: %d rows exceed the plan's %d", io->rows, p->cfg.max_extend_rows);
+  if (io->batch <= 0 || io->batch > p->cfg.cache_batch) return set_error(FM_ERR_SHAPE, "extend_context: bad batch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const fm_model_desc& m = p->m;
+  const int D = p->D, L = p->L, R = io->rows;
+  fm_status st;
+  ExtendPrepArgs ea{};
+  ea.cu_rows = io->cu_rows;
+  ea.lengths = io->lengths;
+  ea.token_seq = p->ext_seq;
+  ea.positions = p->ext_pos;
+  ea.rows = R;
+  ea.B = io->batch;
+  ea.rope_len = m.rope_len;
+  ea.cache_len = p->cfg.cache_len;
+  ea.err = p->err;
+  if ((st = launch_extend_prep(ea, s, true))) return st;
+  GemmPlan g_fc, g_kv;
+  if ((st = gemm_prepare(&g_fc, m.fc_w, D, p->ctxw, p->ctxw, io->target_hidden, R, p->ctxw, EPI_STORE, p->gemm_ws,
+                         p->gemm_counters, p->err)))
+    return st;
+  g_fc.args.out = p->ext_fc;
+  g_fc.args.ldo = D;
+  if ((st = gemm_launch(g_fc, s, true))) return st;
+  if ((st = launch_rmsnorm(p->ext_fc, static_cast<const __nv_bfloat16*>(m.hidden_norm_w), p->ext_ctx, R, D, m.rms_eps,
+                           s, true)))
+    return st;
+  if ((st = gemm_prepare(&g_kv, m.cross_kv_w, (int64_t)L * 2 * D, D, D, p->ext_ctx, R, D, EPI_KVCACHE, p->gemm_ws,
+                         p->gemm_counters, p->err)))
+    return st;
+  {
+    GemmArgs& a = g_kv.args;
+    a.norm_w0 = static_cast<const __nv_bfloat16*>(m.cross_k_norm);
+    a.norm_layer_stride = p->hd;
+    a.part_rows = D;
+    a.head_dim = p->hd;
+    a.eps = m.qk_eps;
+    a.rope_cos = m.rope_cos;
+    a.rope_sin = m.rope_sin;
+    a.rope_len = m.rope_len;
+    a.positions = p->ext_pos;
+    a.token_seq = p->ext_seq;
+    a.cache = static_cast<__nv_bfloat16*>(p->cfg.cache);
+    a.cache_batch = p->cfg.cache_batch;
+    a.cache_heads = p->H;
+    a.cache_len = p->cfg.cache_len;
+  }
+  if ((st = gemm_launch(g_kv, s, true))) return st;
+  return launch_extend_commit(io->cu_rows, io->lengths, io->batch, s, true);
+}

@@ -1,0 +1,276 @@
+/*
+ * flashmap_b200 — C ABI of the B200 (sm_100a) FlashMap drafter hot path.
+ *
+ * The reference (al-jshen/flashmap v0.2.1) is pure Python; its hot path is
+ * FlashMapDraftModel.draft()/forward()/extend_context() and the acceptance
+ * block of spec_generate() in flashmap/modeling_flashmap.py, plus the
+ * torch.library operators of its serving plugins.  Each entry point below
+ * names the reference interface it replaces.
+ *
+ * Conventions
+ *   - Every function returns fm_status (0 = FM_OK).  fm_last_error() gives a
+ *     thread-local message for the last failure.  Nothing aborts or traps;
+ *     device-side problems (an index out of range, a wait that ran out) are
+ *     written to the caller's int32 error word, read back with the stream
+ *     synchronised.
+ *   - The caller owns all memory: weights, caches, workspaces and outputs
+ *     are device pointers it allocated.  No entry point allocates device
+ *     memory; plans hold host memory only (TMA descriptors, sizes).
+ *   - All kernels run on the given CUDA stream (0 = legacy default) with no
+ *     host synchronisation, so sequences of calls can be captured in a CUDA
+ *     graph.  Per-step values that change between replays (anchor ids,
+ *     cache lengths) are read from device memory.
+ *   - Tensors are row-major and contiguous unless a leading dimension is
+ *     given.  bf16 = 16-bit bfloat16 stored as uint16_t.
+ */
+#ifndef FLASHMAP_B200_H_
+#define FLASHMAP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define FM_API __attribute__((visibility("default")))
+#else
+#define FM_API
+#endif
+
+typedef int fm_status;
+enum {
+  FM_OK = 0,
+  FM_ERR_INVALID = 1,     /* null pointer / bad argument */
+  FM_ERR_SHAPE = 2,       /* unsupported or inconsistent shape */
+  FM_ERR_ALIGN = 3,       /* pointer or stride misaligned for TMA (16 bytes) */
+  FM_ERR_ARCH = 4,        /* device is not sm_100 */
+  FM_ERR_LAUNCH = 5,      /* kernel launch failed */
+  FM_ERR_CUDA = 6,        /* other CUDA runtime error */
+  FM_ERR_UNSUPPORTED = 7, /* configuration outside what the kernels serve */
+  FM_ERR_WORKSPACE = 8    /* workspace too small */
+};
+
+typedef void* fm_stream; /* cudaStream_t */
+
+FM_API const char* fm_last_error(void);
+FM_API int fm_version(void);
+/* 0 when the current device is an sm_100 part this library was built for. */
+FM_API fm_status fm_check_device(void);
+
+/* ------------------------------------------------------------------------
+ * Primitive operators (unit-test entry points and building blocks).
+ * ------------------------------------------------------------------------ */
+
+/* Epilogue selectors of fm_gemm_bf16. */
+enum {
+  FM_EPI_STORE = 0, /* out = bf16(X W^T + bias) */
+  FM_EPI_GELU = 1,  /* out = bf16(gelu(bf16(X W^T + bias))) */
+  FM_EPI_SWIGLU = 2,/* W rows interleaved per 128 (64 gate, 64 up): out = bf16(bf16(silu(g)) * u) */
+  FM_EPI_RESID = 3, /* out += bf16(gate * bf16(X W^T + bias)) (in place, bf16 rounding per op) */
+  FM_EPI_F32 = 7    /* out (fp32) = X W^T */
+};
+
+/* Y = X W^T with a fused epilogue, on tcgen05 tensor cores.
+ * Replaces the nn.Linear calls of modeling_flashmap.py (:89-90, 105,
+ * 129-132, 159-163, 250-264) and F.linear of the LM head (:475).
+ *   W   [M, K] bf16 (nn.Linear layout), X [N, K] bf16 (tokens), K % 8 == 0
+ *   out [N, ldo] bf16 (fp32 for FM_EPI_F32); bias/gate [M] bf16 or NULL
+ *   workspace: fm_gemm_workspace_size() bytes; counters must be zero on the
+ *   first call and are left zero after every call. */
+FM_API size_t fm_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
+FM_API fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K, int64_t ldo,
+                       const void* bias, const void* gate, int epilogue, void* workspace, size_t workspace_bytes,
+                       int32_t* err, fm_stream stream);
+
+/* RMSNorm of modeling_flashmap.py:69-80: y = x * bf16(w * rsqrt(mean(x^2) + eps)). */
+FM_API fm_status fm_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
+                     fm_stream stream);
+
+/* AdaLN of modeling_flashmap.py:112-115 (LayerNorm without affine, then
+ * * (1 + scale) + shift, each op rounded to bf16). mod = [scale|shift|gate] x D. */
+FM_API fm_status fm_adaln(const void* x, const void* mod, void* y, int64_t rows, int64_t cols, float eps,
+                   fm_stream stream);
+
+/* RoPE tables of modeling_flashmap.py:53-58: cos/sin[pos][i] of the fp32 angle pos * inv_freq[i],
+ * inv_freq [head_dim/2] = 1 / theta^(2i/head_dim) as the reference computes it (fp32). */
+FM_API fm_status fm_rope_table(float* cos_out, float* sin_out, int64_t max_pos, int64_t head_dim,
+                               const float* inv_freq, fm_stream stream);
+
+/* Philox4x32-10 standard normals (Box-Muller) rounded to bf16: the draft noise z
+ * of modeling_flashmap.py:465.  Elements 2p and 2p+1 use counter (p, 0, offset, 4). */
+FM_API fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, uint32_t offset, fm_stream stream);
+
+/* Self-attention over the block slots (modeling_flashmap.py:188 with :144-147);
+ * qkv [B*K, 3*D] with q, k already normed and rotated. Replaces the
+ * flashmap_vllm::block_self_attention / flashmap_sglang::block_self_attention ops. */
+FM_API fm_status fm_block_self_attn(const void* qkv, void* out, int64_t batch, int64_t block, int64_t heads,
+                             int64_t head_dim, fm_stream stream);
+
+/* Cross-attention of the 16 block slots of each sequence over its context cache
+ * positions 0..lengths[b] (modeling_flashmap.py:190, :218-219).  Replaces
+ * flashmap_vllm::paged_cross_attention (vllm/model.py:93) for a dense cache.
+ *   cache (L, 2, cache_batch, heads, cache_len, head_dim) bf16; q/out [B*16, heads*head_dim]
+ *   workspace: fm_cross_attn_workspace_size() bytes (counters zero). */
+FM_API size_t fm_cross_attn_workspace_size(int64_t batch, int64_t heads, int64_t head_dim, int64_t nsplit);
+FM_API fm_status fm_cross_attn(const void* q, const void* cache, void* out, const int32_t* lengths, int64_t batch,
+                        int64_t heads, int64_t head_dim, int64_t layers, int64_t layer, int64_t cache_batch,
+                        int64_t cache_len, int64_t nsplit, void* workspace, size_t workspace_bytes, int32_t* err,
+                        fm_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Sampling and acceptance (modeling_flashmap.py:553-557, :579-594).
+ * Randomness: Philox4x32-10 keyed by seed; counters documented per call.
+ * ------------------------------------------------------------------------ */
+
+/* Per-row max m and sum of exp(x/T - m) (fixed reduction order) and the first
+ * argmax of bf16 rows. stats [rows][2] fp32, argmax [rows] int64 (either may be NULL). */
+FM_API fm_status fm_row_stats(const void* logits, int64_t rows, int64_t V, float temperature, float* stats,
+                       int64_t* argmax, fm_stream stream);
+
+/* probs = softmax(logits / T) in fp32, rows of V (draft_probs of :556). */
+FM_API fm_status fm_softmax_rows(const void* logits, int64_t rows, int64_t V, float temperature, float* probs,
+                          fm_stream stream);
+
+/* Draft tokens: T <= 0 argmax; else a categorical draw from probs (row r = b*K + k
+ * uses uniform counter (k, b, offset, 3)). tokens [B*K] int64. */
+FM_API fm_status fm_sample_rows(const void* logits, const float* probs, int64_t B, int64_t K, int64_t V,
+                         float temperature, uint64_t seed, uint32_t offset, int64_t* tokens, fm_stream stream);
+
+/* Greedy acceptance (:579-582). target_logits [B, K+1, V] bf16, draft [B, K] int64
+ * -> accepted [B], bonus [B] (int64). */
+FM_API fm_status fm_accept_greedy(const void* target_logits, const int64_t* draft, int64_t B, int64_t K, int64_t V,
+                           int64_t* accepted, int64_t* bonus, void* workspace, size_t workspace_bytes,
+                           fm_stream stream);
+
+/* Rejection acceptance (:583-594). q [B, K, V] fp32 draft probabilities.
+ * u[b,k] = uniform (k, b, offset, 1); bonus draw uniform (0, b, offset, 2). */
+FM_API size_t fm_accept_workspace_size(int64_t B, int64_t K);
+FM_API fm_status fm_accept_rejection(const void* target_logits, const int64_t* draft, const float* q, int64_t B,
+                              int64_t K, int64_t V, float temperature, uint64_t seed, uint32_t offset,
+                              int64_t* accepted, int64_t* bonus, void* workspace, size_t workspace_bytes,
+                              fm_stream stream);
+
+/* Helpers of the one-time constants (time conditioning, embedding transpose). */
+FM_API fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, int64_t cols, fm_stream stream);
+/* rows 0 and 1: [cos | sin] of (s resp. t) * scale * 10000^(-i/(dim/2)) (modeling_flashmap.py:92-96) */
+FM_API fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, fm_stream stream);
+FM_API fm_status fm_silu(const void* x, void* y, int64_t n, fm_stream stream);
+FM_API fm_status fm_add(const void* a, const void* b, void* y, int64_t n, fm_stream stream);
+
+/* ------------------------------------------------------------------------
+ * The whole drafter: a plan over caller-owned weights and buffers.
+ * ------------------------------------------------------------------------ */
+
+typedef struct fm_layer_weights {
+  const void* self_qkv_w;  /* [3D, D]: q_proj; k_proj; v_proj rows */
+  const void* self_o_w;    /* [D, D] */
+  const void* self_q_norm; /* [hd] */
+  const void* self_k_norm; /* [hd] */
+  const void* cross_q_w;   /* [D, D] */
+  const void* cross_o_w;   /* [D, D] */
+  const void* cross_q_norm;/* [hd] */
+  const void* mlp_w1;      /* gelu: fc1 [I, D]; swiglu: gate_up [2I, D] interleaved per 64 rows */
+  const void* mlp_b1;      /* gelu: fc1 bias [I]; swiglu: NULL */
+  const void* mlp_w2;      /* fc2 / down_proj [D, I] */
+  const void* mlp_b2;      /* fc2 bias [D] or NULL */
+} fm_layer_weights;
+
+typedef struct fm_model_desc {
+  int32_t hidden, heads, head_dim, inter, layers, target_hidden, n_target_layers, block;
+  int32_t vocab;       /* target vocabulary V */
+  int32_t state_vocab; /* S: rows of lm_head/embedding the state lives on (= V without draft_ids) */
+  int32_t swiglu;      /* 0 gelu, 1 swiglu */
+  float rms_eps, qk_eps, ln_eps;
+  const void* fc_w;          /* [D, n_target_layers*Ht] */
+  const void* hidden_norm_w; /* [D] */
+  const void* anchor_proj_w; /* [D, Ht] */
+  const void* anchor_proj_b; /* [D] */
+  const void* anchor_norm_w; /* [D] */
+  const void* noise_norm_w;  /* [Ht] */
+  const void* x_embed_w;     /* [D, Ht] */
+  const void* x_embed_b;     /* [D] */
+  const void* head_w;        /* [Ht, D] */
+  const void* head_b;        /* [Ht] */
+  const void* cross_kv_w;    /* [L*2*D, D]: per layer cross k_proj then v_proj */
+  const void* cross_k_norm;  /* [L, hd] */
+  const fm_layer_weights* layer; /* host array of L entries */
+  const void* embed;         /* target embedding [V, Ht] */
+  const void* lm_w;          /* state-vocab rows of the target lm_head [S, Ht] */
+  const void* lm_b;          /* [S] or NULL */
+  const int64_t* draft_ids;  /* [S] ids into V, or NULL (S == V) */
+  const void* embed_state_t; /* E_S^T [Ht, S] (multi-step drafts), or NULL */
+  const void* chol;          /* L with L L^T = E_S^T E_S, [Ht, Ht] lower triangular */
+  const void* uniform_embeds;/* bf16(1/S) summed over E_S rows: the s = 0 posterior embedding [Ht] */
+  const void* state_norm_w;  /* [Ht] */
+  const float* rope_cos;     /* [rope_len, hd/2] */
+  const float* rope_sin;
+  int32_t rope_len;
+} fm_model_desc;
+
+/* One jump of a draft: its modulations and noise-gate value. */
+typedef struct fm_jump {
+  const void* mods;  /* [(3L+1), 3, D] bf16: per layer (self, cross, mlp), then final; each scale|shift|gate */
+  float noise_gate;  /* bf16-rounded noise_gate * (t - s) (or noise_gate for "constant") */
+  float s, next;     /* start time and the time the state moves to (next == 1: last jump) */
+} fm_jump;
+
+typedef struct fm_plan_config {
+  int32_t batch;        /* sequences drafted together */
+  int32_t num_steps;    /* jumps per draft */
+  const fm_jump* jumps; /* host array of num_steps entries */
+  void* cache;          /* (L, 2, cache_batch, heads, cache_len, hd) bf16 */
+  int32_t cache_batch, cache_len;
+  int32_t max_extend_rows; /* largest extend_context call (rows over all sequences) */
+} fm_plan_config;
+
+typedef struct fm_plan fm_plan;
+
+/* Device workspace the plan needs (bytes). */
+FM_API fm_status fm_plan_workspace_size(const fm_model_desc* model, const fm_plan_config* cfg, size_t* bytes);
+/* Build a plan over caller-owned memory (host allocation only). The workspace
+ * must stay valid for the plan's lifetime; its first bytes must be zero. */
+FM_API fm_status fm_plan_create(const fm_model_desc* model, const fm_plan_config* cfg, void* workspace,
+                         size_t workspace_bytes, fm_plan** plan);
+FM_API fm_status fm_plan_destroy(fm_plan* plan);
+/* Device error word of the plan (int32, 0 = none). */
+FM_API int32_t* fm_plan_error_word(fm_plan* plan);
+
+typedef struct fm_draft_io {
+  const int64_t* anchor_ids; /* [B] device */
+  const int32_t* lengths;    /* [B] device: verified positions per sequence */
+  const void* z;             /* [B*K, Ht] bf16 one-step noise, or NULL (drawn by Philox) */
+  const float* noise;        /* [B*K, S] fp32 multi-step start state, or NULL (drawn) */
+  uint64_t seed;
+  uint32_t offset;           /* Philox counter word 2 for this draft */
+  void* logits;              /* [B*K, ldl] bf16 output or NULL */
+  int64_t ldl;               /* logits row stride (V, or S when not scattering) */
+  int32_t scatter;           /* 1: write at draft_ids columns of a V-wide row */
+  int64_t* tokens;           /* [B*K] argmax tokens (target ids) or NULL */
+  void* hidden;              /* [B*K, Ht] bf16 DiT output of the last jump, or NULL */
+} fm_draft_io;
+
+/* One draft of the whole block (modeling_flashmap.py:422-479): the anchor row
+ * of every layer's context, the noise, all jumps of the DiT, the LM head and
+ * the argmax.  Replaces FlashMapDraftModel.draft/forward and the plugins'
+ * forward + compute_draft_logits (vllm/model.py:991-1045). */
+FM_API fm_status fm_draft(fm_plan* plan, const fm_draft_io* io, fm_stream stream);
+
+typedef struct fm_extend_io {
+  const void* target_hidden; /* [rows, n_target_layers*Ht] bf16 */
+  int32_t rows;
+  const int32_t* cu_rows;    /* [B+1] device: rows of sequence b are cu_rows[b]..cu_rows[b+1] */
+  int32_t* lengths;          /* [B] device: rows are written at lengths[b].., then lengths += n_b */
+  int32_t batch;
+} fm_extend_io;
+
+/* extend_context (modeling_flashmap.py:342-351): fc, hidden_norm, then every
+ * layer's cross k (k_norm + RoPE) and v written into the cache. */
+FM_API fm_status fm_extend_context(fm_plan* plan, const fm_extend_io* io, fm_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHMAP_B200_H_ */

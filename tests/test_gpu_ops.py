@@ -1,0 +1,299 @@
+"""GPU parity of the primitive kernels against fp32 torch math and the CPU oracle.
+
+Tolerances: bf16 outputs may differ from an fp32-accumulated reference only
+by the order of fp32 summation, so at most one bf16 unit in the last place
+and on a small fraction of elements; fp32 GEMM outputs within 1e-4 relative.
+Sampling and acceptance are bit-exact against the C oracle.
+"""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():  # collected on CPU, skipped there
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from flashmap_b200 import _lib, ops  # noqa: E402
+from oracle import accept as oracle_accept  # noqa: E402
+from oracle import flashmap_oracle as O  # noqa: E402
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device_ok():
+    _lib.require_device()
+
+
+def bf16_ulp(x: torch.Tensor) -> torch.Tensor:
+    """Size of one bf16 unit in the last place at |x| (fp32 tensor)."""
+    e = torch.floor(torch.log2(x.abs().clamp_min(1e-30)))
+    return torch.pow(2.0, e - 7)
+
+
+def assert_bf16_close(got: torch.Tensor, ref: torch.Tensor, max_ulps=1, min_exact=0.98, what=""):
+    g, r = got.float(), ref.float()
+    assert g.shape == r.shape
+    assert torch.isfinite(g).all(), f"{what}: non-finite output"
+    diff = (g - r).abs()
+    tol = max_ulps * bf16_ulp(torch.maximum(g.abs(), r.abs())) + 1e-30
+    bad = diff > tol
+    if bad.any():
+        idx = bad.nonzero()[:8].tolist()
+        detail = "; ".join(f"{tuple(i)}: got {g[tuple(i)].item():.8g} ref {r[tuple(i)].item():.8g}" for i in idx)
+        raise AssertionError(f"{what}: {int(bad.sum())} elements beyond {max_ulps} ulp: {detail}")
+    exact = (g == r).float().mean().item()
+    assert exact >= min_exact, f"{what}: only {exact:.4f} of elements bit-equal"
+
+
+def assert_close_scaled(got, ref, ulps=1, atol_frac=1e-5, what="", extra_tol=None):
+    """|got - ref| <= ulps * ulp(ref) + atol_frac * max|ref| (+ extra_tol): rounding
+    differences only, with an absolute floor for values that cancel to ~0."""
+    g, r = got.float(), ref.float()
+    assert g.shape == r.shape
+    assert torch.isfinite(g).all(), f"{what}: non-finite output"
+    tol = ulps * bf16_ulp(r) + atol_frac * r.abs().max().clamp_min(1e-30)
+    if extra_tol is not None:
+        tol = tol + extra_tol
+    bad = (g - r).abs() > tol
+    if bad.any():
+        idx = bad.nonzero()[:8].tolist()
+        detail = "; ".join(f"{tuple(i)}: got {g[tuple(i)].item():.8g} ref {r[tuple(i)].item():.8g}" for i in idx)
+        raise AssertionError(f"{what}: {int(bad.sum())} elements out of tolerance: {detail}")
+
+
+def rand(shape, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(shape, generator=g, device=DEV) * scale).to(torch.bfloat16)
+
+
+GEMM_SHAPES = [
+    (128, 1, 64), (256, 16, 256), (2048, 16, 2048), (3000, 17, 320), (6144, 16, 2048), (2048, 16, 8192),
+    (16384, 16, 4096), (512, 64, 1024), (512, 128, 1024), (1024, 200, 512), (2048, 1024, 2048), (384, 2048, 256),
+    (4096, 5, 4096),
+]
+
+
+@pytest.mark.parametrize("M,N,K", GEMM_SHAPES)
+def test_gemm_store_bias(M, N, K):
+    W = rand((M, K), 1 / math.sqrt(K), 1)
+    X = rand((N, K), 1.0, 2)
+    b = rand((M,), 0.1, 3)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.gemm(W, X, ops.STORE, bias=b, err=err)
+    acc = X.float() @ W.float().T + b.float()
+    ref = acc.to(torch.bfloat16)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    # near a rounding boundary the fp32 sums of two summation orders may round apart
+    near = ((acc - ref.float()).abs() > 0.45 * bf16_ulp(acc)).float().mean().item()
+    assert_close_scaled(out, ref, ulps=1, atol_frac=1e-5, what=f"gemm {M}x{N}x{K} (near-boundary {near:.4f})")
+    assert (out == ref).float().mean().item() > 0.98
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512)])
+def test_gemm_fp32_and_determinism(M, N, K):
+    W = rand((M, K), 1 / math.sqrt(K), 4)
+    X = rand((N, K), 1.0, 5)
+    a = ops.gemm(W, X, ops.F32)
+    b = ops.gemm(W, X, ops.F32)
+    ref = X.float() @ W.float().T
+    assert torch.equal(a, b), "split-K reduction must not depend on arrival order"
+    torch.testing.assert_close(a, ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("N", [16, 64, 300])
+def test_gemm_gelu(N):
+    M, K = 8192, 2048
+    W = rand((M, K), 1 / math.sqrt(K), 6)
+    X = rand((N, K), 1.0, 7)
+    b = rand((M,), 0.1, 8)
+    out = ops.gemm(W, X, ops.GELU, bias=b)
+    y = (X.float() @ W.float().T + b.float()).to(torch.bfloat16).float()
+    ref = (0.5 * y * (1.0 + torch.erf(y * 0.7071067811865476))).to(torch.bfloat16)
+    # a one-ulp flip of the rounded pre-activation y moves gelu by about gelu'(y) * ulp(y)
+    assert_close_scaled(out, ref, ulps=2, atol_frac=1e-5, what="gelu", extra_tol=1.2 * bf16_ulp(y))
+    assert (out == ref).float().mean().item() > 0.97
+
+
+@pytest.mark.parametrize("N", [16, 48])
+def test_gemm_swiglu(N):
+    I, K = 384, 256
+    Wg = rand((I, K), 1 / math.sqrt(K), 9)
+    Wu = rand((I, K), 1 / math.sqrt(K), 10)
+    W = torch.stack([Wg.view(I // 64, 64, K), Wu.view(I // 64, 64, K)], dim=1).reshape(2 * I, K).contiguous()
+    X = rand((N, K), 1.0, 11)
+    out = ops.gemm(W, X, ops.SWIGLU)
+    g = (X.float() @ Wg.float().T).to(torch.bfloat16)
+    u = (X.float() @ Wu.float().T).to(torch.bfloat16)
+    ref = (torch.nn.functional.silu(g.float()).to(torch.bfloat16).float() * u.float()).to(torch.bfloat16)
+    assert_bf16_close(out, ref, max_ulps=2, min_exact=0.97, what="swiglu")
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (2048, 16, 8192), (256, 1024, 512)])
+def test_gemm_gated_residual(M, N, K):
+    W = rand((M, K), 1 / math.sqrt(K), 12)
+    X = rand((N, K), 1.0, 13)
+    b = rand((M,), 0.1, 14)
+    gate = rand((M,), 0.5, 15)
+    x0 = rand((N, M), 1.0, 16)
+    out = x0.clone()
+    ops.gemm(W, X, ops.RESID, bias=b, gate=gate, out=out)
+    y = (X.float() @ W.float().T + b.float()).to(torch.bfloat16)
+    gy = (gate.float() * y.float()).to(torch.bfloat16)
+    ref = (x0.float() + gy.float()).to(torch.bfloat16)
+    # a one-ulp flip of the rounded y moves gate*y by |gate| ulp(y), plus its own rounding
+    extra = gate.float().abs() * bf16_ulp(y.float()) + bf16_ulp(gy.float())
+    assert_close_scaled(out, ref, ulps=1, atol_frac=1e-5, what="residual", extra_tol=extra)
+    assert (out == ref).float().mean().item() > 0.97
+
+
+def test_rmsnorm_matches_oracle():
+    x = rand((37, 4096), 2.0, 20)
+    w = (1 + 0.1 * rand((4096,), 1.0, 21).float()).to(torch.bfloat16)
+    got = ops.rmsnorm(x, w, 1e-6)
+    ref = O.rms_norm(x.cpu(), w.cpu(), 1e-6)
+    assert_bf16_close(got.cpu(), ref, max_ulps=1, min_exact=0.995, what="rmsnorm")
+
+
+def test_adaln_matches_oracle():
+    D = 2048
+    x = rand((16, D), 3.0, 22)
+    mod = rand((3 * D,), 0.5, 23)
+    got = ops.adaln(x, mod, 1e-6)
+    scale, shift, gate = mod.cpu().view(1, 3 * D).chunk(3, dim=-1)
+    ref, _ = O.ada_layer_norm(x.cpu(), (scale, shift, gate), 1e-6)
+    assert_bf16_close(got.cpu(), ref, max_ulps=1, min_exact=0.995, what="adaln")
+
+
+@pytest.mark.parametrize("hd,theta", [(128, 10000.0), (64, 1e6)])
+def test_rope_table_matches_oracle(hd, theta):
+    cs, sn = ops.rope_table(9000, hd, theta)
+    pos = torch.arange(9000)[None]
+    rc, rs = O.rope_tables(pos, hd, theta)
+    torch.testing.assert_close(cs.cpu(), rc[0, :, 0], rtol=0, atol=2e-6)
+    torch.testing.assert_close(sn.cpu(), rs[0, :, 0], rtol=0, atol=2e-6)
+
+
+def test_philox_normal_statistics_and_determinism():
+    a = ops.philox_normal((64, 4096), seed=1234, offset=3)
+    b = ops.philox_normal((64, 4096), seed=1234, offset=3)
+    c = ops.philox_normal((64, 4096), seed=1234, offset=4)
+    assert torch.equal(a, b) and not torch.equal(a, c)
+    f = a.float()
+    assert abs(f.mean().item()) < 0.01 and abs(f.std().item() - 1.0) < 0.01
+
+
+def sdpa_ref(q, k, v):
+    """fp32 softmax attention with bf16-rounded numerators (the CPU flash order)."""
+    s = (q.float() @ k.float().transpose(-1, -2)) * (1.0 / math.sqrt(q.shape[-1]))
+    m = s.max(-1, keepdim=True).values
+    e = torch.exp(s - m)
+    return ((e.to(torch.bfloat16).float() @ v.float()) / e.sum(-1, keepdim=True)).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("B,H,hd", [(1, 16, 128), (3, 4, 64)])
+def test_block_self_attention(B, H, hd):
+    D = H * hd
+    qkv = rand((B * 16, 3 * D), 1.0, 30)
+    got = ops.block_self_attn(qkv, B, 16, H, hd)
+    q, k, v = qkv.view(B, 16, 3, H, hd).permute(2, 0, 3, 1, 4)
+    ref = sdpa_ref(q, k, v).permute(0, 2, 1, 3).reshape(B * 16, D)
+    assert_bf16_close(got, ref, max_ulps=2, min_exact=0.95, what="self-attn")
+    # and against the reference's own op (torch SDPA on the CPU)
+    cpu = torch.nn.functional.scaled_dot_product_attention(q.cpu(), k.cpu(), v.cpu())
+    cpu = cpu.permute(0, 2, 1, 3).reshape(B * 16, D)
+    assert_close_scaled(got.cpu(), cpu, ulps=2, atol_frac=2 ** -8, what="self-attn vs CPU SDPA")
+
+
+@pytest.mark.parametrize("B,H,hd,lens,nsplit", [
+    (1, 16, 128, [2048], 0), (1, 16, 128, [2048], 1), (3, 4, 64, [0, 17, 129], 0), (2, 20, 128, [4096, 1023], 3),
+    (4, 16, 128, [63, 64, 65, 4000], 0),
+])
+def test_cross_attention(B, H, hd, lens, nsplit):
+    L, Tc = 2, max(lens) + 20
+    cache = rand((L, 2, B + 1, H, Tc, hd), 1.0, 40)
+    q = rand((B * 16, H * hd), 1.0, 41)
+    lengths = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for layer in range(L):
+        got = ops.cross_attn(q, cache, lengths, layer, nsplit, err=err)
+        for b, n in enumerate(lens):
+            k = cache[layer, 0, b, :, : n + 1]
+            v = cache[layer, 1, b, :, : n + 1]
+            qb = q[b * 16 : (b + 1) * 16].view(16, H, hd).transpose(0, 1)
+            ref = sdpa_ref(qb, k, v).transpose(0, 1).reshape(16, H * hd)
+            # numerators are rounded to bf16 relative to a running (per split) maximum
+            assert_close_scaled(got[b * 16 : (b + 1) * 16], ref, ulps=2, atol_frac=2 ** -9,
+                                what=f"cross-attn b={b} len={n}")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+
+
+# ------------------------------------------------------------------ sampling / acceptance (bit-exact)
+
+@pytest.mark.parametrize("V", [2048, 3001, 151936])
+def test_row_stats_and_softmax_bit_exact(V):
+    logits = (2.0 * torch.randn(5, V, generator=torch.Generator().manual_seed(V))).to(torch.bfloat16)
+    stats, am = ops.row_stats(logits.to(DEV), 0.7)
+    for r in range(5):
+        m, s = oracle_accept.row_stats(logits[r], 0.7)
+        assert stats[r, 0].item() == m and stats[r, 1].item() == s
+        assert am[r].item() == int(logits[r].argmax())
+    probs = ops.softmax_rows(logits.to(DEV), 0.7).cpu()
+    assert torch.equal(probs, oracle_accept.softmax_rows(logits, 0.7))
+
+
+@pytest.mark.parametrize("V,T", [(2048, 1.0), (3001, 0.7), (151936, 1.0)])
+def test_sample_rows_bit_exact(V, T):
+    B, K = 2, 16
+    logits = (2.0 * torch.randn(B, K, V, generator=torch.Generator().manual_seed(7))).to(torch.bfloat16)
+    ld = logits.to(DEV)
+    probs = ops.softmax_rows(ld, T)
+    toks = ops.sample_rows(ld, probs, T, seed=1234, offset=5).cpu()
+    ref, _ = oracle_accept.sample_rows(logits, T, seed=1234, offset=5)
+    assert torch.equal(toks, ref)
+    greedy = ops.sample_rows(ld, None, 0.0, 1234, 5).cpu()
+    assert torch.equal(greedy, logits.argmax(-1))
+
+
+@pytest.mark.parametrize("B,K,V,seed", [(34, 16, 3001, 5), (8, 16, 151936, 11)])
+def test_accept_greedy_bit_exact(B, K, V, seed):
+    from tests.golden.inputs import acceptance_inputs
+
+    target, draft, _ = acceptance_inputs(B, K, V, seed, 0.0)
+    acc, bonus = ops.accept_greedy(target.to(DEV), draft.to(DEV))
+    racc, rbonus = oracle_accept.accept_greedy(target, draft)
+    assert acc.cpu().tolist() == racc.tolist() and bonus.cpu().tolist() == rbonus.tolist()
+
+
+@pytest.mark.parametrize("B,K,V,seed,T", [(24, 16, 3001, 6, 1.0), (24, 16, 2048, 7, 0.7), (6, 16, 151936, 9, 1.0)])
+def test_accept_rejection_bit_exact(B, K, V, seed, T):
+    from tests.golden.inputs import acceptance_inputs
+
+    target, draft, q = acceptance_inputs(B, K, V, seed, T)
+    acc, bonus = ops.accept_rejection(target.to(DEV), draft.to(DEV), q.to(DEV), T, seed=1234, offset=0)
+    racc, rbonus = oracle_accept.accept_rejection(target, draft, q, T, seed=1234, offset=0)
+    assert acc.cpu().tolist() == racc.tolist()
+    assert bonus.cpu().tolist() == rbonus.tolist()
+
+
+def test_acceptance_golden_cases_through_cuda():
+    """The reference's own acceptance decisions (golden file) reproduced on the GPU."""
+    import os
+
+    from tests.golden.inputs import acceptance_inputs
+
+    cases = torch.load(os.path.join(os.path.dirname(__file__), "golden", "acceptance_cases.pt"))
+    for name, c in cases.items():
+        target, draft, q = acceptance_inputs(c["B"], c["K"], c["V"], c["seed"], c["temperature"])
+        if c["temperature"] <= 0:
+            acc, bonus = ops.accept_greedy(target.to(DEV), draft.to(DEV))
+        else:
+            acc, bonus = ops.accept_rejection(target.to(DEV), draft.to(DEV), q.to(DEV), c["temperature"],
+                                              seed=c["rng_seed"], offset=0)
+        assert acc.cpu().tolist() == c["accepted"], name
+        assert bonus.cpu().tolist() == c["bonus"], name
