@@ -56,6 +56,11 @@ class DraftIO(ctypes.Structure):
                 ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p)]
 
 
+class ForwardIO(ctypes.Structure):
+    _fields_ = [("inputs", c_void_p), ("positions", c_void_p), ("ctx_last", c_void_p), ("mods", c_void_p),
+                ("hidden", c_void_p)]
+
+
 class ExtendIO(ctypes.Structure):
     _fields_ = [("target_hidden", c_void_p), ("rows", c_int32), ("cu_rows", c_void_p), ("lengths", c_void_p),
                 ("batch", c_int32)]
@@ -76,17 +81,17 @@ _SIGNATURES = {
     "fm_cross_attn_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
     "fm_cross_attn": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                               c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p, c_void_p]),
-    "fm_row_stats": (c_int, [c_void_p, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
-    "fm_softmax_rows": (c_int, [c_void_p, c_int64, c_int64, c_float, c_void_p, c_void_p]),
-    "fm_sample_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_uint64, c_uint32, c_void_p,
-                               c_void_p]),
+    "fm_row_stats": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
+    "fm_softmax_rows": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p]),
+    "fm_sample_rows": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_float, c_uint64, c_uint32,
+                               c_void_p, c_void_p]),
     "fm_accept_workspace_size": (c_size_t, [c_int64, c_int64]),
-    "fm_accept_greedy": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
-                                 c_size_t, c_void_p]),
-    "fm_accept_rejection": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_uint64,
-                                    c_uint32, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "fm_accept_greedy": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                 c_void_p, c_size_t, c_void_p]),
+    "fm_accept_rejection": (c_int, [c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float,
+                                    c_uint64, c_uint32, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "fm_transpose_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
-    "fm_time_sinusoid": (c_int, [c_void_p, c_int64, c_float, c_float, c_float, c_void_p]),
+    "fm_time_sinusoid": (c_int, [c_void_p, c_int64, c_float, c_float, c_float, c_void_p, c_void_p]),
     "fm_silu": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "fm_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "fm_plan_workspace_size": (c_int, [ctypes.POINTER(ModelDesc), ctypes.POINTER(PlanConfig),
@@ -97,6 +102,7 @@ _SIGNATURES = {
     "fm_plan_error_word": (c_void_p, [c_void_p]),
     "fm_draft": (c_int, [c_void_p, ctypes.POINTER(DraftIO), c_void_p]),
     "fm_extend_context": (c_int, [c_void_p, ctypes.POINTER(ExtendIO), c_void_p]),
+    "fm_forward": (c_int, [c_void_p, ctypes.POINTER(ForwardIO), c_void_p]),
 }
 
 _lib = None

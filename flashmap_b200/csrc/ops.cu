@@ -64,9 +64,25 @@ __device__ __forceinline__ int block_max_int(int v, int* red) {
   return r;
 }
 
-// 8 consecutive bf16 of a row (vector `vec`), zero-padded past V
-__device__ __forceinline__ void load8_bf16(const __nv_bfloat16* row, long long vec, long long V, bool aligned,
-                                           float* x) {
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return bf2f(v); }
+__device__ __forceinline__ float to_f(float v) { return v; }
+
+// 8 consecutive elements of a row (vector `vec`), zero-padded past V
+__device__ __forceinline__ void load8(const float* row, long long vec, long long V, bool aligned, float* x) {
+  const long long v0 = vec * 8;
+  if (aligned && v0 + 8 <= V) {
+    const float4 a = *reinterpret_cast<const float4*>(row + v0);
+    const float4 b = *reinterpret_cast<const float4*>(row + v0 + 4);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = (v0 + j < V) ? row[v0 + j] : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* row, long long vec, long long V, bool aligned,
+                                      float* x) {
   const long long v0 = vec * 8;
   if (aligned && v0 + 8 <= V) {
     const uint4 raw = *reinterpret_cast<const uint4*>(row + v0);
@@ -83,7 +99,8 @@ __device__ __forceinline__ void load8_bf16(const __nv_bfloat16* row, long long v
 }
 
 // max of x/T, and (first) argmax of the raw values, over one row
-__device__ void row_max_argmax(const __nv_bfloat16* row, long long V, float temperature, float* red, float* m_out,
+template <typename T>
+__device__ void row_max_argmax(const T* row, long long V, float temperature, float* red, float* m_out,
                                long long* arg_out) {
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const long long nvec = (V + 7) / 8;
@@ -91,7 +108,7 @@ __device__ void row_max_argmax(const __nv_bfloat16* row, long long V, float temp
   long long bi = V;  // sentinel larger than any index
   for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
     float x[8];
-    load8_bf16(row, vec, V, aligned, x);
+    load8(row, vec, V, aligned, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const long long v = vec * 8 + j;
@@ -136,13 +153,14 @@ __device__ void row_max_argmax(const __nv_bfloat16* row, long long V, float temp
 }
 
 // fixed-order sum of fm_exp(x/T - m): thread i walks vectors i, i+256, ...
-__device__ float row_sumexp(const __nv_bfloat16* row, long long V, float temperature, float m, float* red) {
+template <typename T>
+__device__ float row_sumexp(const T* row, long long V, float temperature, float m, float* red) {
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const long long nvec = (V + 7) / 8;
   float acc = 0.0f;
   for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
     float x[8];
-    load8_bf16(row, vec, V, aligned, x);
+    load8(row, vec, V, aligned, x);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       if (vec * 8 + j >= V) break;
@@ -437,12 +455,13 @@ __global__ void extend_commit_kernel(const int32_t* cu, int32_t* lengths, int B)
 
 // ------------------------------------------------------------------ sampling / acceptance
 
-__global__ void __launch_bounds__(RT) row_stats_kernel(const __nv_bfloat16* logits, long long V, float temperature,
+template <typename T>
+__global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long long V, float temperature,
                                                        float* stats, int64_t* argmax) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
-  const __nv_bfloat16* row = logits + (long long)blockIdx.x * V;
+  const T* row = logits + (long long)blockIdx.x * V;
   float m;
   long long am;
   row_max_argmax(row, V, temperature, red, &m, &am);
@@ -456,19 +475,20 @@ __global__ void __launch_bounds__(RT) row_stats_kernel(const __nv_bfloat16* logi
   }
 }
 
-__global__ void __launch_bounds__(RT) softmax_rows_kernel(const __nv_bfloat16* logits, long long V,
-                                                          float temperature, float* probs) {
+template <typename T>
+__global__ void __launch_bounds__(RT) softmax_rows_kernel(const T* logits, long long V, float temperature,
+                                                          float* probs) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
-  const __nv_bfloat16* row = logits + (long long)blockIdx.x * V;
+  const T* row = logits + (long long)blockIdx.x * V;
   float m;
   long long am;
   row_max_argmax(row, V, temperature, red, &m, &am);
   const float s = row_sumexp(row, V, temperature, m, red);
   float* pr = probs + (long long)blockIdx.x * V;
   for (long long v = threadIdx.x; v < V; v += RT)
-    pr[v] = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(bf2f(row[v]), temperature), m)), s);
+    pr[v] = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(to_f(row[v]), temperature), m)), s);
 }
 
 __global__ void __launch_bounds__(RT) sample_rows_kernel(const float* probs, long long V, int K, uint64_t seed,
@@ -494,7 +514,8 @@ __global__ void accept_greedy_kernel(const int64_t* draft, const int64_t* argmax
   bonus[b] = argmax[(long long)b * (K + 1) + acc];
 }
 
-__global__ void __launch_bounds__(RT) accept_rejection_kernel(const __nv_bfloat16* target, const int64_t* draft,
+template <typename T>
+__global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, const int64_t* draft,
                                                               const float* q, long long V, int K, float temperature,
                                                               uint64_t seed, uint32_t offset, const float* stats,
                                                               int64_t* accepted, int64_t* bonus) {
@@ -510,7 +531,7 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const __nv_bfloat1
       const long long row = (long long)b * (K + 1) + acc;
       const long long d = draft[(long long)b * K + acc];
       const float m = stats[2 * row], s = stats[2 * row + 1];
-      const float x = __fdiv_rn(bf2f(target[row * V + d]), temperature);
+      const float x = __fdiv_rn(to_f(target[row * V + d]), temperature);
       const float p = __fdiv_rn(fm_exp(__fsub_rn(x, m)), s);
       const float qd = q[((long long)b * K + acc) * V + d];
       const float u = philox_uniform(seed, (uint32_t)acc, (uint32_t)b, offset, 1u);
@@ -522,11 +543,11 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const __nv_bfloat1
   __syncthreads();
   const int acc = s_acc;
   const long long row = (long long)b * (K + 1) + acc;
-  const __nv_bfloat16* tr = target + row * V;
+  const T* tr = target + row * V;
   const float m = stats[2 * row], s = stats[2 * row + 1];
   const float* qr = q + ((long long)b * K + (acc < K ? acc : 0)) * V;
   auto target_p = [&](long long v) {
-    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(bf2f(tr[v]), temperature), m)), s);
+    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(to_f(tr[v]), temperature), m)), s);
   };
   auto residual = [&](long long v) {
     const float pv = target_p(v);
@@ -563,14 +584,13 @@ __global__ void transpose_bf16_kernel(const __nv_bfloat16* in, __nv_bfloat16* ou
   }
 }
 
-__global__ void time_sinusoid_kernel(__nv_bfloat16* out, int dim, float s, float t, float scale) {
+__global__ void time_sinusoid_kernel(__nv_bfloat16* out, int dim, float s, float t, float scale, const float* freqs) {
   const int half = dim / 2;
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= 2 * half) return;
   const int row = idx / half, i = idx % half;
-  // modeling_flashmap.py:93-96 in fp32
-  const float freq = expf(__fdiv_rn(__fmul_rn(-9.21034037197618273607f, (float)i), (float)half));
-  const float arg = __fmul_rn(__fmul_rn(row == 0 ? s : t, scale), freq);
+  // modeling_flashmap.py:95-96 in fp32: (t * scale) * freq
+  const float arg = __fmul_rn(__fmul_rn(row == 0 ? s : t, scale), freqs[i]);
   out[row * dim + i] = f2bf(cosf(arg));
   out[row * dim + half + i] = f2bf(sinf(arg));
 }
@@ -732,31 +752,42 @@ extern "C" fm_status fm_cross_attn(const void* q, const void* cache, void* out, 
   return launch_cross_attn(a, tm, as_stream(stream), false);
 }
 
-extern "C" fm_status fm_row_stats(const void* logits, int64_t rows, int64_t V, float temperature, float* stats,
-                                  int64_t* argmax, fm_stream stream) {
+namespace {
+// launch a kernel template instantiated for bf16 (dtype 0) or fp32 (dtype 1) logits
+#define FM_DISPATCH_LOGITS(dtype, KERNEL, grid, ptr, ...)                                                      \
+  ((dtype) == 0 ? launch_kernel(KERNEL<__nv_bfloat16>, grid, dim3(RT), 0, as_stream(stream), false,            \
+                                static_cast<const __nv_bfloat16*>(ptr), __VA_ARGS__)                           \
+                : launch_kernel(KERNEL<float>, grid, dim3(RT), 0, as_stream(stream), false,                   \
+                                static_cast<const float*>(ptr), __VA_ARGS__))
+bool bad_dtype(int32_t d) { return d != 0 && d != 1; }
+}  // namespace
+
+extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
+                                  float* stats, int64_t* argmax, fm_stream stream) {
   if (!logits) return set_error(FM_ERR_INVALID, "row_stats: null logits");
-  if (rows <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "row_stats: empty shape");
-  return launch_kernel(row_stats_kernel, dim3((unsigned)rows), dim3(RT), 0, as_stream(stream), false, cbf(logits),
-                       (long long)V, temperature, stats, argmax);
+  if (rows <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "row_stats: bad arguments");
+  return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), logits, (long long)V, temperature, stats,
+                            argmax);
 }
 
-extern "C" fm_status fm_softmax_rows(const void* logits, int64_t rows, int64_t V, float temperature, float* probs,
-                                     fm_stream stream) {
+extern "C" fm_status fm_softmax_rows(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
+                                     float* probs, fm_stream stream) {
   if (!logits || !probs) return set_error(FM_ERR_INVALID, "softmax_rows: null pointer");
-  if (rows <= 0 || V <= 0 || !(temperature > 0.0f)) return set_error(FM_ERR_SHAPE, "softmax_rows: bad arguments");
-  return launch_kernel(softmax_rows_kernel, dim3((unsigned)rows), dim3(RT), 0, as_stream(stream), false,
-                       cbf(logits), (long long)V, temperature, probs);
+  if (rows <= 0 || V <= 0 || !(temperature > 0.0f) || bad_dtype(dtype))
+    return set_error(FM_ERR_SHAPE, "softmax_rows: bad arguments");
+  return FM_DISPATCH_LOGITS(dtype, softmax_rows_kernel, dim3((unsigned)rows), logits, (long long)V, temperature,
+                            probs);
 }
 
-extern "C" fm_status fm_sample_rows(const void* logits, const float* probs, int64_t B, int64_t K, int64_t V,
-                                    float temperature, uint64_t seed, uint32_t offset, int64_t* tokens,
+extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const float* probs, int64_t B, int64_t K,
+                                    int64_t V, float temperature, uint64_t seed, uint32_t offset, int64_t* tokens,
                                     fm_stream stream) {
   if (!tokens) return set_error(FM_ERR_INVALID, "sample_rows: null tokens");
-  if (B <= 0 || K <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "sample_rows: empty shape");
+  if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "sample_rows: bad arguments");
   if (temperature <= 0.0f) {
     if (!logits) return set_error(FM_ERR_INVALID, "sample_rows: null logits");
-    return launch_kernel(row_stats_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false,
-                         cbf(logits), (long long)V, 0.0f, (float*)nullptr, tokens);
+    return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * K)), logits, (long long)V, 0.0f,
+                              (float*)nullptr, tokens);
   }
   if (!probs) return set_error(FM_ERR_INVALID, "sample_rows: T > 0 needs probs");
   return launch_kernel(sample_rows_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false, probs,
@@ -767,36 +798,36 @@ extern "C" size_t fm_accept_workspace_size(int64_t B, int64_t K) {
   return (size_t)B * (K + 1) * (2 * sizeof(float) + sizeof(int64_t)) + 256;
 }
 
-extern "C" fm_status fm_accept_greedy(const void* target_logits, const int64_t* draft, int64_t B, int64_t K,
-                                      int64_t V, int64_t* accepted, int64_t* bonus, void* workspace,
+extern "C" fm_status fm_accept_greedy(const void* target_logits, int32_t dtype, const int64_t* draft, int64_t B,
+                                      int64_t K, int64_t V, int64_t* accepted, int64_t* bonus, void* workspace,
                                       size_t workspace_bytes, fm_stream stream) {
   if (!target_logits || !draft || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept: null pointer");
-  if (B <= 0 || K <= 0 || V <= 0) return set_error(FM_ERR_SHAPE, "accept: empty shape");
+  if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "accept: bad arguments");
   if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
     return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
   int64_t* am = static_cast<int64_t*>(workspace);
-  fm_status st = launch_kernel(row_stats_kernel, dim3((unsigned)(B * (K + 1))), dim3(RT), 0, as_stream(stream),
-                               false, cbf(target_logits), (long long)V, 0.0f, (float*)nullptr, am);
+  fm_status st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits,
+                                    (long long)V, 0.0f, (float*)nullptr, am);
   if (st) return st;
   return launch_kernel(accept_greedy_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
                        (const int64_t*)am, (int)K, accepted, bonus);
 }
 
-extern "C" fm_status fm_accept_rejection(const void* target_logits, const int64_t* draft, const float* q,
-                                         int64_t B, int64_t K, int64_t V, float temperature, uint64_t seed,
-                                         uint32_t offset, int64_t* accepted, int64_t* bonus, void* workspace,
-                                         size_t workspace_bytes, fm_stream stream) {
+extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtype, const int64_t* draft,
+                                         const float* q, int64_t B, int64_t K, int64_t V, float temperature,
+                                         uint64_t seed, uint32_t offset, int64_t* accepted, int64_t* bonus,
+                                         void* workspace, size_t workspace_bytes, fm_stream stream) {
   if (!target_logits || !draft || !q || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept: null pointer");
-  if (B <= 0 || K <= 0 || V <= 0 || !(temperature > 0.0f)) return set_error(FM_ERR_SHAPE, "accept: bad arguments");
+  if (B <= 0 || K <= 0 || V <= 0 || !(temperature > 0.0f) || bad_dtype(dtype))
+    return set_error(FM_ERR_SHAPE, "accept: bad arguments");
   if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
     return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
   float* stats = static_cast<float*>(workspace);
-  fm_status st = launch_kernel(row_stats_kernel, dim3((unsigned)(B * (K + 1))), dim3(RT), 0, as_stream(stream),
-                               false, cbf(target_logits), (long long)V, temperature, stats, (int64_t*)nullptr);
+  fm_status st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits,
+                                    (long long)V, temperature, stats, (int64_t*)nullptr);
   if (st) return st;
-  return launch_kernel(accept_rejection_kernel, dim3((unsigned)B), dim3(RT), 0, as_stream(stream), false,
-                       cbf(target_logits), draft, q, (long long)V, (int)K, temperature, seed, offset,
-                       (const float*)stats, accepted, bonus);
+  return FM_DISPATCH_LOGITS(dtype, accept_rejection_kernel, dim3((unsigned)B), target_logits, draft, q, (long long)V,
+                            (int)K, temperature, seed, offset, (const float*)stats, accepted, bonus);
 }
 
 extern "C" fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, int64_t cols, fm_stream stream) {
@@ -807,11 +838,12 @@ extern "C" fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, 
                        (long long)rows, (long long)cols);
 }
 
-extern "C" fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, fm_stream stream) {
-  if (!out) return set_error(FM_ERR_INVALID, "time_sinusoid: null pointer");
+extern "C" fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, const float* freqs,
+                                      fm_stream stream) {
+  if (!out || !freqs) return set_error(FM_ERR_INVALID, "time_sinusoid: null pointer");
   if (dim <= 0 || dim % 2) return set_error(FM_ERR_SHAPE, "time_sinusoid: bad dim");
   return launch_kernel(time_sinusoid_kernel, dim3(blocks_for(dim, 256)), dim3(256), 0, as_stream(stream), false,
-                       bf(out), (int)dim, s, t, scale);
+                       bf(out), (int)dim, s, t, scale, freqs);
 }
 
 extern "C" fm_status fm_silu(const void* x, void* y, int64_t n, fm_stream stream) {

@@ -59,6 +59,7 @@ struct fm_plan {
   GemmPlan g_state_first, g_state_next;
   std::vector<GemmPlan> g_layer;  // 6 per layer: qkv, o, q, cross_o, mlp1, mlp2
   CUtensorMap cache_map;
+  bool has_target;
 };
 
 namespace {
@@ -222,11 +223,10 @@ fm_status validate(const fm_model_desc* m, const fm_plan_config* c) {
     return set_error(FM_ERR_ALIGN, "plan: widths must be multiples of 8");
   if (c->batch <= 0 || c->num_steps <= 0 || !c->jumps || !c->cache)
     return set_error(FM_ERR_INVALID, "plan: bad config");
-  if (c->num_steps > 1 && !m->embed_state_t)
+  if (c->num_steps > 1 && m->embed && !m->embed_state_t)
     return set_error(FM_ERR_INVALID, "plan: multi-step drafts need embed_state_t");
   if (c->cache_batch < c->batch) return set_error(FM_ERR_SHAPE, "plan: cache batch smaller than plan batch");
-  if (!m->layer || !m->embed || !m->lm_w || !m->chol || !m->rope_cos || !m->rope_sin)
-    return set_error(FM_ERR_INVALID, "plan: missing weights");
+  if (!m->layer || !m->rope_cos || !m->rope_sin) return set_error(FM_ERR_INVALID, "plan: missing weights");
   return FM_OK;
 }
 
@@ -301,11 +301,14 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
     a.cache_heads = p->H;
     a.cache_len = c->cache_len;
   }
+  p->has_target = m->embed && m->lm_w && m->chol && m->uniform_embeds;
   // noise path
-  if ((st = gemm_prepare(&p->g_zl, m->chol, Ht, Ht, Ht, p->z, T, Ht, EPI_STORE, ws, gc, err))) return fail(st);
+  if (p->has_target &&
+      (st = gemm_prepare(&p->g_zl, m->chol, Ht, Ht, Ht, p->z, T, Ht, EPI_STORE, ws, gc, err)))
+    return fail(st);
   p->g_zl.args.out = p->zl;
   p->g_zl.args.ldo = Ht;
-  if (c->num_steps > 1) {
+  if (c->num_steps > 1 && p->has_target) {
     if ((st = gemm_prepare(&p->g_state_first, m->embed_state_t, Ht, S, S, p->srows, T, S, EPI_STORE, ws, gc, err)))
       return fail(st);
     p->g_state_first.args.out = p->semb;
@@ -363,9 +366,12 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
   p->g_head.args.out = p->hidden;
   p->g_head.args.ldo = Ht;
   p->g_head.args.bias = static_cast<const __nv_bfloat16*>(m->head_b);
-  if ((st = gemm_prepare(&p->g_lm, m->lm_w, S, Ht, Ht, p->hidden, T, Ht, EPI_LOGITS, ws, gc, err))) return fail(st);
-  p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_b);
-  p->g_lm.args.argmax_keys = p->keys;
+  if (p->has_target) {
+    if ((st = gemm_prepare(&p->g_lm, m->lm_w, S, Ht, Ht, p->hidden, T, Ht, EPI_LOGITS, ws, gc, err)))
+      return fail(st);
+    p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_b);
+    p->g_lm.args.argmax_keys = p->keys;
+  }
   // the cache as one [rows, head_dim] matrix for the cross-attention TMA
   const uint64_t rows = (uint64_t)L * 2 * c->cache_batch * p->H * c->cache_len;
   if ((st = make_tmap_bf16(&p->cache_map, c->cache, rows, (uint64_t)p->hd, (uint64_t)p->hd, 64))) return fail(st);
@@ -442,8 +448,29 @@ fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s) {
 
 }  // namespace
 
+extern "C" fm_status fm_forward(fm_plan* p, const fm_forward_io* io, fm_stream stream) {
+  if (!p || !io || !io->inputs || !io->positions || !io->ctx_last || !io->mods || !io->hidden)
+    return set_error(FM_ERR_INVALID, "forward: null argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t T = (size_t)p->T;
+  fm_status st;
+  if ((st = check_cuda(cudaMemcpyAsync(p->inputs, io->inputs, T * p->Ht * 2, cudaMemcpyDeviceToDevice, s),
+                       "forward: inputs")) ||
+      (st = check_cuda(cudaMemcpyAsync(p->slot_pos, io->positions, T * 4, cudaMemcpyDeviceToDevice, s),
+                       "forward: positions")) ||
+      (st = check_cuda(cudaMemcpyAsync(p->anchor_pos, io->ctx_last, (size_t)p->B * 4, cudaMemcpyDeviceToDevice, s),
+                       "forward: context")))
+    return st;
+  fm_jump j{};
+  j.mods = io->mods;
+  if ((st = run_dit(p, j, s))) return st;
+  return check_cuda(cudaMemcpyAsync(io->hidden, p->hidden, T * p->Ht * 2, cudaMemcpyDeviceToDevice, s),
+                    "forward: hidden");
+}
+
 extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream stream) {
   if (!p || !io || !io->anchor_ids || !io->lengths) return set_error(FM_ERR_INVALID, "draft: null argument");
+  if (!p->has_target) return set_error(FM_ERR_INVALID, "draft: the plan was built without the target's weights");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const fm_model_desc& m = p->m;
   const int T = p->T, Ht = p->Ht, S = p->S;

@@ -26,6 +26,12 @@ def _stream():
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
+def _logits_dtype(t) -> int:
+    if not t.is_cuda or not t.is_contiguous() or t.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"logits must be a contiguous CUDA bf16 or fp32 tensor, got {t.dtype} on {t.device}")
+    return 0 if t.dtype == torch.bfloat16 else 1
+
+
 def _need(t, dtype, name):
     if t is None:
         return
@@ -120,47 +126,48 @@ def cross_attn(q, cache_kv, lengths, layer: int, nsplit: int = 0, err=None):
 
 
 def row_stats(logits, temperature: float):
-    _need(logits, torch.bfloat16, "logits")
+    dt = _logits_dtype(logits)
     V = logits.shape[-1]
     rows = logits.numel() // V
     stats = torch.empty(rows, 2, device=logits.device, dtype=torch.float32)
     am = torch.empty(rows, device=logits.device, dtype=torch.int64)
-    _lib.call("fm_row_stats", _p(logits), rows, V, float(temperature), _p(stats), _p(am), _stream())
+    _lib.call("fm_row_stats", _p(logits), dt, rows, V, float(temperature), _p(stats), _p(am), _stream())
     return stats, am
 
 
 def softmax_rows(logits, temperature: float):
-    _need(logits, torch.bfloat16, "logits")
+    dt = _logits_dtype(logits)
     V = logits.shape[-1]
     probs = torch.empty(logits.shape, device=logits.device, dtype=torch.float32)
-    _lib.call("fm_softmax_rows", _p(logits), logits.numel() // V, V, float(temperature), _p(probs), _stream())
+    _lib.call("fm_softmax_rows", _p(logits), dt, logits.numel() // V, V, float(temperature), _p(probs), _stream())
     return probs
 
 
 def sample_rows(logits, probs, temperature: float, seed: int, offset: int):
     """Draft tokens (B, K) from logits (B, K, V): argmax at T <= 0, else drawn from probs."""
     B, K, V = logits.shape
+    dt = _logits_dtype(logits)
     tokens = torch.empty(B, K, device=logits.device, dtype=torch.int64)
-    _lib.call("fm_sample_rows", _p(logits), _p(probs), B, K, V, float(temperature), int(seed), int(offset),
+    _lib.call("fm_sample_rows", _p(logits), dt, _p(probs), B, K, V, float(temperature), int(seed), int(offset),
               _p(tokens), _stream())
     return tokens
 
 
 def accept_greedy(target_logits, draft):
-    _need(target_logits, torch.bfloat16, "target_logits")
+    dt = _logits_dtype(target_logits)
     _need(draft, torch.int64, "draft")
     B, K1, V = target_logits.shape
     acc = torch.empty(B, device=draft.device, dtype=torch.int64)
     bonus = torch.empty_like(acc)
     wsb = _lib.load().fm_accept_workspace_size(B, K1 - 1)
     ws = torch.empty(wsb, dtype=torch.uint8, device=draft.device)
-    _lib.call("fm_accept_greedy", _p(target_logits), _p(draft), B, K1 - 1, V, _p(acc), _p(bonus), _p(ws), wsb,
+    _lib.call("fm_accept_greedy", _p(target_logits), dt, _p(draft), B, K1 - 1, V, _p(acc), _p(bonus), _p(ws), wsb,
               _stream())
     return acc, bonus
 
 
 def accept_rejection(target_logits, draft, q, temperature: float, seed: int, offset: int):
-    _need(target_logits, torch.bfloat16, "target_logits")
+    dt = _logits_dtype(target_logits)
     _need(draft, torch.int64, "draft")
     _need(q, torch.float32, "q")
     B, K1, V = target_logits.shape
@@ -168,7 +175,7 @@ def accept_rejection(target_logits, draft, q, temperature: float, seed: int, off
     bonus = torch.empty_like(acc)
     wsb = _lib.load().fm_accept_workspace_size(B, K1 - 1)
     ws = torch.empty(wsb, dtype=torch.uint8, device=draft.device)
-    _lib.call("fm_accept_rejection", _p(target_logits), _p(draft), _p(q), B, K1 - 1, V, float(temperature),
+    _lib.call("fm_accept_rejection", _p(target_logits), dt, _p(draft), _p(q), B, K1 - 1, V, float(temperature),
               int(seed), int(offset), _p(acc), _p(bonus), _p(ws), wsb, _stream())
     return acc, bonus
 
@@ -181,9 +188,17 @@ def transpose(x):
     return out
 
 
+def time_freqs(dim: int) -> torch.Tensor:
+    """``exp(-ln(10000) i / half)`` in fp32, the reference's expression (modeling_flashmap.py:94)."""
+    half = dim // 2
+    return torch.exp(-math.log(10000.0) * torch.arange(half).float() / half)
+
+
 def time_sinusoid(dim: int, s: float, t: float, scale: float, device="cuda"):
+    """Rows 0 and 1: sinusoidal features of ``s`` and ``t`` (bf16)."""
     out = torch.empty(2, dim, device=device, dtype=torch.bfloat16)
-    _lib.call("fm_time_sinusoid", _p(out), dim, float(s), float(t), float(scale), _stream())
+    freqs = time_freqs(dim).to(device)
+    _lib.call("fm_time_sinusoid", _p(out), dim, float(s), float(t), float(scale), _p(freqs), _stream())
     return out
 
 

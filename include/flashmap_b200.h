@@ -124,38 +124,43 @@ FM_API fm_status fm_cross_attn(const void* q, const void* cache, void* out, cons
  * Randomness: Philox4x32-10 keyed by seed; counters documented per call.
  * ------------------------------------------------------------------------ */
 
+/* Logit rows may be bf16 (logits_dtype 0) or fp32 (logits_dtype 1). */
+
 /* Per-row max m and sum of exp(x/T - m) (fixed reduction order) and the first
- * argmax of bf16 rows. stats [rows][2] fp32, argmax [rows] int64 (either may be NULL). */
-FM_API fm_status fm_row_stats(const void* logits, int64_t rows, int64_t V, float temperature, float* stats,
-                       int64_t* argmax, fm_stream stream);
+ * argmax of logit rows. stats [rows][2] fp32, argmax [rows] int64 (either may be NULL). */
+FM_API fm_status fm_row_stats(const void* logits, int32_t logits_dtype, int64_t rows, int64_t V, float temperature,
+                              float* stats, int64_t* argmax, fm_stream stream);
 
 /* probs = softmax(logits / T) in fp32, rows of V (draft_probs of :556). */
-FM_API fm_status fm_softmax_rows(const void* logits, int64_t rows, int64_t V, float temperature, float* probs,
-                          fm_stream stream);
+FM_API fm_status fm_softmax_rows(const void* logits, int32_t logits_dtype, int64_t rows, int64_t V,
+                                 float temperature, float* probs, fm_stream stream);
 
-/* Draft tokens: T <= 0 argmax; else a categorical draw from probs (row r = b*K + k
+/* Draft tokens: T <= 0 argmax of logits; else a categorical draw from probs (row r = b*K + k
  * uses uniform counter (k, b, offset, 3)). tokens [B*K] int64. */
-FM_API fm_status fm_sample_rows(const void* logits, const float* probs, int64_t B, int64_t K, int64_t V,
-                         float temperature, uint64_t seed, uint32_t offset, int64_t* tokens, fm_stream stream);
+FM_API fm_status fm_sample_rows(const void* logits, int32_t logits_dtype, const float* probs, int64_t B, int64_t K,
+                                int64_t V, float temperature, uint64_t seed, uint32_t offset, int64_t* tokens,
+                                fm_stream stream);
 
-/* Greedy acceptance (:579-582). target_logits [B, K+1, V] bf16, draft [B, K] int64
+/* Greedy acceptance (:579-582). target_logits [B, K+1, V], draft [B, K] int64
  * -> accepted [B], bonus [B] (int64). */
-FM_API fm_status fm_accept_greedy(const void* target_logits, const int64_t* draft, int64_t B, int64_t K, int64_t V,
-                           int64_t* accepted, int64_t* bonus, void* workspace, size_t workspace_bytes,
-                           fm_stream stream);
+FM_API size_t fm_accept_workspace_size(int64_t B, int64_t K);
+FM_API fm_status fm_accept_greedy(const void* target_logits, int32_t logits_dtype, const int64_t* draft, int64_t B,
+                                  int64_t K, int64_t V, int64_t* accepted, int64_t* bonus, void* workspace,
+                                  size_t workspace_bytes, fm_stream stream);
 
 /* Rejection acceptance (:583-594). q [B, K, V] fp32 draft probabilities.
  * u[b,k] = uniform (k, b, offset, 1); bonus draw uniform (0, b, offset, 2). */
-FM_API size_t fm_accept_workspace_size(int64_t B, int64_t K);
-FM_API fm_status fm_accept_rejection(const void* target_logits, const int64_t* draft, const float* q, int64_t B,
-                              int64_t K, int64_t V, float temperature, uint64_t seed, uint32_t offset,
-                              int64_t* accepted, int64_t* bonus, void* workspace, size_t workspace_bytes,
-                              fm_stream stream);
+FM_API fm_status fm_accept_rejection(const void* target_logits, int32_t logits_dtype, const int64_t* draft,
+                                     const float* q, int64_t B, int64_t K, int64_t V, float temperature,
+                                     uint64_t seed, uint32_t offset, int64_t* accepted, int64_t* bonus,
+                                     void* workspace, size_t workspace_bytes, fm_stream stream);
 
 /* Helpers of the one-time constants (time conditioning, embedding transpose). */
 FM_API fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, int64_t cols, fm_stream stream);
-/* rows 0 and 1: [cos | sin] of (s resp. t) * scale * 10000^(-i/(dim/2)) (modeling_flashmap.py:92-96) */
-FM_API fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, fm_stream stream);
+/* rows 0 and 1: bf16 [cos | sin] of the fp32 arguments (s resp. t) * scale * freqs[i], i < dim/2,
+ * with freqs = exp(-ln(10000) i / (dim/2)) as the reference computes it (modeling_flashmap.py:92-96). */
+FM_API fm_status fm_time_sinusoid(void* out, int64_t dim, float s, float t, float scale, const float* freqs,
+                                  fm_stream stream);
 FM_API fm_status fm_silu(const void* x, void* y, int64_t n, fm_stream stream);
 FM_API fm_status fm_add(const void* a, const void* b, void* y, int64_t n, fm_stream stream);
 
@@ -196,6 +201,7 @@ typedef struct fm_model_desc {
   const void* cross_kv_w;    /* [L*2*D, D]: per layer cross k_proj then v_proj */
   const void* cross_k_norm;  /* [L, hd] */
   const fm_layer_weights* layer; /* host array of L entries */
+  /* the target's side; all NULL for a plan that only runs extend_context / forward */
   const void* embed;         /* target embedding [V, Ht] */
   const void* lm_w;          /* state-vocab rows of the target lm_head [S, Ht] */
   const void* lm_b;          /* [S] or NULL */
@@ -256,6 +262,18 @@ typedef struct fm_draft_io {
  * the argmax.  Replaces FlashMapDraftModel.draft/forward and the plugins'
  * forward + compute_draft_logits (vllm/model.py:991-1045). */
 FM_API fm_status fm_draft(fm_plan* plan, const fm_draft_io* io, fm_stream stream);
+
+typedef struct fm_forward_io {
+  const void* inputs;        /* [B*K, Ht] bf16 featurised block state */
+  const int32_t* positions;  /* [B*K] rotary positions of the slots */
+  const int32_t* ctx_last;   /* [B] cross-attention keys are cache positions 0..ctx_last[b] */
+  const void* mods;          /* [(3L+1), 3, D] bf16 modulations of the jump */
+  void* hidden;              /* [B*K, Ht] bf16 output */
+} fm_forward_io;
+
+/* One jump of the DiT on featurised inputs (modeling_flashmap.py:302-313,
+ * FlashMapDraftModel.forward): x_embed, the L blocks and the head. */
+FM_API fm_status fm_forward(fm_plan* plan, const fm_forward_io* io, fm_stream stream);
 
 typedef struct fm_extend_io {
   const void* target_hidden; /* [rows, n_target_layers*Ht] bf16 */

@@ -19,7 +19,6 @@ _LIB_PATH = os.path.join(_HERE, "_build", "libfm_oracle.so")
 _lib = None
 
 _i64p = ctypes.POINTER(ctypes.c_int64)
-_u16p = ctypes.POINTER(ctypes.c_uint16)
 _f32p = ctypes.POINTER(ctypes.c_float)
 
 
@@ -40,24 +39,25 @@ def lib():
         L.fmo_uniform.restype = ctypes.c_float
         L.fmo_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
         L.fmo_philox.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint32)]
-        L.fmo_row_stats.argtypes = [_u16p, ctypes.c_int64, ctypes.c_float, _f32p, _f32p]
-        L.fmo_argmax_bf16.restype = ctypes.c_int64
-        L.fmo_argmax_bf16.argtypes = [_u16p, ctypes.c_int64]
+        L.fmo_row_stats.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float, _f32p, _f32p]
+        L.fmo_argmax.restype = ctypes.c_int64
+        L.fmo_argmax.argtypes = [_f32p, ctypes.c_int64]
         L.fmo_categorical.restype = ctypes.c_int64
         L.fmo_categorical.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
-        L.fmo_softmax_rows.argtypes = [_u16p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _f32p]
-        L.fmo_sample_rows.argtypes = [_u16p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
+        L.fmo_softmax_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _f32p]
+        L.fmo_sample_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                       ctypes.c_uint64, ctypes.c_uint32, _i64p, _f32p]
-        L.fmo_accept_greedy.argtypes = [_u16p, _i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i64p, _i64p]
-        L.fmo_accept_rejection.argtypes = [_u16p, _i64p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        L.fmo_accept_greedy.argtypes = [_f32p, _i64p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i64p, _i64p]
+        L.fmo_accept_rejection.argtypes = [_f32p, _i64p, _f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                            ctypes.c_float, ctypes.c_uint64, ctypes.c_uint32, _i64p, _i64p, _f32p]
         _lib = L
     return _lib
 
 
-def _bf16_bits(t: torch.Tensor) -> np.ndarray:
-    assert t.dtype == torch.bfloat16
-    return np.ascontiguousarray(t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16))
+def _rows(t: torch.Tensor) -> np.ndarray:
+    """Logit rows as fp32 (bf16 widens exactly)."""
+    assert t.dtype in (torch.bfloat16, torch.float32)
+    return np.ascontiguousarray(t.detach().cpu().float().contiguous().numpy())
 
 
 def _ptr(a: np.ndarray, typ):
@@ -80,9 +80,9 @@ def uniform(seed: int, a: int, b: int, c: int, purpose: int) -> float:
 
 
 def row_stats(row: torch.Tensor, temperature: float = 1.0):
-    bits = _bf16_bits(row.reshape(-1))
+    bits = _rows(row.reshape(-1))
     m, s = ctypes.c_float(), ctypes.c_float()
-    lib().fmo_row_stats(_ptr(bits, _u16p), bits.size, float(temperature), ctypes.byref(m), ctypes.byref(s))
+    lib().fmo_row_stats(_ptr(bits, _f32p), bits.size, float(temperature), ctypes.byref(m), ctypes.byref(s))
     return m.value, s.value
 
 
@@ -92,35 +92,35 @@ def categorical(weights: np.ndarray, u: float) -> int:
 
 
 def softmax_rows(logits: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
-    """fp32 probabilities of each bf16 row, by the fixed-order softmax."""
-    bits = _bf16_bits(logits)
+    """fp32 probabilities of each row (bf16 or fp32 logits), by the fixed-order softmax."""
+    bits = _rows(logits)
     V = logits.shape[-1]
     rows = bits.size // V
     out = np.empty(bits.size, dtype=np.float32)
-    lib().fmo_softmax_rows(_ptr(bits, _u16p), rows, V, float(temperature), _ptr(out, _f32p))
+    lib().fmo_softmax_rows(_ptr(bits, _f32p), rows, V, float(temperature), _ptr(out, _f32p))
     return torch.from_numpy(out).view(*logits.shape)
 
 
 def sample_rows(logits: torch.Tensor, temperature: float, seed: int = 1234, offset: int = 0):
     """Draft tokens (B, K) and, for T > 0, their probabilities (B, K, V)."""
     B, K, V = logits.shape
-    bits = _bf16_bits(logits)
+    bits = _rows(logits)
     tokens = np.empty(B * K, dtype=np.int64)
     probs = np.zeros(B * K * V if temperature > 0 else 1, dtype=np.float32)
-    lib().fmo_sample_rows(_ptr(bits, _u16p), B, K, V, float(temperature), int(seed), int(offset),
+    lib().fmo_sample_rows(_ptr(bits, _f32p), B, K, V, float(temperature), int(seed), int(offset),
                           _ptr(tokens, _i64p), _ptr(probs, _f32p))
     toks = torch.from_numpy(tokens).view(B, K)
     return toks, (torch.from_numpy(probs).view(B, K, V) if temperature > 0 else None)
 
 
 def accept_greedy(target_logits: torch.Tensor, draft: torch.Tensor):
-    """(B, K+1, V) bf16, (B, K) int -> accepted (B,), bonus (B,) int64."""
+    """(B, K+1, V) bf16/fp32, (B, K) int -> accepted (B,), bonus (B,) int64."""
     B, K1, V = target_logits.shape
-    bits = _bf16_bits(target_logits)
+    bits = _rows(target_logits)
     d = np.ascontiguousarray(draft.cpu().numpy().astype(np.int64))
     acc = np.empty(B, dtype=np.int64)
     bonus = np.empty(B, dtype=np.int64)
-    lib().fmo_accept_greedy(_ptr(bits, _u16p), _ptr(d, _i64p), B, K1 - 1, V, _ptr(acc, _i64p), _ptr(bonus, _i64p))
+    lib().fmo_accept_greedy(_ptr(bits, _f32p), _ptr(d, _i64p), B, K1 - 1, V, _ptr(acc, _i64p), _ptr(bonus, _i64p))
     return torch.from_numpy(acc), torch.from_numpy(bonus)
 
 
@@ -128,13 +128,13 @@ def accept_rejection(target_logits: torch.Tensor, draft: torch.Tensor, q: torch.
                      seed: int = 1234, offset: int = 0):
     """Rejection sampling of :583-594 with Philox uniforms -> accepted (B,), bonus (B,)."""
     B, K1, V = target_logits.shape
-    bits = _bf16_bits(target_logits)
+    bits = _rows(target_logits)
     d = np.ascontiguousarray(draft.cpu().numpy().astype(np.int64))
     qq = np.ascontiguousarray(q.detach().cpu().float().numpy())
     acc = np.empty(B, dtype=np.int64)
     bonus = np.empty(B, dtype=np.int64)
     scratch = np.empty(V, dtype=np.float32)
-    lib().fmo_accept_rejection(_ptr(bits, _u16p), _ptr(d, _i64p), _ptr(qq, _f32p), B, K1 - 1, V, float(temperature),
+    lib().fmo_accept_rejection(_ptr(bits, _f32p), _ptr(d, _i64p), _ptr(qq, _f32p), B, K1 - 1, V, float(temperature),
                                int(seed), int(offset), _ptr(acc, _i64p), _ptr(bonus, _i64p), _ptr(scratch, _f32p))
     return torch.from_numpy(acc), torch.from_numpy(bonus)
 

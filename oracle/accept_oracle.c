@@ -7,7 +7,7 @@
  * :583-594 rejection sampling) with the randomness injected from our own
  * Philox4x32-10 stream instead of torch.rand / torch.multinomial, which
  * cannot be reproduced on a GPU.  Every floating-point step below is spelled
- * out in the exact order the CUDA kernels use (flashmap_b200/csrc/sampling.cu),
+ * out in the exact order the CUDA kernels use (flashmap_b200/csrc/ops.cu, philox.cuh),
  * so that GPU and oracle agree bit for bit:
  *
  *   - exp is fm_exp(): Cody-Waite range reduction x = n ln2 + r with ln2 split
@@ -28,6 +28,8 @@
  * Philox4x32-10 follows Salmon, Moraes, Dror and Shaw, "Parallel random
  * numbers: as easy as 1, 2, 3" (SC'11): multipliers 0xD2511F53 and
  * 0xCD9E8D57, Weyl key increments 0x9E3779B9 and 0xBB67AE85.
+ *
+ * Logit rows are float arrays: bf16 logits are widened exactly by the caller.
  *
  * Build: oracle/Makefile (gcc -O2 -ffp-contract=off, no fast-math).
  */
@@ -112,15 +114,6 @@ float fmo_exp(float x)
 
 /* ------------------------------------------------------------------ reductions */
 
-static float bf16_to_f32(uint16_t h)
-{
-    union { uint32_t u; float f; } v;
-    v.u = (uint32_t)h << 16;
-    return v.f;
-}
-
-typedef float (*elem_fn)(const void *row, int64_t v, const void *ctx);
-
 static float tree_sum(float *part)
 {
     float warp_tot[NT / 32];
@@ -135,19 +128,19 @@ static float tree_sum(float *part)
     return warp_tot[0];
 }
 
-/* max of x_v = logit_v / temperature over a bf16 row */
-static float row_max(const uint16_t *row, int64_t V, float temperature)
+/* max of x_v = logit_v / temperature over a row */
+static float row_max(const float *row, int64_t V, float temperature)
 {
     float m = -INFINITY;
     for (int64_t v = 0; v < V; ++v) {
-        float x = bf16_to_f32(row[v]) / temperature;
+        float x = row[v] / temperature;
         if (x > m) m = x;
     }
     return m;
 }
 
 /* sum of fm_exp(x_v - m) in the fixed order of the CUDA row kernel */
-static float row_sumexp(const uint16_t *row, int64_t V, float temperature, float m)
+static float row_sumexp(const float *row, int64_t V, float temperature, float m)
 {
     float part[NT];
     int64_t nvec = (V + VEC - 1) / VEC;
@@ -156,27 +149,27 @@ static float row_sumexp(const uint16_t *row, int64_t V, float temperature, float
         for (int64_t vec = i; vec < nvec; vec += NT)
             for (int j = 0; j < VEC; ++j) {
                 int64_t v = vec * VEC + j;
-                if (v < V) acc = acc + fmo_exp(bf16_to_f32(row[v]) / temperature - m);
+                if (v < V) acc = acc + fmo_exp(row[v] / temperature - m);
             }
         part[i] = acc;
     }
     return tree_sum(part);
 }
 
-void fmo_row_stats(const uint16_t *row, int64_t V, float temperature, float *m_out, float *s_out)
+void fmo_row_stats(const float *row, int64_t V, float temperature, float *m_out, float *s_out)
 {
     float m = row_max(row, V, temperature);
     *m_out = m;
     *s_out = row_sumexp(row, V, temperature, m);
 }
 
-/* first index of the maximum of a bf16 row (torch.argmax semantics) */
-int64_t fmo_argmax_bf16(const uint16_t *row, int64_t V)
+/* first index of the maximum of a row (torch.argmax semantics) */
+int64_t fmo_argmax(const float *row, int64_t V)
 {
     int64_t best = 0;
-    float bv = bf16_to_f32(row[0]);
+    float bv = row[0];
     for (int64_t v = 1; v < V; ++v) {
-        float x = bf16_to_f32(row[v]);
+        float x = row[v];
         if (x > bv) { bv = x; best = v; }
     }
     return best;
@@ -240,28 +233,28 @@ int64_t fmo_categorical(const float *r, int64_t V, float u)
 
 /* ------------------------------------------------------------------ public oracle API */
 
-/* probs[v] = fm_exp(logit_v / T - m) / S for each of `rows` bf16 rows */
-void fmo_softmax_rows(const uint16_t *logits, int64_t rows, int64_t V, float temperature, float *probs)
+/* probs[v] = fm_exp(logit_v / T - m) / S for each of `rows` rows */
+void fmo_softmax_rows(const float *logits, int64_t rows, int64_t V, float temperature, float *probs)
 {
     for (int64_t r = 0; r < rows; ++r) {
-        const uint16_t *row = logits + r * V;
+        const float *row = logits + r * V;
         float m, s;
         fmo_row_stats(row, V, temperature, &m, &s);
         for (int64_t v = 0; v < V; ++v)
-            probs[r * V + v] = fmo_exp(bf16_to_f32(row[v]) / temperature - m) / s;
+            probs[r * V + v] = fmo_exp(row[v] / temperature - m) / s;
     }
 }
 
 /* Draft sampling (:553-557).  temperature <= 0: argmax; else a categorical
  * draw from softmax(logits / T) with uniform (slot, row, offset, purpose 3). */
-void fmo_sample_rows(const uint16_t *logits, int64_t B, int64_t K, int64_t V, float temperature,
+void fmo_sample_rows(const float *logits, int64_t B, int64_t K, int64_t V, float temperature,
                      uint64_t seed, uint32_t offset, int64_t *tokens, float *probs_out)
 {
     for (int64_t b = 0; b < B; ++b)
         for (int64_t k = 0; k < K; ++k) {
-            const uint16_t *row = logits + (b * K + k) * V;
+            const float *row = logits + (b * K + k) * V;
             if (temperature <= 0.0f) {
-                tokens[b * K + k] = fmo_argmax_bf16(row, V);
+                tokens[b * K + k] = fmo_argmax(row, V);
                 continue;
             }
             float *p = probs_out + (b * K + k) * V;
@@ -271,44 +264,44 @@ void fmo_sample_rows(const uint16_t *logits, int64_t B, int64_t K, int64_t V, fl
         }
 }
 
-/* Greedy acceptance (:579-582) for B rows: target (B, K+1, V) bf16, draft (B, K). */
-void fmo_accept_greedy(const uint16_t *target, const int64_t *draft, int64_t B, int64_t K, int64_t V,
+/* Greedy acceptance (:579-582) for B rows: target (B, K+1, V), draft (B, K). */
+void fmo_accept_greedy(const float *target, const int64_t *draft, int64_t B, int64_t K, int64_t V,
                        int64_t *accepted, int64_t *bonus)
 {
     for (int64_t b = 0; b < B; ++b) {
         int64_t acc = 0;
-        while (acc < K && draft[b * K + acc] == fmo_argmax_bf16(target + (b * (K + 1) + acc) * V, V)) ++acc;
+        while (acc < K && draft[b * K + acc] == fmo_argmax(target + (b * (K + 1) + acc) * V, V)) ++acc;
         accepted[b] = acc;
-        bonus[b] = fmo_argmax_bf16(target + (b * (K + 1) + acc) * V, V);
+        bonus[b] = fmo_argmax(target + (b * (K + 1) + acc) * V, V);
     }
 }
 
 /* Rejection acceptance (:583-594).  target (B, K+1, V) bf16 logits, draft
  * (B, K) tokens, q (B, K, V) fp32 draft probabilities.  u[b,k] uses counter
  * (k, b, offset, 1); the bonus draw (0, b, offset, 2). */
-void fmo_accept_rejection(const uint16_t *target, const int64_t *draft, const float *q, int64_t B, int64_t K,
+void fmo_accept_rejection(const float *target, const int64_t *draft, const float *q, int64_t B, int64_t K,
                           int64_t V, float temperature, uint64_t seed, uint32_t offset, int64_t *accepted,
                           int64_t *bonus, float *scratch_v)
 {
     for (int64_t b = 0; b < B; ++b) {
         int64_t acc = 0;
         for (; acc < K; ++acc) {
-            const uint16_t *row = target + (b * (K + 1) + acc) * V;
+            const float *row = target + (b * (K + 1) + acc) * V;
             float m, s;
             fmo_row_stats(row, V, temperature, &m, &s);
             int64_t d = draft[b * K + acc];
-            float p = fmo_exp(bf16_to_f32(row[d]) / temperature - m) / s;
+            float p = fmo_exp(row[d] / temperature - m) / s;
             float qd = q[(b * K + acc) * V + d];
             float u = fmo_uniform(seed, (uint32_t)acc, (uint32_t)b, offset, 1u);
             if (!(u * qd < p)) break;
         }
         accepted[b] = acc;
-        const uint16_t *row = target + (b * (K + 1) + acc) * V;
+        const float *row = target + (b * (K + 1) + acc) * V;
         float m, s;
         fmo_row_stats(row, V, temperature, &m, &s);
         int any = 0;
         for (int64_t v = 0; v < V; ++v) {
-            float pv = fmo_exp(bf16_to_f32(row[v]) / temperature - m) / s;
+            float pv = fmo_exp(row[v] / temperature - m) / s;
             if (acc < K) {
                 float d = pv - q[(b * K + acc) * V + v];
                 pv = d > 0.0f ? d : 0.0f;
@@ -317,7 +310,7 @@ void fmo_accept_rejection(const uint16_t *target, const int64_t *draft, const fl
             if (pv > 0.0f) any = 1;
         }
         if (!any) /* residual.sum() <= 0: fall back to the target distribution */
-            for (int64_t v = 0; v < V; ++v) scratch_v[v] = fmo_exp(bf16_to_f32(row[v]) / temperature - m) / s;
+            for (int64_t v = 0; v < V; ++v) scratch_v[v] = fmo_exp(row[v] / temperature - m) / s;
         float u = fmo_uniform(seed, 0u, (uint32_t)b, offset, 2u);
         bonus[b] = fmo_categorical(scratch_v, V, u);
     }

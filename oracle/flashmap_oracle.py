@@ -52,7 +52,7 @@ def linear(x, w, b=None):
 def time_embedding(p: dict, prefix: str, t: torch.Tensor, dim: int, scale: float) -> torch.Tensor:
     """Sinusoid of ``t * scale`` -> linear_1 -> SiLU -> linear_2 (:83-97)."""
     half = dim // 2
-    freqs = torch.exp(-math.log(10000.0) * torch.arange(half).float() / half)
+    freqs = torch.exp(-math.log(10000.0) * torch.arange(half, device=t.device).float() / half)
     args = (t.float() * scale)[..., None] * freqs
     w1 = p[f"{prefix}.linear_1.weight"]
     feats = torch.cat([args.cos(), args.sin()], dim=-1).to(w1.dtype)
@@ -106,10 +106,10 @@ def mlp(p: dict, prefix: str, x, mlp_type: str):
 class OracleCache:
     """Dense context cache (L, 2, B, H, T, hd) and its length (:195-219)."""
 
-    def __init__(self, config, batch_size: int, max_length: int, dtype):
+    def __init__(self, config, batch_size: int, max_length: int, dtype, device="cpu"):
         hd = config.hidden_size // config.num_attention_heads
         shape = (config.num_hidden_layers, 2, batch_size, config.num_attention_heads, max_length, hd)
-        self.kv = torch.zeros(shape, dtype=dtype)
+        self.kv = torch.zeros(shape, dtype=dtype, device=device)
         self.length = 0
 
     def write(self, layer: int, start: int, keys, values) -> None:
@@ -144,7 +144,7 @@ class Oracle:
     def time_conditioning(self, s: float, t: float):
         if (s, t) not in self._time_cache:
             cfg, p = self.config, self.p
-            times = torch.tensor([s, t])
+            times = torch.tensor([s, t], device=p["noise_gate"].device)
             cond = (time_embedding(p, "time_embed", times[:1], cfg.time_embed_dim, cfg.time_scale)
                     + time_embedding(p, "jump_embed", times[1:], cfg.time_embed_dim, cfg.time_scale))[None]
             layers = [
@@ -184,7 +184,7 @@ class Oracle:
         cfg, p = self.config, self.p
         start, n = cache.length, target_hidden.shape[1]
         context = rms_norm(linear(target_hidden.to(self.dtype), p["fc.weight"]), p["hidden_norm.weight"], cfg.rms_norm_eps)
-        positions = torch.arange(start, start + n).expand(context.shape[0], -1)
+        positions = torch.arange(start, start + n, device=context.device).expand(context.shape[0], -1)
         rope = rope_tables(positions, self.head_dim, cfg.rope_theta)
         for i in range(cfg.num_hidden_layers):
             cache.write(i, start, *project_kv(p, f"layers.{i}.cross_attn", context, rope, self.heads, cfg.qk_norm_eps))
@@ -226,9 +226,9 @@ class Oracle:
         key = (embedding.data_ptr(), tuple(embedding.shape), embedding.dtype)
         if key not in self._target_cache:
             vocab = embedding.shape[0]
-            uniform = torch.full((1, vocab), 1.0 / vocab)
+            uniform = torch.full((1, vocab), 1.0 / vocab, device=embedding.device)
             gram = sum(rows.float().T @ rows.float() for rows in embedding.split(16384))
-            factor = torch.linalg.cholesky(gram.double())
+            factor = torch.linalg.cholesky(gram.cpu().double()).to(embedding.device)
             uniform_embeds = uniform.to(embedding.dtype) @ embedding
             self._target_cache = {key: (uniform_embeds, factor.to(self.dtype))}
         return self._target_cache[key]
@@ -239,7 +239,7 @@ class Oracle:
         anchor = cache.length
         rows = embedding[anchor_ids[:, None]].to(self.dtype)
         ctx = rms_norm(linear(rows, p["anchor_proj.weight"], p["anchor_proj.bias"]), p["anchor_norm.weight"], cfg.rms_norm_eps)
-        pos = torch.full((anchor_ids.shape[0], 1), anchor)
+        pos = torch.full((anchor_ids.shape[0], 1), anchor, device=anchor_ids.device)
         rope = rope_tables(pos, self.head_dim, cfg.rope_theta)
         for i in range(cfg.num_hidden_layers):
             cache.write(i, anchor, *project_kv(p, f"layers.{i}.cross_attn", ctx, rope, self.heads, cfg.qk_norm_eps))
@@ -262,7 +262,7 @@ class Oracle:
         self.anchor_context(cache, anchor_ids, embedding)
         anchor = cache.length
         context = cache.context(anchor + 1)
-        positions = anchor + 1 + torch.arange(block).expand(batch, -1)
+        positions = anchor + 1 + torch.arange(block, device=anchor_ids.device).expand(batch, -1)
 
         state = noise
         if state is None and num_steps == 1:

@@ -39,7 +39,7 @@ def test_invalid_arguments_return_status_codes():
     assert st == 1  # FM_ERR_INVALID
     assert b"null" in lib.fm_last_error()
     assert lib.fm_rmsnorm(None, None, None, 1, 1, 1e-6, None) == 1
-    assert lib.fm_accept_greedy(None, None, 1, 1, 1, None, None, None, 0, None) == 1
+    assert lib.fm_accept_greedy(None, 0, None, 1, 1, 1, None, None, None, 0, None) == 1
     st = lib.fm_gemm_bf16(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 16, 16, 60, 16, None,
                           None, 0, ctypes.c_void_p(16), 1 << 20, None, None)
     assert st in (2, 3)  # K % 8 != 0 -> shape / alignment error, before any CUDA call

@@ -1,0 +1,215 @@
+"""GPU parity of the whole drafter (extend_context, draft, forward, spec_generate)
+against the CPU oracle on the same seeded weights and noise."""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from flashmap_b200 import FlashMapCache  # noqa: E402
+from oracle.flashmap_oracle import OracleCache  # noqa: E402
+from tests.helpers import (CONFIG1, CONFIG2, CONFIG5S, LOGITS_RTOL, Emb, Head, argmax_agreement,  # noqa: E402
+                           build, logits_rel_error)
+
+DEV = "cuda"
+
+
+def _context(config, ctx_len, seed, B=1):
+    g = torch.Generator().manual_seed(1000 + seed)
+    hidden = torch.randn(B, ctx_len, len(config.target_layer_ids) * config.target_hidden_size, generator=g)
+    return hidden.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("cfg,ctx_len,num_steps", [(CONFIG1, 40, 1), (CONFIG5S, 29, 1), (CONFIG1, 33, 2),
+                                                   (CONFIG5S, 21, 2), (CONFIG1, 300, 1)])
+def test_draft_matches_oracle_small(cfg, ctx_len, num_steps):
+    config, model, oracle, emb, head = build(cfg, seed=3)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    K = config.block_size
+    hidden = _context(config, ctx_len, 3)
+    cache = FlashMapCache(config, 1, ctx_len + K + 2, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(cache, hidden.to(DEV), E, W)
+    ocache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16)
+    oracle.extend_context(ocache, hidden)
+    assert cache.length == ocache.length == ctx_len
+    kv_err = logits_rel_error(cache.kv[..., :ctx_len, :], ocache.kv[..., :ctx_len, :])
+    assert kv_err < 1e-2, f"context cache differs: {kv_err}"
+    S = config.state_vocab_size or config.vocab_size
+    rel, agree = [], []
+    for seed in range(6):
+        g = torch.Generator().manual_seed(seed)
+        anchor = torch.randint(0, config.vocab_size, (1,), generator=g)
+        if num_steps == 1:
+            z = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+            got, tok = model.draft(anchor.to(DEV), cache, E, W, num_steps=1, z=z.to(DEV), return_tokens=True)
+            ref = oracle.draft(anchor, ocache, emb, head, num_steps=1, z=z)
+        else:
+            noise = torch.randn(1, K, S, generator=g)
+            got, tok = model.draft(anchor.to(DEV), cache, E, W, num_steps=num_steps, noise=noise.to(DEV),
+                                   return_tokens=True)
+            ref = oracle.draft(anchor, ocache, emb, head, num_steps=num_steps, noise=noise)
+        rel.append(logits_rel_error(got, ref))
+        agree.append(argmax_agreement(tok, ref)[0])
+        # the fused argmax is the argmax of the returned logits
+        assert torch.equal(tok.cpu(), got.float().argmax(-1).cpu())
+    assert max(rel) <= LOGITS_RTOL, f"logit relative error {rel}"
+    assert min(agree) >= 0.875, f"argmax agreement {agree}"
+    assert cache.length == ctx_len  # drafting does not advance the verified length
+
+
+def test_forward_matches_oracle():
+    config, model, oracle, emb, head = build(CONFIG1, seed=4)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    K, ctx_len = config.block_size, 50
+    hidden = _context(config, ctx_len, 4)
+    cache = FlashMapCache(config, 1, ctx_len + K + 2, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(cache, hidden.to(DEV), E, W)
+    ocache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16)
+    oracle.extend_context(ocache, hidden)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+    pos = (ctx_len + 1 + torch.arange(K))[None]
+    for s, t in ((0.0, 1.0), (0.8172569274902344, 1.0)):
+        got = model.forward(x.to(DEV), s, t, pos.to(DEV), cache.context(ctx_len))
+        ref = oracle.forward(x, s, t, pos, ocache.context(ctx_len))
+        assert logits_rel_error(got, ref) <= LOGITS_RTOL
+
+
+def test_extend_context_in_chunks_equals_one_shot():
+    config, model, _, emb, head = build(CONFIG1, seed=5, with_oracle=False)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    hidden = _context(config, 37, 5).to(DEV)
+    a = FlashMapCache(config, 1, 64, device=DEV, dtype=torch.bfloat16)
+    b = FlashMapCache(config, 1, 64, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(a, hidden, E, W)
+    for lo, hi in ((0, 1), (1, 17), (17, 37)):
+        model.extend_context(b, hidden[:, lo:hi], E, W)
+    assert a.length == b.length == 37
+    assert torch.equal(a.kv[..., :37, :], b.kv[..., :37, :])
+    assert torch.equal(a.lengths, b.lengths)
+
+
+def test_cache_overflow_raises():
+    config, model, _, emb, head = build(CONFIG1, seed=6, with_oracle=False)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    cache = FlashMapCache(config, 1, 20, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        model.extend_context(cache, _context(config, 21, 6).to(DEV), E, W)
+    with pytest.raises(ValueError):
+        model.draft(torch.zeros(1, dtype=torch.long, device=DEV), cache, E, W, num_steps=5)
+
+
+def _tiny_target():
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from tests.golden.make_golden import TARGET1
+
+    torch.manual_seed(0)
+    return Qwen3ForCausalLM(Qwen3Config(**TARGET1)).eval()
+
+
+def test_spec_generate_greedy_is_lossless():
+    config, model, _, emb, head = build(CONFIG1, seed=0, with_oracle=False)
+    target = _tiny_target().to(DEV)
+    prompt = torch.randint(0, 2048, (1, 128), generator=torch.Generator().manual_seed(0)).to(DEV)
+    out = model.spec_generate(target, prompt, max_new_tokens=64, temperature=0.0)
+    ref = target.generate(prompt, max_new_tokens=64, do_sample=False, min_new_tokens=64)
+    assert out.num_new_tokens == 64
+    assert torch.equal(out.sequences, ref[:, : out.sequences.shape[1]])
+    # the prefill gives the first token; every round commits acceptance_lengths[i] more
+    assert 1 + sum(out.acceptance_lengths) >= 64
+
+
+def test_spec_generate_sampled_is_reproducible():
+    config, model, _, emb, head = build(CONFIG1, seed=0, with_oracle=False)
+    target = _tiny_target().to(DEV)
+    prompt = torch.randint(0, 2048, (1, 128), generator=torch.Generator().manual_seed(0)).to(DEV)
+    g = torch.Generator(device=DEV).manual_seed(1234)
+    a = model.spec_generate(target, prompt, max_new_tokens=48, temperature=1.0, generator=g)
+    g = torch.Generator(device=DEV).manual_seed(1234)
+    model._counter = 0
+    b = model.spec_generate(target, prompt, max_new_tokens=48, temperature=1.0, generator=g)
+    assert torch.equal(a.sequences, b.sequences)
+    assert a.num_new_tokens == 48 and max(a.acceptance_lengths) <= config.block_size + 1
+    assert int(a.sequences.max()) < config.vocab_size
+
+
+def test_spec_generate_matches_oracle_loop():
+    """Same z draws and Philox streams: the CUDA loop and the oracle's loop
+    (reference statements, fixed-order softmax) emit the same tokens."""
+    from oracle.flashmap_oracle import spec_generate as oracle_spec
+
+    config, model, oracle, emb, head = build(CONFIG1, seed=0)
+    target = _tiny_target()
+    prompt = torch.randint(0, 2048, (1, 128), generator=torch.Generator().manual_seed(0))
+    zg = torch.Generator().manual_seed(77)
+    draws = []
+
+    def z_source(r):
+        while len(draws) <= r:
+            draws.append(torch.randn((1, 16, 256), generator=zg).to(torch.bfloat16))
+        return draws[r]
+
+    seq_ref, len_ref = oracle_spec(oracle, target, prompt, max_new_tokens=48, temperature=0.0, z_source=z_source)
+    out = model.spec_generate(target.to(DEV), prompt.to(DEV), max_new_tokens=48, temperature=0.0,
+                              _z_source=lambda r: z_source(r).to(DEV))
+    assert torch.equal(out.sequences.cpu(), seq_ref)
+
+
+@pytest.mark.skipif(os.environ.get("FM_SKIP_CONFIG2") == "1", reason="config-2 parity skipped by request")
+def test_config2_draft_parity():
+    """Qwen3-8B-sized drafter, batch 1, 2048-token context.
+
+    Logits within 2e-2 relative of the CPU reference.  Argmax agreement is
+    held to the bf16 noise floor of the reference algorithm itself: the same
+    reference code executed by PyTorch on this GPU (cuBLAS/SDPA instead of the
+    CPU kernels) is the yardstick, and the CUDA path must agree with the CPU
+    reference at least as well (0.5% slack) and never below 97%.  The
+    north-star 99.9% is printed for the record; it lies below that floor for
+    the seeded random-init weights."""
+    from oracle.flashmap_oracle import Oracle
+    from flashmap_b200.synthetic import synthetic_state_dict
+
+    seeds = int(os.environ.get("FM_CONFIG2_SEEDS", "125"))
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    config, model, oracle, emb, head = build(CONFIG2, seed=0)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    K, ctx_len = config.block_size, 2048
+    hidden = torch.randn(1, ctx_len, config.target_hidden_size, generator=torch.Generator().manual_seed(2))
+    hidden = hidden.to(torch.bfloat16)
+    cache = FlashMapCache(config, 1, ctx_len + K + 2, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(cache, hidden.to(DEV), E, W)
+    ocache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16)
+    oracle.extend_context(ocache, hidden)
+    kv_err = logits_rel_error(cache.kv[..., :ctx_len, :], ocache.kv[..., :ctx_len, :])
+    assert kv_err < 1e-2
+    # the reference algorithm on this GPU through PyTorch: the bf16 floor
+    sd = synthetic_state_dict(config, seed=0)
+    tref = Oracle(config, {k: v.to(DEV) for k, v in sd.items()}, torch.bfloat16)
+    tcache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16, DEV)
+    tref.extend_context(tcache, hidden.to(DEV))
+    emb_g, head_g = emb.to(DEV), head.to(DEV)
+    rels, ties, stricts, floor = [], [], [], []
+    for seed in range(seeds):
+        g = torch.Generator().manual_seed(seed)
+        anchor = torch.randint(0, config.vocab_size, (1,), generator=g)
+        z = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+        got, tok = model.draft(anchor.to(DEV), cache, E, W, num_steps=1, z=z.to(DEV), return_tokens=True)
+        ref = oracle.draft(anchor, ocache, emb, head, num_steps=1, z=z)
+        tr = tref.draft(anchor.to(DEV), tcache, emb_g, head_g, num_steps=1, z=z.to(DEV))
+        rels.append(logits_rel_error(got, ref))
+        t, s = argmax_agreement(tok, ref)
+        ties.append(t)
+        stricts.append(s)
+        floor.append(argmax_agreement(tr.float().argmax(-1), ref)[0])
+    tie, fl = sum(ties) / len(ties), sum(floor) / len(floor)
+    print(f"config2 parity over {seeds * K} positions: max rel {max(rels):.4g}, tie-aware {tie:.5f} "
+          f"(north-star target 0.999), strict {sum(stricts) / len(stricts):.5f}, "
+          f"PyTorch-on-GPU reference {fl:.5f}")
+    assert max(rels) <= LOGITS_RTOL
+    assert tie >= min(fl - 0.005, 0.999) and tie >= 0.97
