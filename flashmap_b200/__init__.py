@@ -9,7 +9,7 @@ by the CUDA library ``libflashmap_b200.so`` (C ABI: include/flashmap_b200.h).
 from transformers import AutoConfig, AutoModel
 
 from .configuration_flashmap import DEFAULT_JUMP_GRIDS, FlashMapConfig, jump_times
-from .modeling_flashmap import FlashMapCache, FlashMapDraftModel, FlashMapGenerateOutput
+from .modeling_flashmap import DraftSession, FlashMapCache, FlashMapDraftModel, FlashMapGenerateOutput
 
 # AutoModel loads FlashMap release folders once the package is imported
 # (the reference registers the same way, flashmap/__init__.py:9-12).
@@ -18,6 +18,7 @@ AutoModel.register(FlashMapConfig, FlashMapDraftModel, exist_ok=True)
 
 __all__ = [
     "DEFAULT_JUMP_GRIDS",
+    "DraftSession",
     "FlashMapCache",
     "FlashMapConfig",
     "FlashMapDraftModel",

@@ -52,7 +52,8 @@ class PlanConfig(ctypes.Structure):
 
 class DraftIO(ctypes.Structure):
     _fields_ = [("anchor_ids", c_void_p), ("lengths", c_void_p), ("z", c_void_p), ("noise", c_void_p),
-                ("seed", c_uint64), ("offset", c_uint32), ("logits", c_void_p), ("ldl", c_int64),
+                ("seed", c_uint64), ("offset", c_uint32), ("offset_ptr", c_void_p), ("logits", c_void_p),
+                ("ldl", c_int64),
                 ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p)]
 
 
@@ -100,6 +101,8 @@ _SIGNATURES = {
                                ctypes.POINTER(c_void_p)]),
     "fm_plan_destroy": (c_int, [c_void_p]),
     "fm_plan_error_word": (c_void_p, [c_void_p]),
+    "fm_plan_last_launches": (c_int64, [c_void_p]),
+    "fm_plan_lm_head": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "fm_draft": (c_int, [c_void_p, ctypes.POINTER(DraftIO), c_void_p]),
     "fm_extend_context": (c_int, [c_void_p, ctypes.POINTER(ExtendIO), c_void_p]),
     "fm_forward": (c_int, [c_void_p, ctypes.POINTER(ForwardIO), c_void_p]),

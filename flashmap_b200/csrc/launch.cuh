@@ -14,6 +14,9 @@ namespace fm {
 
 fm_status set_error(fm_status code, const char* fmt, ...);
 
+// kernels launched by this thread through launch_kernel (for launch accounting)
+long long& launch_counter();
+
 inline fm_status check_cuda(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return FM_OK;
   return set_error(FM_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -38,6 +41,7 @@ fm_status launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t 
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (e != cudaSuccess) return set_error(FM_ERR_LAUNCH, "kernel launch failed: %s", cudaGetErrorString(e));
+  ++launch_counter();
   return FM_OK;
 }
 

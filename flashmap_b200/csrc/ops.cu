@@ -311,6 +311,7 @@ __global__ void __launch_bounds__(RT) draft_prep_kernel(DraftPrepArgs a) {
   if (threadIdx.x == 0) {
     a.anchor_pos[b] = len;
     a.anchor_seq[b] = b;
+    if (b == 0 && a.offset_bump) *a.offset_bump += 1u;
   }
   for (int k = threadIdx.x; k < a.K; k += RT) {
     a.slot_pos[b * a.K + k] = len + 1 + k;
@@ -356,9 +357,11 @@ __device__ __forceinline__ void normal_pair(uint64_t seed, uint32_t offset, long
   z1 = rad * sv;
 }
 
-__global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset) {
+__global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
+                                          const uint32_t* offset_ptr) {
   pdl_wait();
   pdl_launch_dependents();
+  if (offset_ptr) offset += *offset_ptr;
   const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (2 * p >= count) return;
   float z0, z1;
@@ -367,9 +370,11 @@ __global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, u
   if (2 * p + 1 < count) out[2 * p + 1] = f2bf(z1);
 }
 
-__global__ void philox_normal_f32_kernel(float* out, long long count, uint64_t seed, uint32_t offset) {
+__global__ void philox_normal_f32_kernel(float* out, long long count, uint64_t seed, uint32_t offset,
+                                         const uint32_t* offset_ptr) {
   pdl_wait();
   pdl_launch_dependents();
+  if (offset_ptr) offset += *offset_ptr;
   const long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (2 * p >= count) return;
   float z0, z1;
@@ -627,14 +632,14 @@ fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(mix_state_kernel, dim3(a.T), dim3(RT), 0, s, pdl, a);
 }
 fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
-                                    cudaStream_t s, bool pdl) {
+                                    const uint32_t* offset_ptr, cudaStream_t s, bool pdl) {
   return launch_kernel(philox_normal_bf16_kernel, dim3(blocks_for((count + 1) / 2, 256)), dim3(256), 0, s, pdl,
-                       out, count, seed, offset);
+                       out, count, seed, offset, offset_ptr);
 }
-fm_status launch_philox_normal_f32(float* out, long long count, uint64_t seed, uint32_t offset, cudaStream_t s,
-                                   bool pdl) {
+fm_status launch_philox_normal_f32(float* out, long long count, uint64_t seed, uint32_t offset,
+                                   const uint32_t* offset_ptr, cudaStream_t s, bool pdl) {
   return launch_kernel(philox_normal_f32_kernel, dim3(blocks_for((count + 1) / 2, 256)), dim3(256), 0, s, pdl, out,
-                       count, seed, offset);
+                       count, seed, offset, offset_ptr);
 }
 fm_status launch_argmax_tokens(const unsigned long long* keys, int64_t* tokens, int n, cudaStream_t s, bool pdl) {
   return launch_kernel(argmax_tokens_kernel, dim3(blocks_for(n, 128)), dim3(128), 0, s, pdl, keys, tokens, n);
@@ -695,7 +700,7 @@ extern "C" fm_status fm_rope_table(float* cos_out, float* sin_out, int64_t max_p
 extern "C" fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, uint32_t offset, fm_stream stream) {
   if (!out) return set_error(FM_ERR_INVALID, "philox_normal: null pointer");
   if (count <= 0) return FM_OK;
-  return launch_philox_normal_bf16(bf(out), count, seed, offset, as_stream(stream), false);
+  return launch_philox_normal_bf16(bf(out), count, seed, offset, nullptr, as_stream(stream), false);
 }
 
 extern "C" fm_status fm_block_self_attn(const void* qkv, void* out, int64_t batch, int64_t block, int64_t heads,

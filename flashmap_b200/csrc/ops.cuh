@@ -22,6 +22,7 @@ struct DraftPrepArgs {
   int B, K, Ht;
   long long V;
   int rope_len, cache_len;
+  uint32_t* offset_bump;  // incremented once per draft when non-null
   int* err;
 };
 fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl);
@@ -40,10 +41,11 @@ struct MixArgs {
 };
 fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl);
 
+// offset_ptr (device, optional): its value is added to `offset` when the kernel runs
 fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
-                                    cudaStream_t s, bool pdl);
-fm_status launch_philox_normal_f32(float* out, long long count, uint64_t seed, uint32_t offset, cudaStream_t s,
-                                   bool pdl);
+                                    const uint32_t* offset_ptr, cudaStream_t s, bool pdl);
+fm_status launch_philox_normal_f32(float* out, long long count, uint64_t seed, uint32_t offset,
+                                   const uint32_t* offset_ptr, cudaStream_t s, bool pdl);
 fm_status launch_argmax_tokens(const unsigned long long* keys, int64_t* tokens, int n, cudaStream_t s, bool pdl);
 
 // multi-step state featurisation inputs: rows [0, T) = bf16(softmax(state * c)) (when with_posterior),

@@ -60,6 +60,7 @@ struct fm_plan {
   std::vector<GemmPlan> g_layer;  // 6 per layer: qkv, o, q, cross_o, mlp1, mlp2
   CUtensorMap cache_map;
   bool has_target;
+  long long last_launches;
 };
 
 namespace {
@@ -386,6 +387,18 @@ extern "C" fm_status fm_plan_destroy(fm_plan* p) {
 
 extern "C" int32_t* fm_plan_error_word(fm_plan* p) { return p ? p->err : nullptr; }
 
+extern "C" int64_t fm_plan_last_launches(const fm_plan* p) { return p ? p->last_launches : -1; }
+
+extern "C" fm_status fm_plan_lm_head(fm_plan* p, void* logits, int64_t ldl, fm_stream stream) {
+  if (!p || !p->has_target) return set_error(FM_ERR_INVALID, "lm_head: plan without target");
+  GemmPlan lm = p->g_lm;
+  lm.args.out = logits ? static_cast<__nv_bfloat16*>(logits) : p->logits_s;
+  lm.args.ldo = logits ? ldl : p->S;
+  lm.args.scatter = 0;
+  lm.args.col_ids = reinterpret_cast<const long long*>(p->m.draft_ids);
+  return gemm_launch(lm, static_cast<cudaStream_t>(stream), false);
+}
+
 namespace {
 
 fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s) {
@@ -471,6 +484,12 @@ extern "C" fm_status fm_forward(fm_plan* p, const fm_forward_io* io, fm_stream s
 extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream stream) {
   if (!p || !io || !io->anchor_ids || !io->lengths) return set_error(FM_ERR_INVALID, "draft: null argument");
   if (!p->has_target) return set_error(FM_ERR_INVALID, "draft: the plan was built without the target's weights");
+  const long long launches0 = launch_counter();
+  struct Count {
+    fm_plan* p;
+    long long l0;
+    ~Count() { p->last_launches = launch_counter() - l0; }
+  } count{p, launches0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const fm_model_desc& m = p->m;
   const int T = p->T, Ht = p->Ht, S = p->S;
@@ -490,6 +509,7 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
   pa.V = m.vocab;
   pa.rope_len = m.rope_len;
   pa.cache_len = p->cfg.cache_len;
+  pa.offset_bump = io->offset_ptr;
   pa.err = p->err;
   if ((st = launch_draft_prep(pa, s, true))) return st;
   if ((st = gemm_launch(p->g_anchor_proj, s, true))) return st;
@@ -514,7 +534,7 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
         if ((st = check_cuda(cudaMemcpyAsync(p->z, io->z, (size_t)T * Ht * 2, cudaMemcpyDeviceToDevice, s),
                              "draft: copy z")))
           return st;
-      } else if ((st = launch_philox_normal_bf16(p->z, (long long)T * Ht, io->seed, io->offset, s, true))) {
+      } else if ((st = launch_philox_normal_bf16(p->z, (long long)T * Ht, io->seed, io->offset, io->offset_ptr, s, true))) {
         return st;
       }
       if ((st = gemm_launch(p->g_zl, s, true))) return st;
@@ -527,7 +547,7 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
           if ((st = check_cuda(cudaMemcpyAsync(p->state, io->noise, (size_t)T * S * 4, cudaMemcpyDeviceToDevice, s),
                                "draft: copy noise")))
             return st;
-        } else if ((st = launch_philox_normal_f32(p->state, (long long)T * S, io->seed, io->offset, s, true))) {
+        } else if ((st = launch_philox_normal_f32(p->state, (long long)T * S, io->seed, io->offset, io->offset_ptr, s, true))) {
           return st;
         }
       }

@@ -38,6 +38,11 @@ fm_status set_error(fm_status code, const char* fmt, ...) {
   return code;
 }
 
+long long& launch_counter() {
+  static thread_local long long n = 0;
+  return n;
+}
+
 int num_sms() {
   static thread_local int dev_cached = -1, sms = 148;
   int dev = 0;

@@ -376,8 +376,9 @@ class _Plan:
             pass
 
     def draft(self, anchor_ids, seed: int, offset: int, logits=None, ldl=0, scatter=False, tokens=None, z=None,
-              noise=None, hidden=None):
+              noise=None, hidden=None, offset_dev=None):
         io = _lib.DraftIO()
+        io.offset_ptr = None if offset_dev is None else offset_dev.data_ptr()
         io.anchor_ids, io.lengths = anchor_ids.data_ptr(), self.cache.lengths.data_ptr()
         io.z = None if z is None else z.data_ptr()
         io.noise = None if noise is None else noise.data_ptr()
@@ -399,6 +400,14 @@ class _Plan:
         io.target_hidden, io.rows = hidden_rows.data_ptr(), hidden_rows.shape[0]
         io.cu_rows, io.lengths, io.batch = cu_rows.data_ptr(), self.cache.lengths.data_ptr(), batch
         _lib.check(_lib.load().fm_extend_context(self.handle, ctypes.byref(io), _stream_handle()), "fm_extend_context")
+
+    def lm_head(self, logits=None) -> None:
+        """Launch the LM-head GEMM of the plan alone (timing the pass's largest kernel)."""
+        _lib.check(_lib.load().fm_plan_lm_head(self.handle, _ptr(logits), 0 if logits is None else logits.shape[-1],
+                                               _stream_handle()), "fm_plan_lm_head")
+
+    def last_launches(self) -> int:
+        return int(_lib.load().fm_plan_last_launches(self.handle))
 
     def check_device_errors(self):
         code = int(self.err.item())
@@ -699,4 +708,77 @@ class FlashMapDraftModel(PreTrainedModel):
                                       acceptance_lengths=lengths)
 
 
-__all__ = ["FlashMapCache", "FlashMapDraftModel", "FlashMapGenerateOutput"]
+class DraftSession:
+    """A serving-loop draft: one ``fm_draft`` captured in a CUDA graph over a
+    fixed cache, batch and number of jumps, replayed per call.
+
+    ``draft(anchor_ids)`` copies the anchors from pinned host memory, replays
+    the graph (all ~100 kernels, chained by programmatic dependent launch) and
+    returns the drafted tokens in pinned host memory.  Every replay draws fresh
+    Philox noise (a device counter advances per draft).  The cache's per-
+    sequence lengths are read on the device, so ``extend_context`` between
+    replays is honoured without re-capturing."""
+
+    def __init__(self, model: "FlashMapDraftModel", cache: FlashMapCache, embed_tokens: nn.Module, lm_head: nn.Module,
+                 num_steps: Optional[int] = None, with_logits: bool = False, seed: Optional[int] = None,
+                 use_graph: bool = True):
+        model._check_cache(cache)
+        num_steps = model._steps(num_steps)
+        self.model, self.cache = model, cache
+        pack = model._pack(cache.kv.device, embed_tokens, lm_head)
+        model._caches.add(cache)
+        B, K = cache.kv.shape[2], model.config.block_size
+        self.plan = model._plan(pack, cache, B, num_steps)
+        dev = cache.kv.device
+        self.B, self.K = B, K
+        self.anchor = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.tokens = torch.zeros(B * K, dtype=torch.int64, device=dev)
+        self.offset = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.logits = None
+        self.scatter = pack.draft_ids is not None
+        if with_logits:
+            self.logits = torch.full((B * K, model.config.vocab_size), float("-inf"), device=dev,
+                                     dtype=torch.bfloat16)
+        self.seed = int(torch.initial_seed() if seed is None else seed)
+        self.anchor_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.tokens_host = torch.zeros(B * K, dtype=torch.int64).pin_memory()
+        self.graph = None
+        self._launch()  # eager warm-up: builds every lazy constant before capture
+        torch.cuda.synchronize(dev)
+        if use_graph:
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._launch()
+            torch.cuda.synchronize(dev)
+
+    def _launch(self):
+        self.plan.draft(self.anchor, self.seed, 0, logits=self.logits,
+                        ldl=0 if self.logits is None else self.logits.shape[1], scatter=self.scatter,
+                        tokens=self.tokens, offset_dev=self.offset)
+
+    def replay(self) -> None:
+        """One draft on the device with the current contents of the static buffers."""
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._launch()
+
+    @property
+    def launches(self) -> int:
+        """Kernels one draft launches."""
+        return self.plan.last_launches()
+
+    def draft(self, anchor_ids) -> torch.Tensor:
+        """Anchor ids (B,) (host or device) -> drafted tokens (B, K) in pinned host memory."""
+        if isinstance(anchor_ids, torch.Tensor) and anchor_ids.is_cuda:
+            self.anchor.copy_(anchor_ids, non_blocking=True)
+        else:
+            self.anchor_host.copy_(torch.as_tensor(anchor_ids, dtype=torch.int64).reshape(-1))
+            self.anchor.copy_(self.anchor_host, non_blocking=True)
+        self.replay()
+        self.tokens_host.copy_(self.tokens, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return self.tokens_host.view(self.B, self.K)
+
+
+__all__ = ["DraftSession", "FlashMapCache", "FlashMapDraftModel", "FlashMapGenerateOutput"]

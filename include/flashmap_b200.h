@@ -242,6 +242,11 @@ FM_API fm_status fm_plan_create(const fm_model_desc* model, const fm_plan_config
 FM_API fm_status fm_plan_destroy(fm_plan* plan);
 /* Device error word of the plan (int32, 0 = none). */
 FM_API int32_t* fm_plan_error_word(fm_plan* plan);
+/* Kernels launched by the plan's last fm_draft call. */
+FM_API int64_t fm_plan_last_launches(const fm_plan* plan);
+/* The plan's LM-head GEMM alone (logits + argmax of the plan's current DiT
+ * output; state-vocabulary columns), for timing the pass's largest kernel. */
+FM_API fm_status fm_plan_lm_head(fm_plan* plan, void* logits, int64_t ldl, fm_stream stream);
 
 typedef struct fm_draft_io {
   const int64_t* anchor_ids; /* [B] device */
@@ -249,7 +254,9 @@ typedef struct fm_draft_io {
   const void* z;             /* [B*K, Ht] bf16 one-step noise, or NULL (drawn by Philox) */
   const float* noise;        /* [B*K, S] fp32 multi-step start state, or NULL (drawn) */
   uint64_t seed;
-  uint32_t offset;           /* Philox counter word 2 for this draft */
+  uint32_t offset;           /* Philox counter word 2 for this draft ... */
+  uint32_t* offset_ptr;      /* ... plus this device word when non-NULL; every draft first increments it,
+                                so replays of a captured draft draw fresh noise */
   void* logits;              /* [B*K, ldl] bf16 output or NULL */
   int64_t ldl;               /* logits row stride (V, or S when not scattering) */
   int32_t scatter;           /* 1: write at draft_ids columns of a V-wide row */
