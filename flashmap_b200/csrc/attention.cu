@@ -5,56 +5,67 @@
 namespace fm {
 
 // ------------------------------------------------------------------ self-attention
-__global__ void __launch_bounds__(128) self_attn_kernel(SelfAttnArgs a) {
+// One CTA of 256 threads per (sequence, head).  q and k rows are padded by one
+// float in shared memory so the per-pair dot products read distinct banks.
+constexpr int SA_THREADS = 256;
+
+__global__ void __launch_bounds__(SA_THREADS) self_attn_kernel(SelfAttnArgs a) {
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x / a.heads, h = blockIdx.x % a.heads;
-  const int K = a.block, hd = a.head_dim, D = a.hidden;
+  const int K = a.block, hd = a.head_dim, D = a.hidden, ld = hd + 1;
   extern __shared__ float sm[];
   float* sq = sm;
-  float* sk = sq + K * hd;
-  float* sv = sk + K * hd;
-  float* sp = sv + K * hd;
-  float* sl = sp + K * K;
-  for (int idx = threadIdx.x; idx < K * hd; idx += blockDim.x) {
-    const int i = idx / hd, d = idx % hd;
+  float* sk = sq + K * ld;
+  float* sv = sk + K * ld;
+  float* sp = sv + K * hd;  // [K][K + 1]
+  float* sl = sp + K * (K + 1);
+  for (int idx = threadIdx.x; idx < K * hd / 2; idx += SA_THREADS) {
+    const int i = (2 * idx) / hd, d = (2 * idx) % hd;
     const __nv_bfloat16* row = a.qkv + (long long)(b * K + i) * 3 * D + h * hd + d;
-    sq[idx] = bf2f(row[0]);
-    sk[idx] = bf2f(row[D]);
-    sv[idx] = bf2f(row[2 * D]);
+    const __nv_bfloat162 q2 = *reinterpret_cast<const __nv_bfloat162*>(row);
+    const __nv_bfloat162 k2 = *reinterpret_cast<const __nv_bfloat162*>(row + D);
+    const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(row + 2 * D);
+    sq[i * ld + d] = __low2float(q2);
+    sq[i * ld + d + 1] = __high2float(q2);
+    sk[i * ld + d] = __low2float(k2);
+    sk[i * ld + d + 1] = __high2float(k2);
+    sv[i * hd + d] = __low2float(v2);
+    sv[i * hd + d + 1] = __high2float(v2);
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < K * K; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < K * K; idx += SA_THREADS) {
     const int i = idx / K, j = idx % K;
-    float s = 0.0f;
-    for (int d = 0; d < hd; ++d) s = fmaf(sq[i * hd + d], sk[j * hd + d], s);
-    sp[idx] = __fmul_rn(s, a.scale);
+    float acc = 0.0f;
+    for (int d = 0; d < hd; ++d) acc = fmaf(sq[i * ld + d], sk[j * ld + d], acc);
+    sp[i * (K + 1) + j] = __fmul_rn(acc, a.scale);
   }
   __syncthreads();
-  if (threadIdx.x < K) {
-    const int i = threadIdx.x;
+  for (int i = threadIdx.x; i < K; i += SA_THREADS) {
     float m = -INFINITY;
-    for (int j = 0; j < K; ++j) m = fmaxf(m, sp[i * K + j]);
+    for (int j = 0; j < K; ++j) m = fmaxf(m, sp[i * (K + 1) + j]);
     float l = 0.0f;
     for (int j = 0; j < K; ++j) {
-      const float e = expf(__fsub_rn(sp[i * K + j], m));
+      const float e = expf(__fsub_rn(sp[i * (K + 1) + j], m));
       l = __fadd_rn(l, e);
-      sp[i * K + j] = round_bf(e);
+      sp[i * (K + 1) + j] = round_bf(e);  // bf16 numerators, fp32 sum
     }
     sl[i] = l;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < K * hd; idx += blockDim.x) {
+  for (int idx = threadIdx.x; idx < K * hd; idx += SA_THREADS) {
     const int i = idx / hd, d = idx % hd;
     float acc = 0.0f;
-    for (int j = 0; j < K; ++j) acc = fmaf(sp[i * K + j], sv[j * hd + d], acc);
+    for (int j = 0; j < K; ++j) acc = fmaf(sp[i * (K + 1) + j], sv[j * hd + d], acc);
     a.out[(long long)(b * K + i) * D + h * hd + d] = f2bf(__fdiv_rn(acc, sl[i]));
   }
 }
 
 fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl) {
-  const size_t smem = (size_t)(3 * a.block * a.head_dim + a.block * a.block + a.block) * sizeof(float);
+  const int K = a.block, hd = a.head_dim;
+  const size_t smem = (size_t)(2 * K * (hd + 1) + K * hd + K * (K + 1) + K) * sizeof(float);
   if (smem > 200 * 1024) return set_error(FM_ERR_SHAPE, "self-attention block too large");
+  if (hd % 2) return set_error(FM_ERR_SHAPE, "self-attention needs an even head_dim");
   static int configured = -1;
   int dev;
   cudaGetDevice(&dev);
@@ -62,7 +73,7 @@ fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream
     cudaFuncSetAttribute(self_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     configured = dev;
   }
-  return launch_kernel(self_attn_kernel, dim3(batch * a.heads), dim3(128), smem, stream, pdl, a);
+  return launch_kernel(self_attn_kernel, dim3(batch * a.heads), dim3(SA_THREADS), smem, stream, pdl, a);
 }
 
 // ------------------------------------------------------------------ cross-attention
@@ -140,7 +151,8 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
   const int per = ((((ctx + a.nsplit - 1) / a.nsplit) + XA_TILE - 1) / XA_TILE) * XA_TILE;
   const int k_begin = split * per;
   const int k_end = min(ctx, k_begin + per);
-  const int ntiles = k_begin < k_end ? (k_end - k_begin + XA_TILE - 1) / XA_TILE : 0;
+  if (k_begin >= ctx) return;  // no keys here; the merge counts only splits that own keys
+  const int ntiles = (k_end - k_begin + XA_TILE - 1) / XA_TILE;
   const long long krow = ((((long long)a.layer * 2 + 0) * a.cache_batch + b) * a.heads + h) * a.cache_len;
   const long long vrow = ((((long long)a.layer * 2 + 1) * a.cache_batch + b) * a.heads + h) * a.cache_len;
 
@@ -283,17 +295,17 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
   l1 = __fadd_rn(l1, __shfl_xor_sync(0xffffffffu, l1, 2));
   __syncthreads();  // pipeline smem is free from here on
 
-  // merge the 4 warps: mrg[w][16][HD] = O, then m[4][16], l[4][16]
+  // merge the 4 warps: mO[w][16][HD], mM / mL [4][16], then per-row weights
   float* mO = mrg;
   float* mM = mrg + 4 * 16 * HD;
   float* mL = mM + 64;
+  float* mF = mL + 64;   // [4][16] exp(m_w - m)
+  float* mR = mF + 64;   // [16] merged m, [16] merged l
 #pragma unroll
   for (int i = 0; i < NT; ++i) {
     const int col = i * 8 + tig * 2;
-    mO[(warp * 16 + gid) * HD + col] = o[i][0];
-    mO[(warp * 16 + gid) * HD + col + 1] = o[i][1];
-    mO[(warp * 16 + gid + 8) * HD + col] = o[i][2];
-    mO[(warp * 16 + gid + 8) * HD + col + 1] = o[i][3];
+    *reinterpret_cast<float2*>(&mO[(warp * 16 + gid) * HD + col]) = make_float2(o[i][0], o[i][1]);
+    *reinterpret_cast<float2*>(&mO[(warp * 16 + gid + 8) * HD + col]) = make_float2(o[i][2], o[i][3]);
   }
   if (tig == 0) {
     mM[warp * 16 + gid] = m0;
@@ -302,59 +314,113 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
     mL[warp * 16 + gid + 8] = l1;
   }
   __syncthreads();
-  const int nsp = a.nsplit;
-  float* mine = a.part + (long long)(bh * nsp + split) * (16 * HD + 32);
-  for (int idx = threadIdx.x; idx < 16 * HD; idx += 128) {
-    const int i = idx / HD;
+  if (threadIdx.x < 16) {
+    const int i = threadIdx.x;
     float mm = -INFINITY;
     for (int w = 0; w < 4; ++w) mm = fmaxf(mm, mM[w * 16 + i]);
-    float ll = 0.0f, oo = 0.0f;
+    float ll = 0.0f;
     for (int w = 0; w < 4; ++w) {
       const float f = mM[w * 16 + i] == -INFINITY ? 0.0f : expf(__fsub_rn(mM[w * 16 + i], mm));
+      mF[w * 16 + i] = f;
       ll = __fadd_rn(ll, __fmul_rn(mL[w * 16 + i], f));
-      oo = __fadd_rn(oo, __fmul_rn(mO[(w * 16 + i) * HD + (idx % HD)], f));
     }
-    if (nsp == 1) {
-      a.out[(long long)(b * 16 + i) * a.hidden + h * HD + (idx % HD)] = f2bf(__fdiv_rn(oo, ll));
+    mR[i] = mm;
+    mR[16 + i] = ll;
+  }
+  __syncthreads();
+  const int nsp = a.nsplit;
+  const int n_active = (ctx + per - 1) / per;  // splits that own keys (the rest exit above)
+  float* mine = a.part + (long long)(bh * nsp + split) * (16 * HD + 32);
+  // each thread: 4 consecutive dims of one row per step (float4)
+  for (int v4 = threadIdx.x; v4 < 16 * HD / 4; v4 += 128) {
+    const int i = (v4 * 4) / HD, d = (v4 * 4) % HD;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float f = mF[w * 16 + i];
+      const float4 ow = *reinterpret_cast<const float4*>(&mO[(w * 16 + i) * HD + d]);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(ow.x, f));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(ow.y, f));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(ow.z, f));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(ow.w, f));
+    }
+    if (n_active == 1) {
+      const float ll = mR[16 + i];
+      __nv_bfloat16* dst = a.out + (long long)(b * 16 + i) * a.hidden + h * HD + d;
+      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(__fdiv_rn(acc.x, ll), __fdiv_rn(acc.y, ll));
+      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(__fdiv_rn(acc.z, ll), __fdiv_rn(acc.w, ll));
     } else {
-      __stcg(mine + idx, oo);
-      if (idx % HD == 0) {
-        __stcg(mine + 16 * HD + i, mm);
-        __stcg(mine + 16 * HD + 16 + i, ll);
-      }
+      __stcg(reinterpret_cast<float4*>(mine + i * HD + d), acc);
     }
   }
-  if (nsp == 1) return;
+  if (n_active == 1) return;
+  if (threadIdx.x < 16) {
+    __stcg(mine + 16 * HD + threadIdx.x, mR[threadIdx.x]);
+    __stcg(mine + 16 * HD + 16 + threadIdx.x, mR[16 + threadIdx.x]);
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int old = atomicAdd(a.counters + bh, 1);
-    sflag[1] = (old == nsp - 1);
+    sflag[1] = (old == n_active - 1);
   }
   __syncthreads();
   if (!sflag[1]) return;
   __threadfence();
+  // last split of this (sequence, head): merge all splits in split order
   const float* base = a.part + (long long)bh * nsp * (16 * HD + 32);
-  for (int idx = threadIdx.x; idx < 16 * HD; idx += 128) {
-    const int i = idx / HD;
+  float* sF = mO;  // reuse: [n_active][16] weights, then [16] l
+  for (int t = threadIdx.x; t < 16; t += 128) {
     float mm = -INFINITY;
-    for (int sp = 0; sp < nsp; ++sp) mm = fmaxf(mm, __ldcg(base + (long long)sp * (16 * HD + 32) + 16 * HD + i));
-    float ll = 0.0f, oo = 0.0f;
-    for (int sp = 0; sp < nsp; ++sp) {
+    for (int sp = 0; sp < n_active; ++sp) mm = fmaxf(mm, __ldcg(base + (long long)sp * (16 * HD + 32) + 16 * HD + t));
+    float ll = 0.0f;
+    for (int sp = 0; sp < n_active; ++sp) {
       const float* ps = base + (long long)sp * (16 * HD + 32);
-      const float ms = __ldcg(ps + 16 * HD + i);
+      const float ms = __ldcg(ps + 16 * HD + t);
       const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, mm));
-      ll = __fadd_rn(ll, __fmul_rn(__ldcg(ps + 16 * HD + 16 + i), f));
-      oo = __fadd_rn(oo, __fmul_rn(__ldcg(ps + idx), f));
+      sF[sp * 16 + t] = f;
+      ll = __fadd_rn(ll, __fmul_rn(__ldcg(ps + 16 * HD + 16 + t), f));
     }
-    a.out[(long long)(b * 16 + i) * a.hidden + h * HD + (idx % HD)] = f2bf(__fdiv_rn(oo, ll));
+    sF[n_active * 16 + t] = ll;
+  }
+  __syncthreads();
+  for (int v4 = threadIdx.x; v4 < 16 * HD / 4; v4 += 128) {
+    const int i = (v4 * 4) / HD, d = (v4 * 4) % HD;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int sp = 0;
+    for (; sp + 4 <= n_active; sp += 4) {
+      float4 t4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        t4[u] = __ldcg(reinterpret_cast<const float4*>(base + (long long)(sp + u) * (16 * HD + 32) + i * HD + d));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float f = sF[(sp + u) * 16 + i];
+        acc.x = __fadd_rn(acc.x, __fmul_rn(t4[u].x, f));
+        acc.y = __fadd_rn(acc.y, __fmul_rn(t4[u].y, f));
+        acc.z = __fadd_rn(acc.z, __fmul_rn(t4[u].z, f));
+        acc.w = __fadd_rn(acc.w, __fmul_rn(t4[u].w, f));
+      }
+    }
+    for (; sp < n_active; ++sp) {
+      const float4 t = __ldcg(reinterpret_cast<const float4*>(base + (long long)sp * (16 * HD + 32) + i * HD + d));
+      const float f = sF[sp * 16 + i];
+      acc.x = __fadd_rn(acc.x, __fmul_rn(t.x, f));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(t.y, f));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(t.z, f));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(t.w, f));
+    }
+    const float ll = sF[n_active * 16 + i];
+    __nv_bfloat16* dst = a.out + (long long)(b * 16 + i) * a.hidden + h * HD + d;
+    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(__fdiv_rn(acc.x, ll), __fdiv_rn(acc.y, ll));
+    *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(__fdiv_rn(acc.z, ll), __fdiv_rn(acc.w, ll));
   }
   if (threadIdx.x == 0) a.counters[bh] = 0;
 }
 
 size_t cross_attn_smem(int hd) {
   const size_t pipe = (size_t)XA_STAGES * 2 * XA_TILE * hd * 2;
-  const size_t merge = (size_t)(4 * 16 * hd + 128) * sizeof(float);
+  const size_t merge = (size_t)(4 * 16 * hd + 256) * sizeof(float);
   return 1024 + (pipe > merge ? pipe : merge) + 128;
 }
 

@@ -1,4 +1,6 @@
 // Host side of the tcgen05 GEMM: template dispatch, plans and the C ABI.
+#include <cstdlib>
+
 #include "gemm_plan.cuh"
 
 namespace fm {
@@ -64,9 +66,16 @@ int gemm_bn_for(int64_t N) {
   return 256;
 }
 
+// CTAs of a launch: one per SM by default.  FM_GEMM_CTAS_PER_SM (tuning
+// experiments) scales it; the result never exceeds the unit count.
 static int64_t gemm_grid_for(int64_t units) {
-  const int64_t sms = num_sms();
-  return units < sms ? units : sms;
+  static const int per_sm = [] {
+    const char* e = getenv("FM_GEMM_CTAS_PER_SM");
+    const int v = e ? atoi(e) : 1;
+    return v >= 1 && v <= 4 ? v : 1;
+  }();
+  const int64_t g = (int64_t)num_sms() * per_sm;
+  return units < g ? units : g;
 }
 
 size_t gemm_partials_bytes(int64_t M, int64_t N, int64_t K) {

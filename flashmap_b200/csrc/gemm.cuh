@@ -173,6 +173,24 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
         w = a.norm_w0 + (long long)layer * a.norm_layer_stride;
       const float wd = bf2f(w[d]);
       const int half = hd >> 1;
+      // all positions, then all rotary factors: independent loads issued together
+      int pos[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = n0 + j;
+        int pj = (n < a.N) ? a.positions[n] : 0;
+        if (pj < 0 || pj >= a.rope_len) {
+          if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
+          pj = 0;
+        }
+        pos[j] = pj;
+      }
+      float rc[16], rs[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        rc[j] = a.rope_cos[(long long)pos[j] * half + (d >> 1)];
+        rs[j] = a.rope_sin[(long long)pos[j] * half + (d >> 1)];
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float tot = 0.0f;
@@ -182,14 +200,8 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
         const float scale = round_bf(__fmul_rn(wd, inv));
         const float xn = round_bf(__fmul_rn(y[j], scale));
         const float other = __shfl_xor_sync(0xffffffffu, xn, 1);
-        const int n = n0 + j;
-        int pos = (n < a.N) ? a.positions[n] : 0;
-        if (pos < 0 || pos >= a.rope_len) {
-          if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
-          pos = 0;
-        }
-        const float cs = a.rope_cos[(long long)pos * half + (d >> 1)];
-        const float sn = a.rope_sin[(long long)pos * half + (d >> 1)];
+        const float cs = rc[j];
+        const float sn = rs[j];
         float o;
         if ((d & 1) == 0)
           o = __fsub_rn(__fmul_rn(xn, cs), __fmul_rn(other, sn));
@@ -456,17 +468,30 @@ __global__ void __launch_bounds__(192, 1)
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-            for (long long cc = c_first; cc <= c_last; ++cc) {
-              if (cc == c) {
+            // partials are summed in contributor order (deterministic); the loads
+            // of four contributors are issued together to overlap their latency
+            for (long long cc0 = c_first; cc0 <= c_last; cc0 += 4) {
+              float t[4][16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], own[j]);
-              } else {
-                const long long first_tile = ((long long)cc * U / G) / kb;
-                const int cs = (first_tile == tile) ? 0 : 1;
-                const float* p = a.ws + ((cc * 2 + cs) * BN + c0) * 128 + r;
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const long long cc = cc0 + q4;
+                if (cc <= c_last && cc != c) {
+                  const long long first_tile = ((long long)cc * U / G) / kb;
+                  const int cs = (first_tile == tile) ? 0 : 1;
+                  const float* p = a.ws + ((cc * 2 + cs) * BN + c0) * 128 + r;
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], __ldcg(p + (long long)j * 128));
+                  for (int j = 0; j < 16; ++j) t[q4][j] = __ldcg(p + (long long)j * 128);
+                } else {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) t[q4][j] = own[j];
+                }
               }
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                if (cc0 + q4 <= c_last) {
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], t[q4][j]);
+                }
             }
             epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64);
           }

@@ -257,28 +257,45 @@ __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, con
   }
 }
 
+// AdaLN of one row: the row is read once into registers (VPT values per
+// thread, cols <= VPT * 256), then mean, variance and the modulated output.
+template <int VPT>
 __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const __nv_bfloat16* mod,
                                                    __nv_bfloat16* y, int cols, float eps) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
   const __nv_bfloat16* xr = x + (long long)blockIdx.x * cols;
+  float v[VPT];
   float s = 0.0f;
-  for (int c = threadIdx.x; c < cols; c += RT) s = __fadd_rn(s, bf2f(xr[c]));
-  const float mean = __fdiv_rn(block_sum(s, red), (float)cols);
-  float v = 0.0f;
-  for (int c = threadIdx.x; c < cols; c += RT) {
-    const float d = __fsub_rn(bf2f(xr[c]), mean);
-    v = __fmaf_rn(d, d, v);
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * RT;
+    v[i] = c < cols ? bf2f(xr[c]) : 0.0f;
+    s = __fadd_rn(s, v[i]);
   }
-  const float var = __fdiv_rn(block_sum(v, red), (float)cols);
+  const float mean = __fdiv_rn(block_sum(s, red), (float)cols);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * RT;
+    if (c < cols) {
+      const float d = __fsub_rn(v[i], mean);
+      q = __fmaf_rn(d, d, q);
+    }
+  }
+  const float var = __fdiv_rn(block_sum(q, red), (float)cols);
   const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   __nv_bfloat16* yr = y + (long long)blockIdx.x * cols;
-  for (int c = threadIdx.x; c < cols; c += RT) {
-    const float ln = round_bf(__fmul_rn(__fsub_rn(bf2f(xr[c]), mean), rstd));
-    const float one_plus = round_bf(__fadd_rn(1.0f, bf2f(mod[c])));
-    const float scaled = round_bf(__fmul_rn(ln, one_plus));
-    yr[c] = f2bf(__fadd_rn(scaled, bf2f(mod[cols + c])));
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int c = threadIdx.x + i * RT;
+    if (c < cols) {
+      const float ln = round_bf(__fmul_rn(__fsub_rn(v[i], mean), rstd));
+      const float one_plus = round_bf(__fadd_rn(1.0f, bf2f(mod[c])));
+      const float scaled = round_bf(__fmul_rn(ln, one_plus));
+      yr[c] = f2bf(__fadd_rn(scaled, bf2f(mod[cols + c])));
+    }
   }
 }
 
@@ -623,7 +640,13 @@ fm_status launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bf
 }
 fm_status launch_adaln(const __nv_bfloat16* x, const __nv_bfloat16* mod, __nv_bfloat16* y, int64_t rows,
                        int64_t cols, float eps, cudaStream_t s, bool pdl) {
-  return launch_kernel(adaln_kernel, dim3((unsigned)rows), dim3(RT), 0, s, pdl, x, mod, y, (int)cols, eps);
+  const dim3 g((unsigned)rows), b(RT);
+  if (cols <= 1 * RT) return launch_kernel(adaln_kernel<1>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
+  if (cols <= 4 * RT) return launch_kernel(adaln_kernel<4>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
+  if (cols <= 8 * RT) return launch_kernel(adaln_kernel<8>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
+  if (cols <= 12 * RT) return launch_kernel(adaln_kernel<12>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
+  if (cols <= 16 * RT) return launch_kernel(adaln_kernel<16>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
+  return set_error(FM_ERR_UNSUPPORTED, "adaln: width %lld above 4096", (long long)cols);
 }
 fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(draft_prep_kernel, dim3(a.B), dim3(RT), 0, s, pdl, a);

@@ -125,9 +125,10 @@ size_t max_gemm_tiles(const fm_model_desc* m, const fm_plan_config* c) {
   return (size_t)mx;
 }
 
+// splits of every (sequence, head)'s keys: about one CTA per SM in total
 int pick_nsplit(int B, int H, int cache_len) {
   const int sms = num_sms();
-  int ns = (2 * sms + B * H - 1) / (B * H);
+  int ns = (sms + B * H - 1) / (B * H);
   const int maxs = (cache_len + 63) / 64;
   if (ns > maxs) ns = maxs;
   if (ns < 1) ns = 1;

@@ -116,7 +116,7 @@ def cross_attn(q, cache_kv, lengths, layer: int, nsplit: int = 0, err=None):
     L, _, Bc, H, Tc, hd = cache_kv.shape
     B = lengths.shape[0]
     if nsplit <= 0:
-        nsplit = max(1, min((2 * 148 + B * H - 1) // (B * H), (Tc + 63) // 64))
+        nsplit = max(1, min((148 + B * H - 1) // (B * H), (Tc + 63) // 64))
     out = torch.empty(B * 16, H * hd, device=q.device, dtype=torch.bfloat16)
     wsb = _lib.load().fm_cross_attn_workspace_size(B, H, hd, nsplit)
     ws = torch.zeros(wsb, dtype=torch.uint8, device=q.device)
