@@ -89,6 +89,8 @@ _SIGNATURES = {
     "fm_accept_workspace_size": (c_size_t, [c_int64, c_int64]),
     "fm_accept_greedy": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_size_t, c_void_p]),
+    "fm_accept_greedy_noalloc": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_void_p,
+                                         c_void_p, c_void_p]),
     "fm_accept_rejection": (c_int, [c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float,
                                     c_uint64, c_uint32, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "fm_transpose_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),

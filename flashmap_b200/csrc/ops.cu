@@ -1,5 +1,7 @@
 // Row-wise, noise, sampling and acceptance kernels of the FlashMap hot path,
 // and their C-ABI entry points.
+#include <mutex>
+
 #include "attention.cuh"
 #include "ops.cuh"
 #include "philox.cuh"
@@ -886,4 +888,69 @@ extern "C" fm_status fm_add(const void* a, const void* b, void* y, int64_t n, fm
   if (n <= 0) return FM_OK;
   return launch_kernel(add_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, as_stream(stream), false, cbf(a), cbf(b),
                        bf(y), (long long)n);
+}
+
+// ====================================================================== allocation-free greedy acceptance
+//
+// Some callers cannot allocate device memory when they accept a block: a
+// serving engine that plans every device buffer before it captures its decode
+// step in a CUDA graph, or host code in another language that is handed the
+// logits and token buffers and has no device allocator of its own.  For them
+// fm_accept_greedy_noalloc keeps its per-row argmax scratch in a fixed array
+// inside this library instead of a caller workspace.
+//
+// The array is shared by every call on a device and keeps the last call's
+// contents; each call overwrites the rows it reads, so nothing needs to start
+// at zero.  Calls that overlap on the GPU (different streams, no ordering)
+// race on it.  Its device address is looked up once per device, by the first
+// call made with that device current; make that first call before any stream
+// capture begins.
+static __device__ __align__(256) int64_t g_accept_noalloc_scratch[FM_ACCEPT_NOALLOC_MAX_ROWS];
+
+namespace {
+
+int64_t* accept_noalloc_scratch(fm_status* st) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static int64_t* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *st = set_error(FM_ERR_CUDA, "accept_noalloc: no usable current device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_accept_noalloc_scratch);
+    if (e != cudaSuccess) {
+      *st = set_error(FM_ERR_CUDA, "accept_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = static_cast<int64_t*>(p);
+  }
+  *st = FM_OK;
+  return addr[dev];
+}
+
+}  // namespace
+
+extern "C" fm_status fm_accept_greedy_noalloc(const void* target_logits, int32_t dtype, const int64_t* draft,
+                                              int64_t B, int64_t K, int64_t V, int64_t* accepted, int64_t* bonus,
+                                              fm_stream stream) {
+  if (!target_logits || !draft || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept_noalloc: null pointer");
+  if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "accept_noalloc: bad arguments");
+  if (B * (K + 1) > FM_ACCEPT_NOALLOC_MAX_ROWS)
+    return set_error(FM_ERR_WORKSPACE,
+                     "accept_noalloc: %lld target rows (B*(K+1)) exceed the built-in scratch of %d rows; "
+                     "use fm_accept_greedy with a workspace",
+                     (long long)(B * (K + 1)), FM_ACCEPT_NOALLOC_MAX_ROWS);
+  fm_status st;
+  int64_t* am = accept_noalloc_scratch(&st);
+  if (!am) return st;
+  st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits, (long long)V, 0.0f,
+                          (float*)nullptr, am);
+  if (st) return st;
+  return launch_kernel(accept_greedy_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
+                       (const int64_t*)am, (int)K, accepted, bonus);
 }

@@ -148,6 +148,21 @@ FM_API fm_status fm_accept_greedy(const void* target_logits, int32_t logits_dtyp
                                   int64_t K, int64_t V, int64_t* accepted, int64_t* bonus, void* workspace,
                                   size_t workspace_bytes, fm_stream stream);
 
+/* Greedy acceptance like fm_accept_greedy, for callers that cannot allocate
+ * device memory at this point (an engine that plans all buffers before
+ * capturing its decode step in a CUDA graph; host code in another language
+ * that only holds the tensors it was given).  No counterpart in the reference:
+ * its per-row argmax scratch is a fixed array inside the library, so
+ * B*(K+1) may not exceed FM_ACCEPT_NOALLOC_MAX_ROWS (larger calls return
+ * FM_ERR_WORKSPACE).  The array is shared by all calls on a device and keeps
+ * the last call's contents; calls that overlap on the GPU race on it.  The
+ * first call on each device looks the array's address up (make it before any
+ * stream capture); no call allocates or frees memory. */
+#define FM_ACCEPT_NOALLOC_MAX_ROWS 16384
+FM_API fm_status fm_accept_greedy_noalloc(const void* target_logits, int32_t logits_dtype, const int64_t* draft,
+                                          int64_t B, int64_t K, int64_t V, int64_t* accepted, int64_t* bonus,
+                                          fm_stream stream);
+
 /* Rejection acceptance (:583-594). q [B, K, V] fp32 draft probabilities.
  * u[b,k] = uniform (k, b, offset, 1); bonus draw uniform (0, b, offset, 2). */
 FM_API fm_status fm_accept_rejection(const void* target_logits, int32_t logits_dtype, const int64_t* draft,
