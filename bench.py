@@ -103,7 +103,7 @@ def algorithmic_bytes(c: dict, context: int) -> dict:
 PROFILE_SMALL = dict(CONFIG2, num_hidden_layers=2, vocab_size=32768)
 
 
-def build_workload(seed: int = 0, small: bool = False):
+def build_workload(seed: int = 0, small: bool = False, launch: str = "auto"):
     from flashmap_b200 import DraftSession, FlashMapCache, FlashMapConfig, FlashMapDraftModel
     from flashmap_b200.synthetic import synthetic_state_dict, synthetic_target_head
     from torch import nn
@@ -112,6 +112,7 @@ def build_workload(seed: int = 0, small: bool = False):
     dev = torch.device("cuda", torch.cuda.current_device())
     with torch.device(dev):
         model = FlashMapDraftModel(config).to(torch.bfloat16).eval()
+    model.launch_mode = launch
     model.load_state_dict(synthetic_state_dict(config, seed=seed, dtype=torch.bfloat16, device=dev), strict=True)
     emb_w, head_w = synthetic_target_head(config, seed=seed, dtype=torch.bfloat16, device=dev)
     embed, head = nn.Embedding(*emb_w.shape, device=dev, dtype=torch.bfloat16), nn.Linear(1, 1, bias=False)
@@ -260,7 +261,7 @@ def run_ours(args, world, rank, local):
     from flashmap_b200 import _lib
 
     _lib.require_device()
-    config, model, cache, session = build_workload(seed=rank, small=args.profile_small)
+    config, model, cache, session = build_workload(seed=rank, small=args.profile_small, launch=args.launch)
     K = config.block_size
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
@@ -330,7 +331,8 @@ def run_ours(args, world, rank, local):
                    "batch_per_gpu": 1, "block": 16, "context": CONTEXT, "num_steps": 1,
                    "parallelism": f"replicas x{world} (request-sharded, no collective)",
                    "l2": "inputs larger than L2: %.2f GB of weights + context streamed per pass" % (nbytes["total"] / 1e9),
-                   "timing": "CUDA-graph replays, CUDA events, max over ranks"},
+                   "timing": "CUDA-graph replays, CUDA events, max over ranks",
+                   "launch": args.launch},
         "pass_us": ms_per_step * 1000.0,
         "pass_roofline": {"bound": "hbm", "algorithmic_bytes": nbytes["total"], "achieved": pass_gbs, "peak": peak,
                           "unit": "GB/s", "frac": pass_gbs / peak, "peak_kind": peak_kind,
@@ -361,6 +363,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch", choices=["auto", "kernels", "persistent"], default="auto",
+                    help="launch structure of a draft: the kernel sequence or one persistent launch")
     ap.add_argument("--profile-small", action="store_true",
                     help="2 layers and a 32768-row LM head: the same kernels on < 2 GB, for ncu captures")
     args = ap.parse_args()

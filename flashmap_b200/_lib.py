@@ -47,14 +47,18 @@ class Jump(ctypes.Structure):
 
 class PlanConfig(ctypes.Structure):
     _fields_ = [("batch", c_int32), ("num_steps", c_int32), ("jumps", ctypes.POINTER(Jump)), ("cache", c_void_p),
-                ("cache_batch", c_int32), ("cache_len", c_int32), ("max_extend_rows", c_int32)]
+                ("cache_batch", c_int32), ("cache_len", c_int32), ("max_extend_rows", c_int32),
+                ("launch_mode", c_int32)]
+
+
+LAUNCH_AUTO, LAUNCH_KERNELS, LAUNCH_PERSISTENT = 0, 1, 2
 
 
 class DraftIO(ctypes.Structure):
     _fields_ = [("anchor_ids", c_void_p), ("lengths", c_void_p), ("z", c_void_p), ("noise", c_void_p),
                 ("seed", c_uint64), ("offset", c_uint32), ("offset_ptr", c_void_p), ("logits", c_void_p),
                 ("ldl", c_int64),
-                ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p)]
+                ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p), ("trace", c_void_p)]
 
 
 class ForwardIO(ctypes.Structure):
@@ -104,6 +108,8 @@ _SIGNATURES = {
     "fm_plan_destroy": (c_int, [c_void_p]),
     "fm_plan_error_word": (c_void_p, [c_void_p]),
     "fm_plan_last_launches": (c_int64, [c_void_p]),
+    "fm_plan_persistent": (c_int32, [c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
+    "fm_plan_pass_shape": (c_int, [c_void_p, ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
     "fm_plan_lm_head": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "fm_draft": (c_int, [c_void_p, ctypes.POINTER(DraftIO), c_void_p]),
     "fm_extend_context": (c_int, [c_void_p, ctypes.POINTER(ExtendIO), c_void_p]),

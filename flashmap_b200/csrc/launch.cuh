@@ -50,6 +50,12 @@ fm_status launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t 
 fm_status make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
                          uint32_t box_rows);
 
+// The same matrix viewed as [cols / 64][rows][64] (cols % 64 == 0): boxes of
+// box_blocks consecutive 64-column blocks of box_rows rows, each block landing
+// as its own 128-byte-swizzled [box_rows x 64] tile.
+fm_status make_tmap_bf16_blocks(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                                uint32_t box_rows, uint32_t box_blocks);
+
 int num_sms();
 
 }  // namespace fm

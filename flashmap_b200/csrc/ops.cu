@@ -5,6 +5,7 @@
 #include "attention.cuh"
 #include "ops.cuh"
 #include "philox.cuh"
+#include "rows.cuh"
 
 namespace fm {
 
@@ -239,66 +240,37 @@ __device__ long long block_categorical(F weight, long long V, float u, float* sm
 
 // ------------------------------------------------------------------ kernels
 
+// One warp per row (rows.cuh gives the reduction order): 8 rows per CTA.
+constexpr int ROWS_PER_CTA = RT / 32;
+
 __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
-                                                     __nv_bfloat16* y, int cols, float eps) {
+                                                     __nv_bfloat16* y, long long rows, int cols, float eps) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[16];
-  const __nv_bfloat16* xr = x + (long long)blockIdx.x * cols;
-  float ss = 0.0f;
-  for (int c = threadIdx.x; c < cols; c += RT) {
-    const float v = bf2f(xr[c]);
-    ss = __fmaf_rn(v, v, ss);
-  }
-  ss = block_sum(ss, red);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps)));
-  __nv_bfloat16* yr = y + (long long)blockIdx.x * cols;
-  for (int c = threadIdx.x; c < cols; c += RT) {
-    const float scale = round_bf(__fmul_rn(bf2f(w[c]), inv));
-    yr[c] = f2bf(__fmul_rn(bf2f(xr[c]), scale));
-  }
+  const int lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const __nv_bfloat16* xr = x + r * cols;
+  const float inv = inv_rms(warp_row_sumsq(xr, cols, lane), cols, eps);
+  __nv_bfloat16* yr = y + r * cols;
+  for (int c = lane; c < cols; c += 32) yr[c] = f2bf(rms_value(bf2f(xr[c]), bf2f(w[c]), inv));
 }
 
-// AdaLN of one row: the row is read once into registers (VPT values per
-// thread, cols <= VPT * 256), then mean, variance and the modulated output.
-template <int VPT>
+// AdaLN of one row per warp: LayerNorm statistics, then the modulated output
+// (mod = [scale | shift], each `cols` wide)
 __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const __nv_bfloat16* mod,
-                                                   __nv_bfloat16* y, int cols, float eps) {
+                                                   __nv_bfloat16* y, long long rows, int cols, float eps) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[16];
-  const __nv_bfloat16* xr = x + (long long)blockIdx.x * cols;
-  float v[VPT];
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = threadIdx.x + i * RT;
-    v[i] = c < cols ? bf2f(xr[c]) : 0.0f;
-    s = __fadd_rn(s, v[i]);
-  }
-  const float mean = __fdiv_rn(block_sum(s, red), (float)cols);
-  float q = 0.0f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = threadIdx.x + i * RT;
-    if (c < cols) {
-      const float d = __fsub_rn(v[i], mean);
-      q = __fmaf_rn(d, d, q);
-    }
-  }
-  const float var = __fdiv_rn(block_sum(q, red), (float)cols);
-  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  __nv_bfloat16* yr = y + (long long)blockIdx.x * cols;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = threadIdx.x + i * RT;
-    if (c < cols) {
-      const float ln = round_bf(__fmul_rn(__fsub_rn(v[i], mean), rstd));
-      const float one_plus = round_bf(__fadd_rn(1.0f, bf2f(mod[c])));
-      const float scaled = round_bf(__fmul_rn(ln, one_plus));
-      yr[c] = f2bf(__fadd_rn(scaled, bf2f(mod[cols + c])));
-    }
-  }
+  const int lane = threadIdx.x & 31;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const __nv_bfloat16* xr = x + r * cols;
+  float mean, rstd;
+  warp_row_meanrstd(xr, cols, eps, lane, &mean, &rstd);
+  __nv_bfloat16* yr = y + r * cols;
+  for (int c = lane; c < cols; c += 32)
+    yr[c] = f2bf(adaln_value(bf2f(xr[c]), mean, rstd, bf2f(mod[c]), bf2f(mod[cols + c])));
 }
 
 __global__ void rope_table_kernel(float* cs, float* sn, int max_pos, int hd, const float* inv_freq) {
@@ -341,39 +313,17 @@ __global__ void __launch_bounds__(RT) draft_prep_kernel(DraftPrepArgs a) {
 __global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float red[16];
-  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  if (t >= a.T) return;
   const __nv_bfloat16* pr = a.post + (long long)t * a.post_stride;
   const __nv_bfloat16* sr = a.state + (long long)t * a.Ht;
-  float sp = 0.0f, ss = 0.0f;
-  for (int c = threadIdx.x; c < a.Ht; c += RT) {
-    const float p = bf2f(pr[c]), s = bf2f(sr[c]);
-    sp = __fmaf_rn(p, p, sp);
-    ss = __fmaf_rn(s, s, ss);
-  }
-  sp = block_sum(sp, red);
-  ss = block_sum(ss, red);
-  const float ip = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sp, (float)a.Ht), a.eps)));
-  const float is = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.Ht), a.eps)));
+  const float ip = inv_rms(warp_row_sumsq(pr, a.Ht, lane), a.Ht, a.eps);
+  const float is = inv_rms(warp_row_sumsq(sr, a.Ht, lane), a.Ht, a.eps);
   __nv_bfloat16* o = a.out + (long long)t * a.Ht;
-  for (int c = threadIdx.x; c < a.Ht; c += RT) {
-    const float pn = round_bf(__fmul_rn(bf2f(pr[c]), round_bf(__fmul_rn(bf2f(a.state_norm_w[c]), ip))));
-    const float nn = round_bf(__fmul_rn(bf2f(sr[c]), round_bf(__fmul_rn(bf2f(a.noise_norm_w[c]), is))));
-    const float term = round_bf(__fmul_rn(a.gate, nn));
-    o[c] = f2bf(__fadd_rn(pn, term));
-  }
-}
-
-// Box-Muller on Philox words: pair p = element / 2 uses counter (p, 0, offset, 4)
-__device__ __forceinline__ void normal_pair(uint64_t seed, uint32_t offset, long long p, float& z0, float& z1) {
-  const Philox4 r = philox4x32_10((uint32_t)p, (uint32_t)(p >> 32), offset, 4u, seed);
-  const float u1 = __fmul_rn((float)(r.v[0] >> 8) + 0.5f, 5.9604644775390625e-08f);
-  const float u2 = __fmul_rn((float)(r.v[1] >> 8), 5.9604644775390625e-08f);
-  const float rad = sqrtf(-2.0f * logf(u1));
-  float sv, cv;
-  sincospif(2.0f * u2, &sv, &cv);
-  z0 = rad * cv;
-  z1 = rad * sv;
+  for (int c = lane; c < a.Ht; c += 32)
+    o[c] = f2bf(mix_value(bf2f(pr[c]), bf2f(sr[c]), bf2f(a.state_norm_w[c]), bf2f(a.noise_norm_w[c]), ip, is,
+                          a.gate));
 }
 
 __global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
@@ -638,23 +588,19 @@ inline unsigned blocks_for(long long n, int per) { return (unsigned)((n + per - 
 // ------------------------------------------------------------------ launchers
 fm_status launch_rmsnorm(const __nv_bfloat16* x, const __nv_bfloat16* w, __nv_bfloat16* y, int64_t rows,
                          int64_t cols, float eps, cudaStream_t s, bool pdl) {
-  return launch_kernel(rmsnorm_kernel, dim3((unsigned)rows), dim3(RT), 0, s, pdl, x, w, y, (int)cols, eps);
+  return launch_kernel(rmsnorm_kernel, dim3(blocks_for(rows, ROWS_PER_CTA)), dim3(RT), 0, s, pdl, x, w, y,
+                       (long long)rows, (int)cols, eps);
 }
 fm_status launch_adaln(const __nv_bfloat16* x, const __nv_bfloat16* mod, __nv_bfloat16* y, int64_t rows,
                        int64_t cols, float eps, cudaStream_t s, bool pdl) {
-  const dim3 g((unsigned)rows), b(RT);
-  if (cols <= 1 * RT) return launch_kernel(adaln_kernel<1>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
-  if (cols <= 4 * RT) return launch_kernel(adaln_kernel<4>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
-  if (cols <= 8 * RT) return launch_kernel(adaln_kernel<8>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
-  if (cols <= 12 * RT) return launch_kernel(adaln_kernel<12>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
-  if (cols <= 16 * RT) return launch_kernel(adaln_kernel<16>, g, b, 0, s, pdl, x, mod, y, (int)cols, eps);
-  return set_error(FM_ERR_UNSUPPORTED, "adaln: width %lld above 4096", (long long)cols);
+  return launch_kernel(adaln_kernel, dim3(blocks_for(rows, ROWS_PER_CTA)), dim3(RT), 0, s, pdl, x, mod, y,
+                       (long long)rows, (int)cols, eps);
 }
 fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(draft_prep_kernel, dim3(a.B), dim3(RT), 0, s, pdl, a);
 }
 fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl) {
-  return launch_kernel(mix_state_kernel, dim3(a.T), dim3(RT), 0, s, pdl, a);
+  return launch_kernel(mix_state_kernel, dim3(blocks_for(a.T, ROWS_PER_CTA)), dim3(RT), 0, s, pdl, a);
 }
 fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
                                     const uint32_t* offset_ptr, cudaStream_t s, bool pdl) {

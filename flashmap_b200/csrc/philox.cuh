@@ -68,4 +68,16 @@ __device__ __forceinline__ float fm_exp(float x) {
   return __fmul_rn(__fmul_rn(p, __uint_as_float((uint32_t)(e + 126 + 127) << 23)), __uint_as_float(1u << 23));
 }
 
+// Box-Muller on Philox words: pair p (elements 2p, 2p+1) uses counter (p, 0, offset, 4)
+__device__ __forceinline__ void normal_pair(uint64_t seed, uint32_t offset, long long p, float& z0, float& z1) {
+  const Philox4 r = philox4x32_10((uint32_t)p, (uint32_t)(p >> 32), offset, 4u, seed);
+  const float u1 = __fmul_rn((float)(r.v[0] >> 8) + 0.5f, 5.9604644775390625e-08f);
+  const float u2 = __fmul_rn((float)(r.v[1] >> 8), 5.9604644775390625e-08f);
+  const float rad = sqrtf(-2.0f * logf(u1));
+  float sv, cv;
+  sincospif(2.0f * u2, &sv, &cv);
+  z0 = rad * cv;
+  z1 = rad * sv;
+}
+
 }  // namespace fm

@@ -74,6 +74,27 @@ fm_status make_tmap_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint
   return FM_OK;
 }
 
+fm_status make_tmap_bf16_blocks(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                                uint32_t box_rows, uint32_t box_blocks) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0) return set_error(FM_ERR_ALIGN, "TMA base not 16-byte aligned");
+  if ((ld * 2) % 16 != 0) return set_error(FM_ERR_ALIGN, "TMA row stride not a multiple of 16 bytes");
+  if (cols % 64 != 0 || box_blocks == 0 || box_blocks > 256 || box_blocks > cols / 64)
+    return set_error(FM_ERR_SHAPE, "block view needs cols %% 64 == 0 and 1..256 blocks per box");
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(FM_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {64, rows, cols / 64};
+  cuuint64_t strides[2] = {ld * 2, 128};
+  cuuint32_t box[3] = {64, box_rows, box_blocks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(FM_ERR_CUDA, "cuTensorMapEncodeTiled (blocks) failed (%d) rows=%llu cols=%llu box=%u", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols, box_blocks);
+  return FM_OK;
+}
+
 }  // namespace fm
 
 extern "C" const char* fm_last_error(void) { return fm::g_last_error; }

@@ -306,7 +306,7 @@ class _Plan:
     """A ``fm_plan`` over one cache, batch and number of jumps, with its workspace."""
 
     def __init__(self, model: "FlashMapDraftModel", pack: _Pack, cache: FlashMapCache, batch: int, num_steps: int,
-                 max_extend_rows: int):
+                 max_extend_rows: int, launch_mode: int = _lib.LAUNCH_AUTO):
         cfg = model.config
         lib = _lib.load()
         grid = cfg.jump_grids[str(num_steps)]
@@ -352,6 +352,7 @@ class _Plan:
         c.cache = cache.kv.data_ptr()
         c.cache_batch, c.cache_len = cache.kv.shape[2], cache.kv.shape[4]
         c.max_extend_rows = max_extend_rows
+        c.launch_mode = launch_mode
         self.cfg = c
         size = ctypes.c_size_t(0)
         _lib.check(lib.fm_plan_workspace_size(ctypes.byref(d), ctypes.byref(c), ctypes.byref(size)), "plan size")
@@ -361,6 +362,7 @@ class _Plan:
                                       ctypes.byref(handle)), "fm_plan_create")
         self.handle = handle
         self.batch, self.num_steps, self.max_extend_rows = batch, num_steps, max_extend_rows
+        self.launch_mode = launch_mode
         self.target_key = pack.target_key
         self.pack = pack
         self.cache = cache
@@ -376,8 +378,9 @@ class _Plan:
             pass
 
     def draft(self, anchor_ids, seed: int, offset: int, logits=None, ldl=0, scatter=False, tokens=None, z=None,
-              noise=None, hidden=None, offset_dev=None):
+              noise=None, hidden=None, offset_dev=None, trace=None):
         io = _lib.DraftIO()
+        io.trace = None if trace is None else trace.data_ptr()
         io.offset_ptr = None if offset_dev is None else offset_dev.data_ptr()
         io.anchor_ids, io.lengths = anchor_ids.data_ptr(), self.cache.lengths.data_ptr()
         io.z = None if z is None else z.data_ptr()
@@ -408,6 +411,19 @@ class _Plan:
 
     def last_launches(self) -> int:
         return int(_lib.load().fm_plan_last_launches(self.handle))
+
+    def persistent(self) -> tuple:
+        """(True, "") when a draft runs as one persistent launch, else (False, why)."""
+        why = ctypes.create_string_buffer(256)
+        on = _lib.load().fm_plan_persistent(self.handle, why, len(why))
+        return bool(on), why.value.decode()
+
+    def pass_shape(self) -> tuple:
+        """(grid, stages) of the persistent pass: the trace buffer of ``draft``
+        holds grid x stages x 8 timestamps."""
+        g, n = ctypes.c_int32(0), ctypes.c_int32(0)
+        _lib.load().fm_plan_pass_shape(self.handle, ctypes.byref(g), ctypes.byref(n))
+        return g.value, n.value
 
     def check_device_errors(self):
         code = int(self.err.item())
@@ -447,6 +463,11 @@ class FlashMapDraftModel(PreTrainedModel):
         self.post_init()
 
     # values derived from the weights are rebuilt after a move or a reload (:271-285)
+    # "auto": the faster launch structure for the shape; "kernels": the kernel
+    # sequence; "persistent": one persistent launch per batch-1, one-jump draft.
+    # All three give identical results.
+    launch_mode = "auto"
+
     def _clear_caches(self) -> None:
         self._packs, self._plans, self._counter = {}, {}, 0
         if not hasattr(self, "_caches"):
@@ -475,11 +496,13 @@ class FlashMapDraftModel(PreTrainedModel):
         max_pos = cache.max_length + self.config.block_size + 2
         if pack.ensure_rope(self.config, max_pos):
             self._plans = {}
-        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, pack.device)
+        mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS,
+                "persistent": _lib.LAUNCH_PERSISTENT}[self.launch_mode]
+        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, pack.device)
         plan = self._plans.get(key)
         if plan is None or plan.max_extend_rows < extend_rows or plan.target_key != pack.target_key:
             rows = max(extend_rows, 2 * (plan.max_extend_rows if plan else 0), 64)
-            plan = _Plan(self, pack, cache, batch, num_steps, rows)
+            plan = _Plan(self, pack, cache, batch, num_steps, rows, mode)
             self._plans[key] = plan
         return plan
 

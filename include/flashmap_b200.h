@@ -237,6 +237,15 @@ typedef struct fm_jump {
   float s, next;     /* start time and the time the state moves to (next == 1: last jump) */
 } fm_jump;
 
+/* How fm_draft launches its work.  Both give identical results. */
+enum {
+  FM_LAUNCH_AUTO = 0,       /* the faster of the two for the plan's shape (today: the kernel sequence) */
+  FM_LAUNCH_KERNELS = 1,    /* the kernel sequence: one launch per operation, chained by programmatic
+                               dependent launch */
+  FM_LAUNCH_PERSISTENT = 2  /* one persistent cooperative launch for the whole draft (batch 1, one jump;
+                               other shapes run the kernel sequence) */
+};
+
 typedef struct fm_plan_config {
   int32_t batch;        /* sequences drafted together */
   int32_t num_steps;    /* jumps per draft */
@@ -244,6 +253,7 @@ typedef struct fm_plan_config {
   void* cache;          /* (L, 2, cache_batch, heads, cache_len, hd) bf16 */
   int32_t cache_batch, cache_len;
   int32_t max_extend_rows; /* largest extend_context call (rows over all sequences) */
+  int32_t launch_mode;     /* FM_LAUNCH_* */
 } fm_plan_config;
 
 typedef struct fm_plan fm_plan;
@@ -259,6 +269,14 @@ FM_API fm_status fm_plan_destroy(fm_plan* plan);
 FM_API int32_t* fm_plan_error_word(fm_plan* plan);
 /* Kernels launched by the plan's last fm_draft call. */
 FM_API int64_t fm_plan_last_launches(const fm_plan* plan);
+/* 1 when fm_draft runs as one persistent launch (FM_LAUNCH_PERSISTENT, batch 1,
+ * one jump, target attached, the launch fits the device); else 0, with the reason
+ * written to `why` (when non-NULL, up to why_len bytes including the NUL).
+ * No counterpart in the reference (its draft is a sequence of torch ops). */
+FM_API int32_t fm_plan_persistent(const fm_plan* plan, char* why, size_t why_len);
+/* CTAs and stages of the persistent pass (both 0 when it is off): the size of
+ * fm_draft_io.trace.  No counterpart in the reference. */
+FM_API fm_status fm_plan_pass_shape(const fm_plan* plan, int32_t* grid, int32_t* stages);
 /* The plan's LM-head GEMM alone (logits + argmax of the plan's current DiT
  * output; state-vocabulary columns), for timing the pass's largest kernel. */
 FM_API fm_status fm_plan_lm_head(fm_plan* plan, void* logits, int64_t ldl, fm_stream stream);
@@ -277,6 +295,10 @@ typedef struct fm_draft_io {
   int32_t scatter;           /* 1: write at draft_ids columns of a V-wide row */
   int64_t* tokens;           /* [B*K] argmax tokens (target ids) or NULL */
   void* hidden;              /* [B*K, Ht] bf16 DiT output of the last jump, or NULL */
+  uint64_t* trace;           /* persistent pass only, or NULL: [grid][stages][8] device timestamps (ns) of
+                                each stage in each CTA: start, inputs ready, operand loads issued, loads
+                                landed, operand built, first epilogue done, last epilogue done, arrived
+                                (slots a stage does not pass through keep their old value) */
 } fm_draft_io;
 
 /* One draft of the whole block (modeling_flashmap.py:422-479): the anchor row
