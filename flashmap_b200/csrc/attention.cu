@@ -61,8 +61,54 @@ __global__ void __launch_bounds__(SA_THREADS) self_attn_kernel(SelfAttnArgs a) {
   }
 }
 
+// Blocks of 16 slots with head_dim 64 or 128: one warp per (sequence, head) on
+// the tensor cores (block_attn_head, attention.cuh); the persistent pass runs
+// the same function.
+constexpr int SA_MMA_WARPS = 4;
+
+template <int HD>
+__global__ void __launch_bounds__(SA_MMA_WARPS * 32) self_attn_mma_kernel(SelfAttnArgs a, int items) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ __align__(1024) uint8_t sa_smem[];
+  constexpr int PART = 16 * HD * 2;  // one of q, k, v of a head
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int it = blockIdx.x * SA_MMA_WARPS + warp;
+  if (it >= items) return;
+  const int b = it / a.heads, h = it % a.heads, D = a.hidden;
+  uint8_t* st = sa_smem + warp * 3 * PART;
+  // q | k | v rows of this head into the swizzled layout
+  for (int idx = lane; idx < 3 * 16 * (HD / 8); idx += 32) {
+    const int part = idx / (16 * (HD / 8)), rem = idx % (16 * (HD / 8)), row = rem / (HD / 8), ch = rem % (HD / 8);
+    const uint4 v = *reinterpret_cast<const uint4*>(a.qkv + (long long)(b * 16 + row) * 3 * D + part * D + h * HD + ch * 8);
+    *reinterpret_cast<uint4*>(st + part * PART + blk_sw(row, ch)) = v;
+  }
+  __syncwarp();
+  const uint32_t base = smem_u32(st);
+  __nv_bfloat16* out = a.out + (long long)(b * 16) * D + h * HD;
+  block_attn_head<HD>(base, base + PART, base + 2 * PART, a.scale, [&](int i, int d, float lo, float hi) {
+    *reinterpret_cast<__nv_bfloat162*>(out + (long long)i * D + d) = __floats2bfloat162_rn(lo, hi);
+  });
+}
+
 fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl) {
   const int K = a.block, hd = a.head_dim;
+  if (K == 16 && (hd == 64 || hd == 128)) {
+    const int items = batch * a.heads;
+    const unsigned grid = (unsigned)((items + SA_MMA_WARPS - 1) / SA_MMA_WARPS);
+    const size_t smem = (size_t)SA_MMA_WARPS * 3 * 16 * hd * 2;
+    static int configured = -1;
+    int dev;
+    cudaGetDevice(&dev);
+    if (configured != dev) {
+      cudaFuncSetAttribute(self_attn_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      cudaFuncSetAttribute(self_attn_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+      configured = dev;
+    }
+    if (hd == 128)
+      return launch_kernel(self_attn_mma_kernel<128>, dim3(grid), dim3(SA_MMA_WARPS * 32), smem, stream, pdl, a, items);
+    return launch_kernel(self_attn_mma_kernel<64>, dim3(grid), dim3(SA_MMA_WARPS * 32), smem, stream, pdl, a, items);
+  }
   const size_t smem = (size_t)(2 * K * (hd + 1) + K * hd + K * (K + 1) + K) * sizeof(float);
   if (smem > 200 * 1024) return set_error(FM_ERR_SHAPE, "self-attention block too large");
   if (hd % 2) return set_error(FM_ERR_SHAPE, "self-attention needs an even head_dim");

@@ -27,6 +27,7 @@ enum DeviceError : int {
   DEV_TIMEOUT_ACC = 3,     // epilogue / MMA waited too long on TMEM hand-off
   DEV_BAD_INDEX = 4,       // an index from device memory was out of range
   DEV_TIMEOUT_OTHER = 5,
+  DEV_BAD_COPY = 6,        // an asynchronous copy that would break a TMA rule was skipped
 };
 
 __device__ __forceinline__ void record_error(int* err, int code) {
@@ -117,6 +118,13 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
           "r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
+}
+// A tensor map that lives in global memory (written by a copy from the host,
+// possibly over an older map at the same address) must be acquired by the
+// tensor-map proxy before a TMA uses it, or a stale cached copy may be used.
+__device__ __forceinline__ void tmap_acquire(const void* map) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(map))
+               : "memory");
 }
 // 2D tile into L2 only (no shared-memory destination, no completion)
 __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {

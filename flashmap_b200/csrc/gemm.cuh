@@ -56,6 +56,8 @@ struct GemmArgs {
   const float* rope_sin;
   int rope_len;
   const int* positions;  // [N]
+  const float* tok_cos;  // optional [N][head_dim/2]: rotary factors of the N tokens' positions
+  const float* tok_sin;  //   (QKNORM reads these instead of positions + tables when set)
   const int* token_seq;  // [N] (KVCACHE)
   __nv_bfloat16* cache;  // (L, 2, cache_batch, heads, cache_len, head_dim)
   int cache_batch, cache_heads, cache_len;
@@ -165,7 +167,21 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
       }
       named_bar_sync(1, 128);
       const int hq = hd >> 5;  // warp quarters per head
-      const int q0 = (q / hq) * hq;
+      // one thread per (head of the tile, token) finishes the statistic: the
+      // quarters' sums in order, mean, 1 / sqrt(mean + eps)
+      float* xinv = xch + 64;
+      {
+        const int t = (int)threadIdx.x - 64;
+        if (t < (128 / hd) * 16) {
+          const int hh = t >> 4, jj = t & 15;
+          float tot = 0.0f;
+          for (int qq = hh * hq; qq < hh * hq + hq; ++qq) tot = __fadd_rn(tot, xch[qq * 16 + jj]);
+          const float mean = __fdiv_rn(tot, (float)hd);
+          xinv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        }
+      }
+      named_bar_sync(1, 128);
+      const int hrow = (q / hq) * 16;  // this thread's head's entries of xinv
       const __nv_bfloat16* w;
       if constexpr (EPI == EPI_QKNORM)
         w = part == 0 ? a.norm_w0 : a.norm_w1;
@@ -173,30 +189,37 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
         w = a.norm_w0 + (long long)layer * a.norm_layer_stride;
       const float wd = bf2f(w[d]);
       const int half = hd >> 1;
-      // all positions, then all rotary factors: independent loads issued together
-      int pos[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = n0 + j;
-        int pj = (n < a.N) ? a.positions[n] : 0;
-        if (pj < 0 || pj >= a.rope_len) {
-          if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
-          pj = 0;
-        }
-        pos[j] = pj;
-      }
       float rc[16], rs[16];
+      if (EPI == EPI_QKNORM && a.tok_cos != nullptr) {
+        // the tokens' rotary factors, gathered once per launch (positions checked there)
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        rc[j] = a.rope_cos[(long long)pos[j] * half + (d >> 1)];
-        rs[j] = a.rope_sin[(long long)pos[j] * half + (d >> 1)];
+        for (int j = 0; j < 16; ++j) {
+          const int n = (n0 + j < a.N) ? n0 + j : 0;
+          rc[j] = a.tok_cos[n * half + (d >> 1)];
+          rs[j] = a.tok_sin[n * half + (d >> 1)];
+        }
+      } else {
+        // all positions, then all rotary factors: independent loads issued together
+        int pos[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = n0 + j;
+          int pj = (n < a.N) ? a.positions[n] : 0;
+          if (pj < 0 || pj >= a.rope_len) {
+            if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
+            pj = 0;
+          }
+          pos[j] = pj;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          rc[j] = a.rope_cos[(long long)pos[j] * half + (d >> 1)];
+          rs[j] = a.rope_sin[(long long)pos[j] * half + (d >> 1)];
+        }
       }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        float tot = 0.0f;
-        for (int qq = q0; qq < q0 + hq; ++qq) tot = __fadd_rn(tot, xch[qq * 16 + j]);
-        const float mean = __fdiv_rn(tot, (float)hd);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        const float inv = xinv[hrow + j];
         const float scale = round_bf(__fmul_rn(wd, inv));
         const float xn = round_bf(__fmul_rn(y[j], scale));
         const float other = __shfl_xor_sync(0xffffffffu, xn, 1);

@@ -241,7 +241,26 @@ __device__ long long block_categorical(F weight, long long V, float u, float* sm
 // ------------------------------------------------------------------ kernels
 
 // One warp per row (rows.cuh gives the reduction order): 8 rows per CTA.
+// Rows up to 2048 wide (one chunk round) whose width is a multiple of 8 with
+// 16-byte aligned pointers keep the row and its per-column vectors in
+// registers, all loaded at once; other rows take the general loop.
 constexpr int ROWS_PER_CTA = RT / 32;
+
+__device__ __forceinline__ bool vec_ok(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// the lane's chunks (lane + 32 i, i < 8) of a row: count, loaded together
+__device__ __forceinline__ int lane_load8(const __nv_bfloat16* row, int nch, int lane, uint4* raw) {
+  int n = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < nch) {
+      raw[i] = *reinterpret_cast<const uint4*>(row + ch * 8);
+      n = i + 1;
+    }
+  }
+  return n;
+}
 
 __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
                                                      __nv_bfloat16* y, long long rows, int cols, float eps) {
@@ -251,8 +270,36 @@ __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, con
   const long long r = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   if (r >= rows) return;
   const __nv_bfloat16* xr = x + r * cols;
-  const float inv = inv_rms(warp_row_sumsq(xr, cols, lane), cols, eps);
   __nv_bfloat16* yr = y + r * cols;
+  if (cols % 8 == 0 && cols <= 2048 && vec_ok(xr) && vec_ok(yr) && vec_ok(w)) {
+    const int nch = cols / 8;
+    uint4 xv[8], wv[8];
+    const int n = lane_load8(xr, nch, lane, xv);
+    lane_load8(w, nch, lane, wv);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n) {
+        float xf[8], t[8];
+        unpack_bf16x8(xv[i], xf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = __fmul_rn(xf[e], xf[e]);
+        s = __fadd_rn(s, chunk_tree(t, 8));
+      }
+    const float inv = inv_rms(warp_allsum(s), cols, eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n) {
+        float xf[8], wf[8], o[8];
+        unpack_bf16x8(xv[i], xf);
+        unpack_bf16x8(wv[i], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rms_value(xf[e], wf[e], inv);
+        *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
+      }
+    return;
+  }
+  const float inv = inv_rms(warp_row_sumsq(xr, cols, lane), cols, eps);
   for (int c = lane; c < cols; c += 32) yr[c] = f2bf(rms_value(bf2f(xr[c]), bf2f(w[c]), inv));
 }
 
@@ -266,9 +313,51 @@ __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const
   const long long r = (long long)blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   if (r >= rows) return;
   const __nv_bfloat16* xr = x + r * cols;
+  __nv_bfloat16* yr = y + r * cols;
+  if (cols % 8 == 0 && cols <= 2048 && vec_ok(xr) && vec_ok(yr) && vec_ok(mod)) {
+    const int nch = cols / 8;
+    uint4 xv[8], sv[8], hv[8];
+    const int n = lane_load8(xr, nch, lane, xv);
+    lane_load8(mod, nch, lane, sv);
+    lane_load8(mod + cols, nch, lane, hv);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n) {
+        float xf[8];
+        unpack_bf16x8(xv[i], xf);
+        s = __fadd_rn(s, chunk_tree(xf, 8));
+      }
+    const float mean = __fdiv_rn(warp_allsum(s), (float)cols);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n) {
+        float xf[8], t[8];
+        unpack_bf16x8(xv[i], xf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = __fsub_rn(xf[e], mean);
+          t[e] = __fmul_rn(d, d);
+        }
+        q = __fadd_rn(q, chunk_tree(t, 8));
+      }
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_allsum(q), (float)cols), eps)));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < n) {
+        float xf[8], sc[8], sh[8], o[8];
+        unpack_bf16x8(xv[i], xf);
+        unpack_bf16x8(sv[i], sc);
+        unpack_bf16x8(hv[i], sh);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
+        *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
+      }
+    return;
+  }
   float mean, rstd;
   warp_row_meanrstd(xr, cols, eps, lane, &mean, &rstd);
-  __nv_bfloat16* yr = y + r * cols;
   for (int c = lane; c < cols; c += 32)
     yr[c] = f2bf(adaln_value(bf2f(xr[c]), mean, rstd, bf2f(mod[c]), bf2f(mod[cols + c])));
 }
@@ -318,6 +407,53 @@ __global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
   if (t >= a.T) return;
   const __nv_bfloat16* pr = a.post + (long long)t * a.post_stride;
   const __nv_bfloat16* sr = a.state + (long long)t * a.Ht;
+  __nv_bfloat16* orow = a.out + (long long)t * a.Ht;
+  if (a.Ht % 8 == 0 && a.Ht <= 4096 && vec_ok(pr) && vec_ok(sr) && vec_ok(orow) && vec_ok(a.state_norm_w) &&
+      vec_ok(a.noise_norm_w)) {
+    // two rounds of 8 chunks per lane at most; sums in the canonical order
+    const int nch = a.Ht / 8;
+    float sp = 0.0f, ss = 0.0f;
+    for (int rd = 0; rd * 256 < nch; ++rd) {
+      uint4 pv[8], zv[8];
+      const int n = lane_load8(pr + rd * 2048, nch - rd * 256, lane, pv);
+      lane_load8(sr + rd * 2048, nch - rd * 256, lane, zv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < n) {
+          float f[8], t2[8];
+          unpack_bf16x8(pv[i], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t2[e] = __fmul_rn(f[e], f[e]);
+          sp = __fadd_rn(sp, chunk_tree(t2, 8));
+          unpack_bf16x8(zv[i], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t2[e] = __fmul_rn(f[e], f[e]);
+          ss = __fadd_rn(ss, chunk_tree(t2, 8));
+        }
+    }
+    const float ip = inv_rms(warp_allsum(sp), a.Ht, a.eps);
+    const float is = inv_rms(warp_allsum(ss), a.Ht, a.eps);
+    for (int rd = 0; rd * 256 < nch; ++rd) {
+      uint4 pv[8], zv[8], av[8], bv[8];
+      const int n = lane_load8(pr + rd * 2048, nch - rd * 256, lane, pv);
+      lane_load8(sr + rd * 2048, nch - rd * 256, lane, zv);
+      lane_load8(a.state_norm_w + rd * 2048, nch - rd * 256, lane, av);
+      lane_load8(a.noise_norm_w + rd * 2048, nch - rd * 256, lane, bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < n) {
+          float pf[8], zf[8], af[8], bf_[8], o[8];
+          unpack_bf16x8(pv[i], pf);
+          unpack_bf16x8(zv[i], zf);
+          unpack_bf16x8(av[i], af);
+          unpack_bf16x8(bv[i], bf_);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = mix_value(pf[e], zf[e], af[e], bf_[e], ip, is, a.gate);
+          *reinterpret_cast<uint4*>(orow + rd * 2048 + (lane + 32 * i) * 8) = pack_bf16x8(o);
+        }
+    }
+    return;
+  }
   const float ip = inv_rms(warp_row_sumsq(pr, a.Ht, lane), a.Ht, a.eps);
   const float is = inv_rms(warp_row_sumsq(sr, a.Ht, lane), a.Ht, a.eps);
   __nv_bfloat16* o = a.out + (long long)t * a.Ht;

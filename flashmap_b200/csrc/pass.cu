@@ -37,20 +37,24 @@ constexpr int B_SLOTS = 64;            // K up to 4096 per CTA range
 constexpr int B_REGION = B_SLOTS * B_SLOT;
 constexpr int BAR_BYTES = 256;
 constexpr int FLAG_BYTES = 128;
-constexpr int XCH_BYTES = 5120;
+constexpr int XCH_BYTES = 4096;  // epilogue exchange: 64 x 16 floats (SwiGLU) or 64 keys
 constexpr int STAT_BYTES = 1024;
 constexpr int STAGE_BYTES = 768;  // this CTA's copy of the current stage descriptor
 constexpr int MAX_STAGES = 96;
 constexpr int LITE_BYTES = MAX_STAGES * 32;  // the fields the producer and MMA warps read, every stage
+constexpr int ROPE_BYTES = 16 * 64 * 2 * 4;   // rotary factors of the 16 slot positions, head_dim <= 128
 constexpr int SMEM =
-    1024 + NA * A_BYTES + B_REGION + BAR_BYTES + FLAG_BYTES + XCH_BYTES + STAT_BYTES + STAGE_BYTES + LITE_BYTES;
+    1024 + NA * A_BYTES + B_REGION + BAR_BYTES + FLAG_BYTES + XCH_BYTES + STAT_BYTES + STAGE_BYTES + LITE_BYTES +
+    ROPE_BYTES;
 constexpr int TMEM_COLS = 32;
 constexpr int WORKERS = 192;  // warps 2..7
 constexpr int XA_TILE = 64;
 constexpr int XA_STAGES = 2;
 constexpr uint32_t PF_TILES = 24;
-constexpr int TRACE_SLOTS = 8;  // per stage and CTA: start, inputs ready, loads issued, loads landed, operand
-                                // built, first epilogue done, last epilogue done, arrived  // weight tiles a CTA keeps requested into L2 ahead of its loads
+constexpr int TRACE_SLOTS = 14;  // per stage and CTA: start, inputs ready, loads issued, loads landed, operand
+                                 // built, first epilogue done, last epilogue done, arrived, statistics done,
+                                 // transform done; split-tile owner: contributors in, partials in, summed,
+                                 // epilogue done  // weight tiles a CTA keeps requested into L2 ahead of its loads
 static_assert(sizeof(Stage) <= STAGE_BYTES && sizeof(Stage) % 16 == 0, "stage slot");
 
 struct StageLite {
@@ -75,6 +79,7 @@ struct Smem {
   float* stats;  // [0..15] mean, [16..32] 1/std or 1/rms of up to 17 rows
   Stage* stage;
   StageLite* lite;
+  float* rope;  // [2][16][head_dim / 2]: cos then sin of the slot positions
 };
 
 __device__ __forceinline__ Smem carve_smem(uint8_t* raw) {
@@ -101,6 +106,7 @@ __device__ __forceinline__ Smem carve_smem(uint8_t* raw) {
   m.stats = reinterpret_cast<float*>(after + FLAG_BYTES + XCH_BYTES);
   m.stage = reinterpret_cast<Stage*>(after + FLAG_BYTES + XCH_BYTES + STAT_BYTES);
   m.lite = reinterpret_cast<StageLite*>(after + FLAG_BYTES + XCH_BYTES + STAT_BYTES + STAGE_BYTES);
+  m.rope = reinterpret_cast<float*>(after + FLAG_BYTES + XCH_BYTES + STAT_BYTES + STAGE_BYTES + LITE_BYTES);
   return m;
 }
 
@@ -108,6 +114,14 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   unsigned long long v;
   asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ int ld_acquire_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
@@ -130,6 +144,34 @@ __device__ bool grid_wait(const PassArgs& P, unsigned long long target, volatile
         give_up(P, sabort, DEV_TIMEOUT_OTHER);
         return false;
       }
+    }
+  }
+}
+
+// Every asynchronous copy of the pass is checked before it is issued: 16-byte
+// aligned addresses and sizes, a tile's innermost coordinate on a 16-byte
+// boundary, and a shared-memory destination inside [lo, hi).  A copy that
+// fails is recorded (DEV_BAD_COPY) and skipped; the wait that expects its
+// bytes then runs out and reports too.
+__device__ __forceinline__ bool copy_checked(const PassArgs& P, const void* dst, uint32_t bytes, const void* lo,
+                                             const void* hi, const void* src, int x) {
+  const uintptr_t d = reinterpret_cast<uintptr_t>(dst);
+  const bool ok = (d & 15) == 0 && bytes > 0 && (bytes & 15) == 0 && d >= reinterpret_cast<uintptr_t>(lo) &&
+                  d + bytes <= reinterpret_cast<uintptr_t>(hi) && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                  ((x * 2) & 15) == 0;
+  if (!ok) record_error(P.err, DEV_BAD_COPY);
+  return ok;
+}
+
+// one thread: spin (bounded) until *counter reaches target
+__device__ bool wait_count(const int* counter, int target, volatile int* sabort) {
+  if (ld_acquire_s32(counter) >= target) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_s32(counter) >= target) return true;
+    if ((i & 15u) == 0) {
+      if (*sabort) return false;
+      if (global_ns() - t0 > FM_WAIT_NS) return false;
     }
   }
 }
@@ -187,10 +229,9 @@ __device__ __host__ inline size_t adaln_full_bytes(int K) { return (size_t)BNP *
 __device__ __host__ inline size_t mix_param_bytes(int nk) { return (size_t)3 * nk * 128; }
 // a single staged row and its norm weight
 __device__ __host__ inline size_t row_stage_bytes(int K) { return align_up((size_t)K * 2, 128) * 2; }
-// self-attention: staged heads (q|k|v, bf16) and fp32 scores + row sums
+// self-attention: staged heads (q|k|v, bf16)
 __device__ __host__ inline size_t selfattn_bytes(int heads_touched, int hd) {
-  return (size_t)heads_touched * 3 * BNP * hd * 2 + (size_t)heads_touched * BNP * (BNP + 1) * 4 +
-         (size_t)heads_touched * BNP * 4;
+  return (size_t)heads_touched * 3 * BNP * hd * 2;
 }
 
 // element d of row i of a [16 x 64 * blocks] staged block group
@@ -205,7 +246,8 @@ __device__ __forceinline__ uint4 staged_chunk(const uint8_t* base, int i, int k,
 }
 
 // bulk copies of elements [e0, e0 + n) of a vector, in runs that do not wrap
-__device__ __forceinline__ uint32_t copy_segments(uint8_t* dst, const __nv_bfloat16* vec, int K, int kb, int k0, int nk,
+__device__ __forceinline__ uint32_t copy_segments(const PassArgs* P, const Smem* sm, uint8_t* dst,
+                                                  const __nv_bfloat16* vec, int K, int kb, int k0, int nk,
                                                   uint64_t* bar, bool issue) {
   uint32_t bytes = 0;
   int j = 0;
@@ -213,7 +255,8 @@ __device__ __forceinline__ uint32_t copy_segments(uint8_t* dst, const __nv_bfloa
     const int k = (k0 + j) % kb;
     const int run = min(nk - j, kb - k);
     const uint32_t b = (uint32_t)((min(K, (k + run) * 64) - k * 64) * 2);
-    if (issue) bulk_load(dst + (size_t)j * 128, vec + (size_t)k * 64, b, bar);
+    if (issue && copy_checked(*P, dst + (size_t)j * 128, b, sm->B, sm->B + B_REGION, vec + (size_t)k * 64, 0))
+      bulk_load(dst + (size_t)j * 128, vec + (size_t)k * 64, b, bar);
     bytes += b;
     j += run;
   }
@@ -247,32 +290,39 @@ __device__ uint32_t issue_b_loads(const Stage& S, const PassArgs& P, const Smem&
     total = (uint32_t)(BNP * K * 2 + 2 * K * 2);
   } else if (S.bsrc == BS_COPY || S.bsrc == BS_ADALN || S.bsrc == BS_MIX) {
     total = (uint32_t)nk * B_SLOT;
-    if (S.bsrc == BS_ADALN) total += 2 * copy_segments(nullptr, S.mod, K, kb, k0, nk, nullptr, false);
-    if (S.bsrc == BS_MIX) total += 3 * copy_segments(nullptr, S.aux, K, kb, k0, nk, nullptr, false);
+    if (S.bsrc == BS_ADALN) total += 2 * copy_segments(&P, &sm, nullptr, S.mod, K, kb, k0, nk, nullptr, false);
+    if (S.bsrc == BS_MIX) total += 3 * copy_segments(&P, &sm, nullptr, S.aux, K, kb, k0, nk, nullptr, false);
   } else if (S.bsrc == BS_RMSROW || S.bsrc == BS_GATHER) {
     total = (uint32_t)(K * 2) * (S.bsrc == BS_RMSROW ? 2 : 1);
   } else if (S.bsrc == BS_SELFATTN) {
     total = (uint32_t)nh * 3 * (S.head_dim / 64) * B_SLOT;
   }
   if (total == 0) return 0;
+  if (smap) tmap_acquire(smap);
+  if (fmap) tmap_acquire(fmap);
   fence_async_global();  // inputs written by other CTAs' generic stores, read by the async proxy
   mbar_arrive_expect_tx(sm.b_load, total);
+  const uint8_t* lo = sm.B;
+  const uint8_t* hi = sm.B + B_REGION;
   if (md.inplace) {
-    tma_load_3d(sm.B, fmap, sm.b_load, 0, 0, 0);
+    if (copy_checked(P, sm.B, (uint32_t)kb * B_SLOT, lo, hi, nullptr, 0)) tma_load_3d(sm.B, fmap, sm.b_load, 0, 0, 0);
   } else if (md.staged) {
     uint8_t* rows = tail - (size_t)BNP * K * 2;
-    tma_load_3d(rows, fmap, sm.b_load, 0, 0, 0);
-    bulk_load(rows - (size_t)2 * K * 2, S.mod, (uint32_t)(2 * K * 2), sm.b_load);
+    if (copy_checked(P, rows, (uint32_t)(BNP * K * 2), lo, hi, nullptr, 0)) tma_load_3d(rows, fmap, sm.b_load, 0, 0, 0);
+    if (copy_checked(P, rows - (size_t)2 * K * 2, (uint32_t)(2 * K * 2), lo, hi, S.mod, 0))
+      bulk_load(rows - (size_t)2 * K * 2, S.mod, (uint32_t)(2 * K * 2), sm.b_load);
   } else if (S.bsrc == BS_COPY || S.bsrc == BS_ADALN || S.bsrc == BS_MIX) {
-    for (int j = 0; j < nk; ++j) tma_load_2d(sm.B + j * B_SLOT, smap, sm.b_load, ((k0 + j) % kb) * 64, 0);
+    for (int j = 0; j < nk; ++j)
+      if (copy_checked(P, sm.B + j * B_SLOT, B_SLOT, lo, hi, nullptr, ((k0 + j) % kb) * 64))
+        tma_load_2d(sm.B + j * B_SLOT, smap, sm.b_load, ((k0 + j) % kb) * 64, 0);
     uint8_t* parm = sm.B + (size_t)nk * B_SLOT;
     if (S.bsrc == BS_ADALN) {
-      copy_segments(parm, S.mod, K, kb, k0, nk, sm.b_load, true);
-      copy_segments(parm + (size_t)nk * 128, S.mod + K, K, kb, k0, nk, sm.b_load, true);
+      copy_segments(&P, &sm, parm, S.mod, K, kb, k0, nk, sm.b_load, true);
+      copy_segments(&P, &sm, parm + (size_t)nk * 128, S.mod + K, K, kb, k0, nk, sm.b_load, true);
     } else if (S.bsrc == BS_MIX) {
-      copy_segments(parm, S.aux, K, kb, k0, nk, sm.b_load, true);
-      copy_segments(parm + (size_t)nk * 128, S.w0, K, kb, k0, nk, sm.b_load, true);
-      copy_segments(parm + (size_t)2 * nk * 128, S.w1, K, kb, k0, nk, sm.b_load, true);
+      copy_segments(&P, &sm, parm, S.aux, K, kb, k0, nk, sm.b_load, true);
+      copy_segments(&P, &sm, parm + (size_t)nk * 128, S.w0, K, kb, k0, nk, sm.b_load, true);
+      copy_segments(&P, &sm, parm + (size_t)2 * nk * 128, S.w1, K, kb, k0, nk, sm.b_load, true);
     }
   } else if (S.bsrc == BS_RMSROW || S.bsrc == BS_GATHER) {
     const size_t rb = align_up((size_t)K * 2, 128);
@@ -282,15 +332,17 @@ __device__ uint32_t issue_b_loads(const Stage& S, const PassArgs& P, const Smem&
       if (id < 0 || id >= P.vocab) id = 0;  // recorded as DEV_BAD_INDEX by the prep step
       row = S.aux + id * K;
     }
-    bulk_load(tail - rb, row, (uint32_t)(K * 2), sm.b_load);
-    if (S.bsrc == BS_RMSROW) bulk_load(tail - 2 * rb, S.w0, (uint32_t)(K * 2), sm.b_load);
+    if (copy_checked(P, tail - rb, (uint32_t)(K * 2), lo, hi, row, 0)) bulk_load(tail - rb, row, (uint32_t)(K * 2), sm.b_load);
+    if (S.bsrc == BS_RMSROW && copy_checked(P, tail - 2 * rb, (uint32_t)(K * 2), lo, hi, S.w0, 0))
+      bulk_load(tail - 2 * rb, S.w0, (uint32_t)(K * 2), sm.b_load);
   } else if (S.bsrc == BS_SELFATTN) {
     const int bx = S.head_dim / 64, D = S.heads * S.head_dim;
     uint8_t* st = sm.B + align_up((size_t)nk * B_SLOT, 1024);
-    for (int hi = 0; hi < nh; ++hi)
+    for (int i = 0; i < nh; ++i)
       for (int part = 0; part < 3; ++part)
-        tma_load_3d(st + (size_t)(hi * 3 + part) * bx * B_SLOT, fmap, sm.b_load, 0, 0,
-                    (part * D + heads[hi] * S.head_dim) / 64);
+        if (copy_checked(P, st + (size_t)(i * 3 + part) * bx * B_SLOT, (uint32_t)bx * B_SLOT, lo, hi, nullptr, 0))
+          tma_load_3d(st + (size_t)(i * 3 + part) * bx * B_SLOT, fmap, sm.b_load, 0, 0,
+                      (part * D + heads[i] * S.head_dim) / 64);
   }
   return total;
 }
@@ -385,33 +437,57 @@ __device__ size_t build_b(const Stage& S, const PassArgs& P, const Smem& sm, int
   if (md.staged) {
     const uint8_t* rows = tail - (size_t)BNP * K * 2;
     const __nv_bfloat16* mod = reinterpret_cast<const __nv_bfloat16*>(rows - (size_t)2 * K * 2);
+    // the warp's rows (wid, wid + 6, wid + 12) side by side: independent
+    // accumulations, each in the canonical order of rows.cuh
+    constexpr int RW = (BNP + WORKERS / 32 - 1) / (WORKERS / 32);
     const int nch = K / 8;
-    for (int r = wid; r < S.ntok; r += WORKERS / 32) {
-      float s = 0.0f;
-      for (int ch = lane; ch < nch; ch += 32) {
+    int rr[RW];
+    bool live[RW];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      rr[i] = wid + i * (WORKERS / 32);
+      live[i] = rr[i] < S.ntok;
+      if (!live[i]) rr[i] = 0;
+    }
+    float sum[RW], mean[RW];
+#pragma unroll
+    for (int i = 0; i < RW; ++i) sum[i] = 0.0f;
+    for (int ch = lane; ch < nch; ch += 32) {
+#pragma unroll
+      for (int i = 0; i < RW; ++i) {
         float x[8];
-        unpack_bf16x8(staged_chunk(rows, r, ch >> 3, ch & 7), x);
-        s = __fadd_rn(s, chunk_tree(x, 8));
+        unpack_bf16x8(staged_chunk(rows, rr[i], ch >> 3, ch & 7), x);
+        sum[i] = __fadd_rn(sum[i], chunk_tree(x, 8));
       }
-      const float mean = __fdiv_rn(warp_allsum(s), (float)K);
-      float q = 0.0f;
-      for (int ch = lane; ch < nch; ch += 32) {
+    }
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      mean[i] = __fdiv_rn(warp_allsum(sum[i]), (float)K);
+      sum[i] = 0.0f;
+    }
+    for (int ch = lane; ch < nch; ch += 32) {
+#pragma unroll
+      for (int i = 0; i < RW; ++i) {
         float x[8], t[8];
-        unpack_bf16x8(staged_chunk(rows, r, ch >> 3, ch & 7), x);
+        unpack_bf16x8(staged_chunk(rows, rr[i], ch >> 3, ch & 7), x);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float d = __fsub_rn(x[e], mean);
+          const float d = __fsub_rn(x[e], mean[i]);
           t[e] = __fmul_rn(d, d);
         }
-        q = __fadd_rn(q, chunk_tree(t, 8));
+        sum[i] = __fadd_rn(sum[i], chunk_tree(t, 8));
       }
-      const float var = __fdiv_rn(warp_allsum(q), (float)K);
-      if (lane == 0) {
-        stats[r] = mean;
-        stats[16 + r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, S.eps)));
+    }
+#pragma unroll
+    for (int i = 0; i < RW; ++i) {
+      const float var = __fdiv_rn(warp_allsum(sum[i]), (float)K);
+      if (lane == 0 && live[i]) {
+        stats[rr[i]] = mean[i];
+        stats[16 + rr[i]] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, S.eps)));
       }
     }
     named_bar_sync(2, WORKERS);
+    if (ts && wt == 0) ts[8] = global_ns();
     for (int item = wt; item < nk * 128; item += WORKERS) {
       const int j = item >> 7, rem = item & 127, r = rem >> 3, ch = rem & 7;
       const int k = (k0 + j) % kb;
@@ -424,6 +500,7 @@ __device__ size_t build_b(const Stage& S, const PassArgs& P, const Smem& sm, int
       for (int t = 0; t < 8; ++t) v[t] = adaln_value(x[t], mean, rstd, sc[t], sh[t]);
       *reinterpret_cast<uint4*>(sm.B + j * B_SLOT + b_offset(r, ch)) = pack8(v);
     }
+    if (ts && wt == 0) ts[9] = global_ns();
     return (size_t)nk * B_SLOT;
   }
   if (S.bsrc == BS_RMSROW || S.bsrc == BS_GATHER) {
@@ -483,58 +560,28 @@ __device__ size_t build_b(const Stage& S, const PassArgs& P, const Smem& sm, int
     return (size_t)nk * B_SLOT + (S.bsrc == BS_MIX ? mix_param_bytes(nk) : (size_t)2 * nk * 128);
   }
   if (S.bsrc == BS_SELFATTN) {
-    // self_attn_kernel's arithmetic (attention.cu) on the staged heads:
-    // fp32 scores as one fma chain over d, softmax numerators rounded to
-    // bf16 with an fp32 sum, then P V as one fma chain over the keys
+    // one warp per touched head, on the tensor cores (block_attn_head,
+    // attention.cuh, as the kernel sequence computes it); each writes the
+    // columns of its head that fall in this CTA's k-range into their slots
     const int hd = S.head_dim, bx = hd / 64;
     const uint8_t* st = sm.B + align_up((size_t)nk * B_SLOT, 1024);
-    float* sp = reinterpret_cast<float*>(const_cast<uint8_t*>(st) + (size_t)nh * 3 * bx * B_SLOT);  // [nh][16][17]
-    float* sl = sp + nh * BNP * (BNP + 1);                                                          // [nh][16]
-    for (int idx = wt; idx < nh * BNP * BNP; idx += WORKERS) {
-      const int hi = idx / (BNP * BNP), i = (idx / BNP) % BNP, jj = idx % BNP;
-      const uint8_t* q = st + (size_t)(hi * 3 + 0) * bx * B_SLOT;
-      const uint8_t* kk = st + (size_t)(hi * 3 + 1) * bx * B_SLOT;
-      float acc = 0.0f;
-      for (int d = 0; d < hd; ++d) acc = fmaf(staged_at(q, i, d), staged_at(kk, jj, d), acc);
-      sp[(hi * BNP + i) * (BNP + 1) + jj] = __fmul_rn(acc, S.scale);
+    for (int hi = wid; hi < nh; hi += WORKERS / 32) {
+      const uint32_t q = smem_u32(st + (size_t)(hi * 3 + 0) * bx * B_SLOT);
+      const int h = heads[hi];
+      auto store = [&](int i, int d, float lo, float hi2) {
+        const int k = (h * hd + d) >> 6;
+        const int j = (k - k0 + kb) % kb;
+        if (j >= nk) return;
+        const int dd = d & 63;
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi2);
+        *reinterpret_cast<__nv_bfloat162*>(sm.B + j * B_SLOT + b_offset(i, dd >> 3) + (dd & 7) * 2) = v;
+      };
+      if (hd == 128)
+        block_attn_head<128>(q, q + bx * B_SLOT, q + 2 * bx * B_SLOT, S.scale, store);
+      else
+        block_attn_head<64>(q, q + bx * B_SLOT, q + 2 * bx * B_SLOT, S.scale, store);
     }
-    named_bar_sync(2, WORKERS);
-    if (wt < nh * BNP) {
-      float* row = sp + wt * (BNP + 1);
-      float m = -INFINITY;
-      for (int jj = 0; jj < BNP; ++jj) m = fmaxf(m, row[jj]);
-      float l = 0.0f;
-      for (int jj = 0; jj < BNP; ++jj) {
-        const float e = expf(__fsub_rn(row[jj], m));
-        l = __fadd_rn(l, e);
-        row[jj] = round_bf(e);
-      }
-      sl[wt] = l;
-    }
-    named_bar_sync(2, WORKERS);
-    for (int item = wt; item < nk * 128; item += WORKERS) {
-      const int j = item >> 7, rem = item & 127, r = rem >> 3, ch = rem & 7;
-      const int k = (k0 + j) % kb;
-      const int hi = slot_head[j];
-      const int d0 = k * 64 + ch * 8 - heads[hi] * hd;
-      const uint8_t* vv = st + (size_t)(hi * 3 + 2) * bx * B_SLOT;
-      const float* prow = sp + (hi * BNP + r) * (BNP + 1);
-      float acc[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) acc[t] = 0.0f;
-      for (int jj = 0; jj < BNP; ++jj) {
-        const float pj = prow[jj];
-        float vx[8];
-        unpack_bf16x8(staged_chunk(vv, jj, d0 >> 6, (d0 & 63) >> 3), vx);
-#pragma unroll
-        for (int t = 0; t < 8; ++t) acc[t] = fmaf(pj, vx[t], acc[t]);
-      }
-      const float l = sl[hi * BNP + r];
-      float v[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) v[t] = __fdiv_rn(acc[t], l);
-      *reinterpret_cast<uint4*>(sm.B + j * B_SLOT + b_offset(r, ch)) = pack8(v);
-    }
+    if (ts && wt == 0) ts[9] = global_ns();
     return (size_t)nk * B_SLOT;
   }
   return md.inplace ? (size_t)kb * B_SLOT : (size_t)nk * B_SLOT;
@@ -615,8 +662,10 @@ __device__ void xattn_item(const PassArgs& P, const Smem& sm, int layer, int bh,
     const int row = k_begin + issued * XA_TILE;
 #pragma unroll
     for (int bx = 0; bx < HD / 64; ++bx) {
-      tma_load_2d(dst + bx * XA_TILE * 128, P.cache_map, &sm.xa_full[s], bx * 64, (int)(krow + row));
-      tma_load_2d(dst + TILE_BYTES + bx * XA_TILE * 128, P.cache_map, &sm.xa_full[s], bx * 64, (int)(vrow + row));
+      if (copy_checked(P, dst + bx * XA_TILE * 128, XA_TILE * 128, sm.B, sm.B + B_REGION, nullptr, bx * 64))
+        tma_load_2d(dst + bx * XA_TILE * 128, P.cache_map, &sm.xa_full[s], bx * 64, (int)(krow + row));
+      if (copy_checked(P, dst + TILE_BYTES + bx * XA_TILE * 128, XA_TILE * 128, sm.B, sm.B + B_REGION, nullptr, bx * 64))
+        tma_load_2d(dst + TILE_BYTES + bx * XA_TILE * 128, P.cache_map, &sm.xa_full[s], bx * 64, (int)(vrow + row));
     }
     ++issued;
     return true;
@@ -865,7 +914,7 @@ __device__ void xattn_item(const PassArgs& P, const Smem& sm, int layer, int bh,
 template <int EPI>
 __device__ bool run_segment(const GemmArgs& a, const Smem& sm, uint32_t tmem, int seg, long long u0, long long seg_begin,
                             long long seg_end, long long U, int G, int c, uint8_t* fx, uint32_t fx_cap,
-                            uint32_t& fx_phase, volatile int* sabort) {
+                            uint32_t& fx_phase, volatile int* sabort, unsigned long long* ts) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = warp & 3, r = q * 32 + lane;
   const int kb = a.kb;
@@ -891,94 +940,93 @@ __device__ bool run_segment(const GemmArgs& a, const Smem& sm, uint32_t tmem, in
     tmem_wait_ld();
     epilogue16<EPI>(a, v, r, m, tile, 0, sm.xch, sm.xch64);
   } else {
+    // split tile: its owner is the CTA holding the tile's first k-block (for
+    // which this is the last segment); the others hand it their partials
     const long long c_first = cta_of_unit((long long)tile * kb, U, G);
     const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
-    const int slot = (seg_begin == u0) ? 0 : 1;
-    float* mine = a.ws + ((long long)(c * 2 + slot) * BNP) * 128;
-    {
+    const int ncon = (int)(c_last - c_first + 1);
+    constexpr uint32_t PART = BNP * 128 * 4;  // one contributor's partial tile
+    if (c != c_first) {
+      // a contributor's segment is its first one: slot 0
+      float* mine = a.ws + ((long long)(c * 2) * BNP) * 128;
       float v[16];
       tmem_ld_x16(taddr, v);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) __stcg(mine + (long long)j * 128 + r, v[j]);
-    }
-    __threadfence();
-    named_bar_sync(1, 128);
-    if (threadIdx.x == 64) {
-      const int old = atomicAdd(a.counters + tile, 1);
-      sm.flags[F_SPLIT_LAST] = (old == (int)(c_last - c_first));
-    }
-    named_bar_sync(1, 128);
-    const bool last = sm.flags[F_SPLIT_LAST] != 0;
-    named_bar_sync(1, 128);  // the flag is rewritten by the next segment
-    if (last) {
-      __threadfence();
+      named_bar_sync(1, 128);
+      if (threadIdx.x == 64) red_release_add(a.counters + tile, 1);
+    } else {
       float own[16], v[16];
       tmem_ld_x16(taddr, own);
       tmem_wait_ld();
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-      const int ncon = (int)(c_last - c_first + 1);
-      constexpr uint32_t PART = BNP * 128 * 4;  // one contributor's partial tile
-      if (fx != nullptr && (uint32_t)ncon * PART <= fx_cap) {
-        // every other contributor's partial in one round trip (bulk copies)
-        if (threadIdx.x == 64) {
-          fence_async_global();
-          mbar_arrive_expect_tx(sm.fix, (uint32_t)(ncon - 1) * PART);
-          for (long long cc = c_first; cc <= c_last; ++cc) {
-            if (cc == c) continue;
-            const long long first_tile = ((long long)cc * U / G) / kb;
-            const int cs = (first_tile == tile) ? 0 : 1;
-            bulk_load(fx + (cc - c_first) * PART, a.ws + ((cc * 2 + cs) * BNP) * 128, PART, sm.fix);
-          }
-          const bool ok = mbar_wait(sm.fix, fx_phase & 1u, sabort);
-          if (!ok) {
-            *sabort = 1;
-            record_error(a.err, DEV_TIMEOUT_FULL);
-          }
-          sm.flags[F_FIX] = ok ? 1 : 0;
-        }
-        ++fx_phase;
-        named_bar_sync(1, 128);
-        const bool ok = sm.flags[F_FIX] != 0;
-        named_bar_sync(1, 128);  // the flag is rewritten by the next fix-up
-        if (!ok) return false;
-        for (long long cc = c_first; cc <= c_last; ++cc) {
-          if (cc == c) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], own[j]);
-          } else {
-            const float* p = reinterpret_cast<const float*>(fx + (cc - c_first) * PART) + r;
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], p[j * 128]);
+      const bool staged = fx != nullptr && (uint32_t)ncon * PART <= fx_cap;
+      if (threadIdx.x == 64) {
+        // every other contributor arrived (bounded wait), then their partials
+        // in one round trip when shared memory has room
+        bool ok = wait_count(a.counters + tile, ncon - 1, sabort);
+        if (ts) ts[10] = global_ns();
+        if (ok) {
+          a.counters[tile] = 0;  // every contributor of this use has arrived
+          if (staged) {
+            fence_async_global();
+            mbar_arrive_expect_tx(sm.fix, (uint32_t)(ncon - 1) * PART);
+            for (long long cc = c_first + 1; cc <= c_last; ++cc) {
+              uint8_t* d = fx + (cc - c_first) * PART;
+              const float* src = a.ws + ((cc * 2) * BNP) * 128;
+              if ((reinterpret_cast<uintptr_t>(d) & 15) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                  d >= sm.B && d + PART <= sm.B + B_REGION)
+                bulk_load(d, src, PART, sm.fix);
+              else
+                record_error(a.err, DEV_BAD_COPY);
+            }
+            ok = mbar_wait(sm.fix, fx_phase & 1u, sabort);
           }
         }
-      } else
-      for (long long cc0 = c_first; cc0 <= c_last; cc0 += 4) {
-        float tv[4][16];
+        if (ts) ts[11] = global_ns();
+        if (!ok) {
+          *sabort = 1;
+          record_error(a.err, DEV_TIMEOUT_OTHER);
+        }
+        sm.flags[F_FIX] = ok ? 1 : 0;
+      }
+      if (staged) ++fx_phase;
+      named_bar_sync(1, 128);
+      const bool ok = sm.flags[F_FIX] != 0;
+      named_bar_sync(1, 128);  // the flag is rewritten by the next fix-up
+      if (!ok) return false;
+      // partials summed in contributor order (the owner is the first)
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const long long cc = cc0 + q4;
-          if (cc <= c_last && cc != c) {
-            const long long first_tile = ((long long)cc * U / G) / kb;
-            const int cs = (first_tile == tile) ? 0 : 1;
-            const float* p = a.ws + ((cc * 2 + cs) * BNP) * 128 + r;
+      for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], own[j]);
+      if (staged) {
+        for (long long cc = c_first + 1; cc <= c_last; ++cc) {
+          const float* p = reinterpret_cast<const float*>(fx + (cc - c_first) * PART) + r;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], p[j * 128]);
+        }
+      } else {
+        for (long long cc0 = c_first + 1; cc0 <= c_last; cc0 += 4) {
+          float tv[4][16];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const long long cc = cc0 + q4 <= c_last ? cc0 + q4 : c_last;
+            const float* p = a.ws + ((cc * 2) * BNP) * 128 + r;
 #pragma unroll
             for (int j = 0; j < 16; ++j) tv[q4][j] = __ldcg(p + (long long)j * 128);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) tv[q4][j] = own[j];
           }
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4)
+            if (cc0 + q4 <= c_last) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], tv[q4][j]);
+            }
         }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          if (cc0 + q4 <= c_last) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], tv[q4][j]);
-          }
       }
+      if (ts && threadIdx.x == 64) ts[12] = global_ns();
       epilogue16<EPI>(a, v, r, m, tile, 0, sm.xch, sm.xch64);
-      if (threadIdx.x == 64) a.counters[tile] = 0;
+      if (ts && threadIdx.x == 64) ts[13] = global_ns();
     }
   }
   tc_fence_before();
@@ -989,15 +1037,15 @@ __device__ bool run_segment(const GemmArgs& a, const Smem& sm, uint32_t tmem, in
 
 __device__ bool run_segment_any(int epi, const GemmArgs& a, const Smem& sm, uint32_t tmem, int seg, long long u0,
                                 long long sb, long long se, long long U, int G, int c, uint8_t* fx, uint32_t fx_cap,
-                                uint32_t& fxp, volatile int* sabort) {
+                                uint32_t& fxp, volatile int* sabort, unsigned long long* ts) {
   switch (epi) {
-    case EPI_STORE: return run_segment<EPI_STORE>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_GELU: return run_segment<EPI_GELU>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_SWIGLU: return run_segment<EPI_SWIGLU>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_RESID: return run_segment<EPI_RESID>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_QKNORM: return run_segment<EPI_QKNORM>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_KVCACHE: return run_segment<EPI_KVCACHE>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
-    case EPI_LOGITS: return run_segment<EPI_LOGITS>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort);
+    case EPI_STORE: return run_segment<EPI_STORE>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_GELU: return run_segment<EPI_GELU>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_SWIGLU: return run_segment<EPI_SWIGLU>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_RESID: return run_segment<EPI_RESID>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_QKNORM: return run_segment<EPI_QKNORM>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_KVCACHE: return run_segment<EPI_KVCACHE>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
+    case EPI_LOGITS: return run_segment<EPI_LOGITS>(a, sm, tmem, seg, u0, sb, se, U, G, c, fx, fx_cap, fxp, sabort, ts);
     default: return false;
   }
 }
@@ -1099,6 +1147,7 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
             stage_units(T.units, G, c, &pf.u, &pf.u1);
             pf.kb = T.kb;
             pf.map = P.tmaps + T.tmap;
+            tmap_acquire(pf.map);
             continue;
           }
           tma_prefetch_l2_2d(pf.map, (int)(pf.u % pf.kb) * 64, (int)(pf.u / pf.kb) * 128);
@@ -1114,8 +1163,9 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
         stage_units(U, G, c, &u0, &u1);
         const int kb = S.kb;
         const CUtensorMap* map = P.tmaps + S.tmap;
+        if (u1 > u0) tmap_acquire(map);
         for (long long u = u0; u < u1; ++u, ++i) {
-          prefetch_to(i + PF_TILES);
+          if (P.pf_tiles) prefetch_to(i + (uint32_t)P.pf_tiles);
           const int slot = i % NA;
           const uint32_t round = i / NA;
           if (round > 0 && !mbar_wait(&sm.a_empty[slot], (round - 1) & 1u, sabort)) {
@@ -1124,8 +1174,9 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
             break;
           }
           mbar_arrive_expect_tx(&sm.a_full[slot], A_BYTES);
-          tma_load_2d_hint(sm.A + slot * A_BYTES, map, &sm.a_full[slot], (int)(u % kb) * 64, (int)(u / kb) * 128,
-                           pol);
+          if (copy_checked(P, sm.A + slot * A_BYTES, A_BYTES, sm.A, sm.A + NA * A_BYTES, nullptr, (int)(u % kb) * 64))
+            tma_load_2d_hint(sm.A + slot * A_BYTES, map, &sm.a_full[slot], (int)(u % kb) * 64, (int)(u / kb) * 128,
+                             pol);
         }
       }
       if (!ok) *sabort = 1;
@@ -1220,6 +1271,17 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
       }
     }
     unsigned long long* trace = P.trace ? P.trace + (size_t)c * P.n_stages * TRACE_SLOTS : nullptr;
+    {
+      // rotary factors of the block slots (positions len + 1 + k) for the q/k norms
+      const int len = P.lengths[0];
+      for (int i = wt; i < P.block * P.rope_half; i += WORKERS) {
+        const int k = i / P.rope_half, f = i % P.rope_half;
+        int pos = len + 1 + k;
+        if (pos < 0 || pos >= P.rope_len) pos = 0;  // recorded as DEV_BAD_INDEX by the prep step
+        sm.rope[k * P.rope_half + f] = P.rope_cos[(long long)pos * P.rope_half + f];
+        sm.rope[(BNP + k) * P.rope_half + f] = P.rope_sin[(long long)pos * P.rope_half + f];
+      }
+    }
     for (int s = 0; s < P.n_stages; ++s) {
       unsigned long long* ts = trace ? trace + s * TRACE_SLOTS : nullptr;
       if (ts && wt == 0) ts[0] = global_ns();
@@ -1261,6 +1323,10 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
           a.ws = P.ws + (long long)par * G * 2 * BNP * 128;
           a.counters = P.counters + (long long)par * P.max_tiles;
           a.err = P.err;
+          if (S.epi == EPI_QKNORM) {
+            a.tok_cos = sm.rope;
+            a.tok_sin = sm.rope + BNP * P.rope_half;
+          }
           if (S.is_lm) {
             a.out = P.logits;
             a.ldo = P.ldl;
@@ -1288,7 +1354,7 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
             const long long seg_begin = u;
             u = seg_end_of(u, u1, kb);
             if (!run_segment_any(S.epi, sm.stage->ep, sm, tmem, seg, u0, seg_begin, u, U, Gs, c, fx, fx_cap, fx_phase,
-                                 sabort))
+                                 sabort, ts))
               break;
             if (ts && wt == 0 && first) ts[5] = global_ns();
             first = false;
@@ -1301,6 +1367,7 @@ __global__ void __launch_bounds__(THREADS, 1) pass_kernel(const __grid_constant_
       } else if (S.type == ST_XATTN) {
         if (warp < 6) {
           fence_async_global();  // cache rows written by other CTAs' epilogues are read by TMA
+          if (wt == 0) tmap_acquire(P.cache_map);
           const int items = P.xa.batch * P.xa.heads * P.xa.nsplit;
           for (int it = c; it < items; it += G) {
             const int bh = it / P.xa.nsplit, split = it % P.xa.nsplit;

@@ -79,11 +79,15 @@ struct PassArgs {
   int* slot_pos;
   unsigned long long* keys;
   int64_t* tokens;
-  unsigned long long* trace;  // optional [grid][n_stages][4] timestamps (ns)
+  unsigned long long* trace;  // optional [grid][n_stages][10] timestamps (ns)
+  int pf_tiles;               // weight tiles a CTA keeps requested into L2 ahead of its loads (0: none)
   __nv_bfloat16* logits;
   long long ldl;
   int scatter;
   int rope_len, cache_len, block;
+  const float* rope_cos;  // [rope_len][rope_half]
+  const float* rope_sin;
+  int rope_half;
   long long vocab;
   CrossAttnArgs xa;
 };

@@ -21,6 +21,7 @@
 // A batch-1, one-jump draft instead runs as one persistent launch (pass.cu)
 // over the same buffers and weights: the stage list built by build_pass.
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <new>
@@ -70,6 +71,7 @@ struct fm_plan {
   bool pass_on;
   char pass_why[160];
   int pass_grid, pass_n_stages, pass_max_tiles;
+  int pass_prefetch;  // L2 prefetch distance in weight tiles (FM_PASS_PREFETCH, tuning)
   pass::Stage* pass_stages;  // device
   CUtensorMap* pass_tmaps;   // device
   CUtensorMap* pass_cache_map;
@@ -508,6 +510,11 @@ void build_pass(fm_plan* p) {
     return pass_off(p, "could not copy the stage list to the device");
   }
   p->pass_cache_map = p->pass_tmaps + (tm.size() - 1);
+  {
+    const char* e = getenv("FM_PASS_PREFETCH");
+    const int v = e ? atoi(e) : 0;
+    p->pass_prefetch = v >= 0 && v <= 256 ? v : 0;
+  }
   p->pass_n_stages = n;
   p->pass_grid = G;
   p->pass_on = true;
@@ -540,6 +547,7 @@ fm_status run_pass(fm_plan* p, const fm_draft_io* io, cudaStream_t s) {
   P.keys = p->keys;
   P.tokens = io->tokens;
   P.trace = reinterpret_cast<unsigned long long*>(io->trace);
+  P.pf_tiles = p->pass_prefetch;
   if (io->logits) {
     P.logits = static_cast<__nv_bfloat16*>(io->logits);
     P.ldl = io->ldl;
@@ -550,6 +558,9 @@ fm_status run_pass(fm_plan* p, const fm_draft_io* io, cudaStream_t s) {
     P.scatter = 0;
   }
   P.rope_len = m.rope_len;
+  P.rope_cos = m.rope_cos;
+  P.rope_sin = m.rope_sin;
+  P.rope_half = p->hd / 2;
   P.cache_len = p->cfg.cache_len;
   P.block = p->K;
   P.vocab = m.vocab;

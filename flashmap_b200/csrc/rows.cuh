@@ -108,6 +108,20 @@ __device__ __forceinline__ void unpack_bf16x8(const uint4 raw, float* x) {
   }
 }
 
+__device__ __forceinline__ uint4 pack_bf16x8(const float* v) {
+  uint4 o;
+  __nv_bfloat162 t;
+  t = __floats2bfloat162_rn(v[0], v[1]);
+  o.x = *reinterpret_cast<uint32_t*>(&t);
+  t = __floats2bfloat162_rn(v[2], v[3]);
+  o.y = *reinterpret_cast<uint32_t*>(&t);
+  t = __floats2bfloat162_rn(v[4], v[5]);
+  o.z = *reinterpret_cast<uint32_t*>(&t);
+  t = __floats2bfloat162_rn(v[6], v[7]);
+  o.w = *reinterpret_cast<uint32_t*>(&t);
+  return o;
+}
+
 // chunks lane + 32 * (base + i), i < 8, that exist
 __device__ __forceinline__ void lane_chunks8(const __nv_bfloat16* row, int nch, int lane, int base, uint4* raw) {
 #pragma unroll

@@ -420,7 +420,7 @@ class _Plan:
 
     def pass_shape(self) -> tuple:
         """(grid, stages) of the persistent pass: the trace buffer of ``draft``
-        holds grid x stages x 8 timestamps."""
+        holds grid x stages x 14 timestamps."""
         g, n = ctypes.c_int32(0), ctypes.c_int32(0)
         _lib.load().fm_plan_pass_shape(self.handle, ctypes.byref(g), ctypes.byref(n))
         return g.value, n.value

@@ -295,9 +295,11 @@ typedef struct fm_draft_io {
   int32_t scatter;           /* 1: write at draft_ids columns of a V-wide row */
   int64_t* tokens;           /* [B*K] argmax tokens (target ids) or NULL */
   void* hidden;              /* [B*K, Ht] bf16 DiT output of the last jump, or NULL */
-  uint64_t* trace;           /* persistent pass only, or NULL: [grid][stages][8] device timestamps (ns) of
+  uint64_t* trace;           /* persistent pass only, or NULL: [grid][stages][14] device timestamps (ns) of
                                 each stage in each CTA: start, inputs ready, operand loads issued, loads
-                                landed, operand built, first epilogue done, last epilogue done, arrived
+                                landed, operand built, first epilogue done, last epilogue done, arrived,
+                                row statistics done, operand transform done, and for the owner of a split
+                                tile: contributors arrived, partials loaded, partials summed, epilogue done
                                 (slots a stage does not pass through keep their old value) */
 } fm_draft_io;
 
