@@ -255,6 +255,181 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ secondary workloads (SURVEY configs 3, 4)
+
+def measured_peak_tensor():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def gemm_flops(c: dict, batch: int, block: int = 16) -> float:
+    """Dense GEMM FLOPs of one one-jump draft of `batch` sequences (slot path
+    and LM head per token, anchor path per sequence)."""
+    D, L, I, Ht, V = c["hidden_size"], c["num_hidden_layers"], c["intermediate_size"], c["target_hidden_size"], \
+        c["vocab_size"]
+    mlp = (3 if c.get("mlp_type") == "swiglu" else 2) * D * I
+    slot = L * (6 * D * D + mlp) + D * Ht + Ht * Ht + D * Ht
+    lm = (c.get("state_vocab_size") or V) * Ht
+    anchor = Ht * D + L * 2 * D * D
+    return 2.0 * batch * (block * (slot + lm) + anchor)
+
+
+def build_batched(c: dict, batch: int, lo: int, hi: int, seed: int, num_steps: int):
+    """A drafter with `batch` sequences whose contexts have ragged lengths
+    uniform in [lo, hi] (seeded), filled through the varlen extend_context."""
+    from flashmap_b200 import DraftSession, FlashMapCache, FlashMapConfig, FlashMapDraftModel
+    from flashmap_b200.synthetic import synthetic_state_dict, synthetic_target_head
+    from torch import nn
+
+    config = FlashMapConfig(**c)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    with torch.device(dev):
+        model = FlashMapDraftModel(config).to(torch.bfloat16).eval()
+    model.load_state_dict(synthetic_state_dict(config, seed=seed, dtype=torch.bfloat16, device=dev), strict=True)
+    emb_w, head_w = synthetic_target_head(config, seed=seed, dtype=torch.bfloat16, device=dev)
+    embed, head = nn.Embedding(*emb_w.shape, device=dev, dtype=torch.bfloat16), nn.Linear(1, 1, bias=False)
+    embed.weight = nn.Parameter(emb_w, requires_grad=False)
+    head.weight = nn.Parameter(head_w, requires_grad=False)
+    g = torch.Generator().manual_seed(seed + 5)
+    lengths = torch.randint(lo, hi + 1, (batch,), generator=g)
+    K = config.block_size
+    cache = FlashMapCache(config, batch, int(lengths.max()) + K + 2, device=dev, dtype=torch.bfloat16)
+    cu = torch.zeros(batch + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lengths, 0)
+    gd = torch.Generator(device=dev).manual_seed(seed + 6)
+    width = len(config.target_layer_ids) * config.target_hidden_size
+    rows = torch.randn(int(cu[-1]), width, generator=gd, device=dev).to(torch.bfloat16)
+    model.extend_context_varlen(cache, rows, cu.to(dev), embed, head)
+    del rows
+    session = DraftSession(model, cache, embed, head, num_steps=num_steps, seed=seed)
+    return config, model, cache, session, lengths
+
+
+def time_replays(session, steps: int, warmup: int, world: int) -> float:
+    for _ in range(warmup):
+        session.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        session.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return max_over_ranks(a.elapsed_time(b), world) / steps
+
+
+def run_config3(args, world, rank, local):
+    """Batched ragged drafting (SURVEY config 3): 64 sequences per GPU,
+    contexts U[512, 4096], one jump and two jumps."""
+    from flashmap_b200 import _lib
+
+    _lib.require_device()
+    batch = 64
+    out = {}
+    for steps_n in (1, 2):
+        config, model, cache, session, lengths = build_batched(CONFIG2, batch, 512, 4096, seed=rank, num_steps=steps_n)
+        ms = time_replays(session, args.steps, args.warmup, world)
+        model._plans[next(iter(model._plans))].check_device_errors()
+        out[steps_n] = (ms, lengths)
+        del model, cache, session
+        torch.cuda.empty_cache()
+    ms1, lengths = out[1]
+    ms2, _ = out[2]
+    K = 16
+    flops = gemm_flops(CONFIG2, batch)
+    kv = float(((lengths + 1).sum()) * CONFIG2["num_hidden_layers"] * 2 * CONFIG2["hidden_size"] * 2)
+    peak_t, kind_t = measured_peak_tensor()
+    peak_h, kind_h = measured_peak_hbm()
+    achieved = flops / (ms1 / 1000.0) / 1e12
+    if rank != 0:
+        return
+    line = {
+        "metric": "drafted tokens/sec (K=16), batch 64 ragged per GPU", "value": world * batch * K / (ms1 / 1000.0),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms1,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init config-2 drafter, N(0,1) conditioning, context lengths U[512,4096])",
+        "config": {"workload": "config3: batch 64 ragged, K=16, one jump (and two jumps below)", "batch_per_gpu": batch,
+                   "context_mean": float(lengths.float().mean()), "launch": "kernel sequence"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
+                     "frac": achieved / peak_t, "peak_kind": kind_t, "gemm_tflop_per_pass": flops / 1e12,
+                     "kv_bytes_per_pass": kv, "kv_floor_us": kv / (peak_h * 1e9) * 1e6,
+                     "gemm_floor_us": flops / (peak_t * 1e12) * 1e6},
+        "two_jumps": {"ms_per_step": ms2, "value": world * batch * K / (ms2 / 1000.0), "unit": "tokens/s"},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_config4(args, world, rank, local):
+    """Acceptance (SURVEY config 4): target logits (64, 17, 151936) bf16 ~ N(0, 2^2),
+    drafted tokens U[0, V), draft probabilities softmax(N(0,1)); greedy and
+    rejection at T = 1 with Philox seed 1234."""
+    import ctypes
+
+    from flashmap_b200 import _lib
+
+    _lib.require_device()
+    lib = _lib.load()
+    B, K, V = 64, 16, 151936
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    target = (2.0 * torch.randn(B, K + 1, V, generator=g, device=dev)).to(torch.bfloat16)
+    draft = torch.randint(0, V, (B, K), generator=g, device=dev)
+    q = torch.softmax(torch.randn(B, K, V, generator=g, device=dev), -1)
+    acc = torch.empty(B, dtype=torch.int64, device=dev)
+    bonus = torch.empty_like(acc)
+    wsb = lib.fm_accept_workspace_size(B, K)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+
+    def greedy():
+        lib.fm_accept_greedy(p(target), 0, p(draft), B, K, V, p(acc), p(bonus), p(ws), wsb, ctypes.c_void_p(st))
+
+    def rejection():
+        lib.fm_accept_rejection(p(target), 0, p(draft), p(q), B, K, V, ctypes.c_float(1.0), ctypes.c_uint64(1234),
+                                ctypes.c_uint32(0), p(acc), p(bonus), p(ws), wsb, ctypes.c_void_p(st))
+
+    res = {}
+    for name, fn in (("greedy", greedy), ("rejection", rejection)):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        res[name] = max_over_ranks(a.elapsed_time(b), world) / args.steps * 1000.0  # us
+    peak_h, kind_h = measured_peak_hbm()
+    bytes_g = B * (K + 1) * V * 2
+    bytes_r = bytes_g + B * V * 4
+    if rank != 0:
+        return
+    line = {
+        "metric": "acceptance of a (64 x 17 x 151936) block, us per call (greedy)", "value": res["greedy"],
+        "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["greedy"] / 1000,
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded: logits 2*N(0,1), draft tokens U[0,V), Q = softmax(N(0,1)))",
+        "config": {"workload": "config4: acceptance, B=64, K+1=17, V=151936, T=0 and T=1 (Philox seed 1234)"},
+        "roofline": {"bound": "hbm", "achieved": bytes_g / (res["greedy"] * 1e-6) / 1e9, "peak": peak_h,
+                     "unit": "GB/s", "frac": bytes_g / (res["greedy"] * 1e-6) / 1e9 / peak_h, "peak_kind": kind_h,
+                     "algorithmic_bytes": bytes_g, "floor_us": bytes_g / (peak_h * 1e9) * 1e6},
+        "rejection": {"us": res["rejection"], "algorithmic_bytes": bytes_r,
+                      "achieved_gbs": bytes_r / (res["rejection"] * 1e-6) / 1e9,
+                      "frac": bytes_r / (res["rejection"] * 1e-6) / 1e9 / peak_h,
+                      "floor_us": bytes_r / (peak_h * 1e9) * 1e6},
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------------ our arm
 
 def run_ours(args, world, rank, local):
@@ -365,6 +540,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch", choices=["auto", "kernels", "persistent"], default="auto",
                     help="launch structure of a draft: the kernel sequence or one persistent launch")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4"], default="config2",
+                    help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance)")
     ap.add_argument("--profile-small", action="store_true",
                     help="2 layers and a 32768-row LM head: the same kernels on < 2 GB, for ncu captures")
     args = ap.parse_args()
@@ -375,6 +552,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "config3":
+            run_config3(args, world, rank, local)
+        elif args.workload == "config4":
+            run_config4(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -548,6 +548,32 @@ class FlashMapDraftModel(PreTrainedModel):
         plan.extend(rows, cu, B)
         cache._length += n
 
+    @torch.no_grad()
+    def extend_context_varlen(self, cache: FlashMapCache, target_hidden: torch.Tensor, cu_seqlens: torch.Tensor,
+                              embed_tokens=None, lm_head=None) -> None:
+        """Ragged ``extend_context``: sequence ``b`` appends the rows
+        ``target_hidden[cu_seqlens[b]:cu_seqlens[b+1]]`` (packed ``(sum n_b, ...)``)
+        at its own next positions; every sequence's length advances by its
+        ``n_b`` (the per-sequence form of modeling_flashmap.py:342-351 that the
+        serving plugins use with packed ``cu_seqlens``)."""
+        self._check_cache(cache)
+        cu = cu_seqlens.to(cache.kv.device, torch.int32).contiguous()
+        B = cu.shape[0] - 1
+        if B != cache.kv.shape[2]:
+            raise ValueError(f"cu_seqlens describes {B} sequences, the cache holds {cache.kv.shape[2]}")
+        counts = (cu[1:] - cu[:-1]).cpu()
+        if (counts < 0).any():
+            raise ValueError("cu_seqlens must be non-decreasing")
+        after = cache.lengths.cpu() + counts
+        if int(after.max()) > cache.max_length:
+            raise ValueError(f"FlashMapCache holds {cache.max_length} positions, writing up to {int(after.max())}")
+        rows = target_hidden.to(cache.kv.device, torch.bfloat16).reshape(int(cu[-1].item()), -1).contiguous()
+        pack = self._pack(cache.kv.device, embed_tokens, lm_head)
+        self._caches.add(cache)
+        plan = self._any_plan(pack, cache, rows.shape[0])
+        plan.extend(rows, cu, B)
+        cache._length = int(after.max())
+
     def attach_target(self, embed_tokens: nn.Module, lm_head: nn.Module) -> None:
         """Prepare the target's embedding-derived constants once (the reference
         computes them lazily on the first draft, :401-420)."""
