@@ -213,3 +213,35 @@ def test_config2_draft_parity():
           f"PyTorch-on-GPU reference {fl:.5f}")
     assert max(rels) <= LOGITS_RTOL
     assert tie >= min(fl - 0.005, 0.999) and tie >= 0.97
+
+
+def test_ragged_batch_matches_per_sequence_oracle():
+    """A batch of sequences with ragged contexts (the packed varlen
+    extend_context and one batched draft) equals each sequence drafted alone
+    by the oracle at batch 1 (SURVEY config 3 at config-1/5S sizes)."""
+    for cfg, lens in ((CONFIG1, [40, 7, 129]), (CONFIG5S, [3, 64])):
+        config, model, oracle, emb, head = build(cfg, seed=8)
+        E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+        K, B = config.block_size, len(lens)
+        width = len(config.target_layer_ids) * config.target_hidden_size
+        g = torch.Generator().manual_seed(77)
+        ctx = [torch.randn(n, width, generator=g).to(torch.bfloat16) for n in lens]
+        cache = FlashMapCache(config, B, max(lens) + K + 2, device=DEV, dtype=torch.bfloat16)
+        cu = torch.tensor([0] + list(torch.cumsum(torch.tensor(lens), 0)), dtype=torch.int32)
+        model.extend_context_varlen(cache, torch.cat(ctx).to(DEV), cu.to(DEV), E, W)
+        assert cache.lengths.cpu().tolist() == lens
+        anchors = torch.randint(0, config.vocab_size, (B,), generator=g)
+        z = torch.randn(B, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+        got, tok = model.draft(anchors.to(DEV), cache, E, W, num_steps=1, z=z.to(DEV), return_tokens=True)
+        for b, n in enumerate(lens):
+            oc = OracleCache(config, 1, n + K + 2, torch.bfloat16)
+            oracle.extend_context(oc, ctx[b][None])
+            ref = oracle.draft(anchors[b:b + 1], oc, emb, head, num_steps=1, z=z[b:b + 1])
+            assert logits_rel_error(got[b:b + 1], ref) <= LOGITS_RTOL, (cfg, b)
+            assert argmax_agreement(tok[b:b + 1], ref)[0] >= 0.875
+            # the sequence's own cache rows match a batch-1 extend of the same rows (the
+            # GEMMs split their reductions differently for other row counts: bf16 rounding)
+            if n:
+                one = FlashMapCache(config, 1, max(lens) + K + 2, device=DEV, dtype=torch.bfloat16)
+                model.extend_context(one, ctx[b][None].to(DEV), E, W)
+                assert logits_rel_error(cache.kv[:, :, b, :, :n], one.kv[:, :, 0, :, :n]) < 1e-2
