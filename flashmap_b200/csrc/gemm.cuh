@@ -90,9 +90,41 @@ __device__ __forceinline__ long long cta_of_unit(long long u, long long U, int G
 // ---------------------------------------------------------------------------------------------
 // Epilogue on 16 accumulator columns (tokens n0 .. n0+15) of tile row r (feature m).
 // Threads of the 4 epilogue warps call it together (it may use named barrier 1).
+// Values an epilogue reads from global memory for 16 token columns, loaded
+// ahead of the chunk that needs them (so that a wide tile's chunks overlap
+// their round trips): the residual x (EPI_RESID), the rotary factors from the
+// per-token tables (EPI_QKNORM with tok_cos).  Returns false when the
+// epilogue has nothing to prefetch.
+template <int EPI>
+__device__ __forceinline__ bool epilogue_prefetch(const GemmArgs& a, int m, int n0, float* pre) {
+  if constexpr (EPI == EPI_RESID) {
+    const bool mvalid = m < a.M;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = n0 + j;
+      pre[j] = (mvalid && n < a.N) ? bf2f(a.out[(long long)n * a.ldo + m]) : 0.0f;
+    }
+    return true;
+  } else if constexpr (EPI == EPI_QKNORM) {
+    // only q and k rows are rotated (the tile's part is uniform: rows m & ~127)
+    if (a.tok_cos == nullptr || (m & ~127) / a.part_rows >= 2) return false;
+    const int half = a.head_dim >> 1;
+    const int d = (m % a.part_rows) % a.head_dim;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = (n0 + j < a.N) ? n0 + j : 0;
+      pre[j] = a.tok_cos[n * half + (d >> 1)];
+      pre[16 + j] = a.tok_sin[n * half + (d >> 1)];
+    }
+    return true;
+  } else {
+    return false;
+  }
+}
+
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, int r, int m, int mt, int n0,
-                                           float* xch, unsigned long long* xch64) {
+                                           float* xch, unsigned long long* xch64, const float* pre = nullptr) {
   const int lane = threadIdx.x & 31;
   const int q = (threadIdx.x >> 5) & 3;
   const bool mvalid = m < a.M;
@@ -116,7 +148,7 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
         *dst = f2bf(y);
       } else if constexpr (EPI == EPI_RESID) {
         const float gy = round_bf(__fmul_rn(g, y));
-        *dst = f2bf(__fadd_rn(bf2f(*dst), gy));
+        *dst = f2bf(__fadd_rn(pre ? pre[j] : bf2f(*dst), gy));
       } else {
         *dst = f2bf(y);
       }
@@ -190,8 +222,14 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
       const float wd = bf2f(w[d]);
       const int half = hd >> 1;
       float rc[16], rs[16];
-      if (EPI == EPI_QKNORM && a.tok_cos != nullptr) {
-        // the tokens' rotary factors, gathered once per launch (positions checked there)
+      if (EPI == EPI_QKNORM && pre != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          rc[j] = pre[j];
+          rs[j] = pre[16 + j];
+        }
+      } else if (EPI == EPI_QKNORM && a.tok_cos != nullptr) {
+        // the tokens' rotary factors, gathered once per draft (positions checked there)
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = (n0 + j < a.N) ? n0 + j : 0;
@@ -458,11 +496,19 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const bool whole = (seg_begin == (long long)tile * kb) && (seg_end == (long long)(tile + 1) * kb);
       if (whole) {
+        // chunks of 16 columns; each chunk's global reads issued one chunk ahead
+        float pre[32];
+        bool have = epilogue_prefetch<EPI>(a, m, n0, pre);
         for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
+          float v[16], nxt[32];
           tmem_ld_x16(taddr + c0, v);
+          const bool more = have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
           tmem_wait_ld();
-          epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64);
+          epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
+          if (more) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
+          }
         }
       } else {
         const long long c_first = cta_of_unit((long long)tile * kb, U, G);
@@ -485,9 +531,12 @@ __global__ void __launch_bounds__(192, 1)
         named_bar_sync(1, 128);
         if (flags[1]) {
           __threadfence();
+          float pre[32];
+          const bool have = epilogue_prefetch<EPI>(a, m, n0, pre);
           for (int c0 = 0; c0 < BN; c0 += 16) {
-            float own[16], v[16];
+            float own[16], v[16], nxt[32];
             tmem_ld_x16(taddr + c0, own);
+            const bool more = have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
             tmem_wait_ld();
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = 0.0f;
@@ -516,7 +565,11 @@ __global__ void __launch_bounds__(192, 1)
                   for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], t[q4][j]);
                 }
             }
-            epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64);
+            epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
+            if (more) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
+            }
           }
           if (threadIdx.x == 64) a.counters[tile] = 0;
         }

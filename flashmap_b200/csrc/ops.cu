@@ -397,6 +397,30 @@ __global__ void __launch_bounds__(RT) draft_prep_kernel(DraftPrepArgs a) {
     a.slot_pos[b * a.K + k] = len + 1 + k;
     a.keys[b * a.K + k] = 0ull;
   }
+  // the slots' rotary factors, read once here instead of in every q/k epilogue
+  const int half = a.rope_half;
+  for (int i = threadIdx.x; i < a.K * half; i += RT) {
+    const int k = i / half, f = i - k * half;
+    int pos = len + 1 + k;
+    if (pos < 0 || pos >= a.rope_len) pos = 0;  // recorded above
+    a.tok_cos[(long long)b * a.K * half + i] = a.rope_cos[(long long)pos * half + f];
+    a.tok_sin[(long long)b * a.K * half + i] = a.rope_sin[(long long)pos * half + f];
+  }
+}
+
+__global__ void __launch_bounds__(RT) rope_gather_kernel(const int* positions, int T, const float* rope_cos,
+                                                         const float* rope_sin, int rope_len, int half,
+                                                         float* tok_cos, float* tok_sin, int* err) {
+  const long long i = (long long)blockIdx.x * RT + threadIdx.x;
+  if (i >= (long long)T * half) return;
+  const int t = (int)(i / half), f = (int)(i - (long long)t * half);
+  int pos = positions[t];
+  if (pos < 0 || pos >= rope_len) {
+    if (f == 0) record_error(err, DEV_BAD_INDEX);
+    pos = 0;
+  }
+  tok_cos[i] = rope_cos[(long long)pos * half + f];
+  tok_sin[i] = rope_sin[(long long)pos * half + f];
 }
 
 __global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
@@ -734,6 +758,14 @@ fm_status launch_adaln(const __nv_bfloat16* x, const __nv_bfloat16* mod, __nv_bf
 }
 fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(draft_prep_kernel, dim3(a.B), dim3(RT), 0, s, pdl, a);
+}
+
+fm_status launch_rope_gather(const int* positions, int T, const float* rope_cos, const float* rope_sin, int rope_len,
+                             int half, float* tok_cos, float* tok_sin, int* err, cudaStream_t s) {
+  const long long n = (long long)T * half;
+  if (n == 0) return FM_OK;
+  return launch_kernel(rope_gather_kernel, dim3((unsigned)((n + RT - 1) / RT)), dim3(RT), 0, s, false, positions, T,
+                       rope_cos, rope_sin, rope_len, half, tok_cos, tok_sin, err);
 }
 fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(mix_state_kernel, dim3(blocks_for(a.T, ROWS_PER_CTA)), dim3(RT), 0, s, pdl, a);

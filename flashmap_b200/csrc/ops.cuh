@@ -18,6 +18,9 @@ struct DraftPrepArgs {
   int* anchor_pos;            // [B]
   int* anchor_seq;            // [B]
   int* slot_pos;              // [B*K]
+  float *tok_cos, *tok_sin;   // [B*K][rope_half] rotary factors of the slots' positions
+  const float *rope_cos, *rope_sin;  // [rope_len][rope_half]
+  int rope_half;
   unsigned long long* keys;   // [B*K]
   int B, K, Ht;
   long long V;
@@ -26,6 +29,11 @@ struct DraftPrepArgs {
   int* err;
 };
 fm_status launch_draft_prep(const DraftPrepArgs& a, cudaStream_t s, bool pdl);
+
+// tok_cos/tok_sin[t] = rotary factors of positions[t] (out-of-range positions
+// record DEV_BAD_INDEX and read position 0)
+fm_status launch_rope_gather(const int* positions, int T, const float* rope_cos, const float* rope_sin, int rope_len,
+                             int half, float* tok_cos, float* tok_sin, int* err, cudaStream_t s);
 
 // inputs = bf16(state_norm(post) + bf16(gate * noise_norm(state)))  (modeling_flashmap.py:393-399)
 struct MixArgs {

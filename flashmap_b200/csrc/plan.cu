@@ -54,6 +54,7 @@ struct fm_plan {
   int nsplit;
   __nv_bfloat16 *anchor_rows, *anchor_h, *anchor_ctx;
   int *anchor_pos, *anchor_seq, *slot_pos;
+  float *tok_cos, *tok_sin;  // [T][hd/2] rotary factors of the slots' positions
   unsigned long long* keys;
   __nv_bfloat16 *z, *zl, *inputs, *x, *h, *qkv, *attn, *qc, *mlp, *hidden, *logits_s;
   float* state;
@@ -193,6 +194,8 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
   int* anchor_pos = cv.take<int>(B);
   int* anchor_seq = cv.take<int>(B);
   int* slot_pos = cv.take<int>(T);
+  float* tok_cos = cv.take<float>(T * (hd / 2));
+  float* tok_sin = cv.take<float>(T * (hd / 2));
   unsigned long long* keys = cv.take<unsigned long long>(T);
   __nv_bfloat16* z = cv.take<__nv_bfloat16>(T * Ht);
   __nv_bfloat16* zl = cv.take<__nv_bfloat16>(T * Ht);
@@ -240,6 +243,8 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
     p->anchor_pos = anchor_pos;
     p->anchor_seq = anchor_seq;
     p->slot_pos = slot_pos;
+    p->tok_cos = tok_cos;
+    p->tok_sin = tok_sin;
     p->keys = keys;
     p->z = z;
     p->zl = zl;
@@ -708,6 +713,8 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
       a.rope_sin = m->rope_sin;
       a.rope_len = m->rope_len;
       a.positions = p->slot_pos;
+      a.tok_cos = p->tok_cos;  // filled per draft by draft_prep, per forward by rope_gather
+      a.tok_sin = p->tok_sin;
     }
     g[1].args.out = p->x;
     g[1].args.ldo = D;
@@ -852,6 +859,10 @@ extern "C" fm_status fm_forward(fm_plan* p, const fm_forward_io* io, fm_stream s
       (st = check_cuda(cudaMemcpyAsync(p->anchor_pos, io->ctx_last, (size_t)p->B * 4, cudaMemcpyDeviceToDevice, s),
                        "forward: context")))
     return st;
+  if ((st = launch_rope_gather(p->slot_pos, (int)T, static_cast<const float*>(p->m.rope_cos),
+                               static_cast<const float*>(p->m.rope_sin), p->m.rope_len, p->hd / 2, p->tok_cos,
+                               p->tok_sin, p->err, s)))
+    return st;
   fm_jump j{};
   j.mods = io->mods;
   if ((st = run_dit(p, j, s))) return st;
@@ -881,6 +892,11 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
   pa.anchor_pos = p->anchor_pos;
   pa.anchor_seq = p->anchor_seq;
   pa.slot_pos = p->slot_pos;
+  pa.tok_cos = p->tok_cos;
+  pa.tok_sin = p->tok_sin;
+  pa.rope_cos = static_cast<const float*>(m.rope_cos);
+  pa.rope_sin = static_cast<const float*>(m.rope_sin);
+  pa.rope_half = p->hd / 2;
   pa.keys = p->keys;
   pa.B = p->B;
   pa.K = p->K;
