@@ -71,6 +71,29 @@ class ExtendIO(ctypes.Structure):
                 ("batch", c_int32)]
 
 
+FM_DT_BF16, FM_DT_F32, FM_DT_E4M3, FM_DT_I32, FM_DT_I64 = 0, 1, 2, 3, 4
+FM_NORM_DIT, FM_NORM_FUSED = 0, 1
+
+
+class RopeView(ctypes.Structure):
+    _fields_ = [("cos", c_void_p), ("sin", c_void_p), ("row_stride", c_int64), ("pair_stride", c_int64),
+                ("rows", c_int64)]
+
+
+class PagedAttn(ctypes.Structure):
+    _fields_ = [("q", c_void_p), ("q_dtype", c_int32), ("q_token_stride", c_int64), ("q_head_stride", c_int64),
+                ("cu_seqlens_q", c_void_p), ("q_per_request", c_int64), ("max_q", c_int64),
+                ("k", c_void_p), ("v", c_void_p), ("kv_dtype", c_int32),
+                ("kv_page_stride", c_int64), ("kv_head_stride", c_int64), ("kv_token_stride", c_int64),
+                ("page_size", c_int64), ("num_pages", c_int64),
+                ("page_table", c_void_p), ("page_table_stride", c_int64), ("page_table_cols", c_int64),
+                ("seqused_k", c_void_p), ("max_seqlen_k", c_int64),
+                ("requests", c_int64), ("heads", c_int64), ("head_dim", c_int64),
+                ("softmax_scale", c_float), ("descales", c_void_p), ("quantize_q", c_int32),
+                ("out", c_void_p), ("out_token_stride", c_int64), ("out_head_stride", c_int64),
+                ("workspace", c_void_p), ("workspace_bytes", c_size_t), ("nsplit", c_int32), ("err", c_void_p)]
+
+
 _SIGNATURES = {
     "fm_last_error": (ctypes.c_char_p, []),
     "fm_version": (c_int, []),
@@ -82,10 +105,28 @@ _SIGNATURES = {
     "fm_adaln": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "fm_rope_table": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "fm_philox_normal": (c_int, [c_void_p, c_int64, c_uint64, c_uint32, c_void_p]),
+    "fm_philox_normal_rows": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
+    "fm_mix_state": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float, c_int64,
+                             c_int64, c_void_p]),
     "fm_block_self_attn": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p]),
     "fm_cross_attn_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
     "fm_cross_attn": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                               c_int64, c_int64, c_int64, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "fm_qk_norm_rope": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_int32,
+                                RopeView, c_void_p, c_int32, c_float, c_int32, c_void_p, c_void_p]),
+    "fm_block_self_attn_qknorm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                          c_void_p, c_int32, RopeView, c_void_p, c_int32, c_float, c_float,
+                                          c_void_p, c_void_p]),
+    "fm_paged_attn_nsplit": (c_int32, [c_int64, c_int64, c_int64, c_int64, c_int32]),
+    "fm_paged_attn_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int32]),
+    "fm_paged_cross_attn": (c_int, [ctypes.POINTER(PagedAttn), c_void_p]),
+    "fm_write_context_kv_paged": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                          c_void_p, c_int32, RopeView, c_void_p, c_int64, c_int64, c_int64,
+                                          c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p,
+                                          c_void_p]),
+    "fm_kv_norm_rope_write_pool": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                           c_int32, RopeView, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                                           c_float, c_float, c_float, c_void_p, c_void_p]),
     "fm_row_stats": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
     "fm_softmax_rows": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p]),
     "fm_sample_rows": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_float, c_uint64, c_uint32,

@@ -512,6 +512,25 @@ __global__ void philox_normal_f32_kernel(float* out, long long count, uint64_t s
   if (2 * p + 1 < count) out[2 * p + 1] = z1;
 }
 
+// Row r of n_cols normals keyed by its request's seed and its position:
+// seed = seeds[rows[r]] (0 when rows[r] < 0), counter offset = positions[r];
+// pair p of the row uses counter (p, 0, offset, 4) like philox_normal.
+__global__ void philox_normal_rows_kernel(__nv_bfloat16* out, long long n_rows, long long n_cols,
+                                          const long long* seeds, const long long* rows, const long long* positions,
+                                          float scale) {
+  const long long half = (n_cols + 1) / 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_rows * half) return;
+  const long long r = idx / half, p = idx - r * half;
+  const long long st = rows[r];
+  const uint64_t seed = st >= 0 ? (uint64_t)seeds[st] : 0ull;
+  float z0, z1;
+  normal_pair(seed, (uint32_t)positions[r], p, z0, z1);
+  __nv_bfloat16* o = out + r * n_cols;
+  o[2 * p] = f2bf(__fmul_rn(z0, scale));
+  if (2 * p + 1 < n_cols) o[2 * p + 1] = f2bf(__fmul_rn(z1, scale));
+}
+
 __global__ void argmax_tokens_kernel(const unsigned long long* keys, int64_t* tokens, int n) {
   pdl_wait();
   pdl_launch_dependents();
@@ -840,6 +859,38 @@ extern "C" fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, u
   if (!out) return set_error(FM_ERR_INVALID, "philox_normal: null pointer");
   if (count <= 0) return FM_OK;
   return launch_philox_normal_bf16(bf(out), count, seed, offset, nullptr, as_stream(stream), false);
+}
+
+extern "C" fm_status fm_philox_normal_rows(void* out, int64_t n_rows, int64_t n_cols, const int64_t* seeds,
+                                           const int64_t* rows, const int64_t* positions, float scale,
+                                           fm_stream stream) {
+  if (n_rows < 0 || n_cols < 0) return set_error(FM_ERR_SHAPE, "philox_normal_rows: bad shape");
+  if (n_rows == 0 || n_cols == 0) return FM_OK;
+  if (!out || !seeds || !rows || !positions) return set_error(FM_ERR_INVALID, "philox_normal_rows: null pointer");
+  const long long pairs = n_rows * ((n_cols + 1) / 2);
+  return launch_kernel(philox_normal_rows_kernel, dim3(blocks_for(pairs, 256)), dim3(256), 0, as_stream(stream),
+                       false, bf(out), (long long)n_rows, (long long)n_cols, reinterpret_cast<const long long*>(seeds),
+                       reinterpret_cast<const long long*>(rows), reinterpret_cast<const long long*>(positions), scale);
+}
+
+extern "C" fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,
+                                  const void* noise_norm_w, void* out, float gate, float eps, int64_t rows,
+                                  int64_t cols, fm_stream stream) {
+  if (rows < 0 || cols < 1) return set_error(FM_ERR_SHAPE, "mix_state: bad shape");
+  if (rows == 0) return FM_OK;
+  if (!post || !state || !state_norm_w || !noise_norm_w || !out) return set_error(FM_ERR_INVALID, "mix_state: null pointer");
+  MixArgs a{};
+  a.post = static_cast<const __nv_bfloat16*>(post);
+  a.post_stride = post_stride;
+  a.state = static_cast<const __nv_bfloat16*>(state);
+  a.state_norm_w = static_cast<const __nv_bfloat16*>(state_norm_w);
+  a.noise_norm_w = static_cast<const __nv_bfloat16*>(noise_norm_w);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.gate = gate;
+  a.eps = eps;
+  a.T = (int)rows;
+  a.Ht = (int)cols;
+  return launch_mix_state(a, as_stream(stream), false);
 }
 
 extern "C" fm_status fm_block_self_attn(const void* qkv, void* out, int64_t batch, int64_t block, int64_t heads,

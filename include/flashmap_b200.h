@@ -102,6 +102,19 @@ FM_API fm_status fm_rope_table(float* cos_out, float* sin_out, int64_t max_pos, 
  * of modeling_flashmap.py:465.  Elements 2p and 2p+1 use counter (p, 0, offset, 4). */
 FM_API fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, uint32_t offset, fm_stream stream);
 
+/* Seeded draft noise of the serving plugins (vllm/kernels.py:367-414): row r holds n_cols
+ * bf16 standard normals times scale, keyed by seed seeds[rows[r]] (0 when rows[r] < 0) and
+ * Philox counter offset positions[r], so a seeded request draws the same noise whatever is
+ * batched with it.  rows, seeds and positions are int64. */
+FM_API fm_status fm_philox_normal_rows(void* out, int64_t n_rows, int64_t n_cols, const int64_t* seeds,
+                                       const int64_t* rows, const int64_t* positions, float scale, fm_stream stream);
+
+/* One-jump input mix (modeling_flashmap.py:393-399): out = bf16(state_norm(post) +
+ * bf16(gate * noise_norm(state))), post rows post_stride apart (0: one shared row). */
+FM_API fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,
+                              const void* noise_norm_w, void* out, float gate, float eps, int64_t rows, int64_t cols,
+                              fm_stream stream);
+
 /* Self-attention over the block slots (modeling_flashmap.py:188 with :144-147);
  * qkv [B*K, 3*D] with q, k already normed and rotated. Replaces the
  * flashmap_vllm::block_self_attention / flashmap_sglang::block_self_attention ops. */
@@ -118,6 +131,143 @@ FM_API fm_status fm_cross_attn(const void* q, const void* cache, void* out, cons
                         int64_t heads, int64_t head_dim, int64_t layers, int64_t layer, int64_t cache_batch,
                         int64_t cache_len, int64_t nsplit, void* workspace, size_t workspace_bytes, int32_t* err,
                         fm_stream stream);
+
+/* ------------------------------------------------------------------------
+ * Operators of the serving plugins (flashmap/vllm/kernels.py,
+ * flashmap/vllm/model.py:93, flashmap/sglang/kernels.py,
+ * flashmap/sglang/model.py:127-178, :728-766): q/k RMSNorm + interleaved
+ * RoPE, block self-attention from raw qkv, cross-attention over paged KV
+ * caches (bf16 or e4m3), and the writers of context keys/values into paged
+ * caches.  The torch.library ops of flashmap_b200.serving_ops call these.
+ * ------------------------------------------------------------------------ */
+
+/* Element types of operator arguments. */
+enum { FM_DT_BF16 = 0, FM_DT_F32 = 1, FM_DT_E4M3 = 2, FM_DT_I32 = 3, FM_DT_I64 = 4 };
+
+/* RMSNorm rounding: FM_NORM_DIT is the DiT's x * bf16(w * rsqrt(mean(x^2) + eps))
+ * (modeling_flashmap.py:69-80, vllm/kernels.py:38-46); FM_NORM_FUSED is
+ * bf16(x * rsqrt(mean(x^2) + eps) * w), the context writer of an e4m3 pool
+ * (sglang/kernels.py:309-311). */
+enum { FM_NORM_DIT = 0, FM_NORM_FUSED = 1 };
+
+/* A rotary table: cos(p, i) = cos[p * row_stride + i * pair_stride] (fp32), sin
+ * likewise, for positions p < rows and pairs i < head_dim / 2.  The vLLM table
+ * (positions, hd/2, [cos, sin]) is {t, t + 1, hd, 2}; sglang's per-token freqs
+ * are the same with the token index as position; sglang's writer table
+ * (positions, [cos | sin]) is {t, t + hd/2, hd, 1}. */
+typedef struct fm_rope_view {
+  const float* cos;
+  const float* sin;
+  int64_t row_stride;
+  int64_t pair_stride;
+  int64_t rows;
+} fm_rope_view;
+
+/* RMSNorm then interleaved RoPE of rows x[t, h, :] (rows of head_dim bf16,
+ * heads contiguous, tokens x_token_stride apart) into out (out_token_stride).
+ * The rotary row of token t is positions[t] (int32 or int64), or t when
+ * positions is NULL.  Replaces flashmap_vllm::rms_norm_rope (vllm/kernels.py:100)
+ * and flashmap_sglang::rms_norm_rope (sglang/kernels.py:170).  weight is
+ * head_dim values, bf16 or fp32. */
+FM_API fm_status fm_qk_norm_rope(const void* x, int64_t x_token_stride, void* out, int64_t out_token_stride,
+                                 int64_t tokens, int64_t heads, int64_t head_dim, const void* weight,
+                                 int32_t weight_dtype, fm_rope_view rope, const void* positions,
+                                 int32_t positions_dtype, float eps, int32_t norm_mode, int32_t* err,
+                                 fm_stream stream);
+
+/* Block self-attention from projected qkv (blocks, block, 3, heads, head_dim):
+ * q and k RMSNorm (FM_NORM_DIT) and RoPE at positions[blocks * block] (or the
+ * token index when NULL), unmasked softmax attention with the given scale,
+ * out (blocks * block, heads * head_dim).  One kernel; block == 16 and
+ * head_dim 64 or 128 (FM_ERR_UNSUPPORTED otherwise: compose fm_qk_norm_rope
+ * and fm_block_self_attn).  Replaces flashmap_vllm::block_self_attention
+ * (vllm/kernels.py:193) and flashmap_sglang::block_self_attention
+ * (sglang/kernels.py:84). */
+FM_API fm_status fm_block_self_attn_qknorm(const void* qkv, void* out, int64_t blocks, int64_t block, int64_t heads,
+                                           int64_t head_dim, const void* q_norm, const void* k_norm,
+                                           int32_t weight_dtype, fm_rope_view rope, const void* positions,
+                                           int32_t positions_dtype, float eps, float scale, int32_t* err,
+                                           fm_stream stream);
+
+/* Non-causal attention of each request's query rows onto the first
+ * seqused_k[r] positions of its paged context.  Position p of request r is
+ * row (p % page_size) of page page_table[r * page_table_stride + p / page_size];
+ * its key is k + page * kv_page_stride + head * kv_head_stride +
+ * (p % page_size) * kv_token_stride (elements), its value the same offset from
+ * v.  The vLLM FlashAttention cache (pages, heads, page, 2 * hd) is k = cache,
+ * v = cache + hd; sglang's pools (rows, heads, hd) are page_size 1.
+ * Query rows of request r: cu_seqlens_q[r] .. cu_seqlens_q[r + 1] - 1, or
+ * q_per_request rows from r * q_per_request when cu_seqlens_q is NULL.
+ * e4m3 caches: scores and outputs are descaled by descales (3, requests, heads)
+ * (query, key, value), or, with quantize_q, the bf16 query is quantised to
+ * e4m3 per (request, head) with scale amax / 448 (sglang/model.py:164-170).
+ * A request with no positions gets zero output rows.
+ * Replaces flashmap_vllm::paged_cross_attention (vllm/model.py:93-132),
+ * flashmap_sglang::paged_cross_attention[_fp8] (sglang/model.py:127-175). */
+typedef struct fm_paged_attn {
+  const void* q;
+  int32_t q_dtype; /* FM_DT_BF16 or FM_DT_E4M3 */
+  int64_t q_token_stride, q_head_stride;
+  const int32_t* cu_seqlens_q;
+  int64_t q_per_request;
+  int64_t max_q; /* the most query rows of one request */
+  const void* k;
+  const void* v;
+  int32_t kv_dtype; /* FM_DT_BF16 or FM_DT_E4M3 */
+  int64_t kv_page_stride, kv_head_stride, kv_token_stride;
+  int64_t page_size, num_pages;
+  const int32_t* page_table;
+  int64_t page_table_stride, page_table_cols;
+  const int32_t* seqused_k;
+  int64_t max_seqlen_k;
+  int64_t requests, heads, head_dim;
+  float softmax_scale;
+  const float* descales; /* (3, requests, heads) or NULL */
+  int32_t quantize_q;
+  void* out; /* bf16 */
+  int64_t out_token_stride, out_head_stride;
+  void* workspace; /* fm_paged_attn_workspace_size() bytes, zero on first use */
+  size_t workspace_bytes;
+  int32_t nsplit; /* key splits per (request, head, 16 query rows); 0 = choose */
+  int32_t* err;
+} fm_paged_attn;
+FM_API int32_t fm_paged_attn_nsplit(int64_t requests, int64_t heads, int64_t max_q, int64_t max_seqlen_k,
+                                    int32_t nsplit);
+FM_API size_t fm_paged_attn_workspace_size(int64_t requests, int64_t heads, int64_t head_dim, int64_t max_q,
+                                           int32_t nsplit);
+FM_API fm_status fm_paged_cross_attn(const fm_paged_attn* args, fm_stream stream);
+
+/* Every layer's context keys (k-normed FM_NORM_DIT, rotated at positions[t])
+ * and values of kv (tokens, layers, 2, heads, head_dim) bf16 into paged caches
+ * at slots[t] (negative: skipped).  Head g = layer * heads + h goes to cache
+ * g / heads_per_cache, head slot g % heads_per_cache; element strides (block,
+ * head, token) and the value offset are those of the vLLM FlashAttention cache,
+ * the same for every cache; cache_ptrs is a device array of num_caches data
+ * pointers.  With scales (layers, 2) fp32 the caches are e4m3 and hold key /
+ * k_scale and value / v_scale.  Replaces write_context_kv (vllm/kernels.py:311). */
+FM_API fm_status fm_write_context_kv_paged(const void* kv, int64_t tokens, int64_t layers, int64_t heads,
+                                           int64_t head_dim, const int64_t* positions, const int64_t* slots,
+                                           const void* k_norm, int32_t k_norm_dtype, fm_rope_view rope,
+                                           const int64_t* cache_ptrs, int64_t num_caches, int64_t heads_per_cache,
+                                           int64_t stride_block, int64_t stride_head, int64_t stride_token,
+                                           int64_t v_offset, int64_t block_size, float eps, const float* scales,
+                                           int32_t* err, fm_stream stream);
+
+/* sglang's context writer: kv (tokens, layers, 2, kv_size) bf16 with kv_size =
+ * heads * head_dim; per layer meta (layers, 4) int64 = (key pool pointer, value
+ * pool pointer, key row stride, value row stride) in elements; keys
+ * k-normed (FM_NORM_FUSED) and rotated at positions[t], written with values
+ * at pool row locs[t] (negative: skipped).  With commit_lens (rows of
+ * locs_row_width tokens), token t is written only when t % locs_row_width <
+ * commit_lens[t / locs_row_width].  pool_dtype FM_DT_E4M3 divides keys by
+ * k_scale and values by v_scale.  Replaces kv_norm_rope_write_fp8
+ * (sglang/kernels.py:284-331) and, for bf16 pools, the fused writer sglang/model.py:746-766 calls. */
+FM_API fm_status fm_kv_norm_rope_write_pool(const void* kv, int64_t tokens, int64_t layers, int64_t kv_size,
+                                            int64_t head_dim, const int64_t* meta, const void* k_norm,
+                                            int32_t k_norm_dtype, fm_rope_view rope, const int64_t* positions,
+                                            const int64_t* locs, const int32_t* commit_lens, int64_t locs_row_width,
+                                            int32_t pool_dtype, float k_scale, float v_scale, float eps,
+                                            int32_t* err, fm_stream stream);
 
 /* ------------------------------------------------------------------------
  * Sampling and acceptance (modeling_flashmap.py:553-557, :579-594).
