@@ -126,7 +126,7 @@ _SIGNATURES = {
                                           c_void_p]),
     "fm_kv_norm_rope_write_pool": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                            c_int32, RopeView, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
-                                           c_float, c_float, c_float, c_void_p, c_void_p]),
+                                           c_int32, c_float, c_float, c_float, c_void_p, c_void_p]),
     "fm_row_stats": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p, c_void_p]),
     "fm_softmax_rows": (c_int, [c_void_p, c_int32, c_int64, c_int64, c_float, c_void_p, c_void_p]),
     "fm_sample_rows": (c_int, [c_void_p, c_int32, c_void_p, c_int64, c_int64, c_int64, c_float, c_uint64, c_uint32,

@@ -682,7 +682,7 @@ struct WritePoolArgs {
   const long long* locs;
   const int* commit;
   long long row_w;
-  int fp8;
+  int fp8, mode;
   float ks, vs, eps;
   int* err;
 };
@@ -707,7 +707,7 @@ __global__ void __launch_bounds__(128) write_ctx_pool_kernel(WritePoolArgs a) {
   const int nh = a.KV / a.D;
   for (int h = threadIdx.x >> 5; h < nh; h += 4) {
     float re[NP], ro[NP];
-    warp_norm_rope<NP>(row + (long long)h * a.D, a.D, w, a.kdt, a.eps, FM_NORM_FUSED, a.rope, pos, a.err, re, ro);
+    warp_norm_rope<NP>(row + (long long)h * a.D, a.D, w, a.kdt, a.eps, a.mode, a.rope, pos, a.err, re, ro);
     const __nv_bfloat16* vrow = row + a.KV + (long long)h * a.D;
     if (a.fp8) {
       uint8_t* kd = reinterpret_cast<uint8_t*>(kbuf) + loc * kst + (long long)h * a.D;
@@ -963,8 +963,9 @@ extern "C" fm_status fm_kv_norm_rope_write_pool(const void* kv, int64_t tokens, 
                                                 int64_t head_dim, const int64_t* meta, const void* k_norm,
                                                 int32_t k_norm_dtype, fm_rope_view rope, const int64_t* positions,
                                                 const int64_t* locs, const int32_t* commit_lens,
-                                                int64_t locs_row_width, int32_t pool_dtype, float k_scale,
-                                                float v_scale, float eps, int32_t* err, fm_stream stream) {
+                                                int64_t locs_row_width, int32_t pool_dtype, int32_t norm_mode,
+                                                float k_scale, float v_scale, float eps, int32_t* err,
+                                                fm_stream stream) {
   if (tokens < 0 || layers < 1 || head_dim < 2 || kv_size < head_dim || kv_size % head_dim)
     return set_error(FM_ERR_SHAPE, "kv_norm_rope_write: bad shape");
   if (tokens == 0) return FM_OK;
@@ -974,12 +975,13 @@ extern "C" fm_status fm_kv_norm_rope_write_pool(const void* kv, int64_t tokens, 
   if (!np || head_dim % 2) return set_error(FM_ERR_UNSUPPORTED, "kv_norm_rope_write: head_dim must be even and <= 256");
   if (k_norm_dtype != FM_DT_BF16 && k_norm_dtype != FM_DT_F32) return set_error(FM_ERR_INVALID, "k_norm dtype");
   if (pool_dtype != FM_DT_BF16 && pool_dtype != FM_DT_E4M3) return set_error(FM_ERR_INVALID, "pool dtype");
+  if (norm_mode != FM_NORM_DIT && norm_mode != FM_NORM_FUSED) return set_error(FM_ERR_INVALID, "norm mode");
   fm_status st;
   if ((st = check_rope(rope))) return st;
   WritePoolArgs a{static_cast<const __nv_bfloat16*>(kv), (int)layers, (int)kv_size, (int)head_dim,
                   reinterpret_cast<const long long*>(meta), k_norm, k_norm_dtype, rope_ref(rope),
                   reinterpret_cast<const long long*>(positions), reinterpret_cast<const long long*>(locs),
-                  commit_lens, locs_row_width, pool_dtype == FM_DT_E4M3, k_scale, v_scale, eps, err};
+                  commit_lens, locs_row_width, pool_dtype == FM_DT_E4M3, norm_mode, k_scale, v_scale, eps, err};
   return launch_np<WritePoolK>(np, dim3((unsigned)tokens, (unsigned)layers), dim3(128),
                                static_cast<cudaStream_t>(stream), a);
 }

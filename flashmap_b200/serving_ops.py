@@ -510,8 +510,8 @@ def _pool_write(kv, meta, k_norm_weights, cos_sin, positions, locs, num_layers, 
     err = _err(kv.device)
     _lib.call("fm_kv_norm_rope_write_pool", _p(kv), tokens, num_layers, kv_size, head_dim, _p(meta.contiguous()),
               _p(kn), kdt, rope, _p(pos), _p(lc), _p(cl), int(locs_row_width or 1),
-              _lib.FM_DT_E4M3 if fp8 else _lib.FM_DT_BF16, float(k_scale), float(v_scale), float(eps), _p(err),
-              _stream())
+              _lib.FM_DT_E4M3 if fp8 else _lib.FM_DT_BF16, _lib.FM_NORM_FUSED if fp8 else _lib.FM_NORM_DIT,
+              float(k_scale), float(v_scale), float(eps), _p(err), _stream())
 
 
 def kv_norm_rope_write_fp8(kv, meta, k_norm_weights, cos_sin, positions, locs, num_layers, kv_size, head_dim, eps, *,
@@ -526,7 +526,9 @@ def kv_norm_rope_write(kv, meta, k_norm_weights, cos_sin, positions, locs, num_l
                        is_neox_style=False, commit_lens=None, locs_row_width=None) -> None:
     """The bf16-pool writer with the arguments of the fused writer that
     sglang/model.py:746-766 calls (FlashMap rotates interleaved pairs, so
-    ``is_neox_style`` must be False)."""
+    ``is_neox_style`` must be False).  That writer is sglang's own kernel and
+    is not in the reference; the keys here take the HF path's k_norm rounding
+    (modeling_flashmap.py:76-80), so pool keys equal the HF cache's."""
     if is_neox_style:
         raise OpArgumentError("FlashMap rotates interleaved pairs: is_neox_style must be False")
     _pool_write(kv, meta, k_norm_weights, cos_sin, positions, locs, num_layers, kv_size, head_dim, eps, False,

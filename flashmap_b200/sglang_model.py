@@ -1,0 +1,320 @@
+"""The sglang (DSPARK) draft-model entry point (flashmap/sglang/model.py) on
+this library.
+
+``FlashMapDraftModel`` is the HF-path model (its modules and weights, loaded
+from a release folder as they are) with sglang's draft protocol: the
+constructor ``(config, quant_config=None, prefix="")``, ``load_weights``,
+``attach_shared_modules``, ``prepare``, ``head_logits``, ``forward_embed``,
+``compute_base_logits``, ``write_target_hidden_kv`` and ``forward``, and the
+attributes DSPARK reads (``flashmap``, ``sample_from_anchor``,
+``markov_head``, ``gamma``, ``lm_head``, ``hot_ids``, ``folded_head``).  The
+draft step runs on the library's kernels (``paged_draft``): the pool writer,
+block self-attention, q-norm + RoPE and page-size-1 cross-attention of
+``serving_ops``.
+
+sglang is not imported: the KV pool, the request-to-token table and the
+forward batch are read by attribute, through the hooks ``token_to_kv_pool``
+and ``req_to_token`` (callables; by default sglang's own getters), so the
+model runs inside sglang or against stand-ins.
+
+Differences from the reference plugin: the draft is the HF path's unfolded
+arithmetic (``paged_draft``: no folded head or folded noise, so
+``folded_head`` stays None and ``head_logits`` applies the DiT head and the
+LM head in turn); one jump per block; no tree drafting or FP8 weights; the
+``FLASHMAP_COMPILE`` settings are accepted and have no effect.
+"""
+
+from __future__ import annotations
+
+import logging
+import os
+from dataclasses import dataclass
+from typing import Callable, Iterable, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from . import serving_ops as S
+from .modeling_flashmap import FlashMapDraftModel as FlashMapDiT
+from .paged_draft import PagedDraft, unsupported_steps
+
+logger = logging.getLogger(__name__)
+
+__all__ = ["FlashMapDraftModel", "IdentityMarkov", "LogitsProcessorOutput", "EntryClass"]
+
+
+@dataclass
+class LogitsProcessorOutput:
+    """The fields of sglang's ``LogitsProcessorOutput`` the draft step fills."""
+
+    next_token_logits: Optional[torch.Tensor]
+    hidden_states: Optional[torch.Tensor]
+
+
+class IdentityMarkov(nn.Module):
+    """DSPARK's Markov head slot: FlashMap drafts every position at once and
+    keeps none (sglang/sampler.py's ``IdentityMarkov``)."""
+
+    def __init__(self, vocab_size: int):
+        super().__init__()
+        self.vocab_size = int(vocab_size)
+        self.hot_ids = None
+
+
+class _Head(nn.Module):
+    """What DSPARK reads as the draft's head: rows over the draft vocabulary
+    and the full vocabulary size its sampling buffers take."""
+
+    def __init__(self, weight: torch.Tensor, bias, vocab_size: int):
+        super().__init__()
+        self.register_buffer("weight", weight, persistent=False)
+        self.register_buffer("bias", bias, persistent=False)
+        self.org_vocab_size = int(vocab_size)
+
+
+def _default_pool():
+    from sglang.srt.model_executor.forward_context import get_token_to_kv_pool
+
+    return get_token_to_kv_pool()
+
+
+def _default_req_to_token():
+    from sglang.srt.model_executor.forward_context import get_req_to_token_pool
+
+    return get_req_to_token_pool().req_to_token
+
+
+class FlashMapDraftModel(FlashMapDiT):
+    flashmap = True
+    uses_own_vocab_modules = False
+    supports_pre_gather_target_hidden_projection = False
+
+    def __init__(self, config, quant_config=None, prefix: str = "") -> None:
+        del quant_config, prefix
+        if getattr(config, "flow_map", True) is False:
+            raise ValueError("this checkpoint is a stage-1 flow (flow_map: false), which drafts only by integrating "
+                             "over many steps; serve the flow map instead")
+        super().__init__(config)
+        fm = self.config
+        self.block_size = int(fm.block_size)
+        self.vocab_size = fm.vocab_size
+        self.target_hidden_size = fm.target_hidden_size
+        self.dim = fm.hidden_size
+        self.num_heads = fm.num_attention_heads
+        self.gamma = self.block_size
+        self.num_stages = fm.num_hidden_layers
+        self.rope_theta = fm.rope_theta
+        self.rms_norm_eps = fm.rms_norm_eps
+        self.qk_norm_eps = fm.qk_norm_eps
+        self.layer_norm_eps = fm.layer_norm_eps
+        self.sample_from_anchor = True
+        self.markov_head = IdentityMarkov(self.vocab_size)
+        self.confidence_head = None
+        self.logits_mup_width_multiplier = None
+        self.lm_head = None
+        self.embedding = None
+        self.hot_ids = None
+        self.folded_head = None
+        self.num_steps = int(os.environ.get("FLASHMAP_NUM_STEPS") or fm.num_steps)
+        why = unsupported_steps(self.num_steps)
+        if why:
+            raise ValueError(why)
+        size = os.environ.get("FLASHMAP_DRAFT_VOCAB")
+        size = int(size if size is not None else getattr(config, "draft_vocab_size", 0) or 0)
+        self.state_vocab_size = getattr(fm, "state_vocab_size", None)
+        size = self.state_vocab_size or size
+        self.draft_vocab_size = size if 0 < size < self.vocab_size else 0
+        self._vocab_ranking = None
+        self.noise_temperature = 1.0
+        self._core: Optional[PagedDraft] = None
+        self._fused_write = None
+        self._kv_fp8 = False
+        self._noise_offset = 0
+        self.token_to_kv_pool: Callable = _default_pool
+        self.req_to_token: Callable = _default_req_to_token
+
+    # --- loading -----------------------------------------------------------
+    def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
+        """The folder's weights; ``draft_vocab.safetensors``'s ``ids`` rank the
+        token ids, most frequent first (sglang/model.py:344-403)."""
+        params = {**dict(self.named_parameters()), **dict(self.named_buffers())}
+        loaded = set()
+        for name, tensor in weights:
+            if name in ("ids", "draft_vocab_ids"):
+                self._vocab_ranking = tensor
+                continue
+            if name == "counts":
+                continue
+            if name not in params:
+                raise KeyError(f"unexpected FlashMap weight {name!r}")
+            with torch.no_grad():
+                params[name].copy_(tensor.to(params[name].dtype))
+            loaded.add(name)
+        missing = sorted(n for n in params if n not in loaded and not n.startswith(("markov_head.", "lm_head.")))
+        if missing:
+            raise KeyError(f"FlashMap weights missing from the checkpoint: {missing}")
+        self._clear_caches()
+
+    def attach_shared_modules(self, *, embed_tokens: nn.Module, lm_head: nn.Module):
+        """The target's embedding and LM head (sglang/model.py:405-425)."""
+        if self.logits_mup_width_multiplier:
+            raise NotImplementedError("FlashMap does not support muP-scaled targets")
+        embedding = embed_tokens.weight.detach()
+        head = getattr(lm_head, "weight", None)
+        head = embedding if head is None else head.detach()
+        for name, weight in (("embedding", embedding), ("LM head", head)):
+            if weight.shape != (self.vocab_size, self.target_hidden_size):
+                raise ValueError(f"the target's {name} is {tuple(weight.shape)}, the draft expects "
+                                 f"({self.vocab_size}, {self.target_hidden_size}); padded or sharded vocabularies "
+                                 "are not supported")
+        self.embedding = embedding
+        self.prepare(head)
+
+    @torch.no_grad()
+    def prepare(self, lm_head_weight: torch.Tensor) -> None:
+        """The draft vocabulary, kernel-layout weights and the jump's constants
+        (sglang/model.py:427-473)."""
+        state_vocab = bool(self.state_vocab_size and self.draft_vocab_size)
+        device = self.embedding.device
+        if state_vocab:
+            self.hot_ids = self.draft_ids.to(device)
+        elif self.draft_vocab_size and self._vocab_ranking is None:
+            logger.warning("FlashMap: no draft_vocab.safetensors next to the weights; drafting over the full "
+                           "vocabulary")
+            self.draft_vocab_size = 0
+        elif self.draft_vocab_size:
+            ranking = self._vocab_ranking[: self.draft_vocab_size].to(device=device, dtype=torch.int64)
+            self.hot_ids = ranking.sort().values
+        self._core = core = PagedDraft(self, device)
+        core.attach(self.embedding, lm_head_weight)
+        if self.hot_ids is not None and not state_vocab:
+            core.pack.lm_w = core.pack.lm_w[self.hot_ids].contiguous()
+        self.lm_head = _Head(core.pack.lm_w, core.pack.lm_b, self.vocab_size)
+        self.markov_head.hot_ids = self.hot_ids
+        (self._s, self._t, _), = core.jump(self.num_steps)
+        self._mods = core.modulations(self._s, self._t)
+
+    def _require_core(self) -> PagedDraft:
+        if self._core is None:
+            raise RuntimeError("attach_shared_modules() / prepare() has not run")
+        return self._core
+
+    def head_logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """The draft-vocabulary logits of the DiT's output: the DiT head, then
+        the target's LM head rows."""
+        return self._require_core().draft_logits(hidden.reshape(-1, self.dim))
+
+    # --- DSPARK protocol ------------------------------------------------------
+    def forward_embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        return F.embedding(input_ids, self.embedding)
+
+    def prune_to_ctx_kv_injection(self) -> None:
+        pass
+
+    def compute_base_logits(self, hidden: torch.Tensor):
+        return self.head_logits(hidden), None
+
+    def _write_args(self, pool):
+        """The pool's per-layer (key, value, strides) table, the stacked k-norm
+        weights and the rotary table (sglang/model.py:768-820)."""
+        if self._fused_write is not None and self._fused_write[0] == id(pool):
+            return self._fused_write[1]
+        buffers = [(pool.get_key_buffer(i), pool.get_value_buffer(i)) for i in range(self.num_stages)]
+        hd = self.dim // self.num_heads
+        for buf in (b for pair in buffers for b in pair):
+            if not buf.is_cuda or buf.dtype not in (torch.bfloat16, torch.float8_e4m3fn):
+                raise ValueError(f"the FlashMap draft KV pool must be bf16 or fp8_e4m3 on CUDA, got {buf.dtype} "
+                                 "(--speculative-draft-kv-cache-dtype)")
+            assert buf.shape[1:] == (self.num_heads, hd), buf.shape
+            assert buf.stride(1) == hd and buf.stride(2) == 1
+        self._kv_fp8 = buffers[0][0].dtype == torch.float8_e4m3fn
+        core = self._require_core()
+        device = core.pack.device
+        meta = torch.tensor([[k.data_ptr(), v.data_ptr(), k.stride(0), v.stride(0)] for k, v in buffers],
+                            dtype=torch.int64, device=device)
+        k_norm = core.pack.cross_k_norm
+        rows = max(int(buffers[0][0].shape[0]), int(getattr(self.config, "max_position_embeddings", 0) or 0))
+        pairs = core.rope_pairs(rows + self.block_size + 1)
+        cos_sin = torch.cat([pairs[..., 0], pairs[..., 1]], dim=-1).contiguous()
+        args = (meta, k_norm, cos_sin, self.num_heads * hd, buffers)
+        self._fused_write = (id(pool), args)
+        return args
+
+    def _kv_write(self, kv, args, positions, locs, **commit) -> None:
+        meta, k_norm, cos_sin, kv_size, _ = args
+        hd = self.dim // self.num_heads
+        write = S.kv_norm_rope_write_fp8 if self._kv_fp8 else S.kv_norm_rope_write
+        write(kv, meta, k_norm, cos_sin, positions, locs, self.num_stages, kv_size, hd, self.qk_norm_eps, **commit)
+
+    @torch.no_grad()
+    def write_target_hidden_kv(self, *, target_hidden: torch.Tensor, pool, positions: torch.Tensor,
+                               cache_loc: torch.Tensor, cache_loc_2d: Optional[torch.Tensor] = None,
+                               commit_lens: Optional[torch.Tensor] = None,
+                               target_hidden_is_projected: bool = False) -> None:
+        """Every layer's context keys/values of the target's features at the
+        pool rows ``cache_loc`` (verify windows: only the committed columns of
+        ``cache_loc_2d``) (sglang/model.py:687-733)."""
+        assert not target_hidden_is_projected
+        if target_hidden.shape[0] == 0:
+            return
+        core = self._require_core()
+        args = self._write_args(pool)
+        kv = core.context_kv(core.combine(target_hidden))
+        if cache_loc_2d is not None and commit_lens is not None:
+            self._kv_write(kv, args, positions, cache_loc_2d.reshape(-1), commit_lens=commit_lens,
+                           locs_row_width=cache_loc_2d.shape[1])
+            return
+        self._kv_write(kv, args, positions, cache_loc)
+
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, forward_batch,
+                input_embeds: Optional[torch.Tensor] = None, get_embedding: bool = False,
+                pp_proxy_tensors=None) -> LogitsProcessorOutput:
+        """A block for every request; returns the DiT's final hidden states
+        (``compute_base_logits`` maps them to logits), the first ``gamma`` of
+        each block (sglang/model.py:822-895)."""
+        del input_embeds, get_embedding, pp_proxy_tensors
+        core = self._require_core()
+        bsz, K = forward_batch.batch_size, self.block_size
+        gamma = positions.numel() // bsz
+        assert gamma <= K, f"--speculative-dspark-block-size {gamma} exceeds the map's block of {K} drafts"
+        pool = self.token_to_kv_pool()
+        args = self._write_args(pool)
+        anchor_positions = positions.view(bsz, gamma)[:, 0]
+        block_positions = anchor_positions[:, None] + torch.arange(K, device=positions.device)
+        self._kv_write(core.anchor_kv(input_ids.view(bsz, gamma)[:, 0]), args, anchor_positions,
+                       forward_batch.out_cache_loc.view(bsz, gamma)[:, 0])
+        page_table = self.req_to_token()[forward_batch.req_pool_indices].to(torch.int32)
+        cache_seqlens = (forward_batch.seq_lens + 1).to(torch.int32)
+        freqs = S.rope_freqs(block_positions + 1, core.hd, self.rope_theta).contiguous()
+        keys = [b[0] for b in args[4]]
+        values = [b[1] for b in args[4]]
+        p = core.pack
+        T = bsz * K
+        self._noise_offset += 1
+        z = core.noise(T, scale=self.noise_temperature, seed=int(torch.initial_seed()) & (2**63 - 1),
+                       offset=self._noise_offset)
+        x = core.first_hidden(z, self._s, self._t)
+        cross = S.sglang_paged_cross_attention_fp8 if self._kv_fp8 else S.sglang_paged_cross_attention
+
+        def self_attention(qkv, layer):
+            w = p.layers[layer]
+            return S.sglang_block_self_attention(qkv.view(bsz, K, 3, core.H, core.hd), w["self_q_norm"],
+                                                 w["self_k_norm"], freqs, self.qk_norm_eps)
+
+        def rotate(q, layer):
+            return S.sglang_rms_norm_rope(q.view(bsz, K, core.H, core.hd), p.layers[layer]["cross_q_norm"], freqs,
+                                          self.qk_norm_eps)
+
+        def attend(query, layer):
+            return cross(query.view(bsz, K, core.H, core.hd), keys[layer], values[layer], cache_seqlens, page_table,
+                         cache_seqlens)
+
+        hidden = core.dit(x, self._mods, self_attention, rotate, attend)
+        if gamma < K:
+            hidden = hidden.view(bsz, K, -1)[:, :gamma].reshape(bsz * gamma, -1)
+        return LogitsProcessorOutput(next_token_logits=None, hidden_states=hidden)
+
+
+EntryClass = [FlashMapDraftModel]

@@ -256,7 +256,8 @@ FM_API fm_status fm_write_context_kv_paged(const void* kv, int64_t tokens, int64
 /* sglang's context writer: kv (tokens, layers, 2, kv_size) bf16 with kv_size =
  * heads * head_dim; per layer meta (layers, 4) int64 = (key pool pointer, value
  * pool pointer, key row stride, value row stride) in elements; keys
- * k-normed (FM_NORM_FUSED) and rotated at positions[t], written with values
+ * k-normed (norm_mode: FM_NORM_FUSED is the reference's e4m3 writer,
+ * FM_NORM_DIT the HF path's k_norm) and rotated at positions[t], written with values
  * at pool row locs[t] (negative: skipped).  With commit_lens (rows of
  * locs_row_width tokens), token t is written only when t % locs_row_width <
  * commit_lens[t / locs_row_width].  pool_dtype FM_DT_E4M3 divides keys by
@@ -266,8 +267,8 @@ FM_API fm_status fm_kv_norm_rope_write_pool(const void* kv, int64_t tokens, int6
                                             int64_t head_dim, const int64_t* meta, const void* k_norm,
                                             int32_t k_norm_dtype, fm_rope_view rope, const int64_t* positions,
                                             const int64_t* locs, const int32_t* commit_lens, int64_t locs_row_width,
-                                            int32_t pool_dtype, float k_scale, float v_scale, float eps,
-                                            int32_t* err, fm_stream stream);
+                                            int32_t pool_dtype, int32_t norm_mode, float k_scale, float v_scale,
+                                            float eps, int32_t* err, fm_stream stream);
 
 /* ------------------------------------------------------------------------
  * Sampling and acceptance (modeling_flashmap.py:553-557, :579-594).

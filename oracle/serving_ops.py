@@ -160,8 +160,9 @@ def write_context_kv(kv, positions, slots, k_norm, cos_sin, caches, strides, blo
 def kv_norm_rope_write_pool(kv, k_pools, v_pools, k_norm, cos_sin, positions, locs, L, kv_size, hd, eps, fp8,
                             k_scale=1.0, v_scale=1.0, commit_lens=None, row_width=1):
     """sglang/kernels.py:269-316: kv (tokens, L * 2 * kv_size); keys k-normed
-    (fused rounding), rotated with the ``(positions, [cos | sin])`` table;
-    bf16, or e4m3 of key / k_scale and value / v_scale; pools (rows, kv_size)."""
+    (the e4m3 writer's fused rounding; a bf16 pool takes the HF path's k_norm,
+    modeling_flashmap.py:76-80), rotated with the ``(positions, [cos | sin])``
+    table; bf16, or e4m3 of key / k_scale and value / v_scale; pools (rows, kv_size)."""
     half = hd // 2
     for t in range(kv.shape[0]):
         if commit_lens is not None and t % row_width >= int(commit_lens[t // row_width]):
@@ -174,7 +175,7 @@ def kv_norm_rope_write_pool(kv, k_pools, v_pools, k_norm, cos_sin, positions, lo
         row = kv[t].view(L, 2, kv_size)
         for layer in range(L):
             for h in range(kv_size // hd):
-                key = norm_rope(row[layer, 0, h * hd:(h + 1) * hd], k_norm[layer], cos, sin, eps, fused=True)
+                key = norm_rope(row[layer, 0, h * hd:(h + 1) * hd], k_norm[layer], cos, sin, eps, fused=fp8)
                 val = row[layer, 1, h * hd:(h + 1) * hd].float()
                 if fp8:
                     k_pools[layer][loc, h * hd:(h + 1) * hd] = (key / k_scale).to(FP8)

@@ -2,9 +2,10 @@
 kernels of serving.cu) against the CPU restatement in oracle/serving_ops.py.
 
 Tolerances, written per check:
-* norms and RoPE: bf16 outputs within 2 bf16 ulps plus 1e-3 of the row scale
-  (the fp32 sums run in a different order; the bf16 scale may round the other
-  way), and at least 97% of the elements bit-equal;
+* norms and RoPE: bf16 outputs within 2 bf16 ulps plus 8e-3 of the row's
+  largest value, and at least 97% of the elements bit-equal (the fp32 sums run
+  in a different order, so the bf16-rounded scale of a row may land one bf16
+  step, 2^-8 relative, away; the rotation mixes two such values);
 * attention: |got - ref| <= 2e-2 * max|ref| (bf16 inputs and outputs, fp32
   softmax, bf16 numerators as in FlashAttention) and a mean error below 2e-3;
 * cache writers: values copied bit-exactly; keys like the norms; e4m3 bytes
@@ -45,7 +46,7 @@ def assert_rows_close(got, ref, what, min_exact=0.97):
     g, r = got.float().cpu(), ref.float().cpu()
     assert g.shape == r.shape, what
     assert torch.isfinite(g).all(), what
-    tol = 2 * _ulp(r) + 1e-3 * r.abs().amax(dim=-1, keepdim=True)
+    tol = 2 * _ulp(r) + 8e-3 * r.abs().amax(dim=-1, keepdim=True)
     bad = (g - r).abs() > tol
     assert not bad.any(), f"{what}: {int(bad.sum())} elements off, max diff {float((g - r).abs().max()):.4g}"
     exact = (g == r).float().mean().item()
