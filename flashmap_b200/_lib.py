@@ -101,6 +101,9 @@ _SIGNATURES = {
     "fm_gemm_workspace_size": (c_size_t, [c_int64, c_int64, c_int64]),
     "fm_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                              c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
+    "fm_gemm_grid": (c_int32, [c_int64, c_int64, c_int64]),
+    "fm_gemm_bf16_trace": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                   c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "fm_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "fm_adaln": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "fm_rope_table": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),

@@ -7,7 +7,7 @@ namespace fm {
 
 namespace {
 
-using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs);
+using GemmKernel = void (*)(const CUtensorMap, const CUtensorMap, const GemmArgs, unsigned long long*);
 
 template <int BN>
 struct BnTable {
@@ -58,30 +58,47 @@ bool ensure_smem_attr(GemmKernel k, size_t smem) {
 
 }  // namespace
 
+// FM_GEMM_BN_MAX (tuning experiments) caps the block width.
 int gemm_bn_for(int64_t N) {
-  if (N <= 16) return 16;
-  if (N <= 32) return 32;
-  if (N <= 64) return 64;
-  if (N <= 128) return 128;
-  return 256;
+  static const int cap = [] {
+    const char* e = getenv("FM_GEMM_BN_MAX");
+    const int v = e ? atoi(e) : 256;
+    return (v == 64 || v == 128 || v == 256) ? v : 256;
+  }();
+  int bn = N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : N <= 128 ? 128 : 256;
+  return bn > cap && cap >= 64 && N > 64 ? cap : bn;
 }
 
 // CTAs of a launch: one per SM by default.  FM_GEMM_CTAS_PER_SM (tuning
-// experiments) scales it; the result never exceeds the unit count.
-static int64_t gemm_grid_for(int64_t units) {
+// experiments) scales it; the result never exceeds the unit count.  Wide
+// blocks (BN >= 64, finished by their head CTA from staged partials) are
+// split over at most 2 CTAs per tile when that still occupies half the SMs
+// (each head then stages one partial), else over at most 8
+// (FM_GEMM_MAX_SPLIT overrides the cap for tuning experiments).
+static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn) {
   static const int per_sm = [] {
     const char* e = getenv("FM_GEMM_CTAS_PER_SM");
     const int v = e ? atoi(e) : 1;
     return v >= 1 && v <= 4 ? v : 1;
   }();
-  const int64_t g = (int64_t)num_sms() * per_sm;
+  static const int split_env = [] {
+    const char* e = getenv("FM_GEMM_MAX_SPLIT");
+    const int v = e ? atoi(e) : 0;
+    return v >= 1 && v <= 8 ? v : 0;
+  }();
+  int64_t g = (int64_t)num_sms() * per_sm;
+  if (bn >= 64) {
+    const int64_t max_split = split_env ? split_env : (tiles * 2 >= num_sms() / 2 ? 2 : 8);
+    if (g > tiles * max_split) g = tiles * max_split;
+  }
   return units < g ? units : g;
 }
 
 size_t gemm_partials_bytes(int64_t M, int64_t N, int64_t K) {
   const int bn = gemm_bn_for(N);
-  const int64_t units = ((M + 127) / 128) * ((N + bn - 1) / bn) * ((K + 63) / 64);
-  return (size_t)gemm_grid_for(units) * 2 * bn * 128 * sizeof(float);
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int64_t units = tiles * ((K + 63) / 64);
+  return (size_t)gemm_grid_for(units, tiles, bn) * 2 * bn * 128 * sizeof(float);
 }
 
 fm_status gemm_prepare(GemmPlan* p, const void* W, int64_t M, int64_t K, int64_t ldw, const void* X, int64_t N,
@@ -111,7 +128,7 @@ fm_status gemm_prepare(GemmPlan* p, const void* W, int64_t M, int64_t K, int64_t
   a.err = err;
   p->bn = bn;
   p->epi = epi;
-  p->grid = (int)gemm_grid_for(a.units);
+  p->grid = (int)gemm_grid_for(a.units, (int64_t)a.m_tiles * a.n_tiles, bn);
   size_t smem = 0;
   if (!kernel_for(bn, epi, &smem)) return set_error(FM_ERR_UNSUPPORTED, "gemm: no kernel for epilogue %d", epi);
   p->smem = smem;
@@ -126,7 +143,7 @@ fm_status gemm_launch(const GemmPlan& p, cudaStream_t stream, bool pdl) {
   if (split_possible && (!p.args.ws || !p.args.counters))
     return set_error(FM_ERR_WORKSPACE, "gemm: split-K workspace missing");
   if (!ensure_smem_attr(k, smem)) return set_error(FM_ERR_CUDA, "gemm: cannot set shared memory size");
-  return launch_kernel(k, dim3(p.grid), dim3(192), smem, stream, pdl, p.tmA, p.tmB, p.args);
+  return launch_kernel(k, dim3(p.grid), dim3(192), smem, stream, pdl, p.tmA, p.tmB, p.args, p.trace);
 }
 
 }  // namespace fm
@@ -139,9 +156,9 @@ extern "C" size_t fm_gemm_workspace_size(int64_t M, int64_t N, int64_t K) {
   return 256 + ((tiles * sizeof(int) + 255) / 256) * 256 + gemm_partials_bytes(M, N, K);
 }
 
-extern "C" fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
-                                  int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
-                                  size_t workspace_bytes, int32_t* err, fm_stream stream) {
+static fm_status gemm_bf16_call(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
+                                int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
+                                size_t workspace_bytes, int32_t* err, uint64_t* trace, fm_stream stream) {
   if (!out) return set_error(FM_ERR_INVALID, "gemm: null output");
   if (epilogue != EPI_STORE && epilogue != EPI_GELU && epilogue != EPI_SWIGLU && epilogue != EPI_RESID &&
       epilogue != EPI_F32)
@@ -165,5 +182,28 @@ extern "C" fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64
   p.args.ldo = ldo;
   p.args.bias = static_cast<const __nv_bfloat16*>(bias);
   p.args.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.trace = reinterpret_cast<unsigned long long*>(trace);
   return gemm_launch(p, static_cast<cudaStream_t>(stream), false);
+}
+
+extern "C" fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
+                                  int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
+                                  size_t workspace_bytes, int32_t* err, fm_stream stream) {
+  return gemm_bf16_call(W, X, out, M, N, K, ldo, bias, gate, epilogue, workspace, workspace_bytes, err, nullptr,
+                        stream);
+}
+
+extern "C" int32_t fm_gemm_grid(int64_t M, int64_t N, int64_t K) {
+  const int bn = gemm_bn_for(N);
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  return (int32_t)gemm_grid_for(tiles * ((K + 63) / 64), tiles, bn);
+}
+
+extern "C" fm_status fm_gemm_bf16_trace(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
+                                        int64_t ldo, const void* bias, const void* gate, int epilogue,
+                                        void* workspace, size_t workspace_bytes, int32_t* err, uint64_t* trace,
+                                        fm_stream stream) {
+  if (!trace) return set_error(FM_ERR_INVALID, "gemm trace: null trace buffer");
+  return gemm_bf16_call(W, X, out, M, N, K, ldo, bias, gate, epilogue, workspace, workspace_bytes, err, trace,
+                        stream);
 }

@@ -70,6 +70,14 @@ struct GemmArgs {
   int* err;
 };
 
+// Trace slots per CTA: 0 entry, 1 setup done, then per segment s < 3:
+// 2+4s MMA issue done, 3+4s accumulator seen by the epilogue, 4+4s partial
+// written / epilogue done, 5+4s split fix-up done; 14 exit.
+constexpr int GEMM_TRACE = 16;
+__device__ __forceinline__ void gemm_stamp(unsigned long long* trace, int slot) {
+  if (trace) trace[(long long)blockIdx.x * GEMM_TRACE + slot] = global_ns();
+}
+
 template <int BN>
 struct GemmShape {
   static constexpr int A_BYTES = 128 * 64 * 2;
@@ -78,7 +86,11 @@ struct GemmShape {
   static constexpr int ACC = 2;
   static constexpr uint32_t TMEM_COLS =
       ACC * BN <= 32 ? 32 : ACC * BN <= 64 ? 64 : ACC * BN <= 128 ? 128 : ACC * BN <= 256 ? 256 : 512;
-  static constexpr int SCRATCH = 4096 + 1024;  // epilogue exchange (union) + split flags
+  // epilogue exchange (union) + split flags, then for wide blocks a ring of
+  // residual chunks ([16 tokens][128 features] bf16) loaded ahead
+  static constexpr int RING = 4;
+  static constexpr int RING_BYTES = BN >= 64 ? RING * 4096 : 0;
+  static constexpr int SCRATCH = 4096 + 1024 + RING_BYTES;
   static constexpr int BAR_BYTES = 256;
   static constexpr int SMEM = 1024 /*alignment slack*/ + STAGES * (A_BYTES + B_BYTES) + BAR_BYTES + SCRATCH;
 };
@@ -86,6 +98,27 @@ struct GemmShape {
 __device__ __forceinline__ long long cta_of_unit(long long u, long long U, int G) {
   return ((u + 1) * (long long)G - 1) / U;
 }
+
+__device__ __forceinline__ int gemm_ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void gemm_red_release(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Split tiles of wide blocks (BN >= 64) are finished by their head CTA (the
+// one holding the tile's first k-block; the split segment is always its last
+// segment, so its pipeline shared memory is idle by then): it waits (bounded)
+// until the other contributors have published their fp32 partials, stages
+// them into the idle pipeline buffers with bulk copies, and sums them with its
+// own accumulator in contributor order.  Narrow blocks keep the last-arriver
+// fix-up (their partials are a few KB).
+template <int BN>
+struct OwnerFixup {
+  static constexpr bool ON = BN >= 64;
+};
 
 // ---------------------------------------------------------------------------------------------
 // Epilogue on 16 accumulator columns (tokens n0 .. n0+15) of tile row r (feature m).
@@ -120,6 +153,135 @@ __device__ __forceinline__ bool epilogue_prefetch(const GemmArgs& a, int m, int 
   } else {
     return false;
   }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Wide blocks (BN >= 64) with the STORE / GELU / RESID epilogues run each
+// 128 x 16 chunk through shared memory ([16 tokens][128 features] bf16, the
+// 4 KB exchange area): the output (token-major) is then read and written as
+// 16-byte vectors along the features, two per thread, instead of sixteen
+// 2-byte accesses per thread.  Same arithmetic as epilogue16.
+template <int BN, int EPI>
+struct VecEpilogue {
+  static constexpr bool ON = BN >= 64 && (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID);
+};
+
+__device__ __forceinline__ bool vec_epilogue_ok(const GemmArgs& a) {
+  return a.M % 8 == 0 && a.ldo % 8 == 0 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0;
+}
+
+__device__ __forceinline__ void gemm_cp_async16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16u : 0u)
+               : "memory");
+}
+__device__ __forceinline__ void gemm_cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void gemm_cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Residual chunk (tokens n0 .. n0+15, features m0 .. m0+127) into a ring slot
+// [16][128] with asynchronous 16-byte copies (zero-filled outside the output);
+// one commit group per chunk, issued (or empty) by every epilogue thread.
+__device__ __forceinline__ void vec_issue(const GemmArgs& a, int m0, int n0, __nv_bfloat16* slot, bool any) {
+  if (any) {
+    const int t = threadIdx.x - 64;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+      const int n = n0 + nl, m = m0 + gi * 8;
+      const bool ok = n < a.N && m < a.M;
+      gemm_cp_async16(slot + nl * 128 + gi * 8, ok ? (const void*)(a.out + (long long)n * a.ldo + m) : (const void*)a.out,
+                      ok);
+    }
+  }
+  gemm_cp_commit();
+}
+
+// The residual epilogue of a chunk whose residuals sit in `slot` (landed and
+// visible): out = bf16(x + bf16(gate * bf16(acc + bias))) computed in place,
+// then written back as vectors.
+__device__ __forceinline__ void vec_resid16(const GemmArgs& a, const float* v, int r, int m0, int n0,
+                                            __nv_bfloat16* slot) {
+  const int m = m0 + r;
+  const bool mvalid = m < a.M;
+  const float b = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
+  const float g = mvalid ? bf2f(a.gate[m]) : 0.0f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float y = round_bf(__fadd_rn(v[j], b));
+    const float gy = round_bf(__fmul_rn(g, y));
+    slot[j * 128 + r] = f2bf(__fadd_rn(bf2f(slot[j * 128 + r]), gy));
+  }
+  named_bar_sync(1, 128);
+  const int t = threadIdx.x - 64;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+    const int n = n0 + nl, mm = m0 + gi * 8;
+    if (n < a.N && mm < a.M)
+      *reinterpret_cast<uint4*>(a.out + (long long)n * a.ldo + mm) =
+          *reinterpret_cast<const uint4*>(slot + nl * 128 + gi * 8);
+  }
+  named_bar_sync(1, 128);  // the slot is refilled RING - 1 chunks later
+}
+
+// residual vectors of the chunk (tokens n0 .. n0+15, features m0 .. m0+127)
+template <int EPI>
+__device__ __forceinline__ void vec_prefetch(const GemmArgs& a, int m0, int n0, uint4* pre) {
+  if constexpr (EPI == EPI_RESID) {
+    const int t = threadIdx.x - 64;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+      const int n = n0 + nl, m = m0 + gi * 8;
+      pre[k] = (n < a.N && m < a.M) ? *reinterpret_cast<const uint4*>(a.out + (long long)n * a.ldo + m)
+                                    : make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+template <int EPI>
+__device__ __forceinline__ void vec_epilogue16(const GemmArgs& a, const float* v, int r, int m0, int n0,
+                                               __nv_bfloat16* xt, const uint4* pre) {
+  const int m = m0 + r;
+  const bool mvalid = m < a.M;
+  const float b = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
+  const float g = (EPI == EPI_RESID && mvalid) ? bf2f(a.gate[m]) : 0.0f;
+  const int t = threadIdx.x - 64;
+  if constexpr (EPI == EPI_RESID) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+      *reinterpret_cast<uint4*>(xt + nl * 128 + gi * 8) = pre[k];
+    }
+    named_bar_sync(1, 128);
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float y = round_bf(__fadd_rn(v[j], b));
+    __nv_bfloat16 o;
+    if constexpr (EPI == EPI_GELU) {
+      y = __fmul_rn(__fmul_rn(y, 0.5f), __fadd_rn(1.0f, erff(__fmul_rn(y, 0.70710678118654752f))));
+      o = f2bf(y);
+    } else if constexpr (EPI == EPI_RESID) {
+      const float gy = round_bf(__fmul_rn(g, y));
+      o = f2bf(__fadd_rn(bf2f(xt[j * 128 + r]), gy));
+    } else {
+      o = f2bf(y);
+    }
+    xt[j * 128 + r] = o;
+  }
+  named_bar_sync(1, 128);
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+    const int n = n0 + nl, mm = m0 + gi * 8;
+    if (n < a.N && mm < a.M)
+      *reinterpret_cast<uint4*>(a.out + (long long)n * a.ldo + mm) = *reinterpret_cast<const uint4*>(xt + nl * 128 + gi * 8);
+  }
+  named_bar_sync(1, 128);  // the exchange tile is refilled by the next chunk
 }
 
 template <int EPI>
@@ -330,7 +492,7 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const GemmArgs a) {
+                 const GemmArgs a, unsigned long long* trace) {
   using S = GemmShape<BN>;
   constexpr int STAGES = S::STAGES;
   constexpr int ACC = S::ACC;
@@ -344,6 +506,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* acc_empty = acc_full + ACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + ACC);
   int* flags = reinterpret_cast<int*>(tmem_slot + 2);  // [0] abort, [1] last-arriver, [2..3] segment ok
+  uint64_t* fix_bar = reinterpret_cast<uint64_t*>(flags + 6);  // staged-partials barrier (8-byte aligned)
   uint8_t* scratch = smem + STAGES * (S::A_BYTES + S::B_BYTES) + S::BAR_BYTES;
   float* xch = reinterpret_cast<float*>(scratch);
   unsigned long long* xch64 = reinterpret_cast<unsigned long long*>(scratch);
@@ -354,6 +517,7 @@ __global__ void __launch_bounds__(192, 1)
   const int c = blockIdx.x;
   const long long u0 = (long long)c * U / G, u1 = (long long)(c + 1) * U / G;
   const int kb = a.kb;
+  if (threadIdx.x == 0) gemm_stamp(trace, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -368,6 +532,7 @@ __global__ void __launch_bounds__(192, 1)
     flags[1] = 0;
     flags[2] = 0;
     flags[3] = 0;
+    mbar_init(fix_bar, 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -380,6 +545,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) gemm_stamp(trace, 1);
   // every CTA now holds its TMEM: the next kernel may be scheduled
   pdl_launch_dependents();
   volatile int* abort_flag = flags;
@@ -463,6 +629,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         if (!ok) break;
         umma_commit(&acc_full[acc]);
+        if (seg < 3) gemm_stamp(trace, 2 + 4 * seg);
       }
     }
   } else {
@@ -489,13 +656,45 @@ __global__ void __launch_bounds__(192, 1)
       }
       named_bar_sync(1, 128);
       if (!flags[2 + (seg & 1)]) break;
+      if (threadIdx.x == 64 && seg < 3) gemm_stamp(trace, 3 + 4 * seg);
       tc_fence_after();
       const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
       const int m = mt * 128 + r;
       const int n0 = nt * BN;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       const bool whole = (seg_begin == (long long)tile * kb) && (seg_end == (long long)(tile + 1) * kb);
-      if (whole) {
+      const bool vec = VecEpilogue<BN, EPI>::ON && vec_epilogue_ok(a);
+      __nv_bfloat16* xt = reinterpret_cast<__nv_bfloat16*>(xch);
+      __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(scratch + 4096 + 1024);
+      if (whole && vec && EPI == EPI_RESID) {
+        constexpr int NCH = BN / 16, RG = S::RING;
+#pragma unroll
+        for (int pc = 0; pc < RG - 1; ++pc) vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % RG) * 2048, pc < NCH);
+        for (int ci = 0; ci < NCH; ++ci) {
+          float v[16];
+          tmem_ld_x16(taddr + ci * 16, v);
+          const int pc = ci + RG - 1;
+          vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % RG) * 2048, pc < NCH);
+          gemm_cp_wait<S::RING - 1>();
+          tmem_wait_ld();
+          named_bar_sync(1, 128);  // every thread's copies of chunk ci have landed
+          vec_resid16(a, v, r, mt * 128, n0 + ci * 16, ring + (ci % RG) * 2048);
+        }
+        gemm_cp_wait<0>();
+      } else if (whole && vec) {
+        uint4 vp[2];
+        vec_prefetch<EPI>(a, mt * 128, n0, vp);
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          uint4 vn[2];
+          tmem_ld_x16(taddr + c0, v);
+          if (c0 + 16 < BN) vec_prefetch<EPI>(a, mt * 128, n0 + c0 + 16, vn);
+          tmem_wait_ld();
+          vec_epilogue16<EPI>(a, v, r, mt * 128, n0 + c0, xt, vp);
+          vp[0] = vn[0];
+          vp[1] = vn[1];
+        }
+      } else if (whole) {
         // chunks of 16 columns; each chunk's global reads issued one chunk ahead
         float pre[32];
         bool have = epilogue_prefetch<EPI>(a, m, n0, pre);
@@ -508,6 +707,138 @@ __global__ void __launch_bounds__(192, 1)
           if (more) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
+          }
+        }
+      } else if (OwnerFixup<BN>::ON) {
+        const long long c_first = cta_of_unit((long long)tile * kb, U, G);
+        const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
+        if (c != c_first) {
+          // a later contributor: this tile is its first segment (partials slot 0)
+          float* mine = a.ws + ((long long)(c * 2) * BN) * 128;
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld_x16(taddr + c0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) __stcg(mine + (long long)(c0 + j) * 128 + r, v[j]);
+          }
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (threadIdx.x == 64) {
+            if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
+            gemm_red_release(a.counters + tile, 1);
+          }
+        } else {
+          // the head: wait for the others, stage their partials, finish the tile
+          const int others = (int)(c_last - c_first);
+          if (threadIdx.x == 64) {
+            bool ok = gemm_ld_acquire(a.counters + tile) >= others;
+            if (!ok) {
+              const uint64_t t0 = global_ns();
+              for (uint32_t i = 1;; ++i) {
+                if (gemm_ld_acquire(a.counters + tile) >= others) {
+                  ok = true;
+                  break;
+                }
+                if ((i & 63u) == 0 && (*abort_flag || global_ns() - t0 > FM_WAIT_NS)) break;
+                __nanosleep(64);
+              }
+            }
+            if (!ok) {
+              record_error(a.err, DEV_TIMEOUT_OTHER);
+              *abort_flag = 1;
+            } else {
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+            flags[1] = ok ? 1 : 0;
+            if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
+          }
+          named_bar_sync(1, 128);
+          if (flags[1]) {
+            // the pipeline buffers are idle: every k-block of this CTA was consumed
+            float* stage = reinterpret_cast<float*>(sA);
+            constexpr int AREA = STAGES * (S::A_BYTES + S::B_BYTES);
+            const int per_col = others * 128 * 4;
+            int cols = (AREA / per_col) / 16 * 16;
+            if (cols > BN) cols = BN;
+            if (cols < 16) {  // more contributors than the grid cap allows: never staged
+              if (threadIdx.x == 64) record_error(a.err, DEV_BAD_INDEX);
+              cols = BN + 1;
+            }
+            float pre[32];
+            bool have = !vec && epilogue_prefetch<EPI>(a, m, n0, pre);
+            uint4 vp[2];
+            constexpr bool RESID_RING = EPI == EPI_RESID && S::RING_BYTES > 0;
+            constexpr int NCH = BN / 16;
+            if (vec && !RESID_RING) vec_prefetch<EPI>(a, mt * 128, n0, vp);
+            if (vec && RESID_RING)
+#pragma unroll
+              for (int pc = 0; pc < S::RING - 1; ++pc)
+                vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
+            bool staged_ok = true;
+            for (int col0 = 0, round = 0; cols <= BN && col0 < BN; col0 += cols, ++round) {
+              const int ncols = (BN - col0) < cols ? (BN - col0) : cols;
+              if (threadIdx.x == 64) {
+                mbar_arrive_expect_tx(fix_bar, (uint32_t)(others * ncols * 512));
+                for (int o = 0; o < others; ++o)
+                  bulk_load(stage + (long long)o * ncols * 128,
+                            a.ws + ((long long)((c_first + 1 + o) * 2) * BN + col0) * 128, (uint32_t)(ncols * 512),
+                            fix_bar);
+                flags[1] = mbar_wait(fix_bar, (uint32_t)round & 1u, nullptr) ? 1 : 0;
+                if (!flags[1]) {
+                  record_error(a.err, DEV_TIMEOUT_OTHER);
+                  *abort_flag = 1;
+                }
+              }
+              named_bar_sync(1, 128);
+              if (!flags[1]) {
+                staged_ok = false;
+                break;
+              }
+              for (int c0 = col0; c0 < col0 + ncols; c0 += 16) {
+                float v[16], nxt[32];
+                uint4 vn[2];
+                tmem_ld_x16(taddr + c0, v);
+                const bool more =
+                    have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
+                const int ci = c0 / 16;
+                if (vec && !RESID_RING && c0 + 16 < BN) vec_prefetch<EPI>(a, mt * 128, n0 + c0 + 16, vn);
+                if (vec && RESID_RING) {
+                  const int pc = ci + S::RING - 1;
+                  vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
+                  gemm_cp_wait<S::RING - 1>();
+                }
+                tmem_wait_ld();
+                // contributor order: the head's own accumulator first, then the later CTAs
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(0.0f, v[j]);
+                for (int o = 0; o < others; ++o) {
+                  const float* src = stage + ((long long)o * ncols + (c0 - col0)) * 128 + r;
+#pragma unroll
+                  for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], src[j * 128]);
+                }
+                if (vec && RESID_RING) {
+                  named_bar_sync(1, 128);  // every thread's copies of chunk ci have landed
+                  vec_resid16(a, v, r, mt * 128, n0 + c0, ring + (ci % S::RING) * 2048);
+                } else if (vec) {
+                  vec_epilogue16<EPI>(a, v, r, mt * 128, n0 + c0, xt, vp);
+                  vp[0] = vn[0];
+                  vp[1] = vn[1];
+                } else {
+                  epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
+                }
+                if (more) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
+                }
+              }
+              named_bar_sync(1, 128);  // the staging area is refilled by the next round
+            }
+            if (vec && RESID_RING) gemm_cp_wait<0>();
+            if (threadIdx.x == 64) {
+              if (staged_ok) a.counters[tile] = 0;
+              if (seg < 3) gemm_stamp(trace, 5 + 4 * seg);
+            }
           }
         }
       } else {
@@ -525,6 +856,7 @@ __global__ void __launch_bounds__(192, 1)
         __threadfence();
         named_bar_sync(1, 128);
         if (threadIdx.x == 64) {
+          if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
           const int old = atomicAdd(a.counters + tile, 1);
           flags[1] = (old == (int)(c_last - c_first));
         }
@@ -571,7 +903,10 @@ __global__ void __launch_bounds__(192, 1)
               for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
             }
           }
-          if (threadIdx.x == 64) a.counters[tile] = 0;
+          if (threadIdx.x == 64) {
+            a.counters[tile] = 0;
+            if (seg < 3) gemm_stamp(trace, 5 + 4 * seg);
+          }
         }
       }
       tc_fence_before();
@@ -580,6 +915,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
   __syncthreads();
+  if (threadIdx.x == 0) gemm_stamp(trace, 14);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);

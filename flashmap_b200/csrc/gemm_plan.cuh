@@ -14,6 +14,7 @@ struct GemmPlan {
   int epi;
   int grid;
   size_t smem;
+  unsigned long long* trace;  // optional per-CTA timestamps (diagnostics), else null
 };
 
 // Block width (tokens per tile) used for N tokens.

@@ -84,6 +84,17 @@ FM_API fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M
                        const void* bias, const void* gate, int epilogue, void* workspace, size_t workspace_bytes,
                        int32_t* err, fm_stream stream);
 
+/* Diagnostics: the CTAs fm_gemm_bf16 launches for a shape, and the same call
+ * recording per-CTA global-timer stamps (ns) into trace [grid][16]: 0 entry,
+ * 1 setup done; per segment s < 3 (one tile's k-range): 2+4s MMAs issued,
+ * 3+4s accumulator seen by the epilogue, 4+4s split partial written or
+ * epilogue done, 5+4s split fix-up done; 14 exit.  Unwritten slots keep
+ * their contents. */
+FM_API int32_t fm_gemm_grid(int64_t M, int64_t N, int64_t K);
+FM_API fm_status fm_gemm_bf16_trace(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
+                                    int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
+                                    size_t workspace_bytes, int32_t* err, uint64_t* trace, fm_stream stream);
+
 /* RMSNorm of modeling_flashmap.py:69-80: y = x * bf16(w * rsqrt(mean(x^2) + eps)). */
 FM_API fm_status fm_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
                      fm_stream stream);

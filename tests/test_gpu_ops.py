@@ -74,6 +74,8 @@ GEMM_SHAPES = [
     (128, 1, 64), (256, 16, 256), (2048, 16, 2048), (3000, 17, 320), (6144, 16, 2048), (2048, 16, 8192),
     (16384, 16, 4096), (512, 64, 1024), (512, 128, 1024), (1024, 200, 512), (2048, 1024, 2048), (384, 2048, 256),
     (4096, 5, 4096),
+    # wide blocks split over up to 8 CTAs per tile (head-CTA fix-up from staged partials)
+    (2048, 256, 2048), (256, 96, 4096), (640, 64, 8192), (2048, 1024, 8192),
 ]
 
 
@@ -94,7 +96,7 @@ def test_gemm_store_bias(M, N, K):
     assert (out == ref).float().mean().item() > 0.98
 
 
-@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512)])
+@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512), (256, 96, 4096)])
 def test_gemm_fp32_and_determinism(M, N, K):
     W = rand((M, K), 1 / math.sqrt(K), 4)
     X = rand((N, K), 1.0, 5)
@@ -133,7 +135,8 @@ def test_gemm_swiglu(N):
     assert_bf16_close(out, ref, max_ulps=2, min_exact=0.97, what="swiglu")
 
 
-@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (2048, 16, 8192), (256, 1024, 512)])
+@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (2048, 16, 8192), (256, 1024, 512), (2048, 256, 2048),
+                                   (2048, 1024, 8192)])
 def test_gemm_gated_residual(M, N, K):
     W = rand((M, K), 1 / math.sqrt(K), 12)
     X = rand((N, K), 1.0, 13)
