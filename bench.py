@@ -385,29 +385,41 @@ def run_config4(args, world, rank, local):
     bonus = torch.empty_like(acc)
     wsb = lib.fm_accept_workspace_size(B, K)
     ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-    st = torch.cuda.current_stream().cuda_stream
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
 
     def greedy():
-        lib.fm_accept_greedy(p(target), 0, p(draft), B, K, V, p(acc), p(bonus), p(ws), wsb, ctypes.c_void_p(st))
+        cur = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        _lib.check(lib.fm_accept_greedy(p(target), 0, p(draft), B, K, V, p(acc), p(bonus), p(ws), wsb, cur),
+                   "fm_accept_greedy")
 
     def rejection():
-        lib.fm_accept_rejection(p(target), 0, p(draft), p(q), B, K, V, ctypes.c_float(1.0), ctypes.c_uint64(1234),
-                                ctypes.c_uint32(0), p(acc), p(bonus), p(ws), wsb, ctypes.c_void_p(st))
+        cur = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        _lib.check(lib.fm_accept_rejection(p(target), 0, p(draft), p(q), B, K, V, ctypes.c_float(1.0),
+                                           ctypes.c_uint64(1234), ctypes.c_uint32(0), p(acc), p(bonus), p(ws), wsb,
+                                           cur), "fm_accept_rejection")
 
     res = {}
     for name, fn in (("greedy", greedy), ("rejection", rejection)):
         for _ in range(args.warmup):
             fn()
         torch.cuda.synchronize()
+        # each call captured in a CUDA graph, so the timing is the device's and
+        # not the host's ctypes round trip
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
         barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(args.steps):
-            fn()
+            graph.replay()
         b.record()
         torch.cuda.synchronize()
         res[name] = max_over_ranks(a.elapsed_time(b), world) / args.steps * 1000.0  # us
+        del graph
     peak_h, kind_h = measured_peak_hbm()
     bytes_g = B * (K + 1) * V * 2
     bytes_r = bytes_g + B * V * 4

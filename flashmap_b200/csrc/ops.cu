@@ -109,18 +109,26 @@ __device__ void row_max_argmax(const T* row, long long V, float temperature, flo
   const long long nvec = (V + 7) / 8;
   float m = -INFINITY, bv = -INFINITY;
   long long bi = V;  // sentinel larger than any index
-  for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
-    float x[8];
-    load8(row, vec, V, aligned, x);
+  // vectors i, i + RT, ... in order; four loads issued ahead of their use
+  for (long long vec0 = threadIdx.x; vec0 < nvec; vec0 += 4 * RT) {
+    float x[4][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const long long v = vec * 8 + j;
-      if (v >= V) break;
-      if (bi == V || x[j] > bv) {  // strict: the first index of a tie stays
-        bv = x[j];
-        bi = v;
+    for (int u = 0; u < 4; ++u)
+      if (vec0 + u * RT < nvec) load8(row, vec0 + u * RT, V, aligned, x[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long vec = vec0 + u * RT;
+      if (vec >= nvec) break;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const long long v = vec * 8 + j;
+        if (v >= V) break;
+        if (bi == V || x[u][j] > bv) {  // strict: the first index of a tie stays
+          bv = x[u][j];
+          bi = v;
+        }
+        if (temperature > 0.0f) m = fmaxf(m, __fdiv_rn(x[u][j], temperature));
       }
-      if (temperature > 0.0f) m = fmaxf(m, __fdiv_rn(x[j], temperature));
     }
   }
   // block argmax: largest value, smallest index among equals
@@ -161,13 +169,22 @@ __device__ float row_sumexp(const T* row, long long V, float temperature, float 
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const long long nvec = (V + 7) / 8;
   float acc = 0.0f;
-  for (long long vec = threadIdx.x; vec < nvec; vec += RT) {
-    float x[8];
-    load8(row, vec, V, aligned, x);
+  for (long long vec0 = threadIdx.x; vec0 < nvec; vec0 += 4 * RT) {
+    float x[4][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (vec * 8 + j >= V) break;
-      acc = __fadd_rn(acc, fm_exp(__fsub_rn(__fdiv_rn(x[j], temperature), m)));
+    for (int u = 0; u < 4; ++u)
+      if (vec0 + u * RT < nvec) load8(row, vec0 + u * RT, V, aligned, x[u]);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long vec = vec0 + u * RT;
+      if (vec >= nvec) break;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (vec * 8 + j >= V) break;
+        // x / 1 == x exactly, so the division is skipped at T = 1
+        const float xt = temperature == 1.0f ? x[u][j] : __fdiv_rn(x[u][j], temperature);
+        acc = __fadd_rn(acc, fm_exp(__fsub_rn(xt, m)));
+      }
     }
   }
   return block_sum(acc, red);
@@ -180,13 +197,29 @@ __device__ __forceinline__ long long range_width(long long V) {
 
 // Categorical draw over non-negative weights w(v), v < V, with uniform u:
 // contiguous per-thread ranges, scan, two-level search (see the C oracle).
-template <typename F>
-__device__ long long block_categorical(F weight, long long V, float u, float* sm) {
+// A range weight functor that computes nothing in bulk (scalar weights only).
+struct NoBulk {
+  __device__ bool operator()(long long, float*) const { return false; }
+};
+
+// bulk(v0, w) may fill w[0..31] with the weights of v0 .. v0+31 (all < V) from
+// vector loads issued together, returning false when it cannot (alignment);
+// the range sum then takes the scalar weights.  Either way the sum runs in
+// index order, so the result does not depend on which path ran.
+template <typename F, typename B = NoBulk>
+__device__ long long block_categorical(F weight, long long V, float u, float* sm, B bulk = B()) {
   const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
   const long long W = range_width(V);
   const long long lo = (long long)i * W, hi = min(lo + W, V);
   float t = 0.0f;
-  for (long long v = lo; v < hi; ++v) t = __fadd_rn(t, weight(v));
+  long long v = lo;
+  for (; v + 32 <= hi; v += 32) {
+    float w[32];
+    if (!bulk(v, w)) break;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t = __fadd_rn(t, w[j]);
+  }
+  for (; v < hi; ++v) t = __fadd_rn(t, weight(v));
   float h = t;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
@@ -213,16 +246,24 @@ __device__ long long block_categorical(F weight, long long V, float u, float* sm
   const int first = block_min_int(h > target ? i : RT, ired);
   const int lastpos = block_max_int(t > 0.0f ? i : -1, ired);
   __shared__ long long result;
+  // the chosen range's weights, computed by the whole block (the running sum
+  // below stays sequential, in index order)
+  constexpr int WMAX = 4096;
+  __shared__ float wbuf[WMAX];
+  const int chosen = first < RT ? first : lastpos;
+  const long long clo = chosen >= 0 ? (long long)chosen * W : 0, chi = chosen >= 0 ? min(clo + W, V) : 0;
+  const bool staged = chi - clo <= WMAX;
+  if (staged)
+    for (long long v = clo + i; v < chi; v += RT) wbuf[v - clo] = weight(v);
+  __syncthreads();
   if (i == 0) {
-    const int chosen = first < RT ? first : lastpos;
     long long pick = 0;
     if (chosen >= 0) {
       float run = chosen > 0 ? sm[chosen - 1] : 0.0f;
-      const long long clo = (long long)chosen * W, chi = min(clo + W, V);
       long long last = -1;
       pick = -1;
       for (long long v = clo; v < chi; ++v) {
-        const float wv = weight(v);
+        const float wv = staged ? wbuf[v - clo] : weight(v);
         run = __fadd_rn(run, wv);
         if (wv > 0.0f) last = v;
         if (run > target) {
@@ -608,16 +649,89 @@ __global__ void extend_commit_kernel(const int32_t* cu, int32_t* lengths, int B)
 
 // ------------------------------------------------------------------ sampling / acceptance
 
+// Row slices of the many-CTAs-per-row reductions: SLICE_VPT vectors of 8 per
+// thread, loaded together.
+constexpr int SLICE_VPT = 8;
+constexpr long long SLICE_VECS = (long long)SLICE_VPT * RT;
+
+__device__ __forceinline__ uint32_t orderable_f32(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float from_orderable_f32(uint32_t o) {
+  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+}
+
+// Raw row maxima, many CTAs per row (slices of SLICE_VECS vectors): atomicMax
+// of the orderable bits into max_keys[row] (zero beforehand).  For T > 0 the
+// row's max of x / T is the rounded quotient of this maximum, because a
+// correctly rounded division by a positive T never reverses an order.
+template <typename T>
+__global__ void __launch_bounds__(RT) row_max_slice_kernel(const T* logits, long long V, uint32_t* max_keys) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const T* row = logits + (long long)blockIdx.x * V;
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8;
+  const long long v_begin = (long long)blockIdx.y * SLICE_VECS;
+  float mx = -INFINITY;
+  if (sizeof(T) == 2 && aligned && V % 8 == 0) {
+    // bf16 rows of whole vectors: packed bf16x2 maxima
+    uint4 raw[SLICE_VPT];
+#pragma unroll
+    for (int u = 0; u < SLICE_VPT; ++u) {
+      const long long vec = v_begin + u * RT + threadIdx.x;
+      raw[u] = vec < nvec ? *reinterpret_cast<const uint4*>(row + vec * 8)
+                          : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+    }
+    __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80), __ushort_as_bfloat16(0xff80));
+#pragma unroll
+    for (int u = 0; u < SLICE_VPT; ++u) {
+      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    }
+    mx = fmaxf(__low2float(m2), __high2float(m2));
+  } else {
+    float x[SLICE_VPT][8];
+#pragma unroll
+    for (int u = 0; u < SLICE_VPT; ++u) {
+      const long long vec = v_begin + u * RT + threadIdx.x;
+      if (vec < nvec) load8(row, vec, V, aligned, x[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < SLICE_VPT; ++u) {
+      const long long vec = v_begin + u * RT + threadIdx.x;
+      if (vec >= nvec) break;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (vec * 8 + j < V) mx = fmaxf(mx, x[u][j]);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  __shared__ float wm[RT / 32];
+  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < RT / 32; ++w) mx = fmaxf(mx, wm[w]);
+    atomicMax(max_keys + blockIdx.x, orderable_f32(mx));
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long long V, float temperature,
-                                                       float* stats, int64_t* argmax) {
+                                                       float* stats, int64_t* argmax, const uint32_t* max_keys) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
   const T* row = logits + (long long)blockIdx.x * V;
   float m;
-  long long am;
-  row_max_argmax(row, V, temperature, red, &m, &am);
+  long long am = 0;
+  if (max_keys != nullptr && argmax == nullptr && temperature > 0.0f)
+    m = __fdiv_rn(from_orderable_f32(max_keys[blockIdx.x]), temperature);
+  else
+    row_max_argmax(row, V, temperature, red, &m, &am);
   if (argmax && threadIdx.x == 0) argmax[blockIdx.x] = am;
   if (stats) {
     const float s = temperature > 0.0f ? row_sumexp(row, V, temperature, m, red) : 0.0f;
@@ -652,19 +766,142 @@ __global__ void __launch_bounds__(RT) sample_rows_kernel(const float* probs, lon
   const int row = blockIdx.x, b = row / K, k = row % K;
   const float* pr = probs + (long long)row * V;
   const float u = philox_uniform(seed, (uint32_t)k, (uint32_t)b, offset, 3u);
-  const long long pick = block_categorical([&](long long v) { return pr[v]; }, V, u, sm);
+  const bool aligned = (reinterpret_cast<uintptr_t>(pr) & 15) == 0;
+  const long long pick = block_categorical([&](long long v) { return pr[v]; }, V, u, sm, [&](long long v0, float* w) {
+    if (!aligned) return false;
+    float x[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) load8(pr, v0 / 8 + k, V, true, x[k]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) w[k * 8 + j] = x[k][j];
+    return true;
+  });
   if (threadIdx.x == 0) tokens[row] = pick;
 }
 
-__global__ void accept_greedy_kernel(const int64_t* draft, const int64_t* argmax, int K, int64_t* accepted,
-                                     int64_t* bonus) {
+// Argmax of target rows for greedy acceptance, with many CTAs per row: CTA
+// (row, slice) reads SLICE_VECS vectors of 8 (eight 16-byte loads per thread
+// issued together) and merges its best (value, first index) into the row's
+// 64-bit key with atomicMax (argmax_key: larger value, then smaller index, so
+// the merge is order-independent).  keys must be zero beforehand.
+
+template <typename T>
+__global__ void __launch_bounds__(RT) row_argmax_slice_kernel(const T* logits, long long V,
+                                                              unsigned long long* keys) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const T* row = logits + (long long)blockIdx.x * V;
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8;
+  const long long v_begin = (long long)blockIdx.y * SLICE_VECS;
+  if constexpr (sizeof(T) == 2) {
+    if (aligned && V % 8 == 0) {
+      // bf16 rows of whole vectors: the slice maximum by packed bf16x2 max, then
+      // the first index holding it, searched only by the threads that hold it
+      uint4 raw[SLICE_VPT];
+#pragma unroll
+      for (int u = 0; u < SLICE_VPT; ++u) {
+        const long long vec = v_begin + u * RT + threadIdx.x;
+        raw[u] = vec < nvec ? *reinterpret_cast<const uint4*>(row + vec * 8) : make_uint4(0xff80ff80u, 0xff80ff80u,
+                                                                                         0xff80ff80u, 0xff80ff80u);
+      }
+      __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80), __ushort_as_bfloat16(0xff80));
+#pragma unroll
+      for (int u = 0; u < SLICE_VPT; ++u) {
+        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+      }
+      float mloc = fmaxf(__low2float(m2), __high2float(m2));
+      float mb = mloc;
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+      __shared__ float wm[RT / 32];
+      __shared__ unsigned long long wk2[RT / 32];
+      if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mb;
+      __syncthreads();
+      float M = wm[0];
+#pragma unroll
+      for (int w = 1; w < RT / 32; ++w) M = fmaxf(M, wm[w]);
+      unsigned long long key = 0ull;
+      if (mloc == M) {
+        for (int u = 0; u < SLICE_VPT && key == 0ull; ++u) {
+          const long long vec = v_begin + u * RT + threadIdx.x;
+          if (vec >= nvec) break;
+          const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t bits = j & 1 ? (w[j >> 1] & 0xffff0000u) : (w[j >> 1] << 16);
+            if (__uint_as_float(bits) == M) {
+              key = argmax_key(M, (uint32_t)(vec * 8 + j));
+              break;
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if ((threadIdx.x & 31) == 0) wk2[threadIdx.x >> 5] = key;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int w = 0; w < RT / 32; ++w) key = wk2[w] > key ? wk2[w] : key;
+        if (key) atomicMax(keys + blockIdx.x, key);
+      }
+      return;
+    }
+  }
+  float x[SLICE_VPT][8];
+#pragma unroll
+  for (int u = 0; u < SLICE_VPT; ++u) {
+    const long long vec = v_begin + u * RT + threadIdx.x;
+    if (vec < nvec) load8(row, vec, V, aligned, x[u]);
+  }
+  float bv = -INFINITY;
+  long long bi = -1;
+#pragma unroll
+  for (int u = 0; u < SLICE_VPT; ++u) {
+    const long long vec = v_begin + u * RT + threadIdx.x;
+    if (vec >= nvec) break;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const long long v = vec * 8 + j;
+      if (v >= V) break;
+      if (bi < 0 || x[u][j] > bv) {  // indices rise within the thread: the first of a tie stays
+        bv = x[u][j];
+        bi = v;
+      }
+    }
+  }
+  unsigned long long key = bi >= 0 ? argmax_key(bv, (uint32_t)bi) : 0ull;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+    key = other > key ? other : key;
+  }
+  __shared__ unsigned long long wk[RT / 32];
+  if ((threadIdx.x & 31) == 0) wk[threadIdx.x >> 5] = key;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < RT / 32; ++w) key = wk[w] > key ? wk[w] : key;
+    key = wk[0] > key ? wk[0] : key;
+    if (key) atomicMax(keys + blockIdx.x, key);
+  }
+}
+
+__global__ void accept_greedy_keys_kernel(const int64_t* draft, const unsigned long long* keys, int K,
+                                          int64_t* accepted, int64_t* bonus) {
   pdl_wait();
   pdl_launch_dependents();
   const int b = blockIdx.x;  // one thread per sequence
+  const unsigned long long* kr = keys + (long long)b * (K + 1);
   int acc = 0;
-  while (acc < K && draft[(long long)b * K + acc] == argmax[(long long)b * (K + 1) + acc]) ++acc;
+  while (acc < K && draft[(long long)b * K + acc] == (int64_t)argmax_key_index(kr[acc])) ++acc;
   accepted[b] = acc;
-  bonus[b] = argmax[(long long)b * (K + 1) + acc];
+  bonus[b] = (int64_t)argmax_key_index(kr[acc]);
 }
 
 template <typename T>
@@ -678,20 +915,24 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, c
   __shared__ int s_acc;
   __shared__ int s_any;
   const int b = blockIdx.x;
+  // every slot's test u q < p at once (thread k), then the first failure
+  __shared__ int s_fail;
+  if (threadIdx.x == 0) s_fail = K;
+  __syncthreads();
+  for (int k = threadIdx.x; k < K; k += RT) {
+    const long long row = (long long)b * (K + 1) + k;
+    const long long d = draft[(long long)b * K + k];
+    const float m = stats[2 * row], s = stats[2 * row + 1];
+    const float x = __fdiv_rn(to_f(target[row * V + d]), temperature);
+    const float p = __fdiv_rn(fm_exp(__fsub_rn(x, m)), s);
+    const float qd = q[((long long)b * K + k) * V + d];
+    const float u = philox_uniform(seed, (uint32_t)k, (uint32_t)b, offset, 1u);
+    if (!(__fmul_rn(u, qd) < p)) atomicMin(&s_fail, k);
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
-    int acc = 0;
-    for (; acc < K; ++acc) {
-      const long long row = (long long)b * (K + 1) + acc;
-      const long long d = draft[(long long)b * K + acc];
-      const float m = stats[2 * row], s = stats[2 * row + 1];
-      const float x = __fdiv_rn(to_f(target[row * V + d]), temperature);
-      const float p = __fdiv_rn(fm_exp(__fsub_rn(x, m)), s);
-      const float qd = q[((long long)b * K + acc) * V + d];
-      const float u = philox_uniform(seed, (uint32_t)acc, (uint32_t)b, offset, 1u);
-      if (!(__fmul_rn(u, qd) < p)) break;
-    }
-    s_acc = acc;
-    accepted[b] = acc;
+    s_acc = s_fail;
+    accepted[b] = s_fail;
   }
   __syncthreads();
   const int acc = s_acc;
@@ -708,6 +949,42 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, c
     const float dlt = __fsub_rn(pv, qr[v]);
     return dlt > 0.0f ? dlt : 0.0f;
   };
+  // 32 weights from 16-byte loads issued together (rows 16-byte aligned)
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(tr) & 15) == 0 && (reinterpret_cast<uintptr_t>(qr) & 15) == 0;
+  auto target_bulk = [&](long long v0, float* w) {
+    if (!vec_ok) return false;
+    float x[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) load8(tr, v0 / 8 + k, V, true, x[k]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        w[k * 8 + j] = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
+    return true;
+  };
+  auto residual_bulk = [&](long long v0, float* w) {
+    if (!vec_ok) return false;
+    float x[4][8], qv[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      load8(tr, v0 / 8 + k, V, true, x[k]);
+      if (acc < K) load8(qr, v0 / 8 + k, V, true, qv[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float pv = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
+        if (acc >= K) {
+          w[k * 8 + j] = pv;
+        } else {
+          const float dlt = __fsub_rn(pv, qv[k][j]);
+          w[k * 8 + j] = dlt > 0.0f ? dlt : 0.0f;
+        }
+      }
+    return true;
+  };
   int any = 0;
   for (long long v = threadIdx.x; v < V && !any; v += RT) any = residual(v) > 0.0f;
   if (threadIdx.x == 0) s_any = 0;
@@ -717,9 +994,9 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, c
   const float u = philox_uniform(seed, 0u, (uint32_t)b, offset, 2u);
   long long pick;
   if (s_any)
-    pick = block_categorical(residual, V, u, sm);
+    pick = block_categorical(residual, V, u, sm, residual_bulk);
   else
-    pick = block_categorical(target_p, V, u, sm);
+    pick = block_categorical(target_p, V, u, sm, target_bulk);
   if (threadIdx.x == 0) bonus[b] = pick;
 }
 
@@ -955,6 +1232,21 @@ namespace {
                 : launch_kernel(KERNEL<float>, grid, dim3(RT), 0, as_stream(stream), false,                   \
                                 static_cast<const float*>(ptr), __VA_ARGS__))
 bool bad_dtype(int32_t d) { return d != 0 && d != 1; }
+
+// greedy acceptance through the sliced argmax: zero the keys, slice kernel, accept
+fm_status greedy_sliced(const void* logits, int32_t dtype, const int64_t* draft, int64_t B, int64_t K, int64_t V,
+                        int64_t* accepted, int64_t* bonus, unsigned long long* keys, fm_stream stream) {
+  const long long rows = B * (K + 1);
+  fm_status st = check_cuda(cudaMemsetAsync(keys, 0, (size_t)rows * 8, as_stream(stream)), "accept: key reset");
+  if (st) return st;
+  const long long slices = ((V + 7) / 8 + SLICE_VECS - 1) / SLICE_VECS;
+  if (slices > 65535) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large");
+  st = FM_DISPATCH_LOGITS(dtype, row_argmax_slice_kernel, dim3((unsigned)rows, (unsigned)slices), logits,
+                          (long long)V, keys);
+  if (st) return st;
+  return launch_kernel(accept_greedy_keys_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
+                       (const unsigned long long*)keys, (int)K, accepted, bonus);
+}
 }  // namespace
 
 extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
@@ -962,7 +1254,7 @@ extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t row
   if (!logits) return set_error(FM_ERR_INVALID, "row_stats: null logits");
   if (rows <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "row_stats: bad arguments");
   return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), logits, (long long)V, temperature, stats,
-                            argmax);
+                            argmax, (const uint32_t*)nullptr);
 }
 
 extern "C" fm_status fm_softmax_rows(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
@@ -982,7 +1274,7 @@ extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const flo
   if (temperature <= 0.0f) {
     if (!logits) return set_error(FM_ERR_INVALID, "sample_rows: null logits");
     return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * K)), logits, (long long)V, 0.0f,
-                              (float*)nullptr, tokens);
+                              (float*)nullptr, tokens, (const uint32_t*)nullptr);
   }
   if (!probs) return set_error(FM_ERR_INVALID, "sample_rows: T > 0 needs probs");
   return launch_kernel(sample_rows_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false, probs,
@@ -1000,12 +1292,8 @@ extern "C" fm_status fm_accept_greedy(const void* target_logits, int32_t dtype, 
   if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "accept: bad arguments");
   if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
     return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
-  int64_t* am = static_cast<int64_t*>(workspace);
-  fm_status st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits,
-                                    (long long)V, 0.0f, (float*)nullptr, am);
-  if (st) return st;
-  return launch_kernel(accept_greedy_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
-                       (const int64_t*)am, (int)K, accepted, bonus);
+  return greedy_sliced(target_logits, dtype, draft, B, K, V, accepted, bonus,
+                       static_cast<unsigned long long*>(workspace), stream);
 }
 
 extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtype, const int64_t* draft,
@@ -1018,8 +1306,18 @@ extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtyp
   if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
     return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
   float* stats = static_cast<float*>(workspace);
-  fm_status st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits,
-                                    (long long)V, temperature, stats, (int64_t*)nullptr);
+  const long long rows = B * (K + 1);
+  // raw row maxima from many CTAs per row, then per row the fixed-order sum
+  uint32_t* max_keys = reinterpret_cast<uint32_t*>(stats + 2 * rows);
+  fm_status st = check_cuda(cudaMemsetAsync(max_keys, 0, (size_t)rows * 4, as_stream(stream)), "accept: max reset");
+  if (st) return st;
+  const long long slices = ((V + 7) / 8 + SLICE_VECS - 1) / SLICE_VECS;
+  if (slices > 65535) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large");
+  st = FM_DISPATCH_LOGITS(dtype, row_max_slice_kernel, dim3((unsigned)rows, (unsigned)slices), target_logits,
+                          (long long)V, max_keys);
+  if (st) return st;
+  st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), target_logits, (long long)V, temperature,
+                          stats, (int64_t*)nullptr, (const uint32_t*)max_keys);
   if (st) return st;
   return FM_DISPATCH_LOGITS(dtype, accept_rejection_kernel, dim3((unsigned)B), target_logits, draft, q, (long long)V,
                             (int)K, temperature, seed, offset, (const float*)stats, accepted, bonus);
@@ -1113,9 +1411,6 @@ extern "C" fm_status fm_accept_greedy_noalloc(const void* target_logits, int32_t
   fm_status st;
   int64_t* am = accept_noalloc_scratch(&st);
   if (!am) return st;
-  st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * (K + 1))), target_logits, (long long)V, 0.0f,
-                          (float*)nullptr, am);
-  if (st) return st;
-  return launch_kernel(accept_greedy_kernel, dim3((unsigned)B), dim3(1), 0, as_stream(stream), false, draft,
-                       (const int64_t*)am, (int)K, accepted, bonus);
+  return greedy_sliced(target_logits, dtype, draft, B, K, V, accepted, bonus,
+                       reinterpret_cast<unsigned long long*>(am), stream);
 }
