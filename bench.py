@@ -44,6 +44,10 @@ METRIC = "drafted tokens/sec (K=16) at 1/2/4/8 B200; batch-1 pass µs vs HBM flo
 CONFIG2 = dict(target_hidden_size=4096, vocab_size=151936, target_layer_ids=[1], block_size=16, hidden_size=2048,
                num_hidden_layers=8, num_attention_heads=16, intermediate_size=8192, mlp_type="gelu")
 CONTEXT = 2048
+# SURVEY config 5: the Qwen3.8-27B map (SwiGLU, 32768-token state vocabulary of 248320)
+CONFIG5 = dict(target_hidden_size=5120, vocab_size=248320, state_vocab_size=32768, target_layer_ids=[1],
+               block_size=16, hidden_size=2560, num_hidden_layers=10, num_attention_heads=20, intermediate_size=6912,
+               mlp_type="swiglu")
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -325,42 +329,112 @@ def time_replays(session, steps: int, warmup: int, world: int) -> float:
 
 
 def run_config3(args, world, rank, local):
-    """Batched ragged drafting (SURVEY config 3): 64 sequences per GPU,
-    contexts U[512, 4096], one jump and two jumps."""
+    """Batched ragged drafting: SURVEY config 3 (the config-2 map, 64 sequences
+    per GPU, contexts U[512, 4096], one jump and two jumps) or config 5 (the
+    27B map, SwiGLU and a state vocabulary, 64 requests per GPU — the per-GPU
+    chunk of 512 requests over 8 GPUs — contexts U[1024, 8192], one jump).
+    --profile-small keeps the GEMM shapes of config 3 (64 x 16 tokens) with 2
+    layers, a 32768-row LM head and contexts U[64, 256], for ncu captures."""
     from flashmap_b200 import _lib
 
     _lib.require_device()
     batch = 64
+    five = args.workload == "config5"
+    c = CONFIG5 if five else CONFIG2
+    lo, hi = (1024, 8192) if five else (512, 4096)
+    if args.profile_small:
+        c = dict(CONFIG2, num_hidden_layers=2, vocab_size=32768)
+        lo, hi = 64, 256
     out = {}
-    for steps_n in (1, 2):
-        config, model, cache, session, lengths = build_batched(CONFIG2, batch, 512, 4096, seed=rank, num_steps=steps_n)
+    for steps_n in ((1,) if five or args.profile_small else (1, 2)):
+        config, model, cache, session, lengths = build_batched(c, batch, lo, hi, seed=rank, num_steps=steps_n)
         ms = time_replays(session, args.steps, args.warmup, world)
         model._plans[next(iter(model._plans))].check_device_errors()
         out[steps_n] = (ms, lengths)
         del model, cache, session
         torch.cuda.empty_cache()
     ms1, lengths = out[1]
-    ms2, _ = out[2]
+    ms2 = out[2][0] if 2 in out else None
     K = 16
-    flops = gemm_flops(CONFIG2, batch)
-    kv = float(((lengths + 1).sum()) * CONFIG2["num_hidden_layers"] * 2 * CONFIG2["hidden_size"] * 2)
+    flops = gemm_flops(c, batch)
+    kv = float(((lengths + 1).sum()) * c["num_hidden_layers"] * 2 * c["hidden_size"] * 2)
     peak_t, kind_t = measured_peak_tensor()
     peak_h, kind_h = measured_peak_hbm()
     achieved = flops / (ms1 / 1000.0) / 1e12
     if rank != 0:
         return
+    name = "config5" if five else "config3"
     line = {
         "metric": "drafted tokens/sec (K=16), batch 64 ragged per GPU", "value": world * batch * K / (ms1 / 1000.0),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms1,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded random-init config-2 drafter, N(0,1) conditioning, context lengths U[512,4096])",
-        "config": {"workload": "config3: batch 64 ragged, K=16, one jump (and two jumps below)", "batch_per_gpu": batch,
-                   "context_mean": float(lengths.float().mean()), "launch": "kernel sequence"},
+        "data": f"synthetic (seeded random-init {name} drafter, N(0,1) conditioning, context lengths U[{lo},{hi}])",
+        "config": {"workload": (f"{name}: batch 64 ragged, K=16, one jump" + ("" if ms2 is None else
+                                                                               " (and two jumps below)")
+                                + (" [profile-small: 2 layers, 32768-row LM head]" if args.profile_small else "")),
+                   "batch_per_gpu": batch, "context_mean": float(lengths.float().mean()), "launch": "kernel sequence"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_t, "unit": "TFLOP/s",
                      "frac": achieved / peak_t, "peak_kind": kind_t, "gemm_tflop_per_pass": flops / 1e12,
                      "kv_bytes_per_pass": kv, "kv_floor_us": kv / (peak_h * 1e9) * 1e6,
                      "gemm_floor_us": flops / (peak_t * 1e12) * 1e6},
-        "two_jumps": {"ms_per_step": ms2, "value": world * batch * K / (ms2 / 1000.0), "unit": "tokens/s"},
+    }
+    if ms2 is not None:
+        line["two_jumps"] = {"ms_per_step": ms2, "value": world * batch * K / (ms2 / 1000.0), "unit": "tokens/s"}
+    print(json.dumps(line), flush=True)
+
+
+def run_paged(args, world, rank, local):
+    """The vLLM-layout paged cross-attention operator (flashmap_vllm::paged_cross_attention)
+    at the config-2 map's shape: 64 requests x 16 query rows, 16 heads of 128,
+    2048 context positions each in shuffled 16-token pages; HBM roofline on the
+    K/V bytes (1.07 GB per call, larger than L2)."""
+    from flashmap_b200 import _lib
+    from flashmap_b200 import serving_ops as S
+
+    _lib.require_device()
+    R, H, hd, page, ctx = 64, 16, 128, 16, 2048
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(rank)
+    cols = ctx // page
+    cache = torch.randn(R * cols, H, page, 2 * hd, generator=g, device=dev).to(torch.bfloat16)
+    table = torch.randperm(R * cols, generator=g, device=dev).view(R, cols).int()
+    q = torch.randn(R * 16, H, hd, generator=g, device=dev).to(torch.bfloat16)
+    cu = torch.arange(0, (R + 1) * 16, 16, dtype=torch.int32, device=dev)
+    su = torch.full((R,), ctx, dtype=torch.int32, device=dev)
+
+    def call():
+        S.vllm_paged_cross_attention(q, cache, cu, su, table, None, None, 16, ctx, hd ** -0.5, 3)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        call()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = max_over_ranks(a.elapsed_time(b), world) / args.steps * 1000.0
+    del graph
+    peak_h, kind_h = measured_peak_hbm()
+    nbytes = R * ctx * H * hd * 2 * 2
+    if rank != 0:
+        return
+    line = {
+        "metric": "paged cross-attention (vLLM layout), us per call", "value": us, "unit": "us", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": us / 1000.0, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) cache and queries)",
+        "config": {"workload": "paged: 64 requests x 16 queries, 16 heads x 128, ctx 2048, 16-token pages, shuffled",
+                   "timing": "CUDA-graph replays (workspace allocation included), inputs larger than L2"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (us * 1e-6) / 1e9, "peak": peak_h, "unit": "GB/s",
+                     "frac": nbytes / (us * 1e-6) / 1e9 / peak_h, "peak_kind": kind_h, "algorithmic_bytes": nbytes},
     }
     print(json.dumps(line), flush=True)
 
@@ -552,8 +626,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch", choices=["auto", "kernels", "persistent"], default="auto",
                     help="launch structure of a draft: the kernel sequence or one persistent launch")
-    ap.add_argument("--workload", choices=["config2", "config3", "config4"], default="config2",
-                    help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance)")
+    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "paged"], default="config2",
+                    help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance), "
+                         "config5 (27B map, batch 64 ragged), paged (vLLM paged cross-attention operator)")
     ap.add_argument("--profile-small", action="store_true",
                     help="2 layers and a 32768-row LM head: the same kernels on < 2 GB, for ncu captures")
     args = ap.parse_args()
@@ -564,8 +639,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
-        elif args.workload == "config3":
+        elif args.workload in ("config3", "config5"):
             run_config3(args, world, rank, local)
+        elif args.workload == "paged":
+            run_paged(args, world, rank, local)
         elif args.workload == "config4":
             run_config4(args, world, rank, local)
         else:
