@@ -624,8 +624,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--launch", choices=["auto", "kernels", "persistent"], default="auto",
-                    help="launch structure of a draft: the kernel sequence or one persistent launch")
+    ap.add_argument("--launch", choices=["auto", "kernels"], default="auto",
+                    help="launch structure of a draft (both the kernel sequence; the persistent pass is withdrawn)")
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "paged"], default="config2",
                     help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance), "
                          "config5 (27B map, batch 64 ragged), paged (vLLM paged cross-attention operator)")

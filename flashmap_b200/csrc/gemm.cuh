@@ -6,11 +6,13 @@
 //
 // Work decomposition: the (tile, k-block) units of the whole GEMM are split
 // evenly over the grid (stream-K).  A tile whose k-range spans several CTAs
-// is finished by the last contributor to arrive: every contributor writes its
-// fp32 partial to the workspace and bumps a per-tile counter; the one that
-// sees the final count sums all partials in contributor order (so the result
-// does not depend on arrival order) and runs the epilogue.  Nothing spins on
-// another CTA.
+// is finished by its head CTA (the holder of its first k-block): the other
+// contributors write their fp32 partials to the workspace and release-add a
+// per-tile counter; the head waits (bounded, the contributors are resident:
+// the grid never exceeds one CTA per SM) for the count, stages the partials
+// into its idle pipeline buffers with bulk copies, sums them in contributor
+// order (so the result does not depend on arrival order) and runs the
+// epilogue.
 //
 // Roles (192 threads): warp 0 lane 0 issues TMA loads, warp 1 lane 0 issues
 // tcgen05.mma and owns the TMEM allocation, warps 2-5 read the accumulators
@@ -108,17 +110,13 @@ __device__ __forceinline__ void gemm_red_release(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Split tiles of wide blocks (BN >= 64) are finished by their head CTA (the
-// one holding the tile's first k-block; the split segment is always its last
-// segment, so its pipeline shared memory is idle by then): it waits (bounded)
-// until the other contributors have published their fp32 partials, stages
-// them into the idle pipeline buffers with bulk copies, and sums them with its
-// own accumulator in contributor order.  Narrow blocks keep the last-arriver
-// fix-up (their partials are a few KB).
-template <int BN>
-struct OwnerFixup {
-  static constexpr bool ON = BN >= 64;
-};
+// Split tiles are finished by their head CTA (the one holding the tile's
+// first k-block; the split segment is always its last segment, so its
+// pipeline shared memory is idle by then): it waits (bounded) until the other
+// contributors have published their fp32 partials, stages them into the idle
+// pipeline buffers with bulk copies (one round trip for all of them, instead
+// of a few serial ones), and sums them with its own accumulator in
+// contributor order.
 
 // ---------------------------------------------------------------------------------------------
 // Epilogue on 16 accumulator columns (tokens n0 .. n0+15) of tile row r (feature m).
@@ -709,7 +707,7 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
           }
         }
-      } else if (OwnerFixup<BN>::ON) {
+      } else {
         const long long c_first = cta_of_unit((long long)tile * kb, U, G);
         const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
         if (c != c_first) {
@@ -761,21 +759,54 @@ __global__ void __launch_bounds__(192, 1)
             const int per_col = others * 128 * 4;
             int cols = (AREA / per_col) / 16 * 16;
             if (cols > BN) cols = BN;
-            if (cols < 16) {  // more contributors than the grid cap allows: never staged
-              if (threadIdx.x == 64) record_error(a.err, DEV_BAD_INDEX);
-              cols = BN + 1;
+            bool staged_ok = true;
+            if (cols < 16) {
+              // many contributors (narrow blocks, small M, long K): one 16-column
+              // chunk at a time, the partials staged in groups
+              constexpr int MAX_O = AREA / (16 * 512);
+              int round = 0;
+              for (int c0 = 0; c0 < BN && staged_ok; c0 += 16) {
+                float v[16];
+                tmem_ld_x16(taddr + c0, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(0.0f, v[j]);
+                for (int og = 0; og < others; og += MAX_O, ++round) {
+                  const int n = (others - og) < MAX_O ? (others - og) : MAX_O;
+                  named_bar_sync(1, 128);  // the previous group was consumed
+                  if (threadIdx.x == 64) {
+                    mbar_arrive_expect_tx(fix_bar, (uint32_t)(n * 16 * 512));
+                    for (int o = 0; o < n; ++o)
+                      bulk_load(stage + (long long)o * 16 * 128,
+                                a.ws + ((long long)((c_first + 1 + og + o) * 2) * BN + c0) * 128, 16u * 512u,
+                                fix_bar);
+                    flags[1] = mbar_wait(fix_bar, (uint32_t)round & 1u, nullptr) ? 1 : 0;
+                    if (!flags[1]) {
+                      record_error(a.err, DEV_TIMEOUT_OTHER);
+                      *abort_flag = 1;
+                    }
+                  }
+                  named_bar_sync(1, 128);
+                  if (!flags[1]) {
+                    staged_ok = false;
+                    break;
+                  }
+                  for (int o = 0; o < n; ++o) {
+                    const float* src = stage + (long long)o * 16 * 128 + r;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], src[j * 128]);
+                  }
+                }
+                if (!staged_ok) break;
+                epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, nullptr);
+              }
+              cols = BN + 1;  // the staged rounds below are skipped
             }
             float pre[32];
-            bool have = !vec && epilogue_prefetch<EPI>(a, m, n0, pre);
+            bool have = false;
             uint4 vp[2];
             constexpr bool RESID_RING = EPI == EPI_RESID && S::RING_BYTES > 0;
             constexpr int NCH = BN / 16;
-            if (vec && !RESID_RING) vec_prefetch<EPI>(a, mt * 128, n0, vp);
-            if (vec && RESID_RING)
-#pragma unroll
-              for (int pc = 0; pc < S::RING - 1; ++pc)
-                vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
-            bool staged_ok = true;
             for (int col0 = 0, round = 0; cols <= BN && col0 < BN; col0 += cols, ++round) {
               const int ncols = (BN - col0) < cols ? (BN - col0) : cols;
               if (threadIdx.x == 64) {
@@ -784,6 +815,17 @@ __global__ void __launch_bounds__(192, 1)
                   bulk_load(stage + (long long)o * ncols * 128,
                             a.ws + ((long long)((c_first + 1 + o) * 2) * BN + col0) * 128, (uint32_t)(ncols * 512),
                             fix_bar);
+              }
+              if (round == 0) {
+                // the epilogue's own global reads go out after the partials' bulk copies
+                have = !vec && epilogue_prefetch<EPI>(a, m, n0, pre);
+                if (vec && !RESID_RING) vec_prefetch<EPI>(a, mt * 128, n0, vp);
+                if (vec && RESID_RING)
+#pragma unroll
+                  for (int pc = 0; pc < S::RING - 1; ++pc)
+                    vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
+              }
+              if (threadIdx.x == 64) {
                 flags[1] = mbar_wait(fix_bar, (uint32_t)round & 1u, nullptr) ? 1 : 0;
                 if (!flags[1]) {
                   record_error(a.err, DEV_TIMEOUT_OTHER);
@@ -839,73 +881,6 @@ __global__ void __launch_bounds__(192, 1)
               if (staged_ok) a.counters[tile] = 0;
               if (seg < 3) gemm_stamp(trace, 5 + 4 * seg);
             }
-          }
-        }
-      } else {
-        const long long c_first = cta_of_unit((long long)tile * kb, U, G);
-        const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
-        const int slot = (seg_begin == u0) ? 0 : 1;
-        float* mine = a.ws + ((long long)(c * 2 + slot) * BN) * 128;
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          float v[16];
-          tmem_ld_x16(taddr + c0, v);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) __stcg(mine + (long long)(c0 + j) * 128 + r, v[j]);
-        }
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (threadIdx.x == 64) {
-          if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
-          const int old = atomicAdd(a.counters + tile, 1);
-          flags[1] = (old == (int)(c_last - c_first));
-        }
-        named_bar_sync(1, 128);
-        if (flags[1]) {
-          __threadfence();
-          float pre[32];
-          const bool have = epilogue_prefetch<EPI>(a, m, n0, pre);
-          for (int c0 = 0; c0 < BN; c0 += 16) {
-            float own[16], v[16], nxt[32];
-            tmem_ld_x16(taddr + c0, own);
-            const bool more = have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-            // partials are summed in contributor order (deterministic); the loads
-            // of four contributors are issued together to overlap their latency
-            for (long long cc0 = c_first; cc0 <= c_last; cc0 += 4) {
-              float t[4][16];
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
-                const long long cc = cc0 + q4;
-                if (cc <= c_last && cc != c) {
-                  const long long first_tile = ((long long)cc * U / G) / kb;
-                  const int cs = (first_tile == tile) ? 0 : 1;
-                  const float* p = a.ws + ((cc * 2 + cs) * BN + c0) * 128 + r;
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) t[q4][j] = __ldcg(p + (long long)j * 128);
-                } else {
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) t[q4][j] = own[j];
-                }
-              }
-#pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4)
-                if (cc0 + q4 <= c_last) {
-#pragma unroll
-                  for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], t[q4][j]);
-                }
-            }
-            epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
-            if (more) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
-            }
-          }
-          if (threadIdx.x == 64) {
-            a.counters[tile] = 0;
-            if (seg < 3) gemm_stamp(trace, 5 + 4 * seg);
           }
         }
       }

@@ -283,7 +283,11 @@ fm_status validate(const fm_model_desc* m, const fm_plan_config* c) {
   if (c->num_steps > 1 && m->embed && !m->embed_state_t)
     return set_error(FM_ERR_INVALID, "plan: multi-step drafts need embed_state_t");
   if (c->cache_batch < c->batch) return set_error(FM_ERR_SHAPE, "plan: cache batch smaller than plan batch");
-  if (c->launch_mode != FM_LAUNCH_AUTO && c->launch_mode != FM_LAUNCH_KERNELS && c->launch_mode != FM_LAUNCH_PERSISTENT)
+  if (c->launch_mode == FM_LAUNCH_PERSISTENT)
+    return set_error(FM_ERR_UNSUPPORTED,
+                     "plan: the persistent single-launch pass is withdrawn (an intermittent illegal-instruction "
+                     "fault is under investigation); use FM_LAUNCH_KERNELS");
+  if (c->launch_mode != FM_LAUNCH_AUTO && c->launch_mode != FM_LAUNCH_KERNELS)
     return set_error(FM_ERR_INVALID, "plan: unknown launch_mode %d", c->launch_mode);
   if (!m->layer || !m->rope_cos || !m->rope_sin) return set_error(FM_ERR_INVALID, "plan: missing weights");
   return FM_OK;

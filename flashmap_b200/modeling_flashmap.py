@@ -463,9 +463,8 @@ class FlashMapDraftModel(PreTrainedModel):
         self.post_init()
 
     # values derived from the weights are rebuilt after a move or a reload (:271-285)
-    # "auto": the faster launch structure for the shape; "kernels": the kernel
-    # sequence; "persistent": one persistent launch per batch-1, one-jump draft.
-    # All three give identical results.
+    # "auto" and "kernels": the kernel sequence.  "persistent" (one launch per
+    # batch-1, one-jump draft) is withdrawn: plan creation raises.
     launch_mode = "auto"
 
     def _clear_caches(self) -> None:

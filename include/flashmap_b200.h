@@ -399,13 +399,14 @@ typedef struct fm_jump {
   float s, next;     /* start time and the time the state moves to (next == 1: last jump) */
 } fm_jump;
 
-/* How fm_draft launches its work.  Both give identical results. */
+/* How fm_draft launches its work. */
 enum {
-  FM_LAUNCH_AUTO = 0,       /* the faster of the two for the plan's shape (today: the kernel sequence) */
+  FM_LAUNCH_AUTO = 0,       /* the kernel sequence */
   FM_LAUNCH_KERNELS = 1,    /* the kernel sequence: one launch per operation, chained by programmatic
                                dependent launch */
-  FM_LAUNCH_PERSISTENT = 2  /* one persistent cooperative launch for the whole draft (batch 1, one jump;
-                               other shapes run the kernel sequence) */
+  FM_LAUNCH_PERSISTENT = 2  /* withdrawn: fm_plan_create returns FM_ERR_UNSUPPORTED (the single-launch
+                               pass raised an intermittent illegal-instruction fault that is not
+                               understood yet, so it is not run) */
 };
 
 typedef struct fm_plan_config {
