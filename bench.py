@@ -128,6 +128,7 @@ def build_workload(seed: int = 0, small: bool = False, launch: str = "auto"):
     hidden = torch.randn(1, CONTEXT, config.target_hidden_size, generator=g, device=dev).to(torch.bfloat16)
     model.extend_context(cache, hidden, embed, head)
     session = DraftSession(model, cache, embed, head, num_steps=1, seed=seed)
+    session.embed_tokens, session.lm_head = embed, head
     return config, model, cache, session
 
 
@@ -581,6 +582,34 @@ def run_ours(args, world, rank, local):
     lm_gbs = nbytes["lm_head"] / (lm_ms / 1000.0) / 1e9
     pass_gbs = nbytes["total"] / (ms_per_step / 1000.0) / 1e9
 
+    # the serving plugins' fast mode (DiT head folded into the LM-head rows;
+    # changes rounding, outside parity), the same draft reported beside the headline
+    folded = None
+    if not args.profile_small:
+        from flashmap_b200 import DraftSession
+
+        model.fold_head = True
+        fsession = DraftSession(model, cache, session.embed_tokens, session.lm_head, num_steps=1, seed=rank)
+        for _ in range(args.warmup):
+            fsession.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f_steps = max(args.steps // 4, 10)
+        f0.record(stream)
+        for _ in range(f_steps):
+            fsession.replay()
+        f1.record(stream)
+        torch.cuda.synchronize()
+        f_ms = max_over_ranks(f0.elapsed_time(f1), world) / f_steps
+        model.fold_head = False
+        fbytes = nbytes["total"] - nbytes["lm_head"] - CONFIG2["target_hidden_size"] * CONFIG2["hidden_size"] * 2 \
+            + CONFIG2["vocab_size"] * CONFIG2["hidden_size"] * 2
+        folded = {"ms_per_step": f_ms, "value": world * K / (f_ms / 1000.0), "unit": "tokens/s",
+                  "algorithmic_bytes": fbytes, "hbm_frac": fbytes / (f_ms / 1000.0) / 1e9 / peak,
+                  "note": "fold_head fast mode (vllm/fold.py:76-100): outside parity with the HF path"}
+        del fsession
+
     if rank != 0:
         return
     line = {
@@ -608,6 +637,8 @@ def run_ours(args, world, rank, local):
         "gpu_launches_per_step": launches,
         "clocks": clocks,
     }
+    if folded is not None:
+        line["fast_mode_folded_head"] = folded
     if args.profile_small:
         line["config"]["workload"] = "profiling case: config-2 layer shapes, 2 layers, 32768-row LM head"
     if world == 1 and not args.no_cpu_baseline and not args.profile_small:

@@ -736,9 +736,16 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
   p->g_head.args.ldo = Ht;
   p->g_head.args.bias = static_cast<const __nv_bfloat16*>(m->head_b);
   if (p->has_target) {
-    if ((st = gemm_prepare(&p->g_lm, m->lm_w, S, Ht, Ht, p->hidden, T, Ht, EPI_LOGITS, ws, gc, err)))
-      return fail(st);
-    p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_b);
+    if (m->lm_fold_w) {
+      // the folded head: final AdaLN output [T, D] times lm_w·head_w [S, D]
+      if ((st = gemm_prepare(&p->g_lm, m->lm_fold_w, S, D, D, p->h, T, D, EPI_LOGITS, ws, gc, err)))
+        return fail(st);
+      p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_fold_b);
+    } else {
+      if ((st = gemm_prepare(&p->g_lm, m->lm_w, S, Ht, Ht, p->hidden, T, Ht, EPI_LOGITS, ws, gc, err)))
+        return fail(st);
+      p->g_lm.args.bias = static_cast<const __nv_bfloat16*>(m->lm_b);
+    }
     p->g_lm.args.argmax_keys = p->keys;
   }
   // the cache as one [rows, head_dim] matrix for the cross-attention TMA
@@ -790,7 +797,7 @@ extern "C" fm_status fm_plan_lm_head(fm_plan* p, void* logits, int64_t ldl, fm_s
 
 namespace {
 
-fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s) {
+fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s, bool with_head = true) {
   const fm_model_desc& m = p->m;
   const int T = p->T, D = p->D, L = p->L;
   const __nv_bfloat16* mods = static_cast<const __nv_bfloat16*>(j.mods);
@@ -845,7 +852,7 @@ fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s) {
   }
   const __nv_bfloat16* mf = mods + (size_t)(L * 3) * 3 * D;
   if ((st = launch_adaln(p->x, mf, p->h, T, D, m.ln_eps, s, true))) return st;
-  return gemm_launch(p->g_head, s, true);
+  return with_head ? gemm_launch(p->g_head, s, true) : FM_OK;
 }
 
 }  // namespace
@@ -965,8 +972,10 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
       }
     }
     if ((st = launch_mix_state(mx, s, true))) return st;
-    if ((st = run_dit(p, j, s))) return st;
     const bool last = ji == n - 1;
+    // the folded head reads the final AdaLN output; the DiT head then runs only for io->hidden
+    const bool folded = m.lm_fold_w != nullptr;
+    if ((st = run_dit(p, j, s, !folded || (last && io->hidden)))) return st;
     GemmPlan lm = p->g_lm;
     lm.args.col_ids = reinterpret_cast<const long long*>(m.draft_ids);  // token ids of the argmax
     if (last && io->logits) {

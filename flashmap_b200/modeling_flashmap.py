@@ -236,6 +236,7 @@ class _Pack:
         self.S = cfg.state_vocab_size or cfg.vocab_size
         self.target_key = None
         self.embed = self.lm_w = self.lm_b = self.draft_ids = None
+        self.lm_fold_w = self.lm_fold_b = None
         self.embed_state_t = self.uniform_embeds = self.chol = None
         self.rope_len = 0
         self.rope_cos = self.rope_sin = None
@@ -260,6 +261,7 @@ class _Pack:
             self.lm_w = head_w.detach().to(dev, bf).contiguous()
             self.lm_b = None if head_b is None else head_b.detach().to(dev, bf).contiguous()
         self.S = e_s.shape[0]
+        self.lm_fold_w = self.lm_fold_b = None
         self.embed_state_t = ops.transpose(e_s)  # E_S^T [H, S]
         uniform = torch.full((1, self.S), 1.0 / self.S, device=dev).to(bf)
         self.uniform_embeds = ops.gemm(self.embed_state_t, uniform).reshape(-1).contiguous()
@@ -269,6 +271,17 @@ class _Pack:
         self.chol = factor.to(dev, bf).contiguous()
         self.target_key = key
         return True
+
+    def ensure_fold(self):
+        """The folded head of the serving plugins (vllm/fold.py:76-100,
+        sglang/model.py:515-531): ``lm_w @ head_w`` [S, D] and ``lm_w @ head_b``
+        [S], fp32 accumulation rounded to bf16, once per attached target."""
+        if self.lm_fold_w is None:
+            head_t = ops.transpose(self.g["head.weight"])  # [D, Ht]
+            self.lm_fold_w = ops.gemm(head_t, self.lm_w).contiguous()  # [S, D]
+            b = ops.gemm(self.g["head.bias"].view(1, -1).contiguous(), self.lm_w)  # [S, 1]
+            self.lm_fold_b = b.reshape(-1).contiguous()
+        return self.lm_fold_w, self.lm_fold_b
 
     def ensure_rope(self, cfg, max_pos: int):
         if max_pos > self.rope_len:
@@ -346,6 +359,10 @@ class _Plan:
         d.embed_state_t, d.chol, d.uniform_embeds = ptr(pack.embed_state_t), ptr(pack.chol), ptr(pack.uniform_embeds)
         d.state_norm_w = g["state_norm.weight"].data_ptr()
         d.rope_cos, d.rope_sin, d.rope_len = pack.rope_cos.data_ptr(), pack.rope_sin.data_ptr(), pack.rope_len
+        self.folded = bool(getattr(model, "fold_head", False)) and pack.lm_w is not None
+        if self.folded:
+            fw, fb = pack.ensure_fold()
+            d.lm_fold_w, d.lm_fold_b = fw.data_ptr(), fb.data_ptr()
         self.desc = d
         c = _lib.PlanConfig()
         c.batch, c.num_steps, c.jumps = batch, num_steps, jumps
@@ -465,6 +482,12 @@ class FlashMapDraftModel(PreTrainedModel):
     # values derived from the weights are rebuilt after a move or a reload (:271-285)
     # "auto" and "kernels": the kernel sequence.  "persistent" (one launch per
     # batch-1, one-jump draft) is withdrawn: plan creation raises.
+    # fold_head: the serving plugins' fast mode (vllm/fold.py:76-100): the DiT
+    # head folded into the LM-head rows, one [S, D] projection of the final
+    # AdaLN output instead of the head and the [S, Ht] LM head (0.64 GB less
+    # per config-2 draft).  It changes rounding, so it is off by default and
+    # outside parity with the HF path.
+    fold_head = False
     launch_mode = "auto"
 
     def _clear_caches(self) -> None:
@@ -497,7 +520,7 @@ class FlashMapDraftModel(PreTrainedModel):
             self._plans = {}
         mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS,
                 "persistent": _lib.LAUNCH_PERSISTENT}[self.launch_mode]
-        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, pack.device)
+        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, bool(self.fold_head), pack.device)
         plan = self._plans.get(key)
         if plan is None or plan.max_extend_rows < extend_rows or plan.target_key != pack.target_key:
             rows = max(extend_rows, 2 * (plan.max_extend_rows if plan else 0), 64)

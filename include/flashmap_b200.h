@@ -390,6 +390,14 @@ typedef struct fm_model_desc {
   const float* rope_cos;     /* [rope_len, hd/2] */
   const float* rope_sin;
   int32_t rope_len;
+  /* Optional fast mode (the serving plugins' folded head, vllm/fold.py:76-100,
+   * sglang/model.py:515-531): lm_w rows x head_w as one [S, D] weight and its
+   * [S] bias (bf16 of the fp32 products).  When set, fm_draft's logits are
+   * the final AdaLN output times this weight — the DiT head is skipped (it
+   * still runs when fm_draft_io.hidden asks for the head output).  It changes
+   * rounding, so it sits outside parity with the reference's HF path. */
+  const void* lm_fold_w;
+  const void* lm_fold_b;
 } fm_model_desc;
 
 /* One jump of a draft: its modulations and noise-gate value. */

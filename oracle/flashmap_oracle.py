@@ -169,14 +169,26 @@ class Oracle:
 
     # -- forward, :302-313
     @torch.no_grad()
-    def forward(self, inputs_embeds, s: float, t: float, position_ids, context):
+    def forward(self, inputs_embeds, s: float, t: float, position_ids, context, head=None):
+        """``head`` = (weight, bias) replaces the DiT head (the folded head)."""
         layer_mods, final_mod = self.time_conditioning(s, t)
         rope = rope_tables(position_ids, self.head_dim, self.config.rope_theta)
         h = linear(inputs_embeds, self.p["x_embed.weight"], self.p["x_embed.bias"])
         for i in range(self.config.num_hidden_layers):
             h = self.layer(i, h, layer_mods[i], rope, context[i])
         h, _ = ada_layer_norm(h, final_mod, self.config.layer_norm_eps)
+        if head is not None:
+            return linear(h, *head)
         return linear(h, self.p["head.weight"], self.p["head.bias"])
+
+    def fold_head(self, lm_head_w):
+        """The serving plugins' folded head (vllm/fold.py:76-100): the state-vocab
+        rows of the LM head times the DiT head, and times its bias, in fp32,
+        rounded to the LM head's dtype."""
+        rows = lm_head_w if self.config.state_vocab_size is None else lm_head_w[self.p["draft_ids"]]
+        w = (rows.float() @ self.p["head.weight"].float()).to(lm_head_w.dtype)
+        b = (rows.float() @ self.p["head.bias"].float()).to(lm_head_w.dtype)
+        return w, b
 
     # -- extend_context, :342-351
     @torch.no_grad()
@@ -247,7 +259,7 @@ class Oracle:
     # -- draft, :422-479
     @torch.no_grad()
     def draft(self, anchor_ids, cache: OracleCache, embedding, lm_head_w, lm_head_b=None,
-              num_steps=None, z=None, noise=None, return_hidden=False):
+              num_steps=None, z=None, noise=None, return_hidden=False, folded=False):
         """Draft logits (B, K, V).  The random draws are inputs: ``z`` (B, K, H)
         for a one-step draft (what ``torch.randn`` gives at :465), ``noise``
         (B, K, S) fp32 for a multi-step draft (:469)."""
@@ -275,8 +287,12 @@ class Oracle:
         for s, t, nxt in [(a, b, b) for a, b in zip(grid[:-1], grid[1:])]:
             if state is not None:
                 inputs = self.embed_state(state, s, t, emb_s)
-            hidden = self.forward(inputs, s, t, positions, context).to(head_w.dtype)
-            logits = F.linear(hidden, head_w, head_b)
+            if folded:  # the serving plugins' folded head (no lm_head bias there)
+                logits = self.forward(inputs, s, t, positions, context, head=self.fold_head(lm_head_w))
+                hidden = None
+            else:
+                hidden = self.forward(inputs, s, t, positions, context).to(head_w.dtype)
+                logits = F.linear(hidden, head_w, head_b)
             if nxt < 1.0:
                 state = ((1.0 - nxt) * state + (nxt - s) * logits.float().softmax(dim=-1)) / (1.0 - s)
         out = self.token_logits(logits)

@@ -245,3 +245,46 @@ def test_ragged_batch_matches_per_sequence_oracle():
                 one = FlashMapCache(config, 1, max(lens) + K + 2, device=DEV, dtype=torch.bfloat16)
                 model.extend_context(one, ctx[b][None].to(DEV), E, W)
                 assert logits_rel_error(cache.kv[:, :, b, :, :n], one.kv[:, :, 0, :, :n]) < 1e-2
+
+
+@pytest.mark.parametrize("cfg,ctx_len", [(CONFIG1, 40), (CONFIG5S, 29)])
+def test_folded_head_matches_folded_oracle(cfg, ctx_len):
+    """The serving plugins' fast mode (vllm/fold.py:76-100): logits from the
+    DiT head folded into the LM-head rows, held to the oracle's folded draft
+    (same tolerances as the unfolded draft); the folded weights within one
+    bf16 ulp of the fp32 fold plus the fp32 accumulation error of a different
+    summation order (2^-20 of the sum of the products' magnitudes)."""
+    config, model, oracle, emb, head = build(cfg, seed=11)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    K = config.block_size
+    hidden = _context(config, ctx_len, 12)
+    cache = FlashMapCache(config, 1, ctx_len + K + 2, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(cache, hidden.to(DEV), E, W)
+    ocache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16)
+    oracle.extend_context(ocache, hidden)
+    model.fold_head = True
+    try:
+        rel, agree = [], []
+        for seed in range(4):
+            g = torch.Generator().manual_seed(100 + seed)
+            anchor = torch.randint(0, config.vocab_size, (1,), generator=g)
+            z = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+            got, tok = model.draft(anchor.to(DEV), cache, E, W, num_steps=1, z=z.to(DEV), return_tokens=True)
+            ref = oracle.draft(anchor, ocache, emb, head, num_steps=1, z=z, folded=True)
+            rel.append(logits_rel_error(got, ref))
+            agree.append(argmax_agreement(tok, ref)[0])
+        assert max(rel) <= LOGITS_RTOL, f"folded logits relative error {rel}"
+        assert min(agree) >= 0.875, f"folded argmax agreement {agree}"
+        pack = model._pack(DEV, E, W)
+        fw, fb = pack.ensure_fold()
+        rw, rb = oracle.fold_head(head)
+        rows = head.float() if config.state_vocab_size is None else head.float()[oracle.p["draft_ids"]]
+        mags = (rows.abs() @ oracle.p["head.weight"].float().abs(), rows.abs() @ oracle.p["head.bias"].float().abs())
+        for got_t, ref_t, mag, what in ((fw, rw, mags[0], "weight"), (fb, rb, mags[1], "bias")):
+            g32, r32 = got_t.float().cpu(), ref_t.float()
+            ulp = torch.pow(2.0, torch.floor(torch.log2(r32.abs().clamp_min(1e-30))) - 7)
+            tol = ulp + mag * 2.0 ** -20
+            assert ((g32 - r32).abs() <= tol).all(), f"folded {what} beyond tolerance"
+            assert (g32 == r32).float().mean().item() >= 0.99, f"folded {what} not 99% bit-equal"
+    finally:
+        model.fold_head = False
