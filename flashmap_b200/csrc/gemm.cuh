@@ -282,9 +282,28 @@ __device__ __forceinline__ void vec_epilogue16(const GemmArgs& a, const float* v
   named_bar_sync(1, 128);  // the exchange tile is refilled by the next chunk
 }
 
+// The [16 tokens][128 features] tile `xt` (bf16, shared) written to the
+// token-major output as 16-byte vectors, two per epilogue thread; then the
+// tile may be refilled.
+__device__ __forceinline__ void vec_store_tile(const GemmArgs& a, int m0, int n0, const __nv_bfloat16* xt) {
+  named_bar_sync(1, 128);
+  const int t = threadIdx.x - 64;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int idx = t + 128 * k, nl = idx >> 4, gi = idx & 15;
+    const int n = n0 + nl, mm = m0 + gi * 8;
+    if (n < a.N && mm < a.M)
+      *reinterpret_cast<uint4*>(a.out + (long long)n * a.ldo + mm) = *reinterpret_cast<const uint4*>(xt + nl * 128 + gi * 8);
+  }
+  named_bar_sync(1, 128);
+}
+
+// vec_xt (wide blocks, aligned output): QKNORM and unscattered LOGITS store
+// through this [16][128] shared tile as vectors instead of scalars.
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, int r, int m, int mt, int n0,
-                                           float* xch, unsigned long long* xch64, const float* pre = nullptr) {
+                                           float* xch, unsigned long long* xch64, const float* pre = nullptr,
+                                           __nv_bfloat16* vec_xt = nullptr) {
   const int lane = threadIdx.x & 31;
   const int q = (threadIdx.x >> 5) & 3;
   const bool mvalid = m < a.M;
@@ -432,6 +451,12 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
       }
       named_bar_sync(1, 128);  // xch is reused by the next chunk
     }
+    if (EPI == EPI_QKNORM && vec_xt != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) vec_xt[j * 128 + r] = f2bf(y[j]);
+      vec_store_tile(a, mt * 128, n0, vec_xt);
+      return;
+    }
     if (!mvalid) return;
     if constexpr (EPI == EPI_QKNORM) {
 #pragma unroll
@@ -464,16 +489,20 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
     for (int j = 0; j < 16; ++j) {
       const int n = n0 + j;
       const float y = round_bf(__fadd_rn(v[j], b));
-      if (mvalid && n < a.N) a.out[(long long)n * a.ldo + col] = f2bf(y);
+      if (vec_xt != nullptr)
+        vec_xt[j * 128 + r] = f2bf(y);
+      else if (mvalid && n < a.N)
+        a.out[(long long)n * a.ldo + col] = f2bf(y);
       if (!want_argmax) continue;
-      unsigned long long key = mvalid ? argmax_key(y, (uint32_t)id) : 0ull;
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) {
-        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-        key = other > key ? other : key;
-      }
-      if (lane == j) xch64[q * 16 + j] = key;
+      // warp max of the 64-bit key (value bits, then complement index) as two
+      // 32-bit reductions: the largest value, then among its holders the smallest index
+      const unsigned long long key = mvalid ? argmax_key(y, (uint32_t)id) : 0ull;
+      const uint32_t hi = (uint32_t)(key >> 32);
+      const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+      const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? (uint32_t)key : 0u);
+      if (lane == j) xch64[q * 16 + j] = ((unsigned long long)mh << 32) | ml;
     }
+    if (vec_xt != nullptr) vec_store_tile(a, mt * 128, n0, vec_xt);
     if (!want_argmax) return;
     named_bar_sync(1, 128);
     if (threadIdx.x >= 64 && threadIdx.x < 80) {
@@ -507,7 +536,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* fix_bar = reinterpret_cast<uint64_t*>(flags + 6);  // staged-partials barrier (8-byte aligned)
   uint8_t* scratch = smem + STAGES * (S::A_BYTES + S::B_BYTES) + S::BAR_BYTES;
   float* xch = reinterpret_cast<float*>(scratch);
-  unsigned long long* xch64 = reinterpret_cast<unsigned long long*>(scratch);
+  // the argmax keys sit past the 4 KB exchange tile, which the wide LOGITS path fills meanwhile
+  unsigned long long* xch64 = reinterpret_cast<unsigned long long*>(scratch + 4096);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long U = a.units;
@@ -663,6 +693,8 @@ __global__ void __launch_bounds__(192, 1)
       const bool whole = (seg_begin == (long long)tile * kb) && (seg_end == (long long)(tile + 1) * kb);
       const bool vec = VecEpilogue<BN, EPI>::ON && vec_epilogue_ok(a);
       __nv_bfloat16* xt = reinterpret_cast<__nv_bfloat16*>(xch);
+      constexpr bool XT_EPI = BN >= 64 && (EPI == EPI_QKNORM || EPI == EPI_LOGITS);
+      __nv_bfloat16* vxt = (XT_EPI && vec_epilogue_ok(a) && !(EPI == EPI_LOGITS && a.scatter)) ? xt : nullptr;
       __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(scratch + 4096 + 1024);
       if (whole && vec && EPI == EPI_RESID) {
         constexpr int NCH = BN / 16, RG = S::RING;
@@ -701,7 +733,7 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_x16(taddr + c0, v);
           const bool more = have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
           tmem_wait_ld();
-          epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
+          epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr, vxt);
           if (more) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) pre[j] = nxt[j];
@@ -798,7 +830,7 @@ __global__ void __launch_bounds__(192, 1)
                   }
                 }
                 if (!staged_ok) break;
-                epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, nullptr);
+                epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, nullptr, vxt);
               }
               cols = BN + 1;  // the staged rounds below are skipped
             }
@@ -867,7 +899,7 @@ __global__ void __launch_bounds__(192, 1)
                   vp[0] = vn[0];
                   vp[1] = vn[1];
                 } else {
-                  epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr);
+                  epilogue16<EPI>(a, v, r, m, mt, n0 + c0, xch, xch64, have ? pre : nullptr, vxt);
                 }
                 if (more) {
 #pragma unroll
