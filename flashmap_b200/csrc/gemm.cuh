@@ -283,9 +283,10 @@ __device__ __forceinline__ void vec_epilogue16(const GemmArgs& a, const float* v
 }
 
 // The [16 tokens][128 features] tile `xt` (bf16, shared) written to the
-// token-major output as 16-byte vectors, two per epilogue thread; then the
-// tile may be refilled.
-__device__ __forceinline__ void vec_store_tile(const GemmArgs& a, int m0, int n0, const __nv_bfloat16* xt) {
+// token-major output as 16-byte vectors, two per epilogue thread; then (with
+// refill_barrier) the tile may be refilled.
+__device__ __forceinline__ void vec_store_tile(const GemmArgs& a, int m0, int n0, const __nv_bfloat16* xt,
+                                               bool refill_barrier = true) {
   named_bar_sync(1, 128);
   const int t = threadIdx.x - 64;
 #pragma unroll
@@ -295,11 +296,12 @@ __device__ __forceinline__ void vec_store_tile(const GemmArgs& a, int m0, int n0
     if (n < a.N && mm < a.M)
       *reinterpret_cast<uint4*>(a.out + (long long)n * a.ldo + mm) = *reinterpret_cast<const uint4*>(xt + nl * 128 + gi * 8);
   }
-  named_bar_sync(1, 128);
+  if (refill_barrier) named_bar_sync(1, 128);
 }
 
 // vec_xt (wide blocks, aligned output): QKNORM and unscattered LOGITS store
-// through this [16][128] shared tile as vectors instead of scalars.
+// through [16][128] shared tiles as vectors instead of scalars (QKNORM: two
+// tiles from vec_xt on, alternating by chunk; LOGITS: one).
 template <int EPI>
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, int r, int m, int mt, int n0,
                                            float* xch, unsigned long long* xch64, const float* pre = nullptr,
@@ -368,14 +370,32 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
 #pragma unroll
     for (int j = 0; j < 16; ++j) y[j] = round_bf(v[j]);
     if (normed) {  // uniform branch over the whole tile
-      // per-head sum of squares: warp butterfly, then the head's warp quarters in order
+      const __nv_bfloat16* w;
+      if constexpr (EPI == EPI_QKNORM)
+        w = part == 0 ? a.norm_w0 : a.norm_w1;
+      else
+        w = a.norm_w0 + (long long)layer * a.norm_layer_stride;
+      const float wd = bf2f(w[d]);  // issued here: its latency hides under the reduction
+      // per-head sum of squares over the warp's 32 rows, all 16 tokens at once:
+      // each exchange step halves the tokens a lane holds (the half picked by
+      // the lane bit), 8 + 4 + 2 + 1 + 1 shuffles; lanes 2i and 2i+1 end with
+      // token tl's warp sum.  Then the head's warp quarters, in order.
+      float sq[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float s = __fmul_rn(y[j], y[j]);
+      for (int j = 0; j < 16; ++j) sq[j] = __fmul_rn(y[j], y[j]);
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-        if (lane == j) xch[q * 16 + j] = s;
+      for (int width = 8; width >= 1; width >>= 1) {
+        const bool up = (lane & (width * 2)) != 0;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+          const float send = up ? sq[i] : sq[i + width];
+          const float keep = up ? sq[i + width] : sq[i];
+          sq[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, width * 2));
+        }
       }
+      sq[0] = __fadd_rn(sq[0], __shfl_xor_sync(0xffffffffu, sq[0], 1));
+      const int tl = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+      if ((lane & 1) == 0) xch[q * 16 + tl] = sq[0];
       named_bar_sync(1, 128);
       const int hq = hd >> 5;  // warp quarters per head
       // one thread per (head of the tile, token) finishes the statistic: the
@@ -393,12 +413,6 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
       }
       named_bar_sync(1, 128);
       const int hrow = (q / hq) * 16;  // this thread's head's entries of xinv
-      const __nv_bfloat16* w;
-      if constexpr (EPI == EPI_QKNORM)
-        w = part == 0 ? a.norm_w0 : a.norm_w1;
-      else
-        w = a.norm_w0 + (long long)layer * a.norm_layer_stride;
-      const float wd = bf2f(w[d]);
       const int half = hd >> 1;
       float rc[16], rs[16];
       if (EPI == EPI_QKNORM && pre != nullptr) {
@@ -449,12 +463,18 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
           o = __fadd_rn(__fmul_rn(xn, cs), __fmul_rn(other, sn));
         y[j] = round_bf(o);
       }
-      named_bar_sync(1, 128);  // xch is reused by the next chunk
+      // xch is reused by the next chunk; on the vector path the store tile's
+      // barrier (after every thread's last xinv read) orders that instead
+      if (EPI != EPI_QKNORM || vec_xt == nullptr) named_bar_sync(1, 128);
     }
     if (EPI == EPI_QKNORM && vec_xt != nullptr) {
+      // two store tiles used alternately (chunk parity): a tile is rewritten
+      // two chunks later, after barriers that every thread reaches only once
+      // its vector stores from it are done
+      __nv_bfloat16* t = vec_xt + ((n0 >> 4) & 1) * 2048;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) vec_xt[j * 128 + r] = f2bf(y[j]);
-      vec_store_tile(a, mt * 128, n0, vec_xt);
+      for (int j = 0; j < 16; ++j) t[j * 128 + r] = f2bf(y[j]);
+      vec_store_tile(a, mt * 128, n0, t, false);
       return;
     }
     if (!mvalid) return;
@@ -694,8 +714,11 @@ __global__ void __launch_bounds__(192, 1)
       const bool vec = VecEpilogue<BN, EPI>::ON && vec_epilogue_ok(a);
       __nv_bfloat16* xt = reinterpret_cast<__nv_bfloat16*>(xch);
       constexpr bool XT_EPI = BN >= 64 && (EPI == EPI_QKNORM || EPI == EPI_LOGITS);
-      __nv_bfloat16* vxt = (XT_EPI && vec_epilogue_ok(a) && !(EPI == EPI_LOGITS && a.scatter)) ? xt : nullptr;
       __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(scratch + 4096 + 1024);
+      // QKNORM's two store tiles sit in the residual ring (idle for it)
+      __nv_bfloat16* vxt = (XT_EPI && vec_epilogue_ok(a) && !(EPI == EPI_LOGITS && a.scatter))
+                               ? (EPI == EPI_QKNORM ? ring : xt)
+                               : nullptr;
       if (whole && vec && EPI == EPI_RESID) {
         constexpr int NCH = BN / 16, RG = S::RING;
 #pragma unroll

@@ -76,6 +76,8 @@ GEMM_SHAPES = [
     (4096, 5, 4096),
     # wide blocks split over up to 8 CTAs per tile (head-CTA fix-up from staged partials)
     (2048, 256, 2048), (256, 96, 4096), (640, 64, 8192), (2048, 1024, 8192),
+    # at least two tiles per CTA over several column blocks: tiles relabelled column-major
+    (40000, 512, 256), (20000, 300, 512),
 ]
 
 
@@ -96,7 +98,8 @@ def test_gemm_store_bias(M, N, K):
     assert (out == ref).float().mean().item() > 0.98
 
 
-@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512), (256, 96, 4096)])
+@pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512), (256, 96, 4096),
+                                   (20000, 300, 512)])
 def test_gemm_fp32_and_determinism(M, N, K):
     W = rand((M, K), 1 / math.sqrt(K), 4)
     X = rand((N, K), 1.0, 5)
@@ -136,7 +139,7 @@ def test_gemm_swiglu(N):
 
 
 @pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (2048, 16, 8192), (256, 1024, 512), (2048, 256, 2048),
-                                   (2048, 1024, 8192)])
+                                   (2048, 1024, 8192), (16384, 640, 512)])
 def test_gemm_gated_residual(M, N, K):
     W = rand((M, K), 1 / math.sqrt(K), 12)
     X = rand((N, K), 1.0, 13)
