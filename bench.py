@@ -582,33 +582,45 @@ def run_ours(args, world, rank, local):
     lm_gbs = nbytes["lm_head"] / (lm_ms / 1000.0) / 1e9
     pass_gbs = nbytes["total"] / (ms_per_step / 1000.0) / 1e9
 
-    # the serving plugins' fast mode (DiT head folded into the LM-head rows;
-    # changes rounding, outside parity), the same draft reported beside the headline
-    folded = None
+    # the serving plugins' fast modes (changes rounding, outside parity), the same
+    # draft reported beside the headline: the DiT head folded into the LM-head
+    # rows, then that plus the eigen-folded noise
+    folded = folded_all = None
     if not args.profile_small:
         from flashmap_b200 import DraftSession
 
-        model.fold_head = True
-        fsession = DraftSession(model, cache, session.embed_tokens, session.lm_head, num_steps=1, seed=rank)
-        for _ in range(args.warmup):
-            fsession.replay()
-        torch.cuda.synchronize()
-        barrier(world)
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f_steps = max(args.steps // 4, 10)
-        f0.record(stream)
-        for _ in range(f_steps):
-            fsession.replay()
-        f1.record(stream)
-        torch.cuda.synchronize()
-        f_ms = max_over_ranks(f0.elapsed_time(f1), world) / f_steps
-        model.fold_head = False
-        fbytes = nbytes["total"] - nbytes["lm_head"] - CONFIG2["target_hidden_size"] * CONFIG2["hidden_size"] * 2 \
-            + CONFIG2["vocab_size"] * CONFIG2["hidden_size"] * 2
+        def time_folds(fold_head: bool, fold_noise: bool) -> float:
+            model.fold_head, model.fold_noise = fold_head, fold_noise
+            fsession = DraftSession(model, cache, session.embed_tokens, session.lm_head, num_steps=1, seed=rank)
+            for _ in range(args.warmup):
+                fsession.replay()
+            torch.cuda.synchronize()
+            barrier(world)
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f_steps = max(args.steps // 4, 10)
+            f0.record(stream)
+            for _ in range(f_steps):
+                fsession.replay()
+            f1.record(stream)
+            torch.cuda.synchronize()
+            model.fold_head = model.fold_noise = False
+            del fsession
+            return max_over_ranks(f0.elapsed_time(f1), world) / f_steps
+
+        c2 = CONFIG2
+        fbytes = nbytes["total"] - nbytes["lm_head"] - c2["target_hidden_size"] * c2["hidden_size"] * 2 \
+            + c2["vocab_size"] * c2["hidden_size"] * 2
+        f_ms = time_folds(True, False)
         folded = {"ms_per_step": f_ms, "value": world * K / (f_ms / 1000.0), "unit": "tokens/s",
                   "algorithmic_bytes": fbytes, "hbm_frac": fbytes / (f_ms / 1000.0) / 1e9 / peak,
                   "note": "fold_head fast mode (vllm/fold.py:76-100): outside parity with the HF path"}
-        del fsession
+        # the noise fold drops the [Ht, Ht] Cholesky factor (its [D, Ht] weight replaces x_embed's)
+        abytes = fbytes - c2["target_hidden_size"] ** 2 * 2
+        a_ms = time_folds(True, True)
+        folded_all = {"ms_per_step": a_ms, "value": world * K / (a_ms / 1000.0), "unit": "tokens/s",
+                      "algorithmic_bytes": abytes, "hbm_frac": abytes / (a_ms / 1000.0) / 1e9 / peak,
+                      "note": "fold_head + fold_noise fast mode (vllm/fold.py:44-100, sglang/model.py:945-958): "
+                              "outside parity with the HF path"}
 
     if rank != 0:
         return
@@ -639,6 +651,7 @@ def run_ours(args, world, rank, local):
     }
     if folded is not None:
         line["fast_mode_folded_head"] = folded
+        line["fast_mode_folded_head_and_noise"] = folded_all
     if args.profile_small:
         line["config"]["workload"] = "profiling case: config-2 layer shapes, 2 layers, 32768-row LM head"
     if world == 1 and not args.no_cpu_baseline and not args.profile_small:

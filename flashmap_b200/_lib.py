@@ -38,7 +38,7 @@ class ModelDesc(ctypes.Structure):
         + [(n, c_void_p) for n in ("embed", "lm_w", "lm_b", "draft_ids", "embed_state_t", "chol",
                                    "uniform_embeds", "state_norm_w", "rope_cos", "rope_sin")]
         + [("rope_len", c_int32)]
-        + [(n, c_void_p) for n in ("lm_fold_w", "lm_fold_b")]
+        + [(n, c_void_p) for n in ("lm_fold_w", "lm_fold_b", "noise_fold_w", "noise_fold_var", "noise_fold_x0")]
     )
 
 

@@ -527,6 +527,58 @@ __global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
                           a.gate));
 }
 
+// One CTA (NF_THREADS) per token: the variance-weighted sum of squares of its
+// noise row (each thread 8 consecutive entries per step, then the warps' xor
+// trees and the warps in order), then the scaled projection added to the
+// uniform posterior's embedded row, 8 features per thread per step.
+constexpr int NF_THREADS = 256;
+__global__ void __launch_bounds__(NF_THREADS) noise_fold_kernel(NoiseFoldArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[NF_THREADS / 32];
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const __nv_bfloat16* zr = a.z + (long long)t * a.Ht;
+  const __nv_bfloat16* pr = a.proj + (long long)t * a.D;
+  __nv_bfloat16* orow = a.out + (long long)t * a.D;
+  float acc = 0.0f;
+  if (a.Ht % 8 == 0 && vec_ok(zr) && vec_ok(a.var)) {
+    for (int c = threadIdx.x * 8; c < a.Ht; c += NF_THREADS * 8) {
+      float zf[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(zr + c), zf);
+      const float4 v0 = *reinterpret_cast<const float4*>(a.var + c);
+      const float4 v1 = *reinterpret_cast<const float4*>(a.var + c + 4);
+      const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(zf[e], zf[e]), vv[e]));
+    }
+  } else {
+    for (int c = threadIdx.x; c < a.Ht; c += NF_THREADS) {
+      const float zf = bf2f(zr[c]);
+      acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(zf, zf), a.var[c]));
+    }
+  }
+  acc = warp_allsum(acc);
+  if (lane == 0) red[warp] = acc;
+  __syncthreads();
+  float ms = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NF_THREADS / 32; ++w) ms = __fadd_rn(ms, red[w]);
+  const float scale = __fmul_rn(a.gate, __frsqrt_rn(__fadd_rn(ms, a.eps)));
+  if (a.D % 8 == 0 && vec_ok(pr) && vec_ok(a.x0) && vec_ok(orow)) {
+    for (int d = threadIdx.x * 8; d < a.D; d += NF_THREADS * 8) {
+      float pf[8], xf[8], o[8];
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(pr + d), pf);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(a.x0 + d), xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = __fadd_rn(xf[e], round_bf(__fmul_rn(scale, pf[e])));
+      *reinterpret_cast<uint4*>(orow + d) = pack_bf16x8(o);
+    }
+  } else {
+    for (int d = threadIdx.x; d < a.D; d += NF_THREADS)
+      orow[d] = f2bf(__fadd_rn(bf2f(a.x0[d]), round_bf(__fmul_rn(scale, bf2f(pr[d])))));
+  }
+}
+
 __global__ void philox_normal_bf16_kernel(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
                                           const uint32_t* offset_ptr) {
   pdl_wait();
@@ -1065,6 +1117,9 @@ fm_status launch_rope_gather(const int* positions, int T, const float* rope_cos,
 }
 fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl) {
   return launch_kernel(mix_state_kernel, dim3(blocks_for(a.T, ROWS_PER_CTA)), dim3(RT), 0, s, pdl, a);
+}
+fm_status launch_noise_fold(const NoiseFoldArgs& a, cudaStream_t s, bool pdl) {
+  return launch_kernel(noise_fold_kernel, dim3(a.T), dim3(NF_THREADS), 0, s, pdl, a);
 }
 fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
                                     const uint32_t* offset_ptr, cudaStream_t s, bool pdl) {

@@ -49,6 +49,21 @@ struct MixArgs {
 };
 fm_status launch_mix_state(const MixArgs& a, cudaStream_t s, bool pdl);
 
+// The eigen-folded noise's first-layer input (sglang/model.py:945-958): per
+// token t, scale = gate * rsqrt(sum_i var_i z_ti^2 + eps) and
+// out[t] = x0 + bf16(scale * proj[t]), proj = bf16(z W_fold^T) from the GEMM.
+struct NoiseFoldArgs {
+  const __nv_bfloat16* proj;  // [T, D]
+  const __nv_bfloat16* z;     // [T, Ht]
+  const float* var;           // [Ht] lam / Ht
+  const __nv_bfloat16* x0;    // [D] x_embed(state_norm(uniform))
+  __nv_bfloat16* out;         // [T, D]
+  float gate;                 // bf16-representable
+  float eps;
+  int T, D, Ht;
+};
+fm_status launch_noise_fold(const NoiseFoldArgs& a, cudaStream_t s, bool pdl);
+
 // offset_ptr (device, optional): its value is added to `offset` when the kernel runs
 fm_status launch_philox_normal_bf16(__nv_bfloat16* out, long long count, uint64_t seed, uint32_t offset,
                                     const uint32_t* offset_ptr, cudaStream_t s, bool pdl);

@@ -63,6 +63,8 @@ struct fm_plan {
   int *ext_seq, *ext_pos;
   // launch plans
   GemmPlan g_anchor_proj, g_anchor_kv, g_zl, g_xembed, g_head, g_lm;
+  GemmPlan g_nfold;   // eigen-folded noise: z times the folded weight (one-jump drafts)
+  bool noise_folded;
   GemmPlan g_state_first, g_state_next;
   std::vector<GemmPlan> g_layer;  // 6 per layer: qkv, o, q, cross_o, mlp1, mlp2
   CUtensorMap cache_map;
@@ -690,6 +692,13 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
   p->g_xembed.args.out = p->x;
   p->g_xembed.args.ldo = D;
   p->g_xembed.args.bias = static_cast<const __nv_bfloat16*>(m->x_embed_b);
+  p->noise_folded = p->has_target && c->num_steps == 1 && m->noise_fold_w && m->noise_fold_var && m->noise_fold_x0;
+  if (p->noise_folded) {
+    if ((st = gemm_prepare(&p->g_nfold, m->noise_fold_w, D, Ht, Ht, p->z, T, Ht, EPI_STORE, ws, gc, err)))
+      return fail(st);
+    p->g_nfold.args.out = p->attn;  // free until layer 0's attention
+    p->g_nfold.args.ldo = D;
+  }
   // layers
   p->g_layer.resize((size_t)L * 6);
   const int64_t mlp1_rows = m->swiglu ? 2 * (int64_t)p->I : p->I;
@@ -797,12 +806,13 @@ extern "C" fm_status fm_plan_lm_head(fm_plan* p, void* logits, int64_t ldl, fm_s
 
 namespace {
 
-fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s, bool with_head = true) {
+// embed: the first layer's input is x_embed(p->inputs) (else p->x is already it)
+fm_status run_dit(fm_plan* p, const fm_jump& j, cudaStream_t s, bool with_head = true, bool embed = true) {
   const fm_model_desc& m = p->m;
   const int T = p->T, D = p->D, L = p->L;
   const __nv_bfloat16* mods = static_cast<const __nv_bfloat16*>(j.mods);
   fm_status st;
-  if ((st = gemm_launch(p->g_xembed, s, true))) return st;
+  if (embed && (st = gemm_launch(p->g_xembed, s, true))) return st;
   for (int l = 0; l < L; ++l) {
     GemmPlan* g = &p->g_layer[(size_t)l * 6];
     const __nv_bfloat16* ms = mods + (size_t)(l * 3 + 0) * 3 * D;
@@ -943,7 +953,23 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
       } else if ((st = launch_philox_normal_bf16(p->z, (long long)T * Ht, io->seed, io->offset, io->offset_ptr, s, true))) {
         return st;
       }
-      if ((st = gemm_launch(p->g_zl, s, true))) return st;
+      if (p->noise_folded) {
+        if ((st = gemm_launch(p->g_nfold, s, true))) return st;
+        NoiseFoldArgs nf{};
+        nf.proj = p->attn;
+        nf.z = p->z;
+        nf.var = m.noise_fold_var;
+        nf.x0 = static_cast<const __nv_bfloat16*>(m.noise_fold_x0);
+        nf.out = p->x;
+        nf.gate = j.noise_gate;
+        nf.eps = m.rms_eps;
+        nf.T = T;
+        nf.D = p->D;
+        nf.Ht = Ht;
+        if ((st = launch_noise_fold(nf, s, true))) return st;
+      } else if ((st = gemm_launch(p->g_zl, s, true))) {
+        return st;
+      }
       mx.post = static_cast<const __nv_bfloat16*>(m.uniform_embeds);
       mx.post_stride = 0;
       mx.state = p->zl;
@@ -971,11 +997,12 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
         mx.state = p->semb;
       }
     }
-    if ((st = launch_mix_state(mx, s, true))) return st;
+    const bool nfold = n == 1 && p->noise_folded;  // the folded noise wrote layer 0's input
+    if (!nfold && (st = launch_mix_state(mx, s, true))) return st;
     const bool last = ji == n - 1;
     // the folded head reads the final AdaLN output; the DiT head then runs only for io->hidden
     const bool folded = m.lm_fold_w != nullptr;
-    if ((st = run_dit(p, j, s, !folded || (last && io->hidden)))) return st;
+    if ((st = run_dit(p, j, s, !folded || (last && io->hidden), !nfold))) return st;
     GemmPlan lm = p->g_lm;
     lm.args.col_ids = reinterpret_cast<const long long*>(m.draft_ids);  // token ids of the argmax
     if (last && io->logits) {

@@ -237,6 +237,7 @@ class _Pack:
         self.target_key = None
         self.embed = self.lm_w = self.lm_b = self.draft_ids = None
         self.lm_fold_w = self.lm_fold_b = None
+        self.noise_fold = None
         self.embed_state_t = self.uniform_embeds = self.chol = None
         self.rope_len = 0
         self.rope_cos = self.rope_sin = None
@@ -262,6 +263,7 @@ class _Pack:
             self.lm_b = None if head_b is None else head_b.detach().to(dev, bf).contiguous()
         self.S = e_s.shape[0]
         self.lm_fold_w = self.lm_fold_b = None
+        self.noise_fold = None
         self.embed_state_t = ops.transpose(e_s)  # E_S^T [H, S]
         uniform = torch.full((1, self.S), 1.0 / self.S, device=dev).to(bf)
         self.uniform_embeds = ops.gemm(self.embed_state_t, uniform).reshape(-1).contiguous()
@@ -282,6 +284,28 @@ class _Pack:
             b = ops.gemm(self.g["head.bias"].view(1, -1).contiguous(), self.lm_w)  # [S, 1]
             self.lm_fold_b = b.reshape(-1).contiguous()
         return self.lm_fold_w, self.lm_fold_b
+
+    def ensure_noise_fold(self, cfg):
+        """The serving plugins' eigen-folded noise (vllm/fold.py:44-73,
+        sglang/model.py:576-595), once per attached target: with
+        ``E_S^T E_S = Q diag(lam) Q^T`` (the Gram matrix in fp32 accumulation,
+        its eigen-decomposition in float64 on the device, negative round-off
+        eigenvalues clamped to 0), the weight ``W_x diag(w_noise) Q diag(sqrt
+        lam)`` [D, Ht] (float64 product rounded to bf16), ``lam / Ht`` [Ht]
+        (fp32) and ``x_embed(state_norm(uniform_embeds))`` [D] (bf16, the
+        reference's bf16 norm and linear)."""
+        if self.noise_fold is None:
+            g = self.g
+            gram = ops.gemm(self.embed_state_t, self.embed_state_t, ops.F32)  # E_S^T E_S
+            lam, basis = torch.linalg.eigh(gram.double())
+            lam = lam.clamp_min(0)
+            wx = g["x_embed.weight"].double() * g["noise_norm.weight"].double()[None, :]
+            weight = (wx @ (basis * lam.sqrt()[None, :])).to(torch.bfloat16).contiguous()
+            var = (lam / cfg.target_hidden_size).float().contiguous()
+            uniform = ops.rmsnorm(self.uniform_embeds.view(1, -1), g["state_norm.weight"], cfg.rms_norm_eps)
+            x0 = ops.gemm(g["x_embed.weight"], uniform, ops.STORE, bias=g["x_embed.bias"]).reshape(-1).contiguous()
+            self.noise_fold = (weight, var, x0)
+        return self.noise_fold
 
     def ensure_rope(self, cfg, max_pos: int):
         if max_pos > self.rope_len:
@@ -363,6 +387,10 @@ class _Plan:
         if self.folded:
             fw, fb = pack.ensure_fold()
             d.lm_fold_w, d.lm_fold_b = fw.data_ptr(), fb.data_ptr()
+        self.noise_folded = bool(getattr(model, "fold_noise", False)) and num_steps == 1 and pack.chol is not None
+        if self.noise_folded:
+            nw, nv, nx = pack.ensure_noise_fold(cfg)
+            d.noise_fold_w, d.noise_fold_var, d.noise_fold_x0 = nw.data_ptr(), nv.data_ptr(), nx.data_ptr()
         self.desc = d
         c = _lib.PlanConfig()
         c.batch, c.num_steps, c.jumps = batch, num_steps, jumps
@@ -488,6 +516,12 @@ class FlashMapDraftModel(PreTrainedModel):
     # per config-2 draft).  It changes rounding, so it is off by default and
     # outside parity with the HF path.
     fold_head = False
+    # fold_noise: the serving plugins' eigen-folded noise (vllm/fold.py:44-73,
+    # sglang/model.py:576-595), one-jump drafts only: the first layer's input
+    # from one [D, Ht] projection of the noise and a per-token scale, instead
+    # of the [Ht, Ht] Cholesky factor, the noise and state norms and x_embed.
+    # Same distribution from other draws: off by default, outside parity.
+    fold_noise = False
     launch_mode = "auto"
 
     def _clear_caches(self) -> None:
@@ -520,7 +554,8 @@ class FlashMapDraftModel(PreTrainedModel):
             self._plans = {}
         mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS,
                 "persistent": _lib.LAUNCH_PERSISTENT}[self.launch_mode]
-        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, bool(self.fold_head), pack.device)
+        key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, bool(self.fold_head),
+               bool(self.fold_noise), pack.device)
         plan = self._plans.get(key)
         if plan is None or plan.max_extend_rows < extend_rows or plan.target_key != pack.target_key:
             rows = max(extend_rows, 2 * (plan.max_extend_rows if plan else 0), 64)

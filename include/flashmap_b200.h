@@ -398,6 +398,19 @@ typedef struct fm_model_desc {
    * rounding, so it sits outside parity with the reference's HF path. */
   const void* lm_fold_w;
   const void* lm_fold_b;
+  /* Optional fast mode (the serving plugins' eigen-folded noise,
+   * vllm/fold.py:44-73, sglang/model.py:576-595), one-jump drafts only.
+   * With E_S^T E_S = Q diag(lam) Q^T: noise_fold_w = W_x diag(w_noise) Q
+   * diag(sqrt lam) [D, Ht] (bf16), noise_fold_var = lam / Ht [Ht] (fp32),
+   * noise_fold_x0 = x_embed(state_norm(uniform_embeds)) [D] (bf16).  When all
+   * three are set, a one-jump fm_draft forms the first layer's input as
+   * x0 + bf16(gate * rsqrt(sum(var z^2) + rms_eps) * bf16(z noise_fold_w^T))
+   * in place of x_embed(state_norm(u) + gate * noise_norm(z chol^T)): the
+   * same distribution from other draws, so outside parity with the HF path.
+   * Multi-jump drafts ignore these. */
+  const void* noise_fold_w;
+  const float* noise_fold_var;
+  const void* noise_fold_x0;
 } fm_model_desc;
 
 /* One jump of a draft: its modulations and noise-gate value. */

@@ -169,11 +169,16 @@ class Oracle:
 
     # -- forward, :302-313
     @torch.no_grad()
-    def forward(self, inputs_embeds, s: float, t: float, position_ids, context, head=None):
-        """``head`` = (weight, bias) replaces the DiT head (the folded head)."""
+    def forward(self, inputs_embeds, s: float, t: float, position_ids, context, head=None, embedded=None):
+        """``head`` = (weight, bias) replaces the DiT head (the folded head);
+        ``embedded`` is the first layer's input when it is formed outside
+        x_embed (the folded noise)."""
         layer_mods, final_mod = self.time_conditioning(s, t)
         rope = rope_tables(position_ids, self.head_dim, self.config.rope_theta)
-        h = linear(inputs_embeds, self.p["x_embed.weight"], self.p["x_embed.bias"])
+        if embedded is not None:
+            h = embedded.to(self.dtype)
+        else:
+            h = linear(inputs_embeds, self.p["x_embed.weight"], self.p["x_embed.bias"])
         for i in range(self.config.num_hidden_layers):
             h = self.layer(i, h, layer_mods[i], rope, context[i])
         h, _ = ada_layer_norm(h, final_mod, self.config.layer_norm_eps)
@@ -189,6 +194,38 @@ class Oracle:
         w = (rows.float() @ self.p["head.weight"].float()).to(lm_head_w.dtype)
         b = (rows.float() @ self.p["head.bias"].float()).to(lm_head_w.dtype)
         return w, b
+
+    def fold_noise(self, embedding, return_basis=False):
+        """The serving plugins' eigen-folded noise (vllm/fold.py:44-73,
+        sglang/model.py:576-595) for the state vocabulary's rows ``E`` of the
+        target embedding: ``E^T E = Q diag(lam) Q^T`` (the Gram matrix in fp32
+        as noise_factor accumulates it, eigh in float64, negative round-off
+        eigenvalues clamped to 0); ``weight = W_x diag(w_noise) Q diag(sqrt
+        lam)`` [D, H] in the embedding's dtype (the transpose of the
+        reference's ``M``), ``var = lam / H`` in fp32 and ``x0 =
+        x_embed(state_norm(uniform @ E))``."""
+        cfg, p = self.config, self.p
+        emb_s = embedding if cfg.state_vocab_size is None else embedding[p["draft_ids"]]
+        gram = sum(rows.float().T @ rows.float() for rows in emb_s.split(16384))
+        lam, basis = torch.linalg.eigh(gram.double())
+        lam = lam.clamp_min(0)
+        wx = p["x_embed.weight"].double() * p["noise_norm.weight"].double()[None, :]
+        weight = (wx @ (basis * lam.sqrt()[None, :])).to(embedding.dtype)
+        var = (lam / cfg.target_hidden_size).float()
+        uniform = rms_norm(self.target_constants(emb_s)[0].to(self.dtype), p["state_norm.weight"], cfg.rms_norm_eps)
+        x0 = linear(uniform, p["x_embed.weight"], p["x_embed.bias"]).reshape(-1).to(embedding.dtype)
+        fold = (weight, var, x0)
+        return (fold, lam, basis) if return_basis else fold
+
+    def folded_noise_input(self, z, fold, gate):
+        """The first layer's input from the folded noise (sglang/model.py:945-958):
+        ``x0 + (scale * (z @ M)).to(dtype)``, ``scale = gate * rsqrt(sum(var z^2)
+        + eps)`` per token in fp32, ``z @ M`` a matmul in the weight's dtype."""
+        weight, var, x0 = fold
+        mean_square = (z.float().square() * var).sum(-1, keepdim=True)
+        scale = gate.float() * torch.rsqrt(mean_square + self.config.rms_norm_eps)
+        proj = z.to(weight.dtype) @ weight.T
+        return x0 + (scale * proj.float()).to(weight.dtype)
 
     # -- extend_context, :342-351
     @torch.no_grad()
@@ -259,10 +296,12 @@ class Oracle:
     # -- draft, :422-479
     @torch.no_grad()
     def draft(self, anchor_ids, cache: OracleCache, embedding, lm_head_w, lm_head_b=None,
-              num_steps=None, z=None, noise=None, return_hidden=False, folded=False):
+              num_steps=None, z=None, noise=None, return_hidden=False, folded=False, noise_fold=None):
         """Draft logits (B, K, V).  The random draws are inputs: ``z`` (B, K, H)
         for a one-step draft (what ``torch.randn`` gives at :465), ``noise``
-        (B, K, S) fp32 for a multi-step draft (:469)."""
+        (B, K, S) fp32 for a multi-step draft (:469).  ``noise_fold`` (the
+        tuple ``fold_noise`` returns) forms a one-step draft's first layer
+        input by the folded noise instead."""
         cfg = self.config
         num_steps = num_steps or cfg.num_steps
         if str(num_steps) not in cfg.jump_grids:
@@ -277,7 +316,12 @@ class Oracle:
         positions = anchor + 1 + torch.arange(block, device=anchor_ids.device).expand(batch, -1)
 
         state = noise
-        if state is None and num_steps == 1:
+        embedded = None
+        if state is None and num_steps == 1 and noise_fold is not None:
+            jump = 1.0 if cfg.noise_gate == "constant" else grid[1] - grid[0]
+            gate = (self.p["noise_gate"].float() * jump).to(self.dtype)
+            embedded, inputs = self.folded_noise_input(z, noise_fold, gate), None
+        elif state is None and num_steps == 1:
             uniform_embeds, factor = self.target_constants(emb_s)
             inputs = self.mix_state(uniform_embeds, z.to(factor.dtype) @ factor.T, 0.0, grid[1])
         elif state is None:
@@ -288,10 +332,11 @@ class Oracle:
             if state is not None:
                 inputs = self.embed_state(state, s, t, emb_s)
             if folded:  # the serving plugins' folded head (no lm_head bias there)
-                logits = self.forward(inputs, s, t, positions, context, head=self.fold_head(lm_head_w))
+                logits = self.forward(inputs, s, t, positions, context, head=self.fold_head(lm_head_w),
+                                      embedded=embedded)
                 hidden = None
             else:
-                hidden = self.forward(inputs, s, t, positions, context).to(head_w.dtype)
+                hidden = self.forward(inputs, s, t, positions, context, embedded=embedded).to(head_w.dtype)
                 logits = F.linear(hidden, head_w, head_b)
             if nxt < 1.0:
                 state = ((1.0 - nxt) * state + (nxt - s) * logits.float().softmax(dim=-1)) / (1.0 - s)

@@ -288,3 +288,50 @@ def test_folded_head_matches_folded_oracle(cfg, ctx_len):
             assert (g32 == r32).float().mean().item() >= 0.99, f"folded {what} not 99% bit-equal"
     finally:
         model.fold_head = False
+
+
+@pytest.mark.parametrize("cfg,ctx_len", [(CONFIG1, 40), (CONFIG5S, 29)])
+def test_folded_noise_matches_folded_oracle(cfg, ctx_len):
+    """The eigen-folded noise (vllm/fold.py:44-73, sglang/model.py:945-958): a
+    one-jump draft whose first layer input is x0 + bf16(scale * z M), held to
+    the oracle's folded draft fed the library's own fold tensors (the
+    eigenbasis is defined up to signs), alone and with the folded head; the
+    library's fold checked by the basis-free identities weight weight^T =
+    W_x diag(w) E^T E diag(w) W_x^T and sum(var) = tr(E^T E) / H, and x0
+    against the oracle's."""
+    config, model, oracle, emb, head = build(cfg, seed=13)
+    E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
+    K = config.block_size
+    hidden = _context(config, ctx_len, 14)
+    cache = FlashMapCache(config, 1, ctx_len + K + 2, device=DEV, dtype=torch.bfloat16)
+    model.extend_context(cache, hidden.to(DEV), E, W)
+    ocache = OracleCache(config, 1, ctx_len + K + 2, torch.bfloat16)
+    oracle.extend_context(ocache, hidden)
+    model.fold_noise = True
+    try:
+        fold = tuple(t.cpu() for t in model._pack(DEV, E, W).ensure_noise_fold(config))
+        rel, agree = [], []
+        for seed in range(4):
+            g = torch.Generator().manual_seed(200 + seed)
+            anchor = torch.randint(0, config.vocab_size, (1,), generator=g)
+            z = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
+            model.fold_head = seed == 3
+            got, tok = model.draft(anchor.to(DEV), cache, E, W, num_steps=1, z=z.to(DEV), return_tokens=True)
+            ref = oracle.draft(anchor, ocache, emb, head, num_steps=1, z=z, noise_fold=fold, folded=seed == 3)
+            rel.append(logits_rel_error(got, ref))
+            agree.append(argmax_agreement(tok, ref)[0])
+        assert max(rel) <= LOGITS_RTOL, f"folded-noise logits relative error {rel}"
+        assert min(agree) >= 0.875, f"folded-noise argmax agreement {agree}"
+    finally:
+        model.fold_noise = model.fold_head = False
+    weight, var, x0 = fold
+    rows = emb if config.state_vocab_size is None else emb[oracle.p["draft_ids"]]
+    gram = rows.double().T @ rows.double()
+    wx = oracle.p["x_embed.weight"].double() * oracle.p["noise_norm.weight"].double()[None, :]
+    want = wx @ gram @ wx.T
+    got_g = weight.double() @ weight.double().T
+    assert float((got_g - want).abs().max() / want.abs().max()) < 2e-2
+    tr = float(torch.trace(gram)) / config.target_hidden_size
+    assert abs(float(var.double().sum()) - tr) < 1e-3 * tr
+    rx0 = oracle.fold_noise(emb)[2]
+    assert float((x0.float() - rx0.float()).abs().max() / rx0.float().abs().max()) < 1e-2
