@@ -1225,6 +1225,28 @@ extern "C" fm_status fm_mix_state(const void* post, int64_t post_stride, const v
   return launch_mix_state(a, as_stream(stream), false);
 }
 
+extern "C" fm_status fm_noise_fold(const void* proj, const void* z, const float* var, const void* x0, void* out,
+                                   float gate, float eps, int64_t rows, int64_t cols, int64_t noise_cols,
+                                   fm_stream stream) {
+  if (rows < 0 || cols < 1 || noise_cols < 1) return set_error(FM_ERR_SHAPE, "noise_fold: bad shape");
+  if (rows == 0) return FM_OK;
+  if (!proj || !z || !var || !x0 || !out) return set_error(FM_ERR_INVALID, "noise_fold: null pointer");
+  if (rows > INT32_MAX || cols > INT32_MAX || noise_cols > INT32_MAX)
+    return set_error(FM_ERR_SHAPE, "noise_fold: dimension too large");
+  NoiseFoldArgs a{};
+  a.proj = static_cast<const __nv_bfloat16*>(proj);
+  a.z = static_cast<const __nv_bfloat16*>(z);
+  a.var = var;
+  a.x0 = static_cast<const __nv_bfloat16*>(x0);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.gate = gate;
+  a.eps = eps;
+  a.T = (int)rows;
+  a.D = (int)cols;
+  a.Ht = (int)noise_cols;
+  return launch_noise_fold(a, as_stream(stream), false);
+}
+
 extern "C" fm_status fm_block_self_attn(const void* qkv, void* out, int64_t batch, int64_t block, int64_t heads,
                                         int64_t head_dim, fm_stream stream) {
   if (!qkv || !out) return set_error(FM_ERR_INVALID, "self_attn: null pointer");

@@ -262,6 +262,7 @@ class _Pack:
             self.lm_w = head_w.detach().to(dev, bf).contiguous()
             self.lm_b = None if head_b is None else head_b.detach().to(dev, bf).contiguous()
         self.S = e_s.shape[0]
+        self.lm_rows_full = (self.lm_w, self.lm_b)  # before any plugin cuts the head to a draft vocabulary
         self.lm_fold_w = self.lm_fold_b = None
         self.noise_fold = None
         self.embed_state_t = ops.transpose(e_s)  # E_S^T [H, S]

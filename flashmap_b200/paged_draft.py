@@ -3,14 +3,16 @@ cache, on this library's kernels.  The vLLM and sglang plugin models
 (``vllm_model``, ``sglang_model``) drive it; each engine supplies how the
 query rows are rotated and how they attend to its cache.
 
-The arithmetic is the HF path's (modeling_flashmap.py:302-313, 378-420,
-459-475): noise ``z @ L^T`` through the Cholesky factor of ``E^T E``,
+Unfolded, the arithmetic is the HF path's (modeling_flashmap.py:302-313,
+378-420, 459-475): noise ``z @ L^T`` through the Cholesky factor of ``E^T E``,
 ``state_norm(uniform) + bf16(gate * noise_norm(.))``, ``x_embed``, the DiT
 layers, the final AdaLN, and for logits the DiT head followed by the target's
-LM head.  The reference plugins fold the noise and the head into single
-projections (vllm/fold.py:44-100, sglang/model.py:515-595), which changes
-the rounding; this module keeps the unfolded order, so a plugin draft equals
-an HF-path draft of the same context and noise.
+LM head.  The reference plugins fold both ends into single projections
+(vllm/fold.py:44-100, sglang/model.py:515-595, 945-958), which changes the
+rounding: ``fold_head`` maps the final AdaLN output straight to logits through
+the LM-head rows times the DiT head, ``fold_noise`` forms the first layer's
+input from the noise's eigenbasis projection.  The plugin models choose the
+folds their reference counterparts use.
 """
 
 from __future__ import annotations
@@ -30,8 +32,9 @@ class PagedDraft:
     """The drafter's weights in kernel layout (the HF model's pack) and the
     per-jump constants, with the passes the plugin models compose."""
 
-    def __init__(self, model, device):
+    def __init__(self, model, device, fold_head: bool = False, fold_noise: bool = False):
         self.model = model
+        self.fold_head, self.fold_noise = fold_head, fold_noise
         self.cfg = cfg = model.config
         self.pack = model._pack(torch.device(device))
         self.D, self.H = cfg.hidden_size, cfg.num_attention_heads
@@ -44,6 +47,16 @@ class PagedDraft:
     def attach(self, embedding: torch.Tensor, lm_head_weight: torch.Tensor, lm_head_bias=None) -> None:
         """The target's embedding and LM head (modeling_flashmap.py:355-368, 401-420)."""
         self.pack.attach_target(embedding, lm_head_weight, lm_head_bias)
+
+    def restrict_lm_rows(self, rows: torch.Tensor) -> None:
+        """Cut the LM head to ``rows`` of the attached head (a draft vocabulary
+        over the full state vocabulary), always from the full head so that a
+        repeated ``prepare`` cuts once; the folded head is rebuilt from it."""
+        p = self.pack
+        w, b = p.lm_rows_full
+        p.lm_w = w[rows].contiguous()
+        p.lm_b = None if b is None else b[rows].contiguous()
+        p.lm_fold_w = p.lm_fold_b = None
 
     @property
     def attached(self) -> bool:
@@ -108,8 +121,18 @@ class PagedDraft:
 
     def first_hidden(self, z: torch.Tensor, s: float, t: float) -> torch.Tensor:
         """``x_embed(state_norm(uniform) + bf16(gate * noise_norm(z @ L^T)))``
-        (modeling_flashmap.py:393-399, 459-468)."""
+        (modeling_flashmap.py:393-399, 459-468); with ``fold_noise``,
+        ``x0 + bf16(gate * rsqrt(sum(var z^2) + eps) * (z @ M))``
+        (sglang/model.py:945-958)."""
         p, T = self.pack, z.shape[0]
+        if self.fold_noise:
+            weight, var, x0 = p.ensure_noise_fold(self.cfg)
+            proj = ops.gemm(weight, z.contiguous())
+            out = torch.empty(T, self.D, device=p.device, dtype=torch.bfloat16)
+            _lib.call("fm_noise_fold", ops._p(proj), ops._p(z.contiguous()), ops._p(var), ops._p(x0), ops._p(out),
+                      float(p.noise_gate_value(self.cfg, s, t)), float(self.cfg.rms_norm_eps), T, self.D, self.Ht,
+                      ops._stream())
+            return out
         zl = ops.gemm(p.chol, z.contiguous())
         inputs = torch.empty(T, self.Ht, device=p.device, dtype=torch.bfloat16)
         gate = p.noise_gate_value(self.cfg, s, t)
@@ -161,6 +184,11 @@ class PagedDraft:
         return ops.gemm(self.pack.lm_w, hidden.contiguous(), bias=self.pack.lm_b)
 
     def draft_logits(self, final: torch.Tensor) -> torch.Tensor:
+        """Draft-vocabulary logits from the final AdaLN output: the DiT head then
+        the LM head, or with ``fold_head`` their product (vllm/fold.py:76-100)."""
+        if self.fold_head:
+            weight, bias = self.pack.ensure_fold()
+            return ops.gemm(weight, final.contiguous(), bias=bias)
         return self.logits(self.head(final))
 
 

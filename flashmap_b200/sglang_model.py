@@ -17,11 +17,13 @@ forward batch are read by attribute, through the hooks ``token_to_kv_pool``
 and ``req_to_token`` (callables; by default sglang's own getters), so the
 model runs inside sglang or against stand-ins.
 
-Differences from the reference plugin: the draft is the HF path's unfolded
-arithmetic (``paged_draft``: no folded head or folded noise, so
-``folded_head`` stays None and ``head_logits`` applies the DiT head and the
-LM head in turn); one jump per block; no tree drafting or FP8 weights; the
-``FLASHMAP_COMPILE`` settings are accepted and have no effect.
+Like the reference plugin, the DiT head is folded into the LM-head rows
+(``folded_head`` = (weight, bias), ``lm_head`` holds them and ``head_logits``
+applies them to the final AdaLN output; sglang/model.py:449-513), and
+``FLASHMAP_FOLDED_NOISE=1`` draws the noise in the embedding's eigenbasis
+through one projection (``folded_noise``; sglang/model.py:576-595, 945-958).
+Differences from the reference plugin: one jump per block; no tree drafting or
+FP8 weights; the ``FLASHMAP_COMPILE`` settings are accepted and have no effect.
 """
 
 from __future__ import annotations
@@ -116,6 +118,7 @@ class FlashMapDraftModel(FlashMapDiT):
         self.embedding = None
         self.hot_ids = None
         self.folded_head = None
+        self.folded_noise = os.environ.get("FLASHMAP_FOLDED_NOISE", "0") == "1"
         self.num_steps = int(os.environ.get("FLASHMAP_NUM_STEPS") or fm.num_steps)
         why = unsupported_steps(self.num_steps)
         if why:
@@ -186,11 +189,12 @@ class FlashMapDraftModel(FlashMapDiT):
         elif self.draft_vocab_size:
             ranking = self._vocab_ranking[: self.draft_vocab_size].to(device=device, dtype=torch.int64)
             self.hot_ids = ranking.sort().values
-        self._core = core = PagedDraft(self, device)
+        self._core = core = PagedDraft(self, device, fold_head=True, fold_noise=self.folded_noise)
         core.attach(self.embedding, lm_head_weight)
         if self.hot_ids is not None and not state_vocab:
-            core.pack.lm_w = core.pack.lm_w[self.hot_ids].contiguous()
-        self.lm_head = _Head(core.pack.lm_w, core.pack.lm_b, self.vocab_size)
+            core.restrict_lm_rows(self.hot_ids)
+        self.folded_head = core.pack.ensure_fold()
+        self.lm_head = _Head(*self.folded_head, self.vocab_size)
         self.markov_head.hot_ids = self.hot_ids
         (self._s, self._t, _), = core.jump(self.num_steps)
         self._mods = core.modulations(self._s, self._t)
@@ -201,8 +205,8 @@ class FlashMapDraftModel(FlashMapDiT):
         return self._core
 
     def head_logits(self, hidden: torch.Tensor) -> torch.Tensor:
-        """The draft-vocabulary logits of the DiT's output: the DiT head, then
-        the target's LM head rows."""
+        """The draft-vocabulary logits of the DiT's final AdaLN output through
+        the folded head (the target's LM-head rows times the DiT head)."""
         return self._require_core().draft_logits(hidden.reshape(-1, self.dim))
 
     # --- DSPARK protocol ------------------------------------------------------

@@ -17,11 +17,14 @@ set to a callable returning the forward context; by default it is vLLM's
 context cache; vLLM binds them (``bind_cache_layers``) once it has allocated
 the KV cache.
 
-Differences from the reference plugin: the draft is the HF path's unfolded
-arithmetic (``paged_draft``), so it equals ``FlashMapDraftModel.draft`` of the
-same context and noise; one jump per block (``FLASHMAP_NUM_STEPS`` > 1
-raises); ``compile`` is accepted and has no effect (the kernels are already
-whole; CUDA graphs capture them); FP8 weights (``FLASHMAP_FP8``) are not built.
+Like the reference plugin, the draft folds both ends (vllm/fold.py:44-100):
+the noise is drawn in the embedding's eigenbasis and reaches the first layer
+through one projection, and the DiT head is folded into the LM-head rows, so
+a draft equals ``FlashMapDraftModel.draft`` with ``fold_noise`` and
+``fold_head`` set, of the same context and noise.  Differences from the
+reference plugin: one jump per block (``FLASHMAP_NUM_STEPS`` > 1 raises);
+``compile`` is accepted and has no effect (the kernels are already whole; CUDA
+graphs capture them); FP8 weights (``FLASHMAP_FP8``) are not built.
 """
 
 from __future__ import annotations
@@ -261,13 +264,11 @@ class FlashMapDraftModel(nn.Module):
         self.hot_ids = None
         if self.d2t is not None:
             self.hot_ids = torch.arange(self.d2t.shape[0], device=device) + self.d2t.to(device)
-        self._core = core = PagedDraft(self.model, device)
+        self._core = core = PagedDraft(self.model, device, fold_head=True, fold_noise=True)
         core.attach(embed, head, getattr(self.lm_head, "bias", None))
         if self.hot_ids is not None and not self.state_vocab_size:
             # a restricted head over the full state vocabulary: only the LM-head rows are cut
-            pack = core.pack
-            pack.lm_w = pack.lm_w[self.hot_ids].contiguous()
-            pack.lm_b = None if pack.lm_b is None else pack.lm_b[self.hot_ids].contiguous()
+            core.restrict_lm_rows(self.hot_ids)
         self.num_heads, self.head_dim = core.H, core.hd
         self.dim = core.D
         self.softmax_scale = self.head_dim ** -0.5
@@ -440,5 +441,6 @@ class FlashMapDraftModel(nn.Module):
 
     def compute_draft_logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
         """Logits over the draft vocabulary (``hot_ids`` when restricted): the
-        DiT head, then the target's LM head rows."""
+        final AdaLN output times the target's LM-head rows folded with the DiT
+        head (vllm/fold.py:76-100)."""
         return self._require_core().draft_logits(hidden_states)

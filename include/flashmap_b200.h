@@ -126,6 +126,14 @@ FM_API fm_status fm_mix_state(const void* post, int64_t post_stride, const void*
                               const void* noise_norm_w, void* out, float gate, float eps, int64_t rows, int64_t cols,
                               fm_stream stream);
 
+/* Eigen-folded noise, first layer input (sglang/model.py:945-958): per row t,
+ * scale = gate * rsqrt(sum_i var_i z[t,i]^2 + eps) and out[t] = bf16(x0 +
+ * bf16(scale * proj[t])); proj [rows, cols] = z [rows, noise_cols] times the
+ * fold weight (fm_model_desc.noise_fold_w), var [noise_cols] fp32, x0 [cols]. */
+FM_API fm_status fm_noise_fold(const void* proj, const void* z, const float* var, const void* x0, void* out,
+                               float gate, float eps, int64_t rows, int64_t cols, int64_t noise_cols,
+                               fm_stream stream);
+
 /* Self-attention over the block slots (modeling_flashmap.py:188 with :144-147);
  * qkv [B*K, 3*D] with q, k already normed and rotated. Replaces the
  * flashmap_vllm::block_self_attention / flashmap_sglang::block_self_attention ops. */

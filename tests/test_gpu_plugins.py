@@ -1,8 +1,11 @@
 """The vLLM and sglang plugin models on the GPU against stand-in engines: the
 context written through each engine's paged layout, one draft step, and the
 draft logits compared with the CPU oracle's draft of the same context and
-noise (zero noise: ``noise_scale`` / ``noise_temperature`` 0, as the
-reference's own comparisons of deterministic drafts do).
+noise.  The plugins fold like their reference counterparts (vLLM: the head
+and the noise; sglang: the head, the noise with ``FLASHMAP_FOLDED_NOISE``),
+so the oracle drafts folded too, fed the plugin's own noise-fold tensors (the
+eigenbasis is defined up to signs).  The noise rows are given: each test
+replaces the plugin core's noise draw with fixed normals.
 
 Tolerances are the north star's: logits within 2e-2 of the reference's
 scale, and argmax agreement (tie-aware) of at least 0.875 per block.
@@ -33,12 +36,12 @@ def _contexts(config, lengths, seed):
     return [torch.randn(n, width, generator=g).to(torch.bfloat16) for n in lengths]
 
 
-def _oracle_logits(config, oracle, emb, head, hidden, anchor):
+def _oracle_logits(config, oracle, emb, head, hidden, anchor, z, noise_fold):
     K = config.block_size
     oc = OracleCache(config, 1, hidden.shape[0] + K + 2, torch.bfloat16)
     oracle.extend_context(oc, hidden[None])
-    z = torch.zeros(1, K, config.target_hidden_size, dtype=torch.bfloat16)
-    ref = oracle.draft(torch.tensor([anchor]), oc, emb, head, num_steps=1, z=z)[0]
+    ref = oracle.draft(torch.tensor([anchor]), oc, emb, head, num_steps=1, z=z[None], folded=True,
+                       noise_fold=noise_fold)[0]
     if config.state_vocab_size:
         ref = ref[:, oracle.p["draft_ids"].long()] if "draft_ids" in oracle.p else ref
     return ref
@@ -74,9 +77,12 @@ def test_vllm_plugin_draft_matches_oracle(cfg):
     layers = [SimpleNamespace(kv_cache=c, layer_name=f"ctx.{i}", kv_cache_dtype="auto") for i, c in enumerate(caches)]
     vm.bind_cache_layers(layers)
     vm.prepare()
-    vm.noise_scale = 0.0
-
     lengths = [40, 23, 130]
+    gz = torch.Generator().manual_seed(16)
+    z = torch.randn(len(lengths) * K, config.target_hidden_size, generator=gz).to(torch.bfloat16)
+    vm._core.noise = lambda *args, **kwargs: z.to(DEV)
+    fold = tuple(t.cpu() for t in vm._core.pack.ensure_noise_fold(config))
+
     hiddens = _contexts(config, lengths, 5)
     g = torch.Generator().manual_seed(6)
     cols = (max(lengths) + K + PAGE) // PAGE
@@ -106,19 +112,25 @@ def test_vllm_plugin_draft_matches_oracle(cfg):
     logits = vm.compute_draft_logits(hidden)
     torch.cuda.synchronize()
     for r, (n, h) in enumerate(zip(lengths, hiddens)):
-        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]))
+        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]), z[r * K:(r + 1) * K], fold)
         _check(config, logits[r * K:(r + 1) * K], ref, f"vllm request {r}")
 
 
 @pytest.mark.parametrize("cfg", [CONFIG1, CONFIG5S])
-def test_sglang_plugin_draft_matches_oracle(cfg):
+@pytest.mark.parametrize("folded_noise", [False, True])
+def test_sglang_plugin_draft_matches_oracle(cfg, folded_noise):
     config, model, oracle, emb, head = build(cfg, seed=7)
     K, H, hd, L = config.block_size, config.num_attention_heads, config.hidden_size // config.num_attention_heads, \
         config.num_hidden_layers
     sm = SG.FlashMapDraftModel(config).to(DEV, torch.bfloat16)
     sm.load_weights(model.state_dict().items())
+    sm.folded_noise = folded_noise  # FLASHMAP_FOLDED_NOISE, read at construction
     sm.attach_shared_modules(embed_tokens=Emb(emb.to(DEV)), lm_head=Head(head.to(DEV)))
-    sm.noise_temperature = 0.0
+    assert sm.folded_head is not None and sm.lm_head.weight.shape[1] == config.hidden_size
+    gz = torch.Generator().manual_seed(17)
+    z = torch.randn(2 * K, config.target_hidden_size, generator=gz).to(torch.bfloat16)
+    sm._core.noise = lambda *args, **kwargs: z.to(DEV)
+    fold = tuple(t.cpu() for t in sm._core.pack.ensure_noise_fold(config)) if folded_noise else None
     rows = 1024
     kb = [torch.zeros(rows, H, hd, dtype=torch.bfloat16, device=DEV) for _ in range(L)]
     vb = [torch.zeros(rows, H, hd, dtype=torch.bfloat16, device=DEV) for _ in range(L)]
@@ -142,5 +154,5 @@ def test_sglang_plugin_draft_matches_oracle(cfg):
     logits, _ = sm.compute_base_logits(out.hidden_states)
     torch.cuda.synchronize()
     for r, (n, h) in enumerate(zip(lengths, hiddens)):
-        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]))
+        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]), z[r * K:(r + 1) * K], fold)
         _check(config, logits[r * K:(r + 1) * K], ref, f"sglang request {r}")
