@@ -110,6 +110,10 @@ _SIGNATURES = {
     "fm_rope_table": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "fm_philox_normal": (c_int, [c_void_p, c_int64, c_uint64, c_uint32, c_void_p]),
     "fm_philox_normal_rows": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
+    "fm_philox_normal_rows_f32": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_float,
+                                          c_void_p]),
+    "fm_state_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_float, c_int32, c_void_p]),
+    "fm_state_update": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_float, c_float, c_float, c_void_p]),
     "fm_noise_fold": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float, c_int64, c_int64,
                               c_int64, c_void_p]),
     "fm_mix_state": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float, c_int64,

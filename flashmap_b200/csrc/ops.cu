@@ -608,9 +608,12 @@ __global__ void philox_normal_f32_kernel(float* out, long long count, uint64_t s
 // Row r of n_cols normals keyed by its request's seed and its position:
 // seed = seeds[rows[r]] (0 when rows[r] < 0), counter offset = positions[r];
 // pair p of the row uses counter (p, 0, offset, 4) like philox_normal.
-__global__ void philox_normal_rows_kernel(__nv_bfloat16* out, long long n_rows, long long n_cols,
-                                          const long long* seeds, const long long* rows, const long long* positions,
-                                          float scale) {
+__device__ __forceinline__ void put_val(__nv_bfloat16* p, float v) { *p = f2bf(v); }
+__device__ __forceinline__ void put_val(float* p, float v) { *p = v; }
+
+template <typename OutT>
+__global__ void philox_normal_rows_kernel(OutT* out, long long n_rows, long long n_cols, const long long* seeds,
+                                          const long long* rows, const long long* positions, float scale) {
   const long long half = (n_cols + 1) / 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= n_rows * half) return;
@@ -619,9 +622,9 @@ __global__ void philox_normal_rows_kernel(__nv_bfloat16* out, long long n_rows, 
   const uint64_t seed = st >= 0 ? (uint64_t)seeds[st] : 0ull;
   float z0, z1;
   normal_pair(seed, (uint32_t)positions[r], p, z0, z1);
-  __nv_bfloat16* o = out + r * n_cols;
-  o[2 * p] = f2bf(__fmul_rn(z0, scale));
-  if (2 * p + 1 < n_cols) o[2 * p + 1] = f2bf(__fmul_rn(z1, scale));
+  OutT* o = out + r * n_cols;
+  put_val(o + 2 * p, __fmul_rn(z0, scale));
+  if (2 * p + 1 < n_cols) put_val(o + 2 * p + 1, __fmul_rn(z1, scale));
 }
 
 __global__ void argmax_tokens_kernel(const unsigned long long* keys, int64_t* tokens, int n) {
@@ -1200,9 +1203,43 @@ extern "C" fm_status fm_philox_normal_rows(void* out, int64_t n_rows, int64_t n_
   if (n_rows == 0 || n_cols == 0) return FM_OK;
   if (!out || !seeds || !rows || !positions) return set_error(FM_ERR_INVALID, "philox_normal_rows: null pointer");
   const long long pairs = n_rows * ((n_cols + 1) / 2);
-  return launch_kernel(philox_normal_rows_kernel, dim3(blocks_for(pairs, 256)), dim3(256), 0, as_stream(stream),
-                       false, bf(out), (long long)n_rows, (long long)n_cols, reinterpret_cast<const long long*>(seeds),
-                       reinterpret_cast<const long long*>(rows), reinterpret_cast<const long long*>(positions), scale);
+  return launch_kernel(philox_normal_rows_kernel<__nv_bfloat16>, dim3(blocks_for(pairs, 256)), dim3(256), 0,
+                       as_stream(stream), false, bf(out), (long long)n_rows, (long long)n_cols,
+                       reinterpret_cast<const long long*>(seeds), reinterpret_cast<const long long*>(rows),
+                       reinterpret_cast<const long long*>(positions), scale);
+}
+
+extern "C" fm_status fm_philox_normal_rows_f32(float* out, int64_t n_rows, int64_t n_cols, const int64_t* seeds,
+                                               const int64_t* rows, const int64_t* positions, float scale,
+                                               fm_stream stream) {
+  if (n_rows < 0 || n_cols < 0) return set_error(FM_ERR_SHAPE, "philox_normal_rows_f32: bad shape");
+  if (n_rows == 0 || n_cols == 0) return FM_OK;
+  if (!out || !seeds || !rows || !positions) return set_error(FM_ERR_INVALID, "philox_normal_rows_f32: null pointer");
+  const long long pairs = n_rows * ((n_cols + 1) / 2);
+  return launch_kernel(philox_normal_rows_kernel<float>, dim3(blocks_for(pairs, 256)), dim3(256), 0,
+                       as_stream(stream), false, out, (long long)n_rows, (long long)n_cols,
+                       reinterpret_cast<const long long*>(seeds), reinterpret_cast<const long long*>(rows),
+                       reinterpret_cast<const long long*>(positions), scale);
+}
+
+extern "C" fm_status fm_state_rows(const float* state, void* out, int64_t rows, int64_t cols, float evidence,
+                                   int32_t with_posterior, fm_stream stream) {
+  if (rows < 0 || cols < 1) return set_error(FM_ERR_SHAPE, "state_rows: bad shape");
+  if (rows == 0) return FM_OK;
+  if (!state || !out) return set_error(FM_ERR_INVALID, "state_rows: null pointer");
+  if (rows > INT32_MAX || cols > INT32_MAX) return set_error(FM_ERR_SHAPE, "state_rows: dimension too large");
+  return launch_state_rows(state, bf(out), (int)rows, (int)cols, evidence, with_posterior ? 1 : 0,
+                           as_stream(stream), false);
+}
+
+extern "C" fm_status fm_state_update(float* state, const void* logits, int64_t ldl, int64_t rows, int64_t cols,
+                                     float keep, float step, float denom, fm_stream stream) {
+  if (rows < 0 || cols < 1 || ldl < cols) return set_error(FM_ERR_SHAPE, "state_update: bad shape");
+  if (rows == 0) return FM_OK;
+  if (!state || !logits) return set_error(FM_ERR_INVALID, "state_update: null pointer");
+  if (rows > INT32_MAX || cols > INT32_MAX) return set_error(FM_ERR_SHAPE, "state_update: dimension too large");
+  return launch_state_update(state, static_cast<const __nv_bfloat16*>(logits), ldl, (int)rows, (int)cols, keep, step,
+                             denom, as_stream(stream), false);
 }
 
 extern "C" fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,

@@ -280,11 +280,16 @@ class _Pack:
         sglang/model.py:515-531): ``lm_w @ head_w`` [S, D] and ``lm_w @ head_b``
         [S], fp32 accumulation rounded to bf16, once per attached target."""
         if self.lm_fold_w is None:
-            head_t = ops.transpose(self.g["head.weight"])  # [D, Ht]
-            self.lm_fold_w = ops.gemm(head_t, self.lm_w).contiguous()  # [S, D]
-            b = ops.gemm(self.g["head.bias"].view(1, -1).contiguous(), self.lm_w)  # [S, 1]
-            self.lm_fold_b = b.reshape(-1).contiguous()
+            self.lm_fold_w, self.lm_fold_b = self.fold_rows(self.lm_w)
         return self.lm_fold_w, self.lm_fold_b
+
+    def fold_rows(self, rows_w: torch.Tensor):
+        """``rows_w @ head_w`` [R, D] and ``rows_w @ head_b`` [R] (fp32
+        accumulation, bf16) for LM-head rows ``rows_w`` [R, Ht]."""
+        head_t = ops.transpose(self.g["head.weight"])  # [D, Ht]
+        w = ops.gemm(head_t, rows_w).contiguous()
+        b = ops.gemm(self.g["head.bias"].view(1, -1).contiguous(), rows_w)  # [R, 1]
+        return w, b.reshape(-1).contiguous()
 
     def ensure_noise_fold(self, cfg):
         """The serving plugins' eigen-folded noise (vllm/fold.py:44-73,

@@ -80,6 +80,72 @@ class PagedDraft:
     def modulations(self, s: float, t: float) -> torch.Tensor:
         return self.pack.modulations(self.cfg, s, t)
 
+    # -------------------------------------------------------------- several jumps
+    def state_noise(self, tokens: int, seeds=None, rows=None, positions=None, scale: float = 1.0,
+                    seed: int = 0, offset: int = 0) -> torch.Tensor:
+        """The starting state ``(tokens, S)`` fp32 of a multi-jump draft: keyed
+        per row like ``noise`` (vllm/model.py:968-975), else one Philox stream
+        (seed, counter offset + row)."""
+        dev, S = self.pack.device, self.pack.S
+        out = torch.empty(tokens, S, device=dev, dtype=torch.float32)
+        if seeds is None:
+            seeds = torch.tensor([seed], device=dev, dtype=torch.int64)
+            rows = torch.zeros(tokens, device=dev, dtype=torch.int64)
+            positions = offset + torch.arange(tokens, device=dev, dtype=torch.int64)
+        s64 = seeds.to(torch.int64).contiguous()
+        r64 = rows[:tokens].to(torch.int64).contiguous()
+        p64 = positions[:tokens].to(torch.int64).contiguous()
+        _lib.call("fm_philox_normal_rows_f32", ops._p(out), tokens, S, ops._p(s64), ops._p(r64), ops._p(p64),
+                  float(scale), ops._stream())
+        return out
+
+    def embed_state(self, state: torch.Tensor, s: float, t: float) -> torch.Tensor:
+        """``x_embed(state_norm(softmax(e state) @ E) + bf16(gate * noise_norm(state @
+        E)))`` of the fp32 state at jump (s, t), ``e = s / max(1 - s, 1e-3)^2``;
+        at s = 0 the posterior is uniform (modeling_flashmap.py:378-420,
+        vllm/model.py:944-956)."""
+        p = self.pack
+        T, S = state.shape
+        with_post = s != 0.0
+        evidence = s / max(1.0 - s, 1e-3) ** 2 if with_post else 0.0
+        rows = torch.empty(2 * T if with_post else T, S, device=p.device, dtype=torch.bfloat16)
+        _lib.call("fm_state_rows", ops._p(state.contiguous()), ops._p(rows), T, S, float(evidence),
+                  1 if with_post else 0, ops._stream())
+        semb = ops.gemm(p.embed_state_t, rows)  # [2T or T, Ht]
+        if with_post:
+            post, stride, st = semb[:T], self.Ht, semb[T:]
+        else:
+            post, stride, st = p.uniform_embeds, 0, semb
+        inputs = torch.empty(T, self.Ht, device=p.device, dtype=torch.bfloat16)
+        _lib.call("fm_mix_state", ops._p(post), stride, ops._p(st), ops._p(p.g["state_norm.weight"]),
+                  ops._p(p.g["noise_norm.weight"]), ops._p(inputs), float(p.noise_gate_value(self.cfg, s, t)),
+                  float(self.cfg.rms_norm_eps), T, self.Ht, ops._stream())
+        return ops.gemm(p.g["x_embed.weight"], inputs, bias=p.g["x_embed.bias"])
+
+    def jump_logits(self, final: torch.Tensor) -> torch.Tensor:
+        """A jump's prediction logits over every state row (the jump head: the
+        LM head folded with the DiT head with ``fold_head``, vllm/model.py:578-585;
+        else the DiT head then the LM head), whatever draft vocabulary cut the
+        drafting head."""
+        p = self.pack
+        full_w, full_b = p.lm_rows_full
+        if self.fold_head:
+            if p.lm_w is full_w:
+                w, b = p.ensure_fold()
+            else:
+                if getattr(self, "_jump_fold", None) is None or self._jump_fold[0] is not full_w:
+                    self._jump_fold = (full_w, p.fold_rows(full_w))
+                w, b = self._jump_fold[1]
+            return ops.gemm(w, final.contiguous(), bias=b)
+        return ops.gemm(full_w, self.head(final), bias=full_b)
+
+    def state_update(self, state: torch.Tensor, logits: torch.Tensor, s: float, nxt: float) -> None:
+        """``state = ((1 - next) state + (next - s) softmax(logits)) / (1 - s)`` in
+        place (modeling_flashmap.py:470-472)."""
+        T, S = state.shape
+        _lib.call("fm_state_update", ops._p(state), ops._p(logits), logits.stride(0), T, S, float(1.0 - nxt),
+                  float(nxt - s), float(1.0 - s), ops._stream())
+
     # -------------------------------------------------------------- context rows
     def combine(self, hidden_states: torch.Tensor) -> torch.Tensor:
         """``fc`` of the target's features (modeling_flashmap.py:322-340)."""

@@ -22,8 +22,7 @@ the noise is drawn in the embedding's eigenbasis and reaches the first layer
 through one projection, and the DiT head is folded into the LM-head rows, so
 a draft equals ``FlashMapDraftModel.draft`` with ``fold_noise`` and
 ``fold_head`` set, of the same context and noise.  Differences from the
-reference plugin: one jump per block (``FLASHMAP_NUM_STEPS`` > 1 raises);
-``compile`` is accepted and has no effect (the kernels are already whole; CUDA
+reference plugin: ``compile`` is accepted and has no effect (the kernels are already whole; CUDA
 graphs capture them); FP8 weights (``FLASHMAP_FP8``) are not built.
 """
 
@@ -38,7 +37,7 @@ from torch import nn
 
 from . import serving_ops as S
 from .modeling_flashmap import FlashMapDraftModel as _HFModel
-from .paged_draft import PagedDraft, unsupported_steps
+from .paged_draft import PagedDraft
 
 __all__ = ["ContextCachePlan", "FlashMapDraftModel", "attend_by_segments", "plan_context_cache"]
 
@@ -154,7 +153,8 @@ class FlashMapDraftModel(nn.Module):
         self.max_model_len = int(vllm_config.model_config.max_model_len)
         self.block_size = int(config.block_size)
         self.num_steps = int(os.environ.get("FLASHMAP_NUM_STEPS", config.num_steps))
-        why = unsupported_steps(self.num_steps)
+        why = None if str(self.num_steps) in config.jump_grids else (
+            f"no jump grid for {self.num_steps} steps (the checkpoint has {sorted(config.jump_grids, key=int)})")
         if why:
             raise ValueError(why)
         self.cache_plan = self._context_plan(config, vllm_config)
@@ -274,8 +274,8 @@ class FlashMapDraftModel(nn.Module):
         self.softmax_scale = self.head_dim ** -0.5
         self._check_attention()
         self.segments = self.cache_plan.segments
-        (self._s, self._t, _), = core.jump(self.num_steps)
-        self.modulations = core.modulations(self._s, self._t)
+        self._jumps = core.jump(self.num_steps)
+        self.modulations = [core.modulations(s, t) for s, t, _ in self._jumps]
         self.cos_sin = core.rope_pairs(self.max_model_len + self.block_size + 1)
         self.context_k_norm = core.pack.cross_k_norm
 
@@ -387,7 +387,7 @@ class FlashMapDraftModel(nn.Module):
                 inputs_embeds: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Blocks of ``block_size`` rows, each opened by its request's anchor
         (vllm/model.py:991-1041): the anchors' (and any deferred) context rows
-        are written, then one jump of the DiT over the paged context; returns
+        are written, then the jumps of the DiT over the paged context; returns
         the final AdaLN output ``(tokens, dim)``."""
         del inputs_embeds
         core = self._require_core()
@@ -423,8 +423,6 @@ class FlashMapDraftModel(nn.Module):
         seeds = rows = None
         if self._noise_keys is not None:
             seeds, rows = self._noise_keys
-        z = core.noise(tokens, seeds, rows, positions, self.noise_scale)
-        x = core.first_hidden(z, self._s, self._t)
         p = core.pack
 
         def self_attention(qkv, layer):
@@ -437,7 +435,18 @@ class FlashMapDraftModel(nn.Module):
             return S.vllm_rms_norm_rope(q, p.layers[layer]["cross_q_norm"], self.cos_sin, slot_positions,
                                         self.config.qk_norm_eps)
 
-        return core.dit(x, self.modulations, self_attention, rotate, attend)
+        if self.num_steps == 1:
+            (s, t, _), = self._jumps
+            z = core.noise(tokens, seeds, rows, positions, self.noise_scale)
+            return core.dit(core.first_hidden(z, s, t), self.modulations[0], self_attention, rotate, attend)
+        # several jumps (the reference algorithm, a vocabulary-sized state;
+        # vllm/model.py:1020-1040): the state moves to the next grid time between them
+        state = core.state_noise(tokens, seeds, rows, positions, self.noise_scale)
+        for step, (s, t, nxt) in enumerate(self._jumps):
+            hidden = core.dit(core.embed_state(state, s, t), self.modulations[step], self_attention, rotate, attend)
+            if step + 1 < len(self._jumps):
+                core.state_update(state, core.jump_logits(hidden), s, nxt)
+        return hidden
 
     def compute_draft_logits(self, hidden_states: torch.Tensor) -> torch.Tensor:
         """Logits over the draft vocabulary (``hot_ids`` when restricted): the

@@ -120,6 +120,25 @@ FM_API fm_status fm_philox_normal(void* out, int64_t count, uint64_t seed, uint3
 FM_API fm_status fm_philox_normal_rows(void* out, int64_t n_rows, int64_t n_cols, const int64_t* seeds,
                                        const int64_t* rows, const int64_t* positions, float scale, fm_stream stream);
 
+/* fp32 form of fm_philox_normal_rows (the vocabulary-sized starting state of a
+ * multi-jump draft, vllm/model.py:968-975). */
+FM_API fm_status fm_philox_normal_rows_f32(float* out, int64_t n_rows, int64_t n_cols, const int64_t* seeds,
+                                           const int64_t* rows, const int64_t* positions, float scale,
+                                           fm_stream stream);
+
+/* Multi-jump state featurisation rows (modeling_flashmap.py:378-391,
+ * vllm/model.py:944-956): for rows t of the fp32 state [rows, cols], out gets
+ * bf16(state) at row rows + t and, with with_posterior, bf16(softmax(evidence *
+ * state)) at row t (fixed-order max and sum); without, bf16(state) at row t.
+ * out [rows or 2*rows, cols] is the GEMM operand against E_S^T. */
+FM_API fm_status fm_state_rows(const float* state, void* out, int64_t rows, int64_t cols, float evidence,
+                               int32_t with_posterior, fm_stream stream);
+
+/* Jump update (modeling_flashmap.py:470-472): state = (keep * state + step *
+ * softmax(logits)) / denom per row, logits bf16 [rows, ldl] (first cols used). */
+FM_API fm_status fm_state_update(float* state, const void* logits, int64_t ldl, int64_t rows, int64_t cols,
+                                 float keep, float step, float denom, fm_stream stream);
+
 /* One-jump input mix (modeling_flashmap.py:393-399): out = bf16(state_norm(post) +
  * bf16(gate * noise_norm(state))), post rows post_stride apart (0: one shared row). */
 FM_API fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,

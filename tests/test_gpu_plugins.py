@@ -36,12 +36,15 @@ def _contexts(config, lengths, seed):
     return [torch.randn(n, width, generator=g).to(torch.bfloat16) for n in lengths]
 
 
-def _oracle_logits(config, oracle, emb, head, hidden, anchor, z, noise_fold):
+def _oracle_logits(config, oracle, emb, head, hidden, anchor, z, noise_fold, steps=1, state=None):
     K = config.block_size
     oc = OracleCache(config, 1, hidden.shape[0] + K + 2, torch.bfloat16)
     oracle.extend_context(oc, hidden[None])
-    ref = oracle.draft(torch.tensor([anchor]), oc, emb, head, num_steps=1, z=z[None], folded=True,
-                       noise_fold=noise_fold)[0]
+    if steps == 1:
+        ref = oracle.draft(torch.tensor([anchor]), oc, emb, head, num_steps=1, z=z[None], folded=True,
+                           noise_fold=noise_fold)[0]
+    else:
+        ref = oracle.draft(torch.tensor([anchor]), oc, emb, head, num_steps=steps, noise=state[None], folded=True)[0]
     if config.state_vocab_size:
         ref = ref[:, oracle.p["draft_ids"].long()] if "draft_ids" in oracle.p else ref
     return ref
@@ -59,8 +62,12 @@ def _check(config, got, ref, what):
 
 
 @pytest.mark.parametrize("cfg", [CONFIG1, CONFIG5S])
-def test_vllm_plugin_draft_matches_oracle(cfg):
+@pytest.mark.parametrize("steps", [1, 2])
+def test_vllm_plugin_draft_matches_oracle(cfg, steps):
+    """One jump (folded noise and head) or two (the exact vocabulary-sized state,
+    the folded jump head) against the oracle's draft of the same noise."""
     config, model, oracle, emb, head = build(cfg, seed=4)
+    config.num_steps = steps
     K, H, hd, L = config.block_size, config.num_attention_heads, config.hidden_size // config.num_attention_heads, \
         config.num_hidden_layers
     vconf = SimpleNamespace(parallel_config=SimpleNamespace(tensor_parallel_size=1), use_v2_model_runner=True,
@@ -81,6 +88,8 @@ def test_vllm_plugin_draft_matches_oracle(cfg):
     gz = torch.Generator().manual_seed(16)
     z = torch.randn(len(lengths) * K, config.target_hidden_size, generator=gz).to(torch.bfloat16)
     vm._core.noise = lambda *args, **kwargs: z.to(DEV)
+    state = torch.randn(len(lengths) * K, vm._core.pack.S, generator=gz)
+    vm._core.state_noise = lambda *args, **kwargs: state.to(DEV).clone()
     fold = tuple(t.cpu() for t in vm._core.pack.ensure_noise_fold(config))
 
     hiddens = _contexts(config, lengths, 5)
@@ -112,8 +121,9 @@ def test_vllm_plugin_draft_matches_oracle(cfg):
     logits = vm.compute_draft_logits(hidden)
     torch.cuda.synchronize()
     for r, (n, h) in enumerate(zip(lengths, hiddens)):
-        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]), z[r * K:(r + 1) * K], fold)
-        _check(config, logits[r * K:(r + 1) * K], ref, f"vllm request {r}")
+        ref = _oracle_logits(config, oracle, emb, head, h, int(anchors[r]), z[r * K:(r + 1) * K], fold, steps,
+                             state[r * K:(r + 1) * K])
+        _check(config, logits[r * K:(r + 1) * K], ref, f"vllm request {r} ({steps} jumps)")
 
 
 @pytest.mark.parametrize("cfg", [CONFIG1, CONFIG5S])
