@@ -81,6 +81,15 @@ class RopeView(ctypes.Structure):
                 ("rows", c_int64)]
 
 
+class BankJump(ctypes.Structure):
+    _fields_ = [("noise_embed", c_void_p), ("mean_embed", c_void_p), ("log_mass", c_void_p), ("embed", c_void_p),
+                ("state_map", c_void_p), ("bank_rows", c_int64), ("state_rows", c_int64), ("hidden", c_int64),
+                ("slots", c_int64), ("rows", c_void_p), ("seeds", c_void_p), ("ids", c_void_p), ("probs", c_void_p),
+                ("betas", c_void_p), ("support", c_int32), ("topk", c_int32), ("alpha", c_float),
+                ("evidence", c_float), ("slope", c_float), ("temperature", c_float), ("out", c_void_p),
+                ("err", c_void_p)]
+
+
 class PagedAttn(ctypes.Structure):
     _fields_ = [("q", c_void_p), ("q_dtype", c_int32), ("q_token_stride", c_int64), ("q_head_stride", c_int64),
                 ("cu_seqlens_q", c_void_p), ("q_per_request", c_int64), ("max_q", c_int64),
@@ -130,6 +139,13 @@ _SIGNATURES = {
     "fm_paged_attn_nsplit": (c_int32, [c_int64, c_int64, c_int64, c_int64, c_int32]),
     "fm_paged_attn_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int32]),
     "fm_paged_cross_attn": (c_int, [ctypes.POINTER(PagedAttn), c_void_p]),
+    "fm_bank_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int32, c_void_p]),
+    "fm_topk_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                             c_void_p, c_void_p]),
+    "fm_bank_gather": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p]),
+    "fm_bank_jump_rows": (c_int, [ctypes.POINTER(BankJump), c_void_p]),
+    "fm_token_normals": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    "fm_philox_randint": (c_int, [c_void_p, c_int64, c_int64, c_uint64, c_uint32, c_uint32, c_void_p]),
     "fm_write_context_kv_paged": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                           c_void_p, c_int32, RopeView, c_void_p, c_int64, c_int64, c_int64,
                                           c_int64, c_int64, c_int64, c_int64, c_float, c_void_p, c_void_p,

@@ -17,7 +17,10 @@ folds their reference counterparts use.
 
 from __future__ import annotations
 
-from typing import Callable, Optional
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Tuple
+
+import ctypes
 
 import torch
 
@@ -25,6 +28,40 @@ from . import _lib, ops
 from .configuration_flashmap import jump_times
 
 Rotate = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+def bank_coefficients(grid) -> list:
+    """Per jump n: (alpha_n, [beta_n1 .. beta_nn]), the coefficients of the
+    starting noise and of each earlier prediction in the state x_n, from the
+    jump update x <- ((1 - t) x + (t - s) delta) / (1 - s) (jump_bank.py:76-86)."""
+    out, alpha, betas = [(1.0, [])], 1.0, []
+    for start, end in zip(grid[:-2], grid[1:-1]):
+        keep = (1.0 - float(end)) / (1.0 - float(start))
+        alpha *= keep
+        betas = [b * keep for b in betas] + [(float(end) - float(start)) / (1.0 - float(start))]
+        out.append((alpha, list(betas)))
+    return out
+
+
+@dataclass
+class JumpBank:
+    """A noise bank (jump_bank.py:95-150): ``size`` draws z over the state
+    vocabulary with what the later jumps read of them — ``noise_embed`` [size,
+    Ht] = z @ E, and per later jump n ``mean_embed[n-1]`` [size, Ht] =
+    softmax(a_n z) @ E and ``log_mass[n-1]`` [size] = logsumexp(a_n z) —
+    with the per-jump constants (coefficients, e_n, a_n)."""
+    grid: list
+    size: int
+    temperature: float
+    coefficients: list
+    evidence: list
+    slopes: list
+    noise_embed: torch.Tensor
+    mean_embed: torch.Tensor
+    log_mass: torch.Tensor
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.noise_embed, self.mean_embed, self.log_mass))
 Attend = Callable[[torch.Tensor, int], torch.Tensor]
 
 
@@ -109,7 +146,8 @@ class PagedDraft:
         with_post = s != 0.0
         evidence = s / max(1.0 - s, 1e-3) ** 2 if with_post else 0.0
         rows = torch.empty(2 * T if with_post else T, S, device=p.device, dtype=torch.bfloat16)
-        _lib.call("fm_state_rows", ops._p(state.contiguous()), ops._p(rows), T, S, float(evidence),
+        state_c = state.contiguous()  # referenced until the launch below
+        _lib.call("fm_state_rows", ops._p(state_c), ops._p(rows), T, S, float(evidence),
                   1 if with_post else 0, ops._stream())
         semb = ops.gemm(p.embed_state_t, rows)  # [2T or T, Ht]
         if with_post:
@@ -145,6 +183,115 @@ class PagedDraft:
         T, S = state.shape
         _lib.call("fm_state_update", ops._p(state), ops._p(logits), logits.stride(0), T, S, float(1.0 - nxt),
                   float(nxt - s), float(1.0 - s), ops._stream())
+
+    # -------------------------------------------------------------- banked jumps
+    def build_bank(self, grid, size: int, temperature: float, seed: int = 0, chunk: int = 128) -> JumpBank:
+        """The noise bank of a banked multi-jump draft (jump_bank.py:104-150):
+        bank row i draws z = temperature * N(0, I_S) from the Philox stream of
+        (seed, i), so a row does not depend on the chunking; z @ E and the per
+        jump softmax(a_n z) @ E are GEMMs against E_S^T."""
+        p, S, Ht = self.pack, self.pack.S, self.Ht
+        grid = [float(t) for t in grid]
+        coefficients = bank_coefficients(grid)
+        evidence = [t / (1.0 - t) ** 2 for t in grid[1:len(grid) - 1]]
+        slopes = [e * coefficients[n + 1][0] for n, e in enumerate(evidence)]
+        nj = len(slopes)
+        if nj > 8:
+            raise ValueError("a banked draft takes at most 9 jumps")
+        dev = p.device
+        noise_embed = torch.empty(size, Ht, device=dev, dtype=torch.bfloat16)
+        mean_embed = torch.empty(nj, size, Ht, device=dev, dtype=torch.bfloat16)
+        log_mass = torch.empty(nj, size, device=dev, dtype=torch.float32)
+        slope_arr = (ctypes.c_float * 8)(*slopes)
+        seeds = torch.tensor([seed], device=dev, dtype=torch.int64)
+        for start in range(0, size, chunk):
+            rows = min(chunk, size - start)
+            z = torch.empty(rows, S, device=dev, dtype=torch.float32)
+            zeros = torch.zeros(rows, device=dev, dtype=torch.int64)
+            index = start + torch.arange(rows, device=dev, dtype=torch.int64)
+            _lib.call("fm_philox_normal_rows_f32", ops._p(z), rows, S, ops._p(seeds), ops._p(zeros), ops._p(index),
+                      float(temperature), ops._stream())
+            zb = torch.empty(rows, S, device=dev, dtype=torch.bfloat16)
+            probs = torch.empty(max(nj, 1), rows, S, device=dev, dtype=torch.bfloat16)
+            mass = torch.empty(max(nj, 1), rows, device=dev, dtype=torch.float32)
+            _lib.call("fm_bank_rows", ops._p(z), ops._p(zb), ops._p(probs), ops._p(mass), rows, S,
+                      ctypes.cast(slope_arr, ctypes.c_void_p), nj, ops._stream())
+            ops.gemm(p.embed_state_t, zb, out=noise_embed[start:start + rows])
+            for j in range(nj):
+                ops.gemm(p.embed_state_t, probs[j], out=mean_embed[j, start:start + rows])
+                log_mass[j, start:start + rows] = mass[j]
+        return JumpBank(grid, int(size), float(temperature), coefficients, evidence, slopes, noise_embed, mean_embed,
+                        log_mass)
+
+    def bank_draw(self, slots: int, bank: JumpBank, seed: int, offset: int) -> Tuple[torch.Tensor, torch.Tensor]:
+        """A bank row and a slot seed per slot (jump_bank.py:157-161), from the
+        Philox stream (seed, offset)."""
+        dev = self.pack.device
+        rows = torch.empty(slots, device=dev, dtype=torch.int64)
+        seeds = torch.empty(slots, device=dev, dtype=torch.int64)
+        _lib.call("fm_philox_randint", ops._p(rows), slots, bank.size, seed, offset & 0xFFFFFFFF, 5, ops._stream())
+        _lib.call("fm_philox_randint", ops._p(seeds), slots, 2 ** 31 - 1, seed, offset & 0xFFFFFFFF, 6,
+                  ops._stream())
+        return rows, seeds
+
+    def _embed_rows(self, post, post_stride: int, state, s: float, t: float) -> torch.Tensor:
+        p, T = self.pack, state.shape[0]
+        inputs = torch.empty(T, self.Ht, device=p.device, dtype=torch.bfloat16)
+        _lib.call("fm_mix_state", ops._p(post), post_stride, ops._p(state), ops._p(p.g["state_norm.weight"]),
+                  ops._p(p.g["noise_norm.weight"]), ops._p(inputs), float(p.noise_gate_value(self.cfg, s, t)),
+                  float(self.cfg.rms_norm_eps), T, self.Ht, ops._stream())
+        return ops.gemm(p.g["x_embed.weight"], inputs, bias=p.g["x_embed.bias"])
+
+    def bank_first_input(self, bank: JumpBank, rows: torch.Tensor, s: float, t: float) -> torch.Tensor:
+        """``x_embed(state_norm(uniform) + gate * noise_norm(noise_embed[rows]))``
+        (jump_bank.py:164-169): jump 0 from the bank rows' noise."""
+        p, R = self.pack, rows.shape[0]
+        rows = rows.contiguous()
+        noise = torch.empty(R, self.Ht, device=p.device, dtype=torch.bfloat16)
+        _lib.call("fm_bank_gather", ops._p(bank.noise_embed), bank.size, self.Ht, ops._p(rows), R, ops._p(noise),
+                  None, ops._stream())
+        return self._embed_rows(p.uniform_embeds, 0, noise, s, t)
+
+    def bank_jump_rows(self, bank: JumpBank, n: int, rows: torch.Tensor, seeds: torch.Tensor,
+                       supports: List[Tuple[torch.Tensor, torch.Tensor]]) -> torch.Tensor:
+        """Jump n's posterior and noise rows [2R, Ht] before the norms
+        (jump_bank.py:171-205) over the earlier predictions' supports."""
+        p, R = self.pack, rows.shape[0]
+        rows, seeds = rows.contiguous(), seeds.contiguous()  # referenced until the launch below
+        ids = torch.cat([i for i, _ in supports], dim=1).to(torch.int64).contiguous()
+        probs = torch.cat([q for _, q in supports], dim=1).float().contiguous()
+        alpha, betas = bank.coefficients[n]
+        beta_t = torch.tensor(betas, device=p.device, dtype=torch.float32)
+        out = torch.empty(2 * R, self.Ht, device=p.device, dtype=torch.bfloat16)
+        a = _lib.BankJump()
+        a.noise_embed, a.mean_embed = bank.noise_embed.data_ptr(), bank.mean_embed[n - 1].data_ptr()
+        a.log_mass, a.embed = bank.log_mass[n - 1].data_ptr(), p.embed.data_ptr()
+        a.state_map = None if p.draft_ids is None else p.draft_ids.data_ptr()
+        a.bank_rows, a.state_rows, a.hidden, a.slots = bank.size, p.S, self.Ht, R
+        a.rows, a.seeds = rows.data_ptr(), seeds.data_ptr()
+        a.ids, a.probs, a.betas = ids.data_ptr(), probs.data_ptr(), beta_t.data_ptr()
+        a.support, a.topk = ids.shape[1], supports[0][0].shape[1]
+        a.alpha, a.evidence, a.slope = alpha, bank.evidence[n - 1], bank.slopes[n - 1]
+        a.temperature, a.out, a.err = bank.temperature, out.data_ptr(), None
+        _lib.call("fm_bank_jump_rows", ctypes.byref(a), ops._stream())
+        return out
+
+    def bank_jump_input(self, bank: JumpBank, n: int, rows, seeds, supports, s: float, t: float) -> torch.Tensor:
+        """``x_embed(state_norm(posterior) + gate * noise_norm(noise))`` of jump n >= 1."""
+        R = rows.shape[0]
+        both = self.bank_jump_rows(bank, n, rows, seeds, supports)
+        return self._embed_rows(both[:R], self.Ht, both[R:], s, t)
+
+    def top_predictions(self, logits: torch.Tensor, k: int, row_map: Optional[torch.Tensor] = None):
+        """A jump's prediction cut to its top k (jump_bank.py:89-92): (ids, probs),
+        ids mapped through ``row_map`` to state rows when given."""
+        R, V = logits.shape
+        ids = torch.empty(R, k, device=logits.device, dtype=torch.int64)
+        probs = torch.empty(R, k, device=logits.device, dtype=torch.float32)
+        rm = None if row_map is None else row_map.to(torch.int64).contiguous()
+        _lib.call("fm_topk_rows", ops._p(logits), logits.stride(0), R, V, k, None if rm is None else ops._p(rm),
+                  0 if rm is None else rm.numel(), ops._p(ids), ops._p(probs), None, ops._stream())
+        return ids, probs
 
     # -------------------------------------------------------------- context rows
     def combine(self, hidden_states: torch.Tensor) -> torch.Tensor:
@@ -193,9 +340,10 @@ class PagedDraft:
         p, T = self.pack, z.shape[0]
         if self.fold_noise:
             weight, var, x0 = p.ensure_noise_fold(self.cfg)
-            proj = ops.gemm(weight, z.contiguous())
+            z = z.contiguous()  # one tensor, referenced until the launch below
+            proj = ops.gemm(weight, z)
             out = torch.empty(T, self.D, device=p.device, dtype=torch.bfloat16)
-            _lib.call("fm_noise_fold", ops._p(proj), ops._p(z.contiguous()), ops._p(var), ops._p(x0), ops._p(out),
+            _lib.call("fm_noise_fold", ops._p(proj), ops._p(z), ops._p(var), ops._p(x0), ops._p(out),
                       float(p.noise_gate_value(self.cfg, s, t)), float(self.cfg.rms_norm_eps), T, self.D, self.Ht,
                       ops._stream())
             return out
@@ -256,10 +404,3 @@ class PagedDraft:
             weight, bias = self.pack.ensure_fold()
             return ops.gemm(weight, final.contiguous(), bias=bias)
         return self.logits(self.head(final))
-
-
-def unsupported_steps(num_steps: int) -> Optional[str]:
-    if num_steps != 1:
-        return ("the plugin models draft one jump per block on this library (multi-jump drafting runs "
-                "through FlashMapDraftModel.draft)")
-    return None

@@ -373,8 +373,9 @@ def write_context_kv(kv: torch.Tensor, positions: torch.Tensor, slots: torch.Ten
     rope = _pair_table(cos_sin, head_dim, "cos_sin")
     sb, sh, st, voff = (int(s) for s in cache_strides)
     err = _err(kv.device)
+    cache_ptrs = cache_ptrs.contiguous()  # referenced until the launch below
     _lib.call("fm_write_context_kv_paged", _p(kv), tokens, layers, heads, head_dim, _p(pos), _p(sl), _p(kn), kdt,
-              rope, _p(cache_ptrs.contiguous()), num_caches, heads_per_cache, sb, sh, st, voff, int(block_size),
+              rope, _p(cache_ptrs), num_caches, heads_per_cache, sb, sh, st, voff, int(block_size),
               float(eps), _p(scales), _p(err), _stream())
 
 
@@ -508,7 +509,8 @@ def _pool_write(kv, meta, k_norm_weights, cos_sin, positions, locs, num_layers, 
     if commit_lens is not None:
         cl = commit_lens.to(torch.int32).contiguous()
     err = _err(kv.device)
-    _lib.call("fm_kv_norm_rope_write_pool", _p(kv), tokens, num_layers, kv_size, head_dim, _p(meta.contiguous()),
+    meta = meta.contiguous()  # referenced until the launch below
+    _lib.call("fm_kv_norm_rope_write_pool", _p(kv), tokens, num_layers, kv_size, head_dim, _p(meta),
               _p(kn), kdt, rope, _p(pos), _p(lc), _p(cl), int(locs_row_width or 1),
               _lib.FM_DT_E4M3 if fp8 else _lib.FM_DT_BF16, _lib.FM_NORM_FUSED if fp8 else _lib.FM_NORM_DIT,
               float(k_scale), float(v_scale), float(eps), _p(err), _stream())

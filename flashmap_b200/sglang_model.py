@@ -22,8 +22,13 @@ Like the reference plugin, the DiT head is folded into the LM-head rows
 applies them to the final AdaLN output; sglang/model.py:449-513), and
 ``FLASHMAP_FOLDED_NOISE=1`` draws the noise in the embedding's eigenbasis
 through one projection (``folded_noise``; sglang/model.py:576-595, 945-958).
-Differences from the reference plugin: one jump per block; no tree drafting or
-FP8 weights; the ``FLASHMAP_COMPILE`` settings are accepted and have no effect.
+Several jumps (``FLASHMAP_NUM_STEPS``) run banked as the reference plugin
+does (``jump_bank.py``): a bank of ``FLASHMAP_JUMP_BANK`` noise draws built at
+``prepare`` and the earlier predictions cut to their ``FLASHMAP_JUMP_TOPK``
+tokens.  Differences from the reference plugin: the bank's draws and the
+slots' bank rows and seeds come from Philox streams, not torch's generator; no
+tree drafting or FP8 weights; the ``FLASHMAP_COMPILE`` settings are accepted
+and have no effect.
 """
 
 from __future__ import annotations
@@ -39,7 +44,7 @@ from torch import nn
 
 from . import serving_ops as S
 from .modeling_flashmap import FlashMapDraftModel as FlashMapDiT
-from .paged_draft import PagedDraft, unsupported_steps
+from .paged_draft import PagedDraft
 
 logger = logging.getLogger(__name__)
 
@@ -120,9 +125,15 @@ class FlashMapDraftModel(FlashMapDiT):
         self.folded_head = None
         self.folded_noise = os.environ.get("FLASHMAP_FOLDED_NOISE", "0") == "1"
         self.num_steps = int(os.environ.get("FLASHMAP_NUM_STEPS") or fm.num_steps)
-        why = unsupported_steps(self.num_steps)
-        if why:
-            raise ValueError(why)
+        if str(self.num_steps) not in fm.jump_grids:
+            raise ValueError(f"no jump grid for {self.num_steps} steps (the checkpoint has "
+                             f"{sorted(fm.jump_grids, key=int)})")
+        # several jumps draw from a bank of noise draws, their predictions cut
+        # to their top-k (jump_bank.py; sglang/model.py:283-285, 458-471)
+        self.jump_bank_size = int(os.environ.get("FLASHMAP_JUMP_BANK", "8192"))
+        self.jump_topk = int(os.environ.get("FLASHMAP_JUMP_TOPK", "16"))
+        self.jump_bank = None
+        self.head_to_state = None
         size = os.environ.get("FLASHMAP_DRAFT_VOCAB")
         size = int(size if size is not None else getattr(config, "draft_vocab_size", 0) or 0)
         self.state_vocab_size = getattr(fm, "state_vocab_size", None)
@@ -196,8 +207,16 @@ class FlashMapDraftModel(FlashMapDiT):
         self.folded_head = core.pack.ensure_fold()
         self.lm_head = _Head(*self.folded_head, self.vocab_size)
         self.markov_head.hot_ids = self.hot_ids
-        (self._s, self._t, _), = core.jump(self.num_steps)
-        self._mods = core.modulations(self._s, self._t)
+        # the drafting head's columns as state rows (a head cut to a draft
+        # vocabulary over the full state vocabulary)
+        self.head_to_state = self.hot_ids if (self.hot_ids is not None and not state_vocab) else None
+        self._jumps = core.jump(self.num_steps)
+        self._mods = [core.modulations(s, t) for s, t, _ in self._jumps]
+        if self.num_steps > 1:
+            grid = self.config.jump_grids[str(self.num_steps)]
+            self.jump_bank = core.build_bank(grid, self.jump_bank_size, self.noise_temperature)
+            logger.info("FlashMap: %d jumps from a bank of %d noise draws (%.0f MB), predictions cut to %d tokens",
+                        self.num_steps, self.jump_bank_size, self.jump_bank.nbytes() / 2**20, self.jump_topk)
 
     def _require_core(self) -> PagedDraft:
         if self._core is None:
@@ -297,9 +316,7 @@ class FlashMapDraftModel(FlashMapDiT):
         p = core.pack
         T = bsz * K
         self._noise_offset += 1
-        z = core.noise(T, scale=self.noise_temperature, seed=int(torch.initial_seed()) & (2**63 - 1),
-                       offset=self._noise_offset)
-        x = core.first_hidden(z, self._s, self._t)
+        seed = int(torch.initial_seed()) & (2**63 - 1)
         cross = S.sglang_paged_cross_attention_fp8 if self._kv_fp8 else S.sglang_paged_cross_attention
 
         def self_attention(qkv, layer):
@@ -315,7 +332,23 @@ class FlashMapDraftModel(FlashMapDiT):
             return cross(query.view(bsz, K, core.H, core.hd), keys[layer], values[layer], cache_seqlens, page_table,
                          cache_seqlens)
 
-        hidden = core.dit(x, self._mods, self_attention, rotate, attend)
+        if self.num_steps == 1:
+            (s, t, _), = self._jumps
+            z = core.noise(T, scale=self.noise_temperature, seed=seed, offset=self._noise_offset)
+            hidden = core.dit(core.first_hidden(z, s, t), self._mods[0], self_attention, rotate, attend)
+        else:
+            # banked jumps (jump_bank.py; sglang/model.py:958-976): no vocabulary-sized
+            # state, the predictions between jumps from the drafting head's top-k
+            bank = self.jump_bank
+            rows, seeds = core.bank_draw(T, bank, seed, self._noise_offset)
+            supports = []
+            for step, (s, t, _) in enumerate(self._jumps):
+                x = (core.bank_first_input(bank, rows, s, t) if step == 0
+                     else core.bank_jump_input(bank, step, rows, seeds, supports, s, t))
+                hidden = core.dit(x, self._mods[step], self_attention, rotate, attend)
+                if step + 1 < self.num_steps:
+                    supports.append(core.top_predictions(core.draft_logits(hidden), self.jump_topk,
+                                                         self.head_to_state))
         if gamma < K:
             hidden = hidden.view(bsz, K, -1)[:, :gamma].reshape(bsz * gamma, -1)
         return LogitsProcessorOutput(next_token_logits=None, hidden_states=hidden)

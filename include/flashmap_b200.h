@@ -139,6 +139,72 @@ FM_API fm_status fm_state_rows(const float* state, void* out, int64_t rows, int6
 FM_API fm_status fm_state_update(float* state, const void* logits, int64_t ldl, int64_t rows, int64_t cols,
                                  float keep, float step, float denom, fm_stream stream);
 
+/* ---------------------------------------------------------------- banked jumps
+ * The sglang plugin's multi-jump draft without vocabulary-sized states
+ * (flashmap/sglang/jump_bank.py).  A bank row holds, for one draw z of the
+ * starting noise, z @ E and per later jump n softmax(a_n z) @ E and
+ * logsumexp(a_n z); a draft reads only the embedding rows of the earlier
+ * predictions' top-k support. */
+
+/* One chunk of bank draws (jump_bank.py:124-150): z [rows, cols] fp32 (the
+ * temperature applied) -> z_bf16 [rows, cols], and per slope a_j (n_slopes <= 8,
+ * host array) probs[j] = bf16(softmax(a_j z)) [n_slopes, rows, cols] and
+ * log_mass[j] = logsumexp(a_j z) [n_slopes, rows] fp32. */
+FM_API fm_status fm_bank_rows(const float* z, void* z_bf16, void* probs, float* log_mass, int64_t rows,
+                              int64_t cols, const float* slopes, int32_t n_slopes, fm_stream stream);
+
+/* A jump's prediction (jump_bank.py:89-92): per row of bf16 logits [rows, ld],
+ * the top k (1..32; larger value first, then smaller index) as ids (the
+ * column, or row_map[column] when row_map [map_len] is given) and their
+ * probabilities under the row's full fp32 softmax. ids [rows, k] int64,
+ * probs [rows, k] fp32; err (optional) records an out-of-range map index. */
+FM_API fm_status fm_topk_rows(const void* logits, int64_t ld, int64_t rows, int64_t cols, int32_t k,
+                              const int64_t* row_map, int64_t map_len, int64_t* ids, float* probs, int32_t* err,
+                              fm_stream stream);
+
+/* out[i] = table[rows[i]] (bf16 rows of cols); an out-of-range row is
+ * recorded in err (optional) and gives zeros. */
+FM_API fm_status fm_bank_gather(const void* table, int64_t table_rows, int64_t cols, const int64_t* rows,
+                                int64_t n, void* out, int32_t* err, fm_stream stream);
+
+/* A later jump n's state rows per slot (jump_bank.py:171-205), before the
+ * norms: out rows [0, slots) the posterior (mean_embed[row] + sum_v
+ * bf16(r_v) E_v) / (1 + sum_v r_v), rows [slots, 2 slots) the noise term
+ * alpha noise_embed[row] + sum_v bf16(beta delta_v) E_v, both bf16; with
+ * r_v = exp(slope z_v - log_mass[row]) expm1(evidence c_v) on each distinct
+ * support token (c_v its summed prediction weight, z_v = temperature *
+ * normal(seed, v)).  The support is the earlier predictions' top-k
+ * concatenated: ids [slots, support] state rows, probs [slots, support],
+ * betas [support / topk]. */
+typedef struct fm_bank_jump {
+  const void* noise_embed;  /* [bank_rows, hidden] bf16 */
+  const void* mean_embed;   /* [bank_rows, hidden] bf16, this jump's */
+  const float* log_mass;    /* [bank_rows] fp32, this jump's */
+  const void* embed;        /* embedding rows [*, hidden] bf16 */
+  const int64_t* state_map; /* [state_rows] state row -> embed row, or NULL (identity) */
+  int64_t bank_rows, state_rows, hidden, slots;
+  const int64_t* rows;      /* [slots] bank rows */
+  const int64_t* seeds;     /* [slots] slot seeds */
+  const int64_t* ids;       /* [slots, support] */
+  const float* probs;       /* [slots, support] */
+  const float* betas;       /* [support / topk] */
+  int32_t support, topk;
+  float alpha, evidence, slope, temperature;
+  void* out;                /* [2 slots, hidden] bf16 */
+  int32_t* err;             /* optional: out-of-range rows / ids */
+} fm_bank_jump;
+FM_API fm_status fm_bank_jump_rows(const fm_bank_jump* args, fm_stream stream);
+
+/* The per-(seed, token) standard normals of the support (jump_bank.py:62-73):
+ * out[r, l] = normal(seeds[r], ids[r, l]), fp32 [rows, cols]. */
+FM_API fm_status fm_token_normals(const int64_t* seeds, const int64_t* ids, int64_t rows, int64_t cols,
+                                  float* out, fm_stream stream);
+
+/* out[i] = floor(u_i * high), u_i a Philox4x32-10 uniform of counter
+ * (i, offset, purpose) under seed; 1 <= high <= 2^32 - 1 (bank rows, slot seeds). */
+FM_API fm_status fm_philox_randint(int64_t* out, int64_t n, int64_t high, uint64_t seed, uint32_t offset,
+                                   uint32_t purpose, fm_stream stream);
+
 /* One-jump input mix (modeling_flashmap.py:393-399): out = bf16(state_norm(post) +
  * bf16(gate * noise_norm(state))), post rows post_stride apart (0: one shared row). */
 FM_API fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,
