@@ -139,6 +139,10 @@ _SIGNATURES = {
     "fm_paged_attn_nsplit": (c_int32, [c_int64, c_int64, c_int64, c_int64, c_int32]),
     "fm_paged_attn_workspace_size": (c_size_t, [c_int64, c_int64, c_int64, c_int64, c_int32]),
     "fm_paged_cross_attn": (c_int, [ctypes.POINTER(PagedAttn), c_void_p]),
+    "fm_tree_build": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "fm_tree_commit": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
+                               c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p]),
     "fm_bank_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int32, c_void_p]),
     "fm_topk_rows": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
                              c_void_p, c_void_p]),

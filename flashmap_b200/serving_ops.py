@@ -40,7 +40,7 @@ __all__ = [
     "OpArgumentError", "rope_table", "rope_freqs", "vllm_rms_norm", "vllm_rms_norm_rope",
     "vllm_block_self_attention", "vllm_paged_cross_attention", "write_context_kv", "sglang_rms_norm",
     "sglang_rms_norm_rope", "sglang_block_self_attention", "sglang_paged_cross_attention",
-    "sglang_paged_cross_attention_fp8", "kv_norm_rope_write", "kv_norm_rope_write_fp8",
+    "sglang_paged_cross_attention_fp8", "kv_norm_rope_write", "kv_norm_rope_write_fp8", "tree_commit",
 ]
 
 _FP8 = getattr(torch, "float8_e4m3fn", None)
@@ -539,3 +539,35 @@ def kv_norm_rope_write(kv, meta, k_norm_weights, cos_sin, positions, locs, num_l
 
 def attention_scale(head_dim: int) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+def tree_commit(accept_index, num_correct, window, predict, req_pool_indices, prefix_lens, req_to_token):
+    """The tree path's commit after greedy tree verification, one launch for
+    the batch (sglang/kernels.py:363-454): reorders each request's verify
+    window in ``req_to_token`` (in place) so the accepted path comes first (no
+    KV moves) and returns ``(out_tokens (bs, D1) int64, bonus, commit_lens
+    int32, new_seq_lens, inject_locs (bs * W) int64)``."""
+    for t, name in ((accept_index, "accept_index"), (num_correct, "num_correct"), (window, "window"),
+                    (predict, "predict"), (req_pool_indices, "req_pool_indices"), (prefix_lens, "prefix_lens"),
+                    (req_to_token, "req_to_token")):
+        _cuda(t, name)
+    _need(req_to_token.dtype == torch.int32 and req_to_token.stride(1) == 1, "req_to_token must be int32 rows")
+    bs, d1 = accept_index.shape
+    width = window.shape[1]
+    dev = accept_index.device
+    accept = accept_index.to(torch.int32).contiguous()
+    correct = num_correct.to(torch.int32).contiguous()
+    win = window.to(torch.int64).contiguous()
+    pred = predict.to(torch.int32).contiguous()
+    pool = req_pool_indices.to(torch.int64).contiguous()
+    prefix = prefix_lens.to(torch.int64).contiguous()
+    out_tokens = torch.empty(bs, d1, dtype=torch.int64, device=dev)
+    bonus = torch.empty(bs, dtype=torch.int64, device=dev)
+    commit = torch.empty(bs, dtype=torch.int32, device=dev)
+    new_seq_lens = torch.empty(bs, dtype=torch.int64, device=dev)
+    inject = torch.empty(bs * width, dtype=torch.int64, device=dev)
+    err = _err(dev)
+    _lib.call("fm_tree_commit", _p(accept), _p(correct), _p(win), _p(pred), _p(pool), _p(prefix), _p(req_to_token),
+              req_to_token.stride(0), req_to_token.shape[0], bs, width, d1, _p(out_tokens), _p(bonus), _p(commit),
+              _p(new_seq_lens), _p(inject), _p(err), _stream())
+    return out_tokens, bonus, commit, new_seq_lens.to(prefix_lens.dtype), inject

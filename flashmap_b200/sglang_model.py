@@ -25,9 +25,12 @@ through one projection (``folded_noise``; sglang/model.py:576-595, 945-958).
 Several jumps (``FLASHMAP_NUM_STEPS``) run banked as the reference plugin
 does (``jump_bank.py``): a bank of ``FLASHMAP_JUMP_BANK`` noise draws built at
 ``prepare`` and the earlier predictions cut to their ``FLASHMAP_JUMP_TOPK``
-tokens.  Differences from the reference plugin: the bank's draws and the
-slots' bank rows and seeds come from Philox streams, not torch's generator; no
-tree drafting or FP8 weights; the ``FLASHMAP_COMPILE`` settings are accepted
+tokens.  ``FLASHMAP_TREE_N`` >= 1 drafts that many candidate blocks per request in
+one pass and merges them into the verify tree (``tree_outputs``; the trie in
+EAGLE's encoding by ``flashmap_b200.tree.build_tree_abi``; the accepted path's
+commit is ``serving_ops.tree_commit``).  Differences from the reference
+plugin: the bank's draws and the slots' bank rows and seeds come from Philox
+streams, not torch's generator; no FP8 weights; the ``FLASHMAP_COMPILE`` settings are accepted
 and have no effect.
 """
 
@@ -45,6 +48,7 @@ from torch import nn
 from . import serving_ops as S
 from .modeling_flashmap import FlashMapDraftModel as FlashMapDiT
 from .paged_draft import PagedDraft
+from .tree import build_tree_abi
 
 logger = logging.getLogger(__name__)
 
@@ -134,6 +138,18 @@ class FlashMapDraftModel(FlashMapDiT):
         self.jump_topk = int(os.environ.get("FLASHMAP_JUMP_TOPK", "16"))
         self.jump_bank = None
         self.head_to_state = None
+        # Tree drafting (tree_worker.py): up to FLASHMAP_TREE_N candidate blocks
+        # per request from independent noise in one draft pass, merged into a
+        # trie cut to the verify width (block_size + 1 with the root); a batch of
+        # bs requests drafts clamp(FLASHMAP_TREE_BUDGET // bs, 1, N) (sglang/model.py:302-312)
+        self.tree_max_n = int(os.environ.get("FLASHMAP_TREE_N", "0"))
+        self.tree_budget = int(os.environ.get("FLASHMAP_TREE_BUDGET", "32"))
+        self.tree_mode = self.tree_max_n >= 1
+        self.tree_width = self.block_size + 1
+        self._tree_buffers = None
+        self._tree_scratch = None
+        if self.tree_mode and self.num_steps != 1:
+            raise NotImplementedError("tree drafting takes one jump")
         size = os.environ.get("FLASHMAP_DRAFT_VOCAB")
         size = int(size if size is not None else getattr(config, "draft_vocab_size", 0) or 0)
         self.state_vocab_size = getattr(fm, "state_vocab_size", None)
@@ -212,11 +228,66 @@ class FlashMapDraftModel(FlashMapDiT):
         self.head_to_state = self.hot_ids if (self.hot_ids is not None and not state_vocab) else None
         self._jumps = core.jump(self.num_steps)
         self._mods = [core.modulations(s, t) for s, t, _ in self._jumps]
+        if self.tree_mode:
+            self._tree_buffers = self._alloc_tree_buffers(self._graph_max_bs())
         if self.num_steps > 1:
             grid = self.config.jump_grids[str(self.num_steps)]
             self.jump_bank = core.build_bank(grid, self.jump_bank_size, self.noise_temperature)
             logger.info("FlashMap: %d jumps from a bank of %d noise draws (%.0f MB), predictions cut to %d tokens",
                         self.num_steps, self.jump_bank_size, self.jump_bank.nbytes() / 2**20, self.jump_topk)
+
+    @staticmethod
+    def _graph_max_bs() -> int:
+        """The largest batch the engine captures draft graphs for (sglang's
+        decode CUDA-graph setting when sglang is importable, else 64)."""
+        try:
+            from sglang.srt.server_args import get_global_server_args
+
+            return int(get_global_server_args().cuda_graph_max_bs or 64)
+        except Exception:  # sglang absent or not configured: its default
+            return 64
+
+    def _alloc_tree_buffers(self, max_bs: int):
+        """The tree a draft step hands to verification, in EAGLE's encoding
+        (build_tree_kernel_efficient): per request its W - 1 non-root nodes'
+        tokens and ids ``parent * W + index``, the parent list, and (trie nodes,
+        distinct candidates) (sglang/model.py:603-620)."""
+        width, device = self.tree_width, self._require_core().pack.device
+
+        def zeros(*shape):
+            return torch.zeros(*shape, dtype=torch.int64, device=device)
+
+        return zeros(max_bs, width - 1), zeros(max_bs, width - 1), zeros(max_bs, width * (self.block_size - 1) + 1), \
+            zeros(max_bs, 2)
+
+    def tree_outputs(self, bsz: int):
+        """The tree buffers for a batch of ``bsz``: the persistent ones, or
+        (an eager batch above them) scratch ones."""
+        buffers = self._tree_buffers
+        if bsz > buffers[0].shape[0]:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(f"capturing a draft graph for {bsz} requests, above the tree buffers")
+            if self._tree_scratch is None or self._tree_scratch[0].shape[0] < bsz:
+                self._tree_scratch = self._alloc_tree_buffers(bsz)
+            buffers = self._tree_scratch
+        return tuple(buffer[:bsz] for buffer in buffers)
+
+    def tree_n_for(self, bsz: int) -> int:
+        """Candidates per request in a batch of ``bsz``."""
+        return max(1, min(self.tree_max_n, self.tree_budget // max(bsz, 1)))
+
+    def _draft_tree(self, hidden: torch.Tensor, bsz: int, n_cand: int) -> None:
+        """Greedy tokens of every candidate (the first index of each row's
+        maximum), merged into a trie cut to the verify width, written to the
+        tree buffers (sglang/model.py:642-659)."""
+        core = self._require_core()
+        ids, _ = core.top_predictions(core.draft_logits(hidden), 1, self.hot_ids)
+        out_tokens, out_ids, out_parents, out_stats = self.tree_outputs(bsz)
+        node_tokens, node_ids, stats = build_tree_abi(ids.view(bsz, n_cand, self.block_size), self.tree_width)
+        out_tokens.copy_(node_tokens)
+        out_ids.copy_(node_ids)
+        out_parents[:, 1:node_ids.shape[1] + 1].copy_(node_ids)
+        out_stats.copy_(stats)
 
     def _require_core(self) -> PagedDraft:
         if self._core is None:
@@ -306,31 +377,41 @@ class FlashMapDraftModel(FlashMapDiT):
         args = self._write_args(pool)
         anchor_positions = positions.view(bsz, gamma)[:, 0]
         block_positions = anchor_positions[:, None] + torch.arange(K, device=positions.device)
+        # tree drafting: a request's candidate blocks side by side in the
+        # cross-attention's query axis, so its context is read once
+        n_cand = self.tree_n_for(bsz) if self.tree_mode else 1
+        if self.tree_mode:
+            assert gamma == K, "tree drafting verifies the whole block"
         self._kv_write(core.anchor_kv(input_ids.view(bsz, gamma)[:, 0]), args, anchor_positions,
                        forward_batch.out_cache_loc.view(bsz, gamma)[:, 0])
         page_table = self.req_to_token()[forward_batch.req_pool_indices].to(torch.int32)
         cache_seqlens = (forward_batch.seq_lens + 1).to(torch.int32)
-        freqs = S.rope_freqs(block_positions + 1, core.hd, self.rope_theta).contiguous()
+        freqs = S.rope_freqs(block_positions + 1, core.hd, self.rope_theta)
+        if n_cand > 1:
+            freqs = freqs.repeat_interleave(n_cand, dim=0)
+        freqs = freqs.contiguous()
+        blocks = bsz * n_cand
         keys = [b[0] for b in args[4]]
         values = [b[1] for b in args[4]]
         p = core.pack
-        T = bsz * K
+        T = blocks * K
         self._noise_offset += 1
         seed = int(torch.initial_seed()) & (2**63 - 1)
         cross = S.sglang_paged_cross_attention_fp8 if self._kv_fp8 else S.sglang_paged_cross_attention
 
         def self_attention(qkv, layer):
             w = p.layers[layer]
-            return S.sglang_block_self_attention(qkv.view(bsz, K, 3, core.H, core.hd), w["self_q_norm"],
+            return S.sglang_block_self_attention(qkv.view(blocks, K, 3, core.H, core.hd), w["self_q_norm"],
                                                  w["self_k_norm"], freqs, self.qk_norm_eps)
 
         def rotate(q, layer):
-            return S.sglang_rms_norm_rope(q.view(bsz, K, core.H, core.hd), p.layers[layer]["cross_q_norm"], freqs,
-                                          self.qk_norm_eps)
+            return S.sglang_rms_norm_rope(q.view(blocks, K, core.H, core.hd), p.layers[layer]["cross_q_norm"],
+                                          freqs, self.qk_norm_eps)
 
         def attend(query, layer):
-            return cross(query.view(bsz, K, core.H, core.hd), keys[layer], values[layer], cache_seqlens, page_table,
-                         cache_seqlens)
+            out = cross(query.view(bsz, n_cand * K, core.H, core.hd), keys[layer], values[layer], cache_seqlens,
+                        page_table, cache_seqlens)
+            return out.view(blocks, K, core.H, core.hd) if n_cand > 1 else out
 
         if self.num_steps == 1:
             (s, t, _), = self._jumps
@@ -349,6 +430,10 @@ class FlashMapDraftModel(FlashMapDiT):
                 if step + 1 < self.num_steps:
                     supports.append(core.top_predictions(core.draft_logits(hidden), self.jump_topk,
                                                          self.head_to_state))
+        if self.tree_mode:
+            self._draft_tree(hidden, bsz, n_cand)
+            # the proposer takes one block per request: the first candidate's
+            hidden = hidden.view(bsz, n_cand, K, -1)[:, 0].reshape(bsz * K, -1)
         if gamma < K:
             hidden = hidden.view(bsz, K, -1)[:, :gamma].reshape(bsz * gamma, -1)
         return LogitsProcessorOutput(next_token_logits=None, hidden_states=hidden)

@@ -205,6 +205,34 @@ FM_API fm_status fm_token_normals(const int64_t* seeds, const int64_t* ids, int6
 FM_API fm_status fm_philox_randint(int64_t* out, int64_t n, int64_t high, uint64_t seed, uint32_t offset,
                                    uint32_t purpose, fm_stream stream);
 
+/* ---------------------------------------------------------------- tree drafting
+ * The verify tree of N candidate blocks per request (flashmap/sglang/tree.py:9-78,
+ * build_tree_abi): per request, the trie of candidates [bs, N, K] int64 (a
+ * node per distinct prefix, voted by the candidates through it), its
+ * width - 1 best-voted nodes (ties: shallower, then lower candidate) listed by
+ * depth then candidate: tokens [bs, width - 1], ids [bs, width - 1] = parent *
+ * width + index (root 0; a trie with fewer nodes is padded with copies of the
+ * first node under the root), stats [bs, 2] = (trie nodes, distinct
+ * candidates), all int64.  N <= 64, K <= 64, N * K <= 1024. */
+FM_API fm_status fm_tree_build(const int64_t* candidates, int64_t bs, int64_t n, int64_t k, int64_t width,
+                               int64_t* tokens, int64_t* ids, int64_t* stats, fm_stream stream);
+
+/* Commit of the accepted tree paths (flashmap/sglang/kernels.py:363-454,
+ * tree_commit): accept [bs, depth1] int32 global node ids of the path (root
+ * first, -1 past it), num_correct [bs] int32, window [bs, width] int64 KV slots,
+ * predict [bs * width] int32 (the target's token after each node), req_pool /
+ * prefix [bs] int64; req_to_token [req_rows, row_stride] int32 gets the path's
+ * slots first, then the other nodes' in index order, from column prefix.
+ * Returns out_tokens [bs, depth1] int64, bonus [bs] int64, commit [bs] int32 =
+ * n + 1, new_seq_lens [bs] int64 = prefix + n + 1, inject_locs [bs * width]
+ * int64 (the path's slots, 0 elsewhere); err (optional) records an index out
+ * of range (the write is skipped). */
+FM_API fm_status fm_tree_commit(const int32_t* accept, const int32_t* num_correct, const int64_t* window,
+                                const int32_t* predict, const int64_t* req_pool, const int64_t* prefix,
+                                int32_t* req_to_token, int64_t row_stride, int64_t req_rows, int64_t bs,
+                                int64_t width, int64_t depth1, int64_t* out_tokens, int64_t* bonus, int32_t* commit,
+                                int64_t* new_seq_lens, int64_t* inject_locs, int32_t* err, fm_stream stream);
+
 /* One-jump input mix (modeling_flashmap.py:393-399): out = bf16(state_norm(post) +
  * bf16(gate * noise_norm(state))), post rows post_stride apart (0: one shared row). */
 FM_API fm_status fm_mix_state(const void* post, int64_t post_stride, const void* state, const void* state_norm_w,
