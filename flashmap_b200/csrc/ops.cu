@@ -959,19 +959,121 @@ __global__ void accept_greedy_keys_kernel(const int64_t* draft, const unsigned l
   bonus[b] = (int64_t)argmax_key_index(kr[acc]);
 }
 
+// ---------------------------------------------------------------- rejection acceptance
+// Three launches: the K tests of every request (accept_tests_kernel), the
+// residual's slice totals over (request, slice) blocks (residual_slices_kernel)
+// and the bonus draw (residual_pick_kernel).  The bonus is a sliced
+// categorical draw: slices of CAT_SLICE = 256 ranges of CAT_RANGE weights;
+// per slice the ranges' sequential sums and a block inclusive scan give its
+// total; the totals are summed in slice order, the slice holding u * total is
+// rescanned and its range searched in index order (the C oracle's
+// fmo_categorical_sliced).
+constexpr int CAT_RANGE = 32;
+constexpr long long CAT_SLICE = (long long)RT * CAT_RANGE;
+constexpr int CAT_MAX_SLICES = 256;
+
 template <typename T>
-__global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, const int64_t* draft,
-                                                              const float* q, long long V, int K, float temperature,
-                                                              uint64_t seed, uint32_t offset, const float* stats,
-                                                              int64_t* accepted, int64_t* bonus) {
+struct RejectionRow {
+  const T* tr;        // target row of the first rejected slot (or row K)
+  const float* qr;    // the draft's probabilities of that slot (unused when all were accepted)
+  float m, s, temperature;
+  bool residual;      // max(0, p - q) (else the target's p)
+  bool vec;           // rows 16-byte aligned
+  __device__ float p(long long v) const {
+    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(to_f(tr[v]), temperature), m)), s);
+  }
+  __device__ float weight(long long v) const {
+    const float pv = p(v);
+    if (!residual) return pv;
+    const float d = __fsub_rn(pv, qr[v]);
+    return d > 0.0f ? d : 0.0f;
+  }
+  // 32 weights of v0 .. v0 + 31 (all < V) from 16-byte loads issued together
+  __device__ bool bulk(long long v0, long long V, float* w) const {
+    if (!vec) return false;
+    float x[4][8], qv[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      load8(tr, v0 / 8 + k, V, true, x[k]);
+      if (residual) load8(qr, v0 / 8 + k, V, true, qv[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float pv = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
+        if (!residual) {
+          w[k * 8 + j] = pv;
+        } else {
+          const float d = __fsub_rn(pv, qv[k][j]);
+          w[k * 8 + j] = d > 0.0f ? d : 0.0f;
+        }
+      }
+    return true;
+  }
+};
+
+template <typename T>
+__device__ RejectionRow<T> rejection_row(const T* target, const float* q, const float* stats, long long V, int K,
+                                         float temperature, int b, int acc) {
+  RejectionRow<T> r;
+  const long long row = (long long)b * (K + 1) + acc;
+  r.tr = target + row * V;
+  r.qr = q + ((long long)b * K + (acc < K ? acc : 0)) * V;
+  r.m = stats[2 * row];
+  r.s = stats[2 * row + 1];
+  r.temperature = temperature;
+  r.residual = acc < K;
+  r.vec = (reinterpret_cast<uintptr_t>(r.tr) & 15) == 0 && (reinterpret_cast<uintptr_t>(r.qr) & 15) == 0;
+  return r;
+}
+
+// this thread's range sum t and the block's inclusive scan h over slice j
+// (Hillis-Steele inside each warp, then the warp totals in order); sm holds >= 16 floats
+template <typename T, bool TargetOnly>
+__device__ void slice_scan(const RejectionRow<T>& w, long long V, long long j, float* sm, float& t, float& h) {
+  const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+  const long long lo = j * CAT_SLICE + (long long)i * CAT_RANGE, hi = min(lo + CAT_RANGE, V);
+  RejectionRow<T> r = w;
+  if (TargetOnly) r.residual = false;
+  t = 0.0f;
+  float bw[32];
+  if (hi - lo == CAT_RANGE && r.bulk(lo, V, bw)) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) t = __fadd_rn(t, bw[k]);
+  } else {
+    for (long long v = lo; v < hi; ++v) t = __fadd_rn(t, r.weight(v));
+  }
+  h = t;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, h, off);
+    if (lane >= off) h = __fadd_rn(y, h);
+  }
+  if (lane == 31) sm[warp] = h;
+  __syncthreads();
+  if (i == 0) {
+    float base = 0.0f;
+    for (int wp = 0; wp < RT / 32; ++wp) {
+      const float tot = sm[wp];
+      sm[8 + wp] = base;
+      base = (wp == 0) ? tot : __fadd_rn(base, tot);
+    }
+  }
+  __syncthreads();
+  if (warp > 0) h = __fadd_rn(sm[8 + warp], h);
+  __syncthreads();
+}
+
+// every slot's test u q < p at once (thread k), then the first failure
+template <typename T>
+__global__ void __launch_bounds__(RT) accept_tests_kernel(const T* target, const int64_t* draft, const float* q,
+                                                          long long V, int K, float temperature, uint64_t seed,
+                                                          uint32_t offset, const float* stats, int64_t* accepted) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ float sm[RT + 32];
-  __shared__ int s_acc;
-  __shared__ int s_any;
-  const int b = blockIdx.x;
-  // every slot's test u q < p at once (thread k), then the first failure
   __shared__ int s_fail;
+  const int b = blockIdx.x;
   if (threadIdx.x == 0) s_fail = K;
   __syncthreads();
   for (int k = threadIdx.x; k < K; k += RT) {
@@ -985,74 +1087,125 @@ __global__ void __launch_bounds__(RT) accept_rejection_kernel(const T* target, c
     if (!(__fmul_rn(u, qd) < p)) atomicMin(&s_fail, k);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    s_acc = s_fail;
-    accepted[b] = s_fail;
+  if (threadIdx.x == 0) accepted[b] = s_fail;
+}
+
+// the residual's (or, all accepted, the target's) slice totals: block (b, j)
+template <typename T>
+__global__ void __launch_bounds__(RT) residual_slices_kernel(const T* target, const float* q, long long V, int K,
+                                                             float temperature, const float* stats,
+                                                             const int64_t* accepted, float* totals) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float sm[16];
+  const int b = blockIdx.x;
+  const long long j = blockIdx.y;
+  const RejectionRow<T> w = rejection_row(target, q, stats, V, K, temperature, b, (int)accepted[b]);
+  float t, h;
+  slice_scan<T, false>(w, V, j, sm, t, h);
+  if (threadIdx.x == RT - 1) totals[(long long)b * CAT_MAX_SLICES + j] = h;
+}
+
+// the bonus: the slice totals in order, then the chosen slice and range; a
+// residual with no positive weight draws from the target's distribution
+template <typename T>
+__global__ void __launch_bounds__(RT) residual_pick_kernel(const T* target, const float* q, long long V, int K,
+                                                           float temperature, uint64_t seed, uint32_t offset,
+                                                           const float* stats, const int64_t* accepted,
+                                                           const float* totals, int64_t* bonus) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float sm[16];
+  __shared__ float tot[CAT_MAX_SLICES], pre[CAT_MAX_SLICES];
+  __shared__ float g[RT];
+  __shared__ int s_choice;
+  __shared__ float s_base, s_target;
+  __shared__ int ired[RT / 32];
+  const int b = blockIdx.x, i = threadIdx.x;
+  const int S = (int)((V + CAT_SLICE - 1) / CAT_SLICE);
+  RejectionRow<T> w = rejection_row(target, q, stats, V, K, temperature, b, (int)accepted[b]);
+  for (int j = i; j < S; j += RT) tot[j] = totals[(long long)b * CAT_MAX_SLICES + j];
+  __syncthreads();
+  if (i == 0) {
+    float run = 0.0f;
+    for (int j = 0; j < S; ++j) {
+      run = j == 0 ? tot[j] : __fadd_rn(run, tot[j]);
+      pre[j] = run;
+    }
   }
   __syncthreads();
-  const int acc = s_acc;
-  const long long row = (long long)b * (K + 1) + acc;
-  const T* tr = target + row * V;
-  const float m = stats[2 * row], s = stats[2 * row + 1];
-  const float* qr = q + ((long long)b * K + (acc < K ? acc : 0)) * V;
-  auto target_p = [&](long long v) {
-    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(to_f(tr[v]), temperature), m)), s);
-  };
-  auto residual = [&](long long v) {
-    const float pv = target_p(v);
-    if (acc >= K) return pv;
-    const float dlt = __fsub_rn(pv, qr[v]);
-    return dlt > 0.0f ? dlt : 0.0f;
-  };
-  // 32 weights from 16-byte loads issued together (rows 16-byte aligned)
-  const bool vec_ok = (reinterpret_cast<uintptr_t>(tr) & 15) == 0 && (reinterpret_cast<uintptr_t>(qr) & 15) == 0;
-  auto target_bulk = [&](long long v0, float* w) {
-    if (!vec_ok) return false;
-    float x[4][8];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) load8(tr, v0 / 8 + k, V, true, x[k]);
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        w[k * 8 + j] = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
-    return true;
-  };
-  auto residual_bulk = [&](long long v0, float* w) {
-    if (!vec_ok) return false;
-    float x[4][8], qv[4][8];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      load8(tr, v0 / 8 + k, V, true, x[k]);
-      if (acc < K) load8(qr, v0 / 8 + k, V, true, qv[k]);
+  if (!(pre[S - 1] > 0.0f)) {
+    // no positive residual weight: the target's distribution, its slice totals here
+    w.residual = false;
+    for (int j = 0; j < S; ++j) {
+      float t, h;
+      slice_scan<T, true>(w, V, j, sm, t, h);
+      if (i == RT - 1) tot[j] = h;
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float pv = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
-        if (acc >= K) {
-          w[k * 8 + j] = pv;
-        } else {
-          const float dlt = __fsub_rn(pv, qv[k][j]);
-          w[k * 8 + j] = dlt > 0.0f ? dlt : 0.0f;
+    __syncthreads();
+    if (i == 0) {
+      float run = 0.0f;
+      for (int j = 0; j < S; ++j) {
+        run = j == 0 ? tot[j] : __fadd_rn(run, tot[j]);
+        pre[j] = run;
+      }
+    }
+    __syncthreads();
+  }
+  if (i == 0) {
+    const float target_u = __fmul_rn(philox_uniform(seed, 0u, (uint32_t)b, offset, 2u), pre[S - 1]);
+    int js = -1;
+    for (int j = 0; j < S; ++j)
+      if (pre[j] > target_u) {
+        js = j;
+        break;
+      }
+    if (js < 0)
+      for (int j = S - 1; j >= 0; --j)
+        if (tot[j] > 0.0f) {
+          js = j;
+          break;
+        }
+    s_choice = js;
+    s_base = js > 0 ? pre[js - 1] : 0.0f;
+    s_target = target_u;
+  }
+  __syncthreads();
+  const int js = s_choice;
+  if (js < 0) {  // every weight zero
+    if (i == 0) bonus[b] = 0;
+    return;
+  }
+  float t, h;
+  if (w.residual)
+    slice_scan<T, false>(w, V, js, sm, t, h);
+  else
+    slice_scan<T, true>(w, V, js, sm, t, h);
+  g[i] = __fadd_rn(s_base, h);
+  const float target_u = s_target;
+  const int first = block_min_int(g[i] > target_u ? i : RT, ired);
+  const int lastpos = block_max_int(t > 0.0f ? i : -1, ired);
+  if (i == 0) {
+    const int chosen = first < RT ? first : lastpos;
+    long long pick = js * CAT_SLICE;
+    if (chosen >= 0) {
+      float run = chosen > 0 ? g[chosen - 1] : s_base;
+      const long long lo = js * CAT_SLICE + (long long)chosen * CAT_RANGE, hi = min(lo + CAT_RANGE, V);
+      long long last = -1;
+      pick = -1;
+      for (long long v = lo; v < hi; ++v) {
+        const float wv = w.weight(v);
+        run = __fadd_rn(run, wv);
+        if (wv > 0.0f) last = v;
+        if (run > target_u) {
+          pick = v;
+          break;
         }
       }
-    return true;
-  };
-  int any = 0;
-  for (long long v = threadIdx.x; v < V && !any; v += RT) any = residual(v) > 0.0f;
-  if (threadIdx.x == 0) s_any = 0;
-  __syncthreads();
-  if (any) atomicOr(&s_any, 1);
-  __syncthreads();
-  const float u = philox_uniform(seed, 0u, (uint32_t)b, offset, 2u);
-  long long pick;
-  if (s_any)
-    pick = block_categorical(residual, V, u, sm, residual_bulk);
-  else
-    pick = block_categorical(target_p, V, u, sm, target_bulk);
-  if (threadIdx.x == 0) bonus[b] = pick;
+      if (pick < 0) pick = last >= 0 ? last : lo;
+    }
+    bonus[b] = pick;
+  }
 }
 
 __global__ void transpose_bf16_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, long long R, long long C) {
@@ -1396,7 +1549,9 @@ extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const flo
 }
 
 extern "C" size_t fm_accept_workspace_size(int64_t B, int64_t K) {
-  return (size_t)B * (K + 1) * (2 * sizeof(float) + sizeof(int64_t)) + 256;
+  // per target row: stats and a max key; per request: the bonus draw's slice totals
+  return (size_t)B * (K + 1) * (2 * sizeof(float) + sizeof(int64_t)) + (size_t)B * CAT_MAX_SLICES * sizeof(float) +
+         256;
 }
 
 extern "C" fm_status fm_accept_greedy(const void* target_logits, int32_t dtype, const int64_t* draft, int64_t B,
@@ -1433,8 +1588,19 @@ extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtyp
   st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), target_logits, (long long)V, temperature,
                           stats, (int64_t*)nullptr, (const uint32_t*)max_keys);
   if (st) return st;
-  return FM_DISPATCH_LOGITS(dtype, accept_rejection_kernel, dim3((unsigned)B), target_logits, draft, q, (long long)V,
-                            (int)K, temperature, seed, offset, (const float*)stats, accepted, bonus);
+  const long long cat_slices = (V + CAT_SLICE - 1) / CAT_SLICE;
+  if (cat_slices > CAT_MAX_SLICES) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large for the bonus draw");
+  // the slice totals follow the stats and max keys (rows * 12 bytes), 256-byte aligned
+  float* totals = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(max_keys + rows) + 255) & ~uintptr_t(255));
+  st = FM_DISPATCH_LOGITS(dtype, accept_tests_kernel, dim3((unsigned)B), target_logits, draft, q, (long long)V,
+                          (int)K, temperature, seed, offset, (const float*)stats, accepted);
+  if (st) return st;
+  st = FM_DISPATCH_LOGITS(dtype, residual_slices_kernel, dim3((unsigned)B, (unsigned)cat_slices), target_logits, q,
+                          (long long)V, (int)K, temperature, (const float*)stats, (const int64_t*)accepted, totals);
+  if (st) return st;
+  return FM_DISPATCH_LOGITS(dtype, residual_pick_kernel, dim3((unsigned)B), target_logits, q, (long long)V, (int)K,
+                            temperature, seed, offset, (const float*)stats, (const int64_t*)accepted,
+                            (const float*)totals, bonus);
 }
 
 extern "C" fm_status fm_transpose_bf16(const void* in, void* out, int64_t rows, int64_t cols, fm_stream stream) {

@@ -447,7 +447,9 @@ FM_API fm_status fm_accept_greedy_noalloc(const void* target_logits, int32_t log
                                           fm_stream stream);
 
 /* Rejection acceptance (:583-594). q [B, K, V] fp32 draft probabilities.
- * u[b,k] = uniform (k, b, offset, 1); bonus draw uniform (0, b, offset, 2). */
+ * u[b,k] = uniform (k, b, offset, 1); bonus draw uniform (0, b, offset, 2),
+ * a sliced categorical draw (slices of 256 ranges of 32 weights, their totals
+ * summed in slice order; V <= 256 * 8192). */
 FM_API fm_status fm_accept_rejection(const void* target_logits, int32_t logits_dtype, const int64_t* draft,
                                      const float* q, int64_t B, int64_t K, int64_t V, float temperature,
                                      uint64_t seed, uint32_t offset, int64_t* accepted, int64_t* bonus,

@@ -44,6 +44,8 @@ def lib():
         L.fmo_argmax.argtypes = [_f32p, ctypes.c_int64]
         L.fmo_categorical.restype = ctypes.c_int64
         L.fmo_categorical.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
+        L.fmo_categorical_sliced.restype = ctypes.c_int64
+        L.fmo_categorical_sliced.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float]
         L.fmo_softmax_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, _f32p]
         L.fmo_sample_rows.argtypes = [_f32p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_float,
                                       ctypes.c_uint64, ctypes.c_uint32, _i64p, _f32p]
@@ -89,6 +91,13 @@ def row_stats(row: torch.Tensor, temperature: float = 1.0):
 def categorical(weights: np.ndarray, u: float) -> int:
     w = np.ascontiguousarray(weights, dtype=np.float32)
     return int(lib().fmo_categorical(_ptr(w, _f32p), w.size, float(u)))
+
+
+def categorical_sliced(weights: np.ndarray, u: float) -> int:
+    """The rejection bonus draw: the sliced form of ``categorical`` (slices of
+    256 ranges of 32 weights, slice totals summed in order)."""
+    w = np.ascontiguousarray(weights, dtype=np.float32)
+    return int(lib().fmo_categorical_sliced(_ptr(w, _f32p), w.size, float(u)))
 
 
 def softmax_rows(logits: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
@@ -144,6 +153,7 @@ __all__ = [
     "accept_rejection",
     "build",
     "categorical",
+    "categorical_sliced",
     "fm_exp",
     "philox",
     "row_stats",

@@ -24,6 +24,14 @@
  *     sequential sums, an inclusive scan (Hillis-Steele in groups of 32, then
  *     a sequential scan of the 8 group totals), target = u * total, and a
  *     two-level search for the first element whose running sum exceeds it.
+ *   - the rejection step's bonus draw uses the sliced form of that draw
+ *     (fmo_categorical_sliced), so that the GPU spreads it over many blocks:
+ *     slices of 256 ranges of 32 elements; per slice the ranges' sequential
+ *     sums and the same inclusive scan give the slice total; the slice totals
+ *     are summed in order (a sequential prefix), target = u * total picks the
+ *     first slice whose prefix exceeds it, and inside that slice the range and
+ *     then the element are found as above, each running sum starting from the
+ *     prefix of the slices before.
  *
  * Philox4x32-10 follows Salmon, Moraes, Dror and Shaw, "Parallel random
  * numbers: as easy as 1, 2, 3" (SC'11): multipliers 0xD2511F53 and
@@ -39,6 +47,8 @@
 
 #define NT 256
 #define VEC 8
+#define CAT_RANGE 32
+#define CAT_SLICE (NT * CAT_RANGE)
 
 /* ------------------------------------------------------------------ Philox */
 
@@ -183,6 +193,86 @@ int64_t fmo_range_width(int64_t V)
     return (w + VEC - 1) / VEC * VEC;
 }
 
+/* inclusive scan of the NT range sums t into h: Hillis-Steele inside each
+ * group of 32, then a sequential scan of the group totals added to later groups */
+static void block_scan(const float *t, float *h)
+{
+    for (int w = 0; w < NT / 32; ++w) {
+        float *a = h + 32 * w;
+        memcpy(a, t + 32 * w, 32 * sizeof(float));
+        for (int off = 1; off < 32; off <<= 1) {
+            float prev[32];
+            memcpy(prev, a, sizeof(prev));
+            for (int l = off; l < 32; ++l) a[l] = prev[l - off] + prev[l];
+        }
+    }
+    float base = 0.0f;
+    for (int w = 0; w < NT / 32; ++w) {
+        float tot = h[32 * w + 31];
+        if (w > 0)
+            for (int l = 0; l < 32; ++l) h[32 * w + l] = base + h[32 * w + l];
+        base = (w == 0) ? tot : base + tot;
+    }
+}
+
+/* range sums t and their inclusive scan h over slice j of the weights */
+static void slice_scan(const float *r, int64_t V, int64_t j, float *t, float *h)
+{
+    for (int i = 0; i < NT; ++i) {
+        float acc = 0.0f;
+        int64_t lo = j * CAT_SLICE + (int64_t)i * CAT_RANGE;
+        for (int64_t v = lo; v < lo + CAT_RANGE && v < V; ++v) acc = acc + r[v];
+        t[i] = acc;
+    }
+    block_scan(t, h);
+}
+
+/* The sliced categorical draw (see the header): the rejection bonus. */
+int64_t fmo_categorical_sliced(const float *r, int64_t V, float u)
+{
+    const int64_t S = (V + CAT_SLICE - 1) / CAT_SLICE;
+    float t[NT], h[NT];
+    float totals[256], prefix[256];
+    if (S > 256) return -1;
+    float run = 0.0f;
+    for (int64_t j = 0; j < S; ++j) {
+        slice_scan(r, V, j, t, h);
+        totals[j] = h[NT - 1];
+        run = (j == 0) ? totals[j] : run + totals[j];
+        prefix[j] = run;
+    }
+    const float total = prefix[S - 1];
+    const float target = u * total;
+    int64_t js = -1;
+    for (int64_t j = 0; j < S; ++j)
+        if (prefix[j] > target) { js = j; break; }
+    if (js < 0)
+        for (int64_t j = S - 1; j >= 0; --j)
+            if (totals[j] > 0.0f) { js = j; break; }
+    if (js < 0) return 0; /* all weights zero */
+    const float base = js > 0 ? prefix[js - 1] : 0.0f;
+    slice_scan(r, V, js, t, h);
+    float g[NT];
+    for (int i = 0; i < NT; ++i) g[i] = base + h[i];
+    int chosen = -1;
+    for (int i = 0; i < NT; ++i)
+        if (g[i] > target) { chosen = i; break; }
+    if (chosen < 0)
+        for (int i = NT - 1; i >= 0; --i)
+            if (t[i] > 0.0f) { chosen = i; break; }
+    if (chosen < 0) return js * CAT_SLICE;
+    float acc = chosen > 0 ? g[chosen - 1] : base;
+    int64_t lo = js * CAT_SLICE + (int64_t)chosen * CAT_RANGE;
+    int64_t hi = lo + CAT_RANGE < V ? lo + CAT_RANGE : V;
+    int64_t last_pos = -1;
+    for (int64_t v = lo; v < hi; ++v) {
+        acc = acc + r[v];
+        if (r[v] > 0.0f) last_pos = v;
+        if (acc > target) return v;
+    }
+    return last_pos >= 0 ? last_pos : lo;
+}
+
 /* Draw an index from the non-negative weights r[0..V) with uniform u. */
 int64_t fmo_categorical(const float *r, int64_t V, float u)
 {
@@ -193,24 +283,7 @@ int64_t fmo_categorical(const float *r, int64_t V, float u)
         for (int64_t v = (int64_t)i * W; v < (int64_t)(i + 1) * W && v < V; ++v) acc = acc + r[v];
         t[i] = acc;
     }
-    /* inclusive scan: Hillis-Steele inside each group of 32 ... */
-    for (int w = 0; w < NT / 32; ++w) {
-        float *a = h + 32 * w;
-        memcpy(a, t + 32 * w, 32 * sizeof(float));
-        for (int off = 1; off < 32; off <<= 1) {
-            float prev[32];
-            memcpy(prev, a, sizeof(prev));
-            for (int l = off; l < 32; ++l) a[l] = prev[l - off] + prev[l];
-        }
-    }
-    /* ... then a sequential scan of the group totals, added to later groups */
-    float base = 0.0f;
-    for (int w = 0; w < NT / 32; ++w) {
-        float tot = h[32 * w + 31];
-        if (w > 0)
-            for (int l = 0; l < 32; ++l) h[32 * w + l] = base + h[32 * w + l];
-        base = (w == 0) ? tot : base + tot;
-    }
+    block_scan(t, h);
     float total = h[NT - 1];
     float target = u * total;
     int chosen = -1;
@@ -312,6 +385,6 @@ void fmo_accept_rejection(const float *target, const int64_t *draft, const float
         if (!any) /* residual.sum() <= 0: fall back to the target distribution */
             for (int64_t v = 0; v < V; ++v) scratch_v[v] = fmo_exp(row[v] / temperature - m) / s;
         float u = fmo_uniform(seed, 0u, (uint32_t)b, offset, 2u);
-        bonus[b] = fmo_categorical(scratch_v, V, u);
+        bonus[b] = fmo_categorical_sliced(scratch_v, V, u);
     }
 }

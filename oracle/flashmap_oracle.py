@@ -387,7 +387,7 @@ def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, tempera
     draws are Philox uniforms: draft slot k of round r (k, 0, r, 3) — the
     first target token uses (0, 0, 0, 3) — acceptance (k, 0, r, 1) and the
     bonus (0, 0, r, 2), each turned into a token by the oracle's categorical
-    sampler.  Returns ``(sequences, acceptance_lengths)``."""
+    sampler (its sliced form for the bonus).  Returns ``(sequences, acceptance_lengths)``."""
     from transformers import DynamicCache
 
     from . import accept
@@ -450,7 +450,8 @@ def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, tempera
                     residual = (residual - draft_probs[0, accepted]).clamp_min(0)
                     if residual.sum() <= 0:
                         residual = tp[accepted]
-                bonus = torch.tensor([accept.categorical(residual.numpy(), accept.uniform(rng_seed, 0, 0, rounds, 2))])
+                bonus = torch.tensor([accept.categorical_sliced(residual.numpy(),
+                                                                accept.uniform(rng_seed, 0, 0, rounds, 2))])
             rounds += 1
             new = torch.cat([draft[:, :accepted], bonus.view(1, 1)], dim=1)
             hits = torch.isin(new[0], stop).nonzero()

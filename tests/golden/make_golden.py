@@ -119,7 +119,7 @@ def spec_case(flashmap, temperature, max_new_tokens=64, seed=0, rng_seed=1234):
     ``torch.randn((1, 16, 256), generator=Generator().manual_seed(77))``; at
     T > 0 the acceptance uniforms are Philox (k, 0, r, 1), the draft rows'
     categorical draws use Philox (k, 0, r, 3) and the bonus draw (0, 0, r, 2),
-    all through the oracle's categorical sampler."""
+    all through the oracle's categorical sampler (its sliced form for the bonus)."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
     sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
@@ -151,7 +151,7 @@ def spec_case(flashmap, temperature, max_new_tokens=64, seed=0, rng_seed=1234):
             out = [accept.categorical(probs[k].float().numpy(), accept.uniform(rng_seed, k, 0, r, 3))
                    for k in range(probs.shape[0])]
             return torch.tensor(out, dtype=torch.int64)[:, None]
-        tok = accept.categorical(probs.float().numpy(), accept.uniform(rng_seed, 0, 0, r, 2))  # bonus (:594)
+        tok = accept.categorical_sliced(probs.float().numpy(), accept.uniform(rng_seed, 0, 0, r, 2))  # bonus (:594)
         rounds["n"] += 1
         return torch.tensor([tok], dtype=torch.int64)
 
@@ -197,7 +197,8 @@ def acceptance_case(flashmap, B, K, V, seed, temperature, rng_seed=1234):
             return torch.tensor([accept.uniform(rng_seed, k, b, 0, 1) for k in range(shape[0])])
 
         def fake_multinomial(probs, n, generator=None, **kw):
-            return torch.tensor([accept.categorical(probs.float().numpy(), accept.uniform(rng_seed, 0, b, 0, 2))])
+            return torch.tensor([accept.categorical_sliced(probs.float().numpy(),
+                                                           accept.uniform(rng_seed, 0, b, 0, 2))])
 
         class Out:
             logits = target[b : b + 1]
