@@ -299,6 +299,133 @@ __device__ __forceinline__ void vec_store_tile(const GemmArgs& a, int m0, int n0
   if (refill_barrier) named_bar_sync(1, 128);
 }
 
+// The q/k-norm epilogue of a wide tile (vector path), over columns
+// [c_begin, c_end) (chunks of 16), in three phases instead of three barriers
+// per chunk: (1) every chunk's per-warp sums of squares of the rounded
+// values (the transposing shuffle reduction, no barrier between chunks),
+// (2) after one barrier every (head, token) 1/rms by the whole block, written
+// back after a second barrier, (3) every chunk normalised, rotated and
+// stored as vectors through two alternating store tiles.  `chunk(c0, v)`
+// yields the 16 accumulator values of the chunk starting at column c0 (the
+// same values both times it is asked).  Same arithmetic as epilogue16.
+template <typename ChunkFn>
+__device__ __forceinline__ void qknorm_wide(const GemmArgs& a, ChunkFn chunk, int r, int mt, int n_tile, int c_begin,
+                                            int c_end, float* xch, __nv_bfloat16* vec_xt) {
+  const int lane = threadIdx.x & 31;
+  const int q = (threadIdx.x >> 5) & 3;
+  const int m = mt * 128 + r;
+  const int hd = a.head_dim, hq = hd >> 5, heads = 128 / hd;
+  const int ncols = c_end - c_begin;
+  const int part = (mt * 128) / a.part_rows;  // 0 q, 1 k, 2 v (uniform over the tile)
+  const bool normed = part < 2;
+  const int d = (m % a.part_rows) % hd;
+  float wd = 0.0f;
+  if (normed) {
+    wd = bf2f((part == 0 ? a.norm_w0 : a.norm_w1)[d]);
+    for (int c0 = c_begin; c0 < c_end; c0 += 16) {
+      float v[16], sq[16];
+      chunk(c0, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float y = round_bf(v[j]);
+        sq[j] = __fmul_rn(y, y);
+      }
+#pragma unroll
+      for (int width = 8; width >= 1; width >>= 1) {
+        const bool up = (lane & (width * 2)) != 0;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+          const float send = up ? sq[i] : sq[i + width];
+          const float keep = up ? sq[i + width] : sq[i];
+          sq[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, width * 2));
+        }
+      }
+      sq[0] = __fadd_rn(sq[0], __shfl_xor_sync(0xffffffffu, sq[0], 1));
+      const int tl = ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+      if ((lane & 1) == 0) xch[q * ncols + (c0 - c_begin) + tl] = sq[0];
+    }
+    named_bar_sync(1, 128);
+    // the head's warp quarters in order, mean, 1 / sqrt(mean + eps); up to 8 per thread
+    constexpr int MAXI = 8;
+    float inv[MAXI];
+    const int t = r;
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k) {
+      const int idx = t + k * 128;
+      inv[k] = 0.0f;
+      if (idx < heads * ncols) {
+        const int hh = idx / ncols, col = idx % ncols;
+        float tot = 0.0f;
+        for (int qq = hh * hq; qq < hh * hq + hq; ++qq) tot = __fadd_rn(tot, xch[qq * ncols + col]);
+        const float mean = __fdiv_rn(tot, (float)hd);
+        inv[k] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+      }
+    }
+    named_bar_sync(1, 128);
+#pragma unroll
+    for (int k = 0; k < MAXI; ++k)
+      if (t + k * 128 < heads * ncols) xch[t + k * 128] = inv[k];
+    named_bar_sync(1, 128);
+  }
+  const int half = hd >> 1;
+  const float* xinv = xch + (q / hq) * ncols;  // this thread's head's 1/rms, by column
+  for (int c0 = c_begin; c0 < c_end; c0 += 16) {
+    const int n0 = n_tile + c0;
+    float v[16], y[16];
+    chunk(c0, v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = round_bf(v[j]);
+    if (normed) {
+      float rc[16], rs[16];
+      if (a.tok_cos != nullptr) {
+        // the tokens' rotary factors, gathered once per draft (positions checked there)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = (n0 + j < a.N) ? n0 + j : 0;
+          rc[j] = a.tok_cos[n * half + (d >> 1)];
+          rs[j] = a.tok_sin[n * half + (d >> 1)];
+        }
+      } else {
+        int pos[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = n0 + j;
+          int pj = (n < a.N) ? a.positions[n] : 0;
+          if (pj < 0 || pj >= a.rope_len) {
+            if (n < a.N) record_error(a.err, DEV_BAD_INDEX);
+            pj = 0;
+          }
+          pos[j] = pj;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          rc[j] = a.rope_cos[(long long)pos[j] * half + (d >> 1)];
+          rs[j] = a.rope_sin[(long long)pos[j] * half + (d >> 1)];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float scale = round_bf(__fmul_rn(wd, xinv[(c0 - c_begin) + j]));
+        const float xn = round_bf(__fmul_rn(y[j], scale));
+        const float other = __shfl_xor_sync(0xffffffffu, xn, 1);
+        float o;
+        if ((d & 1) == 0)
+          o = __fsub_rn(__fmul_rn(xn, rc[j]), __fmul_rn(other, rs[j]));
+        else
+          o = __fadd_rn(__fmul_rn(xn, rc[j]), __fmul_rn(other, rs[j]));
+        y[j] = round_bf(o);
+      }
+    }
+    // two store tiles used alternately; the store tile's barrier also comes
+    // after every thread's reads of xch (1/rms) for this chunk, so after the
+    // last chunk xch may be refilled
+    __nv_bfloat16* tile = vec_xt + ((n0 >> 4) & 1) * 2048;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) tile[j * 128 + r] = f2bf(y[j]);
+    vec_store_tile(a, mt * 128, n0, tile, false);
+  }
+}
+
 // vec_xt (wide blocks, aligned output): QKNORM and unscattered LOGITS store
 // through [16][128] shared tiles as vectors instead of scalars (QKNORM: two
 // tiles from vec_xt on, alternating by chunk; LOGITS: one).
@@ -719,6 +846,7 @@ __global__ void __launch_bounds__(192, 1)
       __nv_bfloat16* vxt = (XT_EPI && vec_epilogue_ok(a) && !(EPI == EPI_LOGITS && a.scatter))
                                ? (EPI == EPI_QKNORM ? ring : xt)
                                : nullptr;
+      const bool qk_wide = EPI == EPI_QKNORM && vxt != nullptr;  // the three-phase q/k-norm epilogue
       if (whole && vec && EPI == EPI_RESID) {
         constexpr int NCH = BN / 16, RG = S::RING;
 #pragma unroll
@@ -747,6 +875,15 @@ __global__ void __launch_bounds__(192, 1)
           vp[0] = vn[0];
           vp[1] = vn[1];
         }
+      } else if (whole && qk_wide) {
+        if constexpr (EPI == EPI_QKNORM)
+          qknorm_wide(
+              a,
+              [&](int c0, float* v) {
+                tmem_ld_x16(taddr + c0, v);
+                tmem_wait_ld();
+              },
+              r, mt, n0, 0, BN, xch, vxt);
       } else if (whole) {
         // chunks of 16 columns; each chunk's global reads issued one chunk ahead
         float pre[32];
@@ -873,7 +1010,7 @@ __global__ void __launch_bounds__(192, 1)
               }
               if (round == 0) {
                 // the epilogue's own global reads go out after the partials' bulk copies
-                have = !vec && epilogue_prefetch<EPI>(a, m, n0, pre);
+                have = !vec && !qk_wide && epilogue_prefetch<EPI>(a, m, n0, pre);
                 if (vec && !RESID_RING) vec_prefetch<EPI>(a, mt * 128, n0, vp);
                 if (vec && RESID_RING)
 #pragma unroll
@@ -891,6 +1028,26 @@ __global__ void __launch_bounds__(192, 1)
               if (!flags[1]) {
                 staged_ok = false;
                 break;
+              }
+              if (qk_wide) {
+                // the head's accumulator, then the later CTAs' staged partials, in contributor order
+                if constexpr (EPI == EPI_QKNORM)
+                  qknorm_wide(
+                      a,
+                      [&](int c0, float* v) {
+                        tmem_ld_x16(taddr + c0, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(0.0f, v[j]);
+                        for (int o = 0; o < others; ++o) {
+                          const float* src = stage + ((long long)o * ncols + (c0 - col0)) * 128 + r;
+#pragma unroll
+                          for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], src[j * 128]);
+                        }
+                      },
+                      r, mt, n0, col0, col0 + ncols, xch, vxt);
+                named_bar_sync(1, 128);  // the staging area is refilled by the next round
+                continue;
               }
               for (int c0 = col0; c0 < col0 + ncols; c0 += 16) {
                 float v[16], nxt[32];
