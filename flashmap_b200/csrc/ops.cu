@@ -101,6 +101,46 @@ __device__ __forceinline__ void load8(const __nv_bfloat16* row, long long vec, l
   }
 }
 
+// 8 consecutive elements of a row kept as loaded (bf16: four 32-bit words,
+// unpacked a pair at a time where they are used), zero-padded past V
+template <typename T>
+struct Raw8;
+
+template <>
+struct Raw8<__nv_bfloat16> {
+  uint32_t w[4];
+  __device__ __forceinline__ void load(const __nv_bfloat16* row, long long vec, long long V, bool aligned) {
+    const long long v0 = vec * 8;
+    if (aligned && v0 + 8 <= V) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(row + v0);
+      w[0] = raw.x;
+      w[1] = raw.y;
+      w[2] = raw.z;
+      w[3] = raw.w;
+    } else {
+      const unsigned short* h = reinterpret_cast<const unsigned short*>(row);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = (v0 + 2 * i < V) ? h[v0 + 2 * i] : 0u, hi = (v0 + 2 * i + 1 < V) ? h[v0 + 2 * i + 1] : 0u;
+        w[i] = lo | (hi << 16);
+      }
+    }
+  }
+  // elements 2i, 2i + 1
+  __device__ __forceinline__ float2 pair(int i) const {
+    return make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+  }
+};
+
+template <>
+struct Raw8<float> {
+  float x[8];
+  __device__ __forceinline__ void load(const float* row, long long vec, long long V, bool aligned) {
+    load8(row, vec, V, aligned, x);
+  }
+  __device__ __forceinline__ float2 pair(int i) const { return make_float2(x[2 * i], x[2 * i + 1]); }
+};
+
 // max of x/T, and (first) argmax of the raw values, over one row
 template <typename T>
 __device__ void row_max_argmax(const T* row, long long V, float temperature, float* red, float* m_out,
@@ -163,31 +203,52 @@ __device__ void row_max_argmax(const T* row, long long V, float temperature, flo
   *m_out = temperature > 0.0f ? block_max(m, red) : 0.0f;
 }
 
-// fixed-order sum of fm_exp(x/T - m): thread i walks vectors i, i+256, ...
-template <typename T>
-__device__ float row_sumexp(const T* row, long long V, float temperature, float m, float* red) {
+// fixed-order sum of fm_exp(x/T - m): thread i walks vectors i, i+256, ...,
+// the elements of a vector in index order.  Full vectors take fm_exp2 on
+// element pairs (values identical to fm_exp), the partial last one fm_exp.
+template <bool UNIT_T, typename T>
+__device__ float row_sumexp_t(const T* row, long long V, float temperature, float m, float* red) {
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   const long long nvec = (V + 7) / 8;
+  const float2 neg_m = make_float2(-m, -m);  // x - m == x + (-m) exactly
   float acc = 0.0f;
   for (long long vec0 = threadIdx.x; vec0 < nvec; vec0 += 4 * RT) {
-    float x[4][8];
+    Raw8<T> x[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
-      if (vec0 + u * RT < nvec) load8(row, vec0 + u * RT, V, aligned, x[u]);
+      if (vec0 + u * RT < nvec) x[u].load(row, vec0 + u * RT, V, aligned);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const long long vec = vec0 + u * RT;
       if (vec >= nvec) break;
+      // x / 1 == x exactly, so the division is skipped at T = 1
+      if (vec * 8 + 8 <= V) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        if (vec * 8 + j >= V) break;
-        // x / 1 == x exactly, so the division is skipped at T = 1
-        const float xt = temperature == 1.0f ? x[u][j] : __fdiv_rn(x[u][j], temperature);
-        acc = __fadd_rn(acc, fm_exp(__fsub_rn(xt, m)));
+        for (int i = 0; i < 4; ++i) {
+          float2 xt = x[u].pair(i);
+          if (!UNIT_T) xt = make_float2(__fdiv_rn(xt.x, temperature), __fdiv_rn(xt.y, temperature));
+          const float2 e = fm_exp2(__fadd2_rn(xt, neg_m));
+          acc = __fadd_rn(acc, e.x);
+          acc = __fadd_rn(acc, e.y);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 xp = x[u].pair(i);
+          if (vec * 8 + 2 * i < V) acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.x : __fdiv_rn(xp.x, temperature), m)));
+          if (vec * 8 + 2 * i + 1 < V)
+            acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.y : __fdiv_rn(xp.y, temperature), m)));
+        }
       }
     }
   }
   return block_sum(acc, red);
+}
+
+template <typename T>
+__device__ float row_sumexp(const T* row, long long V, float temperature, float m, float* red) {
+  return temperature == 1.0f ? row_sumexp_t<true>(row, V, temperature, m, red)
+                             : row_sumexp_t<false>(row, V, temperature, m, red);
 }
 
 __device__ __forceinline__ long long range_width(long long V) {
@@ -776,17 +837,14 @@ __global__ void __launch_bounds__(RT) row_max_slice_kernel(const T* logits, long
 
 template <typename T>
 __global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long long V, float temperature,
-                                                       float* stats, int64_t* argmax, const uint32_t* max_keys) {
+                                                       float* stats, int64_t* argmax) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
   const T* row = logits + (long long)blockIdx.x * V;
   float m;
   long long am = 0;
-  if (max_keys != nullptr && argmax == nullptr && temperature > 0.0f)
-    m = __fdiv_rn(from_orderable_f32(max_keys[blockIdx.x]), temperature);
-  else
-    row_max_argmax(row, V, temperature, red, &m, &am);
+  row_max_argmax(row, V, temperature, red, &m, &am);
   if (argmax && threadIdx.x == 0) argmax[blockIdx.x] = am;
   if (stats) {
     const float s = temperature > 0.0f ? row_sumexp(row, V, temperature, m, red) : 0.0f;
@@ -794,6 +852,25 @@ __global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long lon
       stats[2 * blockIdx.x] = m;
       stats[2 * blockIdx.x + 1] = s;
     }
+  }
+}
+
+// (max, sum) of one row at T > 0 with the max taken from the sliced raw
+// maxima (row_max_slice_kernel): m = max / T, then the fixed-order sum.  Kept
+// apart from row_stats_kernel so the sum loop does not carry the argmax's
+// registers.
+template <typename T>
+__global__ void __launch_bounds__(RT, sizeof(T) == 2 ? 6 : 4) row_sum_keys_kernel(const T* logits, long long V, float temperature,
+                                                          float* stats, const uint32_t* max_keys) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const T* row = logits + (long long)blockIdx.x * V;
+  const float m = __fdiv_rn(from_orderable_f32(max_keys[blockIdx.x]), temperature);
+  const float s = row_sumexp(row, V, temperature, m, red);
+  if (threadIdx.x == 0) {
+    stats[2 * blockIdx.x] = m;
+    stats[2 * blockIdx.x + 1] = s;
   }
 }
 
@@ -1521,7 +1598,7 @@ extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t row
   if (!logits) return set_error(FM_ERR_INVALID, "row_stats: null logits");
   if (rows <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "row_stats: bad arguments");
   return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), logits, (long long)V, temperature, stats,
-                            argmax, (const uint32_t*)nullptr);
+                            argmax);
 }
 
 extern "C" fm_status fm_softmax_rows(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
@@ -1541,7 +1618,7 @@ extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const flo
   if (temperature <= 0.0f) {
     if (!logits) return set_error(FM_ERR_INVALID, "sample_rows: null logits");
     return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * K)), logits, (long long)V, 0.0f,
-                              (float*)nullptr, tokens, (const uint32_t*)nullptr);
+                              (float*)nullptr, tokens);
   }
   if (!probs) return set_error(FM_ERR_INVALID, "sample_rows: T > 0 needs probs");
   return launch_kernel(sample_rows_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false, probs,
@@ -1585,8 +1662,8 @@ extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtyp
   st = FM_DISPATCH_LOGITS(dtype, row_max_slice_kernel, dim3((unsigned)rows, (unsigned)slices), target_logits,
                           (long long)V, max_keys);
   if (st) return st;
-  st = FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), target_logits, (long long)V, temperature,
-                          stats, (int64_t*)nullptr, (const uint32_t*)max_keys);
+  st = FM_DISPATCH_LOGITS(dtype, row_sum_keys_kernel, dim3((unsigned)rows), target_logits, (long long)V, temperature,
+                          stats, (const uint32_t*)max_keys);
   if (st) return st;
   const long long cat_slices = (V + CAT_SLICE - 1) / CAT_SLICE;
   if (cat_slices > CAT_MAX_SLICES) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large for the bonus draw");

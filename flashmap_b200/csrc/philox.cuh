@@ -52,7 +52,12 @@ __device__ __forceinline__ float fm_exp(float x) {
   if (x != x) return x;
   if (x > 88.7228394f) return __int_as_float(0x7f800000);
   if (x < -103.972084f) return 0.0f;
-  const float n = rintf(__fmul_rn(x, 1.44269502162933349609f));
+  // n = x log2(e) rounded half-to-even (the value rintf gives) by the
+  // 1.5 * 2^23 shifter, exact for |x log2(e)| < 2^22 (here <= 150); the
+  // shifter's low mantissa bits are n as an integer, so no float->int
+  // conversion is issued.
+  const float t = __fadd_rn(__fmul_rn(x, 1.44269502162933349609f), 12582912.0f);
+  const float n = __fsub_rn(t, 12582912.0f);
   float r = __fmaf_rn(-n, 0.693145751953125f, x);
   r = __fmaf_rn(-n, 1.42860682030941723212e-6f, r);
   float p = 1.98412698e-4f;
@@ -63,9 +68,33 @@ __device__ __forceinline__ float fm_exp(float x) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  const int e = (int)n;
+  const int e = __float_as_int(t) - 0x4B400000;
   if (e >= -126) return __fmul_rn(p, __uint_as_float((uint32_t)(e + 127) << 23));
   return __fmul_rn(__fmul_rn(p, __uint_as_float((uint32_t)(e + 126 + 127) << 23)), __uint_as_float(1u << 23));
+}
+
+// fm_exp of two lanes with the packed fp32x2 add / multiply / fma of sm_100:
+// every lane rounds exactly as the scalar steps of fm_exp do (the same
+// operations in the same order; -n * c == n * -c exactly), so each value is
+// fm_exp's.  A pair with a lane that is NaN, above the overflow bound, or
+// whose result would be subnormal or zero (e < -126, which also covers the
+// underflow bound) is recomputed by fm_exp itself.
+__device__ __forceinline__ float2 fm_exp2(float2 x) {
+  const float2 t = __fadd2_rn(__fmul2_rn(x, make_float2(1.44269502162933349609f, 1.44269502162933349609f)),
+                              make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  float2 r = __ffma2_rn(n, make_float2(-0.693145751953125f, -0.693145751953125f), x);
+  r = __ffma2_rn(n, make_float2(-1.42860682030941723212e-6f, -1.42860682030941723212e-6f), r);
+  float2 p = __ffma2_rn(make_float2(1.98412698e-4f, 1.98412698e-4f), r, make_float2(1.38888889e-3f, 1.38888889e-3f));
+  p = __ffma2_rn(p, r, make_float2(8.33333333e-3f, 8.33333333e-3f));
+  p = __ffma2_rn(p, r, make_float2(4.16666667e-2f, 4.16666667e-2f));
+  p = __ffma2_rn(p, r, make_float2(1.66666667e-1f, 1.66666667e-1f));
+  p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
+  p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+  p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
+  const int e0 = (int)(__float_as_uint(t.x) - 0x4B400000u), e1 = (int)(__float_as_uint(t.y) - 0x4B400000u);
+  if (!(x.x <= 88.7228394f && x.y <= 88.7228394f) || min(e0, e1) < -126) return make_float2(fm_exp(x.x), fm_exp(x.y));
+  return __fmul2_rn(p, make_float2(__uint_as_float((uint32_t)(e0 + 127) << 23), __uint_as_float((uint32_t)(e1 + 127) << 23)));
 }
 
 // Box-Muller on Philox words: pair p (elements 2p, 2p+1) uses counter (p, 0, offset, 4)

@@ -253,6 +253,20 @@ def test_row_stats_and_softmax_bit_exact(V):
     assert torch.equal(probs, oracle_accept.softmax_rows(logits, 0.7))
 
 
+def test_fm_exp_full_range_bit_exact():
+    """fm_exp over its whole finite range through fp32 softmax rows at T = 1:
+    x - m spans [-110, 0] (normal, subnormal and zero results), each row's max
+    is 0, and every probability must equal the C oracle's bit for bit."""
+    g = torch.Generator().manual_seed(17)
+    logits = -110.0 * torch.rand(4, 65536, generator=g)
+    logits[:, 0] = 0.0
+    logits[1] = -torch.logspace(-8, 2.04, 65536)  # dense near 0 and out to -110
+    logits[1, 0] = 0.0
+    probs = ops.softmax_rows(logits.to(DEV), 1.0).cpu()
+    assert torch.equal(probs, oracle_accept.softmax_rows(logits, 1.0))
+    assert int((probs == 0).sum()) > 0 and int(((probs > 0) & (probs < 1.1754944e-38)).sum()) > 0
+
+
 @pytest.mark.parametrize("V,T", [(2048, 1.0), (3001, 0.7), (151936, 1.0)])
 def test_sample_rows_bit_exact(V, T):
     B, K = 2, 16
