@@ -1056,9 +1056,9 @@ struct RejectionRow {
   float m, s, temperature;
   bool residual;      // max(0, p - q) (else the target's p)
   bool vec;           // rows 16-byte aligned
-  __device__ float p(long long v) const {
-    return __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(to_f(tr[v]), temperature), m)), s);
-  }
+  bool unit_t;        // T == 1: x / T == x exactly, the division is skipped
+  __device__ float scaled(float x) const { return unit_t ? x : __fdiv_rn(x, temperature); }
+  __device__ float p(long long v) const { return __fdiv_rn(fm_exp(__fsub_rn(scaled(to_f(tr[v])), m)), s); }
   __device__ float weight(long long v) const {
     const float pv = p(v);
     if (!residual) return pv;
@@ -1068,22 +1068,29 @@ struct RejectionRow {
   // 32 weights of v0 .. v0 + 31 (all < V) from 16-byte loads issued together
   __device__ bool bulk(long long v0, long long V, float* w) const {
     if (!vec) return false;
-    float x[4][8], qv[4][8];
+    Raw8<T> x[4];
+    float qv[4][8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      load8(tr, v0 / 8 + k, V, true, x[k]);
+      x[k].load(tr, v0 / 8 + k, V, true);
       if (residual) load8(qr, v0 / 8 + k, V, true, qv[k]);
     }
+    const float2 neg_m = make_float2(-m, -m);  // x - m == x + (-m) exactly
 #pragma unroll
     for (int k = 0; k < 4; ++k)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float pv = __fdiv_rn(fm_exp(__fsub_rn(__fdiv_rn(x[k][j], temperature), m)), s);
-        if (!residual) {
-          w[k * 8 + j] = pv;
-        } else {
-          const float d = __fsub_rn(pv, qv[k][j]);
-          w[k * 8 + j] = d > 0.0f ? d : 0.0f;
+      for (int j = 0; j < 8; j += 2) {
+        const float2 xp = x[k].pair(j / 2);
+        const float2 e = fm_exp2(__fadd2_rn(make_float2(scaled(xp.x), scaled(xp.y)), neg_m));
+        const float pv[2] = {__fdiv_rn(e.x, s), __fdiv_rn(e.y, s)};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (!residual) {
+            w[k * 8 + j + h] = pv[h];
+          } else {
+            const float d = __fsub_rn(pv[h], qv[k][j + h]);
+            w[k * 8 + j + h] = d > 0.0f ? d : 0.0f;
+          }
         }
       }
     return true;
@@ -1102,6 +1109,7 @@ __device__ RejectionRow<T> rejection_row(const T* target, const float* q, const 
   r.temperature = temperature;
   r.residual = acc < K;
   r.vec = (reinterpret_cast<uintptr_t>(r.tr) & 15) == 0 && (reinterpret_cast<uintptr_t>(r.qr) & 15) == 0;
+  r.unit_t = temperature == 1.0f;
   return r;
 }
 
