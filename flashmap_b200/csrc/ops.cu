@@ -1114,16 +1114,19 @@ __device__ RejectionRow<T> rejection_row(const T* target, const float* q, const 
 }
 
 // this thread's range sum t and the block's inclusive scan h over slice j
-// (Hillis-Steele inside each warp, then the warp totals in order); sm holds >= 16 floats
+// (Hillis-Steele inside each warp, then the warp totals in order); sm holds
+// >= 16 floats.  bulk tells whether bw holds the range's 32 weights.
 template <typename T, bool TargetOnly>
-__device__ void slice_scan(const RejectionRow<T>& w, long long V, long long j, float* sm, float& t, float& h) {
+__device__ __forceinline__ void slice_scan(const RejectionRow<T>& w, long long V, long long j, float* sm, float& t,
+                                           float& h, float (&bw)[CAT_RANGE], bool& bulk) {
   const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
   const long long lo = j * CAT_SLICE + (long long)i * CAT_RANGE, hi = min(lo + CAT_RANGE, V);
   RejectionRow<T> r = w;
   if (TargetOnly) r.residual = false;
   t = 0.0f;
-  float bw[32];
+  bulk = false;
   if (hi - lo == CAT_RANGE && r.bulk(lo, V, bw)) {
+    bulk = true;
 #pragma unroll
     for (int k = 0; k < 32; ++k) t = __fadd_rn(t, bw[k]);
   } else {
@@ -1186,8 +1189,9 @@ __global__ void __launch_bounds__(RT) residual_slices_kernel(const T* target, co
   const int b = blockIdx.x;
   const long long j = blockIdx.y;
   const RejectionRow<T> w = rejection_row(target, q, stats, V, K, temperature, b, (int)accepted[b]);
-  float t, h;
-  slice_scan<T, false>(w, V, j, sm, t, h);
+  float t, h, bw[CAT_RANGE];
+  bool bulk;
+  slice_scan<T, false>(w, V, j, sm, t, h, bw, bulk);
   if (threadIdx.x == RT - 1) totals[(long long)b * CAT_MAX_SLICES + j] = h;
 }
 
@@ -1223,8 +1227,9 @@ __global__ void __launch_bounds__(RT) residual_pick_kernel(const T* target, cons
     // no positive residual weight: the target's distribution, its slice totals here
     w.residual = false;
     for (int j = 0; j < S; ++j) {
-      float t, h;
-      slice_scan<T, true>(w, V, j, sm, t, h);
+      float t, h, bw[CAT_RANGE];
+      bool bulk;
+      slice_scan<T, true>(w, V, j, sm, t, h, bw, bulk);
       if (i == RT - 1) tot[j] = h;
     }
     __syncthreads();
@@ -1261,36 +1266,47 @@ __global__ void __launch_bounds__(RT) residual_pick_kernel(const T* target, cons
     if (i == 0) bonus[b] = 0;
     return;
   }
-  float t, h;
+  float t, h, bw[CAT_RANGE];
+  bool bulk;
   if (w.residual)
-    slice_scan<T, false>(w, V, js, sm, t, h);
+    slice_scan<T, false>(w, V, js, sm, t, h, bw, bulk);
   else
-    slice_scan<T, true>(w, V, js, sm, t, h);
+    slice_scan<T, true>(w, V, js, sm, t, h, bw, bulk);
   g[i] = __fadd_rn(s_base, h);
   const float target_u = s_target;
   const int first = block_min_int(g[i] > target_u ? i : RT, ired);
   const int lastpos = block_max_int(t > 0.0f ? i : -1, ired);
-  if (i == 0) {
-    const int chosen = first < RT ? first : lastpos;
-    long long pick = js * CAT_SLICE;
-    if (chosen >= 0) {
-      float run = chosen > 0 ? g[chosen - 1] : s_base;
-      const long long lo = js * CAT_SLICE + (long long)chosen * CAT_RANGE, hi = min(lo + CAT_RANGE, V);
-      long long last = -1;
-      pick = -1;
-      for (long long v = lo; v < hi; ++v) {
-        const float wv = w.weight(v);
-        run = __fadd_rn(run, wv);
-        if (wv > 0.0f) last = v;
-        if (run > target_u) {
-          pick = v;
-          break;
-        }
-      }
-      if (pick < 0) pick = last >= 0 ? last : lo;
-    }
-    bonus[b] = pick;
+  const int chosen = first < RT ? first : lastpos;
+  if (chosen < 0) {
+    if (i == 0) bonus[b] = js * CAT_SLICE;
+    return;
   }
+  // the chosen range's own thread searches it in index order (its weights
+  // are still in registers when the range was loaded in bulk)
+  if (i != chosen) return;
+  float run = chosen > 0 ? g[chosen - 1] : s_base;
+  const long long lo = js * CAT_SLICE + (long long)chosen * CAT_RANGE, hi = min(lo + CAT_RANGE, V);
+  long long last = -1, pick = -1;
+  if (bulk) {
+#pragma unroll
+    for (int k = 0; k < CAT_RANGE; ++k)
+      if (pick < 0) {
+        run = __fadd_rn(run, bw[k]);
+        if (bw[k] > 0.0f) last = lo + k;
+        if (run > target_u) pick = lo + k;
+      }
+  } else {
+    for (long long v = lo; v < hi; ++v) {
+      const float wv = w.weight(v);
+      run = __fadd_rn(run, wv);
+      if (wv > 0.0f) last = v;
+      if (run > target_u) {
+        pick = v;
+        break;
+      }
+    }
+  }
+  bonus[b] = pick >= 0 ? pick : (last >= 0 ? last : lo);
 }
 
 __global__ void transpose_bf16_kernel(const __nv_bfloat16* in, __nv_bfloat16* out, long long R, long long C) {
