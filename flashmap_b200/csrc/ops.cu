@@ -206,23 +206,24 @@ __device__ void row_max_argmax(const T* row, long long V, float temperature, flo
 // fixed-order sum of fm_exp(x/T - m): thread i walks vectors i, i+256, ...,
 // the elements of a vector in index order.  Full vectors take fm_exp2 on
 // element pairs (values identical to fm_exp), the partial last one fm_exp.
+// (Vector indices are 32-bit: the callers bound V below 2^31.)
 template <bool UNIT_T, typename T>
 __device__ float row_sumexp_t(const T* row, long long V, float temperature, float m, float* red) {
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-  const long long nvec = (V + 7) / 8;
+  const int nvec = (int)((V + 7) / 8), nfull = (int)(V / 8);
   const float2 neg_m = make_float2(-m, -m);  // x - m == x + (-m) exactly
   float acc = 0.0f;
-  for (long long vec0 = threadIdx.x; vec0 < nvec; vec0 += 4 * RT) {
+  for (int vec0 = threadIdx.x; vec0 < nvec; vec0 += 4 * RT) {
     Raw8<T> x[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u)
       if (vec0 + u * RT < nvec) x[u].load(row, vec0 + u * RT, V, aligned);
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const long long vec = vec0 + u * RT;
+      const int vec = vec0 + u * RT;
       if (vec >= nvec) break;
       // x / 1 == x exactly, so the division is skipped at T = 1
-      if (vec * 8 + 8 <= V) {
+      if (vec < nfull) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           float2 xt = x[u].pair(i);
@@ -235,8 +236,9 @@ __device__ float row_sumexp_t(const T* row, long long V, float temperature, floa
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 xp = x[u].pair(i);
-          if (vec * 8 + 2 * i < V) acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.x : __fdiv_rn(xp.x, temperature), m)));
-          if (vec * 8 + 2 * i + 1 < V)
+          if ((long long)vec * 8 + 2 * i < V)
+            acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.x : __fdiv_rn(xp.x, temperature), m)));
+          if ((long long)vec * 8 + 2 * i + 1 < V)
             acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.y : __fdiv_rn(xp.y, temperature), m)));
         }
       }
@@ -1620,7 +1622,8 @@ fm_status greedy_sliced(const void* logits, int32_t dtype, const int64_t* draft,
 extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
                                   float* stats, int64_t* argmax, fm_stream stream) {
   if (!logits) return set_error(FM_ERR_INVALID, "row_stats: null logits");
-  if (rows <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "row_stats: bad arguments");
+  if (rows <= 0 || V <= 0 || V >= (1ll << 31) || bad_dtype(dtype))
+    return set_error(FM_ERR_SHAPE, "row_stats: bad arguments");
   return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)rows), logits, (long long)V, temperature, stats,
                             argmax);
 }
@@ -1628,7 +1631,7 @@ extern "C" fm_status fm_row_stats(const void* logits, int32_t dtype, int64_t row
 extern "C" fm_status fm_softmax_rows(const void* logits, int32_t dtype, int64_t rows, int64_t V, float temperature,
                                      float* probs, fm_stream stream) {
   if (!logits || !probs) return set_error(FM_ERR_INVALID, "softmax_rows: null pointer");
-  if (rows <= 0 || V <= 0 || !(temperature > 0.0f) || bad_dtype(dtype))
+  if (rows <= 0 || V <= 0 || V >= (1ll << 31) || !(temperature > 0.0f) || bad_dtype(dtype))
     return set_error(FM_ERR_SHAPE, "softmax_rows: bad arguments");
   return FM_DISPATCH_LOGITS(dtype, softmax_rows_kernel, dim3((unsigned)rows), logits, (long long)V, temperature,
                             probs);

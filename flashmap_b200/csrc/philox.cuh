@@ -76,9 +76,11 @@ __device__ __forceinline__ float fm_exp(float x) {
 // fm_exp of two lanes with the packed fp32x2 add / multiply / fma of sm_100:
 // every lane rounds exactly as the scalar steps of fm_exp do (the same
 // operations in the same order; -n * c == n * -c exactly), so each value is
-// fm_exp's.  A pair with a lane that is NaN, above the overflow bound, or
-// whose result would be subnormal or zero (e < -126, which also covers the
-// underflow bound) is recomputed by fm_exp itself.
+// fm_exp's.  The fast path needs e = bits(t) - 0x4B400000 in [-126, 127] on
+// both lanes (a normal result, no overflow); NaN, infinities, large inputs
+// and subnormal or zero results all fall outside, and such a pair is
+// recomputed by fm_exp itself.  The scale 2^e is (bits(t) << 23) + bits(1.0f),
+// as 0x4B400000 << 23 vanishes modulo 2^32.
 __device__ __forceinline__ float2 fm_exp2(float2 x) {
   const float2 t = __fadd2_rn(__fmul2_rn(x, make_float2(1.44269502162933349609f, 1.44269502162933349609f)),
                               make_float2(12582912.0f, 12582912.0f));
@@ -92,9 +94,10 @@ __device__ __forceinline__ float2 fm_exp2(float2 x) {
   p = __ffma2_rn(p, r, make_float2(0.5f, 0.5f));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
   p = __ffma2_rn(p, r, make_float2(1.0f, 1.0f));
-  const int e0 = (int)(__float_as_uint(t.x) - 0x4B400000u), e1 = (int)(__float_as_uint(t.y) - 0x4B400000u);
-  if (!(x.x <= 88.7228394f && x.y <= 88.7228394f) || min(e0, e1) < -126) return make_float2(fm_exp(x.x), fm_exp(x.y));
-  return __fmul2_rn(p, make_float2(__uint_as_float((uint32_t)(e0 + 127) << 23), __uint_as_float((uint32_t)(e1 + 127) << 23)));
+  const uint32_t b0 = __float_as_uint(t.x), b1 = __float_as_uint(t.y);
+  // e + 126 = bits - (0x4B400000 - 126), in [0, 253] on the fast path
+  if (max(b0 - 0x4B3FFF82u, b1 - 0x4B3FFF82u) > 253u) return make_float2(fm_exp(x.x), fm_exp(x.y));
+  return __fmul2_rn(p, make_float2(__uint_as_float((b0 << 23) + 0x3F800000u), __uint_as_float((b1 << 23) + 0x3F800000u)));
 }
 
 // Box-Muller on Philox words: pair p (elements 2p, 2p+1) uses counter (p, 0, offset, 4)
