@@ -1,7 +1,7 @@
 // Shared device helpers for the FlashMap B200 kernels (sm_100a only).
 //
 // Thin inline-PTX wrappers for the Blackwell data path: mbarriers, TMA
-// tensor copies (cp.async.bulk.tensor, never with cluster multicast),
+// tensor copies (cp.async.bulk.tensor, each CTA loading its own tiles),
 // tcgen05 MMA/TMEM, and programmatic dependent launch (griddepcontrol).
 // Every wait is bounded by the global timer; a wait that runs out records an
 // error code in the caller-provided status word and returns false, so a bug
