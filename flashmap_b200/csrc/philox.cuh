@@ -7,9 +7,9 @@
 //
 // fm_exp: e^x by Cody-Waite range reduction (x = n ln2 + r, ln2 split into a
 // 16-bit head and a tail), the degree-7 Taylor polynomial of e^r in Horner
-// form with fused multiply-adds, and an exact power-of-two scale.  Every
-// operation is an explicitly rounded intrinsic, so host C with the same
-// steps reproduces it bit for bit.
+// form with fused multiply-adds, and an exact power-of-two scale (in two
+// steps below 2^-126 and at 2^128).  Every operation is an explicitly
+// rounded intrinsic, so host C with the same steps reproduces it bit for bit.
 #pragma once
 
 #include "common.cuh"
@@ -69,6 +69,8 @@ __device__ __forceinline__ float fm_exp(float x) {
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
   const int e = __float_as_int(t) - 0x4B400000;
+  // e = 128 (x <= 88.7228): scale by 2^127, then 2, so a product below FLT_MAX stays finite
+  if (e > 127) return __fmul_rn(__fmul_rn(p, __uint_as_float(254u << 23)), 2.0f);
   if (e >= -126) return __fmul_rn(p, __uint_as_float((uint32_t)(e + 127) << 23));
   return __fmul_rn(__fmul_rn(p, __uint_as_float((uint32_t)(e + 126 + 127) << 23)), __uint_as_float(1u << 23));
 }
@@ -77,9 +79,9 @@ __device__ __forceinline__ float fm_exp(float x) {
 // every lane rounds exactly as the scalar steps of fm_exp do (the same
 // operations in the same order; -n * c == n * -c exactly), so each value is
 // fm_exp's.  The fast path needs e = bits(t) - 0x4B400000 in [-126, 127] on
-// both lanes (a normal result, no overflow); NaN, infinities, large inputs
-// and subnormal or zero results all fall outside, and such a pair is
-// recomputed by fm_exp itself.  The scale 2^e is (bits(t) << 23) + bits(1.0f),
+// both lanes, where fm_exp scales with one multiply; NaN, infinities, large
+// inputs and the two-step scales (e < -126, e = 128) all fall outside, and
+// such a pair is recomputed by fm_exp itself.  The scale 2^e is (bits(t) << 23) + bits(1.0f),
 // as 0x4B400000 << 23 vanishes modulo 2^32.
 __device__ __forceinline__ float2 fm_exp2(float2 x) {
   const float2 t = __fadd2_rn(__fmul2_rn(x, make_float2(1.44269502162933349609f, 1.44269502162933349609f)),

@@ -31,11 +31,19 @@ def build() -> str:
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
-            build()
+        try:
+            build()  # make rebuilds the library when accept_oracle.c is newer
+        except (OSError, subprocess.CalledProcessError):
+            if not os.path.exists(_LIB_PATH):
+                raise
         L = ctypes.CDLL(_LIB_PATH)
         L.fmo_exp.restype = ctypes.c_float
         L.fmo_exp.argtypes = [ctypes.c_float]
+        L.fmo_exp_shifter.restype = ctypes.c_float
+        L.fmo_exp_shifter.argtypes = [ctypes.c_float, ctypes.POINTER(ctypes.c_int)]
+        L.fmo_exp_shifter_sweep.restype = ctypes.c_int64
+        L.fmo_exp_shifter_sweep.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_int64,
+                                            ctypes.POINTER(ctypes.c_int64)]
         L.fmo_uniform.restype = ctypes.c_float
         L.fmo_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
         L.fmo_philox.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint32)]
@@ -68,6 +76,21 @@ def _ptr(a: np.ndarray, typ):
 
 def fm_exp(x: float) -> float:
     return lib().fmo_exp(float(x))
+
+
+def fm_exp_shifter(x: float):
+    """The kernels' paired formulation of fm_exp for one lane: (value, fast)."""
+    fast = ctypes.c_int()
+    v = lib().fmo_exp_shifter(float(x), ctypes.byref(fast))
+    return v, bool(fast.value)
+
+
+def fm_exp_shifter_sweep(start: int, stride: int, count: int):
+    """Over the float bit patterns start + i * stride (i < count, modulo 2^32):
+    (inputs on the fast path, those whose value differs from fm_exp)."""
+    fast = ctypes.c_int64()
+    bad = lib().fmo_exp_shifter_sweep(start & 0xFFFFFFFF, stride & 0xFFFFFFFF, int(count), ctypes.byref(fast))
+    return fast.value, bad
 
 
 def philox(ctr, seed: int) -> list:
@@ -155,6 +178,8 @@ __all__ = [
     "categorical",
     "categorical_sliced",
     "fm_exp",
+    "fm_exp_shifter",
+    "fm_exp_shifter_sweep",
     "philox",
     "row_stats",
     "sample_rows",

@@ -13,8 +13,9 @@
  *   - exp is fm_exp(): Cody-Waite range reduction x = n ln2 + r with ln2 split
  *     into a 16-bit head and a tail, the degree-7 Taylor polynomial of e^r
  *     evaluated by Horner with fused multiply-adds, and an exact power-of-two
- *     scale (two steps below 2^-126).  Written from the mathematics; checked
- *     against the C library's expf for accuracy in the tests.
+ *     scale (two steps below 2^-126 and at 2^128).  Written from the
+ *     mathematics; checked against the exact exponential for accuracy in
+ *     tests/test_fm_exp_oracle.py.
  *   - row reductions (max, sum of exp) use 256 "threads": thread i walks the
  *     8-element vectors i, i+256, i+512, ... in order; the 256 partials are
  *     combined by the warp tree (offsets 16,8,4,2,1 within each group of 32,
@@ -112,6 +113,10 @@ float fmo_exp(float x)
     p = fmaf(p, r, 1.0f);
     int e = (int)n;
     union { uint32_t u; float f; } s;
+    if (e > 127) { /* e = 128 (x <= 88.7228): 2^127, then 2 (the product stays finite below FLT_MAX) */
+        s.u = 254u << 23;
+        return (p * s.f) * 2.0f;
+    }
     if (e >= -126) {
         s.u = (uint32_t)(e + 127) << 23;
         return p * s.f;
@@ -120,6 +125,56 @@ float fmo_exp(float x)
     union { uint32_t u; float f; } t;
     t.u = 1u << 23; /* 2^-126 */
     return (p * s.f) * t.f;
+}
+
+/* The formulation of fm_exp that the CUDA kernels evaluate on element pairs
+ * (fm_exp2 in flashmap_b200/csrc/philox.cuh), restated for one lane: n by
+ * the 1.5 * 2^23 shifter t = x * log2(e) + 1.5 * 2^23 (round half to even,
+ * as rintf), the fast path taken when e = bits(t) - 0x4B400000 lies in
+ * [-126, 127] (where fmo_exp scales with one multiply), its scale
+ * (bits(t) << 23) + bits(1.0f).  *fast tells whether
+ * the fast path applies; where it does not, the kernels call fm_exp itself. */
+float fmo_exp_shifter(float x, int* fast)
+{
+    union { float f; uint32_t u; } t, s;
+    volatile float y = x * LOG2E; /* rounded before the shifter, as on the GPU */
+    t.f = y + 12582912.0f;
+    const float n = t.f - 12582912.0f;
+    *fast = (uint32_t)(t.u - 0x4B3FFF82u) <= 253u;
+    if (!*fast) return fmo_exp(x);
+    float r = fmaf(-n, LN2_HI, x);
+    r = fmaf(-n, LN2_LO, r);
+    float p = 1.98412698e-4f;
+    p = fmaf(p, r, 1.38888889e-3f);
+    p = fmaf(p, r, 8.33333333e-3f);
+    p = fmaf(p, r, 4.16666667e-2f);
+    p = fmaf(p, r, 1.66666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    s.u = (t.u << 23) + 0x3F800000u;
+    return p * s.f;
+}
+
+/* Inputs with bit patterns start, start + stride, ... (count of them, modulo
+ * 2^32): how many take the fast path (*fast_count) and how many of those
+ * differ from fmo_exp in any bit (the return value). */
+int64_t fmo_exp_shifter_sweep(uint32_t start, uint32_t stride, int64_t count, int64_t* fast_count)
+{
+    int64_t bad = 0, fast_n = 0;
+    uint32_t u = start;
+    for (int64_t i = 0; i < count; ++i, u += stride) {
+        union { uint32_t u; float f; } x, a, b;
+        x.u = u;
+        int fast = 0;
+        a.f = fmo_exp_shifter(x.f, &fast);
+        if (!fast) continue;
+        ++fast_n;
+        b.f = fmo_exp(x.f);
+        if (a.u != b.u) ++bad;
+    }
+    *fast_count = fast_n;
+    return bad;
 }
 
 /* ------------------------------------------------------------------ reductions */
