@@ -410,11 +410,12 @@ FM_API fm_status fm_kv_norm_rope_write_pool(const void* kv, int64_t tokens, int6
 /* Logit rows may be bf16 (logits_dtype 0) or fp32 (logits_dtype 1). */
 
 /* Per-row max m and sum of exp(x/T - m) (fixed reduction order) and the first
- * argmax of logit rows. stats [rows][2] fp32, argmax [rows] int64 (either may be NULL). */
+ * argmax of logit rows. stats [rows][2] fp32, argmax [rows] int64 (either may be NULL).
+ * V < 2^31 (else FM_ERR_SHAPE). */
 FM_API fm_status fm_row_stats(const void* logits, int32_t logits_dtype, int64_t rows, int64_t V, float temperature,
                               float* stats, int64_t* argmax, fm_stream stream);
 
-/* probs = softmax(logits / T) in fp32, rows of V (draft_probs of :556). */
+/* probs = softmax(logits / T) in fp32, rows of V < 2^31 (draft_probs of :556). */
 FM_API fm_status fm_softmax_rows(const void* logits, int32_t logits_dtype, int64_t rows, int64_t V,
                                  float temperature, float* probs, fm_stream stream);
 
