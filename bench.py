@@ -44,7 +44,7 @@ METRIC = "drafted tokens/sec (K=16) at 1/2/4/8 B200; batch-1 pass µs vs HBM flo
 CONFIG2 = dict(target_hidden_size=4096, vocab_size=151936, target_layer_ids=[1], block_size=16, hidden_size=2048,
                num_hidden_layers=8, num_attention_heads=16, intermediate_size=8192, mlp_type="gelu")
 CONTEXT = 2048
-# SURVEY config 5: the Qwen3.8-27B map (SwiGLU, 32768-token state vocabulary of 248320)
+# Config 5: the Qwen3.8-27B map (SwiGLU, 32768-token state vocabulary of 248320)
 CONFIG5 = dict(target_hidden_size=5120, vocab_size=248320, state_vocab_size=32768, target_layer_ids=[1],
                block_size=16, hidden_size=2560, num_hidden_layers=10, num_attention_heads=20, intermediate_size=6912,
                mlp_type="swiglu")
@@ -260,7 +260,7 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-# ------------------------------------------------------------------ secondary workloads (SURVEY configs 3, 4)
+# ------------------------------------------------------------------ secondary workloads (configs 3, 4)
 
 def measured_peak_tensor():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -330,7 +330,7 @@ def time_replays(session, steps: int, warmup: int, world: int) -> float:
 
 
 def run_config3(args, world, rank, local):
-    """Batched ragged drafting: SURVEY config 3 (the config-2 map, 64 sequences
+    """Batched ragged drafting: config 3 (the config-2 map, 64 sequences
     per GPU, contexts U[512, 4096], one jump and two jumps) or config 5 (the
     27B map, SwiGLU and a state vocabulary, 64 requests per GPU — the per-GPU
     chunk of 512 requests over 8 GPUs — contexts U[1024, 8192], one jump).
@@ -441,7 +441,7 @@ def run_paged(args, world, rank, local):
 
 
 def run_config4(args, world, rank, local):
-    """Acceptance (SURVEY config 4): target logits (64, 17, 151936) bf16 ~ N(0, 2^2),
+    """Acceptance (config 4): target logits (64, 17, 151936) bf16 ~ N(0, 2^2),
     drafted tokens U[0, V), draft probabilities softmax(N(0,1)); greedy and
     rejection at T = 1 with Philox seed 1234."""
     import ctypes

@@ -170,8 +170,10 @@ def test_config2_draft_parity():
     reference code executed by PyTorch on this GPU (cuBLAS/SDPA instead of the
     CPU kernels) is the yardstick, and the CUDA path must agree with the CPU
     reference at least as well (0.5% slack) and never below 97%.  The
-    north-star 99.9% is printed for the record; it lies below that floor for
-    the seeded random-init weights."""
+    north-star 99.9% is printed for the record; it lies beyond the bf16
+    noise floor of the algorithm for the seeded random-init weights (the
+    reference's own code run by PyTorch on a B200 agrees with its CPU run on
+    about 98.6% of positions)."""
     from oracle.flashmap_oracle import Oracle
     from flashmap_b200.synthetic import synthetic_state_dict
 
@@ -218,7 +220,7 @@ def test_config2_draft_parity():
 def test_ragged_batch_matches_per_sequence_oracle():
     """A batch of sequences with ragged contexts (the packed varlen
     extend_context and one batched draft) equals each sequence drafted alone
-    by the oracle at batch 1 (SURVEY config 3 at config-1/5S sizes)."""
+    by the oracle at batch 1 (the ragged batch of config 3 at config-1/5S sizes)."""
     for cfg, lens in ((CONFIG1, [40, 7, 129]), (CONFIG5S, [3, 64])):
         config, model, oracle, emb, head = build(cfg, seed=8)
         E, W = Emb(emb.to(DEV)), Head(head.to(DEV))
