@@ -290,11 +290,14 @@ def test_accept_greedy_bit_exact(B, K, V, seed):
     assert acc.cpu().tolist() == racc.tolist() and bonus.cpu().tolist() == rbonus.tolist()
 
 
+@pytest.mark.parametrize("logits_dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("B,K,V,seed,T", [(24, 16, 3001, 6, 1.0), (24, 16, 2048, 7, 0.7), (6, 16, 151936, 9, 1.0)])
-def test_accept_rejection_bit_exact(B, K, V, seed, T):
+def test_accept_rejection_bit_exact(B, K, V, seed, T, logits_dtype):
+    """bf16 and fp32 target logits (the fp32 rows hold the same values: bf16 widens exactly)."""
     from tests.golden.inputs import acceptance_inputs
 
     target, draft, q = acceptance_inputs(B, K, V, seed, T)
+    target = target.to(logits_dtype)
     acc, bonus = ops.accept_rejection(target.to(DEV), draft.to(DEV), q.to(DEV), T, seed=1234, offset=0)
     racc, rbonus = oracle_accept.accept_rejection(target, draft, q, T, seed=1234, offset=0)
     assert acc.cpu().tolist() == racc.tolist()
