@@ -7,7 +7,7 @@
 (``max_position_embeddings``, ``dspark_config``); and, for a drafter over the
 full vocabulary with a restricted draft vocabulary, ``draft_vocab.safetensors``
 (``counts``, ``ids``).  The folder loads through
-``FlashMapDraftModel.from_pretrained`` and the sglang plugin's
+``FlashMapDraftModel.from_pretrained`` and the vLLM and sglang plugins'
 ``load_weights`` with every tensor and model field as written."""
 
 import json
@@ -77,6 +77,16 @@ def test_from_pretrained_loads_release_folder(tmp_path, cfg):
     assert model.config.dspark_config["mask_token_id"] == config.vocab_size - 1
 
 
+def folder_entries(folder):
+    """(name, tensor) of the folder's safetensors files, as an engine's loader iterates them."""
+    for name in ("model.safetensors", "draft_vocab.safetensors"):
+        path = os.path.join(folder, name)
+        if os.path.exists(path):
+            with safe_open(path, "pt") as handle:
+                for key in handle.keys():
+                    yield key, handle.get_tensor(key)
+
+
 @pytest.mark.parametrize("cfg,draft_vocab", [(CONFIG1, 512), (CONFIG5S, 0)])
 def test_sglang_plugin_loads_release_folder(tmp_path, cfg, draft_vocab):
     from flashmap_b200 import sglang_model as SG
@@ -85,16 +95,7 @@ def test_sglang_plugin_loads_release_folder(tmp_path, cfg, draft_vocab):
     config, weights, ranking = write_release(folder, cfg, draft_vocab=draft_vocab)
     loaded_config = FlashMapConfig.from_pretrained(folder)
     sm = SG.FlashMapDraftModel(loaded_config)
-
-    def entries():
-        for name in ("model.safetensors", "draft_vocab.safetensors"):
-            path = os.path.join(folder, name)
-            if os.path.exists(path):
-                with safe_open(path, "pt") as handle:
-                    for key in handle.keys():
-                        yield key, handle.get_tensor(key)
-
-    sm.load_weights(entries())
+    sm.load_weights(folder_entries(folder))
     params = {**dict(sm.named_parameters()), **dict(sm.named_buffers())}
     for name, tensor in weights.items():
         assert torch.equal(params[name].to(tensor.dtype), tensor), name
@@ -102,3 +103,23 @@ def test_sglang_plugin_loads_release_folder(tmp_path, cfg, draft_vocab):
     assert sm.draft_vocab_size == want
     if ranking is not None:
         assert torch.equal(sm._vocab_ranking, ranking["ids"])
+
+
+@pytest.mark.parametrize("cfg,draft_vocab", [(CONFIG1, 512), (CONFIG5S, 0)])
+def test_vllm_plugin_loads_release_folder(tmp_path, cfg, draft_vocab):
+    """vLLM's loader: ``draft_vocab_size`` from the folder's header sizes d2t,
+    ``draft_ids`` (state vocabulary) or the ranking's ``ids`` fill it."""
+    from flashmap_b200 import vllm_model as VL
+    from tests.test_plugins import vllm_config
+
+    folder = str(tmp_path / "release")
+    config, weights, ranking = write_release(folder, cfg, draft_vocab=draft_vocab)
+    m = VL.FlashMapDraftModel(vllm_config=vllm_config(FlashMapConfig.from_pretrained(folder)))
+    m.load_weights(folder_entries(folder))
+    params = {**dict(m.named_parameters()), **dict(m.named_buffers())}
+    for name, tensor in weights.items():
+        assert torch.equal(params["model." + name].to(tensor.dtype), tensor), name
+    size = config.state_vocab_size or draft_vocab
+    assert m.d2t is not None and m.d2t.shape[0] == size
+    hot = weights["draft_ids"] if config.state_vocab_size else ranking["ids"][:size].sort().values
+    assert torch.equal(m.d2t + torch.arange(size), hot)
