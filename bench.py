@@ -669,7 +669,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch", choices=["auto", "kernels"], default="auto",
-                    help="launch structure of a draft (both the kernel sequence; the persistent pass is withdrawn)")
+                    help="launch structure of a draft (both: the kernel sequence)")
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "paged"], default="config2",
                     help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance), "
                          "config5 (27B map, batch 64 ragged), paged (vLLM paged cross-attention operator)")

@@ -52,14 +52,14 @@ class PlanConfig(ctypes.Structure):
                 ("launch_mode", c_int32)]
 
 
-LAUNCH_AUTO, LAUNCH_KERNELS, LAUNCH_PERSISTENT = 0, 1, 2
+LAUNCH_AUTO, LAUNCH_KERNELS = 0, 1
 
 
 class DraftIO(ctypes.Structure):
     _fields_ = [("anchor_ids", c_void_p), ("lengths", c_void_p), ("z", c_void_p), ("noise", c_void_p),
                 ("seed", c_uint64), ("offset", c_uint32), ("offset_ptr", c_void_p), ("logits", c_void_p),
                 ("ldl", c_int64),
-                ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p), ("trace", c_void_p)]
+                ("scatter", c_int32), ("tokens", c_void_p), ("hidden", c_void_p)]
 
 
 class ForwardIO(ctypes.Structure):
@@ -112,8 +112,6 @@ _SIGNATURES = {
     "fm_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                              c_int, c_void_p, c_size_t, c_void_p, c_void_p]),
     "fm_gemm_grid": (c_int32, [c_int64, c_int64, c_int64]),
-    "fm_gemm_bf16_trace": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
-                                   c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p]),
     "fm_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "fm_adaln": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "fm_rope_table": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
@@ -179,8 +177,6 @@ _SIGNATURES = {
     "fm_plan_destroy": (c_int, [c_void_p]),
     "fm_plan_error_word": (c_void_p, [c_void_p]),
     "fm_plan_last_launches": (c_int64, [c_void_p]),
-    "fm_plan_persistent": (c_int32, [c_void_p, ctypes.c_char_p, ctypes.c_size_t]),
-    "fm_plan_pass_shape": (c_int, [c_void_p, ctypes.POINTER(c_int32), ctypes.POINTER(c_int32)]),
     "fm_plan_lm_head": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
     "fm_draft": (c_int, [c_void_p, ctypes.POINTER(DraftIO), c_void_p]),
     "fm_extend_context": (c_int, [c_void_p, ctypes.POINTER(ExtendIO), c_void_p]),

@@ -62,8 +62,7 @@ __global__ void __launch_bounds__(SA_THREADS) self_attn_kernel(SelfAttnArgs a) {
 }
 
 // Blocks of 16 slots with head_dim 64 or 128: one warp per (sequence, head) on
-// the tensor cores (block_attn_head, attention.cuh); the persistent pass runs
-// the same function.
+// the tensor cores (block_attn_head, attention.cuh).
 constexpr int SA_MMA_WARPS = 4;
 
 template <int HD>

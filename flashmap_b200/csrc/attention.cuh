@@ -49,7 +49,7 @@ struct CrossAttnArgs {
 // writes with 128-byte swizzling).  Scores fp32, scaled; softmax numerators
 // exp(s - m) in fp32 summed per lane then over the quad, rounded to bf16 for
 // P V; out(i, d) = (P V)(i, d) / l(i).  store(i, d, lo, hi) receives columns
-// d, d + 1 of row i.  Both the kernel sequence and the persistent pass use it.
+// d, d + 1 of row i.  The block self-attention and the serving operator share it.
 __device__ __forceinline__ uint32_t blk_sw(int row, int chunk) {
   return (uint32_t)((chunk >> 3) * 2048 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4));
 }

@@ -227,9 +227,11 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 // ----------------------------------------------------------------- math
 // Argmax key: orderable float bits (high word) and the complement of the
 // index (low word), so 64-bit max picks the largest value and, among equal
-// values, the smallest index (torch.argmax semantics).
+// values, the smallest index (torch.argmax semantics).  -0.0 is keyed as
+// +0.0: the two compare equal, so only the index may decide between them.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
   uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0u;
   uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }

@@ -199,6 +199,9 @@ extern "C" int32_t fm_gemm_grid(int64_t M, int64_t N, int64_t K) {
   return (int32_t)gemm_grid_for(tiles * ((K + 63) / 64), tiles, bn);
 }
 
+#ifdef FM_DEBUG_TRACE
+// Debug builds only (not exported by the product library): the same call
+// recording per-CTA global-timer stamps (ns) into trace [grid][16].
 extern "C" fm_status fm_gemm_bf16_trace(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
                                         int64_t ldo, const void* bias, const void* gate, int epilogue,
                                         void* workspace, size_t workspace_bytes, int32_t* err, uint64_t* trace,
@@ -207,3 +210,4 @@ extern "C" fm_status fm_gemm_bf16_trace(const void* W, const void* X, void* out,
   return gemm_bf16_call(W, X, out, M, N, K, ldo, bias, gate, epilogue, workspace, workspace_bytes, err, trace,
                         stream);
 }
+#endif  // FM_DEBUG_TRACE

@@ -1747,9 +1747,10 @@ extern "C" fm_status fm_add(const void* a, const void* b, void* y, int64_t n, fm
 // inside this library instead of a caller workspace.
 //
 // The array is shared by every call on a device and keeps the last call's
-// contents; each call overwrites the rows it reads, so nothing needs to start
-// at zero.  Calls that overlap on the GPU (different streams, no ordering)
-// race on it.  Its device address is looked up once per device, by the first
+// contents.  The argmax keys are merged with atomicMax and must start at
+// zero: greedy_sliced clears the rows a call uses (cudaMemsetAsync on the
+// call's stream) before its kernels run.  Calls that overlap on the GPU
+// (different streams, no ordering) race on it.  Its device address is looked up once per device, by the first
 // call made with that device current; make that first call before any stream
 // capture begins.
 static __device__ __align__(256) int64_t g_accept_noalloc_scratch[FM_ACCEPT_NOALLOC_MAX_ROWS];
@@ -1787,11 +1788,12 @@ extern "C" fm_status fm_accept_greedy_noalloc(const void* target_logits, int32_t
                                               fm_stream stream) {
   if (!target_logits || !draft || !accepted || !bonus) return set_error(FM_ERR_INVALID, "accept_noalloc: null pointer");
   if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "accept_noalloc: bad arguments");
-  if (B * (K + 1) > FM_ACCEPT_NOALLOC_MAX_ROWS)
+  // B*(K+1) <= the maximum, checked without forming a product that could wrap
+  if (K >= FM_ACCEPT_NOALLOC_MAX_ROWS || B > FM_ACCEPT_NOALLOC_MAX_ROWS / (K + 1))
     return set_error(FM_ERR_WORKSPACE,
-                     "accept_noalloc: %lld target rows (B*(K+1)) exceed the built-in scratch of %d rows; "
-                     "use fm_accept_greedy with a workspace",
-                     (long long)(B * (K + 1)), FM_ACCEPT_NOALLOC_MAX_ROWS);
+                     "accept_noalloc: B=%lld, K=%lld needs more target rows (B*(K+1)) than the built-in scratch "
+                     "of %d rows; use fm_accept_greedy with a workspace",
+                     (long long)B, (long long)K, FM_ACCEPT_NOALLOC_MAX_ROWS);
   fm_status st;
   int64_t* am = accept_noalloc_scratch(&st);
   if (!am) return st;

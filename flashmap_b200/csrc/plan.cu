@@ -17,9 +17,6 @@
 //   final adaln -> head GEMM -> LM-head GEMM (logits + argmax fused)  (:312-313, :475)
 //   multi-step: state update between jumps                     (:476-478)
 // Every kernel is launched with programmatic dependent launch on one stream.
-//
-// A batch-1, one-jump draft instead runs as one persistent launch (pass.cu)
-// over the same buffers and weights: the stage list built by build_pass.
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -30,7 +27,6 @@
 #include "attention.cuh"
 #include "gemm_plan.cuh"
 #include "ops.cuh"
-#include "pass.cuh"
 
 namespace fm {
 fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl);
@@ -70,18 +66,6 @@ struct fm_plan {
   CUtensorMap cache_map;
   bool has_target;
   long long last_launches;
-  // persistent pass (batch 1, one jump)
-  bool pass_on;
-  char pass_why[160];
-  int pass_grid, pass_n_stages, pass_max_tiles;
-  int pass_prefetch;  // L2 prefetch distance in weight tiles (FM_PASS_PREFETCH, tuning)
-  pass::Stage* pass_stages;  // device
-  CUtensorMap* pass_tmaps;   // device
-  CUtensorMap* pass_cache_map;
-  unsigned long long* pass_words;  // [0] barrier arrivals, [1] CTAs out
-  int* pass_abort;
-  int* pass_counters;
-  float* pass_ws;
 };
 
 namespace {
@@ -147,7 +131,7 @@ size_t max_gemm_tiles(const fm_model_desc* m, const fm_plan_config* c) {
 }
 
 // splits of every (sequence, head)'s keys: at most one CTA per SM in total,
-// so the cross-attention is one wave (of the kernel, or of the persistent pass)
+// so the cross-attention is one wave
 int pick_nsplit(int B, int H, int cache_len) {
   const int sms = num_sms();
   int ns = sms / (B * H);
@@ -155,20 +139,6 @@ int pick_nsplit(int B, int H, int cache_len) {
   if (ns > maxs) ns = maxs;
   if (ns < 1) ns = 1;
   return ns;
-}
-
-// A plan whose drafts may run as the persistent pass (batch 1, one jump).
-bool pass_shape(const fm_plan_config* c) {
-  return c->batch == 1 && c->num_steps == 1 && c->launch_mode == FM_LAUNCH_PERSISTENT;
-}
-int pass_stage_cap(const fm_model_desc* m) { return 8 + 7 * (int)m->layers; }
-// 128-row tiles of the tallest weight the pass streams
-int pass_tiles(const fm_model_desc* m) {
-  const int64_t D = m->hidden, L = m->layers, mlp1 = m->swiglu ? 2 * (int64_t)m->inter : m->inter;
-  int64_t rows = m->state_vocab;
-  for (int64_t r : {2 * L * D, (int64_t)m->target_hidden, 3 * D, mlp1, D})
-    if (r > rows) rows = r;
-  return (int)((rows + 127) / 128);
 }
 
 // Lay out every buffer; with base == nullptr only the size is computed.
@@ -182,12 +152,6 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
   int* err = cv.take<int>(64);
   int* gc = cv.take<int>(max_gemm_tiles(m, c) + 64);
   int* xc = cv.take<int>((size_t)B * H + 64);
-  const bool pw = pass_shape(c);
-  const int pcap = pw ? pass_stage_cap(m) : 0;
-  const int ptiles = pw ? pass_tiles(m) : 0;
-  unsigned long long* pwords = cv.take<unsigned long long>(pw ? 4 : 0);
-  int* pabort = cv.take<int>(pw ? 4 : 0);
-  int* pcnt = cv.take<int>(pw ? 2 * (size_t)ptiles + 64 : 0);
   float* gws = cv.take<float>(max_gemm_partials(m, c) / sizeof(float) + 64);
   float* xp = cv.take<float>((size_t)B * H * ns * (16 * hd + 32));
   __nv_bfloat16* anchor_rows = cv.take<__nv_bfloat16>(B * Ht);
@@ -221,18 +185,7 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
   __nv_bfloat16* ext_ctx = cv.take<__nv_bfloat16>(R * D);
   int* ext_seq = cv.take<int>(R);
   int* ext_pos = cv.take<int>(R);
-  // split-K partials of the pass: [2 parities][grid][2 slots][16][128]
-  float* pws = cv.take<float>(pw ? 2 * (size_t)num_sms() * 2 * 16 * 128 : 0);
-  pass::Stage* pst = cv.take<pass::Stage>(pcap);
-  CUtensorMap* ptm = cv.take<CUtensorMap>(pw ? pcap + 1 : 0);
   if (p) {
-    p->pass_max_tiles = ptiles;
-    p->pass_words = pwords;
-    p->pass_abort = pabort;
-    p->pass_counters = pcnt;
-    p->pass_ws = pws;
-    p->pass_stages = pst;
-    p->pass_tmaps = ptm;
     p->err = err;
     p->gemm_counters = gc;
     p->xattn_counters = xc;
@@ -286,318 +239,13 @@ fm_status validate(const fm_model_desc* m, const fm_plan_config* c) {
     return set_error(FM_ERR_INVALID, "plan: multi-step drafts need embed_state_t");
   if (c->cache_batch < c->batch) return set_error(FM_ERR_SHAPE, "plan: cache batch smaller than plan batch");
   if (c->launch_mode == FM_LAUNCH_PERSISTENT)
-    return set_error(FM_ERR_UNSUPPORTED,
-                     "plan: the persistent single-launch pass is withdrawn (an intermittent illegal-instruction "
-                     "fault is under investigation); use FM_LAUNCH_KERNELS");
+    return set_error(FM_ERR_UNSUPPORTED, "plan: launch_mode FM_LAUNCH_PERSISTENT is reserved; use FM_LAUNCH_KERNELS");
   if (c->launch_mode != FM_LAUNCH_AUTO && c->launch_mode != FM_LAUNCH_KERNELS)
     return set_error(FM_ERR_INVALID, "plan: unknown launch_mode %d", c->launch_mode);
   if (!m->layer || !m->rope_cos || !m->rope_sin) return set_error(FM_ERR_INVALID, "plan: missing weights");
   return FM_OK;
 }
 
-
-// ------------------------------------------------------------------ persistent pass
-//
-// Stage list of one batch-1, one-jump draft (modeling_flashmap.py:422-479):
-//   z L^T (noise built in place) | anchor_proj (anchor embedding gathered in
-//   place) | x_embed (mix_state built in place) | per layer: qkv, [layer 0:
-//   the anchor's cross k|v into the cache], o (self-attention built in place),
-//   cross q, cross-attention, cross o, fc1, fc2 | head | LM head | tokens.
-// Every stage waits for the one before it except the two leading GEMMs (their
-// inputs are the draft's own arguments) and the anchor k|v (its input, the
-// projected anchor row, is complete once layer 0's qkv stage could start).
-
-void pass_off(fm_plan* p, const char* why) {
-  p->pass_on = false;
-  std::snprintf(p->pass_why, sizeof(p->pass_why), "%s", why);
-}
-
-void build_pass(fm_plan* p) {
-  const fm_model_desc& m = p->m;
-  if (p->cfg.launch_mode != FM_LAUNCH_PERSISTENT) return pass_off(p, "launch_mode is not FM_LAUNCH_PERSISTENT");
-  if (p->B != 1 || p->cfg.num_steps != 1) return pass_off(p, "the persistent pass serves batch-1, one-jump drafts");
-  if (!p->has_target) return pass_off(p, "the plan has no target embedding / LM head");
-  const int G = pass_grid();
-  if (G <= 0) return pass_off(p, "the persistent kernel cannot be resident on this device");
-  if (G > num_sms()) return pass_off(p, "grid larger than the carved split-K workspace");
-  using bf = __nv_bfloat16;
-  const int T = p->T, D = p->D, Ht = p->Ht, L = p->L;
-  const fm_jump& j = p->jumps[0];
-  const bf* mods = static_cast<const bf*>(j.mods);
-  if (!mods) return pass_off(p, "jump without modulations");
-  std::vector<pass::Stage> st;
-  std::vector<CUtensorMap> tm;
-  // TMA sources of the B operands: activation rows [T, width], boxes of 16 x 64
-  auto src_map = [&](const bf* base, int width) -> int {
-    CUtensorMap m{};
-    if (make_tmap_bf16(&m, base, (uint64_t)T, (uint64_t)width, (uint64_t)width, 16)) return -2;
-    tm.push_back(m);
-    return (int)tm.size() - 1;
-  };
-  // the same sources as [width / 64] blocks of 16 x 64: `blocks` blocks per box
-  auto block_map = [&](const bf* base, int width, int blocks) -> int {
-    if (width % 64 != 0 || blocks < 1 || blocks > 256 || blocks > width / 64) return -1;
-    CUtensorMap m{};
-    if (make_tmap_bf16_blocks(&m, base, (uint64_t)T, (uint64_t)width, (uint64_t)width, 16, (uint32_t)blocks))
-      return -1;
-    tm.push_back(m);
-    return (int)tm.size() - 1;
-  };
-  const int map_x = src_map(p->x, D), map_zl = src_map(p->zl, Ht);
-  if (map_x < 0 || map_zl < 0) return pass_off(p, "could not encode the activation tensor maps");
-  const int rows_x = block_map(p->x, D, D / 64);                // AdaLN inputs as whole rows
-  const int head_qkv = block_map(p->qkv, 3 * D, p->hd / 64);    // one head part of q|k|v
-  const int rows_attn = D / 64 <= pass_b_slots() ? block_map(p->attn, D, D / 64) : -1;
-  const int rows_hidden = Ht / 64 <= pass_b_slots() ? block_map(p->hidden, Ht, Ht / 64) : -1;
-  if (head_qkv < 0) return pass_off(p, "could not encode the self-attention tensor map");
-  auto gemm = [&](const GemmPlan& g, int bsrc, int ntok) -> pass::Stage& {
-    pass::Stage S{};
-    S.type = pass::ST_GEMM;
-    S.wait = (int)st.size() - 1;
-    S.smap = -1;
-    S.fmap = -1;
-    S.full = 0;
-    S.tmap = (int)tm.size();
-    tm.push_back(g.tmA);
-    if (bsrc == pass::BS_COPY) {  // the GEMM's own X operand map (box 16 x 64)
-      S.smap = (int)tm.size();
-      tm.push_back(g.tmB);
-    }
-    S.ntok = ntok;
-    S.bsrc = bsrc;
-    S.epi = g.epi;
-    S.ep = g.args;
-    S.xa_layer = -1;
-    st.push_back(S);
-    return st.back();
-  };
-  {
-    pass::Stage& S = gemm(p->g_zl, pass::BS_NOISE, T);
-    S.wait = -1;
-  }
-  {
-    pass::Stage& S = gemm(p->g_anchor_proj, pass::BS_GATHER, 1);
-    S.wait = -1;
-    S.aux = static_cast<const bf*>(m.embed);
-  }
-  {
-    pass::Stage& S = gemm(p->g_xembed, pass::BS_MIX, T);
-    S.smap = map_zl;
-    S.src = p->zl;
-    S.ld = Ht;
-    S.aux = static_cast<const bf*>(m.uniform_embeds);
-    S.w0 = static_cast<const bf*>(m.state_norm_w);
-    S.w1 = static_cast<const bf*>(m.noise_norm_w);
-    S.gate = j.noise_gate;
-    S.eps = m.rms_eps;
-  }
-  const float scale = (float)(1.0 / std::sqrt((double)p->hd));
-  for (int l = 0; l < L; ++l) {
-    const GemmPlan* g = &p->g_layer[(size_t)l * 6];
-    const bf* ms = mods + (size_t)(l * 3 + 0) * 3 * D;
-    const bf* mc = mods + (size_t)(l * 3 + 1) * 3 * D;
-    const bf* mm = mods + (size_t)(l * 3 + 2) * 3 * D;
-    {
-      pass::Stage& S = gemm(g[0], pass::BS_ADALN, T);
-      S.smap = map_x;
-      S.fmap = rows_x;
-      S.src = p->x;
-      S.ld = D;
-      S.mod = ms;
-      S.eps = m.ln_eps;
-    }
-    if (l == 0) {
-      pass::Stage& S = gemm(p->g_anchor_kv, pass::BS_RMSROW, 1);
-      S.wait = -1;
-      S.src = p->anchor_h;
-      S.w0 = static_cast<const bf*>(m.anchor_norm_w);
-      S.eps = m.rms_eps;
-    }
-    {
-      pass::Stage& S = gemm(g[1], pass::BS_SELFATTN, T);
-      S.fmap = head_qkv;
-      S.src = p->qkv;
-      S.ld = 3 * D;
-      S.heads = p->H;
-      S.head_dim = p->hd;
-      S.scale = scale;
-      S.ep.gate = ms + 2 * D;
-    }
-    {
-      pass::Stage& S = gemm(g[2], pass::BS_ADALN, T);
-      S.smap = map_x;
-      S.fmap = rows_x;
-      S.src = p->x;
-      S.ld = D;
-      S.mod = mc;
-      S.eps = m.ln_eps;
-    }
-    {
-      pass::Stage S{};
-      S.type = pass::ST_XATTN;
-      S.wait = (int)st.size() - 1;
-      S.xa_layer = l;
-      st.push_back(S);
-    }
-    {
-      pass::Stage& S = gemm(g[3], pass::BS_COPY, T);
-      S.fmap = rows_attn;
-      S.src = p->attn;
-      S.ld = D;
-      S.ep.gate = mc + 2 * D;
-    }
-    {
-      pass::Stage& S = gemm(g[4], pass::BS_ADALN, T);
-      S.smap = map_x;
-      S.fmap = rows_x;
-      S.src = p->x;
-      S.ld = D;
-      S.mod = mm;
-      S.eps = m.ln_eps;
-    }
-    {
-      pass::Stage& S = gemm(g[5], pass::BS_COPY, T);
-      S.src = p->mlp;
-      S.ld = p->I;
-      S.ep.gate = mm + 2 * D;
-    }
-  }
-  {
-    pass::Stage& S = gemm(p->g_head, pass::BS_ADALN, T);
-    S.smap = map_x;
-    S.fmap = rows_x;
-    S.src = p->x;
-    S.ld = D;
-    S.mod = mods + (size_t)(L * 3) * 3 * D;
-    S.eps = m.ln_eps;
-  }
-  {
-    pass::Stage& S = gemm(p->g_lm, pass::BS_COPY, T);
-    S.fmap = rows_hidden;
-    S.src = p->hidden;
-    S.ld = Ht;
-    S.is_lm = 1;
-    S.ep.col_ids = reinterpret_cast<const long long*>(m.draft_ids);
-  }
-  {
-    pass::Stage S{};
-    S.type = pass::ST_FINAL;
-    S.wait = (int)st.size() - 1;
-    S.xa_layer = -1;
-    st.push_back(S);
-  }
-  // the checks the kernel relies on
-  const int n = (int)st.size();
-  if (n > pass_stage_cap(&m) || n > pass_max_stages()) return pass_off(p, "stage list longer than its carve-out");
-  for (int i = 0; i < n; ++i) {
-    const pass::Stage& S = st[i];
-    if (S.wait != -1 && S.wait != i - 1) return pass_off(p, "a stage waits on other than its predecessor");
-    if (i >= 2 && S.wait < 0 && st[i - 1].wait < 0) return pass_off(p, "two stages in a row without a barrier");
-    if (S.type != pass::ST_GEMM) continue;
-    const long long U = S.ep.units;
-    const long long Gs = U < G ? U : G;
-    const long long per = (U + Gs - 1) / Gs;
-    const long long nk = per < S.ep.kb ? per : S.ep.kb;
-    if (S.ep.n_tiles != 1 || S.ep.N > 16 || S.ntok != S.ep.N) return pass_off(p, "a stage with more than 16 tokens");
-    if (nk > pass_b_slots()) return pass_off(p, "a stage's k-range exceeds the B-operand slots");
-    if (S.ep.m_tiles > p->pass_max_tiles) return pass_off(p, "a stage's tiles exceed the counter carve-out");
-    if (S.bsrc == pass::BS_ADALN && S.fmap >= 0 &&
-        pass_stage_b_bytes(S.bsrc, (int)nk, S.ep.K, S.head_dim, true) <= pass_b_region())
-      st[i].full = 1;  // whole rows fit: statistics from shared memory
-    if (pass_stage_b_bytes(S.bsrc, (int)nk, S.ep.K, S.head_dim, S.full != 0) > pass_b_region())
-      return pass_off(p, "a stage's operand inputs do not fit in shared memory");
-    if ((S.bsrc == pass::BS_COPY || S.bsrc == pass::BS_ADALN || S.bsrc == pass::BS_MIX) && S.smap < 0)
-      return pass_off(p, "a stage without its source tensor map");
-    if (S.ep.K % 8 != 0) return pass_off(p, "a stage's width is not a multiple of 8");
-    // sources of bulk copies start on 16-byte boundaries
-    auto misaligned = [](const void* q) { return q != nullptr && (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
-    if (misaligned(S.src) || misaligned(S.mod) || misaligned(S.w0) || misaligned(S.w1) || misaligned(S.aux))
-      return pass_off(p, "a stage's inputs are not 16-byte aligned");
-  }
-  tm.push_back(p->cache_map);
-  if (cudaMemcpy(p->pass_stages, st.data(), st.size() * sizeof(pass::Stage), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(p->pass_tmaps, tm.data(), tm.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) != cudaSuccess) {
-    cudaGetLastError();
-    return pass_off(p, "could not copy the stage list to the device");
-  }
-  p->pass_cache_map = p->pass_tmaps + (tm.size() - 1);
-  {
-    const char* e = getenv("FM_PASS_PREFETCH");
-    const int v = e ? atoi(e) : 0;
-    p->pass_prefetch = v >= 0 && v <= 256 ? v : 0;
-  }
-  p->pass_n_stages = n;
-  p->pass_grid = G;
-  p->pass_on = true;
-  p->pass_why[0] = 0;
-}
-
-fm_status run_pass(fm_plan* p, const fm_draft_io* io, cudaStream_t s) {
-  const fm_model_desc& m = p->m;
-  pass::PassArgs P{};
-  P.stages = p->pass_stages;
-  P.n_stages = p->pass_n_stages;
-  P.tmaps = p->pass_tmaps;
-  P.cache_map = p->pass_cache_map;
-  P.bar_count = p->pass_words;
-  P.bar_exit = p->pass_words + 1;
-  P.abort = p->pass_abort;
-  P.err = p->err;
-  P.ws = p->pass_ws;
-  P.counters = p->pass_counters;
-  P.max_tiles = p->pass_max_tiles;
-  P.anchor_ids = io->anchor_ids;
-  P.lengths = io->lengths;
-  P.z = static_cast<const __nv_bfloat16*>(io->z);
-  P.seed = io->seed;
-  P.offset = io->offset;
-  P.offset_ptr = io->offset_ptr;
-  P.anchor_pos = p->anchor_pos;
-  P.anchor_seq = p->anchor_seq;
-  P.slot_pos = p->slot_pos;
-  P.keys = p->keys;
-  P.tokens = io->tokens;
-  P.trace = reinterpret_cast<unsigned long long*>(io->trace);
-  P.pf_tiles = p->pass_prefetch;
-  if (io->logits) {
-    P.logits = static_cast<__nv_bfloat16*>(io->logits);
-    P.ldl = io->ldl;
-    P.scatter = (io->scatter && m.draft_ids) ? 1 : 0;
-  } else {
-    P.logits = p->logits_s;
-    P.ldl = p->S;
-    P.scatter = 0;
-  }
-  P.rope_len = m.rope_len;
-  P.rope_cos = m.rope_cos;
-  P.rope_sin = m.rope_sin;
-  P.rope_half = p->hd / 2;
-  P.cache_len = p->cfg.cache_len;
-  P.block = p->K;
-  P.vocab = m.vocab;
-  CrossAttnArgs& ca = P.xa;
-  ca.q = p->qc;
-  ca.out = p->attn;
-  ca.lengths = p->anchor_pos;
-  ca.batch = 1;
-  ca.heads = p->H;
-  ca.head_dim = p->hd;
-  ca.hidden = p->D;
-  ca.layer = 0;
-  ca.cache_batch = p->cfg.cache_batch;
-  ca.cache_len = p->cfg.cache_len;
-  ca.nsplit = p->nsplit;
-  ca.scale = (float)(1.0 / std::sqrt((double)p->hd));
-  ca.part = p->xattn_part;
-  ca.counters = p->xattn_counters;
-  ca.err = p->err;
-  fm_status st = pass_launch(P, p->pass_grid, s);
-  if (st) return st;
-  if (io->hidden)
-    return check_cuda(cudaMemcpyAsync(io->hidden, p->hidden, (size_t)p->T * p->Ht * 2, cudaMemcpyDeviceToDevice, s),
-                      "draft: copy hidden");
-  return FM_OK;
-}
 
 }  // namespace
 
@@ -760,11 +408,6 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
   // the cache as one [rows, head_dim] matrix for the cross-attention TMA
   const uint64_t rows = (uint64_t)L * 2 * c->cache_batch * p->H * c->cache_len;
   if ((st = make_tmap_bf16(&p->cache_map, c->cache, rows, (uint64_t)p->hd, (uint64_t)p->hd, 64))) return fail(st);
-  if (pass_shape(c))
-    build_pass(p);
-  else
-    pass_off(p, c->launch_mode != FM_LAUNCH_PERSISTENT ? "launch_mode is not FM_LAUNCH_PERSISTENT"
-                                                       : "the persistent pass serves batch-1, one-jump drafts");
   *out = p;
   return FM_OK;
 }
@@ -777,22 +420,6 @@ extern "C" fm_status fm_plan_destroy(fm_plan* p) {
 extern "C" int32_t* fm_plan_error_word(fm_plan* p) { return p ? p->err : nullptr; }
 
 extern "C" int64_t fm_plan_last_launches(const fm_plan* p) { return p ? p->last_launches : -1; }
-
-extern "C" fm_status fm_plan_pass_shape(const fm_plan* p, int32_t* grid, int32_t* stages) {
-  if (!p || !grid || !stages) return set_error(FM_ERR_INVALID, "pass_shape: null argument");
-  *grid = p->pass_on ? p->pass_grid : 0;
-  *stages = p->pass_on ? p->pass_n_stages : 0;
-  return FM_OK;
-}
-
-extern "C" int32_t fm_plan_persistent(const fm_plan* p, char* why, size_t why_len) {
-  if (!p) {
-    if (why && why_len) std::snprintf(why, why_len, "null plan");
-    return 0;
-  }
-  if (!p->pass_on && why && why_len) std::snprintf(why, why_len, "%s", p->pass_why);
-  return p->pass_on ? 1 : 0;
-}
 
 extern "C" fm_status fm_plan_lm_head(fm_plan* p, void* logits, int64_t ldl, fm_stream stream) {
   if (!p || !p->has_target) return set_error(FM_ERR_INVALID, "lm_head: plan without target");
@@ -901,7 +528,6 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
     ~Count() { p->last_launches = launch_counter() - l0; }
   } count{p, launches0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (p->pass_on) return run_pass(p, io, s);
   const fm_model_desc& m = p->m;
   const int T = p->T, Ht = p->Ht, S = p->S;
   fm_status st;

@@ -1,6 +1,6 @@
 // Row statistics of the normalisations (LayerNorm of AdaLN, RMSNorm,
-// mix_state) in one canonical order, shared by the row kernels and the
-// persistent draft pass so that both produce identical bits.
+// mix_state) in one canonical order, shared by every kernel that normalises
+// rows so that all of them produce identical bits.
 //
 // One warp per row.  Lane l takes the 8-element chunks l, l+32, l+64, ... of
 // the row; inside a chunk the elements are combined as a pairwise tree

@@ -429,9 +429,8 @@ class _Plan:
             pass
 
     def draft(self, anchor_ids, seed: int, offset: int, logits=None, ldl=0, scatter=False, tokens=None, z=None,
-              noise=None, hidden=None, offset_dev=None, trace=None):
+              noise=None, hidden=None, offset_dev=None):
         io = _lib.DraftIO()
-        io.trace = None if trace is None else trace.data_ptr()
         io.offset_ptr = None if offset_dev is None else offset_dev.data_ptr()
         io.anchor_ids, io.lengths = anchor_ids.data_ptr(), self.cache.lengths.data_ptr()
         io.z = None if z is None else z.data_ptr()
@@ -462,19 +461,6 @@ class _Plan:
 
     def last_launches(self) -> int:
         return int(_lib.load().fm_plan_last_launches(self.handle))
-
-    def persistent(self) -> tuple:
-        """(True, "") when a draft runs as one persistent launch, else (False, why)."""
-        why = ctypes.create_string_buffer(256)
-        on = _lib.load().fm_plan_persistent(self.handle, why, len(why))
-        return bool(on), why.value.decode()
-
-    def pass_shape(self) -> tuple:
-        """(grid, stages) of the persistent pass: the trace buffer of ``draft``
-        holds grid x stages x 14 timestamps."""
-        g, n = ctypes.c_int32(0), ctypes.c_int32(0)
-        _lib.load().fm_plan_pass_shape(self.handle, ctypes.byref(g), ctypes.byref(n))
-        return g.value, n.value
 
     def check_device_errors(self):
         code = int(self.err.item())
@@ -514,8 +500,7 @@ class FlashMapDraftModel(PreTrainedModel):
         self.post_init()
 
     # values derived from the weights are rebuilt after a move or a reload (:271-285)
-    # "auto" and "kernels": the kernel sequence.  "persistent" (one launch per
-    # batch-1, one-jump draft) is withdrawn: plan creation raises.
+    # launch_mode "auto" and "kernels": the kernel sequence.
     # fold_head: the serving plugins' fast mode (vllm/fold.py:76-100): the DiT
     # head folded into the LM-head rows, one [S, D] projection of the final
     # AdaLN output instead of the head and the [S, Ht] LM head (0.64 GB less
@@ -558,8 +543,7 @@ class FlashMapDraftModel(PreTrainedModel):
         max_pos = cache.max_length + self.config.block_size + 2
         if pack.ensure_rope(self.config, max_pos):
             self._plans = {}
-        mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS,
-                "persistent": _lib.LAUNCH_PERSISTENT}[self.launch_mode]
+        mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS}[self.launch_mode]
         key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, bool(self.fold_head),
                bool(self.fold_noise), pack.device)
         plan = self._plans.get(key)

@@ -77,23 +77,20 @@ enum {
  * 129-132, 159-163, 250-264) and F.linear of the LM head (:475).
  *   W   [M, K] bf16 (nn.Linear layout), X [N, K] bf16 (tokens), K % 8 == 0
  *   out [N, ldo] bf16 (fp32 for FM_EPI_F32); bias/gate [M] bf16 or NULL
- *   workspace: fm_gemm_workspace_size() bytes; counters must be zero on the
- *   first call and are left zero after every call. */
+ *   workspace: fm_gemm_workspace_size() bytes, laid out as 256 reserved
+ *   bytes, then one int32 counter per output tile of 128 rows (zero before the
+ *   first call, left zero by every call that completes), then the split-K
+ *   partials.  A split tile's head CTA waits for its contributors' count
+ *   for at most 2 s; if the count never arrives it records a timeout in
+ *   *err (when non-NULL), leaves the tile unwritten and returns. */
 FM_API size_t fm_gemm_workspace_size(int64_t M, int64_t N, int64_t K);
 FM_API fm_status fm_gemm_bf16(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K, int64_t ldo,
                        const void* bias, const void* gate, int epilogue, void* workspace, size_t workspace_bytes,
                        int32_t* err, fm_stream stream);
 
-/* Diagnostics: the CTAs fm_gemm_bf16 launches for a shape, and the same call
- * recording per-CTA global-timer stamps (ns) into trace [grid][16]: 0 entry,
- * 1 setup done; per segment s < 3 (one tile's k-range): 2+4s MMAs issued,
- * 3+4s accumulator seen by the epilogue, 4+4s split partial written or
- * epilogue done, 5+4s split fix-up done; 14 exit.  Unwritten slots keep
- * their contents. */
+/* The CTAs fm_gemm_bf16 launches for a shape (one per SM at most): a
+ * caller sizing its own split-K workspace per launch reads it here. */
 FM_API int32_t fm_gemm_grid(int64_t M, int64_t N, int64_t K);
-FM_API fm_status fm_gemm_bf16_trace(const void* W, const void* X, void* out, int64_t M, int64_t N, int64_t K,
-                                    int64_t ldo, const void* bias, const void* gate, int epilogue, void* workspace,
-                                    size_t workspace_bytes, int32_t* err, uint64_t* trace, fm_stream stream);
 
 /* RMSNorm of modeling_flashmap.py:69-80: y = x * bf16(w * rsqrt(mean(x^2) + eps)). */
 FM_API fm_status fm_rmsnorm(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
@@ -549,9 +546,7 @@ enum {
   FM_LAUNCH_AUTO = 0,       /* the kernel sequence */
   FM_LAUNCH_KERNELS = 1,    /* the kernel sequence: one launch per operation, chained by programmatic
                                dependent launch */
-  FM_LAUNCH_PERSISTENT = 2  /* withdrawn: fm_plan_create returns FM_ERR_UNSUPPORTED (the single-launch
-                               pass raised an intermittent illegal-instruction fault that is not
-                               understood yet, so it is not run) */
+  FM_LAUNCH_PERSISTENT = 2  /* reserved: fm_plan_create returns FM_ERR_UNSUPPORTED */
 };
 
 typedef struct fm_plan_config {
@@ -577,14 +572,6 @@ FM_API fm_status fm_plan_destroy(fm_plan* plan);
 FM_API int32_t* fm_plan_error_word(fm_plan* plan);
 /* Kernels launched by the plan's last fm_draft call. */
 FM_API int64_t fm_plan_last_launches(const fm_plan* plan);
-/* 1 when fm_draft runs as one persistent launch (FM_LAUNCH_PERSISTENT, batch 1,
- * one jump, target attached, the launch fits the device); else 0, with the reason
- * written to `why` (when non-NULL, up to why_len bytes including the NUL).
- * No counterpart in the reference (its draft is a sequence of torch ops). */
-FM_API int32_t fm_plan_persistent(const fm_plan* plan, char* why, size_t why_len);
-/* CTAs and stages of the persistent pass (both 0 when it is off): the size of
- * fm_draft_io.trace.  No counterpart in the reference. */
-FM_API fm_status fm_plan_pass_shape(const fm_plan* plan, int32_t* grid, int32_t* stages);
 /* The plan's LM-head GEMM alone (logits + argmax of the plan's current DiT
  * output; state-vocabulary columns), for timing the pass's largest kernel. */
 FM_API fm_status fm_plan_lm_head(fm_plan* plan, void* logits, int64_t ldl, fm_stream stream);
@@ -603,12 +590,6 @@ typedef struct fm_draft_io {
   int32_t scatter;           /* 1: write at draft_ids columns of a V-wide row */
   int64_t* tokens;           /* [B*K] argmax tokens (target ids) or NULL */
   void* hidden;              /* [B*K, Ht] bf16 DiT output of the last jump, or NULL */
-  uint64_t* trace;           /* persistent pass only, or NULL: [grid][stages][14] device timestamps (ns) of
-                                each stage in each CTA: start, inputs ready, operand loads issued, loads
-                                landed, operand built, first epilogue done, last epilogue done, arrived,
-                                row statistics done, operand transform done, and for the owner of a split
-                                tile: contributors arrived, partials loaded, partials summed, epilogue done
-                                (slots a stage does not pass through keep their old value) */
 } fm_draft_io;
 
 /* One draft of the whole block (modeling_flashmap.py:422-479): the anchor row
