@@ -245,6 +245,20 @@ def cpu_reference(seconds: float = 15.0, seed: int = 0) -> dict:
             "ms_per_pass": 1000.0 * el / n}
 
 
+def workload_config(args, world: int) -> dict:
+    """The ``config`` of both arms' JSON lines (the same workload, the same dict)."""
+    nbytes = algorithmic_bytes(PROFILE_SMALL if args.profile_small else CONFIG2, CONTEXT)
+    cfg = {"workload": "config2: Qwen3-8B-sized drafter pass, batch 1 per GPU, K=16, ctx 2048, 1 jump",
+           "batch_per_gpu": 1, "block": 16, "context": CONTEXT, "num_steps": 1,
+           "parallelism": f"replicas x{world} (request-sharded, no collective)",
+           "l2": "inputs larger than L2: %.2f GB of weights + context streamed per pass" % (nbytes["total"] / 1e9),
+           "timing": "per pass: CUDA events (ours), host clock (reference); max over ranks",
+           "launch": args.launch}
+    if args.profile_small:
+        cfg["workload"] = "profiling case: config-2 layer shapes, 2 layers, 32768-row LM head"
+    return cfg
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
@@ -253,8 +267,7 @@ def run_reference(args, world, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ref["ms_per_pass"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init config-2 drafter, N(0,1) conditioning)",
-            "config": {"workload": "config2: Qwen3-8B-sized drafter pass, batch 1, K=16, ctx 2048, 1 jump",
-                       "batch": 1, "block": 16, "context": CONTEXT, "num_steps": 1},
+            "config": workload_config(args, world),
             "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -629,12 +642,7 @@ def run_ours(args, world, rank, local):
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random-init config-2 drafter weights and target head, N(0,1) conditioning)",
-        "config": {"workload": "config2: Qwen3-8B-sized drafter pass, batch 1 per GPU, K=16, ctx 2048, 1 jump",
-                   "batch_per_gpu": 1, "block": 16, "context": CONTEXT, "num_steps": 1,
-                   "parallelism": f"replicas x{world} (request-sharded, no collective)",
-                   "l2": "inputs larger than L2: %.2f GB of weights + context streamed per pass" % (nbytes["total"] / 1e9),
-                   "timing": "CUDA-graph replays, CUDA events, max over ranks",
-                   "launch": args.launch},
+        "config": workload_config(args, world),
         "pass_us": ms_per_step * 1000.0,
         "pass_roofline": {"bound": "hbm", "algorithmic_bytes": nbytes["total"], "achieved": pass_gbs, "peak": peak,
                           "unit": "GB/s", "frac": pass_gbs / peak, "peak_kind": peak_kind,
@@ -652,8 +660,6 @@ def run_ours(args, world, rank, local):
     if folded is not None:
         line["fast_mode_folded_head"] = folded
         line["fast_mode_folded_head_and_noise"] = folded_all
-    if args.profile_small:
-        line["config"]["workload"] = "profiling case: config-2 layer shapes, 2 layers, 32768-row LM head"
     if world == 1 and not args.no_cpu_baseline and not args.profile_small:
         ref = cpu_reference(seconds=args.cpu_seconds)
         line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}

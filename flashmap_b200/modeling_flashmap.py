@@ -9,9 +9,12 @@ epilogues, TMA flash cross-attention, Philox sampling and acceptance), with
 no PyTorch or CPU fallback.  Weights are served in bf16 on a B200.
 
 Randomness: the one-step draft noise, draft sampling and rejection sampling
-use Philox4x32-10 streams keyed by a 64-bit seed (``generator.initial_seed()``
-or ``torch.initial_seed()``) and a per-call counter, instead of torch's
-generator; the distributions are the reference's.
+use Philox4x32-10 streams instead of torch's generator; the distributions are
+the reference's.  The draft noise is keyed by ``generator.initial_seed()`` (or
+``torch.initial_seed()``) and a per-call counter; ``spec_generate``'s
+sampling and acceptance draws by a key it draws from the generator once per
+call (``philox_key``), with one counter word per decoding round and one for
+the prefill's token.
 """
 
 from __future__ import annotations
@@ -468,6 +471,26 @@ class _Plan:
             raise _lib.FlashMapError(f"a FlashMap kernel reported device error {code} (index or wait)")
 
 
+# ---------------------------------------------------------------- sampled decoding's randomness
+
+# Philox round word of the first target token's draw in spec_generate (the
+# token sampled from the prefill logits): a counter of its own, which no
+# decoding round (words 0, 1, 2, ...) reaches, so that the anchor and the
+# first round's draft are independent draws.
+PREFILL_ROUND = 0xFFFFFFFF
+
+
+def philox_key(generator: Optional[torch.Generator] = None) -> int:
+    """The 63-bit Philox key of one ``spec_generate`` call, drawn from
+    ``generator`` (or torch's default CPU generator).  The draw advances the
+    generator, as the reference's ``torch.rand`` / ``torch.multinomial``
+    draws do (modeling_flashmap.py:557, :587, :594): two calls with one
+    generator use fresh randomness, and a generator seeded alike reproduces
+    a call."""
+    device = generator.device if generator is not None else "cpu"
+    return int(torch.randint(0, 2 ** 63 - 1, (1,), generator=generator, device=device, dtype=torch.int64).item())
+
+
 # ---------------------------------------------------------------- the model
 
 
@@ -741,7 +764,7 @@ class FlashMapDraftModel(PreTrainedModel):
         input_ids = input_ids.to(device)
         K, P = self.config.block_size, input_ids.shape[1]
         num_steps = self._steps(num_steps)
-        seed = generator.initial_seed() if generator is not None else torch.initial_seed()
+        seed = philox_key(generator)
 
         def native(logits):  # bf16 and fp32 logits are read as they are; other floats widen exactly
             return (logits if logits.dtype in (torch.bfloat16, torch.float32) else logits.float()).contiguous()
@@ -761,7 +784,7 @@ class FlashMapDraftModel(PreTrainedModel):
         try:
             target_cache = DynamicCache()
             out = target(input_ids, past_key_values=target_cache, use_cache=True, logits_to_keep=1)
-            tokens = sample(out.logits[:, -1:], 0)[0]
+            tokens = sample(out.logits[:, -1:], PREFILL_ROUND)[0]
             cache = FlashMapCache(self.config, 1, P + max_new_tokens + K + 1, device=device, dtype=torch.bfloat16)
             self.extend_context(cache, features(), embed_tokens, lm_head)
             lengths, rounds = [], 0

@@ -370,24 +370,36 @@ def softmax_probs(logits: torch.Tensor, temperature: float, mode: str) -> torch.
 
     ``mode="torch"`` is the reference's own op; ``mode="fixed"`` is the
     fixed-order ``fm_exp`` softmax of the C oracle, which the CUDA kernels
-    reproduce bit for bit."""
+    reproduce bit for bit.  bf16 and fp32 logits are read as they are (the
+    CUDA path reads both natively); other floats widen to fp32."""
     if mode == "torch":
         return (logits.float() / temperature).softmax(dim=-1)
     from . import accept
 
-    return accept.softmax_rows(logits.to(torch.bfloat16), temperature)
+    native = logits if logits.dtype in (torch.bfloat16, torch.float32) else logits.float()
+    return accept.softmax_rows(native, temperature)
+
+
+# Philox round word of the first target token's draw (sampled from the
+# prefill logits): a counter of its own that no decoding round reaches.
+PREFILL_ROUND = 0xFFFFFFFF
 
 
 @torch.no_grad()
 def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, temperature=0.0, num_steps=None,
-                  stop_token_ids=None, z_source=None, rng_seed=1234, softmax_mode="torch"):
+                  stop_token_ids=None, z_source=None, rng_seed=1234, softmax_mode="torch", draft_fn=None):
     """Speculative decoding loop of :514-612 with injected randomness.
 
     ``z_source(r)`` gives round r's one-step noise (B=1, K, H).  At T > 0 the
     draws are Philox uniforms: draft slot k of round r (k, 0, r, 3) — the
-    first target token uses (0, 0, 0, 3) — acceptance (k, 0, r, 1) and the
-    bonus (0, 0, r, 2), each turned into a token by the oracle's categorical
-    sampler (its sliced form for the bonus).  Returns ``(sequences, acceptance_lengths)``."""
+    first target token, sampled from the prefill, has a counter of its own,
+    (0, 0, PREFILL_ROUND, 3), which no round reaches — acceptance (k, 0, r, 1)
+    and the bonus (0, 0, r, 2), each turned into a token by the oracle's
+    categorical sampler (its sliced form for the bonus).  ``draft_fn(anchor,
+    r)``, when given, supplies round r's draft logits instead of the oracle's
+    drafter (replaying another implementation's drafts through this loop).
+    The target may sit on any device; the oracle's arithmetic runs on the CPU.
+    Returns ``(sequences, acceptance_lengths)``.""",
     from transformers import DynamicCache
 
     from . import accept
@@ -399,10 +411,11 @@ def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, tempera
         eos = target.generation_config.eos_token_id
         stop_token_ids = [] if eos is None else [eos] if isinstance(eos, int) else list(eos)
     stop = torch.tensor(stop_token_ids, dtype=torch.long)
-    embedding = target.get_input_embeddings().weight.detach()
+    embedding = target.get_input_embeddings().weight.detach().cpu()
     head = target.get_output_embeddings()
-    head_w = head.weight.detach()
-    head_b = None if getattr(head, "bias", None) is None else head.bias.detach()
+    head_w = head.weight.detach().cpu()
+    head_b = None if getattr(head, "bias", None) is None else head.bias.detach().cpu()
+    dev = input_ids.device
     K, P = cfg.block_size, input_ids.shape[1]
     rounds = 0
 
@@ -418,29 +431,34 @@ def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, tempera
     hooks = [layers[i].register_forward_hook(
         (lambda i: lambda m, a, o: feats.__setitem__(i, o[0] if isinstance(o, tuple) else o))(i))
         for i in cfg.target_layer_ids]
-    features = lambda: torch.cat([feats[i] for i in cfg.target_layer_ids], dim=-1)  # noqa: E731
+    features = lambda: torch.cat([feats[i] for i in cfg.target_layer_ids], dim=-1).cpu()  # noqa: E731
     try:
         target_cache = DynamicCache()
         out = target(input_ids, past_key_values=target_cache, use_cache=True, logits_to_keep=1)
-        tokens = sample(out.logits[:, -1:], 0)[0]
+        tokens = sample(out.logits[:, -1:].cpu(), PREFILL_ROUND)[0].to(dev)
         cache = OracleCache(cfg, 1, P + max_new_tokens + K + 1, oracle.dtype)
         oracle.extend_context(cache, features())
         lengths = []
-        while tokens.shape[1] < max_new_tokens and not torch.isin(tokens[0, -1], stop):
+        while tokens.shape[1] < max_new_tokens and not torch.isin(tokens[0, -1].cpu(), stop):
             anchor = tokens[:, -1]
-            logits = oracle.draft(anchor, cache, embedding, head_w, head_b, num_steps=num_steps,
-                                  z=z_source(rounds))
+            if draft_fn is not None:
+                logits = draft_fn(anchor, rounds).cpu()
+            else:
+                logits = oracle.draft(anchor.cpu(), cache, embedding, head_w, head_b, num_steps=num_steps,
+                                      z=z_source(rounds))
             draft, draft_probs = sample(logits, rounds)
+            draft = draft.to(dev)
             position = P + tokens.shape[1] - 1
             out = target(torch.cat([anchor[:, None], draft], dim=1),
-                         position_ids=torch.arange(position, position + K + 1)[None],
+                         position_ids=torch.arange(position, position + K + 1, device=dev)[None],
                          past_key_values=target_cache, use_cache=True)
+            draft = draft.cpu()
             if temperature <= 0:
-                tt = out.logits.argmax(dim=-1)
+                tt = out.logits.cpu().argmax(dim=-1)
                 accepted = int((draft == tt[:, :-1]).cumprod(dim=1).sum())
                 bonus = tt[:, accepted]
             else:
-                tp = softmax_probs(out.logits, temperature, softmax_mode)[0]
+                tp = softmax_probs(out.logits.cpu(), temperature, softmax_mode)[0]
                 p = tp[:-1].gather(-1, draft[0, :, None])[:, 0]
                 q = draft_probs[0].gather(-1, draft[0, :, None])[:, 0]
                 u = torch.tensor([accept.uniform(rng_seed, k, 0, rounds, 1) for k in range(K)])
@@ -453,8 +471,8 @@ def spec_generate(oracle: Oracle, target, input_ids, max_new_tokens=256, tempera
                 bonus = torch.tensor([accept.categorical_sliced(residual.numpy(),
                                                                 accept.uniform(rng_seed, 0, 0, rounds, 2))])
             rounds += 1
-            new = torch.cat([draft[:, :accepted], bonus.view(1, 1)], dim=1)
-            hits = torch.isin(new[0], stop).nonzero()
+            new = torch.cat([draft[:, :accepted], bonus.view(1, 1)], dim=1).to(dev)
+            hits = torch.isin(new[0].cpu(), stop).nonzero()
             if len(hits):
                 new = new[:, : int(hits[0]) + 1]
             tokens = torch.cat([tokens, new], dim=1)

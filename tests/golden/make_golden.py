@@ -118,8 +118,10 @@ def spec_case(flashmap, temperature, max_new_tokens=64, seed=0, rng_seed=1234):
     Injected draws: round r's one-step noise z is the r-th draw of
     ``torch.randn((1, 16, 256), generator=Generator().manual_seed(77))``; at
     T > 0 the acceptance uniforms are Philox (k, 0, r, 1), the draft rows'
-    categorical draws use Philox (k, 0, r, 3) and the bonus draw (0, 0, r, 2),
-    all through the oracle's categorical sampler (its sliced form for the bonus)."""
+    categorical draws use Philox (k, 0, r, 3), the bonus draw (0, 0, r, 2)
+    and the first target token (sampled from the prefill) (0, 0, 2^32 - 1, 3),
+    a counter no round reaches, all through the oracle's categorical sampler
+    (its sliced form for the bonus)."""
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
     sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
@@ -130,7 +132,7 @@ def spec_case(flashmap, temperature, max_new_tokens=64, seed=0, rng_seed=1234):
     model, config = build_drafter(flashmap, CONFIG1, torch.float32, seed)
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, 2048, (1, 128), generator=g)
-    zs, rounds = [], {"n": 0, "draft_calls": 0}
+    zs, rounds = [], {"n": 0, "draft_calls": 0, "prefill_done": False}
     zg = torch.Generator().manual_seed(77)
     real_randn = torch.randn
 
@@ -146,9 +148,12 @@ def spec_case(flashmap, temperature, max_new_tokens=64, seed=0, rng_seed=1234):
 
     def fake_multinomial(probs, n, generator=None, **kw):
         r = rounds["n"]
-        if probs.dim() == 2:  # the draft's K rows (:557)
-            rounds["draft_calls"] += 1
-            out = [accept.categorical(probs[k].float().numpy(), accept.uniform(rng_seed, k, 0, r, 3))
+        if probs.dim() == 2:  # the prefill's row (:562), then each round's K draft rows (:557)
+            if rounds["prefill_done"]:
+                rounds["draft_calls"] += 1
+            word = r if rounds["prefill_done"] else 0xFFFFFFFF
+            rounds["prefill_done"] = True
+            out = [accept.categorical(probs[k].float().numpy(), accept.uniform(rng_seed, k, 0, word, 3))
                    for k in range(probs.shape[0])]
             return torch.tensor(out, dtype=torch.int64)[:, None]
         tok = accept.categorical_sliced(probs.float().numpy(), accept.uniform(rng_seed, 0, 0, r, 2))  # bonus (:594)

@@ -68,6 +68,33 @@ def logits_rel_error(got: torch.Tensor, ref: torch.Tensor) -> float:
     return float((got[fin] - ref[fin]).abs().max() / ref[fin].abs().max())
 
 
+def decisive_disagreements(got_tokens: torch.Tensor, got_logits: torch.Tensor, ref_logits: torch.Tensor,
+                            drift: float = 0.0) -> tuple:
+    """Argmax disagreements where the reference's decision is clear.
+
+    The margin of a position is its reference top-1 minus top-2 logit.  The
+    threshold of a block is the larger of the block's largest absolute logit
+    difference (CUDA vs reference, over all its positions and columns) and
+    ``drift`` (the same measure for another faithful execution of the
+    reference, e.g. PyTorch on the GPU).  A position whose margin exceeds
+    the threshold is decisive; there the drafted token must be the
+    reference's (tie-aware: its reference logit equals the maximum).
+
+    Returns (disagreements at decisive positions, positions under the
+    threshold, threshold)."""
+    ref = ref_logits.float().cpu()
+    got = got_logits.float().cpu()
+    fin = torch.isfinite(ref)
+    thr = max(float((got[fin] - ref[fin]).abs().max()), float(drift))
+    top2 = ref.topk(2, dim=-1).values
+    margin = top2[..., 0] - top2[..., 1]
+    tok = got_tokens.cpu().reshape(ref.shape[:-1])
+    picked = ref.gather(-1, tok[..., None])[..., 0]
+    agree = picked == top2[..., 0]
+    decisive = margin > thr
+    return int((decisive & ~agree).sum()), int((~decisive).sum()), thr
+
+
 def argmax_agreement(got_tokens: torch.Tensor, ref_logits: torch.Tensor) -> tuple:
     """(tie-aware agreement, strict agreement) of drafted tokens vs reference logits."""
     ref = ref_logits.float().cpu()

@@ -280,7 +280,7 @@ def test_sample_rows_bit_exact(V, T):
     assert torch.equal(greedy, logits.argmax(-1))
 
 
-@pytest.mark.parametrize("B,K,V,seed", [(34, 16, 3001, 5), (8, 16, 151936, 11)])
+@pytest.mark.parametrize("B,K,V,seed", [(34, 16, 3001, 5), (8, 16, 151936, 11), (64, 16, 151936, 12)])
 def test_accept_greedy_bit_exact(B, K, V, seed):
     from tests.golden.inputs import acceptance_inputs
 
@@ -291,7 +291,8 @@ def test_accept_greedy_bit_exact(B, K, V, seed):
 
 
 @pytest.mark.parametrize("logits_dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("B,K,V,seed,T", [(24, 16, 3001, 6, 1.0), (24, 16, 2048, 7, 0.7), (6, 16, 151936, 9, 1.0)])
+@pytest.mark.parametrize("B,K,V,seed,T", [(24, 16, 3001, 6, 1.0), (24, 16, 2048, 7, 0.7), (6, 16, 151936, 9, 1.0),
+                                         (64, 16, 151936, 13, 1.0)])
 def test_accept_rejection_bit_exact(B, K, V, seed, T, logits_dtype):
     """bf16 and fp32 target logits (the fp32 rows hold the same values: bf16 widens exactly)."""
     from tests.golden.inputs import acceptance_inputs
@@ -320,3 +321,26 @@ def test_acceptance_golden_cases_through_cuda():
                                               seed=c["rng_seed"], offset=0)
         assert acc.cpu().tolist() == c["accepted"], name
         assert bonus.cpu().tolist() == c["bonus"], name
+
+
+@pytest.mark.parametrize("logits_dtype", [torch.bfloat16, torch.float32])
+def test_signed_zero_maximum_takes_first_index(logits_dtype):
+    """A row whose maximum is zero held as both -0.0 and +0.0: torch.argmax
+    compares them equal and returns the first index, whichever sign it has.
+    Greedy acceptance (bonus token), the row statistics' argmax and draft
+    sampling at T = 0 must do the same, wherever the two zeros sit in the row
+    (one vocabulary slice or two)."""
+    V = 151936
+    for first, second in ((5, 9), (5, 100000), (70000, 140000)):
+        for sign_first in (-0.0, 0.0):
+            row = torch.full((V,), -1.0)
+            row[first] = sign_first
+            row[second] = -0.0 if sign_first == 0.0 else 0.0
+            target = row.repeat(1, 17, 1).to(logits_dtype)  # (1, K + 1, V): every row the same
+            draft = torch.full((1, 16), first, dtype=torch.int64)
+            acc, bonus = ops.accept_greedy(target.to(DEV), draft.to(DEV))
+            assert int(acc[0]) == 16 and int(bonus[0]) == first, (first, second, sign_first)
+            _, am = ops.row_stats(target[0].to(DEV).contiguous(), 1.0)
+            assert am.cpu().tolist() == [first] * 17
+            tok = ops.sample_rows(target[:, :16].to(DEV).contiguous(), None, 0.0, 1234, 0)
+            assert tok.cpu().tolist() == [[first] * 16]
