@@ -73,26 +73,30 @@ def decisive_disagreements(got_tokens: torch.Tensor, got_logits: torch.Tensor, r
     """Argmax disagreements where the reference's decision is clear.
 
     The margin of a position is its reference top-1 minus top-2 logit.  The
-    threshold of a block is the larger of the block's largest absolute logit
+    logit error of a block is the larger of its largest absolute logit
     difference (CUDA vs reference, over all its positions and columns) and
     ``drift`` (the same measure for another faithful execution of the
-    reference, e.g. PyTorch on the GPU).  A position whose margin exceeds
-    the threshold is decisive; there the drafted token must be the
-    reference's (tie-aware: its reference logit equals the maximum).
+    reference, e.g. PyTorch on the GPU).  Picking another token than the
+    reference's top-1 moves the two logits involved by at most the error
+    each, so a disagreement needs a margin of at most twice the error; a
+    position whose margin exceeds that is decisive, and there the drafted
+    token must be the reference's (tie-aware: its reference logit equals the
+    maximum).  The tokens must be the argmax of ``got_logits`` for the bound
+    to hold; the callers check that.
 
     Returns (disagreements at decisive positions, positions under the
-    threshold, threshold)."""
+    margin, the block's logit error)."""
     ref = ref_logits.float().cpu()
     got = got_logits.float().cpu()
     fin = torch.isfinite(ref)
-    thr = max(float((got[fin] - ref[fin]).abs().max()), float(drift))
+    err = max(float((got[fin] - ref[fin]).abs().max()), float(drift))
     top2 = ref.topk(2, dim=-1).values
     margin = top2[..., 0] - top2[..., 1]
     tok = got_tokens.cpu().reshape(ref.shape[:-1])
     picked = ref.gather(-1, tok[..., None])[..., 0]
     agree = picked == top2[..., 0]
-    decisive = margin > thr
-    return int((decisive & ~agree).sum()), int((~decisive).sum()), thr
+    decisive = margin > 2.0 * err
+    return int((decisive & ~agree).sum()), int((~decisive).sum()), err
 
 
 def argmax_agreement(got_tokens: torch.Tensor, ref_logits: torch.Tensor) -> tuple:

@@ -9,7 +9,7 @@ replaces the plugin core's noise draw with fixed normals.
 
 Tolerances are the north star's: logits within 2e-2 of the reference's
 scale, and no argmax disagreement (tie-aware) at a decisive position, one
-whose reference top-1/top-2 gap exceeds the block's largest logit
+whose reference top-1/top-2 gap exceeds twice the block's largest logit
 difference.
 """
 

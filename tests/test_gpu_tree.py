@@ -5,7 +5,7 @@ sglang plugin's tree mode: N candidate blocks per request in one pass, the
 tree buffers equal to the oracle's trie of the candidates' greedy tokens,
 those tokens agreeing with the oracle's drafts of the same noise (tie-aware,
 no disagreement at a decisive position: one whose reference top-1/top-2
-gap exceeds the first candidate's largest logit difference), the first candidate's logits within 2e-2."""
+gap exceeds twice the first candidate's largest logit difference), the first candidate's logits within 2e-2."""
 
 import os
 from types import SimpleNamespace
