@@ -85,7 +85,7 @@ def test_out_of_range_anchor_records_bad_index():
     bad = torch.tensor([config.vocab_size + 5], device=DEV)
     model.draft(bad, cache, E, W, num_steps=1, z=z)
     torch.cuda.synchronize()
-    plan = model._plan(model._pack(DEV, E, W), cache, 1, 1)
+    plan = model._plan(model._pack(cache.kv.device, E, W), cache, 1, 1)  # the draft's own plan
     assert int(plan.err.item()) == DEV_BAD_INDEX
     with pytest.raises(_lib.FlashMapError):
         plan.check_device_errors()
