@@ -52,7 +52,7 @@ class PlanConfig(ctypes.Structure):
                 ("launch_mode", c_int32)]
 
 
-LAUNCH_AUTO, LAUNCH_KERNELS = 0, 1
+LAUNCH_AUTO, LAUNCH_KERNELS, LAUNCH_STREAM = 0, 1, 2
 
 
 class DraftIO(ctypes.Structure):

@@ -18,7 +18,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(HERE, "libflashmap_b200.so")
-SOURCES = ["runtime.cu", "gemm.cu", "attention.cu", "ops.cu", "plan.cu", "serving.cu", "bank.cu", "tree.cu"]
+SOURCES = ["runtime.cu", "gemm.cu", "attention.cu", "ops.cu", "plan.cu", "stream.cu", "serving.cu", "bank.cu", "tree.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
          "--expt-relaxed-constexpr", "-I" + os.path.join(ROOT, "include")]

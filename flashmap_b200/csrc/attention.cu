@@ -123,45 +123,13 @@ fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream
 
 // ------------------------------------------------------------------ cross-attention
 namespace {
-
-constexpr int XA_TILE = 64;  // keys per pipeline stage
 constexpr int XA_STAGES = 3;
-
-__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-// byte offset of (row, 8-element chunk) inside a tile written by TMA with
-// 128-byte swizzling as boxes of [64 rows x 64 bf16]
-__device__ __forceinline__ uint32_t sw128_offset(int row, int chunk) {
-  const int box = chunk >> 3, cin = chunk & 7;
-  return (uint32_t)(box * (XA_TILE * 128) + row * 128 + ((cin ^ (row & 7)) << 4));
-}
-
 }  // namespace
 
 template <int HD>
 __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__ CUtensorMap tm, CrossAttnArgs a) {
   constexpr int TILE_BYTES = XA_TILE * HD * 2;  // one of K or V
   constexpr int STAGE_BYTES = 2 * TILE_BYTES;
-  constexpr int NT = HD / 8;  // n8 tiles over head dims
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + XA_STAGES * STAGE_BYTES);
@@ -170,7 +138,6 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
   float* mrg = reinterpret_cast<float*>(smem);  // reused after the pipeline: [4][16*HD] O, then m, l
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int gid = lane >> 2, tig = lane & 3;
   const int bh = blockIdx.x / a.nsplit, split = blockIdx.x % a.nsplit;
   const int b = bh / a.heads, h = bh % a.heads;
 
@@ -193,7 +160,7 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
     if (threadIdx.x == 0) record_error(a.err, DEV_BAD_INDEX);
     ctx = ctx < 1 ? 1 : a.cache_len;
   }
-  const int per = ((((ctx + a.nsplit - 1) / a.nsplit) + XA_TILE - 1) / XA_TILE) * XA_TILE;
+  const int per = xa_split_keys(ctx, a.nsplit);
   const int k_begin = split * per;
   const int k_end = min(ctx, k_begin + per);
   if (k_begin >= ctx) return;  // no keys here; the merge counts only splits that own keys
@@ -219,19 +186,12 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
   uint32_t qa[HD / 16][4];
   {
     const __nv_bfloat16* qb = a.q + (long long)(b * 16) * a.hidden + h * HD;
-#pragma unroll
-    for (int ks = 0; ks < HD / 16; ++ks) {
-      const int c = ks * 16 + tig * 2;
-      qa[ks][0] = *reinterpret_cast<const uint32_t*>(qb + (long long)gid * a.hidden + c);
-      qa[ks][1] = *reinterpret_cast<const uint32_t*>(qb + (long long)(gid + 8) * a.hidden + c);
-      qa[ks][2] = *reinterpret_cast<const uint32_t*>(qb + (long long)gid * a.hidden + c + 8);
-      qa[ks][3] = *reinterpret_cast<const uint32_t*>(qb + (long long)(gid + 8) * a.hidden + c + 8);
-    }
+    xa_load_q<HD>(qa, [&](int row, int col) {
+      return *reinterpret_cast<const uint32_t*>(qb + (long long)row * a.hidden + col);
+    });
   }
-  float o[NT][4];
-#pragma unroll
-  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  XaAcc<HD> st;
+  xa_init<HD>(st);
 
   int consumed = 0;
   for (int t = 0; t < ntiles; ++t) {
@@ -256,76 +216,8 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
     }
     consumed = t + 1;
     const uint32_t kbase = smem_u32(smem + s * STAGE_BYTES);
-    const uint32_t vbase = kbase + TILE_BYTES;
     const int key0 = 16 * warp;  // this warp's 16 keys of the tile
-
-    // S = Q K^T for keys key0 .. key0+15 (two n8 tiles)
-    float sc[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
-      const int kr = key0 + nt * 8 + (lane & 7);
-#pragma unroll
-      for (int ks = 0; ks < HD / 16; ks += 2) {
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(kbase + sw128_offset(kr, 2 * ks + (lane >> 3)), r0, r1, r2, r3);
-        mma_bf16_16816(sc[nt], qa[ks], r0, r1);
-        mma_bf16_16816(sc[nt], qa[ks + 1], r2, r3);
-      }
-    }
-    // scale, mask, online softmax (rows gid and gid+8)
-    const int kabs = k_begin + t * XA_TILE + key0;
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const bool valid = kabs + nt * 8 + tig * 2 + e < k_end;
-        sc[nt][e] = valid ? __fmul_rn(sc[nt][e], a.scale) : -INFINITY;
-        sc[nt][2 + e] = valid ? __fmul_rn(sc[nt][2 + e], a.scale) : -INFINITY;
-        mx0 = fmaxf(mx0, sc[nt][e]);
-        mx1 = fmaxf(mx1, sc[nt][2 + e]);
-      }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float n0 = fmaxf(m0, mx0), n1 = fmaxf(m1, mx1);
-    const float u0 = n0 == -INFINITY ? 0.0f : n0, u1 = n1 == -INFINITY ? 0.0f : n1;
-    const float al0 = expf(__fsub_rn(m0, u0)), al1 = expf(__fsub_rn(m1, u1));
-    m0 = n0;
-    m1 = n1;
-    float p[2][4];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      p[nt][0] = expf(__fsub_rn(sc[nt][0], u0));
-      p[nt][1] = expf(__fsub_rn(sc[nt][1], u0));
-      p[nt][2] = expf(__fsub_rn(sc[nt][2], u1));
-      p[nt][3] = expf(__fsub_rn(sc[nt][3], u1));
-    }
-    l0 = __fadd_rn(__fmul_rn(l0, al0), __fadd_rn(__fadd_rn(p[0][0], p[0][1]), __fadd_rn(p[1][0], p[1][1])));
-    l1 = __fadd_rn(__fmul_rn(l1, al1), __fadd_rn(__fadd_rn(p[0][2], p[0][3]), __fadd_rn(p[1][2], p[1][3])));
-#pragma unroll
-    for (int i = 0; i < NT; ++i) {
-      o[i][0] *= al0;
-      o[i][1] *= al0;
-      o[i][2] *= al1;
-      o[i][3] *= al1;
-    }
-    uint32_t pa[4];
-    pa[0] = pack_bf16(p[0][0], p[0][1]);
-    pa[1] = pack_bf16(p[0][2], p[0][3]);
-    pa[2] = pack_bf16(p[1][0], p[1][1]);
-    pa[3] = pack_bf16(p[1][2], p[1][3]);
-    // O += P V over the 16 keys
-    const int vr = key0 + ((lane >> 3) & 1) * 8 + (lane & 7);
-#pragma unroll
-    for (int dn = 0; dn < NT; dn += 2) {
-      uint32_t r0, r1, r2, r3;
-      ldsm_x4_t(vbase + sw128_offset(vr, dn + (lane >> 4)), r0, r1, r2, r3);
-      mma_bf16_16816(o[dn], pa, r0, r1);
-      mma_bf16_16816(o[dn + 1], pa, r2, r3);
-    }
+    xa_tile<HD>(st, qa, kbase, kbase + TILE_BYTES, key0, k_begin + t * XA_TILE + key0, k_end, a.scale);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }
@@ -334,133 +226,19 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
     const int issued = min(ntiles, consumed + XA_STAGES - 1);
     for (int t = consumed; t < issued; ++t) mbar_wait(&full[t % XA_STAGES], (uint32_t)(t / XA_STAGES) & 1u, nullptr);
   }
-  l0 = __fadd_rn(l0, __shfl_xor_sync(0xffffffffu, l0, 1));
-  l0 = __fadd_rn(l0, __shfl_xor_sync(0xffffffffu, l0, 2));
-  l1 = __fadd_rn(l1, __shfl_xor_sync(0xffffffffu, l1, 1));
-  l1 = __fadd_rn(l1, __shfl_xor_sync(0xffffffffu, l1, 2));
-  __syncthreads();  // pipeline smem is free from here on
-
-  // merge the 4 warps: mO[w][16][HD], mM / mL [4][16], then per-row weights
-  float* mO = mrg;
-  float* mM = mrg + 4 * 16 * HD;
-  float* mL = mM + 64;
-  float* mF = mL + 64;   // [4][16] exp(m_w - m)
-  float* mR = mF + 64;   // [16] merged m, [16] merged l
-#pragma unroll
-  for (int i = 0; i < NT; ++i) {
-    const int col = i * 8 + tig * 2;
-    *reinterpret_cast<float2*>(&mO[(warp * 16 + gid) * HD + col]) = make_float2(o[i][0], o[i][1]);
-    *reinterpret_cast<float2*>(&mO[(warp * 16 + gid + 8) * HD + col]) = make_float2(o[i][2], o[i][3]);
-  }
-  if (tig == 0) {
-    mM[warp * 16 + gid] = m0;
-    mM[warp * 16 + gid + 8] = m1;
-    mL[warp * 16 + gid] = l0;
-    mL[warp * 16 + gid + 8] = l1;
-  }
-  __syncthreads();
-  if (threadIdx.x < 16) {
-    const int i = threadIdx.x;
-    float mm = -INFINITY;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, mM[w * 16 + i]);
-    float ll = 0.0f;
-    for (int w = 0; w < 4; ++w) {
-      const float f = mM[w * 16 + i] == -INFINITY ? 0.0f : expf(__fsub_rn(mM[w * 16 + i], mm));
-      mF[w * 16 + i] = f;
-      ll = __fadd_rn(ll, __fmul_rn(mL[w * 16 + i], f));
-    }
-    mR[i] = mm;
-    mR[16 + i] = ll;
-  }
-  __syncthreads();
+  // the pipeline's shared memory is free after xa_finish's first barrier
   const int nsp = a.nsplit;
   const int n_active = (ctx + per - 1) / per;  // splits that own keys (the rest exit above)
   float* mine = a.part + (long long)(bh * nsp + split) * (16 * HD + 32);
-  // each thread: 4 consecutive dims of one row per step (float4)
-  for (int v4 = threadIdx.x; v4 < 16 * HD / 4; v4 += 128) {
-    const int i = (v4 * 4) / HD, d = (v4 * 4) % HD;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float f = mF[w * 16 + i];
-      const float4 ow = *reinterpret_cast<const float4*>(&mO[(w * 16 + i) * HD + d]);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(ow.x, f));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(ow.y, f));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(ow.z, f));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(ow.w, f));
-    }
-    if (n_active == 1) {
-      const float ll = mR[16 + i];
-      __nv_bfloat16* dst = a.out + (long long)(b * 16 + i) * a.hidden + h * HD + d;
-      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(__fdiv_rn(acc.x, ll), __fdiv_rn(acc.y, ll));
-      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(__fdiv_rn(acc.z, ll), __fdiv_rn(acc.w, ll));
-    } else {
-      __stcg(reinterpret_cast<float4*>(mine + i * HD + d), acc);
-    }
-  }
-  if (n_active == 1) return;
-  if (threadIdx.x < 16) {
-    __stcg(mine + 16 * HD + threadIdx.x, mR[threadIdx.x]);
-    __stcg(mine + 16 * HD + 16 + threadIdx.x, mR[16 + threadIdx.x]);
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(a.counters + bh, 1);
-    sflag[1] = (old == n_active - 1);
-  }
-  __syncthreads();
-  if (!sflag[1]) return;
-  __threadfence();
-  // last split of this (sequence, head): merge all splits in split order
   const float* base = a.part + (long long)bh * nsp * (16 * HD + 32);
-  float* sF = mO;  // reuse: [n_active][16] weights, then [16] l
-  for (int t = threadIdx.x; t < 16; t += 128) {
-    float mm = -INFINITY;
-    for (int sp = 0; sp < n_active; ++sp) mm = fmaxf(mm, __ldcg(base + (long long)sp * (16 * HD + 32) + 16 * HD + t));
-    float ll = 0.0f;
-    for (int sp = 0; sp < n_active; ++sp) {
-      const float* ps = base + (long long)sp * (16 * HD + 32);
-      const float ms = __ldcg(ps + 16 * HD + t);
-      const float f = ms == -INFINITY ? 0.0f : expf(__fsub_rn(ms, mm));
-      sF[sp * 16 + t] = f;
-      ll = __fadd_rn(ll, __fmul_rn(__ldcg(ps + 16 * HD + 16 + t), f));
-    }
-    sF[n_active * 16 + t] = ll;
-  }
-  __syncthreads();
-  for (int v4 = threadIdx.x; v4 < 16 * HD / 4; v4 += 128) {
-    const int i = (v4 * 4) / HD, d = (v4 * 4) % HD;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int sp = 0;
-    for (; sp + 4 <= n_active; sp += 4) {
-      float4 t4[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        t4[u] = __ldcg(reinterpret_cast<const float4*>(base + (long long)(sp + u) * (16 * HD + 32) + i * HD + d));
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float f = sF[(sp + u) * 16 + i];
-        acc.x = __fadd_rn(acc.x, __fmul_rn(t4[u].x, f));
-        acc.y = __fadd_rn(acc.y, __fmul_rn(t4[u].y, f));
-        acc.z = __fadd_rn(acc.z, __fmul_rn(t4[u].z, f));
-        acc.w = __fadd_rn(acc.w, __fmul_rn(t4[u].w, f));
-      }
-    }
-    for (; sp < n_active; ++sp) {
-      const float4 t = __ldcg(reinterpret_cast<const float4*>(base + (long long)sp * (16 * HD + 32) + i * HD + d));
-      const float f = sF[sp * 16 + i];
-      acc.x = __fadd_rn(acc.x, __fmul_rn(t.x, f));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(t.y, f));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(t.z, f));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(t.w, f));
-    }
-    const float ll = sF[n_active * 16 + i];
-    __nv_bfloat16* dst = a.out + (long long)(b * 16 + i) * a.hidden + h * HD + d;
-    *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(__fdiv_rn(acc.x, ll), __fdiv_rn(acc.y, ll));
-    *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(__fdiv_rn(acc.z, ll), __fdiv_rn(acc.w, ll));
-  }
-  if (threadIdx.x == 0) a.counters[bh] = 0;
+  __nv_bfloat16* outp = a.out + (long long)(b * 16) * a.hidden + h * HD;
+  const bool merged = xa_finish<HD>(
+      st, mrg, threadIdx.x, n_active, mine, base, sflag + 1, [] { __syncthreads(); },
+      [&] { return atomicAdd(a.counters + bh, 1) == n_active - 1; },
+      [&](int i, int d, float lo, float hi) {
+        *reinterpret_cast<__nv_bfloat162*>(outp + (long long)i * a.hidden + d) = __floats2bfloat162_rn(lo, hi);
+      });
+  if (merged && n_active > 1 && threadIdx.x == 0) a.counters[bh] = 0;
 }
 
 size_t cross_attn_smem(int hd) {

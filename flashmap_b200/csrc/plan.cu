@@ -17,6 +17,10 @@
 //   final adaln -> head GEMM -> LM-head GEMM (logits + argmax fused)  (:312-313, :475)
 //   multi-step: state update between jumps                     (:476-478)
 // Every kernel is launched with programmatic dependent launch on one stream.
+//
+// A batch-1, one-jump draft may instead run as the streamed single-launch
+// pass (stream.cuh) over the same weights and buffers: build_stream lays out
+// its stage list.
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -27,6 +31,7 @@
 #include "attention.cuh"
 #include "gemm_plan.cuh"
 #include "ops.cuh"
+#include "stream.cuh"
 
 namespace fm {
 fm_status launch_self_attn(const SelfAttnArgs& a, int batch, cudaStream_t stream, bool pdl);
@@ -66,6 +71,17 @@ struct fm_plan {
   CUtensorMap cache_map;
   bool has_target;
   long long last_launches;
+  // streamed single-launch pass (batch 1, one jump)
+  bool stream_on;
+  int stream_grid;
+  stream::Params* sp;  // launch parameters (host), per-call fields filled by fm_draft
+  unsigned long long *st_words, *st_done, *st_tickets;
+  long long st_n_tickets;
+  int* st_zero;
+  float* st_ws;
+  float* st_stats;
+  stream::Stage* st_stages;
+  ~fm_plan() { delete sp; }
 };
 
 namespace {
@@ -141,6 +157,38 @@ int pick_nsplit(int B, int H, int cache_len) {
   return ns;
 }
 
+// The streamed pass's shape: batch 1, one jump, the target attached, the
+// HF-path arithmetic (no folds), head_dim 64 or 128, and not a plan that asks
+// for the kernel sequence.
+bool stream_shape(const fm_model_desc* m, const fm_plan_config* c) {
+  if (c->batch != 1 || c->num_steps != 1 || c->launch_mode == FM_LAUNCH_KERNELS) return false;
+  if (c->launch_mode == FM_LAUNCH_AUTO) {
+    const char* e = getenv("FM_STREAM");
+    if (!e || e[0] != '1') return false;
+  }
+  if (!m->embed || !m->lm_w || !m->chol || !m->uniform_embeds || m->lm_fold_w) return false;
+  if (m->noise_fold_w && m->noise_fold_var && m->noise_fold_x0) return false;
+  return m->head_dim == 64 || m->head_dim == 128;
+}
+int stream_stage_cap(const fm_model_desc* m) { return 16 + 7 * (int)m->layers; }
+int64_t tiles128(int64_t rows) { return (rows + 127) / 128; }
+// every ticket of the pass: per GEMM stage one per 128-row tile, then the
+// self-attention groups and the cross-attention heads of every layer
+int64_t stream_tickets(const fm_model_desc* m) {
+  const int64_t D = m->hidden, Ht = m->target_hidden, L = m->layers, S = m->state_vocab;
+  const int64_t mlp1 = m->swiglu ? 2 * (int64_t)m->inter : m->inter;
+  int64_t n = tiles128(Ht) + tiles128(D) + tiles128(L * 2 * D) + tiles128(D);
+  n += L * (tiles128(3 * D) + 3 * tiles128(D) + tiles128(mlp1) + tiles128(D));
+  n += tiles128(Ht) + tiles128(S);
+  n += L * (D / 128) + L * m->heads;
+  return n;
+}
+constexpr int STREAM_WS_SLOTS = 4;
+int64_t stream_stat_tiles(const fm_model_desc* m) {
+  const int64_t a = tiles128(m->target_hidden), b = tiles128(m->hidden);
+  return a > b ? a : b;
+}
+
 // Lay out every buffer; with base == nullptr only the size is computed.
 size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* base) {
   Carver cv{static_cast<char*>(base)};
@@ -152,6 +200,17 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
   int* err = cv.take<int>(64);
   int* gc = cv.take<int>(max_gemm_tiles(m, c) + 64);
   int* xc = cv.take<int>((size_t)B * H + 64);
+  // the streamed pass: counters, tickets and a zero token index (zero-initialised too)
+  const bool sw = stream_shape(m, c);
+  const int scap = sw ? stream_stage_cap(m) : 0;
+  const int64_t n_tickets = sw ? stream_tickets(m) : 0;
+  unsigned long long* st_words = cv.take<unsigned long long>(sw ? 4 : 0);
+  unsigned long long* st_done = cv.take<unsigned long long>((size_t)scap);
+  unsigned long long* st_tickets = cv.take<unsigned long long>((size_t)n_tickets);
+  int* st_zero = cv.take<int>(sw ? 4 : 0);
+  float* st_ws = cv.take<float>(sw ? (size_t)STREAM_WS_SLOTS * num_sms() * 2 * 16 * 128 : 0);
+  float* st_stats = cv.take<float>(sw ? (size_t)(3 * m->layers + 3) * stream_stat_tiles(m) * 32 : 0);
+  stream::Stage* st_stages = cv.take<stream::Stage>((size_t)scap);
   float* gws = cv.take<float>(max_gemm_partials(m, c) / sizeof(float) + 64);
   float* xp = cv.take<float>((size_t)B * H * ns * (16 * hd + 32));
   __nv_bfloat16* anchor_rows = cv.take<__nv_bfloat16>(B * Ht);
@@ -186,6 +245,14 @@ size_t carve(fm_plan* p, const fm_model_desc* m, const fm_plan_config* c, void* 
   int* ext_seq = cv.take<int>(R);
   int* ext_pos = cv.take<int>(R);
   if (p) {
+    p->st_words = st_words;
+    p->st_done = st_done;
+    p->st_tickets = st_tickets;
+    p->st_n_tickets = n_tickets;
+    p->st_zero = st_zero;
+    p->st_ws = st_ws;
+    p->st_stats = st_stats;
+    p->st_stages = st_stages;
     p->err = err;
     p->gemm_counters = gc;
     p->xattn_counters = xc;
@@ -238,14 +305,286 @@ fm_status validate(const fm_model_desc* m, const fm_plan_config* c) {
   if (c->num_steps > 1 && m->embed && !m->embed_state_t)
     return set_error(FM_ERR_INVALID, "plan: multi-step drafts need embed_state_t");
   if (c->cache_batch < c->batch) return set_error(FM_ERR_SHAPE, "plan: cache batch smaller than plan batch");
-  if (c->launch_mode == FM_LAUNCH_PERSISTENT)
-    return set_error(FM_ERR_UNSUPPORTED, "plan: launch_mode FM_LAUNCH_PERSISTENT is reserved; use FM_LAUNCH_KERNELS");
-  if (c->launch_mode != FM_LAUNCH_AUTO && c->launch_mode != FM_LAUNCH_KERNELS)
+  if (c->launch_mode != FM_LAUNCH_AUTO && c->launch_mode != FM_LAUNCH_KERNELS &&
+      c->launch_mode != FM_LAUNCH_PERSISTENT)
     return set_error(FM_ERR_INVALID, "plan: unknown launch_mode %d", c->launch_mode);
   if (!m->layer || !m->rope_cos || !m->rope_sin) return set_error(FM_ERR_INVALID, "plan: missing weights");
   return FM_OK;
 }
 
+
+// ------------------------------------------------------------------ the streamed pass
+//
+// Stage list of one batch-1, one-jump draft (modeling_flashmap.py:422-479):
+//   prep | z L^T (the noise built in the operand) | anchor_proj (the anchor's
+//   embedding row) | every layer's cross k|v of the anchor row (anchor_norm
+//   in the operand; k-norm + RoPE, into the cache) | x_embed (mix_state in
+//   the operand) | per layer: q|k|v (AdaLN operand; q/k norm + RoPE, then the
+//   block self-attention per head group), o (gated residual), cross q (AdaLN;
+//   q norm + RoPE), cross-attention, cross o (gated residual), fc1 / gate_up
+//   (AdaLN; GELU / SwiGLU), fc2 / down (gated residual) | head (final AdaLN) |
+//   LM head (logits + argmax) | tokens.
+// The residual stages and x_embed publish LayerNorm statistics per tile;
+// z L^T and anchor_proj publish sums of squares (mix_state's and
+// anchor_norm's RMS).
+fm_status build_stream(fm_plan* p) {
+  using namespace stream;
+  const fm_model_desc& m = p->m;
+  const int G = grid_size();
+  if (G <= 0) return set_error(FM_ERR_UNSUPPORTED, "streamed pass: the kernel cannot be resident on every SM");
+  if (G > num_sms()) return set_error(FM_ERR_UNSUPPORTED, "streamed pass: grid beyond the carved partials");
+  using bf = __nv_bfloat16;
+  const int D = p->D, Ht = p->Ht, L = p->L, hd = p->hd;
+  const bf* mods = static_cast<const bf*>(p->jumps[0].mods);
+  if (!mods) return set_error(FM_ERR_INVALID, "streamed pass: jump without modulations");
+  std::vector<Stage> st;
+  Params* P = new (std::nothrow) Params();
+  if (!P) return set_error(FM_ERR_INVALID, "streamed pass: host allocation failed");
+  int n_maps = 0;
+  unsigned long long* tk = p->st_tickets;
+  long long tk_used = 0;
+  float* stats = p->st_stats;
+  const int64_t stat_tiles = stream_stat_tiles(&m);
+  auto take_tickets = [&](int64_t n) {
+    unsigned long long* r = tk + tk_used;
+    tk_used += n;
+    return r;
+  };
+  auto take_stats = [&]() {
+    float* r = stats;
+    stats += stat_tiles * 32;
+    return r;
+  };
+  auto gemm = [&](const GemmPlan& g, int dep, int bkind, int ekind, int stat, int ntok) -> int {
+    Stage S{};
+    S.kind = K_GEMM;
+    S.dep = dep;
+    S.dep2 = -1;
+    S.pieces = g.args.m_tiles;
+    S.map = n_maps;
+    P->maps[n_maps++] = g.tmA;
+    S.bkind = bkind;
+    S.ekind = ekind;
+    S.stats = stat;
+    S.ntok = ntok;
+    S.ep = g.args;
+    S.ep.N = ntok;
+    S.tickets = take_tickets(g.args.m_tiles);
+    S.stats_out = stat != S_NONE ? take_stats() : nullptr;
+    S.eps = m.rms_eps;
+    st.push_back(S);
+    return (int)st.size() - 1;
+  };
+  auto tiles_of = [&](int stage) { return st[stage].ep.m_tiles; };
+  {
+    Stage S{};
+    S.kind = K_PREP;
+    S.dep = S.dep2 = -1;
+    S.pieces = 1;
+    st.push_back(S);
+  }
+  const int s_prep = 0;
+  const int s_zl = gemm(p->g_zl, -1, B_NOISE, E_STORE, S_SQ, 16);
+  const int s_ap = gemm(p->g_anchor_proj, -1, B_GATHER, E_STORE, S_SQ, 1);
+  st[s_ap].aux = static_cast<const bf*>(m.embed);
+  const int s_akv = gemm(p->g_anchor_kv, s_ap, B_RMSROW, E_KVCACHE, S_NONE, 1);
+  st[s_akv].src = p->anchor_h;
+  st[s_akv].ld = D;
+  st[s_akv].w0 = static_cast<const bf*>(m.anchor_norm_w);
+  st[s_akv].stats_in = st[s_ap].stats_out;
+  st[s_akv].stats_tiles = tiles_of(s_ap);
+  st[s_akv].ep.token_seq = p->st_zero;
+  const int s_xe = gemm(p->g_xembed, s_zl, B_MIX, E_STORE, S_LN, 16);
+  st[s_xe].src = p->zl;
+  st[s_xe].ld = Ht;
+  st[s_xe].aux = static_cast<const bf*>(m.uniform_embeds);
+  st[s_xe].w0 = static_cast<const bf*>(m.state_norm_w);
+  st[s_xe].w1 = static_cast<const bf*>(m.noise_norm_w);
+  st[s_xe].gate = p->jumps[0].noise_gate;
+  st[s_xe].stats_in = st[s_zl].stats_out;
+  st[s_xe].stats_tiles = tiles_of(s_zl);
+  int s_x = s_xe;  // the stage that last wrote x (its LayerNorm statistics)
+  auto adaln = [&](int stage, const bf* mod) {
+    Stage& S = st[stage];
+    S.src = p->x;
+    S.ld = D;
+    S.mod = mod;
+    S.eps = m.ln_eps;
+    S.stats_in = st[s_x].stats_out;
+    S.stats_tiles = tiles_of(s_x);
+  };
+  for (int l = 0; l < L; ++l) {
+    const GemmPlan* g = &p->g_layer[(size_t)l * 6];
+    const bf* ms = mods + (size_t)(l * 3 + 0) * 3 * D;
+    const bf* mc = mods + (size_t)(l * 3 + 1) * 3 * D;
+    const bf* mm = mods + (size_t)(l * 3 + 2) * 3 * D;
+    const int s_qkv = gemm(g[0], s_x, B_ADALN, E_QKV, S_NONE, 16);
+    adaln(s_qkv, ms);
+    st[s_qkv].pieces = D / 128;  // head groups whose self-attention is done
+    st[s_qkv].groups = take_tickets(D / 128);
+    st[s_qkv].attn = p->attn;
+    const int s_o = gemm(g[1], s_qkv, B_COPY, E_RESID, S_LN, 16);
+    st[s_o].src = p->attn;
+    st[s_o].ld = D;
+    st[s_o].ep.gate = ms + 2 * D;
+    s_x = s_o;
+    const int s_q = gemm(g[2], s_o, B_ADALN, E_QNORM, S_NONE, 16);
+    adaln(s_q, mc);
+    {
+      Stage S{};
+      S.kind = K_XATTN;
+      S.dep = s_q;
+      S.dep2 = s_akv;
+      S.pieces = p->H;
+      S.layer = l;
+      S.nsplit = p->nsplit;
+      S.q = p->qc;
+      S.out = p->attn;
+      S.part = p->xattn_part;
+      S.xtickets = take_tickets(p->H);
+      st.push_back(S);
+    }
+    const int s_xa = (int)st.size() - 1;
+    const int s_co = gemm(g[3], s_xa, B_COPY, E_RESID, S_LN, 16);
+    st[s_co].src = p->attn;
+    st[s_co].ld = D;
+    st[s_co].ep.gate = mc + 2 * D;
+    s_x = s_co;
+    const int s_f1 = gemm(g[4], s_co, B_ADALN, m.swiglu ? E_SWIGLU : E_GELU, S_NONE, 16);
+    adaln(s_f1, mm);
+    const int s_f2 = gemm(g[5], s_f1, B_COPY, E_RESID, S_LN, 16);
+    st[s_f2].src = p->mlp;
+    st[s_f2].ld = p->I;
+    st[s_f2].ep.gate = mm + 2 * D;
+    s_x = s_f2;
+  }
+  const int s_head = gemm(p->g_head, s_x, B_ADALN, E_STORE, S_NONE, 16);
+  adaln(s_head, mods + (size_t)(L * 3) * 3 * D);
+  const int s_lm = gemm(p->g_lm, s_head, B_COPY, E_LOGITS, S_NONE, 16);
+  st[s_lm].src = p->hidden;
+  st[s_lm].ld = Ht;
+  st[s_lm].dep2 = s_prep;
+  st[s_lm].ep.col_ids = reinterpret_cast<const long long*>(m.draft_ids);
+  {
+    Stage S{};
+    S.kind = K_FINAL;
+    S.dep = s_lm;
+    S.dep2 = -1;
+    S.pieces = 1;
+    st.push_back(S);
+  }
+  const int n = (int)st.size();
+  auto fail = [&](const char* why) {
+    delete P;
+    return set_error(FM_ERR_UNSUPPORTED, "streamed pass: %s", why);
+  };
+  if (n > stream_stage_cap(&m)) return fail("stage list longer than its carve-out");
+  if (tk_used > p->st_n_tickets) return fail("tickets beyond their carve-out");
+  if (n_maps + 1 > MAX_MAPS) return fail("more weight matrices than tensor-map slots");
+  // split-K partial buffers: a stage may reuse a buffer once every earlier user
+  // of it is among its ancestors (their finishers have read their partials
+  // before the completion this stage waits for)
+  std::vector<std::vector<char>> anc(n, std::vector<char>(n, 0));
+  for (int i = 0; i < n; ++i)
+    for (int d : {st[i].dep, st[i].dep2})
+      if (d >= 0) {
+        anc[i][d] = 1;
+        for (int k = 0; k < n; ++k)
+          if (anc[d][k]) anc[i][k] = 1;
+      }
+  std::vector<std::vector<int>> users(STREAM_WS_SLOTS);
+  const size_t slot_floats = (size_t)num_sms() * 2 * 16 * 128;
+  for (int i = 0; i < n; ++i) {
+    if (st[i].kind != K_GEMM) continue;
+    int pick = -1;
+    for (int k = 0; k < STREAM_WS_SLOTS && pick < 0; ++k) {
+      bool okk = true;
+      for (int u : users[k]) okk = okk && anc[i][u];
+      if (okk) pick = k;
+    }
+    if (pick < 0) return fail("no split-K partial buffer is free of a concurrent stage");
+    users[pick].push_back(i);
+    st[i].ws = p->st_ws + pick * slot_floats;
+  }
+  // checks the kernel relies on
+  for (int i = 0; i < n; ++i) {
+    const Stage& S = st[i];
+    if (S.kind != K_GEMM) continue;
+    if (S.ep.n_tiles != 1 || S.ep.N > 16) return fail("a stage with more than 16 tokens");
+    if (S.ep.K % 8) return fail("a stage's width is not a multiple of 8");
+    auto misaligned = [](const void* q) { return q != nullptr && (reinterpret_cast<uintptr_t>(q) & 15) != 0; };
+    if (misaligned(S.src) || misaligned(S.mod) || misaligned(S.w0) || misaligned(S.w1) || misaligned(S.aux) ||
+        (S.ld % 8) != 0)
+      return fail("a stage's operand sources are not 16-byte aligned");
+    if (S.stats != S_NONE && S.ep.M > stat_tiles * 128) return fail("statistics beyond their carve-out");
+    if (S.bkind == B_ADALN && (S.ep.K % 128 || S.stats_tiles * 128 != S.ep.K))
+      return fail("AdaLN rows must be whole 128-feature tiles");
+  }
+  if (D % 128) return fail("hidden must be a multiple of 128");
+  if (cudaMemcpy(p->st_stages, st.data(), st.size() * sizeof(Stage), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    return fail("could not copy the stage list to the device");
+  }
+  P->maps[n_maps] = p->cache_map;
+  P->cache_map = n_maps;
+  P->stages = p->st_stages;
+  P->n_stages = n;
+  P->done = p->st_done;
+  P->words = p->st_words;
+  P->all_tickets = p->st_tickets;
+  P->n_tickets = tk_used;
+  P->err = p->err;
+  {
+    const char* e = getenv("FM_STREAM_PF");
+    const int v = e ? atoi(e) : 12;
+    P->pf = v >= 0 && v <= 256 ? v : 12;
+  }
+  P->keys = p->keys;
+  P->lm_stage = s_lm;
+  P->rope_cos = m.rope_cos;
+  P->rope_sin = m.rope_sin;
+  P->rope_len = m.rope_len;
+  P->half = hd / 2;
+  P->cache_len = p->cfg.cache_len;
+  P->cache_batch = p->cfg.cache_batch;
+  P->heads = p->H;
+  P->head_dim = hd;
+  P->hidden = D;
+  P->target_hidden = Ht;
+  P->vocab = m.vocab;
+  P->block = p->K;
+  P->scale = (float)(1.0 / std::sqrt((double)hd));
+  p->sp = P;
+  p->stream_grid = G;
+  p->stream_on = true;
+  return FM_OK;
+}
+
+fm_status run_stream(fm_plan* p, const fm_draft_io* io, cudaStream_t s) {
+  stream::Params& P = *p->sp;
+  P.anchor_ids = io->anchor_ids;
+  P.lengths = io->lengths;
+  P.z = static_cast<const __nv_bfloat16*>(io->z);
+  P.seed = io->seed;
+  P.offset = io->offset;
+  P.offset_ptr = io->offset_ptr;
+  P.tokens = io->tokens;
+  if (io->logits) {
+    P.logits = static_cast<__nv_bfloat16*>(io->logits);
+    P.ldl = io->ldl;
+    P.scatter = (io->scatter && p->m.draft_ids) ? 1 : 0;
+  } else {
+    P.logits = p->logits_s;
+    P.ldl = p->S;
+    P.scatter = 0;
+  }
+  fm_status st = stream::launch(&P, p->stream_grid, s);
+  if (st) return st;
+  if (io->hidden)
+    return check_cuda(cudaMemcpyAsync(io->hidden, p->hidden, (size_t)p->T * p->Ht * 2, cudaMemcpyDeviceToDevice, s),
+                      "draft: copy hidden");
+  return FM_OK;
+}
 
 }  // namespace
 
@@ -408,6 +747,15 @@ extern "C" fm_status fm_plan_create(const fm_model_desc* m, const fm_plan_config
   // the cache as one [rows, head_dim] matrix for the cross-attention TMA
   const uint64_t rows = (uint64_t)L * 2 * c->cache_batch * p->H * c->cache_len;
   if ((st = make_tmap_bf16(&p->cache_map, c->cache, rows, (uint64_t)p->hd, (uint64_t)p->hd, 64))) return fail(st);
+  // the streamed pass: asked for (FM_LAUNCH_PERSISTENT), or chosen by FM_LAUNCH_AUTO when its shape fits
+  if (stream_shape(m, c) && !p->noise_folded) {
+    st = build_stream(p);
+    if (st && c->launch_mode == FM_LAUNCH_PERSISTENT) return fail(st);
+    if (st) p->stream_on = false;
+  } else if (c->launch_mode == FM_LAUNCH_PERSISTENT) {
+    return fail(set_error(FM_ERR_UNSUPPORTED, "plan: the streamed pass serves batch-1, one-jump drafts of the "
+                                              "unfolded head with head_dim 64 or 128"));
+  }
   *out = p;
   return FM_OK;
 }
@@ -528,6 +876,7 @@ extern "C" fm_status fm_draft(fm_plan* p, const fm_draft_io* io, fm_stream strea
     ~Count() { p->last_launches = launch_counter() - l0; }
   } count{p, launches0};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->stream_on) return run_stream(p, io, s);
   const fm_model_desc& m = p->m;
   const int T = p->T, Ht = p->Ht, S = p->S;
   fm_status st;

@@ -523,7 +523,10 @@ class FlashMapDraftModel(PreTrainedModel):
         self.post_init()
 
     # values derived from the weights are rebuilt after a move or a reload (:271-285)
-    # launch_mode "auto" and "kernels": the kernel sequence.
+    # launch_mode: "kernels" runs a draft as the kernel sequence (one launch per
+    # operation); "stream" runs a batch-1, one-jump draft as the streamed
+    # single-launch pass (plan creation raises for other shapes); "auto" picks
+    # the streamed pass where it applies.
     # fold_head: the serving plugins' fast mode (vllm/fold.py:76-100): the DiT
     # head folded into the LM-head rows, one [S, D] projection of the final
     # AdaLN output instead of the head and the [S, Ht] LM head (0.64 GB less
@@ -566,7 +569,7 @@ class FlashMapDraftModel(PreTrainedModel):
         max_pos = cache.max_length + self.config.block_size + 2
         if pack.ensure_rope(self.config, max_pos):
             self._plans = {}
-        mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS}[self.launch_mode]
+        mode = {"auto": _lib.LAUNCH_AUTO, "kernels": _lib.LAUNCH_KERNELS, "stream": _lib.LAUNCH_STREAM}[self.launch_mode]
         key = (cache.kv.data_ptr(), tuple(cache.kv.shape), batch, num_steps, mode, bool(self.fold_head),
                bool(self.fold_noise), pack.device)
         plan = self._plans.get(key)

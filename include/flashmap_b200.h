@@ -546,7 +546,11 @@ enum {
   FM_LAUNCH_AUTO = 0,       /* the kernel sequence */
   FM_LAUNCH_KERNELS = 1,    /* the kernel sequence: one launch per operation, chained by programmatic
                                dependent launch */
-  FM_LAUNCH_PERSISTENT = 2  /* reserved: fm_plan_create returns FM_ERR_UNSUPPORTED */
+  FM_LAUNCH_PERSISTENT = 2  /* the streamed single-launch pass: one cooperative kernel (one CTA per SM)
+                               streams every weight tile through shared memory while the dependent
+                               steps follow one another across the grid; batch 1, one jump, the
+                               unfolded head, head_dim 64 or 128 (else fm_plan_create returns
+                               FM_ERR_UNSUPPORTED) */
 };
 
 typedef struct fm_plan_config {
