@@ -547,6 +547,11 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             const long long U = S.ep.units;
             const int c_first = (int)cta_of_unit((long long)tile * kb, U, G);
             const int c_last = (int)cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
+            // CTAs between c_first and c_last without units of this stage (a stage of fewer
+            // units than CTAs) contribute nothing
+            int n_contrib = 0;
+            for (int cc = c_first; cc <= c_last; ++cc)
+              n_contrib += (long long)(cc + 1) * U / G > (long long)cc * U / G ? 1 : 0;
             const int slot = sb == u0 ? 0 : 1;
             float* mine = S.ws + ((long long)(c * 2 + slot) * 16) * 128;
 #pragma unroll
@@ -555,7 +560,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             named_bar_sync(1, 128);
             if (t == 0) {
               const unsigned long long old = atomicAdd(S.tickets + tile, 1ull);
-              const bool last = old == (unsigned long long)(c_last - c_first);
+              const bool last = old == (unsigned long long)(n_contrib - 1);
               if (last) S.tickets[tile] = 0ull;
               flags[F_TICKET] = last ? 1 : 0;
             }
@@ -568,6 +573,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
               for (int j = 0; j < 16; ++j) v[j] = 0.0f;
               for (int cc = c_first; cc <= c_last; ++cc) {
                 const long long cu0 = (long long)cc * U / G;
+                if ((long long)(cc + 1) * U / G <= cu0) continue;  // no units of this stage
                 const int cs = cu0 >= (long long)tile * kb ? 0 : 1;
                 const float* p = S.ws + ((long long)(cc * 2 + cs) * 16) * 128 + r;
                 float pv[16];
