@@ -603,8 +603,13 @@ def run_ours(args, world, rank, local):
         from flashmap_b200 import DraftSession
 
         def time_folds(fold_head: bool, fold_noise: bool) -> float:
+            # the folds run as the kernel sequence (the streamed pass serves the unfolded head)
             model.fold_head, model.fold_noise = fold_head, fold_noise
-            fsession = DraftSession(model, cache, session.embed_tokens, session.lm_head, num_steps=1, seed=rank)
+            mode, model.launch_mode = model.launch_mode, ("kernels" if model.launch_mode == "stream" else model.launch_mode)
+            try:
+                fsession = DraftSession(model, cache, session.embed_tokens, session.lm_head, num_steps=1, seed=rank)
+            finally:
+                model.launch_mode = mode
             for _ in range(args.warmup):
                 fsession.replay()
             torch.cuda.synchronize()
@@ -674,8 +679,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--launch", choices=["auto", "kernels"], default="auto",
-                    help="launch structure of a draft (both: the kernel sequence)")
+    ap.add_argument("--launch", choices=["auto", "kernels", "stream"], default="auto",
+                    help="launch structure of a draft: the kernel sequence (kernels), the streamed "
+                         "single-launch pass (stream), or the library's choice (auto)")
     ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "paged"], default="config2",
                     help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance), "
                          "config5 (27B map, batch 64 ragged), paged (vLLM paged cross-attention operator)")
