@@ -96,7 +96,37 @@ def _default_req_to_token():
     return get_req_to_token_pool().req_to_token
 
 
+def _env_int(name: str, default) -> int:
+    value = os.environ.get(name)
+    return int(value) if value not in (None, "") else int(default)
+
+
+@dataclass(frozen=True)
+class _ServeSettings:
+    """The sglang plugin's FLASHMAP_* switches (the reference plugin's
+    variables and defaults, sglang/model.py:277-312), read once per model."""
+
+    num_steps: int
+    folded_noise: bool
+    jump_bank: int
+    jump_topk: int
+    tree_n: int
+    tree_budget: int
+    draft_vocab: int
+
+    @classmethod
+    def read(cls, fm, config) -> "_ServeSettings":
+        return cls(num_steps=_env_int("FLASHMAP_NUM_STEPS", fm.num_steps),
+                   folded_noise=os.environ.get("FLASHMAP_FOLDED_NOISE", "0") == "1",
+                   jump_bank=_env_int("FLASHMAP_JUMP_BANK", 8192),
+                   jump_topk=_env_int("FLASHMAP_JUMP_TOPK", 16),
+                   tree_n=_env_int("FLASHMAP_TREE_N", 0),
+                   tree_budget=_env_int("FLASHMAP_TREE_BUDGET", 32),
+                   draft_vocab=_env_int("FLASHMAP_DRAFT_VOCAB", getattr(config, "draft_vocab_size", 0) or 0))
+
+
 class FlashMapDraftModel(FlashMapDiT):
+    # attributes the DSPARK worker reads
     flashmap = True
     uses_own_vocab_modules = False
     supports_pre_gather_target_hidden_projection = False
@@ -104,59 +134,46 @@ class FlashMapDraftModel(FlashMapDiT):
     def __init__(self, config, quant_config=None, prefix: str = "") -> None:
         del quant_config, prefix
         if getattr(config, "flow_map", True) is False:
-            raise ValueError("this checkpoint is a stage-1 flow (flow_map: false), which drafts only by integrating "
-                             "over many steps; serve the flow map instead")
+            raise ValueError("flow_map is false in this checkpoint: it holds the stage-1 flow, which needs many "
+                             "integration steps per block; the plugin serves the distilled flow map")
         super().__init__(config)
         fm = self.config
-        self.block_size = int(fm.block_size)
-        self.vocab_size = fm.vocab_size
-        self.target_hidden_size = fm.target_hidden_size
-        self.dim = fm.hidden_size
-        self.num_heads = fm.num_attention_heads
-        self.gamma = self.block_size
-        self.num_stages = fm.num_hidden_layers
+        opts = _ServeSettings.read(fm, config)
+        if str(opts.num_steps) not in fm.jump_grids:
+            raise ValueError(f"FLASHMAP_NUM_STEPS={opts.num_steps} has no jump grid in this checkpoint "
+                             f"(grids for {', '.join(sorted(fm.jump_grids, key=int))} steps)")
+        if opts.tree_n >= 1 and opts.num_steps != 1:
+            raise NotImplementedError(f"tree drafting (FLASHMAP_TREE_N={opts.tree_n}) drafts with one jump, "
+                                      f"not {opts.num_steps}")
+        # the model's shape, as the worker and the draft step read it
+        self.block_size = self.gamma = int(fm.block_size)
+        self.vocab_size, self.target_hidden_size = fm.vocab_size, fm.target_hidden_size
+        self.dim, self.num_heads, self.num_stages = fm.hidden_size, fm.num_attention_heads, fm.num_hidden_layers
         self.rope_theta = fm.rope_theta
-        self.rms_norm_eps = fm.rms_norm_eps
-        self.qk_norm_eps = fm.qk_norm_eps
-        self.layer_norm_eps = fm.layer_norm_eps
+        self.rms_norm_eps, self.qk_norm_eps, self.layer_norm_eps = fm.rms_norm_eps, fm.qk_norm_eps, fm.layer_norm_eps
+        # DSPARK's protocol: drafts start from the anchor, no Markov or confidence
+        # head of their own, no muP logit scaling; the target's modules arrive later
         self.sample_from_anchor = True
         self.markov_head = IdentityMarkov(self.vocab_size)
         self.confidence_head = None
         self.logits_mup_width_multiplier = None
-        self.lm_head = None
-        self.embedding = None
-        self.hot_ids = None
-        self.folded_head = None
-        self.folded_noise = os.environ.get("FLASHMAP_FOLDED_NOISE", "0") == "1"
-        self.num_steps = int(os.environ.get("FLASHMAP_NUM_STEPS") or fm.num_steps)
-        if str(self.num_steps) not in fm.jump_grids:
-            raise ValueError(f"no jump grid for {self.num_steps} steps (the checkpoint has "
-                             f"{sorted(fm.jump_grids, key=int)})")
-        # several jumps draw from a bank of noise draws, their predictions cut
-        # to their top-k (jump_bank.py; sglang/model.py:283-285, 458-471)
-        self.jump_bank_size = int(os.environ.get("FLASHMAP_JUMP_BANK", "8192"))
-        self.jump_topk = int(os.environ.get("FLASHMAP_JUMP_TOPK", "16"))
-        self.jump_bank = None
-        self.head_to_state = None
-        # Tree drafting (tree_worker.py): up to FLASHMAP_TREE_N candidate blocks
-        # per request from independent noise in one draft pass, merged into a
-        # trie cut to the verify width (block_size + 1 with the root); a batch of
-        # bs requests drafts clamp(FLASHMAP_TREE_BUDGET // bs, 1, N) (sglang/model.py:302-312)
-        self.tree_max_n = int(os.environ.get("FLASHMAP_TREE_N", "0"))
-        self.tree_budget = int(os.environ.get("FLASHMAP_TREE_BUDGET", "32"))
-        self.tree_mode = self.tree_max_n >= 1
-        self.tree_width = self.block_size + 1
-        self._tree_buffers = None
-        self._tree_scratch = None
-        if self.tree_mode and self.num_steps != 1:
-            raise NotImplementedError("tree drafting takes one jump")
-        size = os.environ.get("FLASHMAP_DRAFT_VOCAB")
-        size = int(size if size is not None else getattr(config, "draft_vocab_size", 0) or 0)
+        self.lm_head = self.embedding = self.hot_ids = self.folded_head = None
+        # the switches
+        self.num_steps = opts.num_steps
+        self.folded_noise = opts.folded_noise
+        self.jump_bank_size, self.jump_topk = opts.jump_bank, opts.jump_topk
+        self.jump_bank = self.head_to_state = None
+        self.tree_max_n, self.tree_budget = opts.tree_n, opts.tree_budget
+        self.tree_mode = opts.tree_n >= 1
+        self.tree_width = self.block_size + 1  # the block and its root
+        self._tree_buffers = self._tree_scratch = None
+        # the vocabulary the state lives on: the drafter's own (state_vocab_size),
+        # else a ranked draft vocabulary of FLASHMAP_DRAFT_VOCAB tokens, else all
         self.state_vocab_size = getattr(fm, "state_vocab_size", None)
-        size = self.state_vocab_size or size
+        size = self.state_vocab_size or opts.draft_vocab
         self.draft_vocab_size = size if 0 < size < self.vocab_size else 0
         self._vocab_ranking = None
-        self.noise_temperature = 1.0
+        self.noise_temperature = 1.0  # scales the starting noise (0: deterministic drafts)
         self._core: Optional[PagedDraft] = None
         self._fused_write = None
         self._kv_fp8 = False
@@ -165,41 +182,51 @@ class FlashMapDraftModel(FlashMapDiT):
         self.req_to_token: Callable = _default_req_to_token
 
     # --- loading -----------------------------------------------------------
+    # tensors of a release folder that are not module weights: the draft
+    # vocabulary's ranking (kept) and its counts (unused)
+    _RANKING_NAMES = ("ids", "draft_vocab_ids")
+    _IGNORED_NAMES = ("counts",)
+
     def load_weights(self, weights: Iterable[Tuple[str, torch.Tensor]]) -> None:
-        """The folder's weights; ``draft_vocab.safetensors``'s ``ids`` rank the
-        token ids, most frequent first (sglang/model.py:344-403)."""
-        params = {**dict(self.named_parameters()), **dict(self.named_buffers())}
-        loaded = set()
+        """Every tensor of the release folder (sglang/model.py:344-403): module
+        weights by name, and ``draft_vocab.safetensors``'s token ranking (most
+        frequent first).  Unknown names and absent weights raise KeyError."""
+        targets = dict(self.named_parameters())
+        targets.update(self.named_buffers())
+        seen = set()
         for name, tensor in weights:
-            if name in ("ids", "draft_vocab_ids"):
+            if name in self._RANKING_NAMES:
                 self._vocab_ranking = tensor
-                continue
-            if name == "counts":
-                continue
-            if name not in params:
-                raise KeyError(f"unexpected FlashMap weight {name!r}")
-            with torch.no_grad():
-                params[name].copy_(tensor.to(params[name].dtype))
-            loaded.add(name)
-        missing = sorted(n for n in params if n not in loaded and not n.startswith(("markov_head.", "lm_head.")))
-        if missing:
-            raise KeyError(f"FlashMap weights missing from the checkpoint: {missing}")
+            elif name in self._IGNORED_NAMES:
+                pass
+            elif name in targets:
+                with torch.no_grad():
+                    targets[name].copy_(tensor.to(targets[name].dtype))
+                seen.add(name)
+            else:
+                raise KeyError(f"the checkpoint holds {name!r}, which is no FlashMap weight")
+        # the Markov head is the plugin's own stand-in and the LM head the target's
+        absent = sorted(set(targets) - seen - {n for n in targets if n.split(".")[0] in ("markov_head", "lm_head")})
+        if absent:
+            raise KeyError(f"the checkpoint lacks FlashMap weights: {absent}")
         self._clear_caches()
 
     def attach_shared_modules(self, *, embed_tokens: nn.Module, lm_head: nn.Module):
-        """The target's embedding and LM head (sglang/model.py:405-425)."""
+        """The target's embedding and LM head (sglang/model.py:405-425).  A
+        head without a weight of its own (tied embeddings) reads the
+        embedding.  Both must be the whole (V, target_hidden) matrix."""
         if self.logits_mup_width_multiplier:
-            raise NotImplementedError("FlashMap does not support muP-scaled targets")
-        embedding = embed_tokens.weight.detach()
-        head = getattr(lm_head, "weight", None)
-        head = embedding if head is None else head.detach()
-        for name, weight in (("embedding", embedding), ("LM head", head)):
-            if weight.shape != (self.vocab_size, self.target_hidden_size):
-                raise ValueError(f"the target's {name} is {tuple(weight.shape)}, the draft expects "
-                                 f"({self.vocab_size}, {self.target_hidden_size}); padded or sharded vocabularies "
-                                 "are not supported")
-        self.embedding = embedding
-        self.prepare(head)
+            raise NotImplementedError("muP-scaled target logits are not supported by the FlashMap draft")
+        emb = embed_tokens.weight.detach()
+        head_w = getattr(lm_head, "weight", None)
+        head_w = emb if head_w is None else head_w.detach()
+        want = (self.vocab_size, self.target_hidden_size)
+        for what, w in (("embedding", emb), ("LM head", head_w)):
+            if tuple(w.shape) != want:
+                raise ValueError(f"the target's {what} has shape {tuple(w.shape)} but the drafter needs {want}: a "
+                                 "vocabulary padded or sharded across tensor-parallel ranks cannot be drafted over")
+        self.embedding = emb
+        self.prepare(head_w)
 
     @torch.no_grad()
     def prepare(self, lm_head_weight: torch.Tensor) -> None:

@@ -30,7 +30,7 @@ from __future__ import annotations
 
 import os
 from dataclasses import dataclass
-from typing import Callable, Iterable, List, Optional, Sequence, Tuple
+from typing import Callable, Iterable, List, NamedTuple, Optional, Sequence, Tuple
 
 import torch
 from torch import nn
@@ -39,89 +39,112 @@ from . import serving_ops as S
 from .modeling_flashmap import FlashMapDraftModel as _HFModel
 from .paged_draft import PagedDraft
 
-__all__ = ["ContextCachePlan", "FlashMapDraftModel", "attend_by_segments", "plan_context_cache"]
+__all__ = ["ContextLayout", "FlashMapDraftModel", "HeadRun", "attend_runs", "context_layout"]
 
-MODES = ("auto", "layers", "virtual")
+# FLASHMAP_CONTEXT_CACHE (the reference plugin's switch): "auto" packs on hybrid
+# targets only, "layers" never packs, "virtual" packs whenever the target allows.
+LAYOUT_MODES = ("auto", "layers", "virtual")
+
+
+class HeadRun(NamedTuple):
+    """Consecutive heads of one DiT layer stored side by side in one cache:
+    ``count`` heads from ``head`` on, at head slots ``slot`` .. of cache ``cache``."""
+
+    cache: int
+    slot: int
+    count: int
+    head: int
 
 
 @dataclass(frozen=True)
-class ContextCachePlan:
-    """Where the DiT's context heads live (flashmap/vllm/context_cache.py:31-84):
-    ``num_caches`` attention layers of ``heads_per_cache`` heads hold the
-    ``num_layers`` x ``heads`` heads in layer-major order."""
+class ContextLayout:
+    """Placement of the DiT's context keys/values in vLLM's paged caches.
 
-    num_layers: int
+    The DiT's ``layers`` x ``heads`` heads are numbered layer-major (head h of
+    layer l is head number l * heads + h) and stored ``per_cache`` to an
+    attention cache, in that order, over ``caches`` caches.  Unpacked, each DiT
+    layer is its own cache (``per_cache == heads``); packed (``packed``), every
+    cache has the page size of the target's full-attention layers and a DiT
+    layer's heads may straddle two or more caches (the layout
+    flashmap/vllm/context_cache.py describes).  ``why`` says why this layout
+    was chosen."""
+
+    layers: int
     heads: int
-    num_caches: int
-    heads_per_cache: int
-    virtual: bool
-    reason: str
+    caches: int
+    per_cache: int
+    packed: bool
+    why: str
 
-    def place(self, layer: int, head: int) -> Tuple[int, int]:
-        """(cache, head slot) of DiT head ``head`` of layer ``layer``."""
-        return divmod(layer * self.heads + head, self.heads_per_cache)
+    def where(self, layer: int, head: int) -> Tuple[int, int]:
+        """(cache, head slot) of head ``head`` of DiT layer ``layer``."""
+        n = layer * self.heads + head
+        return n // self.per_cache, n % self.per_cache
 
-    @property
-    def segments(self) -> List[List[Tuple[int, int, int, int]]]:
-        """Per layer, its heads as runs ``(cache, first slot, count, first head)``."""
-        out = []
-        for layer in range(self.num_layers):
-            runs: List[Tuple[int, int, int, int]] = []
-            for head in range(self.heads):
-                cache, slot = self.place(layer, head)
-                if runs and runs[-1][0] == cache:
-                    c, first, count, h0 = runs[-1]
-                    runs[-1] = (c, first, count + 1, h0)
-                else:
-                    runs.append((cache, slot, 1, head))
-            out.append(runs)
+    def runs(self, layer: int) -> List[HeadRun]:
+        """Layer ``layer``'s heads cut at cache boundaries, in head order."""
+        out: List[HeadRun] = []
+        first, end = layer * self.heads, (layer + 1) * self.heads
+        while first < end:
+            cache, slot = divmod(first, self.per_cache)
+            count = min(self.per_cache - slot, end - first)
+            out.append(HeadRun(cache, slot, count, first - layer * self.heads))
+            first += count
         return out
 
 
-def plan_context_cache(num_layers: int, heads: int, head_dim: int, *, hybrid: bool, target_attention_layers: int,
-                       target_kv_heads: int, target_head_size: int, bf16_cache: bool,
-                       mode: Optional[str] = None) -> ContextCachePlan:
-    """One cache per DiT layer, or (the virtual layout, for hybrid targets) the
-    target's attention layers' page per token packed with DiT heads in order
-    (context_cache.py:87-127)."""
+def context_layout(num_layers: int, heads: int, head_dim: int, *, hybrid: bool, target_attention_layers: int,
+                   target_kv_heads: int, target_head_size: int, bf16_cache: bool,
+                   mode: Optional[str] = None) -> ContextLayout:
+    """The context layout for a DiT of ``num_layers`` layers of ``heads``
+    heads of ``head_dim``, beside a target with ``target_attention_layers``
+    full-attention layers of ``target_kv_heads`` heads of ``target_head_size``.
+
+    Packing pays off on hybrid targets (linear-attention or Mamba layers beside
+    full attention), where vLLM sizes every layer's page to the largest one;
+    it needs a bf16 cache, a target page that holds whole DiT heads, and
+    enough target layers for all the DiT's heads.  Otherwise each DiT layer
+    keeps a cache of its own."""
     mode = mode or os.environ.get("FLASHMAP_CONTEXT_CACHE", "auto")
-    if mode not in MODES:
-        raise ValueError(f"FLASHMAP_CONTEXT_CACHE must be one of {MODES}, got {mode!r}")
-
-    def per_layer(reason: str) -> ContextCachePlan:
-        return ContextCachePlan(num_layers, heads, num_layers, heads, False, reason)
-
+    if mode not in LAYOUT_MODES:
+        raise ValueError(f"FLASHMAP_CONTEXT_CACHE is {mode!r}; expected one of {', '.join(LAYOUT_MODES)}")
+    page = target_kv_heads * target_head_size  # elements per token of one target attention layer
+    fits = page // head_dim if head_dim > 0 and page > 0 and page % head_dim == 0 else 0
     if mode == "layers":
-        return per_layer("FLASHMAP_CONTEXT_CACHE=layers")
-    if mode == "auto" and not hybrid:
-        return per_layer("a target without linear-attention or Mamba layers")
-    if not bf16_cache:
-        return per_layer("an fp8 KV cache")
-    elements = target_kv_heads * target_head_size
-    if target_attention_layers <= 0 or elements <= 0 or elements % head_dim:
-        return per_layer(f"target attention of {target_kv_heads} heads of {target_head_size} does not hold heads "
-                         f"of {head_dim}")
-    per = elements // head_dim
-    if target_attention_layers * per < num_layers * heads:
-        return per_layer(f"{target_attention_layers} target attention layers of {per} heads cannot hold "
-                         f"{num_layers} x {heads} heads")
-    return ContextCachePlan(num_layers, heads, target_attention_layers, per, True,
-                            f"{target_attention_layers} caches of {per} heads of {head_dim}, the target "
-                            "attention's page")
+        why = "per-layer caches requested (FLASHMAP_CONTEXT_CACHE=layers)"
+    elif mode == "auto" and not hybrid:
+        why = "the target has full attention only, so per-layer caches cost no padding"
+    elif not bf16_cache:
+        why = "packed caches need a bf16 KV cache; per-layer caches hold fp8"
+    elif target_attention_layers <= 0 or fits == 0:
+        why = (f"a target attention page ({target_kv_heads} x {target_head_size}) holds no whole number of "
+               f"DiT heads of size {head_dim}")
+    elif target_attention_layers * fits < num_layers * heads:
+        why = (f"{num_layers * heads} DiT heads do not fit in {target_attention_layers} target-sized caches of "
+               f"{fits} heads")
+    else:
+        return ContextLayout(num_layers, heads, target_attention_layers, fits, True,
+                             f"packed: {num_layers * heads} DiT heads in {target_attention_layers} caches of "
+                             f"{fits} heads (the target attention's page)")
+    return ContextLayout(num_layers, heads, num_layers, heads, False, why)
 
 
-def attend_by_segments(query: torch.Tensor, caches: Sequence[torch.Tensor], segments, attend) -> torch.Tensor:
-    """A layer's cross-attention over its head runs (context_cache.py:130-139):
-    ``attend(query heads, cache heads, count)`` per run on head views, the
-    outputs concatenated along the heads."""
+def attend_runs(query: torch.Tensor, caches: Sequence[torch.Tensor], runs: Sequence[HeadRun], attend) -> torch.Tensor:
+    """A DiT layer's cross-attention over a layout's head runs.
+
+    ``query`` is (tokens, heads, head_dim) and ``caches`` vLLM's paged
+    tensors (blocks, heads, block_size, 2 * head_dim).  ``attend(q, c, n)``
+    attends ``n`` query heads to the same ``n`` cache heads; it is called once
+    per run on views of the run's heads (the whole tensors when the run covers
+    both), and the outputs are joined along the heads in run order."""
     heads = query.shape[1]
-    parts = []
-    for cache_id, first_slot, count, first_head in segments:
-        cache = caches[cache_id]
-        q = query if count == heads else query[:, first_head:first_head + count].contiguous()
-        c = cache if count == cache.shape[1] else cache[:, first_slot:first_slot + count]
-        parts.append(attend(q, c, count))
-    return parts[0] if len(parts) == 1 else torch.cat(parts, dim=1)
+    outs = []
+    for run in runs:
+        cache = caches[run.cache]
+        q = query if run.count == heads else query[:, run.head:run.head + run.count].contiguous()
+        c = cache if run.count == cache.shape[1] else cache[:, run.slot:run.slot + run.count]
+        outs.append(attend(q, c, run.count))
+    return outs[0] if len(outs) == 1 else torch.cat(outs, dim=1)
 
 
 def _default_forward_context():
@@ -177,14 +200,14 @@ class FlashMapDraftModel(nn.Module):
         self.kv_scales: Optional[torch.Tensor] = None
 
     @staticmethod
-    def _context_plan(config, vllm_config) -> ContextCachePlan:
+    def _context_plan(config, vllm_config) -> ContextLayout:
         heads = int(config.num_attention_heads)
         head_dim = int(config.hidden_size) // heads
         model_config = vllm_config.model_config
         hybrid = bool(getattr(model_config, "is_hybrid", False))
         cache_config = getattr(vllm_config, "cache_config", None)
         bf16 = str(getattr(cache_config, "cache_dtype", "auto")) in ("auto", "bfloat16")
-        return plan_context_cache(
+        return context_layout(
             int(config.num_hidden_layers), heads, head_dim, hybrid=hybrid,
             target_attention_layers=int(getattr(model_config, "num_attention_layers", 0) or 0),
             target_kv_heads=int(getattr(model_config, "num_kv_heads", 0) or 0),
@@ -197,8 +220,8 @@ class FlashMapDraftModel(nn.Module):
     def bind_cache_layers(self, layers: list) -> None:
         """The attention layers (objects with ``kv_cache``, ``layer_name`` and
         ``kv_cache_dtype``) that hold the context, in cache order."""
-        if len(layers) != self.cache_plan.num_caches:
-            raise ValueError(f"{len(layers)} cache layers for a plan of {self.cache_plan.num_caches}")
+        if len(layers) != self.cache_plan.caches:
+            raise ValueError(f"the context layout has {self.cache_plan.caches} caches, got {len(layers)} layers")
         self._cache_layers = list(layers)
         self._cache_args = None
 
@@ -273,7 +296,7 @@ class FlashMapDraftModel(nn.Module):
         self.dim = core.D
         self.softmax_scale = self.head_dim ** -0.5
         self._check_attention()
-        self.segments = self.cache_plan.segments
+        self.segments = [self.cache_plan.runs(layer) for layer in range(self.cache_plan.layers)]
         self._jumps = core.jump(self.num_steps)
         self.modulations = [core.modulations(s, t) for s, t, _ in self._jumps]
         self.cos_sin = core.rope_pairs(self.max_model_len + self.block_size + 1)
@@ -297,7 +320,7 @@ class FlashMapDraftModel(nn.Module):
             raise ValueError("the context caches mix bf16 and fp8")
         self.kv_fp8 = fp8 == {True}
         if self.kv_fp8:
-            assert not self.cache_plan.virtual, "the virtual layout needs a bf16 cache"
+            assert not self.cache_plan.packed, "packed context caches need a bf16 cache"
             device = self._core.pack.device
 
             def scale(attn, name):
@@ -345,7 +368,7 @@ class FlashMapDraftModel(nn.Module):
         _, ptrs, strides, block_size = layout
         S.write_context_kv(kv.view(-1, len(self.layers), 2, self.num_heads, self.head_dim), positions, slots,
                            self.context_k_norm, self.cos_sin, ptrs, strides, block_size, self.config.qk_norm_eps,
-                           self.kv_scales, self.cache_plan.heads_per_cache)
+                           self.kv_scales, self.cache_plan.per_cache)
 
     def precompute_and_store_context_kv(self, context_states: torch.Tensor, context_positions: torch.Tensor,
                                         context_slot_mapping: Optional[torch.Tensor] = None) -> None:
@@ -379,7 +402,7 @@ class FlashMapDraftModel(nn.Module):
                                                     None if descales is None else descales[..., :count].contiguous(),
                                                     K, self.max_model_len, self.softmax_scale, 3)
 
-            return attend_by_segments(query, caches, self.segments[layer], one)
+            return attend_runs(query, caches, self.segments[layer], one)
 
         return attend
 

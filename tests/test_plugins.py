@@ -67,7 +67,7 @@ def test_vllm_construction_checks():
     config = FlashMapConfig(**CFG)
     m = VL.FlashMapDraftModel(vllm_config=vllm_config(config))
     assert m.noise_scale == 1.0 and m.compile is True and m.hot_ids is None
-    assert m.block_size == 16 and not m.cache_plan.virtual
+    assert m.block_size == 16 and not m.cache_plan.packed
     with pytest.raises(ValueError, match="tensor parallel"):
         VL.FlashMapDraftModel(vllm_config=vllm_config(config, parallel_config=SimpleNamespace(tensor_parallel_size=2)))
     with pytest.raises(ValueError, match="V2 model runner"):
@@ -121,23 +121,33 @@ def test_sglang_construction_and_loading():
                                 lm_head=SimpleNamespace(weight=torch.zeros(10, 256)))
 
 
-def test_context_cache_plan():
-    plan = VL.plan_context_cache(6, 20, 128, hybrid=True, target_attention_layers=16, target_kv_heads=8,
-                                 target_head_size=128, bf16_cache=True)
-    assert plan.virtual and plan.num_caches == 16 and plan.heads_per_cache == 8
-    # layer 0's 20 heads span caches 0, 1, 2 (8 + 8 + 4)
-    assert plan.segments[0] == [(0, 0, 8, 0), (1, 0, 8, 8), (2, 0, 4, 16)]
-    assert plan.segments[1][0] == (2, 4, 4, 0)
-    covered = sorted(plan.place(l, h) for l in range(6) for h in range(20))
-    assert len(set(covered)) == 120
-    assert not VL.plan_context_cache(6, 20, 128, hybrid=False, target_attention_layers=16, target_kv_heads=8,
-                                     target_head_size=128, bf16_cache=True).virtual
-    assert not VL.plan_context_cache(6, 20, 128, hybrid=True, target_attention_layers=16, target_kv_heads=8,
-                                     target_head_size=128, bf16_cache=False).virtual
+def test_context_layout():
+    """The packed layout of the reference plugin's hybrid-target mode: the
+    DiT's heads layer-major in target-sized caches, a layer's heads cut at
+    cache boundaries into runs."""
+    lay = VL.context_layout(6, 20, 128, hybrid=True, target_attention_layers=16, target_kv_heads=8,
+                            target_head_size=128, bf16_cache=True)
+    assert lay.packed and lay.caches == 16 and lay.per_cache == 8
+    # layer 0's 20 heads span caches 0, 1, 2 (8 + 8 + 4); layer 1 starts at slot 4 of cache 2
+    assert lay.runs(0) == [(0, 0, 8, 0), (1, 0, 8, 8), (2, 0, 4, 16)]
+    assert lay.runs(1)[0] == (2, 4, 4, 0)
+    covered = sorted(lay.where(l, h) for l in range(6) for h in range(20))
+    assert len(set(covered)) == 120 and max(covered)[0] < 16
+    for layer in range(6):  # the runs cover each layer's heads once, in order
+        heads = [r.head + i for r in lay.runs(layer) for i in range(r.count)]
+        assert heads == list(range(20))
+        assert all(lay.where(layer, r.head) == (r.cache, r.slot) for r in lay.runs(layer))
+    assert not VL.context_layout(6, 20, 128, hybrid=False, target_attention_layers=16, target_kv_heads=8,
+                                 target_head_size=128, bf16_cache=True).packed
+    assert not VL.context_layout(6, 20, 128, hybrid=True, target_attention_layers=16, target_kv_heads=8,
+                                 target_head_size=128, bf16_cache=False).packed
+    small = VL.context_layout(6, 20, 128, hybrid=True, target_attention_layers=4, target_kv_heads=8,
+                              target_head_size=128, bf16_cache=True)
+    assert not small.packed and small.caches == 6 and small.runs(3) == [(3, 0, 20, 0)]
     with pytest.raises(ValueError):
-        VL.plan_context_cache(2, 4, 64, hybrid=False, target_attention_layers=0, target_kv_heads=0,
-                              target_head_size=0, bf16_cache=True, mode="bogus")
+        VL.context_layout(2, 4, 64, hybrid=False, target_attention_layers=0, target_kv_heads=0,
+                          target_head_size=0, bf16_cache=True, mode="bogus")
     q = torch.arange(2 * 20 * 3.0).view(2, 20, 3)
     caches = [torch.zeros(1, 8, 1, 6) for _ in range(16)]
-    out = VL.attend_by_segments(q, caches, plan.segments[0], lambda pq, pc, n: pq * 2)
+    out = VL.attend_runs(q, caches, lay.runs(0), lambda pq, pc, n: pq * 2)
     assert torch.equal(out, q * 2)
