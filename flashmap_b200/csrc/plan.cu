@@ -355,14 +355,29 @@ fm_status build_stream(fm_plan* p) {
     stats += stat_tiles * 32;
     return r;
   };
+  int rot = 0;
   auto gemm = [&](const GemmPlan& g, int dep, int bkind, int ekind, int stat, int ntok) -> int {
     Stage S{};
     S.kind = K_GEMM;
     S.dep = dep;
     S.dep2 = -1;
     S.pieces = g.args.m_tiles;
+    // the CTAs the stage's units are split over: at most 4 per 128-row tile (so a
+    // tile's partials are few), more when a CTA would otherwise stream over 256 KB
+    const int64_t units = g.args.units, bytes = (int64_t)g.args.M * g.args.K * 2;
+    int64_t vg = std::min<int64_t>(G, (int64_t)g.args.m_tiles * 4);
+    vg = std::max<int64_t>(vg, std::min<int64_t>(G, (bytes + (256 << 10) - 1) >> 18));
+    vg = std::min<int64_t>(vg, units);
+    S.vg = (int)vg;
+    S.rot = rot;
+    rot = (int)((rot + vg) % G);
     S.map = n_maps;
     P->maps[n_maps++] = g.tmA;
+    S.bmap = -1;
+    if (bkind == B_COPY) {
+      S.bmap = n_maps;
+      P->maps[n_maps++] = g.tmB;
+    }
     S.bkind = bkind;
     S.ekind = ekind;
     S.stats = stat;
@@ -376,23 +391,28 @@ fm_status build_stream(fm_plan* p) {
     return (int)st.size() - 1;
   };
   auto tiles_of = [&](int stage) { return st[stage].ep.m_tiles; };
-  {
+  auto aux_stage = [&](int kind, int dep, const bf* src, bf* dst, long long count) -> int {
     Stage S{};
-    S.kind = K_PREP;
-    S.dep = S.dep2 = -1;
-    S.pieces = 1;
+    S.kind = kind;
+    S.dep = dep;
+    S.dep2 = -1;
+    S.pieces = kind == K_NOISE ? G : 1;
+    S.src = src;
+    S.dst = dst;
+    S.count = count;
+    S.eps = m.rms_eps;
     st.push_back(S);
-  }
-  const int s_prep = 0;
-  const int s_zl = gemm(p->g_zl, -1, B_NOISE, E_STORE, S_SQ, 16);
-  const int s_ap = gemm(p->g_anchor_proj, -1, B_GATHER, E_STORE, S_SQ, 1);
-  st[s_ap].aux = static_cast<const bf*>(m.embed);
-  const int s_akv = gemm(p->g_anchor_kv, s_ap, B_RMSROW, E_KVCACHE, S_NONE, 1);
-  st[s_akv].src = p->anchor_h;
-  st[s_akv].ld = D;
-  st[s_akv].w0 = static_cast<const bf*>(m.anchor_norm_w);
-  st[s_akv].stats_in = st[s_ap].stats_out;
-  st[s_akv].stats_tiles = tiles_of(s_ap);
+    return (int)st.size() - 1;
+  };
+  // the anchor's embedding row (and keys reset, index checks); the one-step noise
+  const int s_prep = aux_stage(K_PREP, -1, nullptr, p->anchor_rows, Ht);
+  st[s_prep].aux = static_cast<const bf*>(m.embed);
+  const int s_noise = aux_stage(K_NOISE, -1, nullptr, p->z, (long long)p->T * Ht);
+  const int s_zl = gemm(p->g_zl, s_noise, B_COPY, E_STORE, S_SQ, 16);
+  const int s_ap = gemm(p->g_anchor_proj, s_prep, B_COPY, E_STORE, S_NONE, 1);
+  const int s_an = aux_stage(K_ANORM, s_ap, p->anchor_h, p->anchor_ctx, D);
+  st[s_an].w0 = static_cast<const bf*>(m.anchor_norm_w);
+  const int s_akv = gemm(p->g_anchor_kv, s_an, B_COPY, E_KVCACHE, S_NONE, 1);
   st[s_akv].ep.token_seq = p->st_zero;
   const int s_xe = gemm(p->g_xembed, s_zl, B_MIX, E_STORE, S_LN, 16);
   st[s_xe].src = p->zl;
@@ -519,6 +539,8 @@ fm_status build_stream(fm_plan* p) {
     if (S.stats != S_NONE && S.ep.M > stat_tiles * 128) return fail("statistics beyond their carve-out");
     if (S.bkind == B_ADALN && (S.ep.K % 128 || S.stats_tiles * 128 != S.ep.K))
       return fail("AdaLN rows must be whole 128-feature tiles");
+    if (S.bkind != B_COPY && S.stats_tiles > 40) return fail("source rows wider than 40 tiles of 128");
+    if (S.bkind == B_COPY && S.bmap < 0) return fail("a copied operand without its tensor map");
   }
   if (D % 128) return fail("hidden must be a multiple of 128");
   if (cudaMemcpy(p->st_stages, st.data(), st.size() * sizeof(Stage), cudaMemcpyHostToDevice) != cudaSuccess) {

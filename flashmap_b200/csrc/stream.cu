@@ -17,7 +17,9 @@ constexpr int OFF_B = OFF_A + NA * A_BYTES;
 constexpr int OFF_STAGE = OFF_B + NB * B_BYTES;
 constexpr int OFF_EPI = OFF_STAGE + BATCH * STAGE_SLOT;
 constexpr int OFF_BSTAT = OFF_EPI + EPI_SCRATCH;       // operand warps: [16][2] row statistics, misc
-constexpr int OFF_BAR = OFF_BSTAT + 256;
+constexpr int MAX_STAT_TILES = 40;                      // source rows of up to 40 * 128 features
+constexpr int OFF_SSTAT = OFF_BSTAT + 256;              // the producing stage's per-tile statistics
+constexpr int OFF_BAR = OFF_SSTAT + MAX_STAT_TILES * 16 * 2 * 4;
 constexpr int N_BARS = 2 * NA + 2 * NB + 2 + 2 + 1;
 constexpr int OFF_FLAGS = OFF_BAR + N_BARS * 8;
 constexpr int SMEM_USED = OFF_FLAGS + 64;
@@ -27,7 +29,7 @@ static_assert(OFF_B % 1024 == 0 && OFF_A % 1024 == 0, "UMMA operand rings need 1
 
 // flags: each written by one thread of one warp group and read by the group after a barrier
 constexpr int F_ABORT = 0, F_DEP = 1, F_EPI = 2, F_TICKET = 3, F_XA = 4, F_XW = 5 /* 5, 6 */, F_BDEP = 7,
-              F_BW = 8 /* 8, 9 */;
+              F_BW = 8 /* 8, 9 */, F_BCOPY = 10;
 
 // ------------------------------------------------------------------ cross-CTA counters
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
@@ -88,6 +90,20 @@ __device__ __forceinline__ void unit_range(long long U, int G, int c, long long&
   u0 = (long long)c * U / G;
   u1 = (long long)(c + 1) * U / G;
 }
+// the virtual CTA of CTA c in a GEMM stage (-1: none) and its units
+__device__ __forceinline__ int stage_vcta(const Stage& S, int c, int G) {
+  const int v = (c - S.rot % G + G) % G;
+  return v < S.vg ? v : -1;
+}
+__device__ __forceinline__ int stage_range(const Stage& S, int c, int G, long long& u0, long long& u1) {
+  const int v = stage_vcta(S, c, G);
+  if (v < 0) {
+    u0 = u1 = 0;
+    return -1;
+  }
+  unit_range(S.ep.units, S.vg, v, u0, u1);
+  return v;
+}
 
 // Operand blocks and tiles of a cross-attention item (the split of cross_attn_kernel)
 struct XaItem {
@@ -118,7 +134,7 @@ template <int HD>
 __device__ long long stage_slots(const Params& P, const Stage& S, int c, int G) {
   if (S.kind == K_GEMM) {
     long long u0, u1;
-    unit_range(S.ep.units, G, c, u0, u1);
+    stage_range(S, c, G, u0, u1);
     return u1 - u0;
   }
   if (S.kind == K_XATTN) {
@@ -293,14 +309,6 @@ __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// noise element pairs of the one-step draw (philox_normal_bf16_kernel): z[e]
-// for e = 2p, 2p + 1 from normal_pair(seed, offset, p)
-__device__ __forceinline__ uint4 noise8(const Params& P, uint32_t off, long long e0) {
-  float z[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) normal_pair(P.seed, off, (e0 >> 1) + i, z[2 * i], z[2 * i + 1]);
-  return pack_bf16x8(z);
-}
 
 }  // namespace
 
@@ -372,7 +380,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             pf_started = true;
             if (ps >= n_stages) return;
             const Stage& Q = P.stages[ps];
-            if (Q.kind == K_GEMM) unit_range(Q.ep.units, G, c, pu, pu1);
+            if (Q.kind == K_GEMM) stage_range(Q, c, G, pu, pu1);
             else pu = pu1 = 0;
           }
           const Stage& Q = P.stages[ps];
@@ -387,7 +395,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         const Stage& S = P.stages[s];
         if (S.kind == K_GEMM) {
           long long u0, u1;
-          unit_range(S.ep.units, G, c, u0, u1);
+          stage_range(S, c, G, u0, u1);
           const CUtensorMap* map = &P.maps[S.map];
           for (long long u = u0; u < u1; ++u) {
             if (P.pf > 0) pf_advance(gemm_issued + P.pf);
@@ -468,7 +476,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           continue;
         }
         long long u0, u1;
-        unit_range(S.ep.units, G, c, u0, u1);
+        stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
         for (long long u = u0; u < u1 && ok;) {
           const int tile = (int)(u / kb);
@@ -519,7 +527,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       const Stage& S = P.stages[s];
       if (S.kind == K_GEMM) {
         long long u0, u1;
-        unit_range(S.ep.units, G, c, u0, u1);
+        const int v = stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
         for (long long u = u0; u < u1;) {
           const int tile = (int)(u / kb);
@@ -533,8 +541,8 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             break;
           }
           tc_fence_after();
-          float v[16];
-          tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 16), v);
+          float v16[16];
+          tmem_ld_x16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 16), v16);
           tmem_wait_ld();
           tc_fence_before();
           __syncwarp();
@@ -543,19 +551,22 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           const bool whole = sb == (long long)tile * kb && se == (long long)(tile + 1) * kb;
           bool finisher = whole;
           if (!whole) {
-            // publish this CTA's partial; the last contributor to arrive finishes the tile
+            // publish this CTA's partial (row r's 16 tokens contiguous); the last
+            // contributor to arrive finishes the tile
             const long long U = S.ep.units;
-            const int c_first = (int)cta_of_unit((long long)tile * kb, U, G);
-            const int c_last = (int)cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
-            // CTAs between c_first and c_last without units of this stage (a stage of fewer
-            // units than CTAs) contribute nothing
+            const int vg = S.vg;
+            const int c_first = (int)cta_of_unit((long long)tile * kb, U, vg);
+            const int c_last = (int)cta_of_unit((long long)(tile + 1) * kb - 1, U, vg);
+            // virtual CTAs between c_first and c_last without units (a stage of fewer
+            // units than virtual CTAs) contribute nothing
             int n_contrib = 0;
             for (int cc = c_first; cc <= c_last; ++cc)
-              n_contrib += (long long)(cc + 1) * U / G > (long long)cc * U / G ? 1 : 0;
+              n_contrib += (long long)(cc + 1) * U / vg > (long long)cc * U / vg ? 1 : 0;
             const int slot = sb == u0 ? 0 : 1;
-            float* mine = S.ws + ((long long)(c * 2 + slot) * 16) * 128;
+            float4* mine = reinterpret_cast<float4*>(S.ws + ((long long)(v * 2 + slot) * 128 + r) * 16);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) __stcg(mine + j * 128 + r, v[j]);
+            for (int j = 0; j < 4; ++j)
+              __stcg(mine + j, make_float4(v16[4 * j], v16[4 * j + 1], v16[4 * j + 2], v16[4 * j + 3]));
             __threadfence();
             named_bar_sync(1, 128);
             if (t == 0) {
@@ -568,24 +579,43 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             finisher = flags[F_TICKET] != 0;
             if (finisher) {
               __threadfence();
-              // contributor order: c_first .. c_last (their partials' slots: 0 when the tile holds their first unit)
+              // the contributors' partials in contributor order (slot 0 when the tile holds
+              // their first unit), read four contributors at a time
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-              for (int cc = c_first; cc <= c_last; ++cc) {
-                const long long cu0 = (long long)cc * U / G;
-                if ((long long)(cc + 1) * U / G <= cu0) continue;  // no units of this stage
-                const int cs = cu0 >= (long long)tile * kb ? 0 : 1;
-                const float* p = S.ws + ((long long)(cc * 2 + cs) * 16) * 128 + r;
-                float pv[16];
+              for (int j = 0; j < 16; ++j) v16[j] = 0.0f;
+              int cc = c_first;
+              while (cc <= c_last) {
+                float4 pv[4][4];
+                int n = 0, who[4];
+                for (; cc <= c_last && n < 4; ++cc) {
+                  const long long cu0 = (long long)cc * U / vg;
+                  if ((long long)(cc + 1) * U / vg <= cu0) continue;  // no units of this stage
+                  const int cs = cu0 >= (long long)tile * kb ? 0 : 1;
+                  who[n++] = cc * 2 + cs;
+                }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) pv[j] = __ldcg(p + j * 128);
+                for (int i = 0; i < 4; ++i)
+                  if (i < n) {
+                    const float4* pp = reinterpret_cast<const float4*>(S.ws + ((long long)who[i] * 128 + r) * 16);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], pv[j]);
+                    for (int j = 0; j < 4; ++j) pv[i][j] = __ldcg(pp + j);
+                  }
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  if (i < n) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                      v16[4 * j] = __fadd_rn(v16[4 * j], pv[i][j].x);
+                      v16[4 * j + 1] = __fadd_rn(v16[4 * j + 1], pv[i][j].y);
+                      v16[4 * j + 2] = __fadd_rn(v16[4 * j + 2], pv[i][j].z);
+                      v16[4 * j + 3] = __fadd_rn(v16[4 * j + 3], pv[i][j].w);
+                    }
+                  }
               }
             }
           }
           if (!finisher) continue;
-          finish_tile<HD>(P, S, v, r, tile, escr);
+          finish_tile<HD>(P, S, v16, r, tile, escr);
           __threadfence();
           named_bar_sync(1, 128);
           if (S.ekind == E_QKV) {
@@ -699,9 +729,10 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
   } else {
     // ---------------------------------------------------------- operand builders (warps 6, 7)
     const int tb = (int)threadIdx.x - 192;
-    uint32_t ib = 0;
+    uint32_t ib = 0;  // operand blocks issued into the ring
     bool ok = true;
     const uint32_t noise_off = P.offset + bump;
+    float* sstat = reinterpret_cast<float*>(smem + OFF_SSTAT);
     // the operand slot `slot` free again: one thread waits (bounded) and the group
     // reads the outcome (alternating flags, as for the attention tiles)
     uint32_t nwait = 0;
@@ -711,26 +742,76 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       named_bar_sync(2, 64);
       return *f != 0;
     };
+    auto finish_piece = [&](int s) {
+      __threadfence();
+      named_bar_sync(2, 64);
+      if (tb == 0) red_release_add_u64(P.done + s, 1ull);
+    };
     for (int s = 0; s < n_stages && ok; ++s) {
       const Stage& S = P.stages[s];
       if (S.kind == K_PREP) {
+        // keys reset, index checks, the anchor's embedding row
         if (c == 0) {
           if (tb < P.block) P.keys[tb] = 0ull;
+          long long id = P.anchor_ids[0];
           if (tb == 0) {
-            const long long id = P.anchor_ids[0];
             const int len = P.lengths[0];
             if (id < 0 || id >= P.vocab) record_error(P.err, DEV_BAD_INDEX);
             if (len < 0 || len + P.block + 1 > P.rope_len || len >= P.cache_len) record_error(P.err, DEV_BAD_INDEX);
           }
-          __threadfence();
+          if (id < 0 || id >= P.vocab) id = 0;
+          const uint4* src = reinterpret_cast<const uint4*>(S.aux + id * S.count);
+          uint4* dst = reinterpret_cast<uint4*>(S.dst);
+          for (long long k = tb; k < S.count / 8; k += 64) dst[k] = src[k];
+          finish_piece(s);
+        }
+        continue;
+      }
+      if (S.kind == K_NOISE) {
+        // this CTA's share of the one-step noise: Philox pairs, or the caller's z
+        const long long pairs = S.count / 2;
+        const long long p0 = (long long)c * pairs / G, p1 = (long long)(c + 1) * pairs / G;
+        __nv_bfloat162* dst = reinterpret_cast<__nv_bfloat162*>(S.dst);
+        const __nv_bfloat162* zin = reinterpret_cast<const __nv_bfloat162*>(P.z);
+        for (long long pp = p0 + tb; pp < p1; pp += 64) {
+          if (zin) {
+            dst[pp] = zin[pp];
+          } else {
+            float z0, z1;
+            normal_pair(P.seed, noise_off, pp, z0, z1);
+            dst[pp] = __floats2bfloat162_rn(z0, z1);
+          }
+        }
+        finish_piece(s);
+        continue;
+      }
+      if (S.kind == K_ANORM) {
+        // anchor_norm of the projected anchor row (the rmsnorm kernel's arithmetic)
+        if (c == 0) {
+          if (tb == 0) flags[F_BDEP] = wait_deps(P, S, cta_abort) ? 1 : 0;
           named_bar_sync(2, 64);
-          if (tb == 0) red_release_add_u64(P.done + s, 1ull);
+          if (!flags[F_BDEP]) {
+            ok = false;
+            break;
+          }
+          if (tb < 32) {
+            const float inv = inv_rms(warp_row_sumsq_batched(S.src, (int)S.count, lane), (int)S.count, S.eps);
+            for (int ch = lane; ch < S.count / 8; ch += 32) {
+              float x[8], w8[8], y[8];
+              unpack_bf16x8(__ldcg(reinterpret_cast<const uint4*>(S.src) + ch), x);
+              unpack_bf16x8(*(reinterpret_cast<const uint4*>(S.w0) + ch), w8);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) y[e] = rms_value(x[e], w8[e], inv);
+              *(reinterpret_cast<uint4*>(S.dst) + ch) = pack_bf16x8(y);
+            }
+          }
+          finish_piece(s);
         }
         continue;
       }
       if (S.kind != K_GEMM) continue;
       long long u0, u1;
-      unit_range(S.ep.units, G, c, u0, u1);
+      stage_range(S, c, G, u0, u1);
       if (u1 <= u0) continue;
       if (tb == 0) flags[F_BDEP] = wait_deps(P, S, cta_abort) ? 1 : 0;
       named_bar_sync(2, 64);
@@ -738,117 +819,93 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         ok = false;
         break;
       }
-      const int K = S.ep.K, kb = S.ep.kb, ntok = S.ntok;
-      // per-stage constants: the source rows' statistics
-      if (S.bkind == B_ADALN) {
-        if (tb < 16) {
-          // Chan's combination of the tiles' (sum, M2) in tile order, 128 rows each
+      const int K = S.ep.K, kb = S.ep.kb;
+      if (S.bkind == B_COPY) {
+        // the source rows by TMA ([16 x 64] boxes, 128-byte swizzled: the UMMA
+        // layout), one thread issuing up to the ring's depth ahead of the MMA
+        if (tb == 0) {
+          fence_proxy_async_global();  // rows written by other CTAs' epilogues, read by TMA
+          const CUtensorMap* map = &P.maps[S.bmap];
+          bool good = true;
+          for (long long u = u0; u < u1; ++u) {
+            const int slot = ib % NB;
+            if (ib >= NB && !ring_wait(P, &bempty[slot], ((ib / NB) - 1) & 1u, cta_abort)) {
+              good = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&bfull[slot], B_BYTES);
+            tma_load_2d(sB + slot * B_BYTES, map, &bfull[slot], (int)(u % kb) * 64, 0);
+            ++ib;
+          }
+          flags[F_BCOPY] = good ? 1 : 0;
+        }
+        named_bar_sync(2, 64);
+        if (tb != 0) ib += (uint32_t)(u1 - u0);  // thread 0 counted its copies as it issued them
+        if (!flags[F_BCOPY]) {
+          ok = false;
+          break;
+        }
+        continue;
+      }
+      // transforms: the producing stage's per-tile statistics into shared memory
+      // (one round trip), combined per token in tile order
+      for (int k = tb; k < S.stats_tiles * 8; k += 64)
+        cp16(sstat + k * 4, S.stats_in + k * 4, true);
+      cp_commit();
+      cp_wait<0>();
+      named_bar_sync(2, 64);
+      if (tb < 16) {
+        if (S.bkind == B_ADALN) {
+          // Chan's combination of the tiles' (sum, sum of squared deviations), 128 rows each
           float tot = 0.0f;
-          for (int i = 0; i < S.stats_tiles; ++i) tot = __fadd_rn(tot, __ldcg(S.stats_in + (i * 16 + tb) * 2));
+          for (int i = 0; i < S.stats_tiles; ++i) tot = __fadd_rn(tot, sstat[(i * 16 + tb) * 2]);
           const float mean = __fdiv_rn(tot, (float)K);
           float m2 = 0.0f;
           for (int i = 0; i < S.stats_tiles; ++i) {
-            const float st = __ldcg(S.stats_in + (i * 16 + tb) * 2);
-            const float dm = __fsub_rn(__fdiv_rn(st, 128.0f), mean);
-            m2 = __fadd_rn(m2, __fadd_rn(__ldcg(S.stats_in + (i * 16 + tb) * 2 + 1), __fmul_rn(128.0f, __fmul_rn(dm, dm))));
+            const float dm = __fsub_rn(__fdiv_rn(sstat[(i * 16 + tb) * 2], 128.0f), mean);
+            m2 = __fadd_rn(m2, __fadd_rn(sstat[(i * 16 + tb) * 2 + 1], __fmul_rn(128.0f, __fmul_rn(dm, dm))));
           }
-          const float var = __fdiv_rn(m2, (float)K);
           bstat[tb * 2] = mean;
-          bstat[tb * 2 + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, S.eps)));
-        }
-      } else if (S.bkind == B_MIX || S.bkind == B_RMSROW) {
-        if (tb < 16) {
+          bstat[tb * 2 + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(m2, (float)K), S.eps)));
+        } else {
           float ss = 0.0f;
-          for (int i = 0; i < S.stats_tiles; ++i) ss = __fadd_rn(ss, __ldcg(S.stats_in + (i * 16 + tb) * 2));
+          for (int i = 0; i < S.stats_tiles; ++i) ss = __fadd_rn(ss, sstat[(i * 16 + tb) * 2]);
           bstat[tb * 2] = inv_rms(ss, K, S.eps);
         }
-        if (S.bkind == B_MIX && tb >= 32) {
-          // the uniform posterior row's RMS (a constant row)
-          const float ssu = warp_row_sumsq_batched(S.aux, K, lane);
-          if (lane == 0) bstat[32] = inv_rms(ssu, K, S.eps);
-        }
+      }
+      if (S.bkind == B_MIX && tb >= 32) {
+        // the uniform posterior row's RMS (a constant row)
+        const float ssu = warp_row_sumsq_batched(S.aux, K, lane);
+        if (lane == 0) bstat[32] = inv_rms(ssu, K, S.eps);
       }
       named_bar_sync(2, 64);
-      if (S.bkind == B_COPY || (S.bkind == B_NOISE && P.z != nullptr)) {
-        // plain rows: asynchronous 16-byte copies straight into the operand ring, 8 blocks in flight
-        const bf16* src = S.bkind == B_COPY ? S.src : P.z;
-        const long long ld = S.bkind == B_COPY ? S.ld : (long long)K;
-        constexpr int DEPTH = 8;
-        long long done_u = u0;
-        for (long long u = u0; u < u1; ++u) {
-          const int slot = ib % NB;
-          if (ib >= NB && !slot_free(slot, ((ib / NB) - 1) & 1u)) {
-            ok = false;
-            break;
-          }
-          const int kk = (int)(u % kb);
-          uint8_t* dst = sB + slot * B_BYTES;
+      // raw rows and constant rows of up to BATCH blocks staged, then the operand computed
+      for (long long ub = u0; ub < u1 && ok; ub += BATCH) {
+        const int nb = (int)min((long long)BATCH, u1 - ub);
+        for (int j = 0; j < nb; ++j) {
+          const int kk = (int)((ub + j) % kb);
+          uint8_t* st = sStage + j * STAGE_SLOT;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const int idx = tb + 64 * i, n = idx >> 3, ch = idx & 7;
             const int k0 = kk * 64 + ch * 8;
-            const bool valid = n < ntok && k0 < K;
-            cp16(dst + b_off(n, ch), valid ? (const void*)(src + (long long)n * ld + k0) : (const void*)src, valid);
+            const bool valid = k0 < K;
+            cp16(st + n * 128 + ch * 16, valid ? (const void*)(S.src + (long long)n * S.ld + k0) : (const void*)S.src,
+                 valid);
           }
-          cp_commit();
-          ++ib;
-          if (u - u0 + 1 > DEPTH) {
-            cp_wait<DEPTH>();
-            fence_proxy_async_smem();
-            named_bar_sync(2, 64);
-            if (tb == 0) mbar_arrive(&bfull[(ib - 1 - DEPTH) % NB]);
-            ++done_u;
+          // constant rows: [scale, shift] (AdaLN) or [uniform, state_norm, noise_norm] (mix_state)
+          if (tb < 24) {
+            const int row = tb >> 3, ch = tb & 7;
+            const int k0 = kk * 64 + ch * 8;
+            const bf16* src = S.bkind == B_ADALN ? (row == 0 ? S.mod : row == 1 ? S.mod + K : nullptr)
+                                                 : (row == 0 ? S.aux : row == 1 ? S.w0 : S.w1);
+            const bool valid = src != nullptr && k0 < K;
+            cp16(st + B_BYTES + row * 128 + ch * 16, valid ? (const void*)(src + k0) : (const void*)S.src, valid);
           }
         }
-        if (!ok) break;
+        cp_commit();
         cp_wait<0>();
-        fence_proxy_async_smem();
         named_bar_sync(2, 64);
-        if (tb == 0)
-          for (long long i = done_u; i < u1; ++i) mbar_arrive(&bfull[(ib - (uint32_t)(u1 - i)) % NB]);
-        continue;
-      }
-      // transforms: raw rows and constant rows of up to BATCH blocks staged, then the operand computed
-      for (long long ub = u0; ub < u1 && ok; ub += BATCH) {
-        const int nb = (int)min((long long)BATCH, u1 - ub);
-        if (S.bkind != B_NOISE) {
-          for (int j = 0; j < nb; ++j) {
-            const int kk = (int)((ub + j) % kb);
-            uint8_t* st = sStage + j * STAGE_SLOT;
-            // data rows (row-major [16][64] bf16)
-            if (S.bkind == B_ADALN || S.bkind == B_MIX || S.bkind == B_RMSROW) {
-              const bf16* src = S.src;
-#pragma unroll
-              for (int i = 0; i < 2; ++i) {
-                const int idx = tb + 64 * i, n = idx >> 3, ch = idx & 7;
-                const int k0 = kk * 64 + ch * 8;
-                const bool valid = n < ntok && k0 < K;
-                cp16(st + n * 128 + ch * 16, valid ? (const void*)(src + (long long)n * S.ld + k0) : (const void*)src,
-                     valid);
-              }
-            }
-            // constant rows: [scale, shift] / [uniform, state_norm, noise_norm] / [norm] / [embedding row]
-            if (tb < 24) {
-              const int row = tb >> 3, ch = tb & 7;
-              const int k0 = kk * 64 + ch * 8;
-              const bf16* src = nullptr;
-              if (S.bkind == B_ADALN) src = row == 0 ? S.mod : row == 1 ? S.mod + K : nullptr;
-              else if (S.bkind == B_MIX) src = row == 0 ? S.aux : row == 1 ? S.w0 : S.w1;
-              else if (S.bkind == B_RMSROW) src = row == 0 ? S.w0 : nullptr;
-              else if (S.bkind == B_GATHER && row == 0) {
-                long long id = P.anchor_ids[0];
-                if (id < 0 || id >= P.vocab) id = 0;  // recorded by the prep stage
-                src = S.aux + id * (long long)K;
-              }
-              const bool valid = src != nullptr && k0 < K;
-              cp16(st + B_BYTES + row * 128 + ch * 16, valid ? (const void*)(src + k0) : (const void*)P.lengths,
-                   valid);
-            }
-          }
-          cp_commit();
-          cp_wait<0>();
-          named_bar_sync(2, 64);
-        }
         for (int j = 0; j < nb; ++j) {
           const int slot = ib % NB;
           if (ib >= NB && !slot_free(slot, ((ib / NB) - 1) & 1u)) {
@@ -863,38 +920,26 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             const int idx = tb + 64 * i, n = idx >> 3, ch = idx & 7;
             const int k0 = kk * 64 + ch * 8;
             uint4 o = make_uint4(0u, 0u, 0u, 0u);
-            if (n < ntok && k0 < K) {
+            if (k0 < K) {
               float x[8], y[8];
-              if (S.bkind == B_NOISE) {
-                o = noise8(P, noise_off, (long long)n * K + k0);
-              } else if (S.bkind == B_GATHER) {
-                o = *reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16);
+              unpack_bf16x8(*reinterpret_cast<const uint4*>(st + n * 128 + ch * 16), x);
+              if (S.bkind == B_ADALN) {
+                float sc[8], sh[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), sc);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sh);
+                const float mean = bstat[n * 2], rstd = bstat[n * 2 + 1];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) y[e] = adaln_value(x[e], mean, rstd, sc[e], sh[e]);
               } else {
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + n * 128 + ch * 16), x);
-                if (S.bkind == B_ADALN) {
-                  float sc[8], sh[8];
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), sc);
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sh);
-                  const float mean = bstat[n * 2], rstd = bstat[n * 2 + 1];
+                float pu[8], sw[8], nw[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), pu);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sw);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 256 + ch * 16), nw);
+                const float ip = bstat[32], is = bstat[n * 2];
 #pragma unroll
-                  for (int e = 0; e < 8; ++e) y[e] = adaln_value(x[e], mean, rstd, sc[e], sh[e]);
-                } else if (S.bkind == B_MIX) {
-                  float pu[8], sw[8], nw[8];
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), pu);
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sw);
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 256 + ch * 16), nw);
-                  const float ip = bstat[32], is = bstat[n * 2];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) y[e] = mix_value(pu[e], x[e], sw[e], nw[e], ip, is, S.gate);
-                } else {  // B_RMSROW
-                  float w8[8];
-                  unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), w8);
-                  const float inv = bstat[n * 2];
-#pragma unroll
-                  for (int e = 0; e < 8; ++e) y[e] = rms_value(x[e], w8[e], inv);
-                }
-                o = pack_bf16x8(y);
+                for (int e = 0; e < 8; ++e) y[e] = mix_value(pu[e], x[e], sw[e], nw[e], ip, is, S.gate);
               }
+              o = pack_bf16x8(y);
             }
             *reinterpret_cast<uint4*>(dst + b_off(n, ch)) = o;
           }
@@ -906,6 +951,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         named_bar_sync(2, 64);  // the staging slots are refilled by the next round
       }
     }
+    // operand copies issued by TMA land before the CTA's shared memory goes away
+    if (tb == 0 && !ok)
+      for (uint32_t i = ib > NB ? ib - NB : 0; i < ib; ++i) mbar_wait(&bfull[i % NB], (i / NB) & 1u, nullptr);
     cp_wait<0>();  // no copy into shared memory outlives the CTA
   }
 

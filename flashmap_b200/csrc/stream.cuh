@@ -49,12 +49,13 @@ constexpr int NA = 8;                     // weight ring slots
 constexpr int A_BYTES = 128 * 64 * 2;     // one 128 x 64 weight tile
 constexpr int NB = 16;                    // operand ring slots
 constexpr int B_BYTES = 16 * 64 * 2;      // one 16 x 64 operand block
-constexpr int BATCH = 12;                 // operand blocks staged per round for a transform
+constexpr int BATCH = 10;                 // operand blocks staged per round for a transform
 constexpr int STAGE_SLOT = B_BYTES + 3 * 128;  // staged rows of one block + up to three constant rows
-constexpr int MAX_MAPS = 96;
+constexpr int MAX_MAPS = 112;
 
-enum Kind : int { K_PREP = 0, K_GEMM = 1, K_XATTN = 2, K_FINAL = 3 };
-enum BKind : int { B_NOISE = 0, B_GATHER = 1, B_RMSROW = 2, B_MIX = 3, B_ADALN = 4, B_COPY = 5 };
+enum Kind : int { K_PREP = 0, K_GEMM = 1, K_XATTN = 2, K_FINAL = 3, K_NOISE = 4, K_ANORM = 5 };
+// operand sources: rows copied by TMA, or computed from staged rows (mix_state, AdaLN)
+enum BKind : int { B_COPY = 0, B_MIX = 1, B_ADALN = 2 };
 enum EKind : int { E_STORE = 0, E_GELU = 1, E_SWIGLU = 2, E_RESID = 3, E_QKV = 4, E_QNORM = 5, E_KVCACHE = 6,
                    E_LOGITS = 7 };
 enum Stats : int { S_NONE = 0, S_LN = 1, S_SQ = 2 };
@@ -63,8 +64,11 @@ struct Stage {
   int kind;
   int dep, dep2;     // stages whose completion this stage's inputs need (-1: none)
   int pieces;        // completion count of this stage per draft
-  // GEMM
+  // GEMM: the units are split over `vg` of the CTAs, virtual CTA v being CTA
+  // (v + rot) % grid, so that the small stages of a chain spread over the grid
+  int vg, rot;
   int map;           // weight tensor map (index into Params::maps)
+  int bmap;          // B_COPY: the operand source's tensor map ([rows, K], boxes of 16 x 64)
   int bkind, ekind, stats;
   int ntok;          // operand rows that hold data (16, or 1 for the anchor row)
   const bf16* src;   // operand source rows [ntok, K] (stride ld)
@@ -72,12 +76,14 @@ struct Stage {
   const bf16* mod;   // B_ADALN: scale | shift rows (K each)
   const bf16* w0;    // B_RMSROW: norm weight; B_MIX: state_norm weight
   const bf16* w1;    // B_MIX: noise_norm weight
-  const bf16* aux;   // B_MIX: uniform-posterior row; B_GATHER: embedding [V, K]
+  const bf16* aux;   // B_MIX: uniform-posterior row; K_PREP: the embedding [V, count]
+  bf16* dst;         // K_PREP: anchor row; K_NOISE: noise rows; K_ANORM: normalised anchor row
+  long long count;   // elements of dst
   const float* stats_in;  // statistics of the source rows: [tiles][16][2]
   int stats_tiles;
   float* stats_out;  // this stage's statistics: [m_tiles][16][2]
   float eps, gate;
-  float* ws;         // split-K partials [grid][2][16][128]
+  float* ws;         // split-K partials [virtual CTA][2 slots][128 rows][16 tokens]
   unsigned long long* tickets;  // [m_tiles] contributors arrived
   unsigned long long* groups;   // E_QKV: [D / 128] finished tiles of each (q, k, v) group
   bf16* attn;        // E_QKV: block self-attention output [16, D]
