@@ -172,10 +172,40 @@ __device__ __forceinline__ void token_sums(float* val, float* xch, float* out, i
 }
 
 // ------------------------------------------------------------------ epilogue of one finished tile
+// The inputs of a tile's epilogue that do not depend on its sums (bias,
+// gate, the residual rows, the rotary factors), loaded before the tile's
+// accumulator is ready so that finishing the tile takes no extra round trip.
+struct EpiPre {
+  float bias, gate;
+  float pre[32];
+};
+__device__ __forceinline__ void epi_prefetch(const Params& P, const Stage& S, int mt, int r, EpiPre& e) {
+  const GemmArgs& a = S.ep;
+  const int m = mt * 128 + r;
+  const bool mvalid = m < a.M;
+  e.bias = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
+  e.gate = (S.ekind == E_RESID && mvalid) ? bf2f(a.gate[m]) : 0.0f;
+  if (S.ekind == E_RESID) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) e.pre[j] = (mvalid && j < a.N) ? bf2f(__ldcg(a.out + (long long)j * a.ldo + m)) : 0.0f;
+  } else if (S.ekind == E_QKV || S.ekind == E_QNORM) {
+    // rotary factors of the slots' positions lengths[0] + 1 + j
+    const int d = (m % a.part_rows) % a.head_dim;
+    const int base = P.lengths[0] + 1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      int pos = base + j;
+      if (pos < 0 || pos >= P.rope_len) pos = 0;  // recorded by the prep stage
+      e.pre[j] = P.rope_cos[(long long)pos * P.half + (d >> 1)];
+      e.pre[16 + j] = P.rope_sin[(long long)pos * P.half + (d >> 1)];
+    }
+  }
+}
+
 // v: the tile's fp32 sums for tokens 0..15 of row r.  Stores the outputs
 // (the arithmetic of gemm_bf16_tc's epilogues) and the tile's row statistics.
 template <int HD>
-__device__ void finish_tile(const Params& P, const Stage& S, float* v, int r, int mt, uint8_t* escr) {
+__device__ void finish_tile(const Params& P, const Stage& S, float* v, int r, int mt, uint8_t* escr, EpiPre& e) {
   const int lane = threadIdx.x & 31, q = (threadIdx.x >> 5) & 3, t = (int)threadIdx.x - 64;
   float* xch = reinterpret_cast<float*>(escr);
   unsigned long long* xch64 = reinterpret_cast<unsigned long long*>(escr + 4096);
@@ -187,14 +217,8 @@ __device__ void finish_tile(const Params& P, const Stage& S, float* v, int r, in
 #pragma unroll
   for (int j = 0; j < 16; ++j) y[j] = 0.0f;
   if (S.ekind == E_STORE || S.ekind == E_GELU || S.ekind == E_RESID) {
-    const float b = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
-    const float g = (S.ekind == E_RESID && mvalid) ? bf2f(a.gate[m]) : 0.0f;
-    float pre[16];
-    if (S.ekind == E_RESID) {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        pre[j] = (mvalid && j < a.N) ? bf2f(__ldcg(a.out + (long long)j * a.ldo + m)) : 0.0f;
-    }
+    const float b = e.bias, g = e.gate;
+    const float* pre = e.pre;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       float o = round_bf(__fadd_rn(v[j], b));
@@ -212,18 +236,7 @@ __device__ void finish_tile(const Params& P, const Stage& S, float* v, int r, in
   } else if (S.ekind == E_SWIGLU) {
     epilogue16<EPI_SWIGLU>(a, v, r, m, mt, 0, xch, xch64);
   } else if (S.ekind == E_QKV || S.ekind == E_QNORM) {
-    // rotary factors of the slots' positions lengths[0] + 1 + j
-    float pre[32];
-    const int d = (m % a.part_rows) % a.head_dim;
-    const int base = P.lengths[0] + 1;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      int pos = base + j;
-      if (pos < 0 || pos >= P.rope_len) pos = 0;  // recorded by the prep stage
-      pre[j] = P.rope_cos[(long long)pos * P.half + (d >> 1)];
-      pre[16 + j] = P.rope_sin[(long long)pos * P.half + (d >> 1)];
-    }
-    epilogue16<EPI_QKNORM>(a, v, r, m, mt, 0, xch, xch64, pre);
+    epilogue16<EPI_QKNORM>(a, v, r, m, mt, 0, xch, xch64, e.pre);
   } else if (S.ekind == E_KVCACHE) {
     a.positions = P.lengths;  // the anchor row (token 0 of sequence 0) sits at position lengths[0]
     epilogue16<EPI_KVCACHE>(a, v, r, m, mt, 0, xch, xch64);
@@ -392,7 +405,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       long long gemm_issued = 0;
       bool ok = true;
       for (int s = 0; s < n_stages && ok; ++s) {
-        const Stage& S = P.stages[s];
+        const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
         if (S.kind == K_GEMM) {
           long long u0, u1;
           stage_range(S, c, G, u0, u1);
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       uint32_t ia = 0, ib = 0, sg = 0;
       bool ok = true, any = false;
       for (int s = 0; s < n_stages && ok; ++s) {
-        const Stage& S = P.stages[s];
+        const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
         if (S.kind != K_GEMM) {
           ia += (uint32_t)stage_slots<HD>(P, S, c, G);
           continue;
@@ -524,16 +537,28 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     uint32_t ia = 0, sg = 0;
     bool ok = true;
     for (int s = 0; s < n_stages && ok; ++s) {
-      const Stage& S = P.stages[s];
+      const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
       if (S.kind == K_GEMM) {
         long long u0, u1;
         const int v = stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
+        if (u1 > u0 && S.ekind == E_RESID) {
+          // the residual rows are final once the stage's inputs are (every earlier
+          // writer of x is an ancestor of its dependency): wait before prefetching them
+          if (t == 0) flags[F_DEP] = wait_deps(P, S, cta_abort) ? 1 : 0;
+          named_bar_sync(1, 128);
+          if (!flags[F_DEP]) {
+            ok = false;
+            break;
+          }
+        }
         for (long long u = u0; u < u1;) {
           const int tile = (int)(u / kb);
           const long long sb = u, se = min((long long)(tile + 1) * kb, u1);
           u = se;
           const int acc = sg & 1;
+          EpiPre pf;
+          epi_prefetch(P, S, tile, r, pf);
           if (t == 0) flags[F_EPI] = ring_wait(P, &acc_full[acc], (sg >> 1) & 1u, cta_abort) ? 1 : 0;
           named_bar_sync(1, 128);
           if (!flags[F_EPI]) {
@@ -615,7 +640,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             }
           }
           if (!finisher) continue;
-          finish_tile<HD>(P, S, v16, r, tile, escr);
+          finish_tile<HD>(P, S, v16, r, tile, escr, pf);
           __threadfence();
           named_bar_sync(1, 128);
           if (S.ekind == E_QKV) {
@@ -748,7 +773,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       if (tb == 0) red_release_add_u64(P.done + s, 1ull);
     };
     for (int s = 0; s < n_stages && ok; ++s) {
-      const Stage& S = P.stages[s];
+      const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
       if (S.kind == K_PREP) {
         // keys reset, index checks, the anchor's embedding row
         if (c == 0) {
