@@ -19,13 +19,15 @@ constexpr int OFF_EPI = OFF_STAGE + BATCH * STAGE_SLOT;
 constexpr int OFF_BSTAT = OFF_EPI + EPI_SCRATCH;       // operand warps: [16][2] row statistics, misc
 constexpr int MAX_STAT_TILES = 40;                      // source rows of up to 40 * 128 features
 constexpr int OFF_SSTAT = OFF_BSTAT + 256;              // the producing stage's per-tile statistics
-constexpr int OFF_BAR = OFF_SSTAT + MAX_STAT_TILES * 16 * 2 * 4;
+constexpr int OFF_SDESC = OFF_SSTAT + MAX_STAT_TILES * 16 * 2 * 4;  // stage descriptors: 2 per warp group
+constexpr int OFF_BAR = OFF_SDESC + 4 * (int)sizeof(Stage);
 constexpr int N_BARS = 2 * NA + 2 * NB + 2 + 2 + 1;
 constexpr int OFF_FLAGS = OFF_BAR + N_BARS * 8;
 constexpr int SMEM_USED = OFF_FLAGS + 64;
 constexpr int SMEM_TOTAL = SMEM_USED + 1024;  // alignment slack
 static_assert(SMEM_TOTAL <= 232448, "streamed pass exceeds the shared memory of one SM");
 static_assert(OFF_B % 1024 == 0 && OFF_A % 1024 == 0, "UMMA operand rings need 1024-byte alignment");
+static_assert(sizeof(Stage) % 16 == 0 && OFF_SDESC % 16 == 0, "stage descriptors are copied as 16-byte vectors");
 
 // flags: each written by one thread of one warp group and read by the group after a barrier
 constexpr int F_ABORT = 0, F_DEP = 1, F_EPI = 2, F_TICKET = 3, F_XA = 4, F_XW = 5 /* 5, 6 */, F_BDEP = 7,
@@ -83,6 +85,14 @@ __device__ __forceinline__ bool ring_wait(const Params& P, uint64_t* bar, uint32
   if (mbar_wait(bar, parity, cta_abort)) return true;
   if (!*cta_abort) raise_abort(P, cta_abort, DEV_TIMEOUT_FULL);
   return false;
+}
+
+// A warp group's shared copy of stage s's descriptor (threads t < nthreads of
+// the group copy it; the caller's barrier publishes it).  Threads then read
+// the descriptor from shared memory instead of each holding a local copy.
+__device__ __forceinline__ void load_stage(const Params& P, int s, Stage* dst, int t, int nthreads) {
+  const uint4* src = reinterpret_cast<const uint4*>(P.stages + s);
+  for (int i = t; i < (int)(sizeof(Stage) / 16); i += nthreads) reinterpret_cast<uint4*>(dst)[i] = __ldg(src + i);
 }
 
 // CTA c's units of a stream-K split of U units over G CTAs
@@ -345,6 +355,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
   int* flags = reinterpret_cast<int*>(smem + OFF_FLAGS);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(flags + 12);
   volatile int* cta_abort = flags + F_ABORT;
+  Stage* sdesc = reinterpret_cast<Stage*>(smem + OFF_SDESC);  // [0, 1] epilogue warps, [2, 3] operand warps
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
@@ -537,7 +548,11 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     uint32_t ia = 0, sg = 0;
     bool ok = true;
     for (int s = 0; s < n_stages && ok; ++s) {
-      const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
+      // the group's shared copy of the descriptor (double-buffered: the barrier after
+      // each copy orders it after every reader of the copy two stages back)
+      load_stage(P, s, sdesc + (s & 1), t, 128);
+      named_bar_sync(1, 128);
+      const Stage& S = sdesc[s & 1];
       if (S.kind == K_GEMM) {
         long long u0, u1;
         const int v = stage_range(S, c, G, u0, u1);
@@ -773,7 +788,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       if (tb == 0) red_release_add_u64(P.done + s, 1ull);
     };
     for (int s = 0; s < n_stages && ok; ++s) {
-      const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
+      load_stage(P, s, sdesc + 2 + (s & 1), tb, 64);
+      named_bar_sync(2, 64);
+      const Stage& S = sdesc[2 + (s & 1)];
       if (S.kind == K_PREP) {
         // keys reset, index checks, the anchor's embedding row
         if (c == 0) {
