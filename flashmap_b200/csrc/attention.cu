@@ -234,7 +234,11 @@ __global__ void __launch_bounds__(128) cross_attn_kernel(const __grid_constant__
   __nv_bfloat16* outp = a.out + (long long)(b * 16) * a.hidden + h * HD;
   const bool merged = xa_finish<HD>(
       st, mrg, threadIdx.x, n_active, mine, base, sflag + 1, [] { __syncthreads(); },
-      [&] { return atomicAdd(a.counters + bh, 1) == n_active - 1; },
+      [&] {
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(a.counters + bh) : "memory");
+        return old == n_active - 1;
+      },
       [&](int i, int d, float lo, float hi) {
         *reinterpret_cast<__nv_bfloat162*>(outp + (long long)i * a.hidden + d) = __floats2bfloat162_rn(lo, hi);
       });

@@ -306,8 +306,9 @@ __host__ __device__ constexpr int xa_merge_floats() {
 // 0..127, `bar()` a barrier over them), then either write the attention of
 // the 16 rows (when this is the only split with keys) or publish this
 // split's partial (fp32 [16][HD] numerators, 16 maxima, 16 sums) at
-// `mine` and take a ticket (`ticket()`, called by t == 0, true for the last
-// split to arrive); the last split merges every split's partial in split
+// `mine` and take a ticket (`ticket()`, called by t == 0 between two barriers
+// of the group, an atomic with acquire-release semantics at GPU scope, true
+// for the last split to arrive); the last split merges every split's partial in split
 // order from `base` (stride 16*HD + 32 floats) and writes the rows.
 // store(i, d, lo, hi) writes columns d, d + 1 of row i.  Returns whether this
 // CTA wrote the rows.
@@ -378,12 +379,10 @@ __device__ __forceinline__ bool xa_finish(XaAcc<HD>& s, float* mrg, int t, int n
     __stcg(mine + 16 * HD + t, mR[t]);
     __stcg(mine + 16 * HD + 16 + t, mR[16 + t]);
   }
-  __threadfence();
   bar();
-  if (t == 0) *flag = ticket() ? 1 : 0;
+  if (t == 0) *flag = ticket() ? 1 : 0;  // an acquire-release ticket: orders the split's stores and the merge's loads
   bar();
   if (!*flag) return false;
-  __threadfence();
   // the last split of this (sequence, head): every split in split order
   float* sF = mO;  // reuse: [n_active][16] weights, then [16] l
   bar();

@@ -42,6 +42,13 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// atomic add with acquire-release semantics at GPU scope: the caller's CTA
+// barrier before it orders the group's stores, the one after it the group's loads
+__device__ __forceinline__ unsigned long long atom_add_acqrel_u64(unsigned long long* p, unsigned long long v) {
+  unsigned long long old;
+  asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+  return old;
+}
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
@@ -267,7 +274,7 @@ __device__ void finish_tile(const Params& P, const Stage& S, float* v, int r, in
       token_sums(w, xch, sums, q, lane, t);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
-        const float dd = mvalid ? __fsub_rn(y[j], __fdiv_rn(sums[j], 128.0f)) : 0.0f;
+        const float dd = mvalid ? __fsub_rn(y[j], __fmul_rn(sums[j], 0.0078125f)) : 0.0f;  // mean over 128 rows
         w[j] = __fmul_rn(dd, dd);
       }
       token_sums(w, xch, sums + 16, q, lane, t);
@@ -607,10 +614,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               __stcg(mine + j, make_float4(v16[4 * j], v16[4 * j + 1], v16[4 * j + 2], v16[4 * j + 3]));
-            __threadfence();
             named_bar_sync(1, 128);
             if (t == 0) {
-              const unsigned long long old = atomicAdd(S.tickets + tile, 1ull);
+              const unsigned long long old = atom_add_acqrel_u64(S.tickets + tile, 1ull);
               const bool last = old == (unsigned long long)(n_contrib - 1);
               if (last) S.tickets[tile] = 0ull;
               flags[F_TICKET] = last ? 1 : 0;
@@ -618,7 +624,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             named_bar_sync(1, 128);
             finisher = flags[F_TICKET] != 0;
             if (finisher) {
-              __threadfence();
               // the contributors' partials in contributor order (slot 0 when the tile holds
               // their first unit), read four contributors at a time
 #pragma unroll
@@ -656,22 +661,19 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           }
           if (!finisher) continue;
           finish_tile<HD>(P, S, v16, r, tile, escr, pf);
-          __threadfence();
           named_bar_sync(1, 128);
           if (S.ekind == E_QKV) {
             // the last of the group's q, k, v tiles runs the group's self-attention
             const int g = tile % (P.hidden / 128);
             if (t == 0) {
-              const unsigned long long old = atomicAdd(S.groups + g, 1ull);
+              const unsigned long long old = atom_add_acqrel_u64(S.groups + g, 1ull);
               const bool last = old == 2ull;
               if (last) S.groups[g] = 0ull;
               flags[F_TICKET] = last ? 1 : 0;
             }
             named_bar_sync(1, 128);
             if (!flags[F_TICKET]) continue;
-            __threadfence();
             group_attention<HD>(P, S, g, escr);
-            __threadfence();
             named_bar_sync(1, 128);
           }
           if (t == 0) red_release_add_u64(P.done + s, 1ull);
@@ -738,7 +740,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
               acc, reinterpret_cast<float*>(escr), t, n_active, mine, base, flags + F_XA,
               [] { named_bar_sync(1, 128); },
               [&] {
-                const unsigned long long old = atomicAdd(xt, 1ull);
+                const unsigned long long old = atom_add_acqrel_u64(xt, 1ull);
                 const bool last = old == (unsigned long long)(n_active - 1);
                 if (last) *xt = 0ull;
                 return last;
@@ -747,7 +749,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
                 *reinterpret_cast<__nv_bfloat162*>(outp + (long long)i * P.hidden + d) = __floats2bfloat162_rn(lo, hi);
               });
           if (merged) {
-            __threadfence();
             named_bar_sync(1, 128);
             if (t == 0) red_release_add_u64(P.done + s, 1ull);
           }
@@ -783,7 +784,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       return *f != 0;
     };
     auto finish_piece = [&](int s) {
-      __threadfence();
       named_bar_sync(2, 64);
       if (tb == 0) red_release_add_u64(P.done + s, 1ull);
     };
@@ -889,41 +889,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         }
         continue;
       }
-      // transforms: the producing stage's per-tile statistics into shared memory
-      // (one round trip), combined per token in tile order
-      for (int k = tb; k < S.stats_tiles * 8; k += 64)
-        cp16(sstat + k * 4, S.stats_in + k * 4, true);
-      cp_commit();
-      cp_wait<0>();
-      named_bar_sync(2, 64);
-      if (tb < 16) {
-        if (S.bkind == B_ADALN) {
-          // Chan's combination of the tiles' (sum, sum of squared deviations), 128 rows each
-          float tot = 0.0f;
-          for (int i = 0; i < S.stats_tiles; ++i) tot = __fadd_rn(tot, sstat[(i * 16 + tb) * 2]);
-          const float mean = __fdiv_rn(tot, (float)K);
-          float m2 = 0.0f;
-          for (int i = 0; i < S.stats_tiles; ++i) {
-            const float dm = __fsub_rn(__fdiv_rn(sstat[(i * 16 + tb) * 2], 128.0f), mean);
-            m2 = __fadd_rn(m2, __fadd_rn(sstat[(i * 16 + tb) * 2 + 1], __fmul_rn(128.0f, __fmul_rn(dm, dm))));
-          }
-          bstat[tb * 2] = mean;
-          bstat[tb * 2 + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(m2, (float)K), S.eps)));
-        } else {
-          float ss = 0.0f;
-          for (int i = 0; i < S.stats_tiles; ++i) ss = __fadd_rn(ss, sstat[(i * 16 + tb) * 2]);
-          bstat[tb * 2] = inv_rms(ss, K, S.eps);
-        }
-      }
-      if (S.bkind == B_MIX && tb >= 32) {
-        // the uniform posterior row's RMS (a constant row)
-        const float ssu = warp_row_sumsq_batched(S.aux, K, lane);
-        if (lane == 0) bstat[32] = inv_rms(ssu, K, S.eps);
-      }
-      named_bar_sync(2, 64);
-      // raw rows and constant rows of up to BATCH blocks staged, then the operand computed
-      for (long long ub = u0; ub < u1 && ok; ub += BATCH) {
-        const int nb = (int)min((long long)BATCH, u1 - ub);
+      // transforms: the producing stage's per-tile statistics and the first batch's
+      // rows staged in one round trip; the statistics combined per token in tile order
+      auto stage_batch = [&](long long ub, int nb) {
         for (int j = 0; j < nb; ++j) {
           const int kk = (int)((ub + j) % kb);
           uint8_t* st = sStage + j * STAGE_SLOT;
@@ -945,15 +913,56 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             cp16(st + B_BYTES + row * 128 + ch * 16, valid ? (const void*)(src + k0) : (const void*)S.src, valid);
           }
         }
-        cp_commit();
-        cp_wait<0>();
-        named_bar_sync(2, 64);
-        for (int j = 0; j < nb; ++j) {
-          const int slot = ib % NB;
-          if (ib >= NB && !slot_free(slot, ((ib / NB) - 1) & 1u)) {
-            ok = false;
-            break;
+      };
+      for (int k = tb; k < S.stats_tiles * 8; k += 64) cp16(sstat + k * 4, S.stats_in + k * 4, true);
+      stage_batch(u0, (int)min((long long)BATCH, u1 - u0));
+      cp_commit();
+      cp_wait<0>();
+      named_bar_sync(2, 64);
+      if (tb < 16) {
+        if (S.bkind == B_ADALN) {
+          // Chan's combination of the tiles' (sum, sum of squared deviations), 128 rows each
+          float tot = 0.0f;
+          for (int i = 0; i < S.stats_tiles; ++i) tot = __fadd_rn(tot, sstat[(i * 16 + tb) * 2]);
+          const float mean = __fdiv_rn(tot, (float)K);
+          float m2 = 0.0f;
+          for (int i = 0; i < S.stats_tiles; ++i) {
+            const float dm = __fsub_rn(__fmul_rn(sstat[(i * 16 + tb) * 2], 0.0078125f), mean);  // tile mean - mean
+            m2 = __fadd_rn(m2, __fadd_rn(sstat[(i * 16 + tb) * 2 + 1], __fmul_rn(128.0f, __fmul_rn(dm, dm))));
           }
+          bstat[tb * 2] = mean;
+          bstat[tb * 2 + 1] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(m2, (float)K), S.eps)));
+        } else {
+          float ss = 0.0f;
+          for (int i = 0; i < S.stats_tiles; ++i) ss = __fadd_rn(ss, sstat[(i * 16 + tb) * 2]);
+          bstat[tb * 2] = inv_rms(ss, K, S.eps);
+        }
+      }
+      if (S.bkind == B_MIX && tb >= 32) {
+        // the uniform posterior row's RMS (a constant row)
+        const float ssu = warp_row_sumsq_batched(S.aux, K, lane);
+        if (lane == 0) bstat[32] = inv_rms(ssu, K, S.eps);
+      }
+      named_bar_sync(2, 64);
+      // per batch: the operand blocks computed from the staged rows, one proxy fence,
+      // then the blocks handed to the MMA
+      for (long long ub = u0; ub < u1 && ok; ub += BATCH) {
+        const int nb = (int)min((long long)BATCH, u1 - ub);
+        if (ub != u0) {
+          stage_batch(ub, nb);
+          cp_commit();
+          cp_wait<0>();
+          named_bar_sync(2, 64);
+        }
+        // the batch's slots are free once the MMA has consumed the block NB before
+        // its last one (the MMA consumes in order)
+        const uint32_t last = ib + (uint32_t)nb - 1;
+        if (last >= NB && !slot_free(last % NB, ((last / NB) - 1) & 1u)) {
+          ok = false;
+          break;
+        }
+        for (int j = 0; j < nb; ++j) {
+          const int slot = (ib + j) % NB;
           const int kk = (int)((ub + j) % kb);
           const uint8_t* st = sStage + j * STAGE_SLOT;
           uint8_t* dst = sB + slot * B_BYTES;
@@ -985,11 +994,12 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             }
             *reinterpret_cast<uint4*>(dst + b_off(n, ch)) = o;
           }
-          fence_proxy_async_smem();
-          named_bar_sync(2, 64);
-          if (tb == 0) mbar_arrive(&bfull[slot]);
-          ++ib;
         }
+        fence_proxy_async_smem();
+        named_bar_sync(2, 64);
+        if (tb == 0)
+          for (int j = 0; j < nb; ++j) mbar_arrive(&bfull[(ib + j) % NB]);
+        ib += (uint32_t)nb;
         named_bar_sync(2, 64);  // the staging slots are refilled by the next round
       }
     }
