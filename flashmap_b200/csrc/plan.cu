@@ -368,6 +368,8 @@ fm_status build_stream(fm_plan* p) {
     int64_t vg = std::min<int64_t>(G, (int64_t)g.args.m_tiles * 4);
     vg = std::max<int64_t>(vg, std::min<int64_t>(G, (bytes + (256 << 10) - 1) >> 18));
     vg = std::min<int64_t>(vg, units);
+    // a transform stage stages the constant rows of all of a CTA's units at once
+    if (bkind != B_COPY) vg = std::max<int64_t>(vg, (units + MAX_TRANSFORM_UNITS - 1) / MAX_TRANSFORM_UNITS);
     S.vg = (int)vg;
     S.rot = rot;
     rot = (int)((rot + vg) % G);
@@ -540,6 +542,8 @@ fm_status build_stream(fm_plan* p) {
     if (S.bkind == B_ADALN && (S.ep.K % 128 || S.stats_tiles * 128 != S.ep.K))
       return fail("AdaLN rows must be whole 128-feature tiles");
     if (S.bkind != B_COPY && S.stats_tiles > 40) return fail("source rows wider than 40 tiles of 128");
+    if (S.bkind != B_COPY && (S.vg > G || (S.ep.units + S.vg - 1) / S.vg > MAX_TRANSFORM_UNITS))
+      return fail("a transform stage with more units per CTA than its constant staging holds");
     if (S.bkind == B_COPY && S.bmap < 0) return fail("a copied operand without its tensor map");
   }
   if (D % 128) return fail("hidden must be a multiple of 128");

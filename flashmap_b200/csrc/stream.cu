@@ -15,7 +15,8 @@ constexpr int EPI_SCRATCH = 34 * 1024;  // epilogue / attention warps: exchange 
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + NA * A_BYTES;
 constexpr int OFF_STAGE = OFF_B + NB * B_BYTES;
-constexpr int OFF_EPI = OFF_STAGE + BATCH * STAGE_SLOT;
+constexpr int OFF_CONST = OFF_STAGE + BATCH * STAGE_SLOT;  // constant rows of a transform stage's units
+constexpr int OFF_EPI = OFF_CONST + MAX_TRANSFORM_UNITS * CONST_SLOT;
 constexpr int OFF_BSTAT = OFF_EPI + EPI_SCRATCH;       // operand warps: [16][2] row statistics, misc
 constexpr int MAX_STAT_TILES = 40;                      // source rows of up to 40 * 128 features
 constexpr int OFF_SSTAT = OFF_BSTAT + 256;              // the producing stage's per-tile statistics
@@ -193,19 +194,29 @@ __device__ __forceinline__ void token_sums(float* val, float* xch, float* out, i
 // gate, the residual rows, the rotary factors), loaded before the tile's
 // accumulator is ready so that finishing the tile takes no extra round trip.
 struct EpiPre {
-  float bias, gate;
+  float bias, gate, warm;
   float pre[32];
 };
-__device__ __forceinline__ void epi_prefetch(const Params& P, const Stage& S, int mt, int r, EpiPre& e) {
+// the tile's constants: bias, gate, rotary factors, and a touch of the norm
+// weight and column ids the fused epilogue reads (so they sit in L1)
+__device__ __forceinline__ void epi_constants(const Params& P, const Stage& S, int mt, int r, EpiPre& e) {
   const GemmArgs& a = S.ep;
   const int m = mt * 128 + r;
   const bool mvalid = m < a.M;
   e.bias = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
   e.gate = (S.ekind == E_RESID && mvalid) ? bf2f(a.gate[m]) : 0.0f;
-  if (S.ekind == E_RESID) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) e.pre[j] = (mvalid && j < a.N) ? bf2f(__ldcg(a.out + (long long)j * a.ldo + m)) : 0.0f;
-  } else if (S.ekind == E_QKV || S.ekind == E_QNORM) {
+  e.warm = 0.0f;
+  if (S.ekind == E_QKV || S.ekind == E_QNORM || S.ekind == E_KVCACHE) {
+    const int part = (mt * 128) / a.part_rows;
+    const int d = (m % a.part_rows) % a.head_dim;
+    const __nv_bfloat16* w = S.ekind == E_KVCACHE ? a.norm_w0 + (long long)((mt * 128) / (2 * a.part_rows)) *
+                                                                    a.norm_layer_stride
+                                                  : (part == 0 ? a.norm_w0 : a.norm_w1);
+    if (w != nullptr && part < 2) e.warm = bf2f(w[d]);
+  } else if (S.ekind == E_LOGITS && a.col_ids && mvalid) {
+    e.warm = (float)a.col_ids[m];
+  }
+  if (S.ekind == E_QKV || S.ekind == E_QNORM) {
     // rotary factors of the slots' positions lengths[0] + 1 + j
     const int d = (m % a.part_rows) % a.head_dim;
     const int base = P.lengths[0] + 1;
@@ -217,6 +228,14 @@ __device__ __forceinline__ void epi_prefetch(const Params& P, const Stage& S, in
       e.pre[16 + j] = P.rope_sin[(long long)pos * P.half + (d >> 1)];
     }
   }
+}
+// the residual rows (E_RESID), final once the stage's inputs are
+__device__ __forceinline__ void epi_residual(const Stage& S, int mt, int r, EpiPre& e) {
+  const GemmArgs& a = S.ep;
+  const int m = mt * 128 + r;
+  const bool mvalid = m < a.M;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) e.pre[j] = (mvalid && j < a.N) ? bf2f(__ldcg(a.out + (long long)j * a.ldo + m)) : 0.0f;
 }
 
 // v: the tile's fp32 sums for tokens 0..15 of row r.  Stores the outputs
@@ -564,9 +583,12 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         long long u0, u1;
         const int v = stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
+        // the first segment's constants are loaded before any wait: their latency hides under it
+        EpiPre pf;
+        if (u1 > u0) epi_constants(P, S, (int)(u0 / kb), r, pf);
         if (u1 > u0 && S.ekind == E_RESID) {
           // the residual rows are final once the stage's inputs are (every earlier
-          // writer of x is an ancestor of its dependency): wait before prefetching them
+          // writer of x is an ancestor of its dependency): wait before reading them
           if (t == 0) flags[F_DEP] = wait_deps(P, S, cta_abort) ? 1 : 0;
           named_bar_sync(1, 128);
           if (!flags[F_DEP]) {
@@ -579,8 +601,8 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           const long long sb = u, se = min((long long)(tile + 1) * kb, u1);
           u = se;
           const int acc = sg & 1;
-          EpiPre pf;
-          epi_prefetch(P, S, tile, r, pf);
+          if (sb != u0) epi_constants(P, S, tile, r, pf);
+          if (S.ekind == E_RESID) epi_residual(S, tile, r, pf);
           if (t == 0) flags[F_EPI] = ring_wait(P, &acc_full[acc], (sg >> 1) & 1u, cta_abort) ? 1 : 0;
           named_bar_sync(1, 128);
           if (!flags[F_EPI]) {
@@ -774,6 +796,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     bool ok = true;
     const uint32_t noise_off = P.offset + bump;
     float* sstat = reinterpret_cast<float*>(smem + OFF_SSTAT);
+    uint8_t* sConst = smem + OFF_CONST;
     // the operand slot `slot` free again: one thread waits (bounded) and the group
     // reads the outcome (alternating flags, as for the attention tiles)
     uint32_t nwait = 0;
@@ -855,6 +878,27 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       long long u0, u1;
       stage_range(S, c, G, u0, u1);
       if (u1 <= u0) continue;
+      if (S.bkind != B_COPY) {
+        // the constant rows of every unit ([scale, shift] of an AdaLN, [uniform posterior,
+        // state_norm, noise_norm] of mix_state) staged before the wait: they do not depend
+        // on the stage's inputs, and their HBM latency hides under the wait
+        for (int k = tb; k < (int)(u1 - u0) * 24; k += 64) {
+          const int j = k / 24, row = (k % 24) >> 3, ch = k & 7;
+          const int kk = (int)((u0 + j) % S.ep.kb);
+          const int k0 = kk * 64 + ch * 8;
+          const bf16* src = S.bkind == B_ADALN ? (row == 0 ? S.mod : row == 1 ? S.mod + S.ep.K : nullptr)
+                                               : (row == 0 ? S.aux : row == 1 ? S.w0 : S.w1);
+          const bool valid = src != nullptr && k0 < S.ep.K;
+          cp16(sConst + j * CONST_SLOT + row * 128 + ch * 16, valid ? (const void*)(src + k0) : (const void*)S.src,
+               valid);
+        }
+        cp_commit();
+        if (S.bkind == B_MIX && tb >= 32) {
+          // the uniform posterior row's RMS (a constant row)
+          const float ssu = warp_row_sumsq_batched(S.aux, S.ep.K, lane);
+          if (lane == 0) bstat[32] = inv_rms(ssu, S.ep.K, S.eps);
+        }
+      }
       if (tb == 0) flags[F_BDEP] = wait_deps(P, S, cta_abort) ? 1 : 0;
       named_bar_sync(2, 64);
       if (!flags[F_BDEP]) {
@@ -890,7 +934,8 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         continue;
       }
       // transforms: the producing stage's per-tile statistics and the first batch's
-      // rows staged in one round trip; the statistics combined per token in tile order
+      // source rows staged in one round trip (the constant rows were staged on entry,
+      // before the dependency wait); the statistics combined per token in tile order
       auto stage_batch = [&](long long ub, int nb) {
         for (int j = 0; j < nb; ++j) {
           const int kk = (int)((ub + j) % kb);
@@ -902,15 +947,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             const bool valid = k0 < K;
             cp16(st + n * 128 + ch * 16, valid ? (const void*)(S.src + (long long)n * S.ld + k0) : (const void*)S.src,
                  valid);
-          }
-          // constant rows: [scale, shift] (AdaLN) or [uniform, state_norm, noise_norm] (mix_state)
-          if (tb < 24) {
-            const int row = tb >> 3, ch = tb & 7;
-            const int k0 = kk * 64 + ch * 8;
-            const bf16* src = S.bkind == B_ADALN ? (row == 0 ? S.mod : row == 1 ? S.mod + K : nullptr)
-                                                 : (row == 0 ? S.aux : row == 1 ? S.w0 : S.w1);
-            const bool valid = src != nullptr && k0 < K;
-            cp16(st + B_BYTES + row * 128 + ch * 16, valid ? (const void*)(src + k0) : (const void*)S.src, valid);
           }
         }
       };
@@ -938,11 +974,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           bstat[tb * 2] = inv_rms(ss, K, S.eps);
         }
       }
-      if (S.bkind == B_MIX && tb >= 32) {
-        // the uniform posterior row's RMS (a constant row)
-        const float ssu = warp_row_sumsq_batched(S.aux, K, lane);
-        if (lane == 0) bstat[32] = inv_rms(ssu, K, S.eps);
-      }
       named_bar_sync(2, 64);
       // per batch: the operand blocks computed from the staged rows, one proxy fence,
       // then the blocks handed to the MMA
@@ -965,6 +996,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           const int slot = (ib + j) % NB;
           const int kk = (int)((ub + j) % kb);
           const uint8_t* st = sStage + j * STAGE_SLOT;
+          const uint8_t* cst = sConst + (int)(ub + j - u0) * CONST_SLOT;
           uint8_t* dst = sB + slot * B_BYTES;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
@@ -976,16 +1008,16 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
               unpack_bf16x8(*reinterpret_cast<const uint4*>(st + n * 128 + ch * 16), x);
               if (S.bkind == B_ADALN) {
                 float sc[8], sh[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), sc);
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sh);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(cst + ch * 16), sc);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(cst + 128 + ch * 16), sh);
                 const float mean = bstat[n * 2], rstd = bstat[n * 2 + 1];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) y[e] = adaln_value(x[e], mean, rstd, sc[e], sh[e]);
               } else {
                 float pu[8], sw[8], nw[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + ch * 16), pu);
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 128 + ch * 16), sw);
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(st + B_BYTES + 256 + ch * 16), nw);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(cst + ch * 16), pu);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(cst + 128 + ch * 16), sw);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(cst + 256 + ch * 16), nw);
                 const float ip = bstat[32], is = bstat[n * 2];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) y[e] = mix_value(pu[e], x[e], sw[e], nw[e], ip, is, S.gate);

@@ -49,8 +49,10 @@ constexpr int NA = 8;                     // weight ring slots
 constexpr int A_BYTES = 128 * 64 * 2;     // one 128 x 64 weight tile
 constexpr int NB = 16;                    // operand ring slots
 constexpr int B_BYTES = 16 * 64 * 2;      // one 16 x 64 operand block
-constexpr int BATCH = 10;                 // operand blocks staged per round for a transform
-constexpr int STAGE_SLOT = B_BYTES + 3 * 128;  // staged rows of one block + up to three constant rows
+constexpr int BATCH = 8;                  // operand blocks whose source rows are staged per round
+constexpr int STAGE_SLOT = B_BYTES;       // the 16 source rows of one block
+constexpr int MAX_TRANSFORM_UNITS = 16;   // units per CTA of a transform stage (their constant rows staged at once)
+constexpr int CONST_SLOT = 3 * 128;       // up to three constant rows of one block
 constexpr int MAX_MAPS = 112;
 
 enum Kind : int { K_PREP = 0, K_GEMM = 1, K_XATTN = 2, K_FINAL = 3, K_NOISE = 4, K_ANORM = 5 };
