@@ -542,6 +542,8 @@ fm_status build_stream(fm_plan* p) {
     if (S.bkind == B_ADALN && (S.ep.K % 128 || S.stats_tiles * 128 != S.ep.K))
       return fail("AdaLN rows must be whole 128-feature tiles");
     if (S.bkind != B_COPY && S.stats_tiles > 40) return fail("source rows wider than 40 tiles of 128");
+    if (S.kind == K_GEMM && S.ep.units * (int64_t)G >= (int64_t(1) << 31))
+      return fail("a GEMM stage of more units than the 32-bit split arithmetic holds");
     if (S.bkind != B_COPY && (S.vg > G || (S.ep.units + S.vg - 1) / S.vg > MAX_TRANSFORM_UNITS))
       return fail("a transform stage with more units per CTA than its constant staging holds");
     if (S.bkind == B_COPY && S.bmap < 0) return fail("a copied operand without its tensor map");
@@ -560,11 +562,6 @@ fm_status build_stream(fm_plan* p) {
   P->all_tickets = p->st_tickets;
   P->n_tickets = tk_used;
   P->err = p->err;
-  {
-    const char* e = getenv("FM_STREAM_PF");
-    const int v = e ? atoi(e) : 12;
-    P->pf = v >= 0 && v <= 256 ? v : 12;
-  }
   P->keys = p->keys;
   P->lm_stage = s_lm;
   P->rope_cos = m.rope_cos;

@@ -103,23 +103,29 @@ __device__ __forceinline__ void load_stage(const Params& P, int s, Stage* dst, i
   for (int i = t; i < (int)(sizeof(Stage) / 16); i += nthreads) reinterpret_cast<uint4*>(dst)[i] = __ldg(src + i);
 }
 
-// CTA c's units of a stream-K split of U units over G CTAs
-__device__ __forceinline__ void unit_range(long long U, int G, int c, long long& u0, long long& u1) {
-  u0 = (long long)c * U / G;
-  u1 = (long long)(c + 1) * U / G;
+// CTA c's units of a stream-K split of U units over G CTAs (32-bit: the host
+// checks U * G < 2^31, so the products and quotients stay in range)
+__device__ __forceinline__ int split_at(int U, int G, int c) { return (int)((uint32_t)c * (uint32_t)U / (uint32_t)G); }
+__device__ __forceinline__ void unit_range(int U, int G, int c, int& u0, int& u1) {
+  u0 = split_at(U, G, c);
+  u1 = split_at(U, G, c + 1);
+}
+// the CTA of a split whose range holds unit u
+__device__ __forceinline__ int cta_of(int u, int U, int G) {
+  return (int)(((uint32_t)u * (uint32_t)G + (uint32_t)G - 1u) / (uint32_t)U);
 }
 // the virtual CTA of CTA c in a GEMM stage (-1: none) and its units
 __device__ __forceinline__ int stage_vcta(const Stage& S, int c, int G) {
   const int v = (c - S.rot % G + G) % G;
   return v < S.vg ? v : -1;
 }
-__device__ __forceinline__ int stage_range(const Stage& S, int c, int G, long long& u0, long long& u1) {
+__device__ __forceinline__ int stage_range(const Stage& S, int c, int G, int& u0, int& u1) {
   const int v = stage_vcta(S, c, G);
   if (v < 0) {
     u0 = u1 = 0;
     return -1;
   }
-  unit_range(S.ep.units, S.vg, v, u0, u1);
+  unit_range((int)S.ep.units, S.vg, v, u0, u1);
   return v;
 }
 
@@ -149,17 +155,17 @@ __host__ __device__ constexpr int xa_slots() {
 
 // slots this CTA takes from the weight ring in stage S
 template <int HD>
-__device__ long long stage_slots(const Params& P, const Stage& S, int c, int G) {
+__device__ int stage_slots(const Params& P, const Stage& S, int c, int G) {
   if (S.kind == K_GEMM) {
-    long long u0, u1;
+    int u0, u1;
     stage_range(S, c, G, u0, u1);
     return u1 - u0;
   }
   if (S.kind == K_XATTN) {
-    long long n = 0;
+    int n = 0;
     XaItem x;
     for (int it = c; it < P.heads * S.nsplit; it += G)
-      if (xa_item(P, S, it, x)) n += (long long)x.ntiles * xa_slots<HD>();
+      if (xa_item(P, S, it, x)) n += x.ntiles * xa_slots<HD>();
     return n;
   }
   return 0;
@@ -419,36 +425,15 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       uint32_t ia = 0;
-      // L2 prefetch cursor over this CTA's weight tiles, P.pf tiles ahead of the ring
-      int ps = 0;
-      long long pu = 0, pu1 = 0, issued_pf = 0;
-      bool pf_started = false;
-      auto pf_advance = [&](long long upto) {
-        while (issued_pf < upto) {
-          while (pu >= pu1) {
-            if (pf_started) ++ps;
-            pf_started = true;
-            if (ps >= n_stages) return;
-            const Stage& Q = P.stages[ps];
-            if (Q.kind == K_GEMM) stage_range(Q, c, G, pu, pu1);
-            else pu = pu1 = 0;
-          }
-          const Stage& Q = P.stages[ps];
-          tma_prefetch_l2_2d(&P.maps[Q.map], (int)(pu % Q.ep.kb) * 64, (int)(pu / Q.ep.kb) * 128);
-          ++pu;
-          ++issued_pf;
-        }
-      };
-      long long gemm_issued = 0;
       bool ok = true;
       for (int s = 0; s < n_stages && ok; ++s) {
         const Stage S = P.stages[s];  // a local copy: its fields are read without a global round trip
         if (S.kind == K_GEMM) {
-          long long u0, u1;
+          int u0, u1;
           stage_range(S, c, G, u0, u1);
           const CUtensorMap* map = &P.maps[S.map];
-          for (long long u = u0; u < u1; ++u) {
-            if (P.pf > 0) pf_advance(gemm_issued + P.pf);
+          if (u1 > u0) tma_prefetch_desc(map);
+          for (int u = u0; u < u1; ++u) {
             const int slot = ia % NA;
             if (ia >= NA && !ring_wait(P, &empty[slot], ((ia / NA) - 1) & 1u, cta_abort)) {
               ok = false;
@@ -458,7 +443,6 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             tma_load_2d_hint(sA + slot * A_BYTES, map, &full[slot], (int)(u % S.ep.kb) * 64, (int)(u / S.ep.kb) * 128,
                              pol);
             ++ia;
-            ++gemm_issued;
           }
         } else if (S.kind == K_XATTN) {
           constexpr int TB = XA_TILE * HD * 2;  // bytes of K (or V) of one tile
@@ -525,12 +509,12 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           ia += (uint32_t)stage_slots<HD>(P, S, c, G);
           continue;
         }
-        long long u0, u1;
+        int u0, u1;
         stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
-        for (long long u = u0; u < u1 && ok;) {
-          const int tile = (int)(u / kb);
-          const long long sb = u, se = min((long long)(tile + 1) * kb, u1);
+        for (int u = u0; u < u1 && ok;) {
+          const int tile = u / kb;
+          const int sb = u, se = min((tile + 1) * kb, u1);
           const int acc = sg & 1;
           if (sg >= 2 && !ring_wait(P, &acc_empty[acc], ((sg >> 1) - 1) & 1u, cta_abort)) {
             ok = false;
@@ -580,12 +564,12 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       named_bar_sync(1, 128);
       const Stage& S = sdesc[s & 1];
       if (S.kind == K_GEMM) {
-        long long u0, u1;
+        int u0, u1;
         const int v = stage_range(S, c, G, u0, u1);
         const int kb = S.ep.kb;
         // the first segment's constants are loaded before any wait: their latency hides under it
         EpiPre pf;
-        if (u1 > u0) epi_constants(P, S, (int)(u0 / kb), r, pf);
+        if (u1 > u0) epi_constants(P, S, u0 / kb, r, pf);
         if (u1 > u0 && S.ekind == E_RESID) {
           // the residual rows are final once the stage's inputs are (every earlier
           // writer of x is an ancestor of its dependency): wait before reading them
@@ -596,9 +580,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             break;
           }
         }
-        for (long long u = u0; u < u1;) {
-          const int tile = (int)(u / kb);
-          const long long sb = u, se = min((long long)(tile + 1) * kb, u1);
+        for (int u = u0; u < u1;) {
+          const int tile = u / kb;
+          const int sb = u, se = min((tile + 1) * kb, u1);
           u = se;
           const int acc = sg & 1;
           if (sb != u0) epi_constants(P, S, tile, r, pf);
@@ -617,20 +601,23 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[acc]);
           ++sg;
-          const bool whole = sb == (long long)tile * kb && se == (long long)(tile + 1) * kb;
+          const bool whole = sb == tile * kb && se == (tile + 1) * kb;
           bool finisher = whole;
           if (!whole) {
             // publish this CTA's partial (row r's 16 tokens contiguous); the last
             // contributor to arrive finishes the tile
-            const long long U = S.ep.units;
+            const int U = (int)S.ep.units;
             const int vg = S.vg;
-            const int c_first = (int)cta_of_unit((long long)tile * kb, U, vg);
-            const int c_last = (int)cta_of_unit((long long)(tile + 1) * kb - 1, U, vg);
+            const int c_first = cta_of(tile * kb, U, vg);
+            const int c_last = cta_of((tile + 1) * kb - 1, U, vg);
             // virtual CTAs between c_first and c_last without units (a stage of fewer
             // units than virtual CTAs) contribute nothing
             int n_contrib = 0;
-            for (int cc = c_first; cc <= c_last; ++cc)
-              n_contrib += (long long)(cc + 1) * U / vg > (long long)cc * U / vg ? 1 : 0;
+            for (int cc = c_first, a0 = split_at(U, vg, c_first); cc <= c_last; ++cc) {
+              const int a1 = split_at(U, vg, cc + 1);
+              n_contrib += a1 > a0 ? 1 : 0;
+              a0 = a1;
+            }
             const int slot = sb == u0 ? 0 : 1;
             float4* mine = reinterpret_cast<float4*>(S.ws + ((long long)(v * 2 + slot) * 128 + r) * 16);
 #pragma unroll
@@ -655,9 +642,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
                 float4 pv[4][4];
                 int n = 0, who[4];
                 for (; cc <= c_last && n < 4; ++cc) {
-                  const long long cu0 = (long long)cc * U / vg;
-                  if ((long long)(cc + 1) * U / vg <= cu0) continue;  // no units of this stage
-                  const int cs = cu0 >= (long long)tile * kb ? 0 : 1;
+                  const int cu0 = split_at(U, vg, cc);
+                  if (split_at(U, vg, cc + 1) <= cu0) continue;  // no units of this stage
+                  const int cs = cu0 >= tile * kb ? 0 : 1;
                   who[n++] = cc * 2 + cs;
                 }
 #pragma unroll
@@ -875,16 +862,19 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         continue;
       }
       if (S.kind != K_GEMM) continue;
-      long long u0, u1;
+      int u0, u1;
       stage_range(S, c, G, u0, u1);
       if (u1 <= u0) continue;
+      // the operand's tensor map fetched before the wait (its first use would otherwise
+      // fetch the descriptor on the critical path)
+      if (S.bkind == B_COPY && tb == 0) tma_prefetch_desc(&P.maps[S.bmap]);
       if (S.bkind != B_COPY) {
         // the constant rows of every unit ([scale, shift] of an AdaLN, [uniform posterior,
         // state_norm, noise_norm] of mix_state) staged before the wait: they do not depend
         // on the stage's inputs, and their HBM latency hides under the wait
-        for (int k = tb; k < (int)(u1 - u0) * 24; k += 64) {
+        for (int k = tb; k < (u1 - u0) * 24; k += 64) {
           const int j = k / 24, row = (k % 24) >> 3, ch = k & 7;
-          const int kk = (int)((u0 + j) % S.ep.kb);
+          const int kk = (u0 + j) % S.ep.kb;
           const int k0 = kk * 64 + ch * 8;
           const bf16* src = S.bkind == B_ADALN ? (row == 0 ? S.mod : row == 1 ? S.mod + S.ep.K : nullptr)
                                                : (row == 0 ? S.aux : row == 1 ? S.w0 : S.w1);
@@ -913,7 +903,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           fence_proxy_async_global();  // rows written by other CTAs' epilogues, read by TMA
           const CUtensorMap* map = &P.maps[S.bmap];
           bool good = true;
-          for (long long u = u0; u < u1; ++u) {
+          for (int u = u0; u < u1; ++u) {
             const int slot = ib % NB;
             if (ib >= NB && !ring_wait(P, &bempty[slot], ((ib / NB) - 1) & 1u, cta_abort)) {
               good = false;
@@ -936,9 +926,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       // transforms: the producing stage's per-tile statistics and the first batch's
       // source rows staged in one round trip (the constant rows were staged on entry,
       // before the dependency wait); the statistics combined per token in tile order
-      auto stage_batch = [&](long long ub, int nb) {
+      auto stage_batch = [&](int ub, int nb) {
         for (int j = 0; j < nb; ++j) {
-          const int kk = (int)((ub + j) % kb);
+          const int kk = (ub + j) % kb;
           uint8_t* st = sStage + j * STAGE_SLOT;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
@@ -951,7 +941,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         }
       };
       for (int k = tb; k < S.stats_tiles * 8; k += 64) cp16(sstat + k * 4, S.stats_in + k * 4, true);
-      stage_batch(u0, (int)min((long long)BATCH, u1 - u0));
+      stage_batch(u0, min(BATCH, u1 - u0));
       cp_commit();
       cp_wait<0>();
       named_bar_sync(2, 64);
@@ -977,8 +967,8 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       named_bar_sync(2, 64);
       // per batch: the operand blocks computed from the staged rows, one proxy fence,
       // then the blocks handed to the MMA
-      for (long long ub = u0; ub < u1 && ok; ub += BATCH) {
-        const int nb = (int)min((long long)BATCH, u1 - ub);
+      for (int ub = u0; ub < u1 && ok; ub += BATCH) {
+        const int nb = min(BATCH, u1 - ub);
         if (ub != u0) {
           stage_batch(ub, nb);
           cp_commit();

@@ -62,7 +62,7 @@ enum EKind : int { E_STORE = 0, E_GELU = 1, E_SWIGLU = 2, E_RESID = 3, E_QKV = 4
                    E_LOGITS = 7 };
 enum Stats : int { S_NONE = 0, S_LN = 1, S_SQ = 2 };
 
-struct Stage {
+struct alignas(16) Stage {
   int kind;
   int dep, dep2;     // stages whose completion this stage's inputs need (-1: none)
   int pieces;        // completion count of this stage per draft
@@ -108,7 +108,6 @@ struct Params {
   unsigned long long* all_tickets;  // every ticket of the pass (zeroed after an abort)
   long long n_tickets;
   int* err;
-  int pf;                      // weight tiles requested into L2 ahead of the ring
   // per call
   const int64_t* anchor_ids;
   const int32_t* lengths;
