@@ -1,26 +1,33 @@
 #!/usr/bin/env python
 """Benchmark of the FlashMap drafter hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload all|...]
 
-A step is one draft pass (modeling_flashmap.py:422-479) of the BASELINE
-config-2 drafter: Qwen3-8B sizing (hidden 2048, 8 DiT layers, 16 heads x 128,
-GELU 8192, K = 16 slots, LM head over V = 151936 rows of 4096), batch 1, a
-2048-position context, one jump.  Weights are seeded random-init (no
-checkpoint on the box), conditioning states N(0, 1).
+The default line (``--workload all``) measures BASELINE config 5, the
+workload quoted "at 1/2/4/8 B200": 512 requests of the Qwen3.8-27B-sized
+drafter (hidden 2560, 10 DiT layers, SwiGLU 6912, a 32768-token state
+vocabulary of 248320), contexts U[1024, 8192], K = 16, one jump.  Requests
+are sharded over the N ranks by longest-processing-time on context length
+with equal counts per rank (flashmap_b200.sharding); every rank drafts its
+share in chunks of <= 64 with its own weight replica and no collective on the
+data path.  A step drafts all 512 requests once: per chunk, W warm-up and K
+timed replays of the CUDA-graph-captured pass (CUDA events, a barrier
+before), summed over the rank's chunks, the maximum over ranks.  ``value`` is
+512 x 16 drafted tokens / step time (strong scaling: the work is fixed as N
+grows); ``e2e`` is the same through DraftSession.draft with anchors copied
+from pinned host memory and tokens copied back on every call.  Each chunk
+streams ~3 GB of context K/V per pass, more than the 126 MB L2.
 
-Timing: K replays of the CUDA-graph-captured pass, bracketed by a barrier and
-a device synchronise on both sides, CUDA events on the replay stream, the
-maximum over ranks.  Every pass streams 2.5 GB of weights and context, far
-more than the 126 MB L2, so no L2 flush is needed between steps.  ``value``
-is the drafted tokens/s of the whole job (N ranks x 16 tokens per pass);
-``e2e`` is the same through the public DraftSession API with the anchor id
-copied from pinned host memory and the drafted tokens copied back every step.
+Beside it: ``pass_us`` / ``batch1``, the BASELINE config-2 pass (Qwen3-8B
+sizing: hidden 2048, 8 layers, 16 heads x 128, GELU 8192, LM head over
+151936 rows of 4096), batch 1 per rank, a 2048-position context (2.5 GB of
+weights and context streamed per pass), against its HBM floor; on one GPU
+also configs 3 (batch 64 ragged, 1 and 2 jumps) and 4 (acceptance).  Weights
+are seeded random-init (no checkpoint on the box), conditioning N(0, 1).
 
-Multi-GPU: drafting shards by request; every rank drafts its own sequence on
-its own GPU with a full weight replica and no collective on the data path
-(weak scaling).  ``--impl reference`` times the reference algorithm (the CPU
-oracle port of modeling_flashmap.py) on the host cores instead.
+``--impl reference`` times the reference algorithm (the CPU oracle port of
+modeling_flashmap.py) on the host cores over a bounded sample of the same
+workload; under torchrun only rank 0 runs it.
 """
 
 from __future__ import annotations
@@ -211,23 +218,45 @@ def profiled_traffic():
 
 # ------------------------------------------------------------------ CPU side (oracle port)
 
-def cpu_reference(seconds: float = 15.0, seed: int = 0) -> dict:
+def tiled_target_head(config, seed: int):
+    """Target embedding / head of the right shape filled with seeded N(0,1) and
+    U(+-1/sqrt(H)) blocks of 8192 rows repeated down the vocabulary."""
+    V, Ht = config.vocab_size, config.target_hidden_size
+    g = torch.Generator().manual_seed(seed)
+    e_blk = torch.randn(8192, Ht, generator=g).to(torch.bfloat16)
+    h_blk = ((torch.rand(8192, Ht, generator=g) * 2 - 1) / Ht ** 0.5).to(torch.bfloat16)
+    emb, head = torch.empty(V, Ht, dtype=torch.bfloat16), torch.empty(V, Ht, dtype=torch.bfloat16)
+    for r in range(0, V, 8192):
+        n = min(8192, V - r)
+        emb[r:r + n] = e_blk[:n]
+        head[r:r + n] = h_blk[:n]
+    return emb, head
+
+
+def cpu_reference(c: dict, context: int, seconds: float = 15.0, seed: int = 0, label: str = "config-2") -> dict:
     """The reference algorithm (CPU oracle port) on the host cores: a bounded
-    sample of config-2 one-jump draft passes, bf16, batch 1, 2048 context."""
+    sample of one-jump draft passes of the drafter `c`, bf16, batch 1, over a
+    context of `context` positions."""
     from flashmap_b200 import FlashMapConfig
     from flashmap_b200.synthetic import synthetic_state_dict, synthetic_target_head
     from oracle.flashmap_oracle import Oracle, OracleCache
 
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
     torch.set_num_threads(threads)
-    config = FlashMapConfig(**CONFIG2)
+    config = FlashMapConfig(**c)
     t0 = time.perf_counter()
     sd = synthetic_state_dict(config, seed=seed, dtype=torch.bfloat16)
     oracle = Oracle(config, sd, torch.bfloat16)
-    emb, head = synthetic_target_head(config, seed=seed, dtype=torch.bfloat16)
+    if config.vocab_size * config.target_hidden_size > (1 << 30):
+        # a timing sample: the target rows are seeded random 8192-row blocks repeated down the
+        # vocabulary (drawing 2.5 G values one by one takes minutes on the host)
+        emb, head = tiled_target_head(config, seed)
+    else:
+        emb, head = synthetic_target_head(config, seed=seed, dtype=torch.bfloat16)
     K = config.block_size
-    cache = OracleCache(config, 1, CONTEXT + K + 2, torch.bfloat16)
-    hidden = torch.randn(1, CONTEXT, config.target_hidden_size, generator=torch.Generator().manual_seed(2))
+    cache = OracleCache(config, 1, context + K + 2, torch.bfloat16)
+    width = len(config.target_layer_ids) * config.target_hidden_size
+    hidden = torch.randn(1, context, width, generator=torch.Generator().manual_seed(2))
     oracle.extend_context(cache, hidden.to(torch.bfloat16))
     g = torch.Generator().manual_seed(3)
     z = torch.randn(1, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
@@ -240,13 +269,28 @@ def cpu_reference(seconds: float = 15.0, seed: int = 0) -> dict:
         n += 1
     el = time.perf_counter() - t1
     return {"value": K * n / el, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} config-2 one-jump draft passes (bf16, batch 1, ctx {CONTEXT}) of the CPU oracle port "
+            "sample": f"{n} {label} one-jump draft passes (bf16, batch 1, ctx {context}) of the CPU oracle port "
                       f"after one warm-up pass; {el:.1f} s timed, {setup:.1f} s setup",
             "ms_per_pass": 1000.0 * el / n}
 
 
+def shard_context_median() -> int:
+    return int(sorted(shard_lengths())[SHARD_REQUESTS // 2])
+
+
 def workload_config(args, world: int) -> dict:
     """The ``config`` of both arms' JSON lines (the same workload, the same dict)."""
+    if args.workload == "all":
+        return {"workload": "config5: 512 requests of the Qwen3.8-27B-sized drafter (hidden 2560, 10 layers, 20 heads "
+                            "x 128, SwiGLU 6912, 32768-of-248320 state vocabulary), contexts U[1024, 8192], K=16, "
+                            "1 jump, sharded by request over the GPUs; beside it config2 (Qwen3-8B-sized drafter, "
+                            "batch 1 per GPU, ctx 2048)",
+                "requests": SHARD_REQUESTS, "chunk": SHARD_CHUNK, "block": 16, "num_steps": 1,
+                "parallelism": f"request-sharded x{world} (LPT on context length, equal counts, no collective)",
+                "l2": "inputs larger than L2: a 64-request chunk streams ~3 GB of context K/V per pass",
+                "timing": "per chunk: CUDA events over K graph replays (ours), host clock over a bounded sample "
+                          "(reference); a step drafts all 512 requests: sum over chunks, max over ranks",
+                "launch": args.launch}
     nbytes = algorithmic_bytes(PROFILE_SMALL if args.profile_small else CONFIG2, CONTEXT)
     cfg = {"workload": "config2: Qwen3-8B-sized drafter pass, batch 1 per GPU, K=16, ctx 2048, 1 jump",
            "batch_per_gpu": 1, "block": 16, "context": CONTEXT, "num_steps": 1,
@@ -262,11 +306,15 @@ def workload_config(args, world: int) -> dict:
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    ref = cpu_reference(seconds=args.cpu_seconds)
+    if args.workload == "all":
+        ref = cpu_reference(CONFIG5, shard_context_median(), seconds=args.cpu_seconds, label="config-5")
+    else:
+        ref = cpu_reference(CONFIG2, CONTEXT, seconds=args.cpu_seconds)
     line = {"impl": "reference", "metric": METRIC, "value": ref["value"], "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ref["ms_per_pass"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded random-init config-2 drafter, N(0,1) conditioning)",
+            "higher_is_better": True, "scaling": "strong" if args.workload == "all" else "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random-init drafter, N(0,1) conditioning)",
             "config": workload_config(args, world),
             "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": ref["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -296,10 +344,9 @@ def gemm_flops(c: dict, batch: int, block: int = 16) -> float:
     return 2.0 * batch * (block * (slot + lm) + anchor)
 
 
-def build_batched(c: dict, batch: int, lo: int, hi: int, seed: int, num_steps: int):
-    """A drafter with `batch` sequences whose contexts have ragged lengths
-    uniform in [lo, hi] (seeded), filled through the varlen extend_context."""
-    from flashmap_b200 import DraftSession, FlashMapCache, FlashMapConfig, FlashMapDraftModel
+def build_model(c: dict, seed: int):
+    """A seeded random-init drafter of sizing `c` with its target embedding and head, on this GPU."""
+    from flashmap_b200 import FlashMapConfig, FlashMapDraftModel
     from flashmap_b200.synthetic import synthetic_state_dict, synthetic_target_head
     from torch import nn
 
@@ -312,8 +359,16 @@ def build_batched(c: dict, batch: int, lo: int, hi: int, seed: int, num_steps: i
     embed, head = nn.Embedding(*emb_w.shape, device=dev, dtype=torch.bfloat16), nn.Linear(1, 1, bias=False)
     embed.weight = nn.Parameter(emb_w, requires_grad=False)
     head.weight = nn.Parameter(head_w, requires_grad=False)
-    g = torch.Generator().manual_seed(seed + 5)
-    lengths = torch.randint(lo, hi + 1, (batch,), generator=g)
+    return config, model, embed, head
+
+
+def fill_contexts(config, model, embed, head, lengths: torch.Tensor, seed: int, num_steps: int = 1):
+    """A cache of len(lengths) sequences whose contexts (N(0,1) conditioning
+    rows, seeded) go through the varlen extend_context, and a DraftSession on it."""
+    from flashmap_b200 import DraftSession, FlashMapCache
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    batch = int(lengths.numel())
     K = config.block_size
     cache = FlashMapCache(config, batch, int(lengths.max()) + K + 2, device=dev, dtype=torch.bfloat16)
     cu = torch.zeros(batch + 1, dtype=torch.int32)
@@ -324,7 +379,158 @@ def build_batched(c: dict, batch: int, lo: int, hi: int, seed: int, num_steps: i
     model.extend_context_varlen(cache, rows, cu.to(dev), embed, head)
     del rows
     session = DraftSession(model, cache, embed, head, num_steps=num_steps, seed=seed)
+    return cache, session
+
+
+def build_batched(c: dict, batch: int, lo: int, hi: int, seed: int, num_steps: int):
+    """A drafter with `batch` sequences whose contexts have ragged lengths
+    uniform in [lo, hi] (seeded), filled through the varlen extend_context."""
+    config, model, embed, head = build_model(c, seed)
+    g = torch.Generator().manual_seed(seed + 5)
+    lengths = torch.randint(lo, hi + 1, (batch,), generator=g)
+    cache, session = fill_contexts(config, model, embed, head, lengths, seed, num_steps)
     return config, model, cache, session, lengths
+
+
+# ------------------------------------------------------------------ config 5: 512 requests sharded by request
+
+SHARD_REQUESTS = 512
+SHARD_LENGTHS = (1024, 8192)
+SHARD_CHUNK = 64
+
+
+def shard_lengths() -> list:
+    """The 512 context lengths of the config-5 workload (seeded, U[1024, 8192])."""
+    g = torch.Generator().manual_seed(5)
+    return torch.randint(SHARD_LENGTHS[0], SHARD_LENGTHS[1] + 1, (SHARD_REQUESTS,), generator=g).tolist()
+
+
+def time_cross_attention(config, cache, reps: int = 20) -> dict:
+    """The cross-attention kernel of one layer over a drafted chunk's cache, timed
+    alone with CUDA events: the config-5 pass's dominant kernel (the K/V stream)."""
+    from flashmap_b200 import _lib
+
+    lib = _lib.load()
+    L, _, Bc, H, T, hd = cache.kv.shape
+    dev = cache.kv.device
+    B = Bc
+    nsplit = max(1, min((148 + B * H - 1) // (B * H), (T + 63) // 64))
+    q = torch.randn(B * 16, H * hd, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    wsb = lib.fm_cross_attn_workspace_size(B, H, hd, nsplit)
+    ws = torch.zeros(wsb, dtype=torch.uint8, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    p = lambda t: t.data_ptr()  # noqa: E731
+
+    def launch(layer):
+        _lib.call("fm_cross_attn", p(q), p(cache.kv), p(out), p(cache.lengths), B, H, hd, L, layer, Bc, T, nsplit,
+                  p(ws), wsb, p(err), torch.cuda.current_stream().cuda_stream)
+
+    for i in range(3):
+        launch(i % L)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(reps):
+        launch(i % L)  # successive layers: each launch streams K/V rows not read by the one before
+    b.record(stream)
+    torch.cuda.synchronize()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"cross-attention timing recorded device error {int(err.item())}")
+    us = a.elapsed_time(b) / reps * 1000.0
+    keys = int((cache.lengths.to(torch.int64) + 1).sum())
+    nbytes = keys * H * hd * 2 * 2 + 2 * B * 16 * H * hd * 2
+    return {"us": us, "bytes": nbytes}
+
+
+def measure_sharded(args, world, rank, local) -> dict:
+    """Config 5: 512 requests of the 27B map (contexts U[1024, 8192]) sharded by
+    request over the ranks (LPT on context length with equal counts per rank),
+    each rank drafting its share in chunks of <= 64 requests with one weight
+    replica and no collective on the data path.  Per chunk: its contexts are
+    filled (untimed), W warm-up replays, then K timed replays (CUDA events,
+    barrier before), then K drafts through DraftSession.draft with host copies.
+    A step drafts every request once: its time is the sum of the chunk times,
+    the maximum over ranks."""
+    from flashmap_b200 import _lib
+    from flashmap_b200.sharding import balanced_capacity, chunks, lpt_assign, request_costs
+
+    _lib.require_device()
+    lengths = shard_lengths()
+    shares = lpt_assign(request_costs(lengths), world, balanced_capacity(len(lengths), world))
+    # chunks of similar lengths: less padding in each chunk's cache
+    mine = sorted(shares[rank], key=lambda i: (lengths[i], i))
+    config, model, embed, head = build_model(CONFIG5, seed=0)
+    K = config.block_size
+    stream = torch.cuda.current_stream()
+    chunk_ms, e2e_ms, launches, h2d, d2h = [], [], 0, 0, 0
+    xattn = None
+    sampler = ClockSampler(physical_gpu_index(local))
+    my_chunks = chunks(mine, SHARD_CHUNK)
+    for ci, idx in enumerate(my_chunks):
+        lens = torch.tensor([lengths[i] for i in idx])
+        cache, session = fill_contexts(config, model, embed, head, lens, seed=1000 * rank + ci)
+        for _ in range(args.warmup):
+            session.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.steps):
+            session.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        chunk_ms.append(a.elapsed_time(b) / args.steps)
+        launches += session.launches
+        g = torch.Generator().manual_seed(7 + ci)
+        anchors = torch.randint(0, config.vocab_size, (args.steps + 3, len(idx)), generator=g).pin_memory()
+        for i in range(3):
+            session.draft(anchors[args.steps + i])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            session.draft(anchors[i])
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1) / args.steps)
+        h2d += len(idx) * 8
+        d2h += len(idx) * K * 8
+        session.plan.check_device_errors()
+        if ci == len(my_chunks) - 1:
+            xattn = time_cross_attention(config, cache)
+        # the model's plans hold their caches: drop them before the next chunk's cache
+        model._plans.clear()
+        del session, cache
+        torch.cuda.empty_cache()
+    clocks = sampler.stop()
+    step_ms = max_over_ranks(sum(chunk_ms), world)
+    e2e_step_ms = max_over_ranks(sum(e2e_ms), world)
+    peak_h, kind_h = measured_peak_hbm()
+    peak_t, kind_t = measured_peak_tensor()
+    flops = gemm_flops(CONFIG5, len(lengths))
+    kv = float(sum(l + 1 for l in lengths) * CONFIG5["num_hidden_layers"] * 2 * CONFIG5["hidden_size"] * 2)
+    total = SHARD_REQUESTS * K
+    xa_gbs = xattn["bytes"] / (xattn["us"] * 1e-6) / 1e9
+    del model, embed, head
+    torch.cuda.empty_cache()
+    return {
+        "value": total / (step_ms / 1000.0), "ms_per_step": step_ms, "chunk_ms": chunk_ms,
+        "chunks_per_rank": len(my_chunks), "requests_per_rank": len(mine), "gpu_launches": launches * args.steps,
+        "gpu_launches_per_step": launches, "clocks": clocks,
+        "e2e": {"value": total / (e2e_step_ms / 1000.0), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_step_ms,
+                "api": "flashmap_b200.DraftSession.draft, one call per chunk"},
+        "roofline": {"kernel": "cross_attn_kernel<128> (one layer over a 64-request chunk's context cache)",
+                     "bound": "hbm", "achieved": xa_gbs, "peak": peak_h, "unit": "GB/s", "frac": xa_gbs / peak_h,
+                     "peak_kind": f"{kind_h} (burst copy, kernel timed alone)", "traffic": None,
+                     "launch_us": xattn["us"], "algorithmic_bytes": xattn["bytes"]},
+        "pass_floor": {"kv_bytes": kv, "kv_floor_ms": kv / (peak_h * 1e9) * 1e3, "gemm_tflop": flops / 1e12,
+                       "gemm_floor_ms": flops / (peak_t * 1e12) * 1e3,
+                       "floor_ms_per_gpu": (kv / (peak_h * 1e9) + flops / (peak_t * 1e12)) * 1e3 / world,
+                       "peak_kinds": [kind_h, kind_t]},
+    }
 
 
 def time_replays(session, steps: int, warmup: int, world: int) -> float:
@@ -343,6 +549,12 @@ def time_replays(session, steps: int, warmup: int, world: int) -> float:
 
 
 def run_config3(args, world, rank, local):
+    line = measure_config3(args, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_config3(args, world, rank):
     """Batched ragged drafting: config 3 (the config-2 map, 64 sequences
     per GPU, contexts U[512, 4096], one jump and two jumps) or config 5 (the
     27B map, SwiGLU and a state vocabulary, 64 requests per GPU — the per-GPU
@@ -375,8 +587,6 @@ def run_config3(args, world, rank, local):
     peak_t, kind_t = measured_peak_tensor()
     peak_h, kind_h = measured_peak_hbm()
     achieved = flops / (ms1 / 1000.0) / 1e12
-    if rank != 0:
-        return
     name = "config5" if five else "config3"
     line = {
         "metric": "drafted tokens/sec (K=16), batch 64 ragged per GPU", "value": world * batch * K / (ms1 / 1000.0),
@@ -393,8 +603,9 @@ def run_config3(args, world, rank, local):
                      "gemm_floor_us": flops / (peak_t * 1e12) * 1e6},
     }
     if ms2 is not None:
-        line["two_jumps"] = {"ms_per_step": ms2, "value": world * batch * K / (ms2 / 1000.0), "unit": "tokens/s"}
-    print(json.dumps(line), flush=True)
+        line["two_jumps"] = {"ms_per_step": ms2, "value": world * batch * K / (ms2 / 1000.0), "unit": "tokens/s",
+                             "ratio_to_one_jump": ms2 / ms1}
+    return line
 
 
 def run_paged(args, world, rank, local):
@@ -454,6 +665,12 @@ def run_paged(args, world, rank, local):
 
 
 def run_config4(args, world, rank, local):
+    line = measure_config4(args, world, rank)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_config4(args, world, rank):
     """Acceptance (config 4): target logits (64, 17, 151936) bf16 ~ N(0, 2^2),
     drafted tokens U[0, V), draft probabilities softmax(N(0,1)); greedy and
     rejection at T = 1 with Philox seed 1234."""
@@ -511,8 +728,6 @@ def run_config4(args, world, rank, local):
     peak_h, kind_h = measured_peak_hbm()
     bytes_g = B * (K + 1) * V * 2
     bytes_r = bytes_g + B * V * 4
-    if rank != 0:
-        return
     line = {
         "metric": "acceptance of a (64 x 17 x 151936) block, us per call (greedy)", "value": res["greedy"],
         "unit": "us", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["greedy"] / 1000,
@@ -527,12 +742,23 @@ def run_config4(args, world, rank, local):
                       "frac": bytes_r / (res["rejection"] * 1e-6) / 1e9 / peak_h,
                       "floor_us": bytes_r / (peak_h * 1e9) * 1e6},
     }
-    print(json.dumps(line), flush=True)
+    return line
 
 
 # ------------------------------------------------------------------ our arm
 
 def run_ours(args, world, rank, local):
+    """The config-2 batch-1 line alone (``--workload config2``)."""
+    line = measure_batch1(args, world, rank, local)
+    if world == 1 and not args.no_cpu_baseline and not args.profile_small:
+        ref = cpu_reference(CONFIG2, CONTEXT, seconds=args.cpu_seconds)
+        line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def measure_batch1(args, world, rank, local):
+    """The config-2 pass, batch 1 per rank (every rank drafts its own request)."""
     from flashmap_b200 import _lib
 
     _lib.require_device()
@@ -640,8 +866,6 @@ def run_ours(args, world, rank, local):
                       "note": "fold_head + fold_noise fast mode (vllm/fold.py:44-100, sglang/model.py:945-958): "
                               "outside parity with the HF path"}
 
-    if rank != 0:
-        return
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -665,26 +889,65 @@ def run_ours(args, world, rank, local):
     if folded is not None:
         line["fast_mode_folded_head"] = folded
         line["fast_mode_folded_head_and_noise"] = folded_all
-    if world == 1 and not args.no_cpu_baseline and not args.profile_small:
-        ref = cpu_reference(seconds=args.cpu_seconds)
+    del session, cache, model
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_all(args, world, rank, local):
+    """The default line: config 5's 512 requests sharded over the ranks (the
+    headline tokens/s), the config-2 batch-1 pass beside it (``pass_us``,
+    ``batch1``), and at N = 1 configs 3 and 4 and the CPU baselines."""
+    b1 = measure_batch1(args, world, rank, local)
+    sh = measure_sharded(args, world, rank, local)
+    extra = {}
+    if world == 1:
+        extra["config3"] = measure_config3(args, world, rank)
+        extra["config4"] = measure_config4(args, world, rank)
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": sh["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": sh["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded random-init config-5 and config-2 drafters and target heads, N(0,1) conditioning)",
+        "config": workload_config(args, world),
+        "e2e": sh["e2e"], "gpu_launches": sh["gpu_launches"], "gpu_launches_per_step": sh["gpu_launches_per_step"],
+        "clocks": sh["clocks"], "roofline": sh["roofline"],
+        "sharding": {"requests": SHARD_REQUESTS, "requests_per_rank": sh["requests_per_rank"],
+                     "chunks_per_rank": sh["chunks_per_rank"], "chunk_ms_rank0": sh["chunk_ms"],
+                     "pass_floor": sh["pass_floor"]},
+        "pass_us": b1["pass_us"], "pass_roofline": b1["pass_roofline"],
+        "batch1": {k: b1[k] for k in ("value", "ms_per_step", "pass_us", "e2e", "roofline", "clocks",
+                                      "gpu_launches_per_step", "fast_mode_folded_head",
+                                      "fast_mode_folded_head_and_noise") if k in b1},
+    }
+    line["batch1"]["workload"] = "config2: Qwen3-8B-sized drafter pass, batch 1 per GPU, K=16, ctx 2048, 1 jump"
+    line.update(extra)
+    if world == 1 and not args.no_cpu_baseline:
+        ref = cpu_reference(CONFIG5, shard_context_median(), seconds=args.cpu_seconds, label="config-5")
         line["cpu_baseline"] = {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        ref2 = cpu_reference(CONFIG2, CONTEXT, seconds=args.cpu_seconds)
+        line["batch1"]["cpu_baseline"] = {k: ref2[k] for k in ("value", "unit", "cores", "kind", "sample")}
     print(json.dumps(line), flush=True)
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--launch", choices=["auto", "kernels", "stream"], default="auto",
                     help="launch structure of a draft: the kernel sequence (kernels), the streamed "
                          "single-launch pass (stream), or the library's choice (auto)")
-    ap.add_argument("--workload", choices=["config2", "config3", "config4", "config5", "paged"], default="config2",
-                    help="config2 (the headline, batch 1), config3 (batch 64 ragged), config4 (acceptance), "
-                         "config5 (27B map, batch 64 ragged), paged (vLLM paged cross-attention operator)")
+    ap.add_argument("--workload", choices=["all", "config2", "config3", "config4", "config5", "paged"], default="all",
+                    help="all (the default line: config 5's 512 requests sharded over the GPUs, with the config-2 "
+                         "batch-1 pass and, on one GPU, configs 3 and 4 beside it), config2 (batch 1 alone), "
+                         "config3 (batch 64 ragged), config4 (acceptance), config5 (one 64-request chunk), "
+                         "paged (vLLM paged cross-attention operator)")
     ap.add_argument("--profile-small", action="store_true",
                     help="2 layers and a 32768-row LM head: the same kernels on < 2 GB, for ncu captures")
     args = ap.parse_args()
@@ -695,6 +958,8 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "all" and not args.profile_small:
+            run_all(args, world, rank, local)
         elif args.workload in ("config3", "config5"):
             run_config3(args, world, rank, local)
         elif args.workload == "paged":

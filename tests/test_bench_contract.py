@@ -1,7 +1,8 @@
 """The bench's CPU-side contract: the reference arm (``--impl reference``, the
 oracle port timed on the host cores) prints one JSON line with every key the
 driver reads; under a multi-rank launch only rank 0 runs and prints; fewer
-than 3 warm-up steps are refused."""
+than 3 warm-up steps are refused; both arms describe a workload with the same
+``config`` dict; the default workload's 512 requests shard with equal counts."""
 
 import json
 import os
@@ -31,7 +32,8 @@ def test_reference_arm_other_ranks_exit_quietly():
 
 
 def test_reference_arm_prints_the_contract_line():
-    p = run(["--impl", "reference", "--steps", "1", "--warmup", "3", "--cpu-seconds", "0.5"],
+    # the config-2 line (the default config-5 sample builds a 770M-parameter drafter on the host)
+    p = run(["--impl", "reference", "--workload", "config2", "--steps", "1", "--warmup", "3", "--cpu-seconds", "0.5"],
             {"RANK": "0", "WORLD_SIZE": "1"})
     assert p.returncode == 0, p.stderr[-2000:]
     lines = [line for line in p.stdout.splitlines() if line.startswith("{")]
@@ -48,3 +50,23 @@ def test_reference_arm_prints_the_contract_line():
     assert e2e["value"] == d["value"] and e2e["unit"] == d["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     assert d["config"]["workload"].startswith("config2")
+
+
+def test_both_arms_print_the_same_config_and_the_default_shards_evenly():
+    import argparse
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("bench_mod", BENCH)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    from flashmap_b200.sharding import balanced_capacity, lpt_assign, request_costs
+
+    for world in (1, 2, 4, 8):
+        args = argparse.Namespace(workload="all", launch="auto", profile_small=False)
+        a, b = bench.workload_config(args, world), bench.workload_config(args, world)
+        assert a == b and a["requests"] == 512 and a["workload"].startswith("config5")
+        lengths = bench.shard_lengths()
+        assert len(lengths) == 512 and min(lengths) >= 1024 and max(lengths) <= 8192
+        shares = lpt_assign(request_costs(lengths), world, balanced_capacity(512, world))
+        assert sorted(i for s in shares for i in s) == list(range(512))
+        assert {len(s) for s in shares} == {512 // world}

@@ -49,17 +49,55 @@ def _free_port():
         return s.getsockname()[1]
 
 
+# a tiny drafter (CPU oracle) that stands in for the GPU draft of each request
+_TINY = dict(target_hidden_size=64, vocab_size=512, target_layer_ids=[0], block_size=16, hidden_size=64,
+             num_hidden_layers=1, num_attention_heads=2, intermediate_size=128, mlp_type="gelu")
+
+
+def _tiny_drafter():
+    from flashmap_b200 import FlashMapConfig
+    from flashmap_b200.synthetic import synthetic_state_dict, synthetic_target_head
+    from oracle.flashmap_oracle import Oracle
+
+    config = FlashMapConfig(**_TINY)
+    sd = synthetic_state_dict(config, seed=3, dtype=torch.float32)
+    emb, head = synthetic_target_head(config, seed=3, dtype=torch.float32)
+    return config, Oracle(config, sd, torch.float32), emb, head
+
+
+def _draft_request(drafter, i, length):
+    """Request i: its own seeded context of `length` positions, anchor and noise; one jump."""
+    from oracle.flashmap_oracle import OracleCache
+
+    config, oracle, emb, head = drafter
+    g = torch.Generator().manual_seed(100 + i)
+    K = config.block_size
+    cache = OracleCache(config, 1, length + K + 2, torch.float32)
+    oracle.extend_context(cache, torch.randn(1, length, config.target_hidden_size, generator=g))
+    anchor = torch.randint(0, config.vocab_size, (1,), generator=g)
+    z = torch.randn(1, K, config.target_hidden_size, generator=g)
+    logits = oracle.draft(anchor, cache, emb, head, num_steps=1, z=z)
+    return logits.float().argmax(-1).reshape(-1).tolist()
+
+
 def _worker(rank, world, port, lengths, out, fail_rank):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
 
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
-        mine = shard_requests(lengths, world, rank)
-        # a rank's "drafting" step: here the per-request result is a pure function of the request
+        from flashmap_b200.sharding import balanced_capacity
+
+        mine = shard_requests(lengths, world, rank, capacity=balanced_capacity(len(lengths), world))
         ok = torch.tensor([0 if rank == fail_rank else 1], dtype=torch.int32)
-        results = {i: lengths[i] * 3 + 1 for i in mine} if rank != fail_rank else {}
+        results = {}
+        if rank != fail_rank:
+            drafter = _tiny_drafter()
+            for idx in chunks(mine, 4):
+                for i in idx:
+                    results[i] = _draft_request(drafter, i, lengths[i])
         # ranks learn of a failed rank on the host, between steps, before any further work
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         gathered = [None] * world
@@ -72,7 +110,10 @@ def _worker(rank, world, port, lengths, out, fail_rank):
 
 @pytest.mark.parametrize("fail_rank", [-1, 1])
 def test_two_ranks_gloo(fail_rank):
-    lengths = _lengths(200, seed=11)
+    """Two gloo ranks draft their LPT shares of 12 requests with the CPU oracle
+    standing in for the GPU draft; together they reproduce, request by request,
+    the tokens of drafting every request in one process."""
+    lengths = [random.Random(11).randint(4, 40) for _ in range(12)]
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
     port = _free_port()
@@ -92,6 +133,10 @@ def test_two_ranks_gloo(fail_rank):
         merged = {}
         for g in gathered:
             merged.update(g[1])
-        assert merged == {i: c * 3 + 1 for i, c in enumerate(lengths)}
+        assert sorted(merged) == list(range(len(lengths)))
+        assert {len(s) for s in shares} == {len(lengths) // 2}
+        drafter = _tiny_drafter()
+        for i, length in enumerate(lengths):
+            assert merged[i] == _draft_request(drafter, i, length), f"request {i}"
     else:
         assert flags == {0}  # every rank saw the failure
