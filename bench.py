@@ -560,7 +560,9 @@ def measure_config3(args, world, rank):
     27B map, SwiGLU and a state vocabulary, 64 requests per GPU — the per-GPU
     chunk of 512 requests over 8 GPUs — contexts U[1024, 8192], one jump).
     --profile-small keeps the GEMM shapes of config 3 (64 x 16 tokens) with 2
-    layers, a 32768-row LM head and contexts U[64, 256], for ncu captures."""
+    layers, a 32768-row LM head and contexts U[64, 256], for ncu captures; with
+    config5 it keeps the 27B map's cross-attention at its context lengths with
+    8 requests and 2 layers (a 1.3 GB cache)."""
     from flashmap_b200 import _lib
 
     _lib.require_device()
@@ -568,7 +570,11 @@ def measure_config3(args, world, rank):
     five = args.workload == "config5"
     c = CONFIG5 if five else CONFIG2
     lo, hi = (1024, 8192) if five else (512, 4096)
-    if args.profile_small:
+    if args.profile_small and five:
+        # the config-5 cross-attention at its real context lengths: 8 requests, 2 layers (a 1.3 GB cache)
+        c = dict(CONFIG5, num_hidden_layers=2)
+        batch = 8
+    elif args.profile_small:
         c = dict(CONFIG2, num_hidden_layers=2, vocab_size=32768)
         lo, hi = 64, 256
     out = {}
