@@ -11,9 +11,9 @@ attention within 2e-2 of the largest output (mean 2e-3); cache values
 bit-exact; greedy sampling exact; the folded head within one bf16 step
 (the GEMM accumulates in another order); the folded noise, once each
 eigenvector's sign is matched (the device eigen-solver may return -q for q),
-within one bf16 step on >= 99.9% of the elements and four everywhere (the
-device accumulates the fp32 Gram matrix in another order, which perturbs the
-eigenvectors).
+within one bf16 step on >= 99.9% of the elements and within 1% of its
+column's largest magnitude everywhere (the device accumulates the fp32 Gram
+matrix in another order, which perturbs the eigenvectors).
 """
 
 import pytest
@@ -112,6 +112,7 @@ def test_cuda_folds_vs_reference_fold_py(idx, cfg):
     sign[sign == 0] = 1
     bad, err = close_bf16(got * sign[None, :], ref, floor=1e-3)
     assert bad <= 1e-3 * ref.numel(), f"folded noise: {bad} elements more than one bf16 step off, max {err}"
-    bad, err = close_bf16(got * sign[None, :], ref, steps=4.0, floor=1e-3)
-    assert bad == 0, f"folded noise: {bad} elements more than four bf16 steps off, max {err}"
+    col = ref.abs().amax(dim=0, keepdim=True)
+    worst = float(((got * sign[None, :] - ref).abs() / col).max())
+    assert worst <= 1e-2, f"folded noise: an element {worst:.4f} of its column's scale off"
     assert torch.allclose(var.cpu(), fn["var"], rtol=1e-5, atol=1e-7)
