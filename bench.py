@@ -204,6 +204,18 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def profiled_traffic_ratio(name: str, key: str = "traffic_ratio"):
+    """DRAM traffic over algorithmic bytes of a kernel, from its committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.strip().startswith(key + ":"):
+                return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def profiled_traffic():
     """DRAM bytes per LM-head launch from the committed ncu summary, if present."""
     path = os.path.join(ROOT, "profiles", "lm_head_gemm_config2.md")
@@ -513,6 +525,7 @@ def measure_sharded(args, world, rank, local) -> dict:
     kv = float(sum(l + 1 for l in lengths) * CONFIG5["num_hidden_layers"] * 2 * CONFIG5["hidden_size"] * 2)
     total = SHARD_REQUESTS * K
     xa_gbs = xattn["bytes"] / (xattn["us"] * 1e-6) / 1e9
+    ratio = profiled_traffic_ratio("cross_attention_config5.md")
     del model, embed, head
     torch.cuda.empty_cache()
     return {
@@ -524,7 +537,10 @@ def measure_sharded(args, world, rank, local) -> dict:
                 "api": "flashmap_b200.DraftSession.draft, one call per chunk"},
         "roofline": {"kernel": "cross_attn_kernel<128> (one layer over a 64-request chunk's context cache)",
                      "bound": "hbm", "achieved": xa_gbs, "peak": peak_h, "unit": "GB/s", "frac": xa_gbs / peak_h,
-                     "peak_kind": f"{kind_h} (burst copy, kernel timed alone)", "traffic": None,
+                     "peak_kind": f"{kind_h} (burst copy, kernel timed alone)",
+                     "traffic": None if ratio is None else int(ratio * xattn["bytes"]),
+                     "traffic_source": "profiles/cross_attention_config5.md: ncu DRAM bytes of an 8-request "
+                                       "capture over its algorithmic bytes, times this launch's",
                      "launch_us": xattn["us"], "algorithmic_bytes": xattn["bytes"]},
         "pass_floor": {"kv_bytes": kv, "kv_floor_ms": kv / (peak_h * 1e9) * 1e3, "gemm_tflop": flops / 1e12,
                        "gemm_floor_ms": flops / (peak_t * 1e12) * 1e3,
