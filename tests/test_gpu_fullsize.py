@@ -65,11 +65,16 @@ def _batched_vs_oracle(cfg, lengths, steps_list, seed):
     report = []
     for steps in steps_list:
         anchors = torch.randint(0, config.vocab_size, (B,), generator=g)
-        z = torch.randn(B, K, config.target_hidden_size, generator=g).to(torch.bfloat16)
-        got, tok = model.draft(anchors.to(DEV), cache, E, W, num_steps=steps, z=z.to(DEV), return_tokens=True)
+        if steps == 1:  # a one-jump draft starts from z (B, K, Ht), a multi-jump one from noise (B, K, S)
+            draw = dict(z=torch.randn(B, K, config.target_hidden_size, generator=g).to(torch.bfloat16))
+        else:
+            draw = dict(noise=torch.randn(B, K, config.state_vocab_size or config.vocab_size, generator=g))
+        got, tok = model.draft(anchors.to(DEV), cache, E, W, num_steps=steps, return_tokens=True,
+                               **{k: v.to(DEV) for k, v in draw.items()})
         torch.cuda.synchronize()
         for b in range(B):
-            ref = oracle.draft(anchors[b:b + 1], caches[b], emb_c, head_c, num_steps=steps, z=z[b:b + 1])
+            ref = oracle.draft(anchors[b:b + 1], caches[b], emb_c, head_c, num_steps=steps,
+                               **{k: v[b:b + 1] for k, v in draw.items()})
             err = logits_rel_error(got[b:b + 1], ref)
             bad, under, _ = decisive_disagreements(tok[b:b + 1], got[b:b + 1], ref)
             report.append((steps, b, lengths[b], err, bad, under))
