@@ -366,6 +366,53 @@ __device__ __forceinline__ int lane_load8(const __nv_bfloat16* row, int nch, int
   return n;
 }
 
+// Rows wider than 2048 (up to 32 * MAXC * 8 columns): the row held in
+// registers as 16-byte chunks lane + 32 i (the canonical order of rows.cuh),
+// the weight / modulation chunks loaded as each output chunk is formed.
+template <int MAXC>
+__device__ __forceinline__ int lane_load(const __nv_bfloat16* row, int nch, int lane, uint4* raw) {
+  int n = 0;
+#pragma unroll
+  for (int i = 0; i < MAXC; ++i) {
+    const int ch = lane + 32 * i;
+    if (ch < nch) {
+      raw[i] = *reinterpret_cast<const uint4*>(row + ch * 8);
+      n = i + 1;
+    }
+  }
+  return n;
+}
+constexpr int WIDE_CHUNKS = 24;  // rows of up to 6144 columns
+
+__device__ __forceinline__ void rms_row_wide(const __nv_bfloat16* xr, const __nv_bfloat16* w, __nv_bfloat16* yr,
+                                             int cols, float eps, int lane) {
+  const int nch = cols / 8;
+  uint4 xv[WIDE_CHUNKS];
+  const int n = lane_load<WIDE_CHUNKS>(xr, nch, lane, xv);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < WIDE_CHUNKS; ++i)
+    if (i < n) {
+      float xf[8], t[8];
+      unpack_bf16x8(xv[i], xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) t[e] = __fmul_rn(xf[e], xf[e]);
+      s = __fadd_rn(s, chunk_tree(t, 8));
+    }
+  const float inv = inv_rms(warp_allsum(s), cols, eps);
+#pragma unroll
+  for (int i = 0; i < WIDE_CHUNKS; ++i)
+    if (i < n) {
+      const int ch = lane + 32 * i;
+      float xf[8], wf[8], o[8];
+      unpack_bf16x8(xv[i], xf);
+      unpack_bf16x8(*reinterpret_cast<const uint4*>(w + ch * 8), wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = rms_value(xf[e], wf[e], inv);
+      *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
+    }
+}
+
 __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
                                                      __nv_bfloat16* y, long long rows, int cols, float eps) {
   pdl_wait();
@@ -401,6 +448,10 @@ __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, con
         for (int e = 0; e < 8; ++e) o[e] = rms_value(xf[e], wf[e], inv);
         *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
       }
+    return;
+  }
+  if (cols % 8 == 0 && cols <= 32 * 8 * WIDE_CHUNKS && vec_ok(xr) && vec_ok(yr) && vec_ok(w)) {
+    rms_row_wide(xr, w, yr, cols, eps, lane);
     return;
   }
   const float inv = inv_rms(warp_row_sumsq(xr, cols, lane), cols, eps);
@@ -457,6 +508,48 @@ __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
         *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
+      }
+    return;
+  }
+  if (cols % 8 == 0 && cols <= 32 * 8 * WIDE_CHUNKS && vec_ok(xr) && vec_ok(yr) && vec_ok(mod)) {
+    // wide rows: the same canonical order, the modulation read chunk by chunk
+    const int nch = cols / 8;
+    uint4 xv[WIDE_CHUNKS];
+    const int n = lane_load<WIDE_CHUNKS>(xr, nch, lane, xv);
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < WIDE_CHUNKS; ++i)
+      if (i < n) {
+        float xf[8];
+        unpack_bf16x8(xv[i], xf);
+        s = __fadd_rn(s, chunk_tree(xf, 8));
+      }
+    const float mean = __fdiv_rn(warp_allsum(s), (float)cols);
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < WIDE_CHUNKS; ++i)
+      if (i < n) {
+        float xf[8], t[8];
+        unpack_bf16x8(xv[i], xf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = __fsub_rn(xf[e], mean);
+          t[e] = __fmul_rn(d, d);
+        }
+        q = __fadd_rn(q, chunk_tree(t, 8));
+      }
+    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_allsum(q), (float)cols), eps)));
+#pragma unroll
+    for (int i = 0; i < WIDE_CHUNKS; ++i)
+      if (i < n) {
+        const int ch = lane + 32 * i;
+        float xf[8], sc[8], sh[8], o[8];
+        unpack_bf16x8(xv[i], xf);
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(mod + ch * 8), sc);
+        unpack_bf16x8(*reinterpret_cast<const uint4*>(mod + cols + ch * 8), sh);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
+        *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
       }
     return;
   }
@@ -536,9 +629,9 @@ __global__ void __launch_bounds__(RT) mix_state_kernel(MixArgs a) {
   const __nv_bfloat16* pr = a.post + (long long)t * a.post_stride;
   const __nv_bfloat16* sr = a.state + (long long)t * a.Ht;
   __nv_bfloat16* orow = a.out + (long long)t * a.Ht;
-  if (a.Ht % 8 == 0 && a.Ht <= 4096 && vec_ok(pr) && vec_ok(sr) && vec_ok(orow) && vec_ok(a.state_norm_w) &&
+  if (a.Ht % 8 == 0 && vec_ok(pr) && vec_ok(sr) && vec_ok(orow) && vec_ok(a.state_norm_w) &&
       vec_ok(a.noise_norm_w)) {
-    // two rounds of 8 chunks per lane at most; sums in the canonical order
+    // rounds of 8 chunks per lane (chunk lane + 32 k in round k / 8): sums in the canonical order
     const int nch = a.Ht / 8;
     float sp = 0.0f, ss = 0.0f;
     for (int rd = 0; rd * 256 < nch; ++rd) {
