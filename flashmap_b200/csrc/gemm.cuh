@@ -912,7 +912,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) __stcg(mine + (long long)(c0 + j) * 128 + r, v[j]);
           }
-          __threadfence();
+          // the barrier orders every thread's partial stores before thread 64's
+          // release, which publishes them (a per-thread fence would wait, on
+          // every thread, for all of the SM's loads in flight)
           named_bar_sync(1, 128);
           if (threadIdx.x == 64) {
             if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
