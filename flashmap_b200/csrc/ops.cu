@@ -791,6 +791,10 @@ __global__ void argmax_tokens_kernel(const unsigned long long* keys, int64_t* to
 }
 
 // rows of the multi-step featurisation GEMM input
+// The multi-jump state rows (modeling_flashmap.py:378-391): per token the bf16
+// copy of the fp32 state and, with the posterior, softmax(c * state) in bf16.
+// Rows are read as 16-byte vectors of 8 (four in flight per thread), the
+// exponentials two at a time (fm_exp2); scalar loops serve unaligned rows.
 __global__ void __launch_bounds__(RT) state_rows_kernel(const float* state, __nv_bfloat16* out, int T, int S,
                                                         float c, int with_posterior) {
   pdl_wait();
@@ -799,19 +803,84 @@ __global__ void __launch_bounds__(RT) state_rows_kernel(const float* state, __nv
   const int t = blockIdx.x;
   const float* sr = state + (long long)t * S;
   __nv_bfloat16* st_out = out + (long long)(with_posterior ? T + t : t) * S;
-  for (int v = threadIdx.x; v < S; v += RT) st_out[v] = f2bf(sr[v]);
-  if (!with_posterior) return;
-  float m = -INFINITY;
-  for (int v = threadIdx.x; v < S; v += RT) m = fmaxf(m, __fmul_rn(sr[v], c));
-  m = block_max(m, red);
-  float acc = 0.0f;
-  for (int v = threadIdx.x; v < S; v += RT) acc = __fadd_rn(acc, fm_exp(__fsub_rn(__fmul_rn(sr[v], c), m)));
-  const float sum = block_sum(acc, red);
   __nv_bfloat16* po = out + (long long)t * S;
+  const bool vec = S % 8 == 0 && vec_ok(sr) && vec_ok(st_out) && vec_ok(po);
+  const int nvec = S / 8;
+  float m = -INFINITY;
+  if (vec) {
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * RT) {
+      float x[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (v0 + u * RT < nvec) load8(sr, v0 + u * RT, S, true, x[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * RT;
+        if (v >= nvec) break;
+        *reinterpret_cast<uint4*>(st_out + (long long)v * 8) = pack_bf16x8(x[u]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, __fmul_rn(x[u][e], c));
+      }
+    }
+  } else {
+    for (int v = threadIdx.x; v < S; v += RT) {
+      st_out[v] = f2bf(sr[v]);
+      m = fmaxf(m, __fmul_rn(sr[v], c));
+    }
+  }
+  if (!with_posterior) return;
+  m = block_max(m, red);
+  const float2 neg_m = make_float2(-m, -m), c2 = make_float2(c, c);
+  float acc = 0.0f;
+  if (vec) {
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * RT) {
+      float x[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (v0 + u * RT < nvec) load8(sr, v0 + u * RT, S, true, x[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (v0 + u * RT >= nvec) break;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 e = fm_exp2(__fadd2_rn(__fmul2_rn(make_float2(x[u][2 * i], x[u][2 * i + 1]), c2), neg_m));
+          acc = __fadd_rn(__fadd_rn(acc, e.x), e.y);
+        }
+      }
+    }
+  } else {
+    for (int v = threadIdx.x; v < S; v += RT) acc = __fadd_rn(acc, fm_exp(__fsub_rn(__fmul_rn(sr[v], c), m)));
+  }
+  const float sum = block_sum(acc, red);
+  if (vec) {
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * RT) {
+      float x[4][8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (v0 + u * RT < nvec) load8(sr, v0 + u * RT, S, true, x[u]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int v = v0 + u * RT;
+        if (v >= nvec) break;
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 e = fm_exp2(__fadd2_rn(__fmul2_rn(make_float2(x[u][2 * i], x[u][2 * i + 1]), c2), neg_m));
+          o[2 * i] = __fdiv_rn(e.x, sum);
+          o[2 * i + 1] = __fdiv_rn(e.y, sum);
+        }
+        *reinterpret_cast<uint4*>(po + (long long)v * 8) = pack_bf16x8(o);
+      }
+    }
+    return;
+  }
   for (int v = threadIdx.x; v < S; v += RT)
     po[v] = f2bf(__fdiv_rn(fm_exp(__fsub_rn(__fmul_rn(sr[v], c), m)), sum));
 }
 
+// state = (a * state + b * softmax(logits row)) / d per token, the softmax's
+// maximum and sum from vector passes (row_sumexp), the update from 16-byte
+// vectors of logits and state
 __global__ void __launch_bounds__(RT) state_update_kernel(float* state, const __nv_bfloat16* logits, long long ldl,
                                                           int S, float a, float b, float d) {
   pdl_wait();
@@ -820,12 +889,64 @@ __global__ void __launch_bounds__(RT) state_update_kernel(float* state, const __
   const int t = blockIdx.x;
   const __nv_bfloat16* lr = logits + (long long)t * ldl;
   float* sr = state + (long long)t * S;
+  const bool vec = S % 8 == 0 && vec_ok(lr) && vec_ok(sr);
+  const int nvec = S / 8;
   float m = -INFINITY;
-  for (int v = threadIdx.x; v < S; v += RT) m = fmaxf(m, bf2f(lr[v]));
+  if (vec) {
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 4 * RT) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        raw[u] = v0 + u * RT < nvec ? *reinterpret_cast<const uint4*>(lr + (long long)(v0 + u * RT) * 8)
+                                    : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+      __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80), __ushort_as_bfloat16(0xff80));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+      }
+      m = fmaxf(m, fmaxf(__low2float(m2), __high2float(m2)));
+    }
+  } else {
+    for (int v = threadIdx.x; v < S; v += RT) m = fmaxf(m, bf2f(lr[v]));
+  }
   m = block_max(m, red);
-  float acc = 0.0f;
-  for (int v = threadIdx.x; v < S; v += RT) acc = __fadd_rn(acc, fm_exp(__fsub_rn(bf2f(lr[v]), m)));
-  const float sum = block_sum(acc, red);
+  const float sum = row_sumexp(lr, (long long)S, 1.0f, m, red);
+  if (vec) {
+    const float2 neg_m = make_float2(-m, -m);
+    for (int v0 = threadIdx.x; v0 < nvec; v0 += 2 * RT) {
+      uint4 raw[2];
+      float4 st[2][2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+        if (v0 + u * RT < nvec) {
+          const long long v = v0 + u * RT;
+          raw[u] = *reinterpret_cast<const uint4*>(lr + v * 8);
+          st[u][0] = *reinterpret_cast<const float4*>(sr + v * 8);
+          st[u][1] = *reinterpret_cast<const float4*>(sr + v * 8 + 4);
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const long long v = v0 + u * RT;
+        if (v >= nvec) break;
+        const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+        float sv[8] = {st[u][0].x, st[u][0].y, st[u][0].z, st[u][0].w, st[u][1].x, st[u][1].y, st[u][1].z, st[u][1].w};
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 x = make_float2(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xffff0000u));
+          const float2 e = fm_exp2(__fadd2_rn(x, neg_m));
+          const float p0 = __fdiv_rn(e.x, sum), p1 = __fdiv_rn(e.y, sum);
+          o[2 * i] = __fdiv_rn(__fadd_rn(__fmul_rn(a, sv[2 * i]), __fmul_rn(b, p0)), d);
+          o[2 * i + 1] = __fdiv_rn(__fadd_rn(__fmul_rn(a, sv[2 * i + 1]), __fmul_rn(b, p1)), d);
+        }
+        *reinterpret_cast<float4*>(sr + v * 8) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(sr + v * 8 + 4) = make_float4(o[4], o[5], o[6], o[7]);
+      }
+    }
+    return;
+  }
   for (int v = threadIdx.x; v < S; v += RT) {
     const float p = __fdiv_rn(fm_exp(__fsub_rn(bf2f(lr[v]), m)), sum);
     sr[v] = __fdiv_rn(__fadd_rn(__fmul_rn(a, sr[v]), __fmul_rn(b, p)), d);

@@ -368,8 +368,10 @@ fm_status build_stream(fm_plan* p) {
     int64_t vg = std::min<int64_t>(G, (int64_t)g.args.m_tiles * 4);
     vg = std::max<int64_t>(vg, std::min<int64_t>(G, (bytes + (256 << 10) - 1) >> 18));
     vg = std::min<int64_t>(vg, units);
-    // a transform stage stages the constant rows of all of a CTA's units at once
-    if (bkind != B_COPY) vg = std::max<int64_t>(vg, (units + MAX_TRANSFORM_UNITS - 1) / MAX_TRANSFORM_UNITS);
+    // a transform stage builds every operand block of its units on its CTA's two
+    // operand warps: spread it over the whole grid (and its constant rows, staged
+    // at once, must fit)
+    if (bkind != B_COPY) vg = std::min<int64_t>(G, units);
     S.vg = (int)vg;
     S.rot = rot;
     rot = (int)((rot + vg) % G);
