@@ -80,11 +80,15 @@ __device__ __forceinline__ void gemm_stamp(unsigned long long* trace, int slot) 
   if (trace) trace[(long long)blockIdx.x * GEMM_TRACE + slot] = global_ns();
 }
 
-template <int BN>
+// CG = 2: a CTA pair computes 256 x BN tiles with one M = 256 MMA; each CTA
+// stages its 128 weight rows and BN / 2 token rows per k-block (32 KB for
+// BN = 256 instead of 48 KB), so six stages fit where a single CTA held four.
+template <int BN, int CG = 1>
 struct GemmShape {
   static constexpr int A_BYTES = 128 * 64 * 2;
-  static constexpr int B_BYTES = BN * 64 * 2;
-  static constexpr int STAGES = BN <= 16 ? 5 : BN <= 32 ? 4 : BN <= 64 ? 7 : BN <= 128 ? 5 : 4;
+  static constexpr int B_BYTES = (BN / CG) * 64 * 2;
+  static constexpr int STAGES =
+      CG == 2 ? 6 : BN <= 16 ? 5 : BN <= 32 ? 4 : BN <= 64 ? 7 : BN <= 128 ? 5 : 4;
   static constexpr int ACC = 2;
   static constexpr uint32_t TMEM_COLS =
       ACC * BN <= 32 ? 32 : ACC * BN <= 64 ? 64 : ACC * BN <= 128 ? 128 : ACC * BN <= 256 ? 256 : 512;
@@ -491,7 +495,8 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
       layer = (mt * 128) / (2 * a.part_rows);
       part = ((mt * 128) / a.part_rows) & 1;  // 0 k, 1 v
     }
-    const bool normed = (EPI == EPI_QKNORM) ? (part < 2) : (part == 0);
+    // (a pair's second half tile may lie wholly past M: no k-norm weight read for it)
+    const bool normed = (EPI == EPI_QKNORM) ? (part < 2) : (part == 0 && mt * 128 < a.M);
     const int d = (m % a.part_rows) % hd;
     float y[16];
 #pragma unroll
@@ -663,13 +668,19 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
 }
 
 // ---------------------------------------------------------------------------------------------
-template <int BN, int EPI>
+// CG = 1: one CTA per 128 x BN tile.  CG = 2 (launched as clusters of two):
+// a CTA pair per 256 x BN tile, the units (pair tile, k-block) split over the
+// pairs; each CTA finishes its own 128 rows (its own split-K counter and
+// partial slots), so the epilogues are those of the single-CTA tile.
+template <int BN, int EPI, int CG = 1>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const GemmArgs a, unsigned long long* trace) {
-  using S = GemmShape<BN>;
+  using S = GemmShape<BN, CG>;
   constexpr int STAGES = S::STAGES;
   constexpr int ACC = S::ACC;
+  constexpr bool PAIR = CG == 2;
+  static_assert(CG == 1 || (CG == 2 && BN == 256), "CTA pairs run 256 x 256 tiles");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -688,8 +699,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long U = a.units;
-  const int G = gridDim.x;
-  const int c = blockIdx.x;
+  // units are split over the CTAs (CG = 1) or the pairs (CG = 2)
+  const int G = gridDim.x / CG;
+  const int c = blockIdx.x / CG;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const long long u0 = (long long)c * U / G, u1 = (long long)(c + 1) * U / G;
   const int kb = a.kb;
   if (threadIdx.x == 0) gemm_stamp(trace, 0);
@@ -701,7 +714,8 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int i = 0; i < ACC; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      // a pair's accumulator is released by the epilogue warps of both CTAs
+      mbar_init(&acc_empty[i], 4 * CG);
     }
     flags[0] = 0;
     flags[1] = 0;
@@ -713,11 +727,19 @@ __global__ void __launch_bounds__(192, 1)
     tma_prefetch_desc(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, S::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, S::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers initialised before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   if (threadIdx.x == 0) gemm_stamp(trace, 1);
@@ -726,49 +748,110 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = flags;
 
   if (warp == 0) {
-    if (lane == 0 && u1 > u0) {
-      const uint64_t pol = a.n_tiles == 1 ? policy_evict_first() : policy_evict_last();
-      const long long n = u1 - u0;
-      const int pre = (int)(n < STAGES ? n : STAGES);
-      // weights of the first stages before the dependency wait
-      for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int tile = (int)(u / kb), k = (int)(u % kb);
-        mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
-        tma_load_2d_hint(sA + i * S::A_BYTES, &tmA, &full[i], k * 64, (tile / a.n_tiles) * 128, pol);
-      }
-      pdl_wait();
-      for (int i = 0; i < pre; ++i) {
-        const long long u = u0 + i;
-        const int tile = (int)(u / kb), k = (int)(u % kb);
-        tma_load_2d(sB + i * S::B_BYTES, &tmB, &full[i], k * 64, (tile % a.n_tiles) * BN);
-      }
-      bool ok = true;
-      for (long long i = pre; i < n; ++i) {
-        const int s = (int)(i % STAGES);
-        const uint32_t r = (uint32_t)(i / STAGES);
-        if (!mbar_wait(&empty[s], (r - 1) & 1u, abort_flag)) {
-          record_error(a.err, DEV_TIMEOUT_EMPTY);
-          *abort_flag = 1;
-          ok = false;
-          break;
+    if constexpr (!PAIR) {
+      if (lane == 0 && u1 > u0) {
+        const uint64_t pol = a.n_tiles == 1 ? policy_evict_first() : policy_evict_last();
+        const long long n = u1 - u0;
+        const int pre = (int)(n < STAGES ? n : STAGES);
+        // weights of the first stages before the dependency wait
+        for (int i = 0; i < pre; ++i) {
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
+          tma_load_2d_hint(sA + i * S::A_BYTES, &tmA, &full[i], k * 64, (tile / a.n_tiles) * 128, pol);
         }
-        const long long u = u0 + i;
-        const int tile = (int)(u / kb), k = (int)(u % kb);
-        mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
-        tma_load_2d_hint(sA + s * S::A_BYTES, &tmA, &full[s], k * 64, (tile / a.n_tiles) * 128, pol);
-        tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], k * 64, (tile % a.n_tiles) * BN);
+        pdl_wait();
+        for (int i = 0; i < pre; ++i) {
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          tma_load_2d(sB + i * S::B_BYTES, &tmB, &full[i], k * 64, (tile % a.n_tiles) * BN);
+        }
+        bool ok = true;
+        for (long long i = pre; i < n; ++i) {
+          const int s = (int)(i % STAGES);
+          const uint32_t r = (uint32_t)(i / STAGES);
+          if (!mbar_wait(&empty[s], (r - 1) & 1u, abort_flag)) {
+            record_error(a.err, DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          mbar_arrive_expect_tx(&full[s], S::A_BYTES + S::B_BYTES);
+          tma_load_2d_hint(sA + s * S::A_BYTES, &tmA, &full[s], k * 64, (tile / a.n_tiles) * 128, pol);
+          tma_load_2d(sB + s * S::B_BYTES, &tmB, &full[s], k * 64, (tile % a.n_tiles) * BN);
+        }
+        if (!ok) {
+          // drain: every issued stage must land before the CTA's shared memory goes away
+          const long long issued_end = n;
+          for (long long i = (issued_end > STAGES ? issued_end - STAGES : 0); i < issued_end; ++i)
+            mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, nullptr);
+        }
       }
-      if (!ok) {
-        // drain: every issued stage must land before the CTA's shared memory goes away
-        const long long issued_end = n;
-        for (long long i = (issued_end > STAGES ? issued_end - STAGES : 0); i < issued_end; ++i)
-          mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, nullptr);
+    } else {
+      if (lane == 0 && u1 > u0) {
+        // pair producer (both CTAs): this CTA's 128 weight rows and BN / 2 token
+        // rows of each k-block into its own stage buffers, the bytes counted on
+        // rank 0's full barrier, which rank 0 arms for both CTAs' copies
+        const uint64_t pol = a.n_tiles == 1 ? policy_evict_first() : policy_evict_last();
+        const uint64_t pol_b = policy_evict_last();
+        const long long n = u1 - u0;
+        const int pre = (int)(n < STAGES ? n : STAGES);
+        constexpr uint32_t STAGE_TX = CG * (S::A_BYTES + S::B_BYTES);
+        auto a_row = [&](int tile) { return (tile / a.n_tiles) * 256 + (int)rank * 128; };
+        auto b_row = [&](int tile) { return (tile % a.n_tiles) * BN + (int)rank * (BN / 2); };
+        for (int i = 0; i < pre; ++i) {
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          if (rank == 0) mbar_arrive_expect_tx(&full[i], STAGE_TX);
+          tma_load_2d_pair(sA + i * S::A_BYTES, &tmA, mapa_shared(smem_u32(&full[i]), 0), k * 64, a_row(tile), pol);
+        }
+        pdl_wait();
+        for (int i = 0; i < pre; ++i) {
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          tma_load_2d_pair(sB + i * S::B_BYTES, &tmB, mapa_shared(smem_u32(&full[i]), 0), k * 64, b_row(tile), pol_b);
+        }
+        bool ok = true;
+        long long issued = pre;
+        for (long long i = pre; i < n; ++i) {
+          const int s = (int)(i % STAGES);
+          const uint32_t r = (uint32_t)(i / STAGES);
+          if (!mbar_wait(&empty[s], (r - 1) & 1u, abort_flag)) {
+            record_error(a.err, DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          const long long u = u0 + i;
+          const int tile = (int)(u / kb), k = (int)(u % kb);
+          const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[s], STAGE_TX);
+          tma_load_2d_pair(sA + s * S::A_BYTES, &tmA, fb, k * 64, a_row(tile), pol);
+          tma_load_2d_pair(sB + s * S::B_BYTES, &tmB, fb, k * 64, b_row(tile), pol_b);
+          issued = i + 1;
+        }
+        // Every stage this CTA filled is consumed (its empty barrier completed by
+        // rank 0's commit) before the CTA may leave: no commit then arrives on a
+        // barrier of a CTA that has exited.  After a failure rank 0 waits instead
+        // (bounded) for the copies it armed to land.
+        const long long from = issued > STAGES ? issued - STAGES : 0;
+        for (long long i = from; i < issued; ++i) {
+          if (rank == 0 && !ok) mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, nullptr);
+          if (ok && !mbar_wait(&empty[i % STAGES], (uint32_t)(i / STAGES) & 1u, abort_flag)) {
+            record_error(a.err, DEV_TIMEOUT_EMPTY);
+            *abort_flag = 1;
+            ok = false;
+          }
+        }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && u1 > u0) {
-      constexpr uint32_t IDESC = idesc_bf16_f32(128, BN);
+    // CG = 2: only rank 0 issues; its MMAs read both CTAs' stages and write
+    // both CTAs' accumulators, and each commit is sent to both CTAs' barriers
+    if (lane == 0 && u1 > u0 && rank == 0) {
+      constexpr uint32_t IDESC = idesc_bf16_f32(128 * CG, BN);
       long long i = 0;
       int seg = 0;
       for (long long u = u0; u < u1; ++seg) {
@@ -796,14 +879,28 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint64_t ad = sdesc_k_sw128(smem_u32(sA + s * S::A_BYTES));
           const uint64_t bd = sdesc_k_sw128(smem_u32(sB + s * S::B_BYTES));
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(d_tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
-                      (u > seg_begin || kk > 0) ? 1u : 0u);
-          umma_commit(&empty[s]);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16_pair(d_tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
+                             (u > seg_begin || kk > 0) ? 1u : 0u);
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 0));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), 1));
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              umma_bf16(d_tmem, ad + (uint64_t)(kk * 2), bd + (uint64_t)(kk * 2), IDESC,
+                        (u > seg_begin || kk > 0) ? 1u : 0u);
+            umma_commit(&empty[s]);
+          }
         }
         if (!ok) break;
-        umma_commit(&acc_full[acc]);
+        if constexpr (PAIR) {
+          umma_commit_pair(mapa_shared(smem_u32(&acc_full[acc]), 0));
+          umma_commit_pair(mapa_shared(smem_u32(&acc_full[acc]), 1));
+        } else {
+          umma_commit(&acc_full[acc]);
+        }
         if (seg < 3) gemm_stamp(trace, 2 + 4 * seg);
       }
     }
@@ -833,7 +930,9 @@ __global__ void __launch_bounds__(192, 1)
       if (!flags[2 + (seg & 1)]) break;
       if (threadIdx.x == 64 && seg < 3) gemm_stamp(trace, 3 + 4 * seg);
       tc_fence_after();
-      const int mt = tile / a.n_tiles, nt = tile % a.n_tiles;
+      // this CTA's 128-row tile (its half of a pair tile) and its split-K counter
+      const int mt = (tile / a.n_tiles) * CG + (int)rank, nt = tile % a.n_tiles;
+      const int ctile = tile * CG + (int)rank;
       const int m = mt * 128 + r;
       const int n0 = nt * BN;
       const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
@@ -904,7 +1003,7 @@ __global__ void __launch_bounds__(192, 1)
         const long long c_last = cta_of_unit((long long)(tile + 1) * kb - 1, U, G);
         if (c != c_first) {
           // a later contributor: this tile is its first segment (partials slot 0)
-          float* mine = a.ws + ((long long)(c * 2) * BN) * 128;
+          float* mine = a.ws + ((long long)((c * CG + (int)rank) * 2) * BN) * 128;
           for (int c0 = 0; c0 < BN; c0 += 16) {
             float v[16];
             tmem_ld_x16(taddr + c0, v);
@@ -918,17 +1017,17 @@ __global__ void __launch_bounds__(192, 1)
           named_bar_sync(1, 128);
           if (threadIdx.x == 64) {
             if (seg < 3) gemm_stamp(trace, 4 + 4 * seg);
-            gemm_red_release(a.counters + tile, 1);
+            gemm_red_release(a.counters + ctile, 1);
           }
         } else {
           // the head: wait for the others, stage their partials, finish the tile
           const int others = (int)(c_last - c_first);
           if (threadIdx.x == 64) {
-            bool ok = gemm_ld_acquire(a.counters + tile) >= others;
+            bool ok = gemm_ld_acquire(a.counters + ctile) >= others;
             if (!ok) {
               const uint64_t t0 = global_ns();
               for (uint32_t i = 1;; ++i) {
-                if (gemm_ld_acquire(a.counters + tile) >= others) {
+                if (gemm_ld_acquire(a.counters + ctile) >= others) {
                   ok = true;
                   break;
                 }
@@ -972,7 +1071,7 @@ __global__ void __launch_bounds__(192, 1)
                     mbar_arrive_expect_tx(fix_bar, (uint32_t)(n * 16 * 512));
                     for (int o = 0; o < n; ++o)
                       bulk_load(stage + (long long)o * 16 * 128,
-                                a.ws + ((long long)((c_first + 1 + og + o) * 2) * BN + c0) * 128, 16u * 512u,
+                                a.ws + ((long long)(((c_first + 1 + og + o) * CG + rank) * 2) * BN + c0) * 128, 16u * 512u,
                                 fix_bar);
                     flags[1] = mbar_wait(fix_bar, (uint32_t)round & 1u, nullptr) ? 1 : 0;
                     if (!flags[1]) {
@@ -1007,7 +1106,7 @@ __global__ void __launch_bounds__(192, 1)
                 mbar_arrive_expect_tx(fix_bar, (uint32_t)(others * ncols * 512));
                 for (int o = 0; o < others; ++o)
                   bulk_load(stage + (long long)o * ncols * 128,
-                            a.ws + ((long long)((c_first + 1 + o) * 2) * BN + col0) * 128, (uint32_t)(ncols * 512),
+                            a.ws + ((long long)(((c_first + 1 + o) * CG + rank) * 2) * BN + col0) * 128, (uint32_t)(ncols * 512),
                             fix_bar);
               }
               if (round == 0) {
@@ -1092,7 +1191,7 @@ __global__ void __launch_bounds__(192, 1)
             }
             if (vec && RESID_RING) gemm_cp_wait<0>();
             if (threadIdx.x == 64) {
-              if (staged_ok) a.counters[tile] = 0;
+              if (staged_ok) a.counters[ctile] = 0;
               if (seg < 3) gemm_stamp(trace, 5 + 4 * seg);
             }
           }
@@ -1100,14 +1199,27 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+      if (lane == 0) {
+        if constexpr (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));  // rank 0 issues the MMAs
+        else
+          mbar_arrive(&acc_empty[acc]);
+      }
     }
   }
-  __syncthreads();
+  // a pair leaves together: no barrier or TMEM of one CTA is signalled or
+  // read by the other after it exits
+  if constexpr (PAIR)
+    cluster_sync();
+  else
+    __syncthreads();
   if (threadIdx.x == 0) gemm_stamp(trace, 14);
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, S::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
 }
 

@@ -986,71 +986,6 @@ __global__ void extend_commit_kernel(const int32_t* cu, int32_t* lengths, int B)
 constexpr int SLICE_VPT = 8;
 constexpr long long SLICE_VECS = (long long)SLICE_VPT * RT;
 
-__device__ __forceinline__ uint32_t orderable_f32(float v) {
-  const uint32_t b = __float_as_uint(v);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-}
-__device__ __forceinline__ float from_orderable_f32(uint32_t o) {
-  return __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-}
-
-// Raw row maxima, many CTAs per row (slices of SLICE_VECS vectors): atomicMax
-// of the orderable bits into max_keys[row] (zero beforehand).  For T > 0 the
-// row's max of x / T is the rounded quotient of this maximum, because a
-// correctly rounded division by a positive T never reverses an order.
-template <typename T>
-__global__ void __launch_bounds__(RT) row_max_slice_kernel(const T* logits, long long V, uint32_t* max_keys) {
-  pdl_wait();
-  pdl_launch_dependents();
-  const T* row = logits + (long long)blockIdx.x * V;
-  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-  const long long nvec = (V + 7) / 8;
-  const long long v_begin = (long long)blockIdx.y * SLICE_VECS;
-  float mx = -INFINITY;
-  if (sizeof(T) == 2 && aligned && V % 8 == 0) {
-    // bf16 rows of whole vectors: packed bf16x2 maxima
-    uint4 raw[SLICE_VPT];
-#pragma unroll
-    for (int u = 0; u < SLICE_VPT; ++u) {
-      const long long vec = v_begin + u * RT + threadIdx.x;
-      raw[u] = vec < nvec ? *reinterpret_cast<const uint4*>(row + vec * 8)
-                          : make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
-    }
-    __nv_bfloat162 m2 = __halves2bfloat162(__ushort_as_bfloat16(0xff80), __ushort_as_bfloat16(0xff80));
-#pragma unroll
-    for (int u = 0; u < SLICE_VPT; ++u) {
-      const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) m2 = __hmax2(m2, *reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-    }
-    mx = fmaxf(__low2float(m2), __high2float(m2));
-  } else {
-    float x[SLICE_VPT][8];
-#pragma unroll
-    for (int u = 0; u < SLICE_VPT; ++u) {
-      const long long vec = v_begin + u * RT + threadIdx.x;
-      if (vec < nvec) load8(row, vec, V, aligned, x[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < SLICE_VPT; ++u) {
-      const long long vec = v_begin + u * RT + threadIdx.x;
-      if (vec >= nvec) break;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (vec * 8 + j < V) mx = fmaxf(mx, x[u][j]);
-    }
-  }
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  __shared__ float wm[RT / 32];
-  if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < RT / 32; ++w) mx = fmaxf(mx, wm[w]);
-    atomicMax(max_keys + blockIdx.x, orderable_f32(mx));
-  }
-}
-
 template <typename T>
 __global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long long V, float temperature,
                                                        float* stats, int64_t* argmax) {
@@ -1068,25 +1003,6 @@ __global__ void __launch_bounds__(RT) row_stats_kernel(const T* logits, long lon
       stats[2 * blockIdx.x] = m;
       stats[2 * blockIdx.x + 1] = s;
     }
-  }
-}
-
-// (max, sum) of one row at T > 0 with the max taken from the sliced raw
-// maxima (row_max_slice_kernel): m = max / T, then the fixed-order sum.  Kept
-// apart from row_stats_kernel so the sum loop does not carry the argmax's
-// registers.
-template <typename T>
-__global__ void __launch_bounds__(RT, sizeof(T) == 2 ? 6 : 4) row_sum_keys_kernel(const T* logits, long long V, float temperature,
-                                                          float* stats, const uint32_t* max_keys) {
-  pdl_wait();
-  pdl_launch_dependents();
-  __shared__ float red[16];
-  const T* row = logits + (long long)blockIdx.x * V;
-  const float m = __fdiv_rn(from_orderable_f32(max_keys[blockIdx.x]), temperature);
-  const float s = row_sumexp(row, V, temperature, m, red);
-  if (threadIdx.x == 0) {
-    stats[2 * blockIdx.x] = m;
-    stats[2 * blockIdx.x + 1] = s;
   }
 }
 
@@ -1253,7 +1169,7 @@ __global__ void accept_greedy_keys_kernel(const int64_t* draft, const unsigned l
 }
 
 // ---------------------------------------------------------------- rejection acceptance
-// Three launches: the K tests of every request (accept_tests_kernel), the
+// The tests and the rows' statistics (reject_*_kernel below), then the
 // residual's slice totals over (request, slice) blocks (residual_slices_kernel)
 // and the bonus draw (residual_pick_kernel).  The bonus is a sliced
 // categorical draw: slices of CAT_SLICE = 256 ranges of CAT_RANGE weights;
@@ -1369,29 +1285,234 @@ __device__ __forceinline__ void slice_scan(const RejectionRow<T>& w, long long V
   __syncthreads();
 }
 
-// every slot's test u q < p at once (thread k), then the first failure
+// Row statistics of the rejection step.  The exact sum S = sum_v fm_exp(x_v / T - m)
+// runs in a fixed slice-major order: slices of REJ_SLICE_VECS vectors of 8
+// (CAT_SLICE elements); in a slice, thread i sums its REJ_VPT vectors (slice
+// start + u * RT + i, u ascending) element by element, the slice total is
+// block_sum's tree, and the slice totals are added in slice order (the C
+// oracle's row_sumexp_sliced).  fm_exp costs ~18 instructions per element, so
+// the exact sum is formed only for the rows whose outcome needs it:
+//   1. reject_scan_kernel, CTA (row, slice): the slice's raw maximum (exact)
+//      and an approximate sum of 2^((x - max) log2(e) / T) by ex2.approx, in
+//      one read of the slice;
+//   2. reject_decide_kernel, one warp per request: each row's m (exact) and
+//      approximate S'; a test u q < p is settled from p' = e / S' when u q lies
+//      outside p' (1 -+ 2^-10), since S' and S differ by far less (fm_exp's
+//      1-ulp error, ex2.approx's relative error below 2^-21, under a hundred
+//      rounded additions of positive terms); otherwise it stays open.  Listed
+//      for the exact sum: the open tests before the first settled rejection,
+//      then the bonus row (that rejection, or row K);
+//   3. reject_exact_kernel, CTA (request, slice): the listed rows' exact slice totals;
+//   4. reject_final_kernel, one warp per request: the open tests decided with
+//      the exact sums, the accepted length, the bonus row's exact S.
+constexpr int REJ_VPT = 4;
+constexpr long long REJ_SLICE_VECS = (long long)REJ_VPT * RT;
+static_assert(REJ_SLICE_VECS * 8 == CAT_SLICE, "one slicing for the sums and the bonus draw");
+constexpr float REJ_MARGIN = 9.765625e-4f;  // 2^-10
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(RT) accept_tests_kernel(const T* target, const int64_t* draft, const float* q,
-                                                          long long V, int K, float temperature, uint64_t seed,
-                                                          uint32_t offset, const float* stats, int64_t* accepted) {
+__global__ void __launch_bounds__(RT) reject_scan_kernel(const T* logits, long long V, float c, int S,
+                                                         float2* slice_stats) {
   pdl_wait();
   pdl_launch_dependents();
-  __shared__ int s_fail;
-  const int b = blockIdx.x;
-  if (threadIdx.x == 0) s_fail = K;
-  __syncthreads();
-  for (int k = threadIdx.x; k < K; k += RT) {
+  __shared__ float red[16];
+  const T* row = logits + (long long)blockIdx.x * V;
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8;
+  const long long v0 = (long long)blockIdx.y * REJ_SLICE_VECS + threadIdx.x;
+  Raw8<T> x[REJ_VPT];
+#pragma unroll
+  for (int u = 0; u < REJ_VPT; ++u)
+    if (v0 + u * RT < nvec) x[u].load(row, v0 + u * RT, V, aligned);
+  float mx = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < REJ_VPT; ++u) {
+    const long long vec = v0 + u * RT;
+    if (vec >= nvec) break;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 p = x[u].pair(i);
+      if (vec * 8 + 2 * i < V) mx = fmaxf(mx, p.x);
+      if (vec * 8 + 2 * i + 1 < V) mx = fmaxf(mx, p.y);
+    }
+  }
+  mx = block_max(mx, red);
+  float acc = 0.0f;
+  if (mx > -INFINITY && mx < INFINITY) {
+    const float off = -mx * c;
+#pragma unroll
+    for (int u = 0; u < REJ_VPT; ++u) {
+      const long long vec = v0 + u * RT;
+      if (vec >= nvec) break;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 p = x[u].pair(i);
+        if (vec * 8 + 2 * i < V) acc += ex2_approx(fmaf(p.x, c, off));
+        if (vec * 8 + 2 * i + 1 < V) acc += ex2_approx(fmaf(p.y, c, off));
+      }
+    }
+  }
+  acc = block_sum(acc, red);
+  if (threadIdx.x == 0) slice_stats[(long long)blockIdx.x * S + blockIdx.y] = make_float2(mx, acc);
+}
+
+// list[b * (K + 1) + i], i < nlist[b]: rows of request b in ascending order;
+// the last is the bonus candidate, the others open tests
+template <typename T>
+__global__ void __launch_bounds__(32) reject_decide_kernel(const T* target, const int64_t* draft, const float* q,
+                                                           long long V, int K, float temperature, float c,
+                                                           uint64_t seed, uint32_t offset, int S,
+                                                           const float2* slice_stats, float* stats, int* list,
+                                                           int* nlist) {
+  pdl_wait();
+  pdl_launch_dependents();
+  extern __shared__ int state[];  // K entries: 0 accept, 1 reject, 2 open
+  const int b = blockIdx.x, lane = threadIdx.x;
+  const bool unit_t = temperature == 1.0f;
+  for (int k = lane; k <= K; k += 32) {
     const long long row = (long long)b * (K + 1) + k;
+    const float2* ss = slice_stats + row * S;
+    float M = -INFINITY;
+    for (int j = 0; j < S; ++j) M = fmaxf(M, ss[j].x);
+    // max of x / T is the rounded quotient of the raw max (division by T > 0 keeps order)
+    const float m = unit_t ? M : __fdiv_rn(M, temperature);
+    stats[2 * row] = m;
+    if (k == K) break;
+    int st = 2;
+    if (M > -INFINITY && M < INFINITY) {
+      float sa = 0.0f;
+      for (int j = 0; j < S; ++j)
+        if (ss[j].y > 0.0f) sa += ss[j].y * ex2_approx((ss[j].x - M) * c);
+      const long long d = draft[(long long)b * K + k];
+      const float xd = to_f(target[row * V + d]);
+      const float e = fm_exp(__fsub_rn(unit_t ? xd : __fdiv_rn(xd, temperature), m));
+      const float pa = __fdiv_rn(e, sa);
+      const float qd = q[((long long)b * K + k) * V + d];
+      const float u = philox_uniform(seed, (uint32_t)k, (uint32_t)b, offset, 1u);
+      const float uq = __fmul_rn(u, qd);
+      if (uq < __fmul_rn(pa, 1.0f - REJ_MARGIN))
+        st = 0;
+      else if (uq >= __fmul_rn(pa, 1.0f + REJ_MARGIN))
+        st = 1;
+    }
+    state[k] = st;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    int* lst = list + (long long)b * (K + 1);
+    int n = 0, j = 0;
+    for (; j < K && state[j] != 1; ++j)
+      if (state[j] == 2) lst[n++] = j;
+    lst[n++] = j;
+    nlist[b] = n;
+  }
+}
+
+template <typename T, bool UNIT_T>
+__device__ __forceinline__ float reject_exact_slice(const T* row, long long V, float temperature, float m,
+                                                    long long s, float* red) {
+  const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
+  const long long nvec = (V + 7) / 8, nfull = V / 8;
+  const long long v0 = s * REJ_SLICE_VECS + threadIdx.x;
+  const float2 neg_m = make_float2(-m, -m);  // x - m == x + (-m) exactly
+  Raw8<T> x[REJ_VPT];
+#pragma unroll
+  for (int u = 0; u < REJ_VPT; ++u)
+    if (v0 + u * RT < nvec) x[u].load(row, v0 + u * RT, V, aligned);
+  float acc = 0.0f;
+#pragma unroll
+  for (int u = 0; u < REJ_VPT; ++u) {
+    const long long vec = v0 + u * RT;
+    if (vec >= nvec) break;
+    if (vec < nfull) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 xt = x[u].pair(i);
+        if (!UNIT_T) xt = make_float2(__fdiv_rn(xt.x, temperature), __fdiv_rn(xt.y, temperature));
+        const float2 e = fm_exp2(__fadd2_rn(xt, neg_m));
+        acc = __fadd_rn(acc, e.x);
+        acc = __fadd_rn(acc, e.y);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 xp = x[u].pair(i);
+        if (vec * 8 + 2 * i < V)
+          acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.x : __fdiv_rn(xp.x, temperature), m)));
+        if (vec * 8 + 2 * i + 1 < V)
+          acc = __fadd_rn(acc, fm_exp(__fsub_rn(UNIT_T ? xp.y : __fdiv_rn(xp.y, temperature), m)));
+      }
+    }
+  }
+  return block_sum(acc, red);
+}
+
+// CTA (b, s): slice s of each listed row of request b -> exact[b * (K + 1) + i][s]
+template <typename T>
+__global__ void __launch_bounds__(RT) reject_exact_kernel(const T* target, long long V, int K, float temperature,
+                                                             int S, const float* stats, const int* list,
+                                                             const int* nlist, float* exact) {
+  pdl_wait();
+  pdl_launch_dependents();
+  __shared__ float red[16];
+  const int b = blockIdx.x;
+  const long long s = blockIdx.y;
+  const int n = nlist[b];
+  for (int i = 0; i < n; ++i) {
+    const long long row = (long long)b * (K + 1) + list[(long long)b * (K + 1) + i];
+    const float m = stats[2 * row];
+    const float t = temperature == 1.0f
+                        ? reject_exact_slice<T, true>(target + row * V, V, temperature, m, s, red)
+                        : reject_exact_slice<T, false>(target + row * V, V, temperature, m, s, red);
+    if (threadIdx.x == 0) exact[((long long)b * (K + 1) + i) * S + s] = t;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32) reject_final_kernel(const T* target, const int64_t* draft, const float* q,
+                                                          long long V, int K, float temperature, uint64_t seed,
+                                                          uint32_t offset, int S, const int* list, const int* nlist,
+                                                          const float* exact, float* stats, int64_t* accepted) {
+  pdl_wait();
+  pdl_launch_dependents();
+  if (threadIdx.x != 0) return;
+  const int b = blockIdx.x;
+  const int n = nlist[b];
+  const int* lst = list + (long long)b * (K + 1);
+  const bool unit_t = temperature == 1.0f;
+  int j = lst[n - 1];
+  float sj = 0.0f;
+  for (int i = 0; i < n; ++i) {
+    const int k = lst[i];
+    const long long row = (long long)b * (K + 1) + k;
+    const float* ex = exact + ((long long)b * (K + 1) + i) * S;
+    float sum = 0.0f;
+    for (int t = 0; t < S; ++t) sum = __fadd_rn(sum, ex[t]);
+    if (i == n - 1) {
+      sj = sum;
+      break;
+    }
+    // an open test, decided with the exact sum as the C oracle decides it
+    const float m = stats[2 * row];
     const long long d = draft[(long long)b * K + k];
-    const float m = stats[2 * row], s = stats[2 * row + 1];
-    const float x = __fdiv_rn(to_f(target[row * V + d]), temperature);
-    const float p = __fdiv_rn(fm_exp(__fsub_rn(x, m)), s);
+    const float xd = to_f(target[row * V + d]);
+    const float p = __fdiv_rn(fm_exp(__fsub_rn(unit_t ? xd : __fdiv_rn(xd, temperature), m)), sum);
     const float qd = q[((long long)b * K + k) * V + d];
     const float u = philox_uniform(seed, (uint32_t)k, (uint32_t)b, offset, 1u);
-    if (!(__fmul_rn(u, qd) < p)) atomicMin(&s_fail, k);
+    if (!(__fmul_rn(u, qd) < p)) {
+      j = k;
+      sj = sum;
+      break;
+    }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) accepted[b] = s_fail;
+  stats[2 * ((long long)b * (K + 1) + j) + 1] = sj;
+  accepted[b] = j;
 }
 
 // the residual's (or, all accepted, the target's) slice totals: block (b, j)
@@ -1866,10 +1987,30 @@ extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const flo
                        (long long)V, (int)K, seed, offset, tokens);
 }
 
+namespace {
+// Acceptance workspace, 256-byte aligned parts.  Greedy: a 64-bit key per
+// target row.  Rejection: per row (m, S), per (row, slice) the scan's (max,
+// approximate sum) and the listed rows' exact slice totals, per request its
+// row list and count, then the bonus draw's slice totals.
+struct AcceptLayout {
+  size_t stats, slices, exact, list, nlist, totals, bytes;
+  AcceptLayout(int64_t B, int64_t K) {
+    const size_t rows = (size_t)B * (K + 1);
+    auto up = [](size_t x) { return (x + 255) / 256 * 256; };
+    stats = 0;
+    slices = up(rows * 2 * sizeof(float));
+    exact = slices + up(rows * CAT_MAX_SLICES * sizeof(float2));
+    list = exact + up(rows * CAT_MAX_SLICES * sizeof(float));
+    nlist = list + up(rows * sizeof(int));
+    totals = nlist + up((size_t)B * sizeof(int));
+    bytes = totals + up((size_t)B * CAT_MAX_SLICES * sizeof(float));
+  }
+};
+}  // namespace
+
 extern "C" size_t fm_accept_workspace_size(int64_t B, int64_t K) {
-  // per target row: stats and a max key; per request: the bonus draw's slice totals
-  return (size_t)B * (K + 1) * (2 * sizeof(float) + sizeof(int64_t)) + (size_t)B * CAT_MAX_SLICES * sizeof(float) +
-         256;
+  if (B <= 0 || K < 0) return 0;
+  return AcceptLayout(B, K).bytes;
 }
 
 extern "C" fm_status fm_accept_greedy(const void* target_logits, int32_t dtype, const int64_t* draft, int64_t B,
@@ -1892,26 +2033,54 @@ extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtyp
     return set_error(FM_ERR_SHAPE, "accept: bad arguments");
   if (!workspace || workspace_bytes < fm_accept_workspace_size(B, K))
     return set_error(FM_ERR_WORKSPACE, "accept: workspace too small");
-  float* stats = static_cast<float*>(workspace);
-  const long long rows = B * (K + 1);
-  // raw row maxima from many CTAs per row, then per row the fixed-order sum
-  uint32_t* max_keys = reinterpret_cast<uint32_t*>(stats + 2 * rows);
-  fm_status st = check_cuda(cudaMemsetAsync(max_keys, 0, (size_t)rows * 4, as_stream(stream)), "accept: max reset");
-  if (st) return st;
-  const long long slices = ((V + 7) / 8 + SLICE_VECS - 1) / SLICE_VECS;
-  if (slices > 65535) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large");
-  st = FM_DISPATCH_LOGITS(dtype, row_max_slice_kernel, dim3((unsigned)rows, (unsigned)slices), target_logits,
-                          (long long)V, max_keys);
-  if (st) return st;
-  st = FM_DISPATCH_LOGITS(dtype, row_sum_keys_kernel, dim3((unsigned)rows), target_logits, (long long)V, temperature,
-                          stats, (const uint32_t*)max_keys);
-  if (st) return st;
   const long long cat_slices = (V + CAT_SLICE - 1) / CAT_SLICE;
   if (cat_slices > CAT_MAX_SLICES) return set_error(FM_ERR_SHAPE, "accept: vocabulary too large for the bonus draw");
-  // the slice totals follow the stats and max keys (rows * 12 bytes), 256-byte aligned
-  float* totals = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(max_keys + rows) + 255) & ~uintptr_t(255));
-  st = FM_DISPATCH_LOGITS(dtype, accept_tests_kernel, dim3((unsigned)B), target_logits, draft, q, (long long)V,
-                          (int)K, temperature, seed, offset, (const float*)stats, accepted);
+  const AcceptLayout lay(B, K);
+  char* ws = static_cast<char*>(workspace);
+  float* stats = reinterpret_cast<float*>(ws + lay.stats);
+  float2* slice_stats = reinterpret_cast<float2*>(ws + lay.slices);
+  float* exact = reinterpret_cast<float*>(ws + lay.exact);
+  int* list = reinterpret_cast<int*>(ws + lay.list);
+  int* nlist = reinterpret_cast<int*>(ws + lay.nlist);
+  float* totals = reinterpret_cast<float*>(ws + lay.totals);
+  const long long rows = B * (K + 1);
+  const int S = (int)cat_slices;
+  const float c = (float)(1.4426950408889634 / (double)temperature);  // log2(e) / T
+  cudaStream_t cs = as_stream(stream);
+  const bool bf = dtype == 0;
+  const void* tl = target_logits;
+  fm_status st;
+  // 1. slice maxima and approximate sums
+  st = bf ? launch_kernel(reject_scan_kernel<__nv_bfloat16>, dim3((unsigned)rows, (unsigned)S), dim3(RT), 0, cs, false,
+                          static_cast<const __nv_bfloat16*>(tl), (long long)V, c, S, slice_stats)
+          : launch_kernel(reject_scan_kernel<float>, dim3((unsigned)rows, (unsigned)S), dim3(RT), 0, cs, false,
+                          static_cast<const float*>(tl), (long long)V, c, S, slice_stats);
+  if (st) return st;
+  // 2. settled tests and the rows needing exact sums
+  const size_t dsmem = (size_t)(K > 0 ? K : 1) * sizeof(int);
+  if (dsmem > 48 * 1024) return set_error(FM_ERR_SHAPE, "accept: too many slots");
+  st = bf ? launch_kernel(reject_decide_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), dsmem, cs, false,
+                          static_cast<const __nv_bfloat16*>(tl), draft, q, (long long)V, (int)K, temperature, c, seed,
+                          offset, S, (const float2*)slice_stats, stats, list, nlist)
+          : launch_kernel(reject_decide_kernel<float>, dim3((unsigned)B), dim3(32), dsmem, cs, false,
+                          static_cast<const float*>(tl), draft, q, (long long)V, (int)K, temperature, c, seed, offset,
+                          S, (const float2*)slice_stats, stats, list, nlist);
+  if (st) return st;
+  // 3. exact slice totals of the listed rows
+  st = bf ? launch_kernel(reject_exact_kernel<__nv_bfloat16>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, false,
+                          static_cast<const __nv_bfloat16*>(tl), (long long)V, (int)K, temperature, S,
+                          (const float*)stats, (const int*)list, (const int*)nlist, exact)
+          : launch_kernel(reject_exact_kernel<float>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, false,
+                          static_cast<const float*>(tl), (long long)V, (int)K, temperature, S, (const float*)stats,
+                          (const int*)list, (const int*)nlist, exact);
+  if (st) return st;
+  // 4. open tests, accepted lengths, the bonus rows' exact sums
+  st = bf ? launch_kernel(reject_final_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), 0, cs, false,
+                          static_cast<const __nv_bfloat16*>(tl), draft, q, (long long)V, (int)K, temperature, seed,
+                          offset, S, (const int*)list, (const int*)nlist, (const float*)exact, stats, accepted)
+          : launch_kernel(reject_final_kernel<float>, dim3((unsigned)B), dim3(32), 0, cs, false,
+                          static_cast<const float*>(tl), draft, q, (long long)V, (int)K, temperature, seed, offset, S,
+                          (const int*)list, (const int*)nlist, (const float*)exact, stats, accepted);
   if (st) return st;
   st = FM_DISPATCH_LOGITS(dtype, residual_slices_kernel, dim3((unsigned)B, (unsigned)cat_slices), target_logits, q,
                           (long long)V, (int)K, temperature, (const float*)stats, (const int64_t*)accepted, totals);

@@ -133,8 +133,7 @@ size_t max_gemm_tiles(const fm_model_desc* m, const fm_plan_config* c) {
   int64_t mx = 0;
   auto upd = [&](int64_t M, int64_t N) {
     if (N <= 0) return;
-    const int bn = gemm_bn_for(N);
-    const int64_t t = ((M + 127) / 128) * ((N + bn - 1) / bn);
+    const int64_t t = gemm_counter_slots(M, N);
     if (t > mx) mx = t;
   };
   upd(S, T);

@@ -48,6 +48,7 @@ def lib():
         L.fmo_uniform.argtypes = [ctypes.c_uint64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32]
         L.fmo_philox.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint32)]
         L.fmo_row_stats.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float, _f32p, _f32p]
+        L.fmo_rejection_row_stats.argtypes = [_f32p, ctypes.c_int64, ctypes.c_float, _f32p, _f32p]
         L.fmo_argmax.restype = ctypes.c_int64
         L.fmo_argmax.argtypes = [_f32p, ctypes.c_int64]
         L.fmo_categorical.restype = ctypes.c_int64
@@ -108,6 +109,16 @@ def row_stats(row: torch.Tensor, temperature: float = 1.0):
     bits = _rows(row.reshape(-1))
     m, s = ctypes.c_float(), ctypes.c_float()
     lib().fmo_row_stats(_ptr(bits, _f32p), bits.size, float(temperature), ctypes.byref(m), ctypes.byref(s))
+    return m.value, s.value
+
+
+def rejection_row_stats(row: torch.Tensor, temperature: float = 1.0):
+    """(m, S) of a target row as the rejection step forms them: the max of
+    x / T and the slice-major fixed-order sum of fm_exp(x / T - m)."""
+    bits = _rows(row.reshape(-1))
+    m, s = ctypes.c_float(), ctypes.c_float()
+    lib().fmo_rejection_row_stats(_ptr(bits, _f32p), bits.size, float(temperature), ctypes.byref(m),
+                                  ctypes.byref(s))
     return m.value, s.value
 
 
@@ -181,6 +192,7 @@ __all__ = [
     "fm_exp_shifter",
     "fm_exp_shifter_sweep",
     "philox",
+    "rejection_row_stats",
     "row_stats",
     "sample_rows",
     "softmax_rows",

@@ -33,6 +33,10 @@
  *     first slice whose prefix exceeds it, and inside that slice the range and
  *     then the element are found as above, each running sum starting from the
  *     prefix of the slices before.
+ *   - the rejection step's row sums (fmo_rejection_row_stats) run slice-major
+ *     over the same 8192-element slices: in a slice, thread i sums its 4
+ *     vectors (slice start + u * 256 + i) in order, the slice total is the
+ *     warp tree above, and the slice totals are added in slice order.
  *
  * Philox4x32-10 follows Salmon, Moraes, Dror and Shaw, "Parallel random
  * numbers: as easy as 1, 2, 3" (SC'11): multipliers 0xD2511F53 and
@@ -219,6 +223,44 @@ static float row_sumexp(const float *row, int64_t V, float temperature, float m)
         part[i] = acc;
     }
     return tree_sum(part);
+}
+
+/* The rejection step's sum of fm_exp(x_v - m), in the slice-major order of
+ * the CUDA rejection kernels (ops.cu reject_exact_slice): slices of
+ * ACC_VPT * NT vectors of VEC; in a slice, thread i sums its ACC_VPT vectors
+ * (slice start + u * NT + i, u ascending) element by element, the slice total
+ * is the block tree, and the slice totals are added in slice order. */
+#define ACC_VPT 4
+static float row_sumexp_sliced(const float *row, int64_t V, float temperature, float m)
+{
+    int64_t nvec = (V + VEC - 1) / VEC;
+    int64_t slice_vecs = (int64_t)ACC_VPT * NT;
+    float total = 0.0f;
+    for (int64_t s0 = 0; s0 < nvec; s0 += slice_vecs) {
+        float part[NT];
+        for (int i = 0; i < NT; ++i) {
+            float acc = 0.0f;
+            for (int u = 0; u < ACC_VPT; ++u) {
+                int64_t vec = s0 + (int64_t)u * NT + i;
+                if (vec >= nvec) break;
+                for (int j = 0; j < VEC; ++j) {
+                    int64_t v = vec * VEC + j;
+                    if (v < V) acc = acc + fmo_exp(row[v] / temperature - m);
+                }
+            }
+            part[i] = acc;
+        }
+        total = total + tree_sum(part);
+    }
+    return total;
+}
+
+/* (m, S) of a target row in the rejection step (modeling_flashmap.py:583-594) */
+void fmo_rejection_row_stats(const float *row, int64_t V, float temperature, float *m_out, float *s_out)
+{
+    float m = row_max(row, V, temperature);
+    *m_out = m;
+    *s_out = row_sumexp_sliced(row, V, temperature, m);
 }
 
 void fmo_row_stats(const float *row, int64_t V, float temperature, float *m_out, float *s_out)
@@ -416,7 +458,7 @@ void fmo_accept_rejection(const float *target, const int64_t *draft, const float
         for (; acc < K; ++acc) {
             const float *row = target + (b * (K + 1) + acc) * V;
             float m, s;
-            fmo_row_stats(row, V, temperature, &m, &s);
+            fmo_rejection_row_stats(row, V, temperature, &m, &s);
             int64_t d = draft[b * K + acc];
             float p = fmo_exp(row[d] / temperature - m) / s;
             float qd = q[(b * K + acc) * V + d];
@@ -426,7 +468,7 @@ void fmo_accept_rejection(const float *target, const int64_t *draft, const float
         accepted[b] = acc;
         const float *row = target + (b * (K + 1) + acc) * V;
         float m, s;
-        fmo_row_stats(row, V, temperature, &m, &s);
+        fmo_rejection_row_stats(row, V, temperature, &m, &s);
         int any = 0;
         for (int64_t v = 0; v < V; ++v) {
             float pv = fmo_exp(row[v] / temperature - m) / s;
