@@ -141,7 +141,16 @@ int64_t resident_pairs(GemmKernel k, size_t smem) {
 // unit count.  Wide blocks (BN >= 64, finished by their head from staged
 // partials) are split over at most 2 groups per tile when that still occupies
 // half the groups (each head then stages one partial), else over at most 8
-// (FM_GEMM_MAX_SPLIT overrides the cap for tuning experiments).  Returns CTAs.
+// (FM_GEMM_MAX_SPLIT overrides the cap for tuning experiments).
+//
+// Long reductions (K >= 512 k-blocks, the state vocabulary's E_S^T GEMMs)
+// with about as many tiles as groups take whole tiles instead: the grid is
+// the largest divisor of the tile count that fits, every group starts its
+// tiles at k = 0, and the groups advance through K together, so each k-block
+// of A and B is read from DRAM once and served to the other tiles from L2
+// (stream-K would start every group at its own k offset, and the
+// vocabulary-sized B panel, larger than L2, would be re-read per m-tile).
+// Returns CTAs.
 static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64_t cap_groups) {
   static const int per_sm = [] {
     const char* e = getenv("FM_GEMM_CTAS_PER_SM");
@@ -154,6 +163,11 @@ static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64
     return v >= 1 && v <= 8 ? v : 0;
   }();
   const int64_t avail = cg == 2 ? cap_groups : (int64_t)num_sms() * per_sm;
+  const int64_t kb = tiles > 0 ? units / tiles : 0;
+  if (kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
+    for (int64_t g = avail < tiles ? avail : tiles; g * 4 >= avail * 3; --g)
+      if (tiles % g == 0) return g * cg;
+  }
   int64_t g = avail;
   if (bn >= 64) {
     const int64_t max_split = split_env ? split_env : (tiles * 2 >= avail / 2 ? 2 : 8);

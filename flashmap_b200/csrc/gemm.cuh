@@ -467,6 +467,39 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     // rows 64..127 of the tile are the "up" halves of features mt*64 + (r - 64)
+    if (vec_epilogue_ok(a)) {
+      // every thread stages its 16 rounded values in a [16 tokens][128 rows]
+      // bf16 tile, then computes 8 outputs (one token, 8 consecutive
+      // features) and stores them as one 16-byte vector
+      __nv_bfloat16* xt = reinterpret_cast<__nv_bfloat16*>(xch);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) xt[j * 128 + r] = f2bf(v[j]);
+      named_bar_sync(1, 128);
+      const int t = threadIdx.x - 64, jj = t >> 3, f0 = (t & 7) * 8;
+      const int n = n0 + jj, F = mt * 64 + f0;
+      if (n < a.N && F < a.M / 2) {
+        const uint4 gw = *reinterpret_cast<const uint4*>(xt + jj * 128 + f0);
+        const uint4 uw = *reinterpret_cast<const uint4*>(xt + jj * 128 + 64 + f0);
+        const uint32_t g4[4] = {gw.x, gw.y, gw.z, gw.w}, u4[4] = {uw.x, uw.y, uw.z, uw.w};
+        uint32_t o4[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float o[2];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const float gt = __uint_as_float(h ? (g4[i] & 0xffff0000u) : (g4[i] << 16));
+            const float ut = __uint_as_float(h ? (u4[i] & 0xffff0000u) : (u4[i] << 16));
+            const float s = round_bf(__fdiv_rn(gt, __fadd_rn(1.0f, expf(-gt))));
+            o[h] = __fmul_rn(s, ut);
+          }
+          const __nv_bfloat162 pr = __floats2bfloat162_rn(o[0], o[1]);
+          o4[i] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        *reinterpret_cast<uint4*>(a.out + (long long)n * a.ldo + F) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+      }
+      named_bar_sync(1, 128);  // the exchange tile is refilled by the next chunk
+      return;
+    }
     if (r >= 64) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) xch[(r - 64) * 16 + j] = round_bf(v[j]);
@@ -1100,6 +1133,12 @@ __global__ void __launch_bounds__(192, 1)
             uint4 vp[2];
             constexpr bool RESID_RING = EPI == EPI_RESID && S::RING_BYTES > 0;
             constexpr int NCH = BN / 16;
+            // residual epilogue with every partial staged in one round: the
+            // whole residual tile ([BN / 16 chunks][16][128] bf16) follows the
+            // partials in the idle buffers, all of it requested at once
+            const bool preload =
+                vec && RESID_RING && cols == BN && (long long)others * BN * 512 + BN * 256 <= (long long)AREA;
+            __nv_bfloat16* res_tile = reinterpret_cast<__nv_bfloat16*>(stage + (long long)others * BN * 128);
             for (int col0 = 0, round = 0; cols <= BN && col0 < BN; col0 += cols, ++round) {
               const int ncols = (BN - col0) < cols ? (BN - col0) : cols;
               if (threadIdx.x == 64) {
@@ -1113,10 +1152,13 @@ __global__ void __launch_bounds__(192, 1)
                 // the epilogue's own global reads go out after the partials' bulk copies
                 have = !vec && !qk_wide && epilogue_prefetch<EPI>(a, m, n0, pre);
                 if (vec && !RESID_RING) vec_prefetch<EPI>(a, mt * 128, n0, vp);
-                if (vec && RESID_RING)
+                if (preload) {
+                  for (int pc = 0; pc < NCH; ++pc) vec_issue(a, mt * 128, n0 + pc * 16, res_tile + pc * 2048, true);
+                } else if (vec && RESID_RING) {
 #pragma unroll
                   for (int pc = 0; pc < S::RING - 1; ++pc)
                     vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
+                }
               }
               if (threadIdx.x == 64) {
                 flags[1] = mbar_wait(fix_bar, (uint32_t)round & 1u, nullptr) ? 1 : 0;
@@ -1125,6 +1167,7 @@ __global__ void __launch_bounds__(192, 1)
                   *abort_flag = 1;
                 }
               }
+              if (preload && round == 0) gemm_cp_wait<0>();  // this thread's residual copies
               named_bar_sync(1, 128);
               if (!flags[1]) {
                 staged_ok = false;
@@ -1158,7 +1201,7 @@ __global__ void __launch_bounds__(192, 1)
                     have && c0 + 16 < BN && epilogue_prefetch<EPI>(a, m, n0 + c0 + 16, nxt);
                 const int ci = c0 / 16;
                 if (vec && !RESID_RING && c0 + 16 < BN) vec_prefetch<EPI>(a, mt * 128, n0 + c0 + 16, vn);
-                if (vec && RESID_RING) {
+                if (vec && RESID_RING && !preload) {
                   const int pc = ci + S::RING - 1;
                   vec_issue(a, mt * 128, n0 + pc * 16, ring + (pc % S::RING) * 2048, pc < NCH);
                   gemm_cp_wait<S::RING - 1>();
@@ -1172,7 +1215,9 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                   for (int j = 0; j < 16; ++j) v[j] = __fadd_rn(v[j], src[j * 128]);
                 }
-                if (vec && RESID_RING) {
+                if (preload) {
+                  vec_resid16(a, v, r, mt * 128, n0 + c0, res_tile + ci * 2048);
+                } else if (vec && RESID_RING) {
                   named_bar_sync(1, 128);  // every thread's copies of chunk ci have landed
                   vec_resid16(a, v, r, mt * 128, n0 + c0, ring + (ci % S::RING) * 2048);
                 } else if (vec) {

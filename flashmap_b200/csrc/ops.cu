@@ -383,6 +383,12 @@ __device__ __forceinline__ int lane_load(const __nv_bfloat16* row, int nch, int 
   return n;
 }
 constexpr int WIDE_CHUNKS = 24;  // rows of up to 6144 columns
+// Wide rows read their per-column weights (RMSNorm weight, AdaLN scale and
+// shift) WIDE_GROUP chunks at a time, all of a group's 16-byte loads issued
+// before its outputs are stored: read-only loads, so the compiler need not
+// order them after the stores (the output may not alias a weight)
+constexpr int WIDE_GROUP = 8;
+__device__ __forceinline__ uint4 ldg16(const __nv_bfloat16* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
 __device__ __forceinline__ void rms_row_wide(const __nv_bfloat16* xr, const __nv_bfloat16* w, __nv_bfloat16* yr,
                                              int cols, float eps, int lane) {
@@ -401,16 +407,23 @@ __device__ __forceinline__ void rms_row_wide(const __nv_bfloat16* xr, const __nv
     }
   const float inv = inv_rms(warp_allsum(s), cols, eps);
 #pragma unroll
-  for (int i = 0; i < WIDE_CHUNKS; ++i)
-    if (i < n) {
-      const int ch = lane + 32 * i;
-      float xf[8], wf[8], o[8];
-      unpack_bf16x8(xv[i], xf);
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(w + ch * 8), wf);
+  for (int g0 = 0; g0 < WIDE_CHUNKS; g0 += WIDE_GROUP) {
+    uint4 wv[WIDE_GROUP];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = rms_value(xf[e], wf[e], inv);
-      *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
-    }
+    for (int i = 0; i < WIDE_GROUP; ++i)
+      if (g0 + i < n) wv[i] = ldg16(w + (lane + 32 * (g0 + i)) * 8);
+#pragma unroll
+    for (int i = 0; i < WIDE_GROUP; ++i)
+      if (g0 + i < n) {
+        const int ch = lane + 32 * (g0 + i);
+        float xf[8], wf[8], o[8];
+        unpack_bf16x8(xv[g0 + i], xf);
+        unpack_bf16x8(wv[i], wf);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rms_value(xf[e], wf[e], inv);
+        *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
+      }
+  }
 }
 
 __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, const __nv_bfloat16* w,
@@ -540,17 +553,28 @@ __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const
       }
     const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_allsum(q), (float)cols), eps)));
 #pragma unroll
-    for (int i = 0; i < WIDE_CHUNKS; ++i)
-      if (i < n) {
-        const int ch = lane + 32 * i;
-        float xf[8], sc[8], sh[8], o[8];
-        unpack_bf16x8(xv[i], xf);
-        unpack_bf16x8(*reinterpret_cast<const uint4*>(mod + ch * 8), sc);
-        unpack_bf16x8(*reinterpret_cast<const uint4*>(mod + cols + ch * 8), sh);
+    for (int g0 = 0; g0 < WIDE_CHUNKS; g0 += WIDE_GROUP) {
+      uint4 sv[WIDE_GROUP], hv[WIDE_GROUP];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
-        *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
-      }
+      for (int i = 0; i < WIDE_GROUP; ++i)
+        if (g0 + i < n) {
+          const int ch = lane + 32 * (g0 + i);
+          sv[i] = ldg16(mod + ch * 8);
+          hv[i] = ldg16(mod + cols + ch * 8);
+        }
+#pragma unroll
+      for (int i = 0; i < WIDE_GROUP; ++i)
+        if (g0 + i < n) {
+          const int ch = lane + 32 * (g0 + i);
+          float xf[8], sc[8], sh[8], o[8];
+          unpack_bf16x8(xv[g0 + i], xf);
+          unpack_bf16x8(sv[i], sc);
+          unpack_bf16x8(hv[i], sh);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
+          *reinterpret_cast<uint4*>(yr + ch * 8) = pack_bf16x8(o);
+        }
+    }
     return;
   }
   float mean, rstd;
@@ -1292,14 +1316,14 @@ __device__ __forceinline__ void slice_scan(const RejectionRow<T>& w, long long V
 // block_sum's tree, and the slice totals are added in slice order (the C
 // oracle's row_sumexp_sliced).  fm_exp costs ~18 instructions per element, so
 // the exact sum is formed only for the rows whose outcome needs it:
-//   1. reject_scan_kernel, CTA (row, slice): the slice's raw maximum (exact)
-//      and an approximate sum of 2^((x - max) log2(e) / T) by ex2.approx, in
-//      one read of the slice;
+//   1. reject_scan_kernel, CTA (row, chunk of 16384): the chunk's raw maximum
+//      (exact) and an approximate sum of 2^((x - max) log2(e) / T) by a
+//      polynomial exp2_poly2 (relative error under 5e-6), in one read;
 //   2. reject_decide_kernel, one warp per request: each row's m (exact) and
 //      approximate S'; a test u q < p is settled from p' = e / S' when u q lies
 //      outside p' (1 -+ 2^-10), since S' and S differ by far less (fm_exp's
-//      1-ulp error, ex2.approx's relative error below 2^-21, under a hundred
-//      rounded additions of positive terms); otherwise it stays open.  Listed
+//      1-ulp error, exp2_poly2's 5e-6 per term and per chunk merge, a few
+//      hundred rounded additions of positive terms); otherwise it stays open.  Listed
 //      for the exact sum: the open tests before the first settled rejection,
 //      then the bonus row (that rejection, or row K);
 //   3. reject_exact_kernel, CTA (request, slice): the listed rows' exact slice totals;
@@ -1310,56 +1334,86 @@ constexpr long long REJ_SLICE_VECS = (long long)REJ_VPT * RT;
 static_assert(REJ_SLICE_VECS * 8 == CAT_SLICE, "one slicing for the sums and the bonus draw");
 constexpr float REJ_MARGIN = 9.765625e-4f;  // 2^-10
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
+// 2^y of two lanes, y <= 0, for the approximate sums: y clamped at -125 (a
+// term below 2^-124 is invisible in a sum whose largest term is 1), n = rint(y)
+// by the 1.5 * 2^23 shifter, f = y - n in [-1/2, 1/2], 2^f by the degree-5
+// Taylor polynomial of e^(f ln 2) (remainder below (ln2 / 2)^6 / 720 * 2^(1/2)
+// = 3.4e-6 of 2^f >= 2^(-1/2): relative error under 5e-6), 2^n from n's bits
+// as in fm_exp2.  Packed fp32x2 arithmetic throughout.
+__device__ __forceinline__ float2 exp2_poly2(float2 y) {
+  y = make_float2(fmaxf(y.x, -125.0f), fmaxf(y.y, -125.0f));
+  const float2 t = __fadd2_rn(y, make_float2(12582912.0f, 12582912.0f));
+  const float2 n = __fadd2_rn(t, make_float2(-12582912.0f, -12582912.0f));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), y);
+  float2 p = __ffma2_rn(make_float2(1.3333558e-3f, 1.3333558e-3f), f, make_float2(9.6181291e-3f, 9.6181291e-3f));
+  p = __ffma2_rn(p, f, make_float2(5.5504109e-2f, 5.5504109e-2f));
+  p = __ffma2_rn(p, f, make_float2(2.4022651e-1f, 2.4022651e-1f));
+  p = __ffma2_rn(p, f, make_float2(6.9314718e-1f, 6.9314718e-1f));
+  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+  const uint32_t b0 = __float_as_uint(t.x), b1 = __float_as_uint(t.y);
+  return __fmul2_rn(p, make_float2(__uint_as_float((b0 << 23) + 0x3F800000u), __uint_as_float((b1 << 23) + 0x3F800000u)));
 }
 
+// Scan chunks of REJ_SCAN_VECS vectors (16384 elements): each thread's 8
+// vectors in registers, its own maximum and its sum relative to it, then one
+// block merge of the (max, sum) pairs -> (chunk max, approximate chunk sum).
+constexpr int REJ_SCAN_VPT = 8;
+constexpr long long REJ_SCAN_VECS = (long long)REJ_SCAN_VPT * RT;
+
 template <typename T>
-__global__ void __launch_bounds__(RT) reject_scan_kernel(const T* logits, long long V, float c, int S,
-                                                         float2* slice_stats) {
+__global__ void __launch_bounds__(RT) reject_scan_kernel(const T* logits, long long V, float c, int C,
+                                                         float2* chunk_stats) {
   pdl_wait();
   pdl_launch_dependents();
   __shared__ float red[16];
   const T* row = logits + (long long)blockIdx.x * V;
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
-  const long long nvec = (V + 7) / 8;
-  const long long v0 = (long long)blockIdx.y * REJ_SLICE_VECS + threadIdx.x;
-  Raw8<T> x[REJ_VPT];
+  const long long nvec = (V + 7) / 8, nfull = V / 8;
+  const long long v0 = (long long)blockIdx.y * REJ_SCAN_VECS + threadIdx.x;
+  Raw8<T> x[REJ_SCAN_VPT];
 #pragma unroll
-  for (int u = 0; u < REJ_VPT; ++u)
+  for (int u = 0; u < REJ_SCAN_VPT; ++u)
     if (v0 + u * RT < nvec) x[u].load(row, v0 + u * RT, V, aligned);
-  float mx = -INFINITY;
+  float mt = -INFINITY;
 #pragma unroll
-  for (int u = 0; u < REJ_VPT; ++u) {
+  for (int u = 0; u < REJ_SCAN_VPT; ++u) {
     const long long vec = v0 + u * RT;
     if (vec >= nvec) break;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 p = x[u].pair(i);
-      if (vec * 8 + 2 * i < V) mx = fmaxf(mx, p.x);
-      if (vec * 8 + 2 * i + 1 < V) mx = fmaxf(mx, p.y);
+      const bool full = vec < nfull;
+      if (full || vec * 8 + 2 * i < V) mt = fmaxf(mt, p.x);
+      if (full || vec * 8 + 2 * i + 1 < V) mt = fmaxf(mt, p.y);
     }
   }
-  mx = block_max(mx, red);
-  float acc = 0.0f;
-  if (mx > -INFINITY && mx < INFINITY) {
-    const float off = -mx * c;
+  float st = 0.0f;
+  if (mt > -INFINITY && mt < INFINITY) {
+    const float off = -mt * c;
+    const float2 c2 = make_float2(c, c), off2 = make_float2(off, off);
+    float2 acc2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-    for (int u = 0; u < REJ_VPT; ++u) {
+    for (int u = 0; u < REJ_SCAN_VPT; ++u) {
       const long long vec = v0 + u * RT;
       if (vec >= nvec) break;
+      if (vec < nfull) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 p = x[u].pair(i);
-        if (vec * 8 + 2 * i < V) acc += ex2_approx(fmaf(p.x, c, off));
-        if (vec * 8 + 2 * i + 1 < V) acc += ex2_approx(fmaf(p.y, c, off));
+        for (int i = 0; i < 4; ++i) acc2 = __fadd2_rn(acc2, exp2_poly2(__ffma2_rn(x[u].pair(i), c2, off2)));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 e = exp2_poly2(__ffma2_rn(x[u].pair(i), c2, off2));
+          if (vec * 8 + 2 * i < V) acc2.x += e.x;
+          if (vec * 8 + 2 * i + 1 < V) acc2.y += e.y;
+        }
       }
     }
+    st = acc2.x + acc2.y;
   }
-  acc = block_sum(acc, red);
-  if (threadIdx.x == 0) slice_stats[(long long)blockIdx.x * S + blockIdx.y] = make_float2(mx, acc);
+  const float M = block_max(mt, red);
+  const float scaled = (st > 0.0f && M < INFINITY) ? st * exp2_poly2(make_float2((mt - M) * c, 0.0f)).x : 0.0f;
+  const float S = block_sum(scaled, red);
+  if (threadIdx.x == 0) chunk_stats[(long long)blockIdx.x * C + blockIdx.y] = make_float2(M, S);
 }
 
 // list[b * (K + 1) + i], i < nlist[b]: rows of request b in ascending order;
@@ -1367,8 +1421,8 @@ __global__ void __launch_bounds__(RT) reject_scan_kernel(const T* logits, long l
 template <typename T>
 __global__ void __launch_bounds__(32) reject_decide_kernel(const T* target, const int64_t* draft, const float* q,
                                                            long long V, int K, float temperature, float c,
-                                                           uint64_t seed, uint32_t offset, int S,
-                                                           const float2* slice_stats, float* stats, int* list,
+                                                           uint64_t seed, uint32_t offset, int C,
+                                                           const float2* chunk_stats, float* stats, int* list,
                                                            int* nlist) {
   pdl_wait();
   pdl_launch_dependents();
@@ -1377,9 +1431,9 @@ __global__ void __launch_bounds__(32) reject_decide_kernel(const T* target, cons
   const bool unit_t = temperature == 1.0f;
   for (int k = lane; k <= K; k += 32) {
     const long long row = (long long)b * (K + 1) + k;
-    const float2* ss = slice_stats + row * S;
+    const float2* ss = chunk_stats + row * C;
     float M = -INFINITY;
-    for (int j = 0; j < S; ++j) M = fmaxf(M, ss[j].x);
+    for (int j = 0; j < C; ++j) M = fmaxf(M, ss[j].x);
     // max of x / T is the rounded quotient of the raw max (division by T > 0 keeps order)
     const float m = unit_t ? M : __fdiv_rn(M, temperature);
     stats[2 * row] = m;
@@ -1387,8 +1441,8 @@ __global__ void __launch_bounds__(32) reject_decide_kernel(const T* target, cons
     int st = 2;
     if (M > -INFINITY && M < INFINITY) {
       float sa = 0.0f;
-      for (int j = 0; j < S; ++j)
-        if (ss[j].y > 0.0f) sa += ss[j].y * ex2_approx((ss[j].x - M) * c);
+      for (int j = 0; j < C; ++j)
+        if (ss[j].y > 0.0f) sa += ss[j].y * exp2_poly2(make_float2((ss[j].x - M) * c, 0.0f)).x;
       const long long d = draft[(long long)b * K + k];
       const float xd = to_f(target[row * V + d]);
       const float e = fm_exp(__fsub_rn(unit_t ? xd : __fdiv_rn(xd, temperature), m));
@@ -1455,7 +1509,7 @@ __device__ __forceinline__ float reject_exact_slice(const T* row, long long V, f
 
 // CTA (b, s): slice s of each listed row of request b -> exact[b * (K + 1) + i][s]
 template <typename T>
-__global__ void __launch_bounds__(RT) reject_exact_kernel(const T* target, long long V, int K, float temperature,
+__global__ void __launch_bounds__(RT, 5) reject_exact_kernel(const T* target, long long V, int K, float temperature,
                                                              int S, const float* stats, const int* list,
                                                              const int* nlist, float* exact) {
   pdl_wait();
@@ -1936,6 +1990,12 @@ namespace {
                                 static_cast<const __nv_bfloat16*>(ptr), __VA_ARGS__)                           \
                 : launch_kernel(KERNEL<float>, grid, dim3(RT), 0, as_stream(stream), false,                   \
                                 static_cast<const float*>(ptr), __VA_ARGS__))
+// the same with programmatic dependent launch (kernels that call pdl_wait() before any read)
+#define FM_DISPATCH_LOGITS_PDL(dtype, KERNEL, grid, ptr, ...)                                                  \
+  ((dtype) == 0 ? launch_kernel(KERNEL<__nv_bfloat16>, grid, dim3(RT), 0, as_stream(stream), true,             \
+                                static_cast<const __nv_bfloat16*>(ptr), __VA_ARGS__)                           \
+                : launch_kernel(KERNEL<float>, grid, dim3(RT), 0, as_stream(stream), true,                    \
+                                static_cast<const float*>(ptr), __VA_ARGS__))
 bool bad_dtype(int32_t d) { return d != 0 && d != 1; }
 
 // greedy acceptance through the sliced argmax: zero the keys, slice kernel, accept
@@ -2050,42 +2110,43 @@ extern "C" fm_status fm_accept_rejection(const void* target_logits, int32_t dtyp
   const bool bf = dtype == 0;
   const void* tl = target_logits;
   fm_status st;
-  // 1. slice maxima and approximate sums
-  st = bf ? launch_kernel(reject_scan_kernel<__nv_bfloat16>, dim3((unsigned)rows, (unsigned)S), dim3(RT), 0, cs, false,
-                          static_cast<const __nv_bfloat16*>(tl), (long long)V, c, S, slice_stats)
-          : launch_kernel(reject_scan_kernel<float>, dim3((unsigned)rows, (unsigned)S), dim3(RT), 0, cs, false,
-                          static_cast<const float*>(tl), (long long)V, c, S, slice_stats);
+  // 1. chunk maxima and approximate sums
+  const int C = (int)(((V + 7) / 8 + REJ_SCAN_VECS - 1) / REJ_SCAN_VECS);
+  st = bf ? launch_kernel(reject_scan_kernel<__nv_bfloat16>, dim3((unsigned)rows, (unsigned)C), dim3(RT), 0, cs, true,
+                          static_cast<const __nv_bfloat16*>(tl), (long long)V, c, C, slice_stats)
+          : launch_kernel(reject_scan_kernel<float>, dim3((unsigned)rows, (unsigned)C), dim3(RT), 0, cs, true,
+                          static_cast<const float*>(tl), (long long)V, c, C, slice_stats);
   if (st) return st;
   // 2. settled tests and the rows needing exact sums
   const size_t dsmem = (size_t)(K > 0 ? K : 1) * sizeof(int);
   if (dsmem > 48 * 1024) return set_error(FM_ERR_SHAPE, "accept: too many slots");
-  st = bf ? launch_kernel(reject_decide_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), dsmem, cs, false,
+  st = bf ? launch_kernel(reject_decide_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), dsmem, cs, true,
                           static_cast<const __nv_bfloat16*>(tl), draft, q, (long long)V, (int)K, temperature, c, seed,
-                          offset, S, (const float2*)slice_stats, stats, list, nlist)
-          : launch_kernel(reject_decide_kernel<float>, dim3((unsigned)B), dim3(32), dsmem, cs, false,
+                          offset, C, (const float2*)slice_stats, stats, list, nlist)
+          : launch_kernel(reject_decide_kernel<float>, dim3((unsigned)B), dim3(32), dsmem, cs, true,
                           static_cast<const float*>(tl), draft, q, (long long)V, (int)K, temperature, c, seed, offset,
-                          S, (const float2*)slice_stats, stats, list, nlist);
+                          C, (const float2*)slice_stats, stats, list, nlist);
   if (st) return st;
   // 3. exact slice totals of the listed rows
-  st = bf ? launch_kernel(reject_exact_kernel<__nv_bfloat16>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, false,
+  st = bf ? launch_kernel(reject_exact_kernel<__nv_bfloat16>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, true,
                           static_cast<const __nv_bfloat16*>(tl), (long long)V, (int)K, temperature, S,
                           (const float*)stats, (const int*)list, (const int*)nlist, exact)
-          : launch_kernel(reject_exact_kernel<float>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, false,
+          : launch_kernel(reject_exact_kernel<float>, dim3((unsigned)B, (unsigned)S), dim3(RT), 0, cs, true,
                           static_cast<const float*>(tl), (long long)V, (int)K, temperature, S, (const float*)stats,
                           (const int*)list, (const int*)nlist, exact);
   if (st) return st;
   // 4. open tests, accepted lengths, the bonus rows' exact sums
-  st = bf ? launch_kernel(reject_final_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), 0, cs, false,
+  st = bf ? launch_kernel(reject_final_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(32), 0, cs, true,
                           static_cast<const __nv_bfloat16*>(tl), draft, q, (long long)V, (int)K, temperature, seed,
                           offset, S, (const int*)list, (const int*)nlist, (const float*)exact, stats, accepted)
-          : launch_kernel(reject_final_kernel<float>, dim3((unsigned)B), dim3(32), 0, cs, false,
+          : launch_kernel(reject_final_kernel<float>, dim3((unsigned)B), dim3(32), 0, cs, true,
                           static_cast<const float*>(tl), draft, q, (long long)V, (int)K, temperature, seed, offset, S,
                           (const int*)list, (const int*)nlist, (const float*)exact, stats, accepted);
   if (st) return st;
-  st = FM_DISPATCH_LOGITS(dtype, residual_slices_kernel, dim3((unsigned)B, (unsigned)cat_slices), target_logits, q,
+  st = FM_DISPATCH_LOGITS_PDL(dtype, residual_slices_kernel, dim3((unsigned)B, (unsigned)cat_slices), target_logits, q,
                           (long long)V, (int)K, temperature, (const float*)stats, (const int64_t*)accepted, totals);
   if (st) return st;
-  return FM_DISPATCH_LOGITS(dtype, residual_pick_kernel, dim3((unsigned)B), target_logits, q, (long long)V, (int)K,
+  return FM_DISPATCH_LOGITS_PDL(dtype, residual_pick_kernel, dim3((unsigned)B), target_logits, q, (long long)V, (int)K,
                             temperature, seed, offset, (const float*)stats, (const int64_t*)accepted,
                             (const float*)totals, bonus);
 }

@@ -81,6 +81,8 @@ GEMM_SHAPES = [
     # 256-token blocks on CTA pairs (256 x 256 tiles): config-5 shapes, a pair
     # tile whose second half lies past M, ragged token tails in either half
     (7680, 1024, 2560), (2560, 1024, 2560), (13824, 1024, 2560), (130, 1000, 640), (5120, 257, 2560),
+    # long reductions (>= 512 k-blocks) on whole tiles, all groups advancing through K together
+    (4096, 1024, 32768), (14336, 100, 32768),
 ]
 
 
@@ -97,8 +99,11 @@ def test_gemm_store_bias(M, N, K):
     assert int(err.item()) == 0
     # near a rounding boundary the fp32 sums of two summation orders may round apart
     near = ((acc - ref.float()).abs() > 0.45 * bf16_ulp(acc)).float().mean().item()
-    assert_close_scaled(out, ref, ulps=1, atol_frac=1e-5, what=f"gemm {M}x{N}x{K} (near-boundary {near:.4f})")
-    assert (out == ref).float().mean().item() > 0.98
+    # the two orders' fp32 sums drift apart further as K grows (one accumulator
+    # over K / 16 tensor-core steps here): the absolute floor scales with K past 8192
+    long_k = max(1.0, K / 8192)
+    assert_close_scaled(out, ref, ulps=1, atol_frac=1e-5 * long_k, what=f"gemm {M}x{N}x{K} (near-boundary {near:.4f})")
+    assert (out == ref).float().mean().item() > (0.98 if long_k == 1.0 else 0.95)
 
 
 @pytest.mark.parametrize("M,N,K", [(2048, 16, 2048), (3000, 17, 320), (1024, 200, 512), (256, 96, 4096),
