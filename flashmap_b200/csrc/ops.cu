@@ -471,6 +471,53 @@ __global__ void __launch_bounds__(RT) rmsnorm_kernel(const __nv_bfloat16* x, con
   for (int c = lane; c < cols; c += 32) yr[c] = f2bf(rms_value(bf2f(xr[c]), bf2f(w[c]), inv));
 }
 
+// AdaLN of a row of up to NC * 256 columns with the row, scale and shift
+// all loaded before the statistics (one round trip): NC = 8 for rows up to
+// 2048, NC = 12 up to 3072 (the 27B map's 2560).
+template <int NC>
+__device__ __forceinline__ void adaln_row_upfront(const __nv_bfloat16* xr, const __nv_bfloat16* mod,
+                                                  __nv_bfloat16* yr, int cols, float eps, int lane) {
+  const int nch = cols / 8;
+  uint4 xv[NC], sv[NC], hv[NC];
+  const int n = lane_load<NC>(xr, nch, lane, xv);
+  lane_load<NC>(mod, nch, lane, sv);
+  lane_load<NC>(mod + cols, nch, lane, hv);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+    if (i < n) {
+      float xf[8];
+      unpack_bf16x8(xv[i], xf);
+      s = __fadd_rn(s, chunk_tree(xf, 8));
+    }
+  const float mean = __fdiv_rn(warp_allsum(s), (float)cols);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+    if (i < n) {
+      float xf[8], t[8];
+      unpack_bf16x8(xv[i], xf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = __fsub_rn(xf[e], mean);
+        t[e] = __fmul_rn(d, d);
+      }
+      q = __fadd_rn(q, chunk_tree(t, 8));
+    }
+  const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_allsum(q), (float)cols), eps)));
+#pragma unroll
+  for (int i = 0; i < NC; ++i)
+    if (i < n) {
+      float xf[8], sc[8], sh[8], o[8];
+      unpack_bf16x8(xv[i], xf);
+      unpack_bf16x8(sv[i], sc);
+      unpack_bf16x8(hv[i], sh);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
+      *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
+    }
+}
+
 // AdaLN of one row per warp: LayerNorm statistics, then the modulated output
 // (mod = [scale | shift], each `cols` wide)
 __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const __nv_bfloat16* mod,
@@ -483,45 +530,11 @@ __global__ void __launch_bounds__(RT) adaln_kernel(const __nv_bfloat16* x, const
   const __nv_bfloat16* xr = x + r * cols;
   __nv_bfloat16* yr = y + r * cols;
   if (cols % 8 == 0 && cols <= 2048 && vec_ok(xr) && vec_ok(yr) && vec_ok(mod)) {
-    const int nch = cols / 8;
-    uint4 xv[8], sv[8], hv[8];
-    const int n = lane_load8(xr, nch, lane, xv);
-    lane_load8(mod, nch, lane, sv);
-    lane_load8(mod + cols, nch, lane, hv);
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < n) {
-        float xf[8];
-        unpack_bf16x8(xv[i], xf);
-        s = __fadd_rn(s, chunk_tree(xf, 8));
-      }
-    const float mean = __fdiv_rn(warp_allsum(s), (float)cols);
-    float q = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < n) {
-        float xf[8], t[8];
-        unpack_bf16x8(xv[i], xf);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float d = __fsub_rn(xf[e], mean);
-          t[e] = __fmul_rn(d, d);
-        }
-        q = __fadd_rn(q, chunk_tree(t, 8));
-      }
-    const float rstd = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(warp_allsum(q), (float)cols), eps)));
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < n) {
-        float xf[8], sc[8], sh[8], o[8];
-        unpack_bf16x8(xv[i], xf);
-        unpack_bf16x8(sv[i], sc);
-        unpack_bf16x8(hv[i], sh);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = adaln_value(xf[e], mean, rstd, sc[e], sh[e]);
-        *reinterpret_cast<uint4*>(yr + (lane + 32 * i) * 8) = pack_bf16x8(o);
-      }
+    adaln_row_upfront<8>(xr, mod, yr, cols, eps, lane);
+    return;
+  }
+  if (cols % 8 == 0 && cols <= 3072 && vec_ok(xr) && vec_ok(yr) && vec_ok(mod)) {
+    adaln_row_upfront<12>(xr, mod, yr, cols, eps, lane);
     return;
   }
   if (cols % 8 == 0 && cols <= 32 * 8 * WIDE_CHUNKS && vec_ok(xr) && vec_ok(yr) && vec_ok(mod)) {
