@@ -193,8 +193,8 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // of A (its 128 rows) and half of B (N / 2 rows) at the same shared-memory
 // offsets, and its 128 rows of the accumulator in its own TMEM.  The even CTA
 // (rank 0) issues the MMAs; both CTAs' TMA copies complete on rank 0's
-// barrier.  Every load is a plain (non-multicast) copy into the issuing CTA's
-// own shared memory.
+// barrier.  Every load is a plain copy into the issuing CTA's own shared
+// memory.
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
