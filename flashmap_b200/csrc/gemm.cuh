@@ -74,7 +74,8 @@ struct GemmArgs {
 
 // Trace slots per CTA: 0 entry, 1 setup done, then per segment s < 3:
 // 2+4s MMA issue done, 3+4s accumulator seen by the epilogue, 4+4s partial
-// written / epilogue done, 5+4s split fix-up done; 14 exit.
+// written / epilogue done, 5+4s split fix-up done; 14 exit; 15 the head's
+// staged partials landed (first round).
 constexpr int GEMM_TRACE = 16;
 __device__ __forceinline__ void gemm_stamp(unsigned long long* trace, int slot) {
   if (trace) trace[(long long)blockIdx.x * GEMM_TRACE + slot] = global_ns();
@@ -1166,6 +1167,7 @@ __global__ void __launch_bounds__(192, 1)
                   record_error(a.err, DEV_TIMEOUT_OTHER);
                   *abort_flag = 1;
                 }
+                if (round == 0) gemm_stamp(trace, 15);
               }
               if (preload && round == 0) gemm_cp_wait<0>();  // this thread's residual copies
               named_bar_sync(1, 128);
