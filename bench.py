@@ -35,6 +35,7 @@ from __future__ import annotations
 import argparse
 import datetime
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -630,6 +631,167 @@ def measure_config3(args, world, rank):
     return line
 
 
+OPS_REF = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+
+
+def ops_cases(dev, sglang_kernels, vllm_kernels, ours: bool):
+    """The serving operators at a serving batch of the config-2 map (64
+    requests x 16 slots = 1024 token rows, 16 heads x 128, 8 layers; 4096 new
+    context tokens into 16-token pages; greedy rows over a 151936-token
+    vocabulary), seeded alike on both sides.  Returns name -> callable."""
+    g = torch.Generator(device=dev).manual_seed(11)
+    bf = torch.bfloat16
+    T, H, hd, L, eps = 1024, 16, 128, 8, 1e-6
+    rope = vllm_kernels.rope_table(4096, hd, 1e6, dev)  # each side's own table builder
+    x = (2 * torch.randn(T, H, hd, generator=g, device=dev)).to(bf)
+    w = (1 + 0.2 * torch.randn(hd, generator=g, device=dev)).to(bf)
+    pos = torch.randint(0, 4096, (T,), generator=g, device=dev)
+    qkv = torch.randn(T // 16, 16, 3, H, hd, generator=g, device=dev).to(bf)
+    qn = (1 + 0.2 * torch.randn(hd, generator=g, device=dev)).to(bf)
+    kn = (1 + 0.2 * torch.randn(hd, generator=g, device=dev)).to(bf)
+    R, page = 4096, 16
+    kv = torch.randn(R, L, 2, H, hd, generator=g, device=dev).to(bf)
+    kvn = (1 + 0.2 * torch.randn(L, hd, generator=g, device=dev)).to(bf)
+    caches = [torch.zeros(R // page + 8, H, page, 2 * hd, dtype=bf, device=dev) for _ in range(L)]
+    ptrs = torch.tensor([c.data_ptr() for c in caches], dtype=torch.int64, device=dev)
+    slots = torch.randperm(R + 8 * page, generator=g, device=dev)[:R]
+    rpos = torch.randint(0, 4096, (R,), generator=g, device=dev)
+    st = caches[0].stride()
+    ang = torch.rand(64, 16, hd // 2, generator=g, device=dev) * 6.283
+    freqs = torch.stack([ang.cos(), ang.sin()], -1).contiguous()
+    xs = x.view(64, 16, H, hd)
+    wf, qnf, knf = w.float(), qn.float(), kn.float()
+    V = 151936
+    logits = (3 * torch.randn(T, V, generator=g, device=dev)).to(bf)
+    if ours:
+        from flashmap_b200 import ops
+        from flashmap_b200 import serving_ops as S
+
+        return {
+            "vllm rms_norm_rope (1024 x 16 x 128)": lambda: S.vllm_rms_norm_rope(x, w, rope, pos, eps),
+            "vllm block_self_attention (64 blocks x 16, 16 x 128)": lambda: S.vllm_block_self_attention(
+                qkv, qn, kn, rope, pos, eps),
+            "vllm write_context_kv (4096 tokens x 8 layers, 16-token pages)": lambda: S.write_context_kv(
+                kv, rpos, slots, kvn, rope, ptrs, (st[0], st[1], st[2], hd), page, eps),
+            "sglang rms_norm_rope (64 x 16 x 16 x 128)": lambda: S.sglang_rms_norm_rope(xs, wf, freqs, eps),
+            "sglang block_self_attention (64 blocks x 16, 16 x 128)": lambda: S.sglang_block_self_attention(
+                qkv, qnf, knf, freqs, eps),
+            "greedy rows (1024 x 151936)": lambda: ops.sample_rows(logits.view(1, T, V), None, 0.0, 0, 0),
+        }
+    temps = torch.ones(T, device=dev)
+    greedy = torch.ones(T, dtype=torch.int32, device=dev)
+    seed = torch.tensor(7, dtype=torch.int64, device=dev)
+    vk, sk = vllm_kernels, sglang_kernels
+    return {
+        "vllm rms_norm_rope (1024 x 16 x 128)": lambda: vk.rms_norm_rope(x, w, rope, pos, eps),
+        "vllm block_self_attention (64 blocks x 16, 16 x 128)": lambda: vk.block_self_attention(
+            qkv, qn, kn, rope, pos, eps),
+        "vllm write_context_kv (4096 tokens x 8 layers, 16-token pages)": lambda: vk.write_context_kv(
+            kv, rpos, slots, kvn, rope, ptrs, (st[0], st[1], st[2], hd), page, eps),
+        "sglang rms_norm_rope (64 x 16 x 16 x 128)": lambda: sk.rms_norm_rope(xs, wf, freqs, eps),
+        "sglang block_self_attention (64 blocks x 16, 16 x 128)": lambda: sk.block_self_attention(
+            qkv, qnf, knf, freqs, eps),
+        "greedy rows (1024 x 151936)": lambda: sk.sample_rows(logits, temps, greedy, seed),
+    }
+
+
+def time_ops(cases, steps: int, warmup: int) -> dict:
+    """Per operator: the device time of one call (the call captured in a CUDA
+    graph and replayed `steps` times) and the time of one call through its
+    Python entry (host dispatch included)."""
+    out = {}
+    for name, fn in cases.items():
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        row = {"call_us": a.elapsed_time(b) / steps * 1000.0}
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            for _ in range(warmup):
+                graph.replay()
+            torch.cuda.synchronize()
+            a.record()
+            for _ in range(steps):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            row["graph_us"] = a.elapsed_time(b) / steps * 1000.0
+            del graph
+        except Exception as e:  # noqa: BLE001 - reported, not fatal: the call time stands
+            row["graph_error"] = str(e).splitlines()[0][:160]
+        out[name] = row
+    return out
+
+
+def load_reference_module(sub: str, name: str):
+    """A module of the reference's installed copy (baseline/_ref), loaded from
+    its file: its package __init__ (plugin registration) is not run."""
+    import importlib.util
+
+    path = os.path.join(OPS_REF, "flashmap", sub, f"{name}.py")
+    spec = importlib.util.spec_from_file_location(f"ref_{sub}_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_ops(args, world, rank, local):
+    """The serving operators of flashmap_vllm / flashmap_sglang: this library's
+    CUDA kernels beside the reference's own Triton kernels (the installed
+    reference in baseline/_ref, run in a child process because both register
+    the same torch.library names), same shapes and seeded inputs; device time
+    from CUDA-graph replays, and the per-call time through each Python entry."""
+    if args.ops_side == "reference":
+        vk, sk = load_reference_module("vllm", "kernels"), load_reference_module("sglang", "kernels")
+        res = time_ops(ops_cases(torch.device("cuda", 0), sk, vk, ours=False), args.steps, args.warmup)
+        print(json.dumps(res), flush=True)
+        return
+    from flashmap_b200 import _lib
+    from flashmap_b200 import serving_ops as S
+
+    _lib.require_device()
+    ours = time_ops(ops_cases(torch.device("cuda", 0), None, S, ours=True), args.steps, args.warmup)
+    ref, why = None, None
+    if not os.path.isdir(os.path.join(OPS_REF, "flashmap")):
+        why = "baseline/_ref holds no installed reference"
+    else:
+        p = subprocess.run([sys.executable, os.path.abspath(__file__), "--workload", "ops", "--ops-side", "reference",
+                            "--steps", str(args.steps), "--warmup", str(args.warmup)], capture_output=True, text=True)
+        lines = [l for l in p.stdout.splitlines() if l.startswith("{")]
+        if p.returncode == 0 and lines:
+            ref = json.loads(lines[-1])
+        else:
+            why = (p.stderr.strip().splitlines() or ["reference run failed"])[-1][:200]
+    table = {}
+    for name, o in ours.items():
+        row = {"ours_graph_us": o.get("graph_us"), "ours_call_us": o["call_us"]}
+        r = (ref or {}).get(name)
+        if r:
+            row["reference_triton_graph_us"] = r.get("graph_us")
+            row["reference_triton_call_us"] = r["call_us"]
+            if o.get("graph_us") and r.get("graph_us"):
+                row["speedup"] = r["graph_us"] / o["graph_us"]
+            row["speedup_per_call"] = r["call_us"] / o["call_us"]
+        table[name] = row
+    ratios = [r["speedup"] for r in table.values() if "speedup" in r]
+    geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios)) if ratios else None
+    line = {"metric": "serving operators: device-time speed-up over the reference's Triton kernels (geometric mean)",
+            "value": geo, "unit": "x", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": "serving operators at 64 requests x 16 slots, config-2 map"}, "ops": table}
+    if why:
+        line["reference_unavailable"] = why
+    print(json.dumps(line), flush=True)
+
+
 def run_paged(args, world, rank, local):
     """The vLLM-layout paged cross-attention operator (flashmap_vllm::paged_cross_attention)
     at the config-2 map's shape: 64 requests x 16 query rows, 16 heads of 128,
@@ -965,11 +1127,14 @@ def main():
     ap.add_argument("--launch", choices=["auto", "kernels", "stream"], default="auto",
                     help="launch structure of a draft: the kernel sequence (kernels), the streamed "
                          "single-launch pass (stream), or the library's choice (auto)")
-    ap.add_argument("--workload", choices=["all", "config2", "config3", "config4", "config5", "paged"], default="all",
+    ap.add_argument("--workload", choices=["all", "config2", "config3", "config4", "config5", "paged", "ops"],
+                    default="all",
                     help="all (the default line: config 5's 512 requests sharded over the GPUs, with the config-2 "
                          "batch-1 pass and, on one GPU, configs 3 and 4 beside it), config2 (batch 1 alone), "
                          "config3 (batch 64 ragged), config4 (acceptance), config5 (one 64-request chunk), "
-                         "paged (vLLM paged cross-attention operator)")
+                         "paged (vLLM paged cross-attention operator), ops (the serving operators beside the "
+                         "reference's Triton kernels)")
+    ap.add_argument("--ops-side", choices=["ours", "reference"], default="ours", help=argparse.SUPPRESS)
     ap.add_argument("--profile-small", action="store_true",
                     help="2 layers and a 32768-row LM head: the same kernels on < 2 GB, for ncu captures")
     args = ap.parse_args()
@@ -986,6 +1151,8 @@ def main():
             run_config3(args, world, rank, local)
         elif args.workload == "paged":
             run_paged(args, world, rank, local)
+        elif args.workload == "ops":
+            run_ops(args, world, rank, local)
         elif args.workload == "config4":
             run_config4(args, world, rank, local)
         else:
