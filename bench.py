@@ -696,9 +696,10 @@ def ops_cases(dev, sglang_kernels, vllm_kernels, ours: bool):
 
 
 def time_ops(cases, steps: int, warmup: int) -> dict:
-    """Per operator: the device time of one call (the call captured in a CUDA
-    graph and replayed `steps` times) and the time of one call through its
-    Python entry (host dispatch included)."""
+    """Per operator: the time of one call through its Python entry (CUDA
+    events around `steps` back-to-back calls after `warmup`; host dispatch
+    included; the kernels' own device time comes from an ncu launch list of
+    the same command)."""
     out = {}
     for name, fn in cases.items():
         for _ in range(warmup):
@@ -710,24 +711,7 @@ def time_ops(cases, steps: int, warmup: int) -> dict:
             fn()
         b.record()
         torch.cuda.synchronize()
-        row = {"call_us": a.elapsed_time(b) / steps * 1000.0}
-        try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                fn()
-            for _ in range(warmup):
-                graph.replay()
-            torch.cuda.synchronize()
-            a.record()
-            for _ in range(steps):
-                graph.replay()
-            b.record()
-            torch.cuda.synchronize()
-            row["graph_us"] = a.elapsed_time(b) / steps * 1000.0
-            del graph
-        except Exception as e:  # noqa: BLE001 - reported, not fatal: the call time stands
-            row["graph_error"] = str(e).splitlines()[0][:160]
-        out[name] = row
+        out[name] = {"call_us": a.elapsed_time(b) / steps * 1000.0}
     return out
 
 
@@ -747,8 +731,8 @@ def run_ops(args, world, rank, local):
     """The serving operators of flashmap_vllm / flashmap_sglang: this library's
     CUDA kernels beside the reference's own Triton kernels (the installed
     reference in baseline/_ref, run in a child process because both register
-    the same torch.library names), same shapes and seeded inputs; device time
-    from CUDA-graph replays, and the per-call time through each Python entry."""
+    the same torch.library names), same shapes and seeded inputs, each call
+    through its Python entry on both sides."""
     if args.ops_side == "reference":
         vk, sk = load_reference_module("vllm", "kernels"), load_reference_module("sglang", "kernels")
         res = time_ops(ops_cases(torch.device("cuda", 0), sk, vk, ours=False), args.steps, args.warmup)
@@ -772,18 +756,15 @@ def run_ops(args, world, rank, local):
             why = (p.stderr.strip().splitlines() or ["reference run failed"])[-1][:200]
     table = {}
     for name, o in ours.items():
-        row = {"ours_graph_us": o.get("graph_us"), "ours_call_us": o["call_us"]}
+        row = {"ours_call_us": o["call_us"]}
         r = (ref or {}).get(name)
         if r:
-            row["reference_triton_graph_us"] = r.get("graph_us")
             row["reference_triton_call_us"] = r["call_us"]
-            if o.get("graph_us") and r.get("graph_us"):
-                row["speedup"] = r["graph_us"] / o["graph_us"]
-            row["speedup_per_call"] = r["call_us"] / o["call_us"]
+            row["speedup"] = r["call_us"] / o["call_us"]
         table[name] = row
     ratios = [r["speedup"] for r in table.values() if "speedup" in r]
     geo = math.exp(sum(math.log(r) for r in ratios) / len(ratios)) if ratios else None
-    line = {"metric": "serving operators: device-time speed-up over the reference's Triton kernels (geometric mean)",
+    line = {"metric": "serving operators: per-call speed-up over the reference's Triton kernels (geometric mean)",
             "value": geo, "unit": "x", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
             "config": {"workload": "serving operators at 64 requests x 16 slots, config-2 map"}, "ops": table}
