@@ -161,12 +161,12 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) self_attn_qknorm_kernel(SelfQkA
   constexpr int PART = 16 * HD * 2;
   constexpr int NP = HD / 64;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int it = blockIdx.x * SQ_WARPS + warp;
-  if (it >= a.blocks * a.heads) return;
+  // one CTA per (block, head): its warps share the 32 q/k rows, warp 0 attends
+  const int it = blockIdx.x;
   const int b = it / a.heads, h = it % a.heads;
   const long long D = (long long)a.heads * HD;
-  uint8_t* st = sq_smem + warp * 3 * PART;
-  for (int r = 0; r < 16; ++r) {
+  uint8_t* st = sq_smem;
+  for (int r = warp; r < 16; r += SQ_WARPS) {
     const long long tok = (long long)b * 16 + r;
     const long long pos = load_pos(a.pos, a.pdt, tok);
 #pragma unroll
@@ -182,13 +182,14 @@ __global__ void __launch_bounds__(SQ_WARPS * 32) self_attn_qknorm_kernel(SelfQkA
       }
     }
   }
-  for (int idx = lane; idx < 16 * (HD / 8); idx += 32) {
+  for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += SQ_WARPS * 32) {
     const int row = idx / (HD / 8), ch = idx % (HD / 8);
     const uint4 v = *reinterpret_cast<const uint4*>(a.qkv + ((long long)b * 16 + row) * 3 * D + 2 * D +
                                                     (long long)h * HD + ch * 8);
     *reinterpret_cast<uint4*>(st + 2 * PART + blk_sw(row, ch)) = v;
   }
-  __syncwarp();
+  __syncthreads();
+  if (warp != 0) return;
   const uint32_t base = smem_u32(st);
   __nv_bfloat16* out = a.out + (long long)b * 16 * D + (long long)h * HD;
   block_attn_head<HD>(base, base + PART, base + 2 * PART, a.scale, [&](int i, int d, float lo, float hi) {
@@ -825,8 +826,8 @@ extern "C" fm_status fm_block_self_attn_qknorm(const void* qkv, void* out, int64
   if ((st = check_rope(rope))) return st;
   SelfQkArgs a{static_cast<const __nv_bfloat16*>(qkv), static_cast<__nv_bfloat16*>(out), (int)blocks, (int)heads,
                q_norm, k_norm, weight_dtype, rope_ref(rope), positions, positions_dtype, eps, scale, err};
-  const unsigned grid = (unsigned)((blocks * heads + SQ_WARPS - 1) / SQ_WARPS);
-  const size_t smem = (size_t)SQ_WARPS * 3 * 16 * head_dim * 2;
+  const unsigned grid = (unsigned)(blocks * heads);  // one CTA per (block, head)
+  const size_t smem = (size_t)3 * 16 * head_dim * 2;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   static int configured = -1;
   int dev;
