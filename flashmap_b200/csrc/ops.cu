@@ -2052,8 +2052,19 @@ extern "C" fm_status fm_sample_rows(const void* logits, int32_t dtype, const flo
   if (B <= 0 || K <= 0 || V <= 0 || bad_dtype(dtype)) return set_error(FM_ERR_SHAPE, "sample_rows: bad arguments");
   if (temperature <= 0.0f) {
     if (!logits) return set_error(FM_ERR_INVALID, "sample_rows: null logits");
-    return FM_DISPATCH_LOGITS(dtype, row_stats_kernel, dim3((unsigned)(B * K)), logits, (long long)V, 0.0f,
-                              (float*)nullptr, tokens);
+    // the sliced argmax of greedy acceptance: each int64 token holds its row's
+    // 64-bit (value, complement index) key while the slices merge into it by
+    // atomicMax, then the key is turned into its index in place
+    const long long rows = B * K;
+    const long long slices = ((V + 7) / 8 + SLICE_VECS - 1) / SLICE_VECS;
+    if (slices > 65535 || rows >= (1ll << 31)) return set_error(FM_ERR_SHAPE, "sample_rows: too many rows or ids");
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(tokens);
+    fm_status st = check_cuda(cudaMemsetAsync(keys, 0, (size_t)rows * 8, as_stream(stream)), "sample_rows: key reset");
+    if (st) return st;
+    st = FM_DISPATCH_LOGITS(dtype, row_argmax_slice_kernel, dim3((unsigned)rows, (unsigned)slices), logits,
+                            (long long)V, keys);
+    if (st) return st;
+    return launch_argmax_tokens(keys, tokens, (int)rows, as_stream(stream), false);
   }
   if (!probs) return set_error(FM_ERR_INVALID, "sample_rows: T > 0 needs probs");
   return launch_kernel(sample_rows_kernel, dim3((unsigned)(B * K)), dim3(RT), 0, as_stream(stream), false, probs,
