@@ -100,8 +100,21 @@ def _half_table(cos_sin: torch.Tensor, head_dim: int) -> _lib.RopeView:
                          cos_sin.shape[0])
 
 
+_ERR_WORDS: dict = {}
+
+
 def _err(device) -> torch.Tensor:
-    return torch.zeros(1, dtype=torch.int32, device=device)
+    """The device's error word (int32, zero until a kernel records an index or
+    timeout code; the first code sticks), allocated once per device so that a
+    call launches no fill kernel for it."""
+    key = torch.device(device)
+    if key.index is None:
+        key = torch.device(key.type, torch.cuda.current_device())
+    w = _ERR_WORDS.get(key)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=key)
+        _ERR_WORDS[key] = w
+    return w
 
 
 def _bf16_weight(w: torch.Tensor, name: str) -> torch.Tensor:
