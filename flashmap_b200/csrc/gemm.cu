@@ -164,6 +164,11 @@ static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64
   }();
   const int64_t avail = cg == 2 ? cap_groups : (int64_t)num_sms() * per_sm;
   const int64_t kb = tiles > 0 ? units / tiles : 0;
+  // Short reductions of wide blocks (at most 40 k-blocks) with no more tiles
+  // than groups: one whole tile per group.  A split tile's fix-up (partials
+  // published, waited for, staged and summed by its head) costs more than the
+  // half of such a mainloop it saves.
+  if (bn >= 64 && kb <= 40 && tiles <= avail && !split_env) return tiles * cg;
   if (kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
     for (int64_t g = avail < tiles ? avail : tiles; g * 4 >= avail * 3; --g)
       if (tiles % g == 0) return g * cg;
