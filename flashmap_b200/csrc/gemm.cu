@@ -151,7 +151,12 @@ int64_t resident_pairs(GemmKernel k, size_t smem) {
 // (stream-K would start every group at its own k offset, and the
 // vocabulary-sized B panel, larger than L2, would be re-read per m-tile).
 // Returns CTAs.
-static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64_t cap_groups) {
+// `sizing` (workspace bounds) skips the two whole-tile schedules: the
+// stream-K grid bounds theirs for the same shape, and a plan sizes its
+// partials at its largest token counts, which must then bound every smaller
+// call's stream-K grid as well.
+static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64_t cap_groups, bool sizing = false,
+                             bool whole_short = false) {
   static const int per_sm = [] {
     const char* e = getenv("FM_GEMM_CTAS_PER_SM");
     const int v = e ? atoi(e) : 1;
@@ -167,9 +172,12 @@ static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64
   // Short reductions of wide blocks (at most 40 k-blocks) with no more tiles
   // than groups: one whole tile per group.  A split tile's fix-up (partials
   // published, waited for, staged and summed by its head) costs more than the
-  // half of such a mainloop it saves.
-  if (bn >= 64 && kb <= 40 && tiles <= avail && !split_env) return tiles * cg;
-  if (kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
+  // half of such a mainloop it saves.  Only for the DiT layers' residual and
+  // q/k-norm GEMMs (`whole_short`): the context-extension GEMMs keep the split
+  // schedule, under which a context extended in chunks equals one extended at
+  // once bit for bit (their k segmentation then does not change with the rows).
+  if (!sizing && whole_short && bn >= 64 && kb <= 40 && tiles <= avail && !split_env) return tiles * cg;
+  if (!sizing && kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
     for (int64_t g = avail < tiles ? avail : tiles; g * 4 >= avail * 3; --g)
       if (tiles % g == 0) return g * cg;
   }
@@ -196,7 +204,7 @@ GemmGeom gemm_geom(int64_t M, int64_t N, int64_t K) {
   g.n_tiles = (N + g.bn - 1) / g.bn;
   g.kb = (K + 63) / 64;
   g.units = g.m_tiles * g.n_tiles * g.kb;
-  g.grid_bound = gemm_grid_for(g.units, g.m_tiles * g.n_tiles, g.bn, g.cg, num_sms() / 2);
+  g.grid_bound = gemm_grid_for(g.units, g.m_tiles * g.n_tiles, g.bn, g.cg, num_sms() / 2, true);
   return g;
 }
 }  // namespace
@@ -246,7 +254,8 @@ fm_status gemm_prepare(GemmPlan* p, const void* W, int64_t M, int64_t K, int64_t
   if (!k) return set_error(FM_ERR_UNSUPPORTED, "gemm: no kernel for epilogue %d", epi);
   p->smem = smem;
   const int64_t cap = cg == 2 ? resident_pairs(k, smem) : 0;
-  p->grid = (int)gemm_grid_for(a.units, (int64_t)a.m_tiles * a.n_tiles, bn, cg, cap);
+  p->grid = (int)gemm_grid_for(a.units, (int64_t)a.m_tiles * a.n_tiles, bn, cg, cap, false,
+                               epi == EPI_RESID || epi == EPI_QKNORM);
   return FM_OK;
 }
 
