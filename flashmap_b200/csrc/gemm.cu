@@ -172,11 +172,17 @@ static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64
   // Short reductions of wide blocks (at most 40 k-blocks) with no more tiles
   // than groups: one whole tile per group.  A split tile's fix-up (partials
   // published, waited for, staged and summed by its head) costs more than the
-  // half of such a mainloop it saves.  Only for the DiT layers' residual and
-  // q/k-norm GEMMs (`whole_short`): the context-extension GEMMs keep the split
+  // half of such a mainloop it saves.  Only for the DiT layers' residual,
+  // q/k-norm, GELU and SwiGLU GEMMs (`whole_short`): the context-extension GEMMs keep the split
   // schedule, under which a context extended in chunks equals one extended at
   // once bit for bit (their k segmentation then does not change with the rows).
-  if (!sizing && whole_short && bn >= 64 && kb <= 40 && tiles <= avail && !split_env) return tiles * cg;
+  if (!sizing && whole_short && bn >= 64 && kb <= 40 && !split_env) {
+    if (tiles <= avail) return tiles * cg;
+    // w whole tiles per group when they divide evenly and still occupy three
+    // quarters of the groups (each group's first epilogue overlaps its next mainloop)
+    const int64_t w = (tiles + avail - 1) / avail;
+    if (tiles % w == 0 && (tiles / w) * 4 >= avail * 3) return (tiles / w) * cg;
+  }
   if (!sizing && kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
     for (int64_t g = avail < tiles ? avail : tiles; g * 4 >= avail * 3; --g)
       if (tiles % g == 0) return g * cg;
@@ -255,7 +261,7 @@ fm_status gemm_prepare(GemmPlan* p, const void* W, int64_t M, int64_t K, int64_t
   p->smem = smem;
   const int64_t cap = cg == 2 ? resident_pairs(k, smem) : 0;
   p->grid = (int)gemm_grid_for(a.units, (int64_t)a.m_tiles * a.n_tiles, bn, cg, cap, false,
-                               epi == EPI_RESID || epi == EPI_QKNORM);
+                               epi == EPI_RESID || epi == EPI_QKNORM || epi == EPI_GELU || epi == EPI_SWIGLU);
   return FM_OK;
 }
 
