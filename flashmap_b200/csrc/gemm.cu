@@ -178,10 +178,11 @@ static int64_t gemm_grid_for(int64_t units, int64_t tiles, int bn, int cg, int64
   // once bit for bit (their k segmentation then does not change with the rows).
   if (!sizing && whole_short && bn >= 64 && kb <= 40 && !split_env) {
     if (tiles <= avail) return tiles * cg;
-    // w whole tiles per group when they divide evenly and still occupy three
-    // quarters of the groups (each group's first epilogue overlaps its next mainloop)
+    // w whole tiles per group when they divide evenly and still occupy five
+    // eighths of the groups (each group's first epilogue overlaps its next
+    // mainloop; the <= 40 k-blocks a group adds cost less than a split's fix-up)
     const int64_t w = (tiles + avail - 1) / avail;
-    if (tiles % w == 0 && (tiles / w) * 4 >= avail * 3) return (tiles / w) * cg;
+    if (tiles % w == 0 && (tiles / w) * 8 >= avail * 5) return (tiles / w) * cg;
   }
   if (!sizing && kb >= 512 && tiles * 4 >= avail * 3 && !split_env) {
     for (int64_t g = avail < tiles ? avail : tiles; g * 4 >= avail * 3; --g)
