@@ -701,6 +701,57 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, const float* v, in
   }
 }
 
+// The LM-head epilogue of a whole wide tile (vector path, unscattered
+// output): the logits of each 16-column chunk go out through two [16][128]
+// store tiles used alternately (no refill barrier), and each chunk's per-warp
+// argmax keys stay in shared memory ([4 warp quarters][BN]), so the quarters
+// meet once per tile instead of twice per chunk: after the last chunk every
+// thread folds the four quarters' keys of BN / 128 columns and atomicMax-es
+// them into the tokens' keys.  Same values and keys as epilogue16.
+// `ring` holds the two store tiles then the keys (8 KB + 32 * BN bytes).
+template <int BN, typename ChunkFn>
+__device__ __forceinline__ void logits_wide(const GemmArgs& a, ChunkFn chunk, int r, int mt, int n_tile,
+                                            __nv_bfloat16* ring) {
+  const int lane = threadIdx.x & 31;
+  const int q = (threadIdx.x >> 5) & 3;
+  const int m = mt * 128 + r;
+  const bool mvalid = m < a.M;
+  const float b = (a.bias && mvalid) ? bf2f(a.bias[m]) : 0.0f;
+  const uint32_t id = mvalid ? (uint32_t)(a.col_ids ? a.col_ids[m] : (long long)m) : 0u;
+  const bool want_argmax = a.argmax_keys != nullptr;  // uniform over the launch
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(ring + 2 * 2048);
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    float v[16];
+    chunk(c0, v);
+    __nv_bfloat16* tile = ring + ((c0 >> 4) & 1) * 2048;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float y = round_bf(__fadd_rn(v[j], b));
+      tile[j * 128 + r] = f2bf(y);
+      if (!want_argmax) continue;
+      const unsigned long long key = mvalid ? argmax_key(y, id) : 0ull;
+      const uint32_t hi = (uint32_t)(key >> 32);
+      const uint32_t mh = __reduce_max_sync(0xffffffffu, hi);
+      const uint32_t ml = __reduce_max_sync(0xffffffffu, hi == mh ? (uint32_t)key : 0u);
+      if (lane == j) keys[q * BN + c0 + j] = ((unsigned long long)mh << 32) | ml;
+    }
+    // the store tile's barrier also orders the reads of the tile two chunks back
+    vec_store_tile(a, mt * 128, n_tile + c0, tile, false);
+  }
+  if (!want_argmax) return;
+  named_bar_sync(1, 128);
+  const int t = threadIdx.x - 64;
+#pragma unroll
+  for (int k = 0; k < BN / 128; ++k) {
+    const int j = t + 128 * k;
+    unsigned long long key = keys[j];
+#pragma unroll
+    for (int qq = 1; qq < 4; ++qq) key = keys[qq * BN + j] > key ? keys[qq * BN + j] : key;
+    if (n_tile + j < a.N) atomicMax(a.argmax_keys + n_tile + j, key);
+  }
+  named_bar_sync(1, 128);  // the keys and store tiles are refilled by the next tile
+}
+
 // ---------------------------------------------------------------------------------------------
 // CG = 1: one CTA per 128 x BN tile.  CG = 2 (launched as clusters of two):
 // a CTA pair per 256 x BN tile, the units (pair tile, k-block) split over the
@@ -1017,6 +1068,15 @@ __global__ void __launch_bounds__(192, 1)
                 tmem_wait_ld();
               },
               r, mt, n0, 0, BN, xch, vxt);
+      } else if (whole && EPI == EPI_LOGITS && BN >= 128 && vxt != nullptr) {
+        if constexpr (EPI == EPI_LOGITS && BN >= 128)
+          logits_wide<BN>(
+              a,
+              [&](int c0, float* v) {
+                tmem_ld_x16(taddr + c0, v);
+                tmem_wait_ld();
+              },
+              r, mt, n0, ring);
       } else if (whole) {
         // chunks of 16 columns; each chunk's global reads issued one chunk ahead
         float pre[32];
